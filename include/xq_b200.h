@@ -1,0 +1,170 @@
+/*
+ * xq_b200.h -- C ABI of the B200 attention hot path (libxq_b200.so).
+ *
+ * Plain pointers, ggml ne/nb strides, a CUDA stream and an int status: no
+ * torch or C++ types cross this boundary.  All tensor pointers are device
+ * pointers unless stated otherwise.  Every entry point is asynchronous on the
+ * given stream and returns XQ_OK or an XQ_ERR_* code; a kernel-launch failure
+ * returns XQ_ERR_CUDA and xq_last_error() has the CUDA message.
+ *
+ * Each entry point replaces one reference interface (file:line in
+ * hjotha/xllama-qwen35-xbox, whose ggml-cpu kernels live in the llama.cpp
+ * submodule beellama.cpp @ 982eaadaa9dbe761f00205bc20b6c04b7329b58d):
+ *
+ *   xq_flash_attn_ext     GGML_OP_FLASH_ATTN_EXT as dispatched by the ggml
+ *                         scheduler to ggml-cpu
+ *                         (bench/results/diag-ubatch-20261007/snapshot-r108/
+ *                         llama.cpp_ggml_src_ggml-cpu_ggml-cpu.c:2085-2088),
+ *                         incl. the split-KV decode branch
+ *                         (patches/0006-cpu-flash-attn-consistent-kv-reduction.patch:7-14)
+ *   xq_gated_delta_net    GGML_OP_GATED_DELTA_NET (ggml-cpu.c:2148-2150 and the
+ *                         D3D12 kernel dispatch src/bridge/ggml_d3d12.cpp:1905-1941)
+ *   xq_attend_range       RemoteAttnEngine::attend_range
+ *                         (uwp/rkva/remote-attn-engine.h:152-154,
+ *                          remote-attn-engine.cpp:2774-3251)
+ *   xq_fa_partials +      split partials + LSE reduction
+ *   xq_lse_merge          (shaders/rkva/rkva_range_attn.hlsl:59-106,
+ *                          rkva_range_reduce_opt.hlsl:26-133)
+ *   xq_split_k            rkva_rprof::reference_split_k / optimized_split_k
+ *                         (uwp/rkva/rkva-range-profile.h:98-111)
+ *   xq_dequantize_rows    ggml to_float for F16/Q8_0/Q4_0 (ggml-quants.c)
+ *   xq_quantize_rows      ggml from_float reference quantizers (the KV-cache
+ *                         write path, shaders/rkva/rkva_store_f16.hlsl)
+ */
+#ifndef XQ_B200_H
+#define XQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *xq_stream_t; /* == cudaStream_t */
+
+enum xq_status {
+    XQ_OK = 0,
+    XQ_ERR_INVALID = 1,     /* bad argument / shape contract violated */
+    XQ_ERR_UNSUPPORTED = 2, /* valid ggml op this library does not claim */
+    XQ_ERR_CUDA = 3,        /* a CUDA call failed; see xq_last_error() */
+    XQ_ERR_WORKSPACE = 4,   /* workspace missing or too small */
+};
+
+/* ggml type ids (ggml.h enum ggml_type values, stable across versions). */
+enum xq_type { XQ_TYPE_F32 = 0, XQ_TYPE_F16 = 1, XQ_TYPE_Q4_0 = 2, XQ_TYPE_Q8_0 = 8 };
+
+/* A ggml tensor view: ne = elements per dim, nb = byte strides. */
+typedef struct {
+    int32_t type;
+    int32_t reserved;
+    const void *data;
+    int64_t ne[4];
+    uint64_t nb[4];
+} xq_tensor;
+
+/* ------------------------------------------------------------------------ */
+/* GGML_OP_FLASH_ATTN_EXT                                                    */
+/*   q    F32  [DK, n_q, n_head, n_seq]                                      */
+/*   k    F16/Q8_0/Q4_0 [DK, n_kv, n_head_kv, n_seq_kv]  (n_head % n_head_kv */
+/*        == 0, n_seq % n_seq_kv == 0: ggml broadcast)                        */
+/*   v    same type as k, [DV, n_kv, n_head_kv, n_seq_kv], DV == DK          */
+/*   mask F16 [n_kv, >= n_q, m2, m3] or data == NULL (broadcast by modulo)   */
+/*   sinks F32 [n_head] or NULL                                               */
+/*   dst  F32 [DV, n_head, n_q, n_seq] contiguous                             */
+/*   op_params: scale, max_bias, logit_softcap (ggml op_params[0..2])         */
+/* DK in {64, 128, 256}.  Decode-shaped calls (n_q * n_head / n_head_kv <=   */
+/* 16) run the split-KV kernel; larger F16 calls run the tensor-core prefill */
+/* kernel.  Workspace: xq_flash_attn_ext_workspace() bytes, any contents;    */
+/* it may be NULL when that size is 0.                                       */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    xq_tensor q, k, v, mask;
+    const float *sinks;
+    float *dst;
+    float scale, max_bias, softcap;
+    int32_t n_splits; /* 0: automatic (fill the GPU), else KV splits per head */
+} xq_fa_params;
+
+size_t xq_flash_attn_ext_workspace(const xq_fa_params *p);
+int xq_flash_attn_ext(const xq_fa_params *p, void *workspace, size_t workspace_bytes,
+                      xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Split partials for sharded / remote decode.                               */
+/* Same tensors as xq_flash_attn_ext (mask/sinks allowed), but the KV rows   */
+/* are cut into fixed global splits of rows_per_split rows; this call        */
+/* computes splits [split_begin, split_end) and writes their records to      */
+/* partials[(s - split_begin) * n_rows + row] * (DV + 2) floats =            */
+/* (acc[DV] unnormalised, max, denom), row = (seq * n_q + iq1) * n_head + h. */
+/* An empty split writes (0, -FLT_MAX, 0).  The records of all splits,       */
+/* gathered in split order from any number of GPUs, merge bit-identically.   */
+/* ------------------------------------------------------------------------ */
+int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_begin,
+                   int64_t split_end, float *partials, xq_stream_t stream);
+
+/* partials [n_splits][n_rows][D+2] -> out [n_rows][D] (F32) and, if lse is  */
+/* not NULL, lse [n_rows] (natural log).  Fixed split order; empty splits    */
+/* (denom == 0) are skipped; all empty => O = 0, LSE = -inf; a participating */
+/* non-finite state poisons the row with NaN (rkva_range_reduce_opt.hlsl).   */
+int xq_lse_merge(const float *partials, int64_t n_splits, int64_t n_rows, int64_t D,
+                 float *out, float *lse, xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* RKVA RANGE_ATTN: (O, LSE) over a compact KV range [0, active) whose row r */
+/* holds absolute position origin + r.  k/v: [capacity][n_head_kv][D] in     */
+/* storage type (F16/Q8_0/Q4_0); q: F32 [n_tokens][n_head][D]; positions:    */
+/* int32 [n_tokens] absolute.  Query t attends rows                          */
+/* [0, min(active, positions[t] - origin + 1)).  out F32 [n_tokens][n_head]  */
+/* [D], lse F32 [n_tokens][n_head].  Empty => O = 0, LSE = -inf.             */
+/* split_mode: 0 reference policy, 1/2/3 balanced/fine/coarse, 4 automatic.  */
+/* positions must be device memory; workspace per                            */
+/* xq_attend_range_workspace().                                              */
+/* ------------------------------------------------------------------------ */
+size_t xq_attend_range_workspace(int32_t storage, uint32_t n_tokens, uint32_t active,
+                                 uint32_t n_head, uint32_t n_head_kv, uint32_t head_dim,
+                                 uint32_t split_mode);
+int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_head,
+                    uint32_t n_head_kv, uint32_t head_dim, uint32_t origin, uint32_t active,
+                    uint32_t n_tokens, const int32_t *positions, const float *q, float kq_scale,
+                    uint32_t split_mode, float *out, float *lse, void *workspace,
+                    size_t workspace_bytes, xq_stream_t stream);
+
+/* Split count of the reference policies (host function, no GPU). */
+uint32_t xq_split_k(uint32_t active, uint32_t mode);
+
+/* ------------------------------------------------------------------------ */
+/* GGML_OP_GATED_DELTA_NET                                                   */
+/*   q, k  F32 [S, H_k, T, n_seq_qk]   (rows contiguous, any head/token      */
+/*         stride); value head h reads key head h % H_k                      */
+/*   v     F32 [S, H, T, n_seq]                                               */
+/*   g, beta F32 [1, H, T, n_seq]  (scalar gates, already activated)         */
+/*   state F32 [S, S, H, n_seq]    (state[seq][h][col][i])                    */
+/*   dst   F32, contiguous: y [n_seq][T][H][S] then K snapshot slots, each  */
+/*         [n_seq][H][S][S]; slot 0 = state after the last token, slot j =  */
+/*         j tokens earlier; slots older than the first token are untouched. */
+/* S = 128.  slots = op_params[0] in [1, 64].                                */
+/* ------------------------------------------------------------------------ */
+int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                       const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                       float *dst, int32_t slots, xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Block codecs.  n_per_row multiple of 32 for Q8_0/Q4_0.  Rows at byte      */
+/* stride src_row_stride / dst_row_stride.                                   */
+/* ------------------------------------------------------------------------ */
+int xq_dequantize_rows(int32_t type, const void *src, uint64_t src_row_stride, float *dst,
+                       uint64_t dst_row_stride, int64_t n_rows, int64_t n_per_row,
+                       xq_stream_t stream);
+int xq_quantize_rows(int32_t type, const float *src, uint64_t src_row_stride, void *dst,
+                     uint64_t dst_row_stride, int64_t n_rows, int64_t n_per_row,
+                     xq_stream_t stream);
+
+/* Library identity and the last error message of this thread. */
+const char *xq_version(void);
+const char *xq_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* XQ_B200_H */

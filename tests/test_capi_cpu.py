@@ -1,0 +1,67 @@
+"""C ABI checks that need no GPU: the library loads, exports every function
+include/xq_b200.h declares, and its host-only logic (split policy, argument
+contracts that fail before any launch) behaves like the reference."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import REPO, golden
+
+HEADER = os.path.join(REPO, "include", "xq_b200.h")
+
+
+def _lib():
+    import xq._lib as L
+    if not os.path.exists(L.LIB_PATH):
+        import importlib.util
+        spec = importlib.util.spec_from_file_location(
+            "xq_build", os.path.join(REPO, "xllama-qwen35-xbox_b200", "build.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        mod.build()
+    return L.lib()
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(xq_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib()
+    names = declared_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in xq_b200.h but not exported"
+    import xq._lib as XL
+    assert sorted(XL.EXPORTS) == names
+
+
+def test_version_string():
+    assert _lib().xq_version().startswith(b"xq_b200")
+
+
+def test_split_policy_matches_reference():
+    L = _lib()
+    g = golden("split_policy.npz")
+    for a, row in zip(g["active"], g["split_k"]):
+        assert [int(L.xq_split_k(int(a), m)) for m in range(4)] == list(row)
+
+
+def test_contract_errors_before_launch():
+    """Bad shapes are refused on the host with a message, before any launch."""
+    import xq._lib as XL
+    L = _lib()
+    p = XL.FaParams()
+    p.q.type = XL.F32
+    p.q.nb[0] = 4
+    p.k.type = p.v.type = XL.F32  # F32 KV: not claimed
+    assert L.xq_flash_attn_ext(C.byref(p), None, 0, None) == XL.XQ_ERR_UNSUPPORTED
+    assert b"K/V types" in L.xq_last_error()
+    assert L.xq_lse_merge(None, 1, 1, 256, None, None, None) == XL.XQ_ERR_INVALID
+    t = XL.Tensor()
+    assert L.xq_gated_delta_net(*[C.byref(t)] * 6, None, 1, None) == XL.XQ_ERR_INVALID

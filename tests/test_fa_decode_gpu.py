@@ -1,0 +1,155 @@
+"""B200 parity: FLASH_ATTN_EXT decode / short multi-query through the C ABI.
+
+Each case runs libxq_b200.so (via the xq host package) and the CPU oracle (the
+ggml-cpu restatement in oracle/) on the same seeded inputs.  Tolerance is the
+north-star bound |gpu - cpu| <= 2e-3 + 1e-2 * |cpu| (fp32 accumulation on the
+GPU vs ggml-cpu's order, Q8_0-quantized q and fp16 value accumulator).
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+
+
+def _xq():
+    import xq
+    return xq
+
+
+def make_case(seed, ty, D, n_head, n_hkv, n_kv, n_q=1, n_seq=1, n_seq_kv=None, mask=None):
+    rng = np.random.default_rng(seed)
+    n_seq_kv = n_seq if n_seq_kv is None else n_seq_kv
+    q = rng.normal(0, 1, (n_seq, n_head, n_q, D)).astype(np.float32)
+    kf = rng.normal(0, 1, (n_seq_kv, n_kv, n_hkv, D)).astype(np.float32)
+    vf = rng.normal(0, 1, (n_seq_kv, n_kv, n_hkv, D)).astype(np.float32)
+    k = oracle.quantize(ty, kf)
+    v = oracle.quantize(ty, vf)
+    m = None
+    if mask == "random":
+        m = np.zeros((1, 1, max(n_q, 1), n_kv), np.float16)
+        m[rng.random(m.shape) < 0.3] = -np.inf
+    elif mask == "causal":
+        m = np.zeros((1, 1, n_q, n_kv), np.float16)
+        for i in range(n_q):
+            m[0, 0, i, n_kv - n_q + i + 1:] = -np.inf
+    return q, k, v, m
+
+
+def run_both(q, k, v, m, ty, scale, n_splits=0, sinks=None, softcap=0.0, max_bias=0.0,
+             nth=8):
+    xq = _xq()
+    dev = torch.device("cuda")
+    tq = torch.from_numpy(q).to(dev)
+    tk = torch.from_numpy(k).to(dev)
+    tv = torch.from_numpy(v).to(dev)
+    tm = torch.from_numpy(m).to(dev) if m is not None else None
+    ts = torch.from_numpy(sinks).to(dev) if sinks is not None else None
+    got = xq.flash_attn_ext(tq, tk, tv, ty, mask=tm, sinks=ts, scale=scale, n_splits=n_splits,
+                            softcap=softcap, max_bias=max_bias)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(q, k, v, ty, ty, mask=m, sinks=sinks, scale=scale,
+                                 softcap=softcap, max_bias=max_bias, nth=nth)
+    return got.cpu().numpy(), want
+
+
+@pytest.mark.parametrize("ty", [oracle.F16, oracle.Q8_0, oracle.Q4_0])
+@pytest.mark.parametrize("D,n_head,n_hkv,n_kv", [(128, 16, 4, 4096), (256, 16, 2, 4096),
+                                                 (256, 24, 4, 1000), (64, 8, 8, 777)])
+def test_decode_parity(ty, D, n_head, n_hkv, n_kv):
+    q, k, v, m = make_case(D + n_kv + ty, ty, D, n_head, n_hkv, n_kv)
+    got, want = run_both(q, k, v, m, ty, D ** -0.5)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+def test_c1_config_f16_split_kv():
+    """16 Q / 4 KV heads, D=128, kv 4096, F16, seed 0."""
+    q, k, v, m = make_case(0, oracle.F16, 128, 16, 4, 4096)
+    for nth in (1, 6, 8):  # ggml split-KV result depends on the thread count
+        got, want = run_both(q, k, v, m, oracle.F16, 128 ** -0.5, nth=nth)
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("ty", [oracle.Q8_0, oracle.Q4_0])
+def test_c2_config_full_size(ty):
+    """BASELINE config 2 at full size: 16 Q / 2 KV heads, D=256, kv 32768."""
+    q, k, v, m = make_case(0, ty, 256, 16, 2, 32768)
+    got, want = run_both(q, k, v, m, ty, 1.0 / 16)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    ref64, _ = oracle.flash_attn_ext(q, k, v, ty, ty, scale=1.0 / 16, f64=True)
+    np.testing.assert_allclose(got, ref64, rtol=1e-3, atol=1e-4)
+
+
+@pytest.mark.parametrize("n_splits", [1, 2, 7, 64, 0])
+def test_split_count_invariance(n_splits):
+    q, k, v, m = make_case(3, oracle.Q8_0, 256, 16, 2, 3000)
+    got, want = run_both(q, k, v, m, oracle.Q8_0, 1.0 / 16, n_splits=n_splits)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("ty", [oracle.F16, oracle.Q8_0])
+@pytest.mark.parametrize("n_q,n_seq", [(2, 1), (5, 1), (3, 3), (9, 2)])
+def test_multi_query_and_sequences(ty, n_q, n_seq):
+    q, k, v, m = make_case(11 * n_q + n_seq, ty, 256, 24, 4, 900, n_q=n_q, n_seq=n_seq,
+                           mask="causal")
+    got, want = run_both(q, k, v, m, ty, 1.0 / 16)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+def test_kv_sequence_broadcast():
+    q, k, v, m = make_case(5, oracle.Q8_0, 128, 8, 2, 600, n_seq=4, n_seq_kv=2)
+    got, want = run_both(q, k, v, m, oracle.Q8_0, 128 ** -0.5)
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+def test_mask_softcap_alibi_sinks():
+    q, k, v, m = make_case(7, oracle.F16, 128, 8, 2, 1500, n_q=2, mask="random")
+    sinks = np.random.default_rng(1).normal(0, 1, 8).astype(np.float32)
+    for kw in ({"softcap": 30.0}, {"max_bias": 8.0}, {"sinks": sinks}, {}):
+        for n_splits in (1, 0):
+            got, want = run_both(q, k, v, m, oracle.F16, 0.3, n_splits=n_splits, **kw)
+            np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL, err_msg=str(kw))
+
+
+def test_fully_masked_rows_are_zero():
+    q, k, v, _ = make_case(9, oracle.Q4_0, 128, 4, 4, 300)
+    m = np.full((1, 1, 1, 300), -np.inf, np.float16)
+    got, want = run_both(q, k, v, m, oracle.Q4_0, 0.1, n_splits=3)
+    assert np.all(got == 0) and np.all(want == 0)
+
+
+def test_strided_q_view_and_canaries():
+    """q as a permuted view of [n_q][n_head][D] (ggml's permute of the Q
+    projection); the destination is surrounded by canaries that must survive."""
+    xq = _xq()
+    rng = np.random.default_rng(21)
+    D, H, Hkv, n_kv = 256, 16, 2, 2048
+    qbuf = rng.normal(0, 1, (1, 1, H, D)).astype(np.float32)  # [seq][q][head][D]
+    q = np.ascontiguousarray(qbuf)
+    kf = rng.normal(0, 1, (1, n_kv, Hkv, D)).astype(np.float32)
+    k = oracle.quantize(oracle.Q8_0, kf)
+    v = oracle.quantize(oracle.Q8_0, rng.normal(0, 1, (1, n_kv, Hkv, D)).astype(np.float32))
+    tq = torch.from_numpy(q).cuda().permute(0, 2, 1, 3)  # (n_seq, n_head, n_q, D) view
+    canary = torch.full((H * D + 2048,), 1e30, dtype=torch.float32, device="cuda")
+    out = canary[1024:1024 + H * D].view(1, 1, H, D)
+    tk, tv = torch.from_numpy(k).cuda(), torch.from_numpy(v).cuda()
+    before_k = tk.clone()
+    xq.flash_attn_ext(tq, tk, tv, oracle.Q8_0, scale=1 / 16, out=out)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(np.ascontiguousarray(q.transpose(0, 2, 1, 3)), k, v,
+                                 oracle.Q8_0, oracle.Q8_0, scale=1 / 16)
+    np.testing.assert_allclose(out.cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+    c = canary.cpu().numpy()
+    assert np.all(c[:1024] == np.float32(1e30)) and np.all(c[1024 + H * D:] == np.float32(1e30))
+    assert torch.equal(before_k, tk)
+
+
+def test_unsupported_types_fail_loudly():
+    xq = _xq()
+    q = torch.zeros((1, 4, 1, 96), device="cuda")
+    k = torch.zeros((1, 64, 4, 192), dtype=torch.uint8, device="cuda")
+    with pytest.raises(xq.XqError):
+        xq.flash_attn_ext(q, k, k, oracle.F16)

@@ -1,0 +1,133 @@
+"""B200 parity: RKVA range attention, split partials + LSE merge, block codecs.
+
+Golden files are the reference's own numpy models (range_*.npz, reduce.npz)
+and gguf 0.19.0 codecs (codecs.npz); see tests/golden/make_golden.py.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _xq():
+    import xq
+    return xq
+
+
+@pytest.mark.parametrize("name,storage", [("f16", oracle.F16), ("q8_0", oracle.Q8_0),
+                                          ("q4_0", oracle.Q4_0)])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 4])
+def test_attend_range_vs_reference_models(name, storage, mode):
+    xq = _xq()
+    g = golden(f"range_{name}.npz")
+    H, Hkv, D = (int(x) for x in g["shape"])
+    cases = sorted({k.split("_")[0] for k in g.files if k.startswith("c")})
+    for c in cases:
+        active, pos, origin, limit, _ = (int(x) for x in g[c + "_meta"])
+        k = torch.from_numpy(g[c + "_k"]).cuda()
+        v = torch.from_numpy(g[c + "_v"]).cuda()
+        q = torch.from_numpy(g[c + "_q"]).cuda().view(1, H, D)
+        p = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        out, lse = xq.attend_range(storage, k, v, q, p, Hkv, origin, active, 1.0 / 16, mode)
+        out, lse = out.cpu().numpy()[0], lse.cpu().numpy()[0]
+        ref_o, ref_l = g[c + "_o64"], g[c + "_l64"]
+        assert np.array_equal(np.isneginf(lse), np.isneginf(ref_l)), c
+        scale = max(1.0, float(np.abs(ref_o).max()))
+        np.testing.assert_allclose(out, ref_o, rtol=1e-4, atol=2e-5 * scale, err_msg=c)
+        fin = ~np.isneginf(ref_l)
+        np.testing.assert_allclose(lse[fin], ref_l[fin], rtol=1e-5, atol=1e-4, err_msg=c)
+        if limit == 0:
+            assert np.all(out == 0)
+
+
+def test_attend_range_multi_token_causal():
+    xq = _xq()
+    rng = np.random.default_rng(4)
+    H, Hkv, D, active, origin = 24, 4, 256, 700, 5000
+    kf = rng.normal(0, 1, (active, Hkv, D)).astype(np.float32)
+    vf = rng.normal(0, 1, (active, Hkv, D)).astype(np.float32)
+    k, v = oracle.quantize(oracle.Q8_0, kf), oracle.quantize(oracle.Q8_0, vf)
+    q = rng.normal(0, 1, (6, H, D)).astype(np.float32)
+    pos = np.array([origin - 3, origin, origin + 17, origin + 350, origin + 699, origin + 5000],
+                   np.int32)
+    ro, rl = oracle.range_attn(oracle.Q8_0, k, v, q, pos, active, origin, H, Hkv, D, 1 / 16,
+                               split=3)
+    for mode in (0, 2, 4):
+        out, lse = xq.attend_range(oracle.Q8_0, torch.from_numpy(k).cuda(),
+                                   torch.from_numpy(v).cuda(), torch.from_numpy(q).cuda(),
+                                   torch.from_numpy(pos).cuda(), Hkv, origin, active, 1 / 16, mode)
+        out, lse = out.cpu().numpy(), lse.cpu().numpy()
+        np.testing.assert_allclose(out, ro, rtol=1e-3, atol=1e-5)
+        assert np.array_equal(np.isneginf(lse), np.isneginf(rl))
+        fin = ~np.isneginf(rl)
+        np.testing.assert_allclose(lse[fin], rl[fin], rtol=1e-5, atol=1e-4)
+
+
+def test_lse_merge_golden_semantics():
+    xq = _xq()
+    g = golden("reduce.npz")
+    names = sorted({k.rsplit("_", 1)[0] for k in g.files if k.endswith("_partials")})
+    for n in names:
+        part = torch.from_numpy(g[n + "_partials"]).cuda()
+        out, lse = xq.lse_merge(part)
+        out, lse = out.cpu().numpy(), lse.cpu().numpy()
+        ro, rl = g[n + "_out"], g[n + "_lse"]
+        assert np.array_equal(np.isnan(out), np.isnan(ro)), n
+        assert np.array_equal(np.isnan(lse), np.isnan(rl)), n
+        fin = ~np.isnan(ro)
+        np.testing.assert_allclose(out[fin], ro[fin], rtol=1e-6, atol=1e-7, err_msg=n)
+        fl = ~np.isnan(rl)
+        np.testing.assert_allclose(lse[fl], rl[fl], rtol=1e-6, atol=1e-6, err_msg=n)
+
+
+def test_partials_merge_equals_flash_attn_and_is_shard_invariant():
+    """Fixed global splits: computing them in 1, 2, 4 or 8 shards and merging
+    in split order gives bit-identical output."""
+    xq = _xq()
+    rng = np.random.default_rng(8)
+    D, H, Hkv, n_kv, n_seq = 256, 24, 4, 8192, 2
+    q = torch.from_numpy(rng.normal(0, 1, (n_seq, H, 1, D)).astype(np.float32)).cuda()
+    kf = rng.normal(0, 1, (n_seq, n_kv, Hkv, D)).astype(np.float32)
+    vf = rng.normal(0, 1, (n_seq, n_kv, Hkv, D)).astype(np.float32)
+    k = torch.from_numpy(oracle.quantize(oracle.Q8_0, kf)).cuda()
+    v = torch.from_numpy(oracle.quantize(oracle.Q8_0, vf)).cuda()
+    rows, n_splits = 256, n_kv // 256
+    ref = None
+    for shards in (1, 2, 4, 8):
+        per = n_splits // shards
+        parts = [xq.fa_partials(q, k, v, oracle.Q8_0, rows, i * per, (i + 1) * per, scale=1 / 16)
+                 for i in range(shards)]
+        out, _ = xq.lse_merge(torch.cat(parts, 0).contiguous())
+        out = out.cpu().numpy()
+        if ref is None:
+            ref = out
+        assert np.array_equal(out.view(np.uint32), ref.view(np.uint32)), shards
+    want = oracle.flash_attn_ext(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), oracle.Q8_0,
+                                 oracle.Q8_0, scale=1 / 16)
+    np.testing.assert_allclose(ref.reshape(want.shape), want, rtol=1e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("ty,key", [(oracle.Q8_0, "q8"), (oracle.Q4_0, "q4")])
+def test_codecs_bit_exact(ty, key):
+    xq = _xq()
+    g = golden("codecs.npz")
+    raw = torch.from_numpy(g[key]).cuda()
+    deq = xq.dequantize_rows(ty, raw.view(g["x"].shape[0], -1), g["x"].shape[1]).cpu().numpy()
+    assert np.array_equal(deq.view(np.uint32), g[key + "_deq"].astype(np.float32).view(np.uint32))
+    q = xq.quantize_rows(ty, torch.from_numpy(g["x"]).cuda()).cpu().numpy()
+    assert np.array_equal(q.reshape(-1), g[key].reshape(-1))
+
+
+def test_f16_codec_bit_exact():
+    xq = _xq()
+    g = golden("codecs.npz")
+    x = g["f16_in"][: (g["f16_in"].size // 32) * 32].reshape(-1, 32)
+    raw = xq.quantize_rows(oracle.F16, torch.from_numpy(x).cuda()).cpu().numpy()
+    bits = raw.view(np.uint16).reshape(-1)
+    assert np.array_equal(bits, g["f16_bits"][: bits.size])
+    back = xq.dequantize_rows(oracle.F16, torch.from_numpy(raw).cuda(), 32).cpu().numpy()
+    assert np.array_equal(back.reshape(-1), bits.view(np.float16).astype(np.float32))

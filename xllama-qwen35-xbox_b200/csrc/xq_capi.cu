@@ -1,0 +1,433 @@
+// extern "C" entry points of libxq_b200.so (declared in include/xq_b200.h):
+// argument contracts, launch planning and error reporting.  No allocation
+// happens here: scratch comes from the caller's workspace.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "xq_common.cuh"
+#include "xq_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_status(cudaError_t e, const char *what) {
+    if (e == cudaSuccess)
+        return XQ_OK;
+    return fail(XQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+bool kv_type_ok(int t) { return t == XQ_TYPE_F16 || t == XQ_TYPE_Q8_0 || t == XQ_TYPE_Q4_0; }
+
+struct FaPlan {
+    xq::DecodeArgs a;
+    xq::DecodeConfig cfg;
+    int D, n_qblocks;
+    int64_t n_rows, n_splits;
+};
+
+// Validate a FLASH_ATTN_EXT call and fill the decode arguments (without
+// choosing splits).
+int fa_prepare(const xq_fa_params *p, FaPlan *pl) {
+    if (!p)
+        return fail(XQ_ERR_INVALID, "flash_attn_ext: null params");
+    const xq_tensor &q = p->q, &k = p->k, &v = p->v, &m = p->mask;
+    if (q.type != XQ_TYPE_F32 || q.nb[0] != 4)
+        return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: q must be F32 with contiguous rows");
+    if (!kv_type_ok(k.type) || k.type != v.type)
+        return fail(XQ_ERR_UNSUPPORTED,
+                    "flash_attn_ext: K/V types %d/%d (supported: equal F16, Q8_0 or Q4_0)",
+                    k.type, v.type);
+    const int64_t D = q.ne[0];
+    if (k.ne[0] != D || v.ne[0] != D || (D != 64 && D != 128 && D != 256))
+        return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: head dim %lld/%lld/%lld",
+                    (long long)D, (long long)k.ne[0], (long long)v.ne[0]);
+    const int64_t n_q = q.ne[1], n_head = q.ne[2], n_seq = q.ne[3];
+    const int64_t n_kv = k.ne[1], n_hkv = k.ne[2];
+    if (v.ne[1] != n_kv || v.ne[2] != n_hkv || n_hkv <= 0 || n_head % n_hkv ||
+        k.ne[3] <= 0 || v.ne[3] <= 0 || n_seq % k.ne[3] || n_seq % v.ne[3] || n_q <= 0)
+        return fail(XQ_ERR_INVALID, "flash_attn_ext: inconsistent q/k/v shapes");
+    if (n_kv > INT32_MAX || n_q * n_head > INT32_MAX)
+        return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: sizes beyond int32");
+    if (!q.data || !k.data || !v.data || !p->dst)
+        return fail(XQ_ERR_INVALID, "flash_attn_ext: null tensor data");
+    if (m.data) {
+        if (m.type != XQ_TYPE_F16 || m.nb[0] != 2 || m.ne[0] < n_kv || m.ne[1] < n_q ||
+            m.ne[2] <= 0 || m.ne[3] <= 0)
+            return fail(XQ_ERR_INVALID, "flash_attn_ext: mask must be F16 [n_kv, >=n_q, ...]");
+    }
+    xq::DecodeArgs &a = pl->a;
+    memset(&a, 0, sizeof(a));
+    a.q = static_cast<const uint8_t *>(q.data);
+    a.q_nb1 = (int64_t)q.nb[1];
+    a.q_nb2 = (int64_t)q.nb[2];
+    a.q_nb3 = (int64_t)q.nb[3];
+    a.k = static_cast<const uint8_t *>(k.data);
+    a.k_nb1 = (int64_t)k.nb[1];
+    a.k_nb2 = (int64_t)k.nb[2];
+    a.k_nb3 = (int64_t)k.nb[3];
+    a.v = static_cast<const uint8_t *>(v.data);
+    a.v_nb1 = (int64_t)v.nb[1];
+    a.v_nb2 = (int64_t)v.nb[2];
+    a.v_nb3 = (int64_t)v.nb[3];
+    if (m.data) {
+        a.mask = static_cast<const uint8_t *>(m.data);
+        a.m_nb1 = (int64_t)m.nb[1];
+        a.m_nb2 = (int64_t)m.nb[2];
+        a.m_nb3 = (int64_t)m.nb[3];
+        a.m_ne2 = (int)m.ne[2];
+        a.m_ne3 = (int)m.ne[3];
+    } else {
+        a.m_ne2 = a.m_ne3 = 1;
+    }
+    a.dst = p->dst;
+    a.sinks = p->sinks;
+    a.n_q = (int)n_q;
+    a.n_head = (int)n_head;
+    a.n_head_kv = (int)n_hkv;
+    a.n_seq = (int)n_seq;
+    a.n_kv = (int)n_kv;
+    a.G = (int)(n_head / n_hkv);
+    a.rk3 = (int)(n_seq / k.ne[3]);
+    a.rv3 = (int)(n_seq / v.ne[3]);
+    a.n_qrows = (int)(n_q * a.G);
+    a.q_convert = 1;
+    a.softcap = p->softcap;
+    a.scale = p->softcap != 0.0f ? p->scale / p->softcap : p->scale;
+    a.alibi = p->max_bias > 0.0f;
+    const uint32_t nh_log2 = 1u << (uint32_t)floor(log2((double)n_head));
+    a.n_head_log2 = (int)nh_log2;
+    a.m0 = powf(2.0f, -(p->max_bias) / (float)nh_log2);
+    a.m1 = powf(2.0f, -(p->max_bias / 2.0f) / (float)nh_log2);
+    if (!xq::decode_config(k.type, (int)D, a.n_qrows, a, &pl->cfg))
+        return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: K/V rows not 4-byte aligned");
+    pl->D = (int)D;
+    pl->n_qblocks = (a.n_qrows + pl->cfg.NR - 1) / pl->cfg.NR;
+    pl->n_rows = n_seq * n_q * n_head;
+    return XQ_OK;
+}
+
+// Automatic split count: about two CTAs per SM in one wave.
+int64_t auto_splits(int64_t n_kv, int64_t ctas_per_split, int64_t min_rows) {
+    const int64_t target = 2 * (int64_t)sm_count();
+    int64_t s = (target + ctas_per_split - 1) / ctas_per_split;
+    const int64_t cap = (n_kv + min_rows - 1) / min_rows;
+    if (s > cap)
+        s = cap;
+    return s < 1 ? 1 : s;
+}
+
+void plan_splits(FaPlan *pl, int64_t requested) {
+    const int64_t n_kv = pl->a.n_kv;
+    const int64_t per = (int64_t)pl->a.n_head_kv * pl->n_qblocks * pl->a.n_seq;
+    int64_t s = requested > 0 ? requested : auto_splits(n_kv, per, 64);
+    if (n_kv == 0)
+        s = 1;
+    int64_t rows = s > 0 ? (n_kv + s - 1) / s : n_kv;
+    if (rows < 1)
+        rows = 1;
+    pl->a.rows_per_split = rows;
+    pl->n_splits = n_kv == 0 ? 1 : (n_kv + rows - 1) / rows;
+}
+
+} // namespace
+
+extern "C" {
+
+const char *xq_version(void) { return "xq_b200 0.1 sm_100a"; }
+
+const char *xq_last_error(void) { return g_last_error.c_str(); }
+
+uint32_t xq_split_k(uint32_t active, uint32_t mode) {
+    if (mode == 0) {
+        const uint32_t k = (active + 255u) / 256u;
+        return k < 1 ? 1 : (k > 32 ? 32 : k);
+    }
+    uint32_t target = 128, max_splits = 128;
+    if (mode == 2) {
+        target = 32;
+        max_splits = 256;
+    } else if (mode == 3) {
+        target = 512;
+        max_splits = 64;
+    }
+    const uint32_t wanted = (active + target - 1) / target;
+    uint32_t k = wanted < max_splits ? wanted : max_splits;
+    if (k > 256)
+        k = 256;
+    return k < 1 ? 1 : k;
+}
+
+size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
+    FaPlan pl;
+    if (fa_prepare(p, &pl) != XQ_OK)
+        return 0;
+    plan_splits(&pl, p->n_splits);
+    if (pl.n_splits <= 1)
+        return 0;
+    return (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * sizeof(float);
+}
+
+int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t stream) {
+    FaPlan pl;
+    int rc = fa_prepare(p, &pl);
+    if (rc)
+        return rc;
+    plan_splits(&pl, p->n_splits);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    dim3 grid((unsigned)pl.n_splits, (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
+              (unsigned)pl.a.n_seq);
+    if (pl.n_splits == 1) {
+        pl.a.direct = 1;
+        return cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "flash_attn_ext decode");
+    }
+    const size_t need = (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * 4;
+    if (!ws || ws_bytes < need)
+        return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes, need);
+    pl.a.direct = 0;
+    pl.a.partials = static_cast<float *>(ws);
+    rc = cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "flash_attn_ext decode");
+    if (rc)
+        return rc;
+    return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p->dst,
+                                        nullptr, p->sinks, pl.a.n_head, st),
+                       "flash_attn_ext merge");
+}
+
+int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_begin,
+                   int64_t split_end, float *partials, xq_stream_t stream) {
+    FaPlan pl;
+    int rc = fa_prepare(p, &pl);
+    if (rc)
+        return rc;
+    if (p->sinks)
+        return fail(XQ_ERR_UNSUPPORTED, "fa_partials: sinks belong to the merge");
+    if (rows_per_split <= 0 || split_begin < 0 || split_end < split_begin || !partials)
+        return fail(XQ_ERR_INVALID, "fa_partials: bad split range");
+    if (split_end == split_begin)
+        return XQ_OK;
+    pl.a.rows_per_split = rows_per_split;
+    pl.a.split_begin = split_begin;
+    pl.a.direct = 0;
+    pl.a.partials = partials;
+    dim3 grid((unsigned)(split_end - split_begin), (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
+              (unsigned)pl.a.n_seq);
+    return cuda_status(xq::launch_decode(pl.a, pl.cfg, grid,
+                                         reinterpret_cast<cudaStream_t>(stream)),
+                       "fa_partials decode");
+}
+
+int xq_lse_merge(const float *partials, int64_t n_splits, int64_t n_rows, int64_t D, float *out,
+                 float *lse, xq_stream_t stream) {
+    if (!partials || !out || n_splits <= 0 || n_rows < 0 || (D != 64 && D != 128 && D != 256))
+        return fail(XQ_ERR_INVALID, "lse_merge: bad arguments (D must be 64/128/256)");
+    return cuda_status(xq::launch_merge(partials, n_splits, n_rows, (int)D, out, lse, nullptr, 1,
+                                        reinterpret_cast<cudaStream_t>(stream)),
+                       "lse_merge");
+}
+
+// ---------------------------------------------------------------------------
+// RKVA range attention.
+
+static int range_prepare(int32_t storage, const void *k, const void *v, uint32_t n_head,
+                         uint32_t n_hkv, uint32_t D, uint32_t origin, uint32_t active,
+                         uint32_t n_tokens, const int32_t *positions, const float *q,
+                         float kq_scale, float *out, float *lse, xq_fa_params *fp, FaPlan *pl) {
+    if (!kv_type_ok(storage))
+        return fail(XQ_ERR_UNSUPPORTED, "attend_range: storage %d", storage);
+    if (!n_tokens || !positions || !q || !out || !lse || !n_hkv || n_head % n_hkv ||
+        (active && (!k || !v)))
+        return fail(XQ_ERR_INVALID, "attend_range: invalid arguments");
+    memset(fp, 0, sizeof(*fp));
+    const uint64_t rec = (uint64_t)xq::rec_bytes(storage, (int)D);
+    fp->q = {XQ_TYPE_F32, 0, q, {D, n_tokens, n_head, 1},
+             {4, (uint64_t)n_head * D * 4, (uint64_t)D * 4, (uint64_t)n_tokens * n_head * D * 4}};
+    const void *kd = active ? k : q; // any valid pointer: no rows are read
+    const void *vd = active ? v : q;
+    fp->k = {storage, 0, kd, {D, active, n_hkv, 1},
+             {0, n_hkv * rec, rec, (uint64_t)active * n_hkv * rec}};
+    fp->v = {storage, 0, vd, {D, active, n_hkv, 1},
+             {0, n_hkv * rec, rec, (uint64_t)active * n_hkv * rec}};
+    fp->dst = out;
+    fp->scale = kq_scale;
+    int rc = fa_prepare(fp, pl);
+    if (rc)
+        return rc;
+    pl->a.q_convert = 0;
+    pl->a.positions = positions;
+    pl->a.origin = (int)origin;
+    pl->a.active = (int)active;
+    pl->a.lse = lse;
+    return XQ_OK;
+}
+
+static int64_t range_splits(uint32_t active, uint32_t mode, const FaPlan &pl) {
+    if (mode <= 3)
+        return xq_split_k(active, mode);
+    const int64_t per = (int64_t)pl.a.n_head_kv * pl.n_qblocks;
+    return auto_splits(active, per, 64);
+}
+
+size_t xq_attend_range_workspace(int32_t storage, uint32_t n_tokens, uint32_t active,
+                                 uint32_t n_head, uint32_t n_head_kv, uint32_t head_dim,
+                                 uint32_t split_mode) {
+    if (!n_head_kv || !n_tokens)
+        return 0;
+    const uint32_t G = n_head / n_head_kv;
+    const int NR = n_tokens * G <= 4 ? 4 : n_tokens * G <= 8 ? 8 : 16;
+    FaPlan pl;
+    pl.a.n_head_kv = (int)n_head_kv;
+    pl.n_qblocks = (int)((n_tokens * G + NR - 1) / NR);
+    const int64_t s = range_splits(active, split_mode, pl);
+    if (s <= 1)
+        return 0;
+    (void)storage;
+    return (size_t)s * n_tokens * n_head * (head_dim + 2) * sizeof(float);
+}
+
+int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_head,
+                    uint32_t n_head_kv, uint32_t head_dim, uint32_t origin, uint32_t active,
+                    uint32_t n_tokens, const int32_t *positions, const float *q, float kq_scale,
+                    uint32_t split_mode, float *out, float *lse, void *ws, size_t ws_bytes,
+                    xq_stream_t stream) {
+    xq_fa_params fp;
+    FaPlan pl;
+    int rc = range_prepare(storage, k, v, n_head, n_head_kv, head_dim, origin, active, n_tokens,
+                           positions, q, kq_scale, out, lse, &fp, &pl);
+    if (rc)
+        return rc;
+    if (split_mode > 4)
+        return fail(XQ_ERR_INVALID, "attend_range: split mode %u", split_mode);
+    int64_t s = range_splits(active, split_mode, pl);
+    const int64_t rows = active ? (active + s - 1) / s : 1;
+    pl.a.rows_per_split = rows;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    dim3 grid((unsigned)s, (unsigned)(pl.a.n_head_kv * pl.n_qblocks), 1);
+    if (s == 1) {
+        pl.a.direct = 1;
+        return cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "attend_range decode");
+    }
+    const size_t need = (size_t)s * pl.n_rows * (head_dim + 2) * 4;
+    if (!ws || ws_bytes < need)
+        return fail(XQ_ERR_WORKSPACE, "attend_range: workspace %zu < %zu bytes", ws_bytes, need);
+    pl.a.direct = 0;
+    pl.a.lse = nullptr;
+    pl.a.partials = static_cast<float *>(ws);
+    rc = cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "attend_range decode");
+    if (rc)
+        return rc;
+    return cuda_status(xq::launch_merge(pl.a.partials, s, pl.n_rows, (int)head_dim, out, lse,
+                                        nullptr, 1, st),
+                       "attend_range merge");
+}
+
+// ---------------------------------------------------------------------------
+// GATED_DELTA_NET.
+
+int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                       const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                       float *dst, int32_t slots, xq_stream_t stream) {
+    if (!q || !k || !v || !g || !beta || !state || !dst)
+        return fail(XQ_ERR_INVALID, "gated_delta_net: null argument");
+    const xq_tensor *all[6] = {q, k, v, g, beta, state};
+    for (int i = 0; i < 6; ++i) {
+        if (all[i]->type != XQ_TYPE_F32 || !all[i]->data)
+            return fail(XQ_ERR_UNSUPPORTED, "gated_delta_net: src %d must be F32", i);
+        if (all[i]->nb[0] != 4 && all[i]->ne[0] != 1)
+            return fail(XQ_ERR_UNSUPPORTED, "gated_delta_net: src %d rows not contiguous", i);
+    }
+    const int64_t S = v->ne[0], H = v->ne[1], T = v->ne[2], n_seq = v->ne[3];
+    const int64_t H_k = q->ne[1];
+    if (S != 128)
+        return fail(XQ_ERR_UNSUPPORTED, "gated_delta_net: head size %lld (supported: 128)",
+                    (long long)S);
+    if (q->ne[0] != S || k->ne[0] != S || k->ne[1] != H_k || H_k <= 0 || H % H_k ||
+        q->ne[2] != T || k->ne[2] != T || q->ne[3] <= 0 || k->ne[3] <= 0 || n_seq % q->ne[3] ||
+        n_seq % k->ne[3] || T <= 0)
+        return fail(XQ_ERR_INVALID, "gated_delta_net: inconsistent q/k/v shapes");
+    for (const xq_tensor *gt : {g, beta})
+        if (gt->ne[0] != 1 || gt->ne[1] != H || gt->ne[2] != T || gt->ne[3] != n_seq)
+            return fail(XQ_ERR_UNSUPPORTED,
+                        "gated_delta_net: gates must be scalar per head [1, H, T, n_seq]");
+    if (state->ne[0] != S || state->ne[1] != S || state->ne[2] != H || state->ne[3] != n_seq)
+        return fail(XQ_ERR_INVALID, "gated_delta_net: state must be [S, S, H, n_seq]");
+    if (slots < 1 || slots > 64)
+        return fail(XQ_ERR_INVALID, "gated_delta_net: slots %d outside [1, 64]", slots);
+    if (H * n_seq > 65535 * 64)
+        return fail(XQ_ERR_UNSUPPORTED, "gated_delta_net: too many heads x sequences");
+    xq::GdnArgs a;
+    a.q = static_cast<const float *>(q->data);
+    a.k = static_cast<const float *>(k->data);
+    a.v = static_cast<const float *>(v->data);
+    a.g = static_cast<const float *>(g->data);
+    a.beta = static_cast<const float *>(beta->data);
+    a.state = static_cast<const float *>(state->data);
+    a.q_nb1 = (int64_t)q->nb[1]; a.q_nb2 = (int64_t)q->nb[2]; a.q_nb3 = (int64_t)q->nb[3];
+    a.k_nb1 = (int64_t)k->nb[1]; a.k_nb2 = (int64_t)k->nb[2]; a.k_nb3 = (int64_t)k->nb[3];
+    a.v_nb1 = (int64_t)v->nb[1]; a.v_nb2 = (int64_t)v->nb[2]; a.v_nb3 = (int64_t)v->nb[3];
+    a.g_nb1 = (int64_t)g->nb[1]; a.g_nb2 = (int64_t)g->nb[2]; a.g_nb3 = (int64_t)g->nb[3];
+    a.b_nb1 = (int64_t)beta->nb[1]; a.b_nb2 = (int64_t)beta->nb[2]; a.b_nb3 = (int64_t)beta->nb[3];
+    a.s_nb1 = (int64_t)state->nb[1]; a.s_nb2 = (int64_t)state->nb[2];
+    a.s_nb3 = (int64_t)state->nb[3];
+    a.dst = dst;
+    a.H = (int)H;
+    a.H_k = (int)H_k;
+    a.T = (int)T;
+    a.n_seq = (int)n_seq;
+    a.rq3 = (int)(n_seq / q->ne[3]);
+    a.rk3 = (int)(n_seq / k->ne[3]);
+    a.slots = slots;
+    a.scale = 1.0f / sqrtf((float)S);
+    return cuda_status(xq::launch_gdn(a, reinterpret_cast<cudaStream_t>(stream)),
+                       "gated_delta_net");
+}
+
+// ---------------------------------------------------------------------------
+// Codecs.
+
+int xq_dequantize_rows(int32_t type, const void *src, uint64_t src_row_stride, float *dst,
+                       uint64_t dst_row_stride, int64_t n_rows, int64_t n_per_row,
+                       xq_stream_t stream) {
+    if (!kv_type_ok(type))
+        return fail(XQ_ERR_UNSUPPORTED, "dequantize_rows: type %d", type);
+    if (!src || !dst || n_rows < 0 || n_per_row <= 0 || (type != XQ_TYPE_F16 && n_per_row % 32))
+        return fail(XQ_ERR_INVALID, "dequantize_rows: bad arguments");
+    return cuda_status(xq::launch_dequant(type, src, src_row_stride, dst, dst_row_stride, n_rows,
+                                          n_per_row, reinterpret_cast<cudaStream_t>(stream)),
+                       "dequantize_rows");
+}
+
+int xq_quantize_rows(int32_t type, const float *src, uint64_t src_row_stride, void *dst,
+                     uint64_t dst_row_stride, int64_t n_rows, int64_t n_per_row,
+                     xq_stream_t stream) {
+    if (!kv_type_ok(type))
+        return fail(XQ_ERR_UNSUPPORTED, "quantize_rows: type %d", type);
+    if (!src || !dst || n_rows < 0 || n_per_row <= 0 || (type != XQ_TYPE_F16 && n_per_row % 32))
+        return fail(XQ_ERR_INVALID, "quantize_rows: bad arguments");
+    return cuda_status(xq::launch_quant(type, src, src_row_stride, dst, dst_row_stride, n_rows,
+                                        n_per_row, reinterpret_cast<cudaStream_t>(stream)),
+                       "quantize_rows");
+}
+
+} // extern "C"

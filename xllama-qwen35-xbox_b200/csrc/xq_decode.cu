@@ -1,0 +1,583 @@
+// Split-KV flash decode over F16 / Q8_0 / Q4_0 KV caches, and the fixed-order
+// log-sum-exp merge of split partials.
+//
+// Semantics (ggml-cpu FLASH_ATTN_EXT, patches/0008 context lines 4-35 and the
+// split-KV branch of patches/0006 lines 7-14; RKVA range partials
+// shaders/rkva/rkva_range_attn.hlsl:59-106 and reducer
+// rkva_range_reduce_opt.hlsl:26-133):
+//   * q is first converted to K's dot type (F16 for F16 K, Q8_0 for Q8_0/Q4_0
+//     K) when q_convert is set; the RKVA entry uses raw F32 q;
+//   * s = (q . k) * scale, softcap, + slope * mask; masked (-inf) rows skip;
+//   * GQA: q head h reads kv head h / (n_head / n_head_kv);
+//   * KV values are dequantised exactly in registers; products and sums are
+//     fp32 (the float accumulation the target tolerance is written for).
+//
+// Layout of work: one CTA = (split of KV rows, kv head, block of NR q-rows,
+// sequence).  The NR q-rows are the (query, head) pairs that share the kv
+// head, so every K/V byte is read once for all of them.  K/V tiles of R rows
+// stream into shared memory through a 2-stage cp.async pipeline; scores use
+// LPR lanes per row (dims interleaved in 4-dim chunks) and warp shuffles; the
+// PV product gives each thread 4 dims x NR q-rows over a group of rows.
+#include <float.h>
+#include <math.h>
+
+#include "xq_common.cuh"
+#include "xq_internal.h"
+
+namespace xq {
+
+constexpr int kThreads = 256;
+
+template <int T, int D, int NR, int R, int VW>
+__global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs a) {
+    constexpr int REC = rec_bytes(T, D);
+    constexpr int SS = smem_stride(REC);
+    constexpr int NCH = D / 4;          // 4-dim chunks per row
+    constexpr int LPR = kThreads / R;   // score lanes per row
+    constexpr int NRG = kThreads / NCH; // PV row groups
+    constexpr int RPG = R / NRG;        // rows per PV group
+    constexpr int VPR = REC / VW;       // copy vectors per row
+    constexpr int NW = kThreads / 32;
+    static_assert(REC % VW == 0, "row bytes must split into copy vectors");
+    static_assert(NCH % LPR == 0 && R % NRG == 0, "tile shape");
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t *kbuf = smem;                                      // [2][R][SS]
+    uint8_t *vbuf = kbuf + 2 * R * SS;                         // [2][R][SS]
+    float *q_s = reinterpret_cast<float *>(vbuf + 2 * R * SS); // [NR][D]
+    float *p_s = q_s + NR * D;                                 // [R][NR]
+    float *red = p_s + R * NR;                                 // [NW][NR]
+    float *m_s = red + NW * NR;                                // [NR]
+    float *l_s = m_s + NR;                                     // [NR]
+    float *al_s = l_s + NR;                                    // [NR]
+    float *slope_s = al_s + NR;                                // [NR]
+    int64_t *moff_s = reinterpret_cast<int64_t *>(slope_s + NR); // [NR]
+    int *lim_s = reinterpret_cast<int *>(moff_s + NR);         // [NR]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kvh = blockIdx.y % a.n_head_kv;
+    const int qb = blockIdx.y / a.n_head_kv;
+    const int s = blockIdx.z;
+    const int64_t split = a.split_begin + blockIdx.x;
+    const int64_t r0 = split * a.rows_per_split;
+    const int64_t r1 = min((int64_t)a.n_kv, r0 + a.rows_per_split);
+    const int jbase = qb * NR;
+    const int nj = min(NR, a.n_qrows - jbase);
+
+    const uint8_t *kbase = a.k + (int64_t)kvh * a.k_nb2 + (int64_t)(s / a.rk3) * a.k_nb3;
+    const uint8_t *vbase = a.v + (int64_t)kvh * a.v_nb2 + (int64_t)(s / a.rv3) * a.v_nb3;
+
+    auto load_tile = [&](int stage, int64_t t0) {
+        const int nrows = (int)min((int64_t)R, r1 - t0);
+        uint8_t *kd = kbuf + stage * R * SS;
+        uint8_t *vd = vbuf + stage * R * SS;
+        for (int idx = tid; idx < nrows * VPR; idx += kThreads) {
+            const int r = idx / VPR, c = idx - r * VPR;
+            cp_async<VW>(smem_u32(kd + r * SS + c * VW), kbase + (t0 + r) * a.k_nb1 + c * VW);
+            cp_async<VW>(smem_u32(vd + r * SS + c * VW), vbase + (t0 + r) * a.v_nb1 + c * VW);
+        }
+    };
+
+    if (r0 < r1)
+        load_tile(0, r0);
+    cp_async_commit();
+
+    // ---- prologue: q rows (converted to K's dot type), per-row constants ----
+    for (int j = tid; j < NR; j += kThreads) {
+        m_s[j] = -INFINITY;
+        l_s[j] = 0.0f;
+        float slope = 1.0f;
+        int64_t moff = 0;
+        int lim = a.n_kv;
+        if (j < nj) {
+            const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+            if (a.alibi)
+                slope = h < a.n_head_log2 ? powf(a.m0, (float)(h + 1))
+                                          : powf(a.m1, (float)(2 * (h - a.n_head_log2) + 1));
+            moff = (int64_t)iq1 * a.m_nb1 + (int64_t)(h % a.m_ne2) * a.m_nb2 +
+                   (int64_t)(s % a.m_ne3) * a.m_nb3;
+            if (a.positions) {
+                const int pos = a.positions[iq1];
+                lim = pos < a.origin ? 0 : min(a.active, pos - a.origin + 1);
+            }
+        }
+        slope_s[j] = slope;
+        moff_s[j] = moff;
+        lim_s[j] = lim;
+    }
+    if (!a.q_convert || T == kF16) {
+        for (int idx = tid; idx < NR * D; idx += kThreads) {
+            const int j = idx / D, d = idx - j * D;
+            float x = 0.0f;
+            if (j < nj) {
+                const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+                x = *reinterpret_cast<const float *>(a.q + (int64_t)iq1 * a.q_nb1 +
+                                                     (int64_t)h * a.q_nb2 +
+                                                     (int64_t)s * a.q_nb3 + 4 * d);
+                if (a.q_convert)
+                    x = __half2float(__float2half_rn(x));
+            }
+            q_s[idx] = x;
+        }
+    } else {
+        // ggml quantize_row_q8_0 reference arithmetic, one warp per 32-block.
+        for (int blk = warp; blk < NR * (D / 32); blk += NW) {
+            const int j = blk / (D / 32), b = blk - j * (D / 32);
+            float x = 0.0f;
+            if (j < nj) {
+                const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+                x = *reinterpret_cast<const float *>(a.q + (int64_t)iq1 * a.q_nb1 +
+                                                     (int64_t)h * a.q_nb2 +
+                                                     (int64_t)s * a.q_nb3 + 4 * (b * 32 + lane));
+            }
+            const float amax = warp_max(fabsf(x));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            const float qi = roundf(x * id);
+            q_s[j * D + b * 32 + lane] = qi * __half2float(__float2half_rn(d));
+        }
+    }
+    __syncthreads();
+
+    // ---- main loop over R-row tiles ----
+    const int row = tid / LPR, ql = tid % LPR;      // score mapping
+    const int pc = tid % NCH, rg = tid / NCH;        // PV mapping
+    float acc[NR][4];
+#pragma unroll
+    for (int j = 0; j < NR; ++j)
+        acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+
+    int stage = 0;
+    for (int64_t t0 = r0; t0 < r1; t0 += R, stage ^= 1) {
+        if (t0 + R < r1)
+            load_tile(stage ^ 1, t0 + R);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+
+        const uint8_t *ktile = kbuf + stage * R * SS;
+        const uint8_t *vtile = vbuf + stage * R * SS;
+        const int64_t grow = t0 + row;
+        const bool rvalid = grow < r1;
+
+        float sc[NR];
+#pragma unroll
+        for (int j = 0; j < NR; ++j)
+            sc[j] = 0.0f;
+        if (rvalid) {
+            const uint8_t *krow = ktile + row * SS;
+#pragma unroll 4
+            for (int cc = 0; cc < NCH / LPR; ++cc) {
+                const int c = cc * LPR + ql;
+                float kx[4];
+                load4<T>(krow, c, kx);
+#pragma unroll
+                for (int j = 0; j < NR; ++j) {
+                    const float4 qq = *reinterpret_cast<const float4 *>(q_s + j * D + 4 * c);
+                    sc[j] = fmaf(qq.x, kx[0], sc[j]);
+                    sc[j] = fmaf(qq.y, kx[1], sc[j]);
+                    sc[j] = fmaf(qq.z, kx[2], sc[j]);
+                    sc[j] = fmaf(qq.w, kx[3], sc[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < NR; ++j) {
+#pragma unroll
+            for (int o = 1; o < LPR; o <<= 1)
+                sc[j] += __shfl_xor_sync(0xffffffffu, sc[j], o);
+            float x = sc[j] * a.scale;
+            if (a.softcap != 0.0f)
+                x = a.softcap * tanhf(x);
+            if (a.mask && rvalid) {
+                const float mv = slope_s[j] * __half2float(*reinterpret_cast<const __half *>(
+                                                  a.mask + moff_s[j] + 2 * grow));
+                x = mv == -INFINITY ? -INFINITY : x + mv;
+            }
+            if (!rvalid || j >= nj || grow >= lim_s[j])
+                x = -INFINITY;
+            sc[j] = x;
+        }
+        // tile max per q-row: over the rows of this warp, then across warps
+#pragma unroll
+        for (int j = 0; j < NR; ++j) {
+            float mx = sc[j];
+#pragma unroll
+            for (int o = LPR; o < 32; o <<= 1)
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0)
+                red[warp * NR + j] = mx;
+        }
+        __syncthreads();
+        if (tid < NR) {
+            float mt = red[tid];
+#pragma unroll
+            for (int w = 1; w < NW; ++w)
+                mt = fmaxf(mt, red[w * NR + tid]);
+            const float mo = m_s[tid];
+            const float mn = fmaxf(mo, mt);
+            al_s[tid] = mo == -INFINITY ? (mn == -INFINITY ? 1.0f : 0.0f) : expf(mo - mn);
+            m_s[tid] = mn;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < NR; ++j) {
+            const float p = sc[j] == -INFINITY ? 0.0f : expf(sc[j] - m_s[j]);
+            if (ql == (j % LPR))
+                p_s[row * NR + j] = p;
+            float sum = p;
+#pragma unroll
+            for (int o = LPR; o < 32; o <<= 1)
+                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            sc[j] = sum;
+        }
+        __syncthreads(); // red (max) fully consumed before reuse as sums
+        if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < NR; ++j)
+                red[warp * NR + j] = sc[j];
+        }
+        __syncthreads();
+        if (tid < NR) {
+            float lt = red[tid];
+#pragma unroll
+            for (int w = 1; w < NW; ++w)
+                lt += red[w * NR + tid];
+            l_s[tid] = l_s[tid] * al_s[tid] + lt;
+        }
+        // PV
+#pragma unroll
+        for (int j = 0; j < NR; ++j) {
+            const float al = al_s[j];
+            acc[j][0] *= al;
+            acc[j][1] *= al;
+            acc[j][2] *= al;
+            acc[j][3] *= al;
+        }
+        const int nrows = (int)min((int64_t)R, r1 - t0);
+#pragma unroll 2
+        for (int rr = 0; rr < RPG; ++rr) {
+            const int r = rg * RPG + rr;
+            if (r < nrows) {
+                float vx[4];
+                load4<T>(vtile + r * SS, pc, vx);
+#pragma unroll
+                for (int j = 0; j < NR; ++j) {
+                    const float p = p_s[r * NR + j];
+                    acc[j][0] = fmaf(p, vx[0], acc[j][0]);
+                    acc[j][1] = fmaf(p, vx[1], acc[j][1]);
+                    acc[j][2] = fmaf(p, vx[2], acc[j][2]);
+                    acc[j][3] = fmaf(p, vx[3], acc[j][3]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    // ---- epilogue: combine PV row groups in a fixed order ----
+    float *obuf = reinterpret_cast<float *>(kbuf); // [NR][D], aliases stage buffers
+    for (int g = NRG - 1; g >= 1; --g) {
+        if (rg == g) {
+#pragma unroll
+            for (int j = 0; j < NR; ++j) {
+                float4 *o = reinterpret_cast<float4 *>(obuf + j * D + 4 * pc);
+                if (g == NRG - 1) {
+                    *o = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+                } else {
+                    float4 t = *o;
+                    *o = make_float4(t.x + acc[j][0], t.y + acc[j][1], t.z + acc[j][2],
+                                     t.w + acc[j][3]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (rg != 0)
+        return;
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+        if (j >= nj)
+            break;
+        float o[4];
+        if (NRG > 1) {
+            const float4 t = *reinterpret_cast<const float4 *>(obuf + j * D + 4 * pc);
+            o[0] = t.x + acc[j][0];
+            o[1] = t.y + acc[j][1];
+            o[2] = t.z + acc[j][2];
+            o[3] = t.w + acc[j][3];
+        } else {
+            o[0] = acc[j][0];
+            o[1] = acc[j][1];
+            o[2] = acc[j][2];
+            o[3] = acc[j][3];
+        }
+        const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+        const int64_t orow = ((int64_t)s * a.n_q + iq1) * a.n_head + h;
+        float m = m_s[j], l = l_s[j];
+        if (a.direct) {
+            if (a.sinks) {
+                const float sk = a.sinks[h];
+                if (sk > m) {
+                    const float ms = expf(m - sk);
+                    o[0] *= ms;
+                    o[1] *= ms;
+                    o[2] *= ms;
+                    o[3] *= ms;
+                    l = l * ms + 1.0f;
+                    m = sk;
+                } else {
+                    l += expf(sk - m);
+                }
+            }
+            const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+            *reinterpret_cast<float4 *>(a.dst + orow * D + 4 * pc) =
+                make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+            if (a.lse && pc == 0)
+                a.lse[orow] = l == 0.0f ? -INFINITY : m + logf(l);
+        } else {
+            float *rec = a.partials + ((split - a.split_begin) * (int64_t)a.n_seq * a.n_q *
+                                           a.n_head + orow) * (D + 2);
+            rec[4 * pc + 0] = o[0];
+            rec[4 * pc + 1] = o[1];
+            rec[4 * pc + 2] = o[2];
+            rec[4 * pc + 3] = o[3];
+            if (pc == 0) {
+                rec[D] = l == 0.0f ? -FLT_MAX : m;
+                rec[D + 1] = l;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// LSE merge: one CTA per output row, fixed split order for every reduction.
+template <int D>
+__global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict__ part,
+                                                        int64_t n_splits, int64_t n_rows,
+                                                        float *__restrict__ out,
+                                                        float *__restrict__ lse,
+                                                        const float *__restrict__ sinks,
+                                                        int n_head) {
+    constexpr int NT = 128, DPT = (D + NT - 1) / NT;
+    constexpr int CACHE = 2048;
+    __shared__ float w_s[CACHE];
+    __shared__ float red[NT / 32];
+    __shared__ int bad_s;
+    const int tid = threadIdx.x;
+    const int64_t row = blockIdx.x;
+    const int64_t stride = (int64_t)n_rows * (D + 2);
+    const float *base = part + row * (D + 2);
+    if (tid == 0)
+        bad_s = 0;
+    __syncthreads();
+
+    // pass 1: maximum over participating splits, invalid-state detection
+    float mx = -FLT_MAX;
+    int bad = 0;
+    for (int64_t s = tid; s < n_splits; s += NT) {
+        const float m = base[s * stride + D], den = base[s * stride + D + 1];
+        if (den == 0.0f)
+            continue;
+        if (!isfinite(den) || den < 0.0f || !isfinite(m))
+            bad = 1;
+        else
+            mx = fmaxf(mx, m);
+    }
+    mx = warp_max(mx);
+    if ((tid & 31) == 0)
+        red[tid >> 5] = mx;
+    if (bad)
+        atomicOr(&bad_s, 1);
+    __syncthreads();
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; ++w)
+        M = fmaxf(M, red[w]);
+    __syncthreads();
+
+    // pass 2: weights and the denominator (fixed per-thread order + fixed tree)
+    float lsum = 0.0f;
+    for (int64_t s = tid; s < n_splits; s += NT) {
+        const float m = base[s * stride + D], den = base[s * stride + D + 1];
+        const float w = den != 0.0f ? expf(m - M) : 0.0f;
+        if (s < CACHE)
+            w_s[s] = w;
+        if (den != 0.0f)
+            lsum += den * w;
+    }
+    lsum = warp_sum(lsum);
+    if ((tid & 31) == 0)
+        red[tid >> 5] = lsum;
+    __syncthreads();
+    float L = red[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; ++w)
+        L += red[w];
+
+    // pass 3: numerators in split order
+    float acc[DPT];
+#pragma unroll
+    for (int i = 0; i < DPT; ++i)
+        acc[i] = 0.0f;
+    int badn = 0;
+    for (int64_t s = 0; s < n_splits; ++s) {
+        const float *rec = base + s * stride;
+        const float den = rec[D + 1];
+        if (den == 0.0f)
+            continue;
+        const float w = s < CACHE ? w_s[s] : expf(rec[D] - M);
+#pragma unroll
+        for (int i = 0; i < DPT; ++i) {
+            const int d = tid + i * NT;
+            if (d < D) {
+                const float x = rec[d];
+                badn |= !isfinite(x);
+                acc[i] = fmaf(x, w, acc[i]);
+            }
+        }
+    }
+    if (sinks) {
+        const float sk = sinks[row % n_head];
+        if (L == 0.0f || sk > M) {
+            const float ms = L == 0.0f ? 0.0f : expf(M - sk);
+#pragma unroll
+            for (int i = 0; i < DPT; ++i)
+                acc[i] *= ms;
+            L = L * ms + 1.0f;
+            M = sk;
+        } else {
+            L += expf(sk - M);
+        }
+    }
+    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+    float l = L == 0.0f ? -INFINITY : M + logf(L);
+    if (!isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l)))
+        badn = 1;
+#pragma unroll
+    for (int i = 0; i < DPT; ++i)
+        badn |= !isfinite(acc[i] * inv);
+    if (badn)
+        atomicOr(&bad_s, 1);
+    __syncthreads();
+    const bool poison = bad_s != 0;
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) {
+        const int d = tid + i * NT;
+        if (d < D)
+            out[row * D + d] = poison ? NAN : acc[i] * inv;
+    }
+    if (lse && tid == 0)
+        lse[row] = poison ? NAN : l;
+}
+
+// ---------------------------------------------------------------------------
+// Host side: configuration and launch.
+
+template <int T, int D, int NR, int R, int VW>
+static cudaError_t launch_one(const DecodeArgs &a, size_t smem, dim3 grid, cudaStream_t st) {
+    auto kern = fa_decode_kernel<T, D, NR, R, VW>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess)
+            return e;
+        attr_set = true;
+    }
+    kern<<<grid, kThreads, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+static size_t decode_smem(int type, int D, int NR, int R) {
+    const int SS = smem_stride(rec_bytes(type, D));
+    size_t b = (size_t)4 * R * SS;                   // K, V x 2 stages
+    b += (size_t)NR * D * 4 + (size_t)R * NR * 4;     // q, p
+    b += (size_t)(kThreads / 32) * NR * 4 + 4 * NR * 4; // red, m, l, alpha, slope
+    b += (size_t)NR * 8 + (size_t)NR * 4;             // mask offsets, limits
+    const size_t ob = (size_t)NR * D * 4;             // epilogue aliases K stages
+    if (ob > (size_t)2 * R * SS)
+        b += ob;
+    return b;
+}
+
+bool decode_config(int type, int D, int n_qrows, const DecodeArgs &a, DecodeConfig *cfg) {
+    if (type != kF16 && type != kQ8 && type != kQ4)
+        return false;
+    if (D != 64 && D != 128 && D != 256)
+        return false;
+    cfg->type = type;
+    cfg->D = D;
+    cfg->NR = n_qrows <= 4 ? 4 : n_qrows <= 8 ? 8 : 16;
+    cfg->R = smem_stride(rec_bytes(type, D)) > 288 ? 32 : 64;
+    // widest cp.async that every row start and the row length allow
+    const uint64_t rec = (uint64_t)rec_bytes(type, D);
+    const uint64_t align = (uint64_t)(uintptr_t)a.k | (uint64_t)(uintptr_t)a.v |
+                           (uint64_t)a.k_nb1 | (uint64_t)a.k_nb2 | (uint64_t)a.k_nb3 |
+                           (uint64_t)a.v_nb1 | (uint64_t)a.v_nb2 | (uint64_t)a.v_nb3 | rec;
+    cfg->VW = (align % 16 == 0) ? 16 : (align % 8 == 0) ? 8 : (align % 4 == 0) ? 4 : 0;
+    if (!cfg->VW)
+        return false;
+    cfg->smem = decode_smem(type, D, cfg->NR, cfg->R);
+    return true;
+}
+
+template <int T, int D, int NR, int R>
+static cudaError_t dispatch_vw(const DecodeArgs &a, const DecodeConfig &c, dim3 g,
+                               cudaStream_t st) {
+    if constexpr (rec_bytes(T, D) % 16 == 0)
+        if (c.VW == 16)
+            return launch_one<T, D, NR, R, 16>(a, c.smem, g, st);
+    if constexpr (rec_bytes(T, D) % 8 == 0)
+        if (c.VW >= 8)
+            return launch_one<T, D, NR, R, 8>(a, c.smem, g, st);
+    return launch_one<T, D, NR, R, 4>(a, c.smem, g, st);
+}
+
+template <int T, int D>
+static cudaError_t dispatch_nr(const DecodeArgs &a, const DecodeConfig &c, dim3 g,
+                               cudaStream_t st) {
+    constexpr int R = smem_stride(rec_bytes(T, D)) > 288 ? 32 : 64;
+    switch (c.NR) {
+    case 4: return dispatch_vw<T, D, 4, R>(a, c, g, st);
+    case 8: return dispatch_vw<T, D, 8, R>(a, c, g, st);
+    default: return dispatch_vw<T, D, 16, R>(a, c, g, st);
+    }
+}
+
+template <int T>
+static cudaError_t dispatch_d(const DecodeArgs &a, const DecodeConfig &c, dim3 g,
+                              cudaStream_t st) {
+    switch (c.D) {
+    case 64: return dispatch_nr<T, 64>(a, c, g, st);
+    case 128: return dispatch_nr<T, 128>(a, c, g, st);
+    default: return dispatch_nr<T, 256>(a, c, g, st);
+    }
+}
+
+cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &c, dim3 grid,
+                          cudaStream_t st) {
+    switch (c.type) {
+    case kF16: return dispatch_d<kF16>(a, c, grid, st);
+    case kQ8: return dispatch_d<kQ8>(a, c, grid, st);
+    default: return dispatch_d<kQ4>(a, c, grid, st);
+    }
+}
+
+cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
+                         float *out, float *lse, const float *sinks, int n_head,
+                         cudaStream_t st) {
+    if (n_rows <= 0)
+        return cudaSuccess;
+    dim3 grid((unsigned)n_rows);
+    switch (D) {
+    case 64: lse_merge_kernel<64><<<grid, 128, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 128: lse_merge_kernel<128><<<grid, 128, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 256: lse_merge_kernel<256><<<grid, 128, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+} // namespace xq

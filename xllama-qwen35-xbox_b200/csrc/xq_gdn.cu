@@ -1,0 +1,219 @@
+// GATED_DELTA_NET, recurrent form (any T, K rollback slots, n_seq >= 1).
+//
+// Per (sequence, value head h) with state S[col][i] (col = value dim, i = key
+// dim), for each token t (ggml-cpu GATED_DELTA_NET; the fork's host mirror
+// src/bridge/ggml_d3d12.cpp:113-158 and shaders/ggml_d3d12_gated_delta_net.hlsl:40-86):
+//   S   <- exp(g_t) * S
+//   d   =  (v_t[col] - sum_i S[col][i] k_t[i]) * beta_t
+//   S[col][:] += k_t * d
+//   y_t[col] = (sum_i S[col][i] q_t[i]) / sqrt(S_k)
+// with key head h % H_k.  Columns are independent, so a CTA owns CB columns
+// of one (sequence, head) and keeps them in registers for all T tokens.  Eight
+// lanes share a column; lane l holds elements i = l + 8e, accumulates its
+// partial dot in increasing i and the eight partials meet in the tree
+// (l, l+4), (l, l+2), (l, l+1) -- the order of the reference mirror's
+// eight-lane reduction -- with explicit round-to-nearest multiplies and adds
+// (no FMA contraction).  exp(g) is evaluated in double and rounded once.
+#include "xq_common.cuh"
+#include "xq_internal.h"
+
+namespace xq {
+
+template <int S, int CB>
+__global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) {
+    constexpr int TPC = 8;       // lanes per column
+    constexpr int EPT = S / TPC; // elements per lane
+    const int unit = blockIdx.x;
+    const int h = unit % a.H, seq = unit / a.H;
+    const int col = blockIdx.y * CB + threadIdx.x / TPC;
+    const int l = threadIdx.x % TPC;
+    const int hk = h % a.H_k;
+    const int sq = seq / a.rq3, sk = seq / a.rk3;
+
+    const char *st_row = reinterpret_cast<const char *>(a.state) + seq * a.s_nb3 +
+                         (int64_t)h * a.s_nb2 + (int64_t)col * a.s_nb1;
+    float st[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e)
+        st[e] = reinterpret_cast<const float *>(st_row)[l + TPC * e];
+
+    const size_t slot_elems = (size_t)S * S * a.H * a.n_seq;
+    float *snap = a.dst + (size_t)S * a.H * a.T * a.n_seq;
+    const size_t snap_off = ((size_t)(seq * a.H + h) * S + col) * S;
+
+    auto ptr = [](const float *base, int64_t o) {
+        return reinterpret_cast<const float *>(reinterpret_cast<const char *>(base) + o);
+    };
+    const float *qb = ptr(a.q, sq * a.q_nb3 + hk * a.q_nb1);
+    const float *kb = ptr(a.k, sk * a.k_nb3 + hk * a.k_nb1);
+    const float *vb = ptr(a.v, seq * a.v_nb3 + h * a.v_nb1);
+    const float *gb = ptr(a.g, seq * a.g_nb3 + h * a.g_nb1);
+    const float *bb = ptr(a.beta, seq * a.b_nb3 + h * a.b_nb1);
+
+    for (int t = 0; t < a.T; ++t) {
+        const float *qt = ptr(qb, t * a.q_nb2);
+        const float *kt = ptr(kb, t * a.k_nb2);
+        float kx[EPT], qx[EPT];
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            kx[e] = __ldg(kt + l + TPC * e);
+            qx[e] = __ldg(qt + l + TPC * e);
+        }
+        const float vv = __ldg(ptr(vb, t * a.v_nb2) + col);
+        const float gg = __ldg(ptr(gb, t * a.g_nb2));
+        const float beta = __ldg(ptr(bb, t * a.b_nb2));
+        const float decay = (float)exp((double)gg);
+
+        float kv = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            st[e] = __fmul_rn(st[e], decay);
+            kv = __fadd_rn(kv, __fmul_rn(st[e], kx[e]));
+        }
+        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 4));
+        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 2));
+        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 1));
+        const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
+        float at = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            st[e] = __fadd_rn(st[e], __fmul_rn(kx[e], delta));
+            at = __fadd_rn(at, __fmul_rn(st[e], qx[e]));
+        }
+        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 4));
+        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 2));
+        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 1));
+        if (l == 0)
+            a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = __fmul_rn(at, a.scale);
+
+        const int slot = a.T - 1 - t;
+        if ((a.slots > 1 && slot < a.slots) || (a.slots == 1 && t + 1 == a.T)) {
+            float *o = snap + (size_t)(a.slots == 1 ? 0 : slot) * slot_elems + snap_off;
+#pragma unroll
+            for (int e = 0; e < EPT; ++e)
+                o[l + TPC * e] = st[e];
+        }
+    }
+}
+
+cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st) {
+    constexpr int S = 128, CB = 16;
+    dim3 grid((unsigned)(a.H * a.n_seq), S / CB);
+    gdn_recurrent_kernel<S, CB><<<grid, CB * 8, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Block codecs (ggml-quants.c reference arithmetic; one thread per 32-block).
+
+template <int T>
+__global__ void dequant_kernel(const uint8_t *__restrict__ src, uint64_t ss,
+                               float *__restrict__ dst, uint64_t ds, int64_t n_rows,
+                               int64_t n_per_row) {
+    const int64_t nb = T == kF16 ? n_per_row : n_per_row / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * nb)
+        return;
+    const int64_t r = i / nb, b = i - r * nb;
+    const uint8_t *s = src + r * ss;
+    float *d = reinterpret_cast<float *>(reinterpret_cast<char *>(dst) + r * ds);
+    if constexpr (T == kF16) {
+        d[b] = h2f_bits(*reinterpret_cast<const uint16_t *>(s + 2 * b));
+    } else if constexpr (T == kQ8) {
+        const uint8_t *blk = s + 34 * b;
+        const float sc = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+        for (int j = 0; j < 32; ++j)
+            d[32 * b + j] = (float)(int)(int8_t)blk[2 + j] * sc;
+    } else {
+        const uint8_t *blk = s + 18 * b;
+        const float sc = h2f_bits((uint16_t)(blk[0] | (blk[1] << 8)));
+        for (int j = 0; j < 16; ++j) {
+            d[32 * b + j] = (float)((int)(blk[2 + j] & 15) - 8) * sc;
+            d[32 * b + j + 16] = (float)((int)(blk[2 + j] >> 4) - 8) * sc;
+        }
+    }
+}
+
+template <int T>
+__global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t *__restrict__ dst,
+                             uint64_t ds, int64_t n_rows, int64_t n_per_row) {
+    const int64_t nb = T == kF16 ? n_per_row : n_per_row / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * nb)
+        return;
+    const int64_t r = i / nb, b = i - r * nb;
+    const float *x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(src) + r * ss);
+    uint8_t *y = dst + r * ds;
+    if constexpr (T == kF16) {
+        const uint16_t h = __half_as_ushort(__float2half_rn(x[b]));
+        y[2 * b] = (uint8_t)h;
+        y[2 * b + 1] = (uint8_t)(h >> 8);
+    } else if constexpr (T == kQ8) {
+        const float *xb = x + 32 * b;
+        float amax = 0.0f;
+        for (int j = 0; j < 32; ++j)
+            amax = fmaxf(amax, fabsf(xb[j]));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = __half_as_ushort(__float2half_rn(d));
+        uint8_t *blk = y + 34 * b;
+        blk[0] = (uint8_t)dh;
+        blk[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < 32; ++j)
+            blk[2 + j] = (uint8_t)(int8_t)roundf(__fmul_rn(xb[j], id));
+    } else {
+        const float *xb = x + 32 * b;
+        float amax = 0.0f, vmax = 0.0f;
+        for (int j = 0; j < 32; ++j) {
+            if (amax < fabsf(xb[j])) {
+                amax = fabsf(xb[j]);
+                vmax = xb[j];
+            }
+        }
+        const float d = vmax / -8.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        const uint16_t dh = __half_as_ushort(__float2half_rn(d));
+        uint8_t *blk = y + 18 * b;
+        blk[0] = (uint8_t)dh;
+        blk[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < 16; ++j) {
+            const int lo = min(15, (int)(int8_t)__fadd_rn(__fmul_rn(xb[j], id), 8.5f));
+            const int hi = min(15, (int)(int8_t)__fadd_rn(__fmul_rn(xb[16 + j], id), 8.5f));
+            blk[2 + j] = (uint8_t)(lo | (hi << 4));
+        }
+    }
+}
+
+cudaError_t launch_dequant(int type, const void *src, uint64_t ss, float *dst, uint64_t ds,
+                           int64_t n_rows, int64_t n_per_row, cudaStream_t st) {
+    const int64_t units = n_rows * (type == kF16 ? n_per_row : n_per_row / 32);
+    if (units <= 0)
+        return cudaSuccess;
+    const unsigned blocks = (unsigned)((units + 255) / 256);
+    const uint8_t *s = static_cast<const uint8_t *>(src);
+    switch (type) {
+    case kF16: dequant_kernel<kF16><<<blocks, 256, 0, st>>>(s, ss, dst, ds, n_rows, n_per_row); break;
+    case kQ8: dequant_kernel<kQ8><<<blocks, 256, 0, st>>>(s, ss, dst, ds, n_rows, n_per_row); break;
+    case kQ4: dequant_kernel<kQ4><<<blocks, 256, 0, st>>>(s, ss, dst, ds, n_rows, n_per_row); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant(int type, const float *src, uint64_t ss, void *dst, uint64_t ds,
+                         int64_t n_rows, int64_t n_per_row, cudaStream_t st) {
+    const int64_t units = n_rows * (type == kF16 ? n_per_row : n_per_row / 32);
+    if (units <= 0)
+        return cudaSuccess;
+    const unsigned blocks = (unsigned)((units + 255) / 256);
+    uint8_t *d = static_cast<uint8_t *>(dst);
+    switch (type) {
+    case kF16: quant_kernel<kF16><<<blocks, 256, 0, st>>>(src, ss, d, ds, n_rows, n_per_row); break;
+    case kQ8: quant_kernel<kQ8><<<blocks, 256, 0, st>>>(src, ss, d, ds, n_rows, n_per_row); break;
+    case kQ4: quant_kernel<kQ4><<<blocks, 256, 0, st>>>(src, ss, d, ds, n_rows, n_per_row); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+} // namespace xq

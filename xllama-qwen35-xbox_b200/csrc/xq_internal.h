@@ -1,0 +1,67 @@
+// Internal (C++) interface between the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xq {
+
+// One split-KV decode launch.  Byte strides follow ggml nb[].
+struct DecodeArgs {
+    const uint8_t *q;
+    int64_t q_nb1, q_nb2, q_nb3;
+    const uint8_t *k;
+    int64_t k_nb1, k_nb2, k_nb3;
+    const uint8_t *v;
+    int64_t v_nb1, v_nb2, v_nb3;
+    const uint8_t *mask; // F16 or null
+    int64_t m_nb1, m_nb2, m_nb3;
+    int m_ne2, m_ne3;
+    const int32_t *positions; // RKVA causal limit per query, or null
+    int origin, active;
+    float *dst;      // direct mode: F32 [D, n_head, n_q, n_seq]
+    float *lse;      // direct mode, optional: [n_seq][n_q][n_head]
+    float *partials; // partial mode: [split - split_begin][n_rows][D + 2]
+    const float *sinks; // direct mode only
+    int n_q, n_head, n_head_kv, n_seq, n_kv;
+    int G;          // q heads per kv head
+    int rk3, rv3;   // n_seq / ne3 of k, v
+    int n_qrows;    // n_q * G
+    int64_t rows_per_split, split_begin;
+    int direct;     // 1: single split writes dst; 0: write partial records
+    int q_convert;  // 1: ggml converts q to the K dot type; 0: raw F32 (RKVA)
+    float scale, softcap, m0, m1;
+    int n_head_log2, alibi;
+};
+
+struct DecodeConfig {
+    int type, D, NR, R, VW;
+    size_t smem;
+};
+
+// Pick NR/R/VW/shared memory for a shape; returns false if unsupported.
+bool decode_config(int type, int D, int n_qrows, const DecodeArgs &a, DecodeConfig *cfg);
+cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &cfg, dim3 grid,
+                          cudaStream_t st);
+cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
+                         float *out, float *lse, const float *sinks, int n_head,
+                         cudaStream_t st);
+
+struct GdnArgs {
+    const float *q, *k, *v, *g, *beta, *state;
+    int64_t q_nb1, q_nb2, q_nb3, k_nb1, k_nb2, k_nb3, v_nb1, v_nb2, v_nb3;
+    int64_t g_nb1, g_nb2, g_nb3, b_nb1, b_nb2, b_nb3, s_nb1, s_nb2, s_nb3;
+    float *dst;
+    int H, H_k, T, n_seq, rq3, rk3, slots;
+    float scale;
+};
+cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st);
+
+cudaError_t launch_dequant(int type, const void *src, uint64_t src_stride, float *dst,
+                           uint64_t dst_stride, int64_t n_rows, int64_t n_per_row,
+                           cudaStream_t st);
+cudaError_t launch_quant(int type, const float *src, uint64_t src_stride, void *dst,
+                         uint64_t dst_stride, int64_t n_rows, int64_t n_per_row,
+                         cudaStream_t st);
+
+} // namespace xq

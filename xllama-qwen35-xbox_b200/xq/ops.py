@@ -1,0 +1,208 @@
+"""Op-level wrappers: torch tensors in, one C-ABI call each, torch tensors out.
+
+Layouts follow ggml: a torch tensor's shape is ggml's ne reversed and its byte
+strides are nb reversed, so any strided view (e.g. a permuted KV-cache view) is
+passed through unchanged.  Quantized / F16 KV caches travel as raw uint8
+tensors whose last dim holds the bytes of one row of D elements
+(rows of D/32 blocks: Q8_0 = 34 bytes/block, Q4_0 = 18 bytes/block).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import F16, F32, FaParams, Q4_0, Q8_0, Tensor, check, lib
+
+_BLOCK_BYTES = {F16: 2, Q8_0: 34, Q4_0: 18, F32: 4}
+_BLOCK_ELEMS = {F16: 1, Q8_0: 32, Q4_0: 32, F32: 1}
+_ws_cache: dict = {}
+
+
+def row_bytes(ggml_type: int, n: int) -> int:
+    return n // _BLOCK_ELEMS[ggml_type] * _BLOCK_BYTES[ggml_type]
+
+
+def _stream(stream):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _dense(t: torch.Tensor) -> Tensor:
+    """float32 / float16 torch tensor (<= 4 dims) -> ggml view."""
+    assert t.is_cuda, "device tensor expected"
+    ty = {torch.float32: F32, torch.float16: F16}[t.dtype]
+    shape = [1] * (4 - t.dim()) + list(t.shape)
+    strides = [0] * (4 - t.dim()) + list(t.stride())
+    es = t.element_size()
+    x = Tensor()
+    x.type, x.data = ty, t.data_ptr()
+    for i in range(4):
+        x.ne[i] = shape[3 - i]
+        x.nb[i] = strides[3 - i] * es
+    # size-1 dims: keep ggml's dense convention so broadcasting code is happy
+    for i in range(1, 4):
+        if x.ne[i] == 1 and x.nb[i] == 0:
+            x.nb[i] = x.nb[i - 1] * x.ne[i - 1]
+    return x
+
+
+def _kv(raw: torch.Tensor, ggml_type: int, D: int) -> Tensor:
+    """uint8 (n_seq, n_kv, n_head_kv, row_bytes) cache view -> ggml [D, n_kv, n_head_kv, n_seq]."""
+    assert raw.is_cuda and raw.dtype == torch.uint8 and raw.dim() == 4
+    n_seq, n_kv, n_hkv, rb = raw.shape
+    if rb != row_bytes(ggml_type, D) or raw.stride(3) != 1:
+        raise ValueError("KV rows must be contiguous rows of D elements")
+    x = Tensor()
+    x.type, x.data = ggml_type, raw.data_ptr()
+    x.ne[0], x.ne[1], x.ne[2], x.ne[3] = D, n_kv, n_hkv, n_seq
+    x.nb[0] = _BLOCK_BYTES[ggml_type]
+    x.nb[1], x.nb[2], x.nb[3] = raw.stride(1), raw.stride(2), raw.stride(0)
+    return x
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    key = (device.index if device.index is not None else torch.cuda.current_device())
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
+def _fa_params(q, k, v, k_type, v_type, mask, sinks, dst, scale, max_bias, softcap, n_splits):
+    p = FaParams()
+    D = q.shape[-1]
+    p.q = _dense(q)
+    p.k = _kv(k, k_type, D)
+    p.v = _kv(v, v_type, D)
+    if mask is not None:
+        assert mask.dtype == torch.float16
+        p.mask = _dense(mask)
+    p.sinks = sinks.data_ptr() if sinks is not None else None
+    p.dst = dst.data_ptr()
+    p.scale, p.max_bias, p.softcap = scale, max_bias, softcap
+    p.n_splits = n_splits
+    return p
+
+
+def flash_attn_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_type: int,
+                   v_type: int | None = None, mask: torch.Tensor | None = None,
+                   sinks: torch.Tensor | None = None, scale: float = 1.0, max_bias: float = 0.0,
+                   softcap: float = 0.0, n_splits: int = 0, out: torch.Tensor | None = None,
+                   stream=None) -> torch.Tensor:
+    """GGML_OP_FLASH_ATTN_EXT.  q float32 (n_seq, n_head, n_q, D); k/v raw
+    uint8 caches (n_seq_kv, n_kv, n_head_kv, row_bytes); mask float16
+    (m3, m2, >=n_q, n_kv) or None.  Returns float32 (n_seq, n_q, n_head, D)."""
+    v_type = k_type if v_type is None else v_type
+    n_seq, n_head, n_q, D = q.shape
+    dst = out if out is not None else torch.empty((n_seq, n_q, n_head, D), dtype=torch.float32,
+                                                  device=q.device)
+    p = _fa_params(q, k, v, k_type, v_type, mask, sinks, dst, scale, max_bias, softcap, n_splits)
+    L = lib()
+    nbytes = L.xq_flash_attn_ext_workspace(C.byref(p))
+    ws = _workspace(nbytes, q.device)
+    check(L.xq_flash_attn_ext(C.byref(p), ws.data_ptr() if ws is not None else None,
+                              ws.numel() if ws is not None else 0, _stream(stream)))
+    return dst
+
+
+def flash_attn_ext_workspace(q, k, v, k_type, v_type=None, mask=None, n_splits=0) -> int:
+    v_type = k_type if v_type is None else v_type
+    dst = torch.empty(1, device=q.device)
+    p = _fa_params(q, k, v, k_type, v_type, mask, None, dst, 1.0, 0.0, 0.0, n_splits)
+    return int(lib().xq_flash_attn_ext_workspace(C.byref(p)))
+
+
+def fa_partials(q, k, v, k_type, rows_per_split: int, split_begin: int, split_end: int,
+                mask=None, scale=1.0, max_bias=0.0, softcap=0.0, out=None, stream=None):
+    """Partial records (acc[D], max, denom) of global KV splits
+    [split_begin, split_end): float32 (split_end - split_begin, n_rows, D + 2)."""
+    n_seq, n_head, n_q, D = q.shape
+    n_rows = n_seq * n_q * n_head
+    part = out if out is not None else torch.empty(
+        (split_end - split_begin, n_rows, D + 2), dtype=torch.float32, device=q.device)
+    dummy = torch.empty(1, device=q.device)
+    p = _fa_params(q, k, v, k_type, k_type, mask, None, dummy, scale, max_bias, softcap, 0)
+    check(lib().xq_fa_partials(C.byref(p), rows_per_split, split_begin, split_end,
+                               part.data_ptr(), _stream(stream)))
+    return part
+
+
+def lse_merge(partials: torch.Tensor, out=None, lse=None, want_lse=True, stream=None):
+    """partials float32 (n_splits, n_rows, D + 2) -> (out (n_rows, D), lse (n_rows,))."""
+    n_splits, n_rows, d2 = partials.shape
+    assert partials.is_contiguous()
+    D = d2 - 2
+    o = out if out is not None else torch.empty((n_rows, D), dtype=torch.float32,
+                                                device=partials.device)
+    lz = lse if lse is not None else (torch.empty((n_rows,), dtype=torch.float32,
+                                                  device=partials.device) if want_lse else None)
+    check(lib().xq_lse_merge(partials.data_ptr(), n_splits, n_rows, D, o.data_ptr(),
+                             lz.data_ptr() if lz is not None else None, _stream(stream)))
+    return o, lz
+
+
+def split_k(active: int, mode: int) -> int:
+    return int(lib().xq_split_k(active, mode))
+
+
+def attend_range_workspace(storage, n_tokens, active, n_head, n_head_kv, head_dim, mode) -> int:
+    return int(lib().xq_attend_range_workspace(storage, n_tokens, active, n_head, n_head_kv,
+                                               head_dim, mode))
+
+
+def attend_range(storage: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor,
+                 positions: torch.Tensor, n_head_kv: int, origin: int, active: int,
+                 kq_scale: float, split_mode: int = 0, stream=None):
+    """RKVA RANGE_ATTN.  k/v uint8 [capacity][n_head_kv][row_bytes] (contiguous);
+    q float32 (n_tokens, n_head, D); positions int32 (n_tokens,).  Returns
+    (out (n_tokens, n_head, D), lse (n_tokens, n_head))."""
+    n_tokens, n_head, D = q.shape
+    assert q.is_contiguous() and positions.dtype == torch.int32 and positions.is_cuda
+    out = torch.empty((n_tokens, n_head, D), dtype=torch.float32, device=q.device)
+    lse = torch.empty((n_tokens, n_head), dtype=torch.float32, device=q.device)
+    nbytes = attend_range_workspace(storage, n_tokens, active, n_head, n_head_kv, D, split_mode)
+    ws = _workspace(nbytes, q.device)
+    check(lib().xq_attend_range(storage, k.data_ptr() if active else None,
+                                v.data_ptr() if active else None, n_head, n_head_kv, D, origin,
+                                active, n_tokens, positions.data_ptr(), q.data_ptr(), kq_scale,
+                                split_mode, out.data_ptr(), lse.data_ptr(),
+                                ws.data_ptr() if ws is not None else None,
+                                ws.numel() if ws is not None else 0, _stream(stream)))
+    return out, lse
+
+
+def gated_delta_net(q, k, v, g, beta, state, slots: int = 1, out=None, stream=None):
+    """GGML_OP_GATED_DELTA_NET.  q, k (n_seq_qk, T, H_k, S); v (n_seq, T, H, S);
+    g, beta (n_seq, T, H, 1); state (n_seq, H, S, S).  Returns
+    (dst_flat, y (n_seq, T, H, S), snapshots (K, n_seq, H, S, S))."""
+    n_seq, T, H, S = v.shape
+    n_y = S * H * T * n_seq
+    n_snap = slots * S * S * H * n_seq
+    dst = out if out is not None else torch.empty(n_y + n_snap, dtype=torch.float32,
+                                                  device=v.device)
+    ts = [_dense(t) for t in (q, k, v, g, beta, state)]
+    check(lib().xq_gated_delta_net(*[C.byref(t) for t in ts], dst.data_ptr(), slots,
+                                   _stream(stream)))
+    return dst, dst[:n_y].view(n_seq, T, H, S), dst[n_y:].view(slots, n_seq, H, S, S)
+
+
+def dequantize_rows(ggml_type: int, raw: torch.Tensor, n_per_row: int, stream=None):
+    rows = raw.reshape(-1, raw.shape[-1])
+    out = torch.empty((rows.shape[0], n_per_row), dtype=torch.float32, device=raw.device)
+    check(lib().xq_dequantize_rows(ggml_type, rows.data_ptr(), rows.stride(0), out.data_ptr(),
+                                   out.stride(0) * 4, rows.shape[0], n_per_row, _stream(stream)))
+    return out.reshape(raw.shape[:-1] + (n_per_row,))
+
+
+def quantize_rows(ggml_type: int, x: torch.Tensor, stream=None):
+    n = x.shape[-1]
+    rows = x.reshape(-1, n).contiguous()
+    rb = row_bytes(ggml_type, n)
+    out = torch.empty((rows.shape[0], rb), dtype=torch.uint8, device=x.device)
+    check(lib().xq_quantize_rows(ggml_type, rows.data_ptr(), rows.stride(0) * 4, out.data_ptr(),
+                                 rb, rows.shape[0], n, _stream(stream)))
+    return out.reshape(x.shape[:-1] + (rb,))
