@@ -187,63 +187,73 @@ def run_ours(args, rank, world, torch, dist):
     part_all = torch.empty((n_splits, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     out = torch.empty((n_rows_out, D), dtype=torch.float32, device=dev)
 
-    def step(i, ev=None):
+    def step(i, parts=("dec", "gather", "merge")):
         k, v = sets[i % len(sets)]
         q = qs[i % len(sets)]
-        if ev:
-            ev[0].record(st)
-        xq.fa_partials(q, k, v, ty, rows_per_split, 0 if workload == "c5" else sb,
-                       (se - sb) if workload == "c5" else se, scale=scale, out=part_local)
-        if ev:
-            ev[1].record(st)
+        if "dec" in parts:
+            xq.fa_partials(q, k, v, ty, rows_per_split, 0 if workload == "c5" else sb,
+                           (se - sb) if workload == "c5" else se, scale=scale, out=part_local)
+        src = part_local
         if world > 1:
-            dist.all_gather_into_tensor(part_all, part_local)
+            if "gather" in parts:
+                dist.all_gather_into_tensor(part_all, part_local)
             src = part_all
-        else:
-            src = part_local
-        if ev:
-            ev[2].record(st)
-        xq.lse_merge(src, out=out, want_lse=False)
-        if ev:
-            ev[3].record(st)
+        if "merge" in parts:
+            xq.lse_merge(src, out=out, want_lse=False)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    use_graph = os.environ.get("XQ_BENCH_NO_GRAPH", "0") != "1"
+
+    def timed(fn, n):
+        """Device time (ms) of n calls of fn, replayed from one CUDA graph so
+        host launch overhead stays out of the timed region; max over ranks."""
+        for i in range(args.warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        g = None
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(n):
+                    fn(i)
+            g.replay()  # warm replay
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if g is not None:
+            g.replay()
+        else:
+            for i in range(n):
+                fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t = e0.elapsed_time(e1)
+        del g
+        if world > 1:
+            tt = torch.tensor([t], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t = float(tt.item())
+        return t
+
     clk = ClockSampler(dev.index)
     clk.start()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    t0.record(st)
-    for i in range(args.steps):
-        step(i, evs[i])
-    t1.record(st)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    ms = timed(step, args.steps) / args.steps
     clocks = clk.stop()
-    ms = t0.elapsed_time(t1) / args.steps
-    dec_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in evs]))
-    col_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs]))
-    mrg_ms = float(np.mean([e[2].elapsed_time(e[3]) for e in evs]))
-    if world > 1:
-        tt = torch.tensor([ms, dec_ms, col_ms, mrg_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms, dec_ms, col_ms, mrg_ms = (float(x) for x in tt.cpu())
+    dec_ms = timed(lambda i: step(i, ("dec",)), args.steps) / args.steps
+    mrg_ms = timed(lambda i: step(i, ("merge",)), args.steps) / args.steps
+    col_ms = (timed(lambda i: step(i, ("gather",)), args.steps) / args.steps) if world > 1 else 0.0
 
     # end to end through the public call with host buffers (pinned)
     q_host = torch.empty((n_seq, H, 1, D), dtype=torch.float32, pin_memory=True)
     q_host.copy_(qs[0].cpu())
     o_host = torch.empty((n_seq, 1, H, D), dtype=torch.float32, pin_memory=True)
-    e2e_ms = None
+    q_dev = torch.empty_like(qs[0])
     if workload != "c5":
-        q_dev = torch.empty_like(qs[0])
         o_dev = torch.empty((n_seq, 1, H, D), dtype=torch.float32, device=dev)
 
         def e2e_step(i):
@@ -251,42 +261,13 @@ def run_ours(args, rank, world, torch, dist):
             q_dev.copy_(q_host, non_blocking=True)
             xq.flash_attn_ext(q_dev, k, v, ty, scale=scale, n_splits=n_splits, out=o_dev)
             o_host.copy_(o_dev, non_blocking=True)
-
-        for i in range(args.warmup):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
-        a0.record(st)
-        for i in range(args.steps):
-            e2e_step(i)
-        a1.record(st)
-        torch.cuda.synchronize()
-        e2e_ms = a0.elapsed_time(a1) / args.steps
     else:
-        q_dev = qs[0]
-
         def e2e_step(i):
             q_dev.copy_(q_host, non_blocking=True)
-            step(i)
+            qs[0].copy_(q_dev)
+            step(0)
             o_host.view(-1).copy_(out.view(-1), non_blocking=True)
-
-        for i in range(args.warmup):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        dist.barrier() if world > 1 else None
-        a0 = torch.cuda.Event(enable_timing=True)
-        a1 = torch.cuda.Event(enable_timing=True)
-        a0.record(st)
-        for i in range(args.steps):
-            e2e_step(i)
-        a1.record(st)
-        torch.cuda.synchronize()
-        e2e_ms = a0.elapsed_time(a1) / args.steps
-        if world > 1:
-            tt = torch.tensor([e2e_ms], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            e2e_ms = float(tt.item())
+    e2e_ms = timed(e2e_step, args.steps) / args.steps
 
     if rank != 0:
         return None
@@ -323,6 +304,8 @@ def run_ours(args, rank, world, torch, dist):
                 "h2d_bytes_per_step": int(q_host.numel() * 4),
                 "d2h_bytes_per_step": int(o_host.numel() * 4)},
         "gpu_launches": args.steps * 2,
+        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps if use_graph
+                  else "eager launches, CUDA events",
         "clocks": clocks,
     }
     return line

@@ -79,8 +79,10 @@ def test_c2_config_full_size(ty):
     q, k, v, m = make_case(0, ty, 256, 16, 2, 32768)
     got, want = run_both(q, k, v, m, ty, 1.0 / 16)
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+    # ggml quantizes q to Q8_0 before the K dot; both sides do, so both sit
+    # the same distance from exact float64 attention on unquantized q
     ref64, _ = oracle.flash_attn_ext(q, k, v, ty, ty, scale=1.0 / 16, f64=True)
-    np.testing.assert_allclose(got, ref64, rtol=1e-3, atol=1e-4)
+    assert np.abs(got - ref64).max() <= 1.5 * np.abs(want - ref64).max() + 1e-5
 
 
 @pytest.mark.parametrize("n_splits", [1, 2, 7, 64, 0])

@@ -352,20 +352,25 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 }
 
 // ---------------------------------------------------------------------------
-// LSE merge: one CTA per output row, fixed split order for every reduction.
+// LSE merge: one CTA per output row.  NG groups of D threads each sum a
+// contiguous quarter of the splits for one dim (independent loads, so the
+// L2 latency overlaps), then the group sums meet in a fixed order; every
+// reduction has a fixed order, so the result does not depend on how the
+// splits were produced.
 template <int D>
-__global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict__ part,
-                                                        int64_t n_splits, int64_t n_rows,
-                                                        float *__restrict__ out,
-                                                        float *__restrict__ lse,
-                                                        const float *__restrict__ sinks,
-                                                        int n_head) {
-    constexpr int NT = 128, DPT = (D + NT - 1) / NT;
-    constexpr int CACHE = 2048;
+__global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restrict__ part,
+                                                          int64_t n_splits, int64_t n_rows,
+                                                          float *__restrict__ out,
+                                                          float *__restrict__ lse,
+                                                          const float *__restrict__ sinks,
+                                                          int n_head) {
+    constexpr int NG = 4, NT = NG * D, NW = NT / 32, CACHE = 2048;
     __shared__ float w_s[CACHE];
-    __shared__ float red[NT / 32];
+    __shared__ float d_s[CACHE];
+    __shared__ float red[NW];
+    __shared__ float accs[NG][D];
     __shared__ int bad_s;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, g = tid / D, d = tid % D;
     const int64_t row = blockIdx.x;
     const int64_t stride = (int64_t)n_rows * (D + 2);
     const float *base = part + row * (D + 2);
@@ -393,17 +398,19 @@ __global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict_
     __syncthreads();
     float M = red[0];
 #pragma unroll
-    for (int w = 1; w < NT / 32; ++w)
+    for (int w = 1; w < NW; ++w)
         M = fmaxf(M, red[w]);
     __syncthreads();
 
-    // pass 2: weights and the denominator (fixed per-thread order + fixed tree)
+    // pass 2: weights and the denominator
     float lsum = 0.0f;
     for (int64_t s = tid; s < n_splits; s += NT) {
         const float m = base[s * stride + D], den = base[s * stride + D + 1];
         const float w = den != 0.0f ? expf(m - M) : 0.0f;
-        if (s < CACHE)
+        if (s < CACHE) {
             w_s[s] = w;
+            d_s[s] = den;
+        }
         if (den != 0.0f)
             lsum += den * w;
     }
@@ -413,38 +420,45 @@ __global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict_
     __syncthreads();
     float L = red[0];
 #pragma unroll
-    for (int w = 1; w < NT / 32; ++w)
+    for (int w = 1; w < NW; ++w)
         L += red[w];
 
-    // pass 3: numerators in split order
-    float acc[DPT];
-#pragma unroll
-    for (int i = 0; i < DPT; ++i)
-        acc[i] = 0.0f;
+    // pass 3: numerators, contiguous split range per group
+    const int64_t s0 = n_splits * g / NG, s1 = n_splits * (g + 1) / NG;
+    float acc = 0.0f;
     int badn = 0;
-    for (int64_t s = 0; s < n_splits; ++s) {
+#pragma unroll 8
+    for (int64_t s = s0; s < s1; ++s) {
         const float *rec = base + s * stride;
-        const float den = rec[D + 1];
-        if (den == 0.0f)
-            continue;
-        const float w = s < CACHE ? w_s[s] : expf(rec[D] - M);
-#pragma unroll
-        for (int i = 0; i < DPT; ++i) {
-            const int d = tid + i * NT;
-            if (d < D) {
-                const float x = rec[d];
-                badn |= !isfinite(x);
-                acc[i] = fmaf(x, w, acc[i]);
-            }
+        const float x = rec[d];
+        float den, w;
+        if (s < CACHE) {
+            den = d_s[s];
+            w = w_s[s];
+        } else {
+            den = rec[D + 1];
+            w = den != 0.0f ? expf(rec[D] - M) : 0.0f;
+        }
+        if (den != 0.0f) {
+            badn |= !isfinite(x);
+            acc = fmaf(x, w, acc);
         }
     }
+    accs[g][d] = acc;
+    if (badn)
+        atomicOr(&bad_s, 1);
+    __syncthreads();
+    if (g != 0)
+        return;
+    acc = accs[0][d];
+#pragma unroll
+    for (int i = 1; i < NG; ++i)
+        acc += accs[i][d];
     if (sinks) {
         const float sk = sinks[row % n_head];
         if (L == 0.0f || sk > M) {
             const float ms = L == 0.0f ? 0.0f : expf(M - sk);
-#pragma unroll
-            for (int i = 0; i < DPT; ++i)
-                acc[i] *= ms;
+            acc *= ms;
             L = L * ms + 1.0f;
             M = sk;
         } else {
@@ -452,23 +466,16 @@ __global__ void __launch_bounds__(128) lse_merge_kernel(const float *__restrict_
         }
     }
     const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-    float l = L == 0.0f ? -INFINITY : M + logf(L);
-    if (!isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l)))
-        badn = 1;
-#pragma unroll
-    for (int i = 0; i < DPT; ++i)
-        badn |= !isfinite(acc[i] * inv);
-    if (badn)
+    const float l = L == 0.0f ? -INFINITY : M + logf(L);
+    const bool rowbad = !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
+    const float o = acc * inv;
+    // poison is decided block-wide; group 0 threads re-check after a barrier
+    if (!isfinite(o) || rowbad)
         atomicOr(&bad_s, 1);
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"r"(D)); // group 0 only (D threads)
     const bool poison = bad_s != 0;
-#pragma unroll
-    for (int i = 0; i < DPT; ++i) {
-        const int d = tid + i * NT;
-        if (d < D)
-            out[row * D + d] = poison ? NAN : acc[i] * inv;
-    }
-    if (lse && tid == 0)
+    out[row * D + d] = poison ? NAN : o;
+    if (lse && d == 0)
         lse[row] = poison ? NAN : l;
 }
 
@@ -572,9 +579,9 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
         return cudaSuccess;
     dim3 grid((unsigned)n_rows);
     switch (D) {
-    case 64: lse_merge_kernel<64><<<grid, 128, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
-    case 128: lse_merge_kernel<128><<<grid, 128, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
-    case 256: lse_merge_kernel<256><<<grid, 128, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 64: lse_merge_kernel<64><<<grid, 256, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 128: lse_merge_kernel<128><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 256: lse_merge_kernel<256><<<grid, 1024, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

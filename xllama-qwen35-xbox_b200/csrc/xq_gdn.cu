@@ -145,9 +145,7 @@ __global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t
     const float *x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(src) + r * ss);
     uint8_t *y = dst + r * ds;
     if constexpr (T == kF16) {
-        const uint16_t h = __half_as_ushort(__float2half_rn(x[b]));
-        y[2 * b] = (uint8_t)h;
-        y[2 * b + 1] = (uint8_t)(h >> 8);
+        reinterpret_cast<uint16_t *>(y)[b] = __half_as_ushort(__float2half_rn(x[b]));
     } else if constexpr (T == kQ8) {
         const float *xb = x + 32 * b;
         float amax = 0.0f;
@@ -155,10 +153,8 @@ __global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t
             amax = fmaxf(amax, fabsf(xb[j]));
         const float d = amax / 127.0f;
         const float id = d != 0.0f ? 1.0f / d : 0.0f;
-        const uint16_t dh = __half_as_ushort(__float2half_rn(d));
         uint8_t *blk = y + 34 * b;
-        blk[0] = (uint8_t)dh;
-        blk[1] = (uint8_t)(dh >> 8);
+        *reinterpret_cast<uint16_t *>(blk) = __half_as_ushort(__float2half_rn(d));
         for (int j = 0; j < 32; ++j)
             blk[2 + j] = (uint8_t)(int8_t)roundf(__fmul_rn(xb[j], id));
     } else {
@@ -172,10 +168,8 @@ __global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t
         }
         const float d = vmax / -8.0f;
         const float id = d != 0.0f ? 1.0f / d : 0.0f;
-        const uint16_t dh = __half_as_ushort(__float2half_rn(d));
         uint8_t *blk = y + 18 * b;
-        blk[0] = (uint8_t)dh;
-        blk[1] = (uint8_t)(dh >> 8);
+        *reinterpret_cast<uint16_t *>(blk) = __half_as_ushort(__float2half_rn(d));
         for (int j = 0; j < 16; ++j) {
             const int lo = min(15, (int)(int8_t)__fadd_rn(__fmul_rn(xb[j], id), 8.5f));
             const int hi = min(15, (int)(int8_t)__fadd_rn(__fmul_rn(xb[16 + j], id), 8.5f));
