@@ -4,6 +4,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -44,8 +45,23 @@ struct FaPlan {
     xq::DecodeArgs a;
     xq::DecodeConfig cfg;
     int D, n_qblocks;
+    bool mma; // warp-MMA decode kernel (8 q-rows per CTA)
     int64_t n_rows, n_splits;
 };
+
+bool mma_disabled() {
+    static const int off = [] {
+        const char *e = getenv("XQ_DECODE_MMA");
+        return e && e[0] == '0';
+    }();
+    return off != 0;
+}
+
+cudaError_t run_decode(const FaPlan &pl, dim3 grid, cudaStream_t st) {
+    if (pl.mma)
+        return xq::launch_decode_mma(pl.a, pl.cfg.type, pl.D, pl.cfg.VW, grid, st);
+    return xq::launch_decode(pl.a, pl.cfg, grid, st);
+}
 
 // Validate a FLASH_ATTN_EXT call and fill the decode arguments (without
 // choosing splits).
@@ -123,9 +139,60 @@ int fa_prepare(const xq_fa_params *p, FaPlan *pl) {
     if (!xq::decode_config(k.type, (int)D, a.n_qrows, a, &pl->cfg))
         return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: K/V rows not 4-byte aligned");
     pl->D = (int)D;
-    pl->n_qblocks = (a.n_qrows + pl->cfg.NR - 1) / pl->cfg.NR;
+    pl->mma = !mma_disabled() && xq::decode_mma_ok(k.type, (int)D, a);
+    const int per_block = pl->mma ? 8 : pl->cfg.NR;
+    pl->n_qblocks = (a.n_qrows + per_block - 1) / per_block;
     pl->n_rows = n_seq * n_q * n_head;
     return XQ_OK;
+}
+
+bool prefill_disabled() {
+    static const int off = [] {
+        const char *e = getenv("XQ_PREFILL");
+        return e && e[0] == '0';
+    }();
+    return off != 0;
+}
+
+// The tensor-core prefill kernel takes F16 K/V, D 128/256, many queries and
+// no softcap / ALiBi / sinks, with TMA-compatible (16-byte) strides.
+bool prefill_shape(const xq_fa_params *p, const FaPlan &pl, xq::PrefillShape *ps) {
+    const xq_tensor &q = p->q, &k = p->k, &v = p->v, &m = p->mask;
+    if (prefill_disabled() || k.type != XQ_TYPE_F16 || v.type != XQ_TYPE_F16 ||
+        (pl.D != 128 && pl.D != 256) || q.ne[1] < 64 || p->softcap != 0.0f ||
+        p->max_bias > 0.0f || p->sinks)
+        return false;
+    auto a16 = [](uint64_t x) { return x % 16 == 0; };
+    if (!a16((uint64_t)(uintptr_t)k.data) || !a16((uint64_t)(uintptr_t)v.data) ||
+        !a16((uint64_t)(uintptr_t)q.data) || !a16(k.nb[1]) || !a16(k.nb[2]) || !a16(k.nb[3]) ||
+        !a16(v.nb[1]) || !a16(v.nb[2]) || !a16(v.nb[3]) || !a16(q.nb[1]) || !a16(q.nb[2]) ||
+        !a16(q.nb[3]) || k.ne[3] != v.ne[3])
+        return false;
+    ps->q = static_cast<const uint8_t *>(q.data);
+    for (int i = 0; i < 4; ++i) {
+        ps->q_nb[i] = (int64_t)q.nb[i];
+        ps->k_nb[i] = (int64_t)k.nb[i];
+        ps->v_nb[i] = (int64_t)v.nb[i];
+    }
+    ps->k = k.data;
+    ps->v = v.data;
+    ps->mask = static_cast<const uint8_t *>(m.data);
+    ps->m_nb1 = (int64_t)m.nb[1];
+    ps->m_nb2 = (int64_t)m.nb[2];
+    ps->m_nb3 = (int64_t)m.nb[3];
+    ps->m_ne2 = m.data ? (int)m.ne[2] : 1;
+    ps->m_ne3 = m.data ? (int)m.ne[3] : 1;
+    ps->m_planes = ps->m_ne2 * ps->m_ne3;
+    ps->dst = p->dst;
+    ps->D = pl.D;
+    ps->n_q = (int)q.ne[1];
+    ps->n_head = (int)q.ne[2];
+    ps->n_head_kv = (int)k.ne[2];
+    ps->n_seq = (int)q.ne[3];
+    ps->n_seq_kv = (int)k.ne[3];
+    ps->n_kv = (int)k.ne[1];
+    ps->scale = p->scale;
+    return true;
 }
 
 // Automatic split count: about two CTAs per SM in one wave.
@@ -183,6 +250,9 @@ size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
     FaPlan pl;
     if (fa_prepare(p, &pl) != XQ_OK)
         return 0;
+    xq::PrefillShape ps;
+    if (prefill_shape(p, pl, &ps))
+        return xq::prefill_map_bytes(ps);
     plan_splits(&pl, p->n_splits);
     if (pl.n_splits <= 1)
         return 0;
@@ -194,20 +264,33 @@ int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_strea
     int rc = fa_prepare(p, &pl);
     if (rc)
         return rc;
+    xq::PrefillShape ps;
+    if (prefill_shape(p, pl, &ps)) {
+        const size_t need = xq::prefill_map_bytes(ps);
+        if (!ws || ws_bytes < need)
+            return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes,
+                        need);
+        const char *why = "";
+        cudaError_t e = xq::launch_prefill(ps, ws, reinterpret_cast<cudaStream_t>(stream), &why);
+        if (e != cudaSuccess)
+            return fail(XQ_ERR_CUDA, "flash_attn_ext prefill: %s (%s)", cudaGetErrorString(e),
+                        why);
+        return XQ_OK;
+    }
     plan_splits(&pl, p->n_splits);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     dim3 grid((unsigned)pl.n_splits, (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
               (unsigned)pl.a.n_seq);
     if (pl.n_splits == 1) {
         pl.a.direct = 1;
-        return cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "flash_attn_ext decode");
+        return cuda_status(run_decode(pl, grid, st), "flash_attn_ext decode");
     }
     const size_t need = (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * 4;
     if (!ws || ws_bytes < need)
         return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes, need);
     pl.a.direct = 0;
     pl.a.partials = static_cast<float *>(ws);
-    rc = cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "flash_attn_ext decode");
+    rc = cuda_status(run_decode(pl, grid, st), "flash_attn_ext decode");
     if (rc)
         return rc;
     return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p->dst,
@@ -233,8 +316,7 @@ int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_
     pl.a.partials = partials;
     dim3 grid((unsigned)(split_end - split_begin), (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
               (unsigned)pl.a.n_seq);
-    return cuda_status(xq::launch_decode(pl.a, pl.cfg, grid,
-                                         reinterpret_cast<cudaStream_t>(stream)),
+    return cuda_status(run_decode(pl, grid, reinterpret_cast<cudaStream_t>(stream)),
                        "fa_partials decode");
 }
 
@@ -326,7 +408,7 @@ int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_he
     dim3 grid((unsigned)s, (unsigned)(pl.a.n_head_kv * pl.n_qblocks), 1);
     if (s == 1) {
         pl.a.direct = 1;
-        return cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "attend_range decode");
+        return cuda_status(run_decode(pl, grid, st), "attend_range decode");
     }
     const size_t need = (size_t)s * pl.n_rows * (head_dim + 2) * 4;
     if (!ws || ws_bytes < need)
@@ -334,7 +416,7 @@ int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_he
     pl.a.direct = 0;
     pl.a.lse = nullptr;
     pl.a.partials = static_cast<float *>(ws);
-    rc = cuda_status(xq::launch_decode(pl.a, pl.cfg, grid, st), "attend_range decode");
+    rc = cuda_status(run_decode(pl, grid, st), "attend_range decode");
     if (rc)
         return rc;
     return cuda_status(xq::launch_merge(pl.a.partials, s, pl.n_rows, (int)head_dim, out, lse,

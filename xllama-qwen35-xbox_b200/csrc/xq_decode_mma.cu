@@ -1,0 +1,620 @@
+// Split-KV flash decode on warp-level tensor-core MMAs (ggml FLASH_ATTN_EXT
+// semantics; see xq_decode.cu for the reference citations).
+//
+// Per CTA: one split of KV rows x one kv head x up to 8 q-rows (the GQA
+// heads / queries sharing that kv head) x one sequence.  Each of the 4 warps
+// owns every 4th group of 16 keys of the split and streams it through its own
+// 3-stage cp.async ring, so warps never wait on each other until the final
+// fixed-order merge of their (m, l, O) states.
+//
+// Scores, per 16-key group: S^T (16 keys x 8 q-rows)
+//   Q8_0 / Q4_0 K:  one mma.m16n8k32 per 32-element block on the int8 codes
+//                   (q is quantized to Q8_0 first, as ggml does), giving the
+//                   exact integer block sums; s += float(sum) * (d_k * d_q) in
+//                   block order -- ggml's vec_dot_q8_0_q8_0 / q4_0_q8_0.
+//                   Q4_0 nibbles enter unsigned (u8 x s8) and the -8 offset
+//                   is removed exactly as 8 * sum(q) per block.
+//   F16 K:          mma.m16n8k16 on f16 (q rounded to f16, as ggml does),
+//                   A fragments by ldmatrix.
+// Softmax: running max in the log2 domain, rescaled whenever it grows.
+// Values, per group: O^T (D x 8 q-rows) += V^T P^T with mma.m16n8k16 f16:
+//   F16 V:          A fragments by ldmatrix.trans.
+//   Q8_0 / Q4_0 V:  the codes (exact in f16) are gathered from shared memory
+//                   with dims permuted so one 16/32-bit load per key feeds
+//                   two M-tiles; the per-(key, block) scale is folded into P.
+// Accumulation is fp32 throughout.
+#include <float.h>
+#include <math.h>
+
+#include "xq_common.cuh"
+#include "xq_internal.h"
+
+namespace xq {
+namespace dm {
+
+constexpr int NWARP = 4, NT = 32 * NWARP, KG = 16;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                          uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+// cp.async with zero fill when src_bytes == 0.
+template <int VW>
+__device__ __forceinline__ void cp_async_zfill(uint32_t dst, const void *src, int src_bytes) {
+    if constexpr (VW == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+                     "r"(src_bytes));
+    else if constexpr (VW == 8)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src),
+                     "r"(src_bytes));
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src),
+                     "r"(src_bytes));
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+// 32-bit word at a 2-byte aligned shared address (compile-time alignment known).
+template <bool ALIGNED4>
+__device__ __forceinline__ uint32_t ld_word(const uint8_t *p) {
+    if constexpr (ALIGNED4) {
+        return *reinterpret_cast<const uint32_t *>(p);
+    } else {
+        const uint16_t *h = reinterpret_cast<const uint16_t *>(p);
+        return (uint32_t)h[0] | ((uint32_t)h[1] << 16);
+    }
+}
+__device__ __forceinline__ float h2f(const uint8_t *p) {
+    return __half2float(*reinterpret_cast<const __half *>(p));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// Two signed int8 codes (byte 0 and byte 2 of x, already xor 0x80) -> half2.
+__device__ __forceinline__ uint32_t s8pair_to_h2(uint32_t x) {
+    uint32_t h = (x & 0x00FF00FFu) | 0x64006400u; // 1024 + (code + 128)
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&h), __half2(__float2half(1152.0f),
+                                                                  __float2half(1152.0f)));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+// Two unsigned nibble codes (low nibbles of byte 0 and byte 2) -> half2 of code - 8.
+__device__ __forceinline__ uint32_t u4pair_to_h2(uint32_t x) {
+    uint32_t h = (x & 0x000F000Fu) | 0x64006400u; // 1024 + nibble
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&h), __half2(__float2half(1032.0f),
+                                                                  __float2half(1032.0f)));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+
+// Output dim of O^T tile m, fragment row (g or g + 8) -> dim (the V gathers
+// permute dims so that one load per key feeds two M-tiles).
+template <int T>
+__device__ __forceinline__ int out_dim(int m, int row) {
+    if constexpr (T == kF16) {
+        return 16 * m + row;
+    } else if constexpr (T == kQ8) {
+        const int b = m >> 1, hf = m & 1, g = row & 7, hi = row >> 3;
+        return 32 * b + 4 * g + 2 * hf + hi;
+    } else {
+        const int b = m >> 1, hf = m & 1, g = row & 7, hi = row >> 3;
+        return 32 * b + 2 * g + hi + 16 * hf;
+    }
+}
+
+} // namespace dm
+
+template <int T, int D, int STAGES, int VW>
+__global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs a) {
+    using namespace dm;
+    constexpr int REC = rec_bytes(T, D);
+    constexpr int SS = smem_stride(REC);
+    constexpr int NB = D / 32;             // quant blocks per row
+    constexpr int MT = D / 16;             // O^T M-tiles
+    constexpr int GBYTES = KG * SS;        // one 16-key group of K (or V)
+    constexpr int RING = STAGES * 2 * GBYTES;
+    constexpr int VPR = REC / VW;
+    static_assert(REC % VW == 0, "copy width");
+
+    constexpr int OWB = NWARP * 8 * D * 4;  // merge buffer, aliases the rings
+    constexpr int BIG = NWARP * RING > OWB ? NWARP * RING : OWB;
+
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t *rings = smem;                                   // [NWARP][STAGES][K|V][GBYTES]
+    uint8_t *qsm = rings + BIG;                              // q codes: int8 [8][D] or f16 [8][D]
+    float *dq_s = reinterpret_cast<float *>(qsm + 8 * D * 2); // [NB][8]
+    int *qsum_s = reinterpret_cast<int *>(dq_s + NB * 8);    // [NB][8] (8 * sum q)
+    float *pt_s = reinterpret_cast<float *>(qsum_s + NB * 8); // [NWARP][16][8]
+    float *mw_s = pt_s + NWARP * 16 * 8;                     // [NWARP][8]
+    float *lw_s = mw_s + NWARP * 8;                          // [NWARP][8]
+    float *slope_s = lw_s + NWARP * 8;                       // [8]
+    int64_t *moff_s = reinterpret_cast<int64_t *>(slope_s + 8); // [8]
+    int *lim_s = reinterpret_cast<int *>(moff_s + 8);        // [8]
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int kvh = blockIdx.y % a.n_head_kv, qb = blockIdx.y / a.n_head_kv, s = blockIdx.z;
+    const int64_t split = a.split_begin + blockIdx.x;
+    const int64_t r0 = split * a.rows_per_split;
+    const int64_t r1 = min((int64_t)a.n_kv, r0 + a.rows_per_split);
+    const int jbase = qb * 8;
+    const int nj = min(8, a.n_qrows - jbase);
+    const uint8_t *kbase = a.k + (int64_t)kvh * a.k_nb2 + (int64_t)(s / a.rk3) * a.k_nb3;
+    const uint8_t *vbase = a.v + (int64_t)kvh * a.v_nb2 + (int64_t)(s / a.rv3) * a.v_nb3;
+
+    // ---- per-warp load pipeline ----
+    const int64_t n_groups = r1 > r0 ? (r1 - r0 + KG - 1) / KG : 0;
+    uint8_t *ring = rings + warp * RING;
+    auto issue = [&](int64_t grp, int stage) {
+        const int64_t k0 = r0 + grp * KG;
+        uint8_t *kd = ring + stage * 2 * GBYTES;
+        uint8_t *vd = kd + GBYTES;
+        for (int idx = lane; idx < KG * VPR; idx += 32) {
+            const int r = idx / VPR, c = idx - r * VPR;
+            const bool ok = k0 + r < r1;
+            const int64_t row = ok ? k0 + r : r0;
+            cp_async_zfill<VW>(smem_u32(kd + r * SS + c * VW), kbase + row * a.k_nb1 + c * VW,
+                               ok ? VW : 0);
+            cp_async_zfill<VW>(smem_u32(vd + r * SS + c * VW), vbase + row * a.v_nb1 + c * VW,
+                               ok ? VW : 0);
+        }
+    };
+    // my groups: warp + NWARP * i
+    const int64_t my_n = n_groups > warp ? (n_groups - warp + NWARP - 1) / NWARP : 0;
+#pragma unroll
+    for (int st = 0; st < STAGES - 1; ++st) {
+        if (st < my_n)
+            issue(warp + (int64_t)NWARP * st, st);
+        cp_async_commit();
+    }
+
+    // ---- prologue: q in K's dot type, per-q-row constants ----
+    if (tid < 8) {
+        const int j = tid;
+        float slope = 1.0f;
+        int64_t moff = 0;
+        int lim = a.n_kv;
+        if (j < nj) {
+            const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+            if (a.alibi)
+                slope = h < a.n_head_log2 ? powf(a.m0, (float)(h + 1))
+                                          : powf(a.m1, (float)(2 * (h - a.n_head_log2) + 1));
+            moff = (int64_t)iq1 * a.m_nb1 + (int64_t)(h % a.m_ne2) * a.m_nb2 +
+                   (int64_t)(s % a.m_ne3) * a.m_nb3;
+            if (a.positions) {
+                const int pos = a.positions[iq1];
+                lim = pos < a.origin ? 0 : min(a.active, pos - a.origin + 1);
+            }
+        } else {
+            lim = -1; // padding q-row: every key masked
+        }
+        slope_s[j] = slope;
+        moff_s[j] = moff;
+        lim_s[j] = lim;
+    }
+    if constexpr (T == kF16) {
+        __half *q16 = reinterpret_cast<__half *>(qsm);
+        for (int idx = tid; idx < 8 * D; idx += NT) {
+            const int j = idx / D, d = idx - j * D;
+            float x = 0.0f;
+            if (j < nj) {
+                const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+                x = *reinterpret_cast<const float *>(a.q + (int64_t)iq1 * a.q_nb1 +
+                                                     (int64_t)h * a.q_nb2 +
+                                                     (int64_t)s * a.q_nb3 + 4 * d);
+            }
+            q16[idx] = __float2half_rn(x);
+        }
+    } else {
+        int8_t *q8 = reinterpret_cast<int8_t *>(qsm);
+        for (int blk = warp; blk < 8 * NB; blk += NWARP) {
+            const int j = blk / NB, b = blk - j * NB;
+            float x = 0.0f;
+            if (j < nj) {
+                const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+                x = *reinterpret_cast<const float *>(a.q + (int64_t)iq1 * a.q_nb1 +
+                                                     (int64_t)h * a.q_nb2 +
+                                                     (int64_t)s * a.q_nb3 + 4 * (b * 32 + lane));
+            }
+            const float amax = warp_max(fabsf(x));
+            const float d = amax / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            const int qi = (int)roundf(x * id);
+            q8[j * D + b * 32 + lane] = (int8_t)qi;
+            const int qsum = __reduce_add_sync(0xffffffffu, qi);
+            if (lane == 0) {
+                dq_s[b * 8 + j] = __half2float(__float2half_rn(d));
+                qsum_s[b * 8 + j] = 8 * qsum;
+            }
+        }
+    }
+    __syncthreads();
+
+    // q as the B operand (8 q-rows = N), kept in registers
+    constexpr int QREGS = T == kF16 ? D / 8 : D / 16;
+    uint32_t qf[QREGS];
+    if constexpr (T == kF16) {
+        const __half *q16 = reinterpret_cast<const __half *>(qsm);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+            qf[2 * kk] = *reinterpret_cast<const uint32_t *>(q16 + g * D + 16 * kk + 2 * t);
+            qf[2 * kk + 1] = *reinterpret_cast<const uint32_t *>(q16 + g * D + 16 * kk + 8 + 2 * t);
+        }
+    } else {
+        const int8_t *q8 = reinterpret_cast<const int8_t *>(qsm);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            qf[2 * b] = *reinterpret_cast<const uint32_t *>(q8 + g * D + 32 * b + 4 * t);
+            qf[2 * b + 1] = *reinterpret_cast<const uint32_t *>(q8 + g * D + 32 * b + 16 + 4 * t);
+        }
+    }
+    // this lane's two q-rows (columns 2t, 2t+1)
+    const int c0 = 2 * t, c1 = 2 * t + 1;
+    const float slope0 = slope_s[c0], slope1 = slope_s[c1];
+    const int lim0 = lim_s[c0], lim1 = lim_s[c1];
+    const int64_t mo0 = moff_s[c0], mo1 = moff_s[c1];
+
+    float acc[MT][4];
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+        acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
+    float mu0 = -INFINITY, mu1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    float *pt = pt_s + warp * 128;
+
+    for (int64_t i = 0; i < my_n; ++i) {
+        {
+            const int64_t nxt = i + STAGES - 1;
+            if (nxt < my_n)
+                issue(warp + NWARP * nxt, (int)(nxt % STAGES));
+            cp_async_commit();
+        }
+        cp_async_wait<STAGES - 1>();
+        __syncwarp();
+        const int stage = (int)(i % STAGES);
+        const uint8_t *kg = ring + stage * 2 * GBYTES;
+        const uint8_t *vg = kg + GBYTES;
+        const int64_t k0 = r0 + (warp + NWARP * i) * KG;
+
+        // ---------------- scores S^T[key][q-row] ----------------
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f}; // (g,c0) (g,c1) (g+8,c0) (g+8,c1)
+        if constexpr (T == kF16) {
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+                uint32_t a0, a1, a2, a3;
+                const int key = (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int dim = 16 * kk + ((lane >> 4) & 1) * 8;
+                ldsm_x4(smem_u32(kg + key * SS + 2 * dim), a0, a1, a2, a3);
+                mma_f16(sc, a0, a1, a2, a3, qf[2 * kk], qf[2 * kk + 1]);
+            }
+        } else {
+            const uint8_t *rg = kg + g * SS, *rg8 = kg + (g + 8) * SS;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                constexpr int BB = T == kQ8 ? 34 : 18;
+                const int qo = BB * b + 2;
+                int c[4] = {0, 0, 0, 0};
+                if constexpr (T == kQ8) {
+                    uint32_t a0, a1, a2, a3;
+                    if (b & 1) {
+                        a0 = ld_word<true>(rg + qo + 4 * t);
+                        a1 = ld_word<true>(rg8 + qo + 4 * t);
+                        a2 = ld_word<true>(rg + qo + 16 + 4 * t);
+                        a3 = ld_word<true>(rg8 + qo + 16 + 4 * t);
+                    } else {
+                        a0 = ld_word<false>(rg + qo + 4 * t);
+                        a1 = ld_word<false>(rg8 + qo + 4 * t);
+                        a2 = ld_word<false>(rg + qo + 16 + 4 * t);
+                        a3 = ld_word<false>(rg8 + qo + 16 + 4 * t);
+                    }
+                    mma_s8(c, a0, a1, a2, a3, qf[2 * b], qf[2 * b + 1]);
+                } else {
+                    uint32_t w0, w1;
+                    if (b & 1) {
+                        w0 = ld_word<true>(rg + qo + 4 * t);
+                        w1 = ld_word<true>(rg8 + qo + 4 * t);
+                    } else {
+                        w0 = ld_word<false>(rg + qo + 4 * t);
+                        w1 = ld_word<false>(rg8 + qo + 4 * t);
+                    }
+                    mma_u8s8(c, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
+                             (w1 >> 4) & 0x0F0F0F0Fu, qf[2 * b], qf[2 * b + 1]);
+                    const int2 qs8 = *reinterpret_cast<const int2 *>(qsum_s + b * 8 + c0);
+                    c[0] -= qs8.x;
+                    c[1] -= qs8.y;
+                    c[2] -= qs8.x;
+                    c[3] -= qs8.y;
+                }
+                const float dk0 = h2f(rg + BB * b), dk1 = h2f(rg8 + BB * b);
+                const float2 dq = *reinterpret_cast<const float2 *>(dq_s + b * 8 + c0);
+                sc[0] += (float)c[0] * (dk0 * dq.x);
+                sc[1] += (float)c[1] * (dk0 * dq.y);
+                sc[2] += (float)c[2] * (dk1 * dq.x);
+                sc[3] += (float)c[3] * (dk1 * dq.y);
+            }
+        }
+
+        // ---------------- mask, softmax (log2 domain) ----------------
+        const int64_t kA = k0 + g, kB = k0 + g + 8;
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int64_t key = (e < 2) ? kA : kB;
+            const int col = e & 1;
+            float v = sc[e] * a.scale;
+            if (a.softcap != 0.0f)
+                v = a.softcap * tanhf(v);
+            bool dead = key >= r1 || key >= (col ? lim1 : lim0);
+            if (a.mask && !dead) {
+                const float mv = (col ? slope1 : slope0) *
+                                 h2f(a.mask + (col ? mo1 : mo0) + 2 * key);
+                dead = mv == -INFINITY;
+                v += mv;
+            }
+            x[e] = dead ? -INFINITY : v * kLog2e;
+        }
+        float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        if (mx0 > mu0) {
+            const float f = mu0 == -INFINITY ? 0.0f : ex2(mu0 - mx0);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                acc[m][0] *= f;
+                acc[m][2] *= f;
+            }
+            l0 *= f;
+            mu0 = mx0;
+        }
+        if (mx1 > mu1) {
+            const float f = mu1 == -INFINITY ? 0.0f : ex2(mu1 - mx1);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                acc[m][1] *= f;
+                acc[m][3] *= f;
+            }
+            l1 *= f;
+            mu1 = mx1;
+        }
+        const float p0 = x[0] == -INFINITY ? 0.0f : ex2(x[0] - mu0);
+        const float p1 = x[1] == -INFINITY ? 0.0f : ex2(x[1] - mu1);
+        const float p2 = x[2] == -INFINITY ? 0.0f : ex2(x[2] - mu0);
+        const float p3 = x[3] == -INFINITY ? 0.0f : ex2(x[3] - mu1);
+        l0 += p0 + p2;
+        l1 += p1 + p3;
+        // P^T fragment via a per-warp transpose: pt[key][q-row]
+        *reinterpret_cast<float2 *>(pt + g * 8 + c0) = make_float2(p0, p1);
+        *reinterpret_cast<float2 *>(pt + (g + 8) * 8 + c0) = make_float2(p2, p3);
+        __syncwarp();
+        const float pa = pt[(2 * t) * 8 + g], pb = pt[(2 * t + 1) * 8 + g];
+        const float pc = pt[(2 * t + 8) * 8 + g], pd = pt[(2 * t + 9) * 8 + g];
+
+        // ---------------- O^T += V^T P^T ----------------
+        if constexpr (T == kF16) {
+            const uint32_t b0 = pack_h2(pa, pb), b1 = pack_h2(pc, pd);
+            const int key = (lane & 7) + ((lane >> 4) & 1) * 8;
+            const int dsub = ((lane >> 3) & 1) * 8;
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4_t(smem_u32(vg + key * SS + 2 * (16 * m + dsub)), a0, a1, a2, a3);
+                mma_f16(acc[m], a0, a1, a2, a3, b0, b1);
+            }
+        } else {
+            const uint8_t *va = vg + (2 * t) * SS, *vb = vg + (2 * t + 1) * SS;
+            const uint8_t *vc = vg + (2 * t + 8) * SS, *vd = vg + (2 * t + 9) * SS;
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                constexpr int BB = T == kQ8 ? 34 : 18;
+                const uint32_t b0 = pack_h2(pa * h2f(va + BB * b), pb * h2f(vb + BB * b));
+                const uint32_t b1 = pack_h2(pc * h2f(vc + BB * b), pd * h2f(vd + BB * b));
+                if constexpr (T == kQ8) {
+                    const int o = 34 * b + 2 + 4 * g;
+                    uint32_t wa, wb, wc, wd;
+                    if (b & 1) {
+                        wa = ld_word<true>(va + o);
+                        wb = ld_word<true>(vb + o);
+                        wc = ld_word<true>(vc + o);
+                        wd = ld_word<true>(vd + o);
+                    } else {
+                        wa = ld_word<false>(va + o);
+                        wb = ld_word<false>(vb + o);
+                        wc = ld_word<false>(vc + o);
+                        wd = ld_word<false>(vd + o);
+                    }
+                    wa ^= 0x80808080u;
+                    wb ^= 0x80808080u;
+                    wc ^= 0x80808080u;
+                    wd ^= 0x80808080u;
+                    // tile 2b: bytes 0 (row g) and 1 (row g+8); tile 2b+1: bytes 2, 3
+                    mma_f16(acc[2 * b], s8pair_to_h2(__byte_perm(wa, wb, 0x0400)),
+                            s8pair_to_h2(__byte_perm(wa, wb, 0x0501)),
+                            s8pair_to_h2(__byte_perm(wc, wd, 0x0400)),
+                            s8pair_to_h2(__byte_perm(wc, wd, 0x0501)), b0, b1);
+                    mma_f16(acc[2 * b + 1], s8pair_to_h2(__byte_perm(wa, wb, 0x0602)),
+                            s8pair_to_h2(__byte_perm(wa, wb, 0x0703)),
+                            s8pair_to_h2(__byte_perm(wc, wd, 0x0602)),
+                            s8pair_to_h2(__byte_perm(wc, wd, 0x0703)), b0, b1);
+                } else {
+                    const int o = 18 * b + 2 + 2 * g;
+                    const uint32_t ua = *reinterpret_cast<const uint16_t *>(va + o);
+                    const uint32_t ub = *reinterpret_cast<const uint16_t *>(vb + o);
+                    const uint32_t uc = *reinterpret_cast<const uint16_t *>(vc + o);
+                    const uint32_t ud = *reinterpret_cast<const uint16_t *>(vd + o);
+                    const uint32_t xab = ua | (ub << 16), xcd = uc | (ud << 16);
+                    // tile 2b: low nibbles (dims 2g, 2g+1); tile 2b+1: high nibbles
+                    mma_f16(acc[2 * b], u4pair_to_h2(xab), u4pair_to_h2(xab >> 8),
+                            u4pair_to_h2(xcd), u4pair_to_h2(xcd >> 8), b0, b1);
+                    mma_f16(acc[2 * b + 1], u4pair_to_h2(xab >> 4), u4pair_to_h2(xab >> 12),
+                            u4pair_to_h2(xcd >> 4), u4pair_to_h2(xcd >> 12), b0, b1);
+                }
+            }
+        }
+        __syncwarp(); // pt and this stage are reused
+    }
+    cp_async_wait<0>();
+
+    // ---- per-warp state -> shared memory ----
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+    }
+    __syncthreads(); // every warp is done with its ring: reuse it for O
+    float *ow = reinterpret_cast<float *>(rings); // [NWARP][8][D]
+    if (g == 0) {
+        mw_s[warp * 8 + c0] = mu0;
+        mw_s[warp * 8 + c1] = mu1;
+        lw_s[warp * 8 + c0] = l0;
+        lw_s[warp * 8 + c1] = l1;
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+        ow[(warp * 8 + c0) * D + out_dim<T>(m, g)] = acc[m][0];
+        ow[(warp * 8 + c1) * D + out_dim<T>(m, g)] = acc[m][1];
+        ow[(warp * 8 + c0) * D + out_dim<T>(m, g + 8)] = acc[m][2];
+        ow[(warp * 8 + c1) * D + out_dim<T>(m, g + 8)] = acc[m][3];
+    }
+    __syncthreads();
+
+    // ---- fixed-order merge of the warps; direct output or partial record ----
+    for (int idx = tid; idx < nj * D; idx += NT) {
+        const int j = idx / D, d = idx - j * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w)
+            if (lw_s[w * 8 + j] != 0.0f)
+                M = fmaxf(M, mw_s[w * 8 + j]);
+        float L = 0.0f, o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NWARP; ++w) {
+            const float lw = lw_s[w * 8 + j];
+            if (lw != 0.0f) {
+                const float f = ex2(mw_s[w * 8 + j] - M);
+                L += lw * f;
+                o += ow[(w * 8 + j) * D + d] * f;
+            }
+        }
+        float m_nat = M * kLn2;
+        const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+        const int64_t orow = ((int64_t)s * a.n_q + iq1) * a.n_head + h;
+        if (a.direct) {
+            if (a.sinks) {
+                const float sk = a.sinks[h];
+                if (L == 0.0f || sk > m_nat) {
+                    const float ms = L == 0.0f ? 0.0f : expf(m_nat - sk);
+                    o *= ms;
+                    L = L * ms + 1.0f;
+                    m_nat = sk;
+                } else {
+                    L += expf(sk - m_nat);
+                }
+            }
+            const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+            a.dst[orow * D + d] = o * inv;
+            if (a.lse && d == 0)
+                a.lse[orow] = L == 0.0f ? -INFINITY : m_nat + logf(L);
+        } else {
+            float *rec = a.partials +
+                         ((split - a.split_begin) * (int64_t)a.n_seq * a.n_q * a.n_head + orow) *
+                             (D + 2);
+            rec[d] = o;
+            if (d == 0) {
+                rec[D] = L == 0.0f ? -FLT_MAX : m_nat;
+                rec[D + 1] = L;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+static int mma_stages(int type, int D) { return smem_stride(rec_bytes(type, D)) <= 288 ? 3 : 2; }
+
+size_t decode_mma_smem(int type, int D) {
+    const int SS = smem_stride(rec_bytes(type, D));
+    const size_t ring = (size_t)dm::NWARP * mma_stages(type, D) * 2 * dm::KG * SS;
+    const size_t ow = (size_t)dm::NWARP * 8 * D * 4;
+    size_t b = ring > ow ? ring : ow;
+    b += (size_t)8 * D * 2 + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
+    b += (size_t)dm::NWARP * 128 * 4 + 2 * dm::NWARP * 8 * 4 + 8 * 4 + 8 * 8 + 8 * 4;
+    return b;
+}
+
+bool decode_mma_ok(int type, int D, const DecodeArgs &a) {
+    return a.q_convert && (D == 128 || D == 256) &&
+           (type == kF16 || type == kQ8 || type == kQ4);
+}
+
+template <int T, int D, int ST, int VW>
+static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
+    const size_t smem = decode_mma_smem(T, D);
+    auto kern = fa_decode_mma_kernel<T, D, ST, VW>;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess)
+        return e;
+    kern<<<grid, dm::NT, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+template <int T, int D>
+static cudaError_t mma_vw(const DecodeArgs &a, int vw, dim3 grid, cudaStream_t st) {
+    constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
+    if constexpr (rec_bytes(T, D) % 16 == 0)
+        if (vw == 16)
+            return launch_mma<T, D, ST, 16>(a, grid, st);
+    if constexpr (rec_bytes(T, D) % 8 == 0)
+        if (vw >= 8)
+            return launch_mma<T, D, ST, 8>(a, grid, st);
+    return launch_mma<T, D, ST, 4>(a, grid, st);
+}
+
+cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
+                              cudaStream_t st) {
+    switch (type) {
+    case kF16: return D == 128 ? mma_vw<kF16, 128>(a, vw, grid, st) : mma_vw<kF16, 256>(a, vw, grid, st);
+    case kQ8: return D == 128 ? mma_vw<kQ8, 128>(a, vw, grid, st) : mma_vw<kQ8, 256>(a, vw, grid, st);
+    default: return D == 128 ? mma_vw<kQ4, 128>(a, vw, grid, st) : mma_vw<kQ4, 256>(a, vw, grid, st);
+    }
+}
+
+} // namespace xq

@@ -43,9 +43,30 @@ struct DecodeConfig {
 bool decode_config(int type, int D, int n_qrows, const DecodeArgs &a, DecodeConfig *cfg);
 cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &cfg, dim3 grid,
                           cudaStream_t st);
+// Tensor-core (warp MMA) decode: 8 q-rows per CTA, ggml q conversion only.
+bool decode_mma_ok(int type, int D, const DecodeArgs &a);
+size_t decode_mma_smem(int type, int D);
+cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
+                              cudaStream_t st);
 cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
                          float *out, float *lse, const float *sinks, int n_head,
                          cudaStream_t st);
+
+// One tensor-core prefill launch (F16 K/V, F32 q / dst).
+struct PrefillShape {
+    const uint8_t *q;
+    int64_t q_nb[4];
+    const void *k, *v;
+    int64_t k_nb[4], v_nb[4];
+    const uint8_t *mask; // F16 or null
+    int64_t m_nb1, m_nb2, m_nb3;
+    int m_ne2, m_ne3, m_planes;
+    float *dst;
+    int D, n_q, n_head, n_head_kv, n_seq, n_seq_kv, n_kv;
+    float scale;
+};
+size_t prefill_map_bytes(const PrefillShape &ps);
+cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, const char **why);
 
 struct GdnArgs {
     const float *q, *k, *v, *g, *beta, *state;

@@ -1,0 +1,643 @@
+// Causal / masked prefill attention on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), F16 K/V, F32 Q and output (ggml FLASH_ATTN_EXT with
+// many queries; semantics as ggml-cpu's one_chunk path: q rounded to f16,
+// s = scale * q.k + mask, masked -inf entries skipped, rows with no live key
+// give 0; the reference's bring-up kernel shaders/rkva/rkva_flash_attn.hlsl:61-125
+// states the same online-softmax contract).
+//
+// One CTA = 128 query rows of one head (TMEM lane r <-> query row r).
+//   warp 0      TMA producer: K_j, V_j tiles (64 keys x D, SW128) into a
+//               4-slot ring, completion on mbarriers (expect_tx)
+//   warp 1      TMEM allocator + MMA issuer (one lane):
+//                 S_j = Q K_j^T   (SS, M=128, N=64, K=D; S in TMEM, 2 buffers)
+//                 O  += P_j V_j   (TS, A = P_j in TMEM, B = V_j MN-major, N=D)
+//               issue order S_0, S_1, PV_0, S_2, PV_1, ... so the tensor
+//               core computes S_{j+1} while the softmax works on S_j
+//   warps 4-7   softmax: tcgen05.ld S_j, mask, running max in the log2
+//               domain, p = 2^(s - m_used) written back to TMEM as f16 (the
+//               A operand of PV_j), row sums; O is rescaled in TMEM only when
+//               the running max grows by more than 2^8 (lazy rescale, exact:
+//               the same m_used scales both O and l); epilogue O / l
+//   all warps   convert the Q tile F32 -> f16 into the SW128 K-major layout
+// A 128x64 block classification of the mask (all -inf / all 0 / mixed),
+// computed by a pre-pass over the mask, lets every role skip dead blocks and
+// read mask values only for mixed blocks.
+//
+// Every mbarrier wait is bounded: on timeout the kernel records an error code,
+// stops issuing work, drains its own copies and MMAs with bounded waits,
+// frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <float.h>
+#include <math.h>
+
+#include "xq_common.cuh"
+#include "xq_internal.h"
+
+namespace xq {
+
+namespace pf {
+
+constexpr int BM = 128;   // query rows per CTA
+constexpr int BN = 64;    // keys per tile
+constexpr int NSLOT = 4;  // K/V ring slots
+constexpr int NT = 256;   // threads
+constexpr uint64_t kWaitLimitNs = 2000000000ull; // 2 s: far beyond any legitimate wait
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar),
+                 "r"(bytes));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar));
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity));
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: false once another role aborted or after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        if (mbar_try(bar, parity))
+            return true;
+        if (*abort || globaltimer() - t0 > limit_ns)
+            return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: SW128, version 1 (sm100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor, kind::f16: F16 A/B, F32 accumulator.
+__host__ __device__ constexpr uint32_t idesc(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id,
+                                       uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+            bar));
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+
+// 32 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
+        "%28, %29, %30, %31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, "
+        "%10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, "
+        "%27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31]));
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+} // namespace pf
+
+struct PrefillArgs {
+    const uint8_t *q;
+    int64_t q_nb1, q_nb2, q_nb3;
+    const uint8_t *mask;
+    int64_t m_nb1, m_nb2, m_nb3;
+    int m_ne2, m_ne3;
+    const uint8_t *block_map; // [m3][m2][n_qt][n_kt]: 0 dead, 1 all-zero, 2 mixed
+    float *dst;
+    int *err;
+    int n_q, n_head, n_head_kv, n_seq, n_kv, rk3;
+    int n_qt, n_kt;
+    float scale_log2; // scale * log2(e)
+};
+
+template <int D>
+__global__ void __launch_bounds__(pf::NT, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
+    using namespace pf;
+    constexpr int QBYTES = BM * D * 2;            // Q tile, f16
+    constexpr int TBYTES = BN * D * 2;            // one K or V tile
+    constexpr int NBOX = D / 64;                  // 64-element (128 B) column boxes
+    constexpr uint32_t TM_O = 0;                  // O: columns [0, D)
+    constexpr uint32_t TM_S = D;                  // S buffers: [D, D + 2*BN)
+    constexpr uint32_t TM_COLS = D + 2 * BN <= 256 ? 256 : 512;
+    constexpr uint32_t ID_QK = idesc(BM, BN, 0, 0);
+    constexpr uint32_t ID_PV = idesc(BM, D, 0, 1);
+    static_assert(D == 128 || D == 256, "head dim");
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *q_s = smem;
+    uint8_t *ring = smem + QBYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + NSLOT * TBYTES);
+    // bars: full[NSLOT], empty[NSLOT], s_full[2], p_full[2], o_done, drain
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NSLOT + 6);
+    volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int per_q = a.n_head * a.n_seq;
+    const int qt = a.n_qt - 1 - (int)(blockIdx.x / per_q); // heaviest tiles first
+    const int rem = (int)(blockIdx.x % per_q);
+    const int h = rem % a.n_head, s = rem / a.n_head;
+    const int kvh = h / (a.n_head / a.n_head_kv);
+    const int q0 = qt * BM;
+    const uint8_t *bmap = a.block_map +
+                          ((size_t)((s % a.m_ne3) * a.m_ne2 + (h % a.m_ne2)) * a.n_qt + qt) * a.n_kt;
+
+    auto bar = [&](int i) { return smem_u32(bars + i); };
+    const int B_FULL = 0, B_EMPTY = NSLOT, B_S = 2 * NSLOT, B_P = 2 * NSLOT + 2,
+              B_O = 2 * NSLOT + 4, B_DRAIN = 2 * NSLOT + 5;
+
+    if (tid == 0) {
+        for (int i = 0; i < NSLOT; ++i) {
+            mbar_init(bar(B_FULL + i), 1);
+            mbar_init(bar(B_EMPTY + i), 1);
+        }
+        mbar_init(bar(B_S), 1);
+        mbar_init(bar(B_S + 1), 1);
+        mbar_init(bar(B_P), 128);
+        mbar_init(bar(B_P + 1), 128);
+        mbar_init(bar(B_O), 1);
+        mbar_init(bar(B_DRAIN), 1);
+        *abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(TM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+    }
+
+    // ---- Q tile: F32 global -> f16 SW128 K-major boxes [NBOX][BM rows][128 B] ----
+    for (int idx = tid; idx < BM * (D / 8); idx += NT) {
+        const int r = idx / (D / 8), c8 = idx % (D / 8); // 8-element chunk
+        const int d0 = c8 * 8;
+        uint4 packed = make_uint4(0, 0, 0, 0);
+        if (q0 + r < a.n_q) {
+            const float4 *src = reinterpret_cast<const float4 *>(
+                a.q + (int64_t)(q0 + r) * a.q_nb1 + (int64_t)h * a.q_nb2 + (int64_t)s * a.q_nb3 +
+                4 * d0);
+            const float4 x0 = src[0], x1 = src[1];
+            __half2 h0 = __floats2half2_rn(x0.x, x0.y), h1 = __floats2half2_rn(x0.z, x0.w);
+            __half2 h2 = __floats2half2_rn(x1.x, x1.y), h3 = __floats2half2_rn(x1.z, x1.w);
+            packed = make_uint4(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1),
+                                *reinterpret_cast<uint32_t *>(&h2), *reinterpret_cast<uint32_t *>(&h3));
+        }
+        const int box = d0 / 64, chunk = (d0 % 64) / 8;
+        *reinterpret_cast<uint4 *>(q_s + box * (BM * 128) + r * 128 + ((chunk ^ (r & 7)) * 16)) =
+            packed;
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // number of live key tiles for this query tile (same list in every role)
+    int n_live = 0;
+    for (int kt = 0; kt < a.n_kt; ++kt)
+        n_live += bmap[kt] != 0;
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            int j = 0, issued = 0; // K/V tiles issued so far
+            for (int kt = 0; kt < a.n_kt && !*abort_s; ++kt) {
+                if (!bmap[kt])
+                    continue;
+                for (int half = 0; half < 2; ++half) { // 0: K_j, 1: V_j
+                    const int n = 2 * j + half, slot = n % NSLOT, use = n / NSLOT;
+                    if (use > 0 && !mbar_wait(bar(B_EMPTY + slot), (use - 1) & 1, abort_s)) {
+                        *abort_s = 1;
+                        break;
+                    }
+                    const uint32_t dst = smem_u32(ring + slot * TBYTES);
+                    mbar_expect_tx(bar(B_FULL + slot), TBYTES);
+                    const CUtensorMap *m = half ? &vmap : &kmap;
+#pragma unroll
+                    for (int b = 0; b < NBOX; ++b)
+                        tma_load_4d(dst + b * (BN * 128), m, 64 * b, kt * BN, kvh, s / a.rk3,
+                                    bar(B_FULL + slot));
+                    ++issued;
+                }
+                ++j;
+            }
+            if (*abort_s) {
+                // our copies still in flight land on their full barriers
+                volatile int none = 0;
+                for (int n = issued - NSLOT < 0 ? 0 : issued - NSLOT; n < issued; ++n)
+                    mbar_wait(bar(B_FULL + n % NSLOT), (n / NSLOT) & 1, &none, 100000000ull);
+            }
+        }
+    } else if (warp == 1) {
+        // -------------------------------- MMA ---------------------------------
+        if (lane == 0 && n_live > 0) {
+            const uint32_t q_base = smem_u32(q_s);
+            auto issue_s = [&](int j) -> bool {
+                const int n = 2 * j, slot = n % NSLOT, use = n / NSLOT;
+                if (!mbar_wait(bar(B_FULL + slot), use & 1, abort_s))
+                    return false;
+                // S buffer j%2 is free: PV_{j-2} (which read P_{j-2} there) was
+                // issued before this point and the tensor pipe runs in order.
+                tc_fence_after();
+                const uint32_t k_base = smem_u32(ring + slot * TBYTES);
+                const uint32_t d_tm = tmem + TM_S + (j & 1) * BN;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk & 3) * 32; // 16 f16 = 32 B inside the SW128 row
+                    const uint64_t da = sdesc(q_base + (kk / 4) * (BM * 128) + off, 16, 1024);
+                    const uint64_t db = sdesc(k_base + (kk / 4) * (BN * 128) + off, 16, 1024);
+                    mma_ss(d_tm, da, db, ID_QK, kk > 0);
+                }
+                mma_commit(bar(B_S + (j & 1)));
+                mma_commit(bar(B_EMPTY + slot));
+                return true;
+            };
+            bool ok = issue_s(0);
+            for (int j = 0; ok && j < n_live; ++j) {
+                if (j + 1 < n_live)
+                    ok = issue_s(j + 1);
+                if (!ok)
+                    break;
+                // PV_j: wait for P_j from the softmax warps and V_j from TMA
+                if (!mbar_wait(bar(B_P + (j & 1)), (j >> 1) & 1, abort_s)) {
+                    ok = false;
+                    break;
+                }
+                const int n = 2 * j + 1, slot = n % NSLOT, use = n / NSLOT;
+                if (!mbar_wait(bar(B_FULL + slot), use & 1, abort_s)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t v_base = smem_u32(ring + slot * TBYTES);
+                const uint32_t p_tm = tmem + TM_S + (j & 1) * BN;
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    // B = V rows [16kk, 16kk+16) x all D columns, MN-major SW128:
+                    // 64-column boxes BN*128 bytes apart (LBO), 8-row groups
+                    // 1024 bytes apart (SBO)
+                    const uint64_t db = sdesc(v_base + kk * 2048, BN * 128, 1024);
+                    mma_ts(tmem + TM_O, p_tm + kk * 8, db, ID_PV, (j > 0 || kk > 0));
+                }
+                mma_commit(bar(B_O));
+                mma_commit(bar(B_EMPTY + slot));
+            }
+            if (!ok)
+                *abort_s = 1;
+            // every tcgen05.mma issued above has completed once this commits
+            mma_commit(bar(B_DRAIN));
+            volatile int none = 0;
+            mbar_wait(bar(B_DRAIN), 0, &none, 100000000ull);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------ softmax -------------------------------
+        const int r = tid - 128;                 // query row in tile == TMEM lane
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp - 4)) << 16);
+        const int qrow = q0 + r;
+        const uint8_t *mrow = a.mask ? a.mask + (int64_t)min(qrow, a.n_q - 1) * a.m_nb1 +
+                                           (int64_t)(h % a.m_ne2) * a.m_nb2 +
+                                           (int64_t)(s % a.m_ne3) * a.m_nb3
+                                     : nullptr;
+        float m_used = -INFINITY, l = 0.0f;
+        int j = 0;
+        bool ok = true;
+        for (int kt = 0; kt < a.n_kt && ok; ++kt) {
+            const int cls = bmap[kt];
+            if (!cls)
+                continue;
+            // warp-uniform outcome: the tcgen05.ld/st below are warp-collective
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_S + (j & 1)), (j >> 1) & 1, abort_s))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t s_tm = lane_base + TM_S + (j & 1) * BN;
+            float sv[64];
+            {
+                float t[32];
+                tmem_ld32(s_tm, t);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    sv[i] = t[i];
+                tmem_ld32(s_tm + 32, t);
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    sv[32 + i] = t[i];
+            }
+            const int kbase = kt * BN;
+            float mt = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 64; ++i) {
+                float x = sv[i] * a.scale_log2;
+                if (kbase + i >= a.n_kv)
+                    x = -INFINITY;
+                sv[i] = x;
+            }
+            if (cls == 2) {
+                const __half *mp = reinterpret_cast<const __half *>(mrow) + kbase;
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    if (kbase + i < a.n_kv) {
+                        const float mv = __half2float(mp[i]);
+                        sv[i] = mv == -INFINITY ? -INFINITY : sv[i] + mv * 1.4426950408889634f;
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+                mt = fmaxf(mt, sv[i]);
+            // lazy rescale: move m_used only when the max grew by > 8 (log2); the
+            // decision is per row, the TMEM traffic is warp-collective
+            const bool grow = mt > m_used + 8.0f || (m_used == -INFINITY && mt != -INFINITY);
+            const float mnew = grow ? mt : m_used;
+            const float f = (!grow || m_used == -INFINITY) ? (grow ? 0.0f : 1.0f)
+                                                           : ex2(m_used - mnew);
+            if (__any_sync(0xffffffffu, grow && j > 0 && m_used != -INFINITY)) {
+                // O holds PV_0..PV_{j-1}; wait for PV_{j-1} before scaling
+                if (!__all_sync(0xffffffffu, mbar_wait(bar(B_O), (j - 1) & 1, abort_s))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < D; c += 32) {
+                    float o[32];
+                    tmem_ld32(lane_base + TM_O + c, o);
+                    uint32_t w[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        w[i] = __float_as_uint(o[i] * f);
+                    tmem_st32(lane_base + TM_O + c, w);
+                }
+            }
+            l *= f;
+            m_used = mnew;
+            uint32_t pk[32];
+            float lt = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float p0 = sv[2 * i] == -INFINITY ? 0.0f : ex2(sv[2 * i] - m_used);
+                const float p1 = sv[2 * i + 1] == -INFINITY ? 0.0f : ex2(sv[2 * i + 1] - m_used);
+                const __half2 hp = __floats2half2_rn(p0, p1);
+                lt += __low2float(hp) + __high2float(hp);
+                pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
+            }
+            l += lt;
+            tmem_st32(s_tm, pk);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(B_P + (j & 1)));
+            ++j;
+        }
+        // ---- epilogue: O / l ----
+        if (ok && n_live > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_O), (n_live - 1) & 1, abort_s));
+            tc_fence_after();
+        }
+        if (!ok) {
+            *abort_s = 1;
+        } else {
+            const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+            float *out = a.dst + ((int64_t)(s * a.n_q + qrow) * a.n_head + h) * D;
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+                float o[32];
+                if (n_live > 0)
+                    tmem_ld32(lane_base + TM_O + c, o); // all lanes: warp-collective
+                if (qrow < a.n_q) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 v = n_live > 0 ? make_float4(o[i] * inv, o[i + 1] * inv,
+                                                            o[i + 2] * inv, o[i + 3] * inv)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                        *reinterpret_cast<float4 *>(out + c + i) = v;
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- teardown: all roles done; drain on abort; free TMEM ----
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_s && tid == 0)
+        atomicExch(a.err, 1);
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                     "r"(TM_COLS));
+    }
+}
+
+// Mask block classes for BM x BN blocks: 0 all -inf, 1 all 0, 2 otherwise.
+__global__ void mask_block_map_kernel(const uint8_t *mask, int64_t nb1, int64_t nb2, int64_t nb3,
+                                      int m2, int n_q, int n_kv, int n_qt, int n_kt,
+                                      uint8_t *map) {
+    const int kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
+    const int i2 = plane % m2, i3 = plane / m2;
+    int all_inf = 1, all_zero = 1;
+    for (int e = threadIdx.x; e < pf::BM * pf::BN; e += blockDim.x) {
+        const int r = qt * pf::BM + e / pf::BN, c = kt * pf::BN + e % pf::BN;
+        if (r >= n_q || c >= n_kv)
+            continue;
+        const float v = __half2float(*reinterpret_cast<const __half *>(
+            mask + (int64_t)r * nb1 + (int64_t)i2 * nb2 + (int64_t)i3 * nb3 + 2 * (int64_t)c));
+        all_inf &= (v == -INFINITY);
+        all_zero &= (v == 0.0f);
+    }
+    all_inf = __syncthreads_and(all_inf);
+    all_zero = __syncthreads_and(all_zero);
+    if (threadIdx.x == 0) {
+        // a block entirely beyond n_kv is dead as well
+        const bool beyond = kt * pf::BN >= n_kv;
+        map[((size_t)plane * n_qt + qt) * n_kt + kt] =
+            (beyond || all_inf) ? 0 : (all_zero ? 1 : 2);
+    }
+}
+
+__global__ void fill_map_kernel(uint8_t *map, size_t n, int n_kt, int n_kv) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n)
+        map[i] = ((int)(i % n_kt) * pf::BN < n_kv) ? 1 : 0;
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+size_t prefill_map_bytes(const PrefillShape &ps) {
+    const size_t n_qt = (ps.n_q + pf::BM - 1) / pf::BM, n_kt = (ps.n_kv + pf::BN - 1) / pf::BN;
+    return ((size_t)ps.m_planes * n_qt * n_kt + 255) / 256 * 256 + 256;
+}
+
+cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, const char **why) {
+    auto encode = get_encode();
+    if (!encode) {
+        *why = "cuTensorMapEncodeTiled unavailable";
+        return cudaErrorNotSupported;
+    }
+    const int D = ps.D;
+    const int n_qt = (ps.n_q + pf::BM - 1) / pf::BM, n_kt = (ps.n_kv + pf::BN - 1) / pf::BN;
+    uint8_t *map = static_cast<uint8_t *>(ws);
+    int *err = reinterpret_cast<int *>(map + prefill_map_bytes(ps) - 256);
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
+    if (e != cudaSuccess)
+        return e;
+    const int planes = ps.m_planes;
+    if (ps.mask) {
+        dim3 g(n_kt, n_qt, planes);
+        mask_block_map_kernel<<<g, 256, 0, st>>>(ps.mask, ps.m_nb1, ps.m_nb2, ps.m_nb3, ps.m_ne2,
+                                                 ps.n_q, ps.n_kv, n_qt, n_kt, map);
+    } else {
+        const size_t n = (size_t)planes * n_qt * n_kt;
+        fill_map_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(map, n, n_kt, ps.n_kv);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return e;
+
+    CUtensorMap maps[2];
+    const void *bases[2] = {ps.k, ps.v};
+    const int64_t *nbs[2] = {ps.k_nb, ps.v_nb};
+    for (int i = 0; i < 2; ++i) {
+        cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)ps.n_kv, (cuuint64_t)ps.n_head_kv,
+                              (cuuint64_t)ps.n_seq_kv};
+        cuuint64_t strides[3] = {(cuuint64_t)nbs[i][1], (cuuint64_t)nbs[i][2],
+                                 (cuuint64_t)nbs[i][3]};
+        cuuint32_t box[4] = {64, pf::BN, 1, 1};
+        cuuint32_t estr[4] = {1, 1, 1, 1};
+        CUresult r = encode(&maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                            const_cast<void *>(bases[i]), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            *why = "cuTensorMapEncodeTiled rejected the K/V layout";
+            return cudaErrorInvalidValue;
+        }
+    }
+    PrefillArgs a;
+    a.q = ps.q;
+    a.q_nb1 = ps.q_nb[1];
+    a.q_nb2 = ps.q_nb[2];
+    a.q_nb3 = ps.q_nb[3];
+    a.mask = ps.mask;
+    a.m_nb1 = ps.m_nb1;
+    a.m_nb2 = ps.m_nb2;
+    a.m_nb3 = ps.m_nb3;
+    a.m_ne2 = ps.mask ? ps.m_ne2 : 1;
+    a.m_ne3 = ps.mask ? ps.m_ne3 : 1;
+    a.block_map = map;
+    a.dst = ps.dst;
+    a.err = err;
+    a.n_q = ps.n_q;
+    a.n_head = ps.n_head;
+    a.n_head_kv = ps.n_head_kv;
+    a.n_seq = ps.n_seq;
+    a.n_kv = ps.n_kv;
+    a.rk3 = ps.n_seq / ps.n_seq_kv;
+    a.n_qt = n_qt;
+    a.n_kt = n_kt;
+    a.scale_log2 = ps.scale * 1.4426950408889634f;
+    const size_t smem = 1024 + (size_t)pf::BM * D * 2 + (size_t)pf::NSLOT * pf::BN * D * 2 + 256;
+    dim3 grid((unsigned)(n_qt * ps.n_head * ps.n_seq));
+    if (D == 256) {
+        cudaFuncSetAttribute(fa_prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        fa_prefill_kernel<256><<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
+    } else {
+        cudaFuncSetAttribute(fa_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        fa_prefill_kernel<128><<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
+    }
+    return cudaGetLastError();
+}
+
+} // namespace xq
