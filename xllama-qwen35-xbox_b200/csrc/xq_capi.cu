@@ -356,7 +356,10 @@ static int range_prepare(int32_t storage, const void *k, const void *v, uint32_t
     int rc = fa_prepare(fp, pl);
     if (rc)
         return rc;
+    // RKVA multiplies raw F32 q; only the CUDA-core kernel implements that
     pl->a.q_convert = 0;
+    pl->mma = false;
+    pl->n_qblocks = (pl->a.n_qrows + pl->cfg.NR - 1) / pl->cfg.NR;
     pl->a.positions = positions;
     pl->a.origin = (int)origin;
     pl->a.active = (int)active;

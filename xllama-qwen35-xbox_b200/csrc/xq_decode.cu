@@ -352,11 +352,13 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 }
 
 // ---------------------------------------------------------------------------
-// LSE merge: one CTA per output row.  NG groups of D threads each sum a
-// contiguous quarter of the splits for one dim (independent loads, so the
-// L2 latency overlaps), then the group sums meet in a fixed order; every
-// reduction has a fixed order, so the result does not depend on how the
-// splits were produced.
+// LSE merge: one CTA per output row.  NG groups of D threads each own a
+// contiguous quarter of the splits for one dim.  Every global load is issued
+// before the reductions that need it: the split maxima / denominators go to
+// shared memory while each thread already streams its numerators (chunks of
+// CH, next chunk in flight), so the merge costs about one memory latency.
+// All reductions run in a fixed order: the result does not depend on which
+// GPU or launch produced each split.
 template <int D>
 __global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restrict__ part,
                                                           int64_t n_splits, int64_t n_rows,
@@ -364,9 +366,9 @@ __global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restric
                                                           float *__restrict__ lse,
                                                           const float *__restrict__ sinks,
                                                           int n_head) {
-    constexpr int NG = 4, NT = NG * D, NW = NT / 32, CACHE = 2048;
-    __shared__ float w_s[CACHE];
-    __shared__ float d_s[CACHE];
+    constexpr int NG = 4, NT = NG * D, NW = NT / 32, CACHE = 2048, CH = 16;
+    __shared__ float w_s[CACHE];   // m, then the weight of each split
+    __shared__ float d_s[CACHE];   // denominator of each split
     __shared__ float red[NW];
     __shared__ float accs[NG][D];
     __shared__ int bad_s;
@@ -374,15 +376,24 @@ __global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restric
     const int64_t row = blockIdx.x;
     const int64_t stride = (int64_t)n_rows * (D + 2);
     const float *base = part + row * (D + 2);
+    const int64_t s0 = n_splits * g / NG, s1 = n_splits * (g + 1) / NG;
+    const bool cached = n_splits <= CACHE;
+
+    // first numerator chunk in flight before anything else
+    float x[CH];
+#pragma unroll
+    for (int i = 0; i < CH; ++i)
+        x[i] = s0 + i < s1 ? base[(s0 + i) * stride + d] : 0.0f;
     if (tid == 0)
         bad_s = 0;
-    __syncthreads();
-
-    // pass 1: maximum over participating splits, invalid-state detection
     float mx = -FLT_MAX;
     int bad = 0;
     for (int64_t s = tid; s < n_splits; s += NT) {
         const float m = base[s * stride + D], den = base[s * stride + D + 1];
+        if (cached) {
+            w_s[s] = m;
+            d_s[s] = den;
+        }
         if (den == 0.0f)
             continue;
         if (!isfinite(den) || den < 0.0f || !isfinite(m))
@@ -393,24 +404,29 @@ __global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restric
     mx = warp_max(mx);
     if ((tid & 31) == 0)
         red[tid >> 5] = mx;
+    __syncthreads();
     if (bad)
         atomicOr(&bad_s, 1);
-    __syncthreads();
     float M = red[0];
 #pragma unroll
     for (int w = 1; w < NW; ++w)
         M = fmaxf(M, red[w]);
     __syncthreads();
 
-    // pass 2: weights and the denominator
+    // weights and the denominator (fixed per-thread order + fixed tree)
     float lsum = 0.0f;
     for (int64_t s = tid; s < n_splits; s += NT) {
-        const float m = base[s * stride + D], den = base[s * stride + D + 1];
-        const float w = den != 0.0f ? expf(m - M) : 0.0f;
-        if (s < CACHE) {
-            w_s[s] = w;
-            d_s[s] = den;
+        float m, den;
+        if (cached) {
+            m = w_s[s];
+            den = d_s[s];
+        } else {
+            m = base[s * stride + D];
+            den = base[s * stride + D + 1];
         }
+        const float w = den != 0.0f ? expf(m - M) : 0.0f;
+        if (cached)
+            w_s[s] = w;
         if (den != 0.0f)
             lsum += den * w;
     }
@@ -423,26 +439,36 @@ __global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restric
     for (int w = 1; w < NW; ++w)
         L += red[w];
 
-    // pass 3: numerators, contiguous split range per group
-    const int64_t s0 = n_splits * g / NG, s1 = n_splits * (g + 1) / NG;
+    // numerators: consume chunk c while chunk c + 1 is loading
     float acc = 0.0f;
     int badn = 0;
-#pragma unroll 8
-    for (int64_t s = s0; s < s1; ++s) {
-        const float *rec = base + s * stride;
-        const float x = rec[d];
-        float den, w;
-        if (s < CACHE) {
-            den = d_s[s];
-            w = w_s[s];
-        } else {
-            den = rec[D + 1];
-            w = den != 0.0f ? expf(rec[D] - M) : 0.0f;
+    for (int64_t c0 = s0; c0 < s1; c0 += CH) {
+        float nx[CH];
+        const int64_t c1 = c0 + CH;
+#pragma unroll
+        for (int i = 0; i < CH; ++i)
+            nx[i] = c1 + i < s1 ? base[(c1 + i) * stride + d] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            const int64_t s = c0 + i;
+            if (s < s1) {
+                float den, w;
+                if (cached) {
+                    den = d_s[s];
+                    w = w_s[s];
+                } else {
+                    den = base[s * stride + D + 1];
+                    w = den != 0.0f ? expf(base[s * stride + D] - M) : 0.0f;
+                }
+                if (den != 0.0f) {
+                    badn |= !isfinite(x[i]);
+                    acc = fmaf(x[i], w, acc);
+                }
+            }
         }
-        if (den != 0.0f) {
-            badn |= !isfinite(x);
-            acc = fmaf(x, w, acc);
-        }
+#pragma unroll
+        for (int i = 0; i < CH; ++i)
+            x[i] = nx[i];
     }
     accs[g][d] = acc;
     if (badn)
@@ -469,7 +495,6 @@ __global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restric
     const float l = L == 0.0f ? -INFINITY : M + logf(L);
     const bool rowbad = !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
     const float o = acc * inv;
-    // poison is decided block-wide; group 0 threads re-check after a barrier
     if (!isfinite(o) || rowbad)
         atomicOr(&bad_s, 1);
     asm volatile("bar.sync 1, %0;" ::"r"(D)); // group 0 only (D threads)

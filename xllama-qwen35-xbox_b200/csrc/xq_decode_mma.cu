@@ -85,6 +85,45 @@ __device__ __forceinline__ void cp_async_zfill(uint32_t dst, const void *src, in
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src),
                      "r"(src_bytes));
 }
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar),
+                 "r"(bytes));
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\n"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n"
+        "selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity));
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait (2 s, far beyond any legitimate wait); false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try(bar, parity))
+        if (globaltimer() - t0 > 2000000000ull)
+            return false;
+    return true;
+}
+// One bulk (TMA engine) copy global -> shared, completion counted on bar.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+        "[%3];\n" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -141,6 +180,8 @@ __device__ __forceinline__ int out_dim(int m, int row) {
 
 template <int T, int D, int STAGES, int VW>
 __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs a) {
+    // 16-byte aligned rows: one bulk copy per key row; otherwise per-lane cp.async
+    constexpr bool BULK = VW == 16;
     using namespace dm;
     constexpr int REC = rec_bytes(T, D);
     constexpr int SS = smem_stride(REC);
@@ -165,6 +206,7 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     float *slope_s = lw_s + NWARP * 8;                       // [8]
     int64_t *moff_s = reinterpret_cast<int64_t *>(slope_s + 8); // [8]
     int *lim_s = reinterpret_cast<int *>(moff_s + 8);        // [8]
+    uint64_t *bar_s = reinterpret_cast<uint64_t *>(lim_s + 8); // [NWARP][STAGES]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -180,18 +222,43 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     // ---- per-warp load pipeline ----
     const int64_t n_groups = r1 > r0 ? (r1 - r0 + KG - 1) / KG : 0;
     uint8_t *ring = rings + warp * RING;
+    uint64_t *mybar = bar_s + warp * STAGES;
+    if constexpr (BULK) {
+        if (lane < STAGES)
+            mbar_init(smem_u32(mybar + lane), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        __syncwarp();
+    }
     auto issue = [&](int64_t grp, int stage) {
         const int64_t k0 = r0 + grp * KG;
         uint8_t *kd = ring + stage * 2 * GBYTES;
         uint8_t *vd = kd + GBYTES;
-        for (int idx = lane; idx < KG * VPR; idx += 32) {
-            const int r = idx / VPR, c = idx - r * VPR;
-            const bool ok = k0 + r < r1;
-            const int64_t row = ok ? k0 + r : r0;
-            cp_async_zfill<VW>(smem_u32(kd + r * SS + c * VW), kbase + row * a.k_nb1 + c * VW,
-                               ok ? VW : 0);
-            cp_async_zfill<VW>(smem_u32(vd + r * SS + c * VW), vbase + row * a.v_nb1 + c * VW,
-                               ok ? VW : 0);
+        if constexpr (BULK) {
+            const int nrows = (int)min((int64_t)KG, r1 - k0);
+            const uint32_t bar = smem_u32(mybar + stage);
+            if (lane == 0)
+                mbar_expect_tx(bar, (uint32_t)(2 * nrows * REC));
+            const int r = lane & (KG - 1);
+            uint8_t *dst = (lane < KG ? kd : vd) + r * SS;
+            if (r < nrows) {
+                const uint8_t *src = lane < KG ? kbase + (k0 + r) * a.k_nb1
+                                               : vbase + (k0 + r) * a.v_nb1;
+                bulk_g2s(smem_u32(dst), src, REC, bar);
+            } else if (lane >= KG) {
+                // V rows past the split end must be finite zeros (p = 0 there)
+                for (int c = 0; c < REC; c += 16)
+                    *reinterpret_cast<uint4 *>(dst + c) = make_uint4(0, 0, 0, 0);
+            }
+        } else {
+            for (int idx = lane; idx < KG * VPR; idx += 32) {
+                const int r = idx / VPR, c = idx - r * VPR;
+                const bool ok = k0 + r < r1;
+                const int64_t row = ok ? k0 + r : r0;
+                cp_async_zfill<VW>(smem_u32(kd + r * SS + c * VW), kbase + row * a.k_nb1 + c * VW,
+                                   ok ? VW : 0);
+                cp_async_zfill<VW>(smem_u32(vd + r * SS + c * VW), vbase + row * a.v_nb1 + c * VW,
+                                   ok ? VW : 0);
+            }
         }
     };
     // my groups: warp + NWARP * i
@@ -200,7 +267,8 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     for (int st = 0; st < STAGES - 1; ++st) {
         if (st < my_n)
             issue(warp + (int64_t)NWARP * st, st);
-        cp_async_commit();
+        if constexpr (!BULK)
+            cp_async_commit();
     }
 
     // ---- prologue: q in K's dot type, per-q-row constants ----
@@ -301,11 +369,22 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
             const int64_t nxt = i + STAGES - 1;
             if (nxt < my_n)
                 issue(warp + NWARP * nxt, (int)(nxt % STAGES));
-            cp_async_commit();
+            if constexpr (!BULK)
+                cp_async_commit();
         }
-        cp_async_wait<STAGES - 1>();
-        __syncwarp();
         const int stage = (int)(i % STAGES);
+        if constexpr (BULK) {
+            // warp-uniform outcome: the MMAs and shuffles below are warp-collective
+            if (!__all_sync(0xffffffffu,
+                            mbar_wait(smem_u32(mybar + stage), (uint32_t)((i / STAGES) & 1)))) {
+                if (a.err && lane == 0)
+                    atomicExch(a.err, 2);
+                break;
+            }
+        } else {
+            cp_async_wait<STAGES - 1>();
+        }
+        __syncwarp();
         const uint8_t *kg = ring + stage * 2 * GBYTES;
         const uint8_t *vg = kg + GBYTES;
         const int64_t k0 = r0 + (warp + NWARP * i) * KG;
@@ -576,6 +655,7 @@ size_t decode_mma_smem(int type, int D) {
     size_t b = ring > ow ? ring : ow;
     b += (size_t)8 * D * 2 + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
     b += (size_t)dm::NWARP * 128 * 4 + 2 * dm::NWARP * 8 * 4 + 8 * 4 + 8 * 8 + 8 * 4;
+    b += (size_t)dm::NWARP * mma_stages(type, D) * 8; // mbarriers
     return b;
 }
 

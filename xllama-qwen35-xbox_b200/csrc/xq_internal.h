@@ -32,6 +32,7 @@ struct DecodeArgs {
     int q_convert;  // 1: ggml converts q to the K dot type; 0: raw F32 (RKVA)
     float scale, softcap, m0, m1;
     int n_head_log2, alibi;
+    int *err; // optional: set non-zero when a bounded wait gives up
 };
 
 struct DecodeConfig {

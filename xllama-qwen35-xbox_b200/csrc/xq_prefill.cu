@@ -467,7 +467,9 @@ __global__ void __launch_bounds__(pf::NT, 1)
         }
         // ---- epilogue: O / l ----
         if (ok && n_live > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_O), (n_live - 1) & 1, abort_s));
+            // the MMA thread's last commit (B_DRAIN, one phase) covers every MMA;
+            // B_O's parity alone cannot tell PV_{n-1} from a pending PV_{n-2}
+            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_DRAIN), 0, abort_s));
             tc_fence_after();
         }
         if (!ok) {
