@@ -21,6 +21,8 @@ REPO = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "lib", "libxq_b200.so")
+GGML_LIB = os.path.join(PKG, "lib", "libxq_ggml_b200.so")
+GGML_SRC = os.path.join(PKG, "ggml", "ggml_xq_backend.cpp")
 INCLUDE = os.path.join(REPO, "include")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -68,7 +70,26 @@ def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = Fa
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
+    build_ggml_backend(force)
     return LIB
+
+
+def build_ggml_backend(force: bool = False) -> str:
+    """libxq_ggml_b200.so: the ggml backend over libxq_b200.so.  ggml's own
+    symbols stay undefined here; the host process (llama.cpp's libggml-base,
+    or the test harness) provides them at load time."""
+    hdr = os.path.join(PKG, "ggml", "ggml_abi_mirror.h")
+    if not force and not _stale(GGML_LIB, [GGML_SRC, hdr, LIB] + _headers()):
+        return GGML_LIB
+    cuda = os.path.dirname(os.path.dirname(NVCC))
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-I" + INCLUDE,
+           "-I" + os.path.join(PKG, "ggml"), "-I" + os.path.join(cuda, "include"), GGML_SRC,
+           "-o", GGML_LIB, "-L" + os.path.dirname(LIB), "-lxq_b200",
+           "-L" + os.path.join(cuda, "lib64"), "-lcudart", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ggml backend build failed:\n{r.stderr}")
+    return GGML_LIB
 
 
 if __name__ == "__main__":

@@ -360,13 +360,13 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 // All reductions run in a fixed order: the result does not depend on which
 // GPU or launch produced each split.
 template <int D>
-__global__ void __launch_bounds__(4 * D) lse_merge_kernel(const float *__restrict__ part,
+__global__ void __launch_bounds__(512) lse_merge_kernel(const float *__restrict__ part,
                                                           int64_t n_splits, int64_t n_rows,
                                                           float *__restrict__ out,
                                                           float *__restrict__ lse,
                                                           const float *__restrict__ sinks,
                                                           int n_head) {
-    constexpr int NG = 4, NT = NG * D, NW = NT / 32, CACHE = 2048, CH = 16;
+    constexpr int NG = 512 / D, NT = NG * D, NW = NT / 32, CACHE = 2048, CH = 8;
     __shared__ float w_s[CACHE];   // m, then the weight of each split
     __shared__ float d_s[CACHE];   // denominator of each split
     __shared__ float red[NW];
@@ -604,9 +604,9 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
         return cudaSuccess;
     dim3 grid((unsigned)n_rows);
     switch (D) {
-    case 64: lse_merge_kernel<64><<<grid, 256, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 64: lse_merge_kernel<64><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
     case 128: lse_merge_kernel<128><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
-    case 256: lse_merge_kernel<256><<<grid, 1024, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 256: lse_merge_kernel<256><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
