@@ -297,7 +297,9 @@ def run_ours(args, rank, world, torch, dist):
                          "merge_kernel": round(mrg_ms, 5)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "peak_kind": peak_kind, "kernel": "fa_decode_kernel",
+                     "peak_kind": peak_kind,
+                     "kernel": ("fa_decode_kernel" if os.environ.get("XQ_DECODE_MMA") == "0"
+                                else "fa_decode_mma_kernel"),
                      "traffic": traffic},
         "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 5),

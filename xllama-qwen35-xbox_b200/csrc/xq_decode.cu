@@ -352,156 +352,174 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 }
 
 // ---------------------------------------------------------------------------
-// LSE merge: one CTA per output row.  NG groups of D threads each own a
-// contiguous quarter of the splits for one dim.  Every global load is issued
-// before the reductions that need it: the split maxima / denominators go to
-// shared memory while each thread already streams its numerators (chunks of
-// CH, next chunk in flight), so the merge costs about one memory latency.
-// All reductions run in a fixed order: the result does not depend on which
-// GPU or launch produced each split.
+// LSE merge: one thread-block cluster per output row, one CTA per 32 dims.
+// Every CTA reads all splits' (m, l), forms the global max M, the weights
+// w_s = exp(m_s - M) and L = sum l_s w_s (fixed order: thread-strided, then
+// the warp tree, then warps in order); its 8 warps then stream contiguous
+// runs of splits for its 32 dims (lane = dim, one 128-byte line per split)
+// and add the warp sums in warp order.  Any non-finite input of a live split
+// or a non-finite result poisons the whole row (NaN out, NaN lse): the CTAs of
+// the row OR their flags through distributed shared memory.  The order of
+// every sum depends only on the number of splits, never on which GPU or
+// launch produced each split.
+namespace mg {
+constexpr int NT = 256, NW = NT / 32, CACHE = 2048, UN = 8;
+
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ int ld_peer_flag(const int *local, uint32_t rank) {
+    uint32_t addr = (uint32_t)__cvta_generic_to_shared(local), peer;
+    int v;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(peer) : "r"(addr), "r"(rank));
+    asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(peer) : "memory");
+    return v;
+}
+} // namespace mg
+
 template <int D>
-__global__ void __launch_bounds__(512) lse_merge_kernel(const float *__restrict__ part,
-                                                          int64_t n_splits, int64_t n_rows,
-                                                          float *__restrict__ out,
-                                                          float *__restrict__ lse,
-                                                          const float *__restrict__ sinks,
-                                                          int n_head) {
-    constexpr int NG = 512 / D, NT = NG * D, NW = NT / 32, CACHE = 2048, CH = 8;
-    __shared__ float w_s[CACHE];   // m, then the weight of each split
-    __shared__ float d_s[CACHE];   // denominator of each split
+__global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restrict__ part,
+                                                           int64_t n_splits, int64_t n_rows,
+                                                           float *__restrict__ out,
+                                                           float *__restrict__ lse,
+                                                           const float *__restrict__ sinks,
+                                                           int n_head) {
+    using namespace mg;
+    constexpr int NC = D / 32; // CTAs per row (the cluster)
+    __shared__ float2 wd_s[CACHE]; // (m, l), then (w, l) of each split
     __shared__ float red[NW];
-    __shared__ float accs[NG][D];
-    __shared__ int bad_s;
-    const int tid = threadIdx.x, g = tid / D, d = tid % D;
-    const int64_t row = blockIdx.x;
+    __shared__ float accw[NW][32];
+    __shared__ int flag_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int chunk = blockIdx.x % NC; // == rank in the cluster
+    const int64_t row = blockIdx.x / NC;
     const int64_t stride = (int64_t)n_rows * (D + 2);
     const float *base = part + row * (D + 2);
-    const int64_t s0 = n_splits * g / NG, s1 = n_splits * (g + 1) / NG;
     const bool cached = n_splits <= CACHE;
+    auto md = [&](int64_t s) {
+        return make_float2(base[s * stride + D], base[s * stride + D + 1]);
+    };
 
-    // first numerator chunk in flight before anything else
-    float x[CH];
-#pragma unroll
-    for (int i = 0; i < CH; ++i)
-        x[i] = s0 + i < s1 ? base[(s0 + i) * stride + d] : 0.0f;
-    if (tid == 0)
-        bad_s = 0;
+    grid_dep_wait(); // partials come from the preceding kernel
     float mx = -FLT_MAX;
     int bad = 0;
     for (int64_t s = tid; s < n_splits; s += NT) {
-        const float m = base[s * stride + D], den = base[s * stride + D + 1];
-        if (cached) {
-            w_s[s] = m;
-            d_s[s] = den;
-        }
-        if (den == 0.0f)
+        const float2 v = md(s);
+        if (cached)
+            wd_s[s] = v;
+        if (v.y == 0.0f)
             continue;
-        if (!isfinite(den) || den < 0.0f || !isfinite(m))
+        if (!isfinite(v.y) || v.y < 0.0f || !isfinite(v.x))
             bad = 1;
         else
-            mx = fmaxf(mx, m);
+            mx = fmaxf(mx, v.x);
     }
     mx = warp_max(mx);
-    if ((tid & 31) == 0)
-        red[tid >> 5] = mx;
-    __syncthreads();
-    if (bad)
-        atomicOr(&bad_s, 1);
+    if (lane == 0)
+        red[warp] = mx;
+    bad = __syncthreads_or(bad);
     float M = red[0];
 #pragma unroll
     for (int w = 1; w < NW; ++w)
         M = fmaxf(M, red[w]);
     __syncthreads();
 
-    // weights and the denominator (fixed per-thread order + fixed tree)
     float lsum = 0.0f;
     for (int64_t s = tid; s < n_splits; s += NT) {
-        float m, den;
-        if (cached) {
-            m = w_s[s];
-            den = d_s[s];
-        } else {
-            m = base[s * stride + D];
-            den = base[s * stride + D + 1];
-        }
-        const float w = den != 0.0f ? expf(m - M) : 0.0f;
+        const float2 v = cached ? wd_s[s] : md(s);
+        const float w = v.y != 0.0f ? expf(v.x - M) : 0.0f;
         if (cached)
-            w_s[s] = w;
-        if (den != 0.0f)
-            lsum += den * w;
+            wd_s[s] = make_float2(w, v.y);
+        if (v.y != 0.0f)
+            lsum += v.y * w;
     }
     lsum = warp_sum(lsum);
-    if ((tid & 31) == 0)
-        red[tid >> 5] = lsum;
+    if (lane == 0)
+        red[warp] = lsum;
     __syncthreads();
     float L = red[0];
 #pragma unroll
     for (int w = 1; w < NW; ++w)
         L += red[w];
 
-    // numerators: consume chunk c while chunk c + 1 is loading
-    float acc = 0.0f;
-    int badn = 0;
-    for (int64_t c0 = s0; c0 < s1; c0 += CH) {
-        float nx[CH];
-        const int64_t c1 = c0 + CH;
+    // numerators: warp w owns splits [s0, s1), lane owns dim chunk * 32 + lane
+    const int d = chunk * 32 + lane;
+    const int64_t s0 = n_splits * warp / NW, s1 = n_splits * (warp + 1) / NW;
+    const float *xb = base + d;
+    float acc = 0.0f, chk = 0.0f; // chk: NaN iff some live numerator is not finite
+    auto wd = [&](int64_t s) {
+        if (cached)
+            return wd_s[s];
+        const float2 v = md(s);
+        return make_float2(v.y != 0.0f ? expf(v.x - M) : 0.0f, v.y);
+    };
+    int64_t s = s0;
+    for (; s + UN <= s1; s += UN) {
+        float x[UN];
 #pragma unroll
-        for (int i = 0; i < CH; ++i)
-            nx[i] = c1 + i < s1 ? base[(c1 + i) * stride + d] : 0.0f;
+        for (int i = 0; i < UN; ++i)
+            x[i] = xb[(s + i) * stride];
 #pragma unroll
-        for (int i = 0; i < CH; ++i) {
-            const int64_t s = c0 + i;
-            if (s < s1) {
-                float den, w;
-                if (cached) {
-                    den = d_s[s];
-                    w = w_s[s];
-                } else {
-                    den = base[s * stride + D + 1];
-                    w = den != 0.0f ? expf(base[s * stride + D] - M) : 0.0f;
-                }
-                if (den != 0.0f) {
-                    badn |= !isfinite(x[i]);
-                    acc = fmaf(x[i], w, acc);
-                }
+        for (int i = 0; i < UN; ++i) {
+            const float2 v = wd(s + i);
+            const float y = v.y != 0.0f ? x[i] : 0.0f;
+            acc = fmaf(y, v.x, acc);
+            chk = fmaf(y, 0.0f, chk);
+        }
+    }
+    for (; s < s1; ++s) {
+        const float2 v = wd(s);
+        const float y = v.y != 0.0f ? xb[s * stride] : 0.0f;
+        acc = fmaf(y, v.x, acc);
+        chk = fmaf(y, 0.0f, chk);
+    }
+    accw[warp][lane] = acc;
+    bad |= __syncthreads_or(!isfinite(chk));
+
+    float o = 0.0f, l = 0.0f;
+    if (warp == 0) {
+        o = accw[0][lane];
+#pragma unroll
+        for (int w = 1; w < NW; ++w)
+            o += accw[w][lane];
+        // the sink joins as one more split of weight exp(sink - M)
+        if (sinks) {
+            const float sk = sinks[row % n_head];
+            if (L == 0.0f || sk > M) {
+                const float ms = L == 0.0f ? 0.0f : expf(M - sk);
+                o *= ms;
+                L = L * ms + 1.0f;
+                M = sk;
+            } else {
+                L += expf(sk - M);
             }
         }
-#pragma unroll
-        for (int i = 0; i < CH; ++i)
-            x[i] = nx[i];
+        const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+        l = L == 0.0f ? -INFINITY : M + logf(L);
+        const bool rowbad =
+            !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
+        o *= inv;
+        bad |= __any_sync(0xffffffffu, rowbad || !isfinite(o));
+        if (lane == 0)
+            flag_s = bad;
     }
-    accs[g][d] = acc;
-    if (badn)
-        atomicOr(&bad_s, 1);
-    __syncthreads();
-    if (g != 0)
-        return;
-    acc = accs[0][d];
-#pragma unroll
-    for (int i = 1; i < NG; ++i)
-        acc += accs[i][d];
-    if (sinks) {
-        const float sk = sinks[row % n_head];
-        if (L == 0.0f || sk > M) {
-            const float ms = L == 0.0f ? 0.0f : expf(M - sk);
-            acc *= ms;
-            L = L * ms + 1.0f;
-            M = sk;
-        } else {
-            L += expf(sk - M);
-        }
+    // OR the flags of the row's CTAs; the second barrier keeps every CTA's
+    // shared memory alive until all peers have read it
+    cluster_sync();
+    int poison = 0;
+    if (warp == 0 && lane < NC)
+        poison = ld_peer_flag(&flag_s, (uint32_t)lane);
+    poison = __any_sync(0xffffffffu, poison);
+    cluster_sync();
+    if (warp == 0) {
+        out[row * D + d] = poison ? NAN : o;
+        if (lse && chunk == 0 && lane == 0)
+            lse[row] = poison ? NAN : l;
     }
-    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-    const float l = L == 0.0f ? -INFINITY : M + logf(L);
-    const bool rowbad = !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
-    const float o = acc * inv;
-    if (!isfinite(o) || rowbad)
-        atomicOr(&bad_s, 1);
-    asm volatile("bar.sync 1, %0;" ::"r"(D)); // group 0 only (D threads)
-    const bool poison = bad_s != 0;
-    out[row * D + d] = poison ? NAN : o;
-    if (lse && d == 0)
-        lse[row] = poison ? NAN : l;
 }
 
 // ---------------------------------------------------------------------------
@@ -602,14 +620,32 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
                          cudaStream_t st) {
     if (n_rows <= 0)
         return cudaSuccess;
-    dim3 grid((unsigned)n_rows);
+    if (n_rows * (D / 32) > 0x7fffffff)
+        return cudaErrorInvalidValue;
+    void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int);
     switch (D) {
-    case 64: lse_merge_kernel<64><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
-    case 128: lse_merge_kernel<128><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
-    case 256: lse_merge_kernel<256><<<grid, 512, 0, st>>>(partials, n_splits, n_rows, out, lse, sinks, n_head); break;
+    case 64: kern = lse_merge_kernel<64>; break;
+    case 128: kern = lse_merge_kernel<128>; break;
+    case 256: kern = lse_merge_kernel<256>; break;
     default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
+    // one cluster of D / 32 CTAs per row; launched as a programmatic dependent
+    // of the kernel before it on the stream (the merge waits for it in-kernel)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(n_rows * (D / 32)), 1, 1);
+    cfg.blockDim = dim3(mg::NT, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)(D / 32);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, partials, n_splits, n_rows, out, lse, sinks, n_head);
 }
 
 } // namespace xq

@@ -26,6 +26,8 @@
 #include <float.h>
 #include <math.h>
 
+#include <utility>
+
 #include "xq_common.cuh"
 #include "xq_internal.h"
 
@@ -161,6 +163,66 @@ __device__ __forceinline__ uint32_t u4pair_to_h2(uint32_t x) {
     return *reinterpret_cast<uint32_t *>(&r);
 }
 
+// Compile-time loop: f(std::integral_constant<int, I>) for I in [0, N).
+template <class F, int... I>
+__device__ __forceinline__ void static_for_impl(F &&f, std::integer_sequence<int, I...>) {
+    (f(std::integral_constant<int, I>{}), ...);
+}
+template <int N, class F>
+__device__ __forceinline__ void static_for(F &&f) {
+    static_for_impl(f, std::make_integer_sequence<int, N>{});
+}
+// Shared-memory loads at a register base plus a compile-time byte offset.
+template <int OFF>
+__device__ __forceinline__ uint32_t lds16(uint32_t base) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1+%2];\n" : "=h"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ uint32_t lds32(uint32_t base) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];\n" : "=r"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ float2 ldsf2(uint32_t base) {
+    float2 v;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2+%3];\n"
+                 : "=f"(v.x), "=f"(v.y)
+                 : "r"(base), "n"(OFF));
+    return v;
+}
+template <int OFF>
+__device__ __forceinline__ int2 ldsi2(uint32_t base) {
+    int2 v;
+    asm volatile("ld.shared.v2.s32 {%0, %1}, [%2+%3];\n" : "=r"(v.x), "=r"(v.y) : "r"(base), "n"(OFF));
+    return v;
+}
+// 32-bit word at a 2-byte aligned offset (even quant blocks start at +2 mod 4).
+template <int OFF, bool ALIGNED4>
+__device__ __forceinline__ uint32_t ldsw(uint32_t base) {
+    if constexpr (ALIGNED4)
+        return lds32<OFF>(base);
+    else
+        return __byte_perm(lds16<OFF>(base), lds16<OFF + 2>(base), 0x5410);
+}
+__device__ __forceinline__ float u16f(uint32_t h) { return __half2float(__ushort_as_half((uint16_t)h)); }
+template <int OFF>
+__device__ __forceinline__ void ldsm4(uint32_t base, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                      uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4+%5];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(base), "n"(OFF));
+}
+template <int OFF>
+__device__ __forceinline__ void ldsm4t(uint32_t base, uint32_t &r0, uint32_t &r1, uint32_t &r2,
+                                       uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4+%5];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(base), "n"(OFF));
+}
+
 // Output dim of O^T tile m, fragment row (g or g + 8) -> dim (the V gathers
 // permute dims so that one load per key feeds two M-tiles).
 template <int T>
@@ -180,9 +242,9 @@ __device__ __forceinline__ int out_dim(int m, int row) {
 
 template <int T, int D, int STAGES, int VW>
 __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs a) {
+    using namespace dm;
     // 16-byte aligned rows: one bulk copy per key row; otherwise per-lane cp.async
     constexpr bool BULK = VW == 16;
-    using namespace dm;
     constexpr int REC = rec_bytes(T, D);
     constexpr int SS = smem_stride(REC);
     constexpr int NB = D / 32;             // quant blocks per row
@@ -190,9 +252,10 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     constexpr int GBYTES = KG * SS;        // one 16-key group of K (or V)
     constexpr int RING = STAGES * 2 * GBYTES;
     constexpr int VPR = REC / VW;
+    constexpr int BB = T == kQ8 ? 34 : 18; // bytes per quant block
     static_assert(REC % VW == 0, "copy width");
-
-    constexpr int OWB = NWARP * 8 * D * 4;  // merge buffer, aliases the rings
+    constexpr int OWS = D + 4;              // merge buffer row stride (bank spread)
+    constexpr int OWB = NWARP * 8 * OWS * 4; // merge buffer, aliases the rings
     constexpr int BIG = NWARP * RING > OWB ? NWARP * RING : OWB;
 
     extern __shared__ __align__(16) uint8_t smem[];
@@ -214,14 +277,18 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     const int64_t split = a.split_begin + blockIdx.x;
     const int64_t r0 = split * a.rows_per_split;
     const int64_t r1 = min((int64_t)a.n_kv, r0 + a.rows_per_split);
+    const int nrows_split = (int)max((int64_t)0, r1 - r0);
     const int jbase = qb * 8;
     const int nj = min(8, a.n_qrows - jbase);
-    const uint8_t *kbase = a.k + (int64_t)kvh * a.k_nb2 + (int64_t)(s / a.rk3) * a.k_nb3;
-    const uint8_t *vbase = a.v + (int64_t)kvh * a.v_nb2 + (int64_t)(s / a.rv3) * a.v_nb3;
+    const uint8_t *kbase = a.k + (int64_t)kvh * a.k_nb2 + (int64_t)(s / a.rk3) * a.k_nb3 +
+                           r0 * a.k_nb1;
+    const uint8_t *vbase = a.v + (int64_t)kvh * a.v_nb2 + (int64_t)(s / a.rv3) * a.v_nb3 +
+                           r0 * a.v_nb1;
 
-    // ---- per-warp load pipeline ----
-    const int64_t n_groups = r1 > r0 ? (r1 - r0 + KG - 1) / KG : 0;
+    // ---- per-warp load pipeline over this warp's 16-key groups ----
+    const int n_groups = (nrows_split + KG - 1) / KG;
     uint8_t *ring = rings + warp * RING;
+    const uint32_t ring_s = smem_u32(ring);
     uint64_t *mybar = bar_s + warp * STAGES;
     if constexpr (BULK) {
         if (lane < STAGES)
@@ -229,20 +296,20 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         __syncwarp();
     }
-    auto issue = [&](int64_t grp, int stage) {
-        const int64_t k0 = r0 + grp * KG;
+    auto issue = [&](int grp, int stage) {
+        const int k0 = grp * KG; // relative to r0
         uint8_t *kd = ring + stage * 2 * GBYTES;
         uint8_t *vd = kd + GBYTES;
         if constexpr (BULK) {
-            const int nrows = (int)min((int64_t)KG, r1 - k0);
+            const int nrows = min(KG, nrows_split - k0);
             const uint32_t bar = smem_u32(mybar + stage);
             if (lane == 0)
                 mbar_expect_tx(bar, (uint32_t)(2 * nrows * REC));
             const int r = lane & (KG - 1);
             uint8_t *dst = (lane < KG ? kd : vd) + r * SS;
             if (r < nrows) {
-                const uint8_t *src = lane < KG ? kbase + (k0 + r) * a.k_nb1
-                                               : vbase + (k0 + r) * a.v_nb1;
+                const uint8_t *src = lane < KG ? kbase + (int64_t)(k0 + r) * a.k_nb1
+                                               : vbase + (int64_t)(k0 + r) * a.v_nb1;
                 bulk_g2s(smem_u32(dst), src, REC, bar);
             } else if (lane >= KG) {
                 // V rows past the split end must be finite zeros (p = 0 there)
@@ -252,8 +319,8 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
         } else {
             for (int idx = lane; idx < KG * VPR; idx += 32) {
                 const int r = idx / VPR, c = idx - r * VPR;
-                const bool ok = k0 + r < r1;
-                const int64_t row = ok ? k0 + r : r0;
+                const bool ok = k0 + r < nrows_split;
+                const int64_t row = ok ? k0 + r : 0;
                 cp_async_zfill<VW>(smem_u32(kd + r * SS + c * VW), kbase + row * a.k_nb1 + c * VW,
                                    ok ? VW : 0);
                 cp_async_zfill<VW>(smem_u32(vd + r * SS + c * VW), vbase + row * a.v_nb1 + c * VW,
@@ -262,11 +329,11 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
         }
     };
     // my groups: warp + NWARP * i
-    const int64_t my_n = n_groups > warp ? (n_groups - warp + NWARP - 1) / NWARP : 0;
+    const int my_n = n_groups > warp ? (n_groups - warp + NWARP - 1) / NWARP : 0;
 #pragma unroll
     for (int st = 0; st < STAGES - 1; ++st) {
         if (st < my_n)
-            issue(warp + (int64_t)NWARP * st, st);
+            issue(warp + NWARP * st, st);
         if constexpr (!BULK)
             cp_async_commit();
     }
@@ -309,25 +376,46 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
             q16[idx] = __float2half_rn(x);
         }
     } else {
+        // ggml quantize_row_q8_0 reference arithmetic; two threads per 32-block
         int8_t *q8 = reinterpret_cast<int8_t *>(qsm);
-        for (int blk = warp; blk < 8 * NB; blk += NWARP) {
+        for (int u = tid; u < 8 * NB * 2; u += NT) {
+            const int blk = u >> 1, half = u & 1;
             const int j = blk / NB, b = blk - j * NB;
-            float x = 0.0f;
+            float x[16];
             if (j < nj) {
                 const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
-                x = *reinterpret_cast<const float *>(a.q + (int64_t)iq1 * a.q_nb1 +
-                                                     (int64_t)h * a.q_nb2 +
-                                                     (int64_t)s * a.q_nb3 + 4 * (b * 32 + lane));
+                const float *src = reinterpret_cast<const float *>(
+                    a.q + (int64_t)iq1 * a.q_nb1 + (int64_t)h * a.q_nb2 + (int64_t)s * a.q_nb3) +
+                    b * 32 + half * 16;
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    x[i] = src[i];
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    x[i] = 0.0f;
             }
-            const float amax = warp_max(fabsf(x));
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                amax = fmaxf(amax, fabsf(x[i]));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             const float d = amax / 127.0f;
             const float id = d != 0.0f ? 1.0f / d : 0.0f;
-            const int qi = (int)roundf(x * id);
-            q8[j * D + b * 32 + lane] = (int8_t)qi;
-            const int qsum = __reduce_add_sync(0xffffffffu, qi);
-            if (lane == 0) {
+            uint32_t w[4] = {0, 0, 0, 0};
+            int qs = 0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int qi = (int)roundf(x[i] * id);
+                qs += qi;
+                w[i >> 2] |= (uint32_t)(uint8_t)(int8_t)qi << (8 * (i & 3));
+            }
+            qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+            *reinterpret_cast<uint4 *>(q8 + j * D + b * 32 + half * 16) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+            if (half == 0) {
                 dq_s[b * 8 + j] = __half2float(__float2half_rn(d));
-                qsum_s[b * 8 + j] = 8 * qsum;
+                qsum_s[b * 8 + j] = 8 * qs;
             }
         }
     }
@@ -353,9 +441,13 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     }
     // this lane's two q-rows (columns 2t, 2t+1)
     const int c0 = 2 * t, c1 = 2 * t + 1;
+    const bool plain = !a.mask && !a.positions && a.softcap == 0.0f; // uniform
+    const bool live0 = c0 < nj, live1 = c1 < nj;
     const float slope0 = slope_s[c0], slope1 = slope_s[c1];
     const int lim0 = lim_s[c0], lim1 = lim_s[c1];
     const int64_t mo0 = moff_s[c0], mo1 = moff_s[c1];
+    const uint32_t dq_base = smem_u32(dq_s + c0);    // + 32 * b
+    const uint32_t qs_base = smem_u32(qsum_s + c0);  // + 32 * b
 
     float acc[MT][4];
 #pragma unroll
@@ -364,15 +456,15 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     float mu0 = -INFINITY, mu1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
     float *pt = pt_s + warp * 128;
 
-    for (int64_t i = 0; i < my_n; ++i) {
+    for (int i = 0; i < my_n; ++i) {
         {
-            const int64_t nxt = i + STAGES - 1;
+            const int nxt = i + STAGES - 1;
             if (nxt < my_n)
-                issue(warp + NWARP * nxt, (int)(nxt % STAGES));
+                issue(warp + NWARP * nxt, nxt % STAGES);
             if constexpr (!BULK)
                 cp_async_commit();
         }
-        const int stage = (int)(i % STAGES);
+        const int stage = i % STAGES;
         if constexpr (BULK) {
             // warp-uniform outcome: the MMAs and shuffles below are warp-collective
             if (!__all_sync(0xffffffffu,
@@ -385,86 +477,81 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
             cp_async_wait<STAGES - 1>();
         }
         __syncwarp();
-        const uint8_t *kg = ring + stage * 2 * GBYTES;
-        const uint8_t *vg = kg + GBYTES;
-        const int64_t k0 = r0 + (warp + NWARP * i) * KG;
+        const uint32_t kg_s = ring_s + stage * 2 * GBYTES;
+        const uint32_t vg_s = kg_s + GBYTES;
+        const int k0 = (warp + NWARP * i) * KG; // relative to r0
 
         // ---------------- scores S^T[key][q-row] ----------------
-        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f}; // (g,c0) (g,c1) (g+8,c0) (g+8,c1)
+        float2 sA = make_float2(0.0f, 0.0f), sB = make_float2(0.0f, 0.0f); // keys g, g+8
         if constexpr (T == kF16) {
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
+            float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const uint32_t kl = kg_s + ((lane & 7) + ((lane >> 3) & 1) * 8) * SS +
+                                ((lane >> 4) & 1) * 16;
+            static_for<D / 16>([&](auto kk_) {
+                constexpr int kk = decltype(kk_)::value;
                 uint32_t a0, a1, a2, a3;
-                const int key = (lane & 7) + ((lane >> 3) & 1) * 8;
-                const int dim = 16 * kk + ((lane >> 4) & 1) * 8;
-                ldsm_x4(smem_u32(kg + key * SS + 2 * dim), a0, a1, a2, a3);
+                ldsm4<32 * kk>(kl, a0, a1, a2, a3);
                 mma_f16(sc, a0, a1, a2, a3, qf[2 * kk], qf[2 * kk + 1]);
-            }
+            });
+            sA = make_float2(sc[0], sc[1]);
+            sB = make_float2(sc[2], sc[3]);
         } else {
-            const uint8_t *rg = kg + g * SS, *rg8 = kg + (g + 8) * SS;
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                constexpr int BB = T == kQ8 ? 34 : 18;
-                const int qo = BB * b + 2;
+            const uint32_t kA = kg_s + g * SS, kB = kA + 8 * SS;
+            const uint32_t kAt = kA + 4 * t, kBt = kB + 4 * t;
+            static_for<NB>([&](auto b_) {
+                constexpr int b = decltype(b_)::value;
+                constexpr int QO = BB * b + 2;
+                constexpr bool AL = (QO % 4) == 0;
                 int c[4] = {0, 0, 0, 0};
                 if constexpr (T == kQ8) {
-                    uint32_t a0, a1, a2, a3;
-                    if (b & 1) {
-                        a0 = ld_word<true>(rg + qo + 4 * t);
-                        a1 = ld_word<true>(rg8 + qo + 4 * t);
-                        a2 = ld_word<true>(rg + qo + 16 + 4 * t);
-                        a3 = ld_word<true>(rg8 + qo + 16 + 4 * t);
-                    } else {
-                        a0 = ld_word<false>(rg + qo + 4 * t);
-                        a1 = ld_word<false>(rg8 + qo + 4 * t);
-                        a2 = ld_word<false>(rg + qo + 16 + 4 * t);
-                        a3 = ld_word<false>(rg8 + qo + 16 + 4 * t);
-                    }
-                    mma_s8(c, a0, a1, a2, a3, qf[2 * b], qf[2 * b + 1]);
+                    mma_s8(c, ldsw<QO, AL>(kAt), ldsw<QO, AL>(kBt), ldsw<QO + 16, AL>(kAt),
+                           ldsw<QO + 16, AL>(kBt), qf[2 * b], qf[2 * b + 1]);
                 } else {
-                    uint32_t w0, w1;
-                    if (b & 1) {
-                        w0 = ld_word<true>(rg + qo + 4 * t);
-                        w1 = ld_word<true>(rg8 + qo + 4 * t);
-                    } else {
-                        w0 = ld_word<false>(rg + qo + 4 * t);
-                        w1 = ld_word<false>(rg8 + qo + 4 * t);
-                    }
+                    const uint32_t w0 = ldsw<QO, AL>(kAt), w1 = ldsw<QO, AL>(kBt);
                     mma_u8s8(c, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
                              (w1 >> 4) & 0x0F0F0F0Fu, qf[2 * b], qf[2 * b + 1]);
-                    const int2 qs8 = *reinterpret_cast<const int2 *>(qsum_s + b * 8 + c0);
-                    c[0] -= qs8.x;
-                    c[1] -= qs8.y;
-                    c[2] -= qs8.x;
-                    c[3] -= qs8.y;
+                    const int2 q8s = ldsi2<32 * b>(qs_base);
+                    c[0] -= q8s.x;
+                    c[1] -= q8s.y;
+                    c[2] -= q8s.x;
+                    c[3] -= q8s.y;
                 }
-                const float dk0 = h2f(rg + BB * b), dk1 = h2f(rg8 + BB * b);
-                const float2 dq = *reinterpret_cast<const float2 *>(dq_s + b * 8 + c0);
-                sc[0] += (float)c[0] * (dk0 * dq.x);
-                sc[1] += (float)c[1] * (dk0 * dq.y);
-                sc[2] += (float)c[2] * (dk1 * dq.x);
-                sc[3] += (float)c[3] * (dk1 * dq.y);
-            }
+                const float dk0 = u16f(lds16<BB * b>(kA)), dk1 = u16f(lds16<BB * b>(kB));
+                const float2 dq = ldsf2<32 * b>(dq_base);
+                sA = __ffma2_rn(make_float2((float)c[0], (float)c[1]),
+                                __fmul2_rn(make_float2(dk0, dk0), dq), sA);
+                sB = __ffma2_rn(make_float2((float)c[2], (float)c[3]),
+                                __fmul2_rn(make_float2(dk1, dk1), dq), sB);
+            });
         }
 
         // ---------------- mask, softmax (log2 domain) ----------------
-        const int64_t kA = k0 + g, kB = k0 + g + 8;
-        float x[4];
+        const int remk = nrows_split - k0; // keys g < remk are inside the split
+        float x[4] = {sA.x, sA.y, sB.x, sB.y}; // (g,c0) (g,c1) (g+8,c0) (g+8,c1)
+        if (plain) {
+            const float sl = a.scale * kLog2e;
+            x[0] = (g < remk && live0) ? x[0] * sl : -INFINITY;
+            x[1] = (g < remk && live1) ? x[1] * sl : -INFINITY;
+            x[2] = (g + 8 < remk && live0) ? x[2] * sl : -INFINITY;
+            x[3] = (g + 8 < remk && live1) ? x[3] * sl : -INFINITY;
+        } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int64_t key = (e < 2) ? kA : kB;
-            const int col = e & 1;
-            float v = sc[e] * a.scale;
-            if (a.softcap != 0.0f)
-                v = a.softcap * tanhf(v);
-            bool dead = key >= r1 || key >= (col ? lim1 : lim0);
-            if (a.mask && !dead) {
-                const float mv = (col ? slope1 : slope0) *
-                                 h2f(a.mask + (col ? mo1 : mo0) + 2 * key);
-                dead = mv == -INFINITY;
-                v += mv;
+            for (int e = 0; e < 4; ++e) {
+                const int kr = k0 + g + (e >> 1) * 8; // relative key
+                const int64_t key = r0 + kr;
+                const int col = e & 1;
+                float v = x[e] * a.scale;
+                if (a.softcap != 0.0f)
+                    v = a.softcap * tanhf(v);
+                bool dead = kr >= nrows_split || key >= (col ? lim1 : lim0);
+                if (a.mask && !dead) {
+                    const float mv = (col ? slope1 : slope0) *
+                                     h2f(a.mask + (col ? mo1 : mo0) + 2 * key);
+                    dead = mv == -INFINITY;
+                    v += mv;
+                }
+                x[e] = dead ? -INFINITY : v * kLog2e;
             }
-            x[e] = dead ? -INFINITY : v * kLog2e;
         }
         float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
 #pragma unroll
@@ -472,25 +559,23 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
         }
-        if (mx0 > mu0) {
-            const float f = mu0 == -INFINITY ? 0.0f : ex2(mu0 - mx0);
+        if (mx0 > mu0 || mx1 > mu1) {
+            const float f0 = mx0 > mu0 ? (mu0 == -INFINITY ? 0.0f : ex2(mu0 - mx0)) : 1.0f;
+            const float f1 = mx1 > mu1 ? (mu1 == -INFINITY ? 0.0f : ex2(mu1 - mx1)) : 1.0f;
+            const float2 ff = make_float2(f0, f1);
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
-                acc[m][0] *= f;
-                acc[m][2] *= f;
+                float2 lo = __fmul2_rn(make_float2(acc[m][0], acc[m][1]), ff);
+                float2 hi = __fmul2_rn(make_float2(acc[m][2], acc[m][3]), ff);
+                acc[m][0] = lo.x;
+                acc[m][1] = lo.y;
+                acc[m][2] = hi.x;
+                acc[m][3] = hi.y;
             }
-            l0 *= f;
-            mu0 = mx0;
-        }
-        if (mx1 > mu1) {
-            const float f = mu1 == -INFINITY ? 0.0f : ex2(mu1 - mx1);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                acc[m][1] *= f;
-                acc[m][3] *= f;
-            }
-            l1 *= f;
-            mu1 = mx1;
+            l0 *= f0;
+            l1 *= f1;
+            mu0 = fmaxf(mu0, mx0);
+            mu1 = fmaxf(mu1, mx1);
         }
         const float p0 = x[0] == -INFINITY ? 0.0f : ex2(x[0] - mu0);
         const float p1 = x[1] == -INFINITY ? 0.0f : ex2(x[1] - mu1);
@@ -502,46 +587,38 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
         *reinterpret_cast<float2 *>(pt + g * 8 + c0) = make_float2(p0, p1);
         *reinterpret_cast<float2 *>(pt + (g + 8) * 8 + c0) = make_float2(p2, p3);
         __syncwarp();
-        const float pa = pt[(2 * t) * 8 + g], pb = pt[(2 * t + 1) * 8 + g];
-        const float pc = pt[(2 * t + 8) * 8 + g], pd = pt[(2 * t + 9) * 8 + g];
+        const float2 pab = make_float2(pt[(2 * t) * 8 + g], pt[(2 * t + 1) * 8 + g]);
+        const float2 pcd = make_float2(pt[(2 * t + 8) * 8 + g], pt[(2 * t + 9) * 8 + g]);
 
         // ---------------- O^T += V^T P^T ----------------
         if constexpr (T == kF16) {
-            const uint32_t b0 = pack_h2(pa, pb), b1 = pack_h2(pc, pd);
-            const int key = (lane & 7) + ((lane >> 4) & 1) * 8;
-            const int dsub = ((lane >> 3) & 1) * 8;
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
+            const uint32_t b0 = pack_h2(pab.x, pab.y), b1 = pack_h2(pcd.x, pcd.y);
+            const uint32_t vl = vg_s + ((lane & 7) + ((lane >> 4) & 1) * 8) * SS +
+                                ((lane >> 3) & 1) * 16;
+            static_for<MT>([&](auto m_) {
+                constexpr int m = decltype(m_)::value;
                 uint32_t a0, a1, a2, a3;
-                ldsm_x4_t(smem_u32(vg + key * SS + 2 * (16 * m + dsub)), a0, a1, a2, a3);
+                ldsm4t<32 * m>(vl, a0, a1, a2, a3);
                 mma_f16(acc[m], a0, a1, a2, a3, b0, b1);
-            }
+            });
         } else {
-            const uint8_t *va = vg + (2 * t) * SS, *vb = vg + (2 * t + 1) * SS;
-            const uint8_t *vc = vg + (2 * t + 8) * SS, *vd = vg + (2 * t + 9) * SS;
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-                constexpr int BB = T == kQ8 ? 34 : 18;
-                const uint32_t b0 = pack_h2(pa * h2f(va + BB * b), pb * h2f(vb + BB * b));
-                const uint32_t b1 = pack_h2(pc * h2f(vc + BB * b), pd * h2f(vd + BB * b));
+            const uint32_t vA = vg_s + (2 * t) * SS, vB = vA + SS, vC = vA + 8 * SS,
+                           vD = vC + SS;
+            const uint32_t lo = T == kQ8 ? 4 * g : 2 * g; // this lane's code bytes
+            static_for<NB>([&](auto b_) {
+                constexpr int b = decltype(b_)::value;
+                constexpr int SO = BB * b, CO = BB * b + 2;
+                const float2 p01 = __fmul2_rn(
+                    pab, make_float2(u16f(lds16<SO>(vA)), u16f(lds16<SO>(vB))));
+                const float2 p23 = __fmul2_rn(
+                    pcd, make_float2(u16f(lds16<SO>(vC)), u16f(lds16<SO>(vD))));
+                const uint32_t b0 = pack_h2(p01.x, p01.y), b1 = pack_h2(p23.x, p23.y);
                 if constexpr (T == kQ8) {
-                    const int o = 34 * b + 2 + 4 * g;
-                    uint32_t wa, wb, wc, wd;
-                    if (b & 1) {
-                        wa = ld_word<true>(va + o);
-                        wb = ld_word<true>(vb + o);
-                        wc = ld_word<true>(vc + o);
-                        wd = ld_word<true>(vd + o);
-                    } else {
-                        wa = ld_word<false>(va + o);
-                        wb = ld_word<false>(vb + o);
-                        wc = ld_word<false>(vc + o);
-                        wd = ld_word<false>(vd + o);
-                    }
-                    wa ^= 0x80808080u;
-                    wb ^= 0x80808080u;
-                    wc ^= 0x80808080u;
-                    wd ^= 0x80808080u;
+                    constexpr bool AL = (CO % 4) == 0;
+                    const uint32_t wa = ldsw<CO, AL>(vA + lo) ^ 0x80808080u;
+                    const uint32_t wb = ldsw<CO, AL>(vB + lo) ^ 0x80808080u;
+                    const uint32_t wc = ldsw<CO, AL>(vC + lo) ^ 0x80808080u;
+                    const uint32_t wd = ldsw<CO, AL>(vD + lo) ^ 0x80808080u;
                     // tile 2b: bytes 0 (row g) and 1 (row g+8); tile 2b+1: bytes 2, 3
                     mma_f16(acc[2 * b], s8pair_to_h2(__byte_perm(wa, wb, 0x0400)),
                             s8pair_to_h2(__byte_perm(wa, wb, 0x0501)),
@@ -552,23 +629,24 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
                             s8pair_to_h2(__byte_perm(wc, wd, 0x0602)),
                             s8pair_to_h2(__byte_perm(wc, wd, 0x0703)), b0, b1);
                 } else {
-                    const int o = 18 * b + 2 + 2 * g;
-                    const uint32_t ua = *reinterpret_cast<const uint16_t *>(va + o);
-                    const uint32_t ub = *reinterpret_cast<const uint16_t *>(vb + o);
-                    const uint32_t uc = *reinterpret_cast<const uint16_t *>(vc + o);
-                    const uint32_t ud = *reinterpret_cast<const uint16_t *>(vd + o);
-                    const uint32_t xab = ua | (ub << 16), xcd = uc | (ud << 16);
+                    const uint32_t xab = __byte_perm(lds16<CO>(vA + lo), lds16<CO>(vB + lo), 0x5410);
+                    const uint32_t xcd = __byte_perm(lds16<CO>(vC + lo), lds16<CO>(vD + lo), 0x5410);
                     // tile 2b: low nibbles (dims 2g, 2g+1); tile 2b+1: high nibbles
                     mma_f16(acc[2 * b], u4pair_to_h2(xab), u4pair_to_h2(xab >> 8),
                             u4pair_to_h2(xcd), u4pair_to_h2(xcd >> 8), b0, b1);
                     mma_f16(acc[2 * b + 1], u4pair_to_h2(xab >> 4), u4pair_to_h2(xab >> 12),
                             u4pair_to_h2(xcd >> 4), u4pair_to_h2(xcd >> 12), b0, b1);
                 }
-            }
+            });
         }
         __syncwarp(); // pt and this stage are reused
     }
-    cp_async_wait<0>();
+    if constexpr (!BULK)
+        cp_async_wait<0>();
+
+    // the merge kernel that follows may start launching (it waits for this
+    // grid's completion before reading the partials)
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
     // ---- per-warp state -> shared memory ----
 #pragma unroll
@@ -577,68 +655,118 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
         l1 += __shfl_xor_sync(0xffffffffu, l1, o);
     }
     __syncthreads(); // every warp is done with its ring: reuse it for O
-    float *ow = reinterpret_cast<float *>(rings); // [NWARP][8][D]
+    float *ow = reinterpret_cast<float *>(rings); // [NWARP][8][OWS]
     if (g == 0) {
         mw_s[warp * 8 + c0] = mu0;
         mw_s[warp * 8 + c1] = mu1;
         lw_s[warp * 8 + c0] = l0;
         lw_s[warp * 8 + c1] = l1;
     }
+    {
+        float *o0 = ow + (warp * 8 + c0) * OWS, *o1 = ow + (warp * 8 + c1) * OWS;
+        if constexpr (T == kQ8) {
+            // dims 32b + 4g .. +3 of one q-row are adjacent: one 16-byte store
 #pragma unroll
-    for (int m = 0; m < MT; ++m) {
-        ow[(warp * 8 + c0) * D + out_dim<T>(m, g)] = acc[m][0];
-        ow[(warp * 8 + c1) * D + out_dim<T>(m, g)] = acc[m][1];
-        ow[(warp * 8 + c0) * D + out_dim<T>(m, g + 8)] = acc[m][2];
-        ow[(warp * 8 + c1) * D + out_dim<T>(m, g + 8)] = acc[m][3];
+            for (int b = 0; b < NB; ++b) {
+                *reinterpret_cast<float4 *>(o0 + 32 * b + 4 * g) =
+                    make_float4(acc[2 * b][0], acc[2 * b][2], acc[2 * b + 1][0], acc[2 * b + 1][2]);
+                *reinterpret_cast<float4 *>(o1 + 32 * b + 4 * g) =
+                    make_float4(acc[2 * b][1], acc[2 * b][3], acc[2 * b + 1][1], acc[2 * b + 1][3]);
+            }
+        } else if constexpr (T == kQ4) {
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                *reinterpret_cast<float2 *>(o0 + 32 * b + 2 * g) =
+                    make_float2(acc[2 * b][0], acc[2 * b][2]);
+                *reinterpret_cast<float2 *>(o0 + 32 * b + 16 + 2 * g) =
+                    make_float2(acc[2 * b + 1][0], acc[2 * b + 1][2]);
+                *reinterpret_cast<float2 *>(o1 + 32 * b + 2 * g) =
+                    make_float2(acc[2 * b][1], acc[2 * b][3]);
+                *reinterpret_cast<float2 *>(o1 + 32 * b + 16 + 2 * g) =
+                    make_float2(acc[2 * b + 1][1], acc[2 * b + 1][3]);
+            }
+        } else {
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                const int dA = out_dim<T>(m, g), dB = out_dim<T>(m, g + 8);
+                o0[dA] = acc[m][0];
+                o1[dA] = acc[m][1];
+                o0[dB] = acc[m][2];
+                o1[dB] = acc[m][3];
+            }
+        }
     }
     __syncthreads();
-
-    // ---- fixed-order merge of the warps; direct output or partial record ----
-    for (int idx = tid; idx < nj * D; idx += NT) {
-        const int j = idx / D, d = idx - j * D;
+    // per q-row: the warps' merge weights (fixed warp order) with the final
+    // normalisation folded in, the row's statistics, and its output address
+    float4 *wt_s = reinterpret_cast<float4 *>(pt_s); // [8] (pt is free now)
+    float **optr_s = reinterpret_cast<float **>(wt_s + 8); // [8]
+    if (tid < nj) {
+        const int j = tid;
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NWARP; ++w)
             if (lw_s[w * 8 + j] != 0.0f)
                 M = fmaxf(M, mw_s[w * 8 + j]);
-        float L = 0.0f, o = 0.0f;
+        float f[NWARP], L = 0.0f;
 #pragma unroll
         for (int w = 0; w < NWARP; ++w) {
             const float lw = lw_s[w * 8 + j];
-            if (lw != 0.0f) {
-                const float f = ex2(mw_s[w * 8 + j] - M);
-                L += lw * f;
-                o += ow[(w * 8 + j) * D + d] * f;
-            }
+            f[w] = lw != 0.0f ? ex2(mw_s[w * 8 + j] - M) : 0.0f;
+            L += lw * f[w];
         }
-        float m_nat = M * kLn2;
+        float m_nat = M * kLn2, fin = 1.0f;
         const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
         const int64_t orow = ((int64_t)s * a.n_q + iq1) * a.n_head + h;
+        float *optr;
         if (a.direct) {
             if (a.sinks) {
                 const float sk = a.sinks[h];
                 if (L == 0.0f || sk > m_nat) {
                     const float ms = L == 0.0f ? 0.0f : expf(m_nat - sk);
-                    o *= ms;
+                    fin = ms;
                     L = L * ms + 1.0f;
                     m_nat = sk;
                 } else {
                     L += expf(sk - m_nat);
                 }
             }
-            const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-            a.dst[orow * D + d] = o * inv;
-            if (a.lse && d == 0)
+            fin *= L == 0.0f ? 0.0f : 1.0f / L;
+            if (a.lse)
                 a.lse[orow] = L == 0.0f ? -INFINITY : m_nat + logf(L);
+            optr = a.dst + orow * D;
         } else {
-            float *rec = a.partials +
-                         ((split - a.split_begin) * (int64_t)a.n_seq * a.n_q * a.n_head + orow) *
-                             (D + 2);
-            rec[d] = o;
-            if (d == 0) {
-                rec[D] = L == 0.0f ? -FLT_MAX : m_nat;
-                rec[D + 1] = L;
-            }
+            optr = a.partials +
+                   ((split - a.split_begin) * (int64_t)a.n_seq * a.n_q * a.n_head + orow) * (D + 2);
+            optr[D] = L == 0.0f ? -FLT_MAX : m_nat;
+            optr[D + 1] = L;
+        }
+        static_assert(NWARP == 4, "weights are one float4");
+        wt_s[j] = make_float4(f[0] * fin, f[1] * fin, f[2] * fin, f[3] * fin);
+        optr_s[j] = optr;
+    }
+    __syncthreads();
+
+    // ---- merged output: direct, or the split's partial record ----
+    constexpr int HP = D / 2; // dim pairs per q-row
+    const bool vec = ((reinterpret_cast<uintptr_t>(a.direct ? a.dst : a.partials)) & 7) == 0;
+    for (int idx = tid; idx < nj * HP; idx += NT) {
+        const int j = idx / HP, d = 2 * (idx - j * HP);
+        const float4 wt = wt_s[j];
+        const float2 x0 = *reinterpret_cast<const float2 *>(ow + (0 * 8 + j) * OWS + d);
+        const float2 x1 = *reinterpret_cast<const float2 *>(ow + (1 * 8 + j) * OWS + d);
+        const float2 x2 = *reinterpret_cast<const float2 *>(ow + (2 * 8 + j) * OWS + d);
+        const float2 x3 = *reinterpret_cast<const float2 *>(ow + (3 * 8 + j) * OWS + d);
+        float2 o = __fmul2_rn(x0, make_float2(wt.x, wt.x));
+        o = __ffma2_rn(x1, make_float2(wt.y, wt.y), o);
+        o = __ffma2_rn(x2, make_float2(wt.z, wt.z), o);
+        o = __ffma2_rn(x3, make_float2(wt.w, wt.w), o);
+        float *p = optr_s[j] + d;
+        if (vec) {
+            *reinterpret_cast<float2 *>(p) = o;
+        } else {
+            p[0] = o.x;
+            p[1] = o.y;
         }
     }
 }
@@ -651,7 +779,7 @@ static int mma_stages(int type, int D) { return smem_stride(rec_bytes(type, D)) 
 size_t decode_mma_smem(int type, int D) {
     const int SS = smem_stride(rec_bytes(type, D));
     const size_t ring = (size_t)dm::NWARP * mma_stages(type, D) * 2 * dm::KG * SS;
-    const size_t ow = (size_t)dm::NWARP * 8 * D * 4;
+    const size_t ow = (size_t)dm::NWARP * 8 * (D + 4) * 4;
     size_t b = ring > ow ? ring : ow;
     b += (size_t)8 * D * 2 + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
     b += (size_t)dm::NWARP * 128 * 4 + 2 * dm::NWARP * 8 * 4 + 8 * 4 + 8 * 8 + 8 * 4;
