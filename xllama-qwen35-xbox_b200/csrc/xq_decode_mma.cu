@@ -23,8 +23,11 @@
 //                   with dims permuted so one 16/32-bit load per key feeds
 //                   two M-tiles; the per-(key, block) scale is folded into P.
 // Accumulation is fp32 throughout.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <float.h>
 #include <math.h>
+#include <string.h>
 
 #include <utility>
 
@@ -37,6 +40,15 @@ namespace dm {
 constexpr int NWARP = 4, NT = 32 * NWARP, KG = 16;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+// The running max is only moved when a group's max exceeds it by more than
+// this (log2 units), so p = 2^(x - max) stays <= 256 and the accumulator
+// rescale is rare; O = acc / l and lse = max + log(l) hold for any max.
+constexpr float kRescale = 8.0f;
+
+// Load path of a (type, copy width) pair: quantized rows whose length is a
+// multiple of 16 bytes arrive as one TMA box per 16-key group; 16-byte F16
+// rows as one bulk copy per row; anything else by per-lane cp.async.
+__host__ __device__ constexpr bool tma_mode(int T, int VW) { return VW == 16 && T != kF16; }
 
 __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                        uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -124,6 +136,15 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
         "[%3];\n" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+// One TMA tile (a 16-row box of a 4D tensor map) global -> shared.
+__device__ __forceinline__ void tma_rows(uint32_t dst, const CUtensorMap *map, int row, int head,
+                                         int seq, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(head), "r"(seq), "r"(bar)
         : "memory");
 }
 __device__ __forceinline__ float ex2(float x) {
@@ -241,10 +262,12 @@ __device__ __forceinline__ int out_dim(int m, int row) {
 } // namespace dm
 
 template <int T, int D, int STAGES, int VW>
-__global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(dm::NT, 1)
+    fa_decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
+                         const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
     using namespace dm;
-    // 16-byte aligned rows: one bulk copy per key row; otherwise per-lane cp.async
-    constexpr bool BULK = VW == 16;
+    constexpr bool TMA = tma_mode(T, VW);
+    constexpr bool BULK = VW == 16; // mbarrier-tracked copies (TMA boxes or bulk rows)
     constexpr int REC = rec_bytes(T, D);
     constexpr int SS = smem_stride(REC);
     constexpr int NB = D / 32;             // quant blocks per row
@@ -258,7 +281,15 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
     constexpr int OWB = NWARP * 8 * OWS * 4; // merge buffer, aliases the rings
     constexpr int BIG = NWARP * RING > OWB ? NWARP * RING : OWB;
 
-    extern __shared__ __align__(16) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem[];
+    if constexpr (TMA) {
+        // TMA destinations must be 128-byte aligned (all ring offsets are)
+        if (smem_u32(smem) & 127u) {
+            if (a.err && threadIdx.x == 0)
+                atomicExch(a.err, 3);
+            return;
+        }
+    }
     uint8_t *rings = smem;                                   // [NWARP][STAGES][K|V][GBYTES]
     uint8_t *qsm = rings + BIG;                              // q codes: int8 [8][D] or f16 [8][D]
     float *dq_s = reinterpret_cast<float *>(qsm + 8 * D * 2); // [NB][8]
@@ -300,7 +331,18 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
         const int k0 = grp * KG; // relative to r0
         uint8_t *kd = ring + stage * 2 * GBYTES;
         uint8_t *vd = kd + GBYTES;
-        if constexpr (BULK) {
+        if constexpr (TMA) {
+            // rows past the split end arrive too (p = 0 there); rows past n_kv
+            // are zero-filled by the copy engine
+            static_assert(SS == REC, "TMA boxes are dense");
+            if (lane == 0) {
+                const uint32_t bar = smem_u32(mybar + stage);
+                mbar_expect_tx(bar, (uint32_t)(2 * KG * REC));
+                const int row = (int)(r0 + k0);
+                tma_rows(smem_u32(kd), &kmap, row, kvh, s / a.rk3, bar);
+                tma_rows(smem_u32(vd), &vmap, row, kvh, s / a.rv3, bar);
+            }
+        } else if constexpr (BULK) {
             const int nrows = min(KG, nrows_split - k0);
             const uint32_t bar = smem_u32(mybar + stage);
             if (lane == 0)
@@ -559,9 +601,10 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
         }
-        if (mx0 > mu0 || mx1 > mu1) {
-            const float f0 = mx0 > mu0 ? (mu0 == -INFINITY ? 0.0f : ex2(mu0 - mx0)) : 1.0f;
-            const float f1 = mx1 > mu1 ? (mu1 == -INFINITY ? 0.0f : ex2(mu1 - mx1)) : 1.0f;
+        const bool up0 = mx0 > mu0 + kRescale, up1 = mx1 > mu1 + kRescale;
+        if (__any_sync(0xffffffffu, up0 || up1)) {
+            const float f0 = up0 ? (mu0 == -INFINITY ? 0.0f : ex2(mu0 - mx0)) : 1.0f;
+            const float f1 = up1 ? (mu1 == -INFINITY ? 0.0f : ex2(mu1 - mx1)) : 1.0f;
             const float2 ff = make_float2(f0, f1);
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
@@ -574,8 +617,8 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
             }
             l0 *= f0;
             l1 *= f1;
-            mu0 = fmaxf(mu0, mx0);
-            mu1 = fmaxf(mu1, mx1);
+            mu0 = up0 ? mx0 : mu0;
+            mu1 = up1 ? mx1 : mu1;
         }
         const float p0 = x[0] == -INFINITY ? 0.0f : ex2(x[0] - mu0);
         const float p1 = x[1] == -INFINITY ? 0.0f : ex2(x[1] - mu1);
@@ -774,16 +817,15 @@ __global__ void __launch_bounds__(dm::NT) fa_decode_mma_kernel(const DecodeArgs 
 // ---------------------------------------------------------------------------
 // host side
 
-static int mma_stages(int type, int D) { return smem_stride(rec_bytes(type, D)) <= 288 ? 3 : 2; }
-
-size_t decode_mma_smem(int type, int D) {
-    const int SS = smem_stride(rec_bytes(type, D));
-    const size_t ring = (size_t)dm::NWARP * mma_stages(type, D) * 2 * dm::KG * SS;
-    const size_t ow = (size_t)dm::NWARP * 8 * (D + 4) * 4;
+template <int T, int D, int ST>
+constexpr size_t mma_smem() {
+    constexpr int SS = smem_stride(rec_bytes(T, D));
+    constexpr size_t ring = (size_t)dm::NWARP * ST * 2 * dm::KG * SS;
+    constexpr size_t ow = (size_t)dm::NWARP * 8 * (D + 4) * 4;
     size_t b = ring > ow ? ring : ow;
     b += (size_t)8 * D * 2 + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
     b += (size_t)dm::NWARP * 128 * 4 + 2 * dm::NWARP * 8 * 4 + 8 * 4 + 8 * 8 + 8 * 4;
-    b += (size_t)dm::NWARP * mma_stages(type, D) * 8; // mbarriers
+    b += (size_t)dm::NWARP * ST * 8; // mbarriers
     return b;
 }
 
@@ -792,15 +834,47 @@ bool decode_mma_ok(int type, int D, const DecodeArgs &a) {
            (type == kF16 || type == kQ8 || type == kQ4);
 }
 
+// 4D map over one K or V tensor: {row bytes / 2 (u16), n_kv, n_head_kv, n_seq},
+// box = one 16-row group of one head.
+static bool encode_rows_map(CUtensorMap *m, const uint8_t *base, int rec, int n_kv, int n_hkv,
+                            int n_seq, int64_t nb1, int64_t nb2, int64_t nb3) {
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    if (!enc || rec % 16 || rec / 2 > 256 || n_kv <= 0)
+        return false;
+    cuuint64_t dims[4] = {(cuuint64_t)(rec / 2), (cuuint64_t)n_kv, (cuuint64_t)n_hkv,
+                          (cuuint64_t)n_seq};
+    cuuint64_t strides[3] = {(cuuint64_t)nb1, (cuuint64_t)nb2, (cuuint64_t)nb3};
+    cuuint32_t box[4] = {(cuuint32_t)(rec / 2), (cuuint32_t)dm::KG, 1, 1};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<uint8_t *>(base), dims, strides,
+               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int T, int D, int ST, int VW>
 static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
-    const size_t smem = decode_mma_smem(T, D);
+    constexpr size_t smem = mma_smem<T, D, ST>();
     auto kern = fa_decode_mma_kernel<T, D, ST, VW>;
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess)
-        return e;
-    kern<<<grid, dm::NT, smem, st>>>(a);
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess)
+            return e;
+        attr_set = true;
+    }
+    CUtensorMap maps[2];
+    memset(maps, 0, sizeof(maps));
+    if constexpr (dm::tma_mode(T, VW)) {
+        constexpr int REC = rec_bytes(T, D);
+        if (!encode_rows_map(&maps[0], a.k, REC, a.n_kv, a.n_head_kv, a.n_seq / a.rk3, a.k_nb1,
+                             a.k_nb2, a.k_nb3) ||
+            !encode_rows_map(&maps[1], a.v, REC, a.n_kv, a.n_head_kv, a.n_seq / a.rv3, a.v_nb1,
+                             a.v_nb2, a.v_nb3))
+            return cudaErrorNotSupported; // nothing launched: the caller picks another path
+    }
+    kern<<<grid, dm::NT, smem, st>>>(maps[0], maps[1], a);
     return cudaGetLastError();
 }
 
@@ -808,8 +882,12 @@ template <int T, int D>
 static cudaError_t mma_vw(const DecodeArgs &a, int vw, dim3 grid, cudaStream_t st) {
     constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
     if constexpr (rec_bytes(T, D) % 16 == 0)
-        if (vw == 16)
-            return launch_mma<T, D, ST, 16>(a, grid, st);
+        if (vw == 16) {
+            const cudaError_t e = launch_mma<T, D, ST, 16>(a, grid, st);
+            if (e != cudaErrorNotSupported)
+                return e;
+            vw = 8; // the layout has no tensor map: per-lane copies
+        }
     if constexpr (rec_bytes(T, D) % 8 == 0)
         if (vw >= 8)
             return launch_mma<T, D, ST, 8>(a, grid, st);

@@ -46,7 +46,6 @@ cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &cfg, dim3 gri
                           cudaStream_t st);
 // Tensor-core (warp MMA) decode: 8 q-rows per CTA, ggml q conversion only.
 bool decode_mma_ok(int type, int D, const DecodeArgs &a);
-size_t decode_mma_smem(int type, int D);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
                               cudaStream_t st);
 cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
@@ -67,6 +66,8 @@ struct PrefillShape {
     float scale;
 };
 size_t prefill_map_bytes(const PrefillShape &ps);
+// The driver's cuTensorMapEncodeTiled (PFN_cuTensorMapEncodeTiled_v12000), or null.
+void *tensor_map_encoder();
 cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, const char **why);
 
 struct GdnArgs {

@@ -555,6 +555,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
+void *tensor_map_encoder() { return reinterpret_cast<void *>(get_encode()); }
+
 size_t prefill_map_bytes(const PrefillShape &ps) {
     const size_t n_qt = (ps.n_q + pf::BM - 1) / pf::BM, n_kt = (ps.n_kv + pf::BN - 1) / pf::BN;
     return ((size_t)ps.m_planes * n_qt * n_kt + 255) / 256 * 256 + 256;
