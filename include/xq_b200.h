@@ -160,6 +160,38 @@ int xq_quantize_rows(int32_t type, const float *src, uint64_t src_row_stride, vo
                      uint64_t dst_row_stride, int64_t n_rows, int64_t n_per_row,
                      xq_stream_t stream);
 
+/* ------------------------------------------------------------------------ */
+/* Allocation-free FLASH_ATTN_EXT (this entry point has no counterpart in   */
+/* the reference).                                                           */
+/*                                                                           */
+/* Some callers cannot allocate device memory while attention runs: a host  */
+/* whose device memory was fully planned ahead by its own allocator (ggml's */
+/* graph allocator hands a backend only the tensors it planned), or a       */
+/* thread that must not call cudaMalloc because cudaMalloc may synchronize  */
+/* the device and stall every other stream.  Those callers cannot provide   */
+/* the workspace xq_flash_attn_ext needs for its split partials.  This      */
+/* variant takes the same parameters and instead uses a fixed scratch array */
+/* compiled into the library: XQ_NOALLOC_SCRATCH_BYTES of device memory    */
+/* that every GPU which loads the library holds until the process exits.    */
+/*                                                                           */
+/*  - It runs the split-KV decode kernels (never the tensor-core prefill     */
+/*    kernel) and computes the same results as xq_flash_attn_ext.            */
+/*  - The first call on a device looks up the scratch address for that     */
+/*    device (cudaGetSymbolAddress); make that first call before any stream */
+/*    capture.                                                               */
+/*  - A call whose split plan needs more scratch than the maximum returns   */
+/*    XQ_ERR_WORKSPACE with the sizes in xq_last_error(); pass a smaller    */
+/*    n_splits.                                                              */
+/*  - All calls share the one array and it keeps the last call's contents;  */
+/*    nothing in it has to start at zero (every partial record is written   */
+/*    before it is read).  Calls that overlap on the GPU (other streams,    */
+/*    other threads) race on the scratch: serialize them.                   */
+/*  - It allocates nothing: no cudaMalloc, cudaFree or allocating library   */
+/*    routine.                                                               */
+/* ------------------------------------------------------------------------ */
+#define XQ_NOALLOC_SCRATCH_BYTES (8u << 20)
+int xq_flash_attn_ext_noalloc(const xq_fa_params *p, xq_stream_t stream);
+
 /* Library identity and the last error message of this thread. */
 const char *xq_version(void);
 const char *xq_last_error(void);

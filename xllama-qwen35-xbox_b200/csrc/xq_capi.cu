@@ -7,6 +7,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 
 #include "xq_common.cuh"
@@ -516,3 +517,67 @@ int xq_quantize_rows(int32_t type, const float *src, uint64_t src_row_stride, vo
 }
 
 } // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free FLASH_ATTN_EXT: split partials live in a file-scope device
+// array instead of a caller workspace.  In host code the array's name is only
+// a host-side stand-in, never a device address: the address each device uses
+// comes from cudaGetSymbolAddress, looked up once per device with that device
+// current, and is what the kernels receive.
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[XQ_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kNoallocMaxDevices];
+} // namespace
+
+extern "C" int xq_flash_attn_ext_noalloc(const xq_fa_params *p, xq_stream_t stream) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return cuda_status(e, "flash_attn_ext_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kNoallocMaxDevices)
+        return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext_noalloc: device %d beyond %d", dev,
+                    kNoallocMaxDevices);
+    void *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *ptr = nullptr;
+            e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess)
+                return cuda_status(e, "flash_attn_ext_noalloc: cudaGetSymbolAddress");
+            g_noalloc_ptr[dev] = ptr;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    FaPlan pl;
+    int rc = fa_prepare(p, &pl);
+    if (rc)
+        return rc;
+    plan_splits(&pl, p->n_splits);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    dim3 grid((unsigned)pl.n_splits, (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
+              (unsigned)pl.a.n_seq);
+    if (pl.n_splits == 1) {
+        pl.a.direct = 1;
+        return cuda_status(run_decode(pl, grid, st), "flash_attn_ext_noalloc decode");
+    }
+    const size_t need = (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * 4;
+    if (need > (size_t)XQ_NOALLOC_SCRATCH_BYTES)
+        return fail(XQ_ERR_WORKSPACE,
+                    "flash_attn_ext_noalloc: %lld splits x %lld rows need %zu bytes of scratch, "
+                    "the static scratch holds %u; pass a smaller n_splits",
+                    (long long)pl.n_splits, (long long)pl.n_rows, need,
+                    (unsigned)XQ_NOALLOC_SCRATCH_BYTES);
+    pl.a.direct = 0;
+    pl.a.partials = static_cast<float *>(scratch);
+    rc = cuda_status(run_decode(pl, grid, st), "flash_attn_ext_noalloc decode");
+    if (rc)
+        return rc;
+    return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p->dst,
+                                        nullptr, p->sinks, pl.a.n_head, st),
+                       "flash_attn_ext_noalloc merge");
+}

@@ -19,6 +19,7 @@ EXPORTS = (
     "xq_flash_attn_ext_workspace", "xq_flash_attn_ext", "xq_fa_partials", "xq_lse_merge",
     "xq_attend_range_workspace", "xq_attend_range", "xq_split_k", "xq_gated_delta_net",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
+    "xq_flash_attn_ext_noalloc",
 )
 
 
@@ -65,6 +66,7 @@ def lib():
         "xq_gated_delta_net": (C.c_int, [P(Tensor)] * 6 + [vp, i32, vp]),
         "xq_dequantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_quantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
+        "xq_flash_attn_ext_noalloc": (C.c_int, [P(FaParams), vp]),
         "xq_version": (C.c_char_p, []),
         "xq_last_error": (C.c_char_p, []),
     }
