@@ -355,29 +355,34 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 // LSE merge: one thread-block cluster per output row, one CTA per 32 dims.
 // Every CTA reads all splits' (m, l), forms the global max M, the weights
 // w_s = exp(m_s - M) and L = sum l_s w_s (fixed order: thread-strided, then
-// the warp tree, then warps in order); its 8 warps then stream contiguous
-// runs of splits for its 32 dims (lane = dim, one 128-byte line per split)
-// and add the warp sums in warp order.  Any non-finite input of a live split
-// or a non-finite result poisons the whole row (NaN out, NaN lse): the CTAs of
-// the row OR their flags through distributed shared memory.  The order of
-// every sum depends only on the number of splits, never on which GPU or
-// launch produced each split.
+// the warp tree, then warps in order); its 8 warps own contiguous runs of
+// splits for its 32 dims (lane = dim, one 128-byte line per split) and their
+// sums are added in warp order.  The numerators are requested together with
+// (m, l), so the merge costs one memory latency.  Any non-finite input of a
+// live split or a non-finite result poisons the whole row (NaN out, NaN lse):
+// each CTA pushes its flag into every peer's shared memory and one cluster
+// barrier later reads them all.  The order of every sum depends only on the
+// number of splits, never on which GPU or launch produced each split.
 namespace mg {
-constexpr int NT = 256, NW = NT / 32, CACHE = 2048, UN = 8;
+constexpr int NT = 256, NW = NT / 32, CACHE = 2048, XR = 24;
 
 __device__ __forceinline__ void grid_dep_wait() {
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
 }
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n"
                  "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
 }
-__device__ __forceinline__ int ld_peer_flag(const int *local, uint32_t rank) {
+__device__ __forceinline__ void st_peer(int *local, uint32_t rank, int v) {
     uint32_t addr = (uint32_t)__cvta_generic_to_shared(local), peer;
-    int v;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(peer) : "r"(addr), "r"(rank));
-    asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(peer) : "memory");
-    return v;
+    asm volatile("st.shared::cluster.u32 [%0], %1;\n" ::"r"(peer), "r"(v) : "memory");
 }
 } // namespace mg
 
@@ -393,7 +398,7 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     __shared__ float2 wd_s[CACHE]; // (m, l), then (w, l) of each split
     __shared__ float red[NW];
     __shared__ float accw[NW][32];
-    __shared__ int flag_s;
+    __shared__ int flags_s[NC]; // slot r: CTA r's poison flag (written by CTA r)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int chunk = blockIdx.x % NC; // == rank in the cluster
     const int64_t row = blockIdx.x / NC;
@@ -403,8 +408,21 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     auto md = [&](int64_t s) {
         return make_float2(base[s * stride + D], base[s * stride + D + 1]);
     };
+    cluster_arrive_relaxed(); // every peer has started before any DSMEM store below
+    // the next decode may launch now; it waits for this grid before it writes
+    // the partials read here
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
     grid_dep_wait(); // partials come from the preceding kernel
+    // this warp's splits [s0, s1), lane = dim; first XR numerators in flight now
+    const int d = chunk * 32 + lane;
+    const int64_t s0 = n_splits * warp / NW, s1 = n_splits * (warp + 1) / NW;
+    const float *xb = base + d;
+    float x[XR];
+#pragma unroll
+    for (int i = 0; i < XR; ++i)
+        x[i] = s0 + i < s1 ? xb[(s0 + i) * stride] : 0.0f;
+
     float mx = -FLT_MAX;
     int bad = 0;
     for (int64_t s = tid; s < n_splits; s += NT) {
@@ -446,36 +464,33 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     for (int w = 1; w < NW; ++w)
         L += red[w];
 
-    // numerators: warp w owns splits [s0, s1), lane owns dim chunk * 32 + lane
-    const int d = chunk * 32 + lane;
-    const int64_t s0 = n_splits * warp / NW, s1 = n_splits * (warp + 1) / NW;
-    const float *xb = base + d;
     float acc = 0.0f, chk = 0.0f; // chk: NaN iff some live numerator is not finite
-    auto wd = [&](int64_t s) {
-        if (cached)
-            return wd_s[s];
-        const float2 v = md(s);
-        return make_float2(v.y != 0.0f ? expf(v.x - M) : 0.0f, v.y);
-    };
-    int64_t s = s0;
-    for (; s + UN <= s1; s += UN) {
-        float x[UN];
+    if (cached) {
+        for (int64_t c = s0; c < s1; c += XR) {
+            if (c != s0) {
 #pragma unroll
-        for (int i = 0; i < UN; ++i)
-            x[i] = xb[(s + i) * stride];
+                for (int i = 0; i < XR; ++i)
+                    x[i] = c + i < s1 ? xb[(c + i) * stride] : 0.0f;
+            }
 #pragma unroll
-        for (int i = 0; i < UN; ++i) {
-            const float2 v = wd(s + i);
-            const float y = v.y != 0.0f ? x[i] : 0.0f;
-            acc = fmaf(y, v.x, acc);
+            for (int i = 0; i < XR; ++i) {
+                if (c + i < s1) {
+                    const float2 v = wd_s[c + i];
+                    const float y = v.y != 0.0f ? x[i] : 0.0f;
+                    acc = fmaf(y, v.x, acc);
+                    chk = fmaf(y, 0.0f, chk);
+                }
+            }
+        }
+    } else {
+        // more splits than the shared-memory cache: weights recomputed per split
+        for (int64_t c = s0; c < s1; ++c) {
+            const float2 v = md(c);
+            const float w = v.y != 0.0f ? expf(v.x - M) : 0.0f;
+            const float y = v.y != 0.0f ? xb[c * stride] : 0.0f;
+            acc = fmaf(y, w, acc);
             chk = fmaf(y, 0.0f, chk);
         }
-    }
-    for (; s < s1; ++s) {
-        const float2 v = wd(s);
-        const float y = v.y != 0.0f ? xb[s * stride] : 0.0f;
-        acc = fmaf(y, v.x, acc);
-        chk = fmaf(y, 0.0f, chk);
     }
     accw[warp][lane] = acc;
     bad |= __syncthreads_or(!isfinite(chk));
@@ -504,18 +519,17 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
             !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
         o *= inv;
         bad |= __any_sync(0xffffffffu, rowbad || !isfinite(o));
-        if (lane == 0)
-            flag_s = bad;
     }
-    // OR the flags of the row's CTAs; the second barrier keeps every CTA's
-    // shared memory alive until all peers have read it
-    cluster_sync();
-    int poison = 0;
+    // push this CTA's flag into slot `chunk` of every CTA of the row
+    cluster_wait();
     if (warp == 0 && lane < NC)
-        poison = ld_peer_flag(&flag_s, (uint32_t)lane);
-    poison = __any_sync(0xffffffffu, poison);
+        st_peer(&flags_s[chunk], (uint32_t)lane, bad);
     cluster_sync();
     if (warp == 0) {
+        int poison = 0;
+#pragma unroll
+        for (int r = 0; r < NC; ++r)
+            poison |= flags_s[r];
         out[row * D + d] = poison ? NAN : o;
         if (lse && chunk == 0 && lane == 0)
             lse[row] = poison ? NAN : l;

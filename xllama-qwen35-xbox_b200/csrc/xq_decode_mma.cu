@@ -147,6 +147,17 @@ __device__ __forceinline__ void tma_rows(uint32_t dst, const CUtensorMap *map, i
         "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(head), "r"(seq), "r"(bar)
         : "memory");
 }
+// L2 prefetch of one TMA box (no shared-memory destination, no completion).
+__device__ __forceinline__ void tma_prefetch_rows(const CUtensorMap *map, int row, int head,
+                                                  int seq) {
+    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];\n" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(0), "r"(row), "r"(head), "r"(seq)
+                 : "memory");
+}
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -321,11 +332,55 @@ __global__ void __launch_bounds__(dm::NT, 1)
     uint8_t *ring = rings + warp * RING;
     const uint32_t ring_s = smem_u32(ring);
     uint64_t *mybar = bar_s + warp * STAGES;
+    // my groups: warp + NWARP * i
+    const int my_n = n_groups > warp ? (n_groups - warp + NWARP - 1) / NWARP : 0;
+    if constexpr (TMA) {
+        if (tid == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap))
+                         : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap))
+                         : "memory");
+        }
+    }
     if constexpr (BULK) {
+        // before any load is in flight: this fence waits for outstanding memory operations
         if (lane < STAGES)
             mbar_init(smem_u32(mybar + lane), 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         __syncwarp();
+    }
+    if constexpr (TMA) {
+        // Launched as a programmatic dependent: until griddepcontrol.wait the
+        // kernel before this one may still be writing q or the KV cache, so
+        // only L2 prefetches (coherent, no data consumed) are issued here.
+        if (lane == 0)
+            for (int st = 0; st < STAGES - 1 && st < my_n; ++st) {
+                const int row = (int)(r0 + (warp + NWARP * st) * KG);
+                tma_prefetch_rows(&kmap, row, kvh, s / a.rk3);
+                tma_prefetch_rows(&vmap, row, kvh, s / a.rv3);
+            }
+    }
+    grid_dep_wait();
+    // q loads first: their latency overlaps the K/V copies issued next
+    constexpr int QU = T == kF16 ? 0 : 8 * NB * 2; // quantizer units (two per q block)
+    static_assert(QU <= NT && QU % 32 == 0, "one quantizer unit per thread, whole warps");
+    float xq[16];
+    if constexpr (QU > 0) {
+        const int blk = tid >> 1, half = tid & 1;
+        const int j = blk / NB, b = blk - j * NB;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            xq[i] = 0.0f;
+        if (tid < QU && j < nj) {
+            const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+            const float *src = reinterpret_cast<const float *>(
+                                   a.q + (int64_t)iq1 * a.q_nb1 + (int64_t)h * a.q_nb2 +
+                                   (int64_t)s * a.q_nb3) +
+                               b * 32 + half * 16;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                xq[i] = src[i];
+        }
     }
     auto issue = [&](int grp, int stage) {
         const int k0 = grp * KG; // relative to r0
@@ -370,8 +425,6 @@ __global__ void __launch_bounds__(dm::NT, 1)
             }
         }
     };
-    // my groups: warp + NWARP * i
-    const int my_n = n_groups > warp ? (n_groups - warp + NWARP - 1) / NWARP : 0;
 #pragma unroll
     for (int st = 0; st < STAGES - 1; ++st) {
         if (st < my_n)
@@ -420,23 +473,10 @@ __global__ void __launch_bounds__(dm::NT, 1)
     } else {
         // ggml quantize_row_q8_0 reference arithmetic; two threads per 32-block
         int8_t *q8 = reinterpret_cast<int8_t *>(qsm);
-        for (int u = tid; u < 8 * NB * 2; u += NT) {
-            const int blk = u >> 1, half = u & 1;
+        if (tid < QU) {
+            const int blk = tid >> 1, half = tid & 1;
             const int j = blk / NB, b = blk - j * NB;
-            float x[16];
-            if (j < nj) {
-                const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
-                const float *src = reinterpret_cast<const float *>(
-                    a.q + (int64_t)iq1 * a.q_nb1 + (int64_t)h * a.q_nb2 + (int64_t)s * a.q_nb3) +
-                    b * 32 + half * 16;
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    x[i] = src[i];
-            } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    x[i] = 0.0f;
-            }
+            const float *x = xq; // loaded above (zeros for padding q-rows)
             float amax = 0.0f;
 #pragma unroll
             for (int i = 0; i < 16; ++i)
@@ -874,8 +914,19 @@ static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
                              a.v_nb2, a.v_nb3))
             return cudaErrorNotSupported; // nothing launched: the caller picks another path
     }
-    kern<<<grid, dm::NT, smem, st>>>(maps[0], maps[1], a);
-    return cudaGetLastError();
+    // programmatic dependent of the previous kernel on the stream: the kernel
+    // prefetches K/V into L2 before its griddepcontrol.wait
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(dm::NT, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], a);
 }
 
 template <int T, int D>
@@ -883,7 +934,10 @@ static cudaError_t mma_vw(const DecodeArgs &a, int vw, dim3 grid, cudaStream_t s
     constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
     if constexpr (rec_bytes(T, D) % 16 == 0)
         if (vw == 16) {
-            const cudaError_t e = launch_mma<T, D, ST, 16>(a, grid, st);
+            // TMA boxes: two stages (one group in flight behind the one in use)
+            // measured faster than three, as the first wave of requests is smaller
+            constexpr int STV = dm::tma_mode(T, 16) ? 2 : ST;
+            const cudaError_t e = launch_mma<T, D, STV, 16>(a, grid, st);
             if (e != cudaErrorNotSupported)
                 return e;
             vw = 8; // the layout has no tensor map: per-lane copies
