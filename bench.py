@@ -2,7 +2,7 @@
 """Benchmark of the B200 attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c2|c2q4|c5]
+                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c5]
 
 Workloads (seeded synthetic tensors, random data of the
 stated distributions -- no datasets are involved):
@@ -10,6 +10,13 @@ stated distributions -- no datasets are involved):
        (the N=1 headline).  Eight rotated input sets (286 MB > 2 x L2) so every
        step streams its KV from HBM.
   c2q4 the same with Q4_0 KV.
+  c1   config 1: one decode step, F16 KV, 16 Q / 4 KV heads, D=128, kv 4096
+       (31 rotated input sets > 2 x L2).
+  c3a  config 3 decode: GATED_DELTA_NET, 8 sequences x 1 token, 32 v-heads /
+       16 k-heads, d 128 (fp32 state read + written; 9 rotated sets).
+  c3b  config 3 prefill: GATED_DELTA_NET, 1 sequence x 4096 tokens.
+  c4   config 4: causal prefill, 8192 tokens, 24 Q / 4 KV heads, D=256, F16
+       K/V, explicit causal F16 mask (tensor-core kernel); metric TFLOP/s.
   c5   config 5: 8 sequences x 262144 KV rows, 24 Q / 4 KV heads, D=256, Q8_0;
        the KV rows are cut into 256 fixed global splits, each GPU holds and
        reads its contiguous block of splits, the (m, l, O) partials are
@@ -113,7 +120,11 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # workloads
 
+C1 = dict(n_head=16, n_hkv=4, D=128, n_kv=4096, n_seq=1)
 C2 = dict(n_head=16, n_hkv=2, D=256, n_kv=32768, n_seq=1)
+C3 = dict(S=128, H=32, H_k=16, slots=1)
+C4 = dict(n_head=24, n_hkv=4, D=256, n_q=8192)
+TYPE_NAMES = {0: "f32", 1: "f16", 2: "q4_0", 8: "q8_0"}
 C5 = dict(n_head=24, n_hkv=4, D=256, n_kv=262144, n_seq=8)
 
 
@@ -141,6 +152,44 @@ def make_kv(torch, xq, w, ty, n_rows, seed, dev):
     return out
 
 
+def graph_timed(torch, fn, n, warmup, world=1, dist=None, dev=None, use_graph=True):
+    """Device time (ms) of n calls of fn, replayed from one CUDA graph so host
+    launch overhead stays out of the timed region; max over ranks."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    g = None
+    if use_graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                fn(i)
+        g.replay()  # warm replay
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    if g is not None:
+        g.replay()
+    else:
+        for i in range(n):
+            fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = e0.elapsed_time(e1)
+    del g
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = float(tt.item())
+    return t
+
+
 def run_ours(args, rank, world, torch, dist):
     import xq
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -148,8 +197,8 @@ def run_ours(args, rank, world, torch, dist):
     workload = args.workload
     if workload == "auto":
         workload = "c2" if world == 1 else "c5"
-    ty = xq.Q4_0 if workload == "c2q4" else xq.Q8_0
-    w = C5 if workload == "c5" else C2
+    ty = {"c2q4": xq.Q4_0, "c1": xq.F16}.get(workload, xq.Q8_0)
+    w = {"c5": C5, "c1": C1}.get(workload, C2)
     hbm, _, peak_kind = peaks()
     st = torch.cuda.current_stream()
     D, H, Hkv, n_seq = w["D"], w["n_head"], w["n_hkv"], w["n_seq"]
@@ -204,41 +253,7 @@ def run_ours(args, rank, world, torch, dist):
     use_graph = os.environ.get("XQ_BENCH_NO_GRAPH", "0") != "1"
 
     def timed(fn, n):
-        """Device time (ms) of n calls of fn, replayed from one CUDA graph so
-        host launch overhead stays out of the timed region; max over ranks."""
-        for i in range(args.warmup):
-            fn(i)
-        torch.cuda.synchronize()
-        g = None
-        if use_graph:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                for i in range(n):
-                    fn(i)
-            g.replay()  # warm replay
-            torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        if g is not None:
-            g.replay()
-        else:
-            for i in range(n):
-                fn(i)
-        e1.record()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        t = e0.elapsed_time(e1)
-        del g
-        if world > 1:
-            tt = torch.tensor([t], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            t = float(tt.item())
-        return t
+        return graph_timed(torch, fn, n, args.warmup, world, dist, dev, use_graph)
 
     clk = ClockSampler(dev.index)
     clk.start()
@@ -283,10 +298,11 @@ def run_ours(args, rank, world, torch, dist):
         "scaling": "strong" if workload == "c5" else "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1), ggml reference quantizer)",
-        "config": {"workload": {"c2": "BASELINE config 2 (Q8_0 decode, kv 32768)",
+        "config": {"workload": {"c1": "BASELINE config 1 (F16 decode, kv 4096)",
+                                "c2": "BASELINE config 2 (Q8_0 decode, kv 32768)",
                                 "c2q4": "BASELINE config 2, Q4_0 variant",
                                 "c5": "BASELINE config 5 (8 x 262144 Q8_0, KV-sharded)"}[workload],
-                   "kv_type": "q8_0" if ty == xq.Q8_0 else "q4_0",
+                   "kv_type": TYPE_NAMES[ty],
                    "n_seq": n_seq, "n_head": H, "n_head_kv": Hkv, "head_dim": D,
                    "kv_len": w["n_kv"], "kv_splits": n_splits, "rows_per_split": rows_per_split,
                    "parallelism": f"kv-shard{world}" if world > 1 else "single",
@@ -317,8 +333,8 @@ def cpu_oracle_sample(workload, seconds_cap=20.0, sample_kv=None):
     """Time the CPU restatement of ggml-cpu FLASH_ATTN_EXT on a bounded sample
     of the workload (all host threads); returns (GB/s, info)."""
     import oracle
-    w = C5 if workload == "c5" else C2
-    ty = oracle.Q4_0 if workload == "c2q4" else oracle.Q8_0
+    w = {"c5": C5, "c1": C1}.get(workload, C2)
+    ty = {"c2q4": oracle.Q4_0, "c1": oracle.F16}.get(workload, oracle.Q8_0)
     n_kv = sample_kv or w["n_kv"]
     n_seq = 1
     rng = np.random.default_rng(0)
@@ -328,11 +344,12 @@ def cpu_oracle_sample(workload, seconds_cap=20.0, sample_kv=None):
     v = oracle.quantize(ty, rng.normal(0, 1, kf.shape).astype(np.float32))
     del kf
     cores = os.cpu_count() or 1
-    oracle.flash_attn_ext(q, k, v, ty, ty, scale=1 / 16, nth=cores, n_workers=cores)  # warm
+    sc = 1.0 / math.sqrt(w["D"])
+    oracle.flash_attn_ext(q, k, v, ty, ty, scale=sc, nth=cores, n_workers=cores)  # warm
     t = time.perf_counter()
     reps = 0
     while True:
-        oracle.flash_attn_ext(q, k, v, ty, ty, scale=1 / 16, nth=cores, n_workers=cores)
+        oracle.flash_attn_ext(q, k, v, ty, ty, scale=sc, nth=cores, n_workers=cores)
         reps += 1
         if time.perf_counter() - t > min(seconds_cap, 3.0) or reps >= 5:
             break
@@ -342,13 +359,217 @@ def cpu_oracle_sample(workload, seconds_cap=20.0, sample_kv=None):
                           f"{dt * 1e3:.1f} ms each, {cores} threads"}
 
 
+# ---------------------------------------------------------------------------
+# GATED_DELTA_NET (config 3) and causal prefill (config 4)
+
+def gdn_bytes(n_seq, T, w=C3):
+    S, H, Hk, K = w["S"], w["H"], w["H_k"], w["slots"]
+    state = n_seq * H * S * S * 4
+    ins = 2 * n_seq * T * Hk * S * 4 + n_seq * T * H * S * 4 + 2 * n_seq * T * H * 4
+    y = n_seq * T * H * S * 4
+    return state * (1 + K) + ins + y, ins, y
+
+
+def gdn_inputs(torch, dev, n_seq, T, seed, w=C3):
+    """q, k L2-normalised N(0,1); v N(0,1); g = -softplus(N(0,1)); beta =
+    sigmoid(N(0,1)); state 0.1 N(0,1) -- the config-3 distributions."""
+    F = torch.nn.functional
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    S, H, Hk = w["S"], w["H"], w["H_k"]
+    rn = lambda *shape: torch.randn(shape, generator=g, device=dev)
+    q = F.normalize(rn(n_seq, T, Hk, S), dim=-1)
+    k = F.normalize(rn(n_seq, T, Hk, S), dim=-1)
+    v = rn(n_seq, T, H, S)
+    gate = -F.softplus(rn(n_seq, T, H, 1))
+    beta = torch.sigmoid(rn(n_seq, T, H, 1))
+    state = 0.1 * rn(n_seq, H, S, S)
+    return [q, k, v, gate, beta, state]
+
+
+def run_gdn(args, torch, workload):
+    import xq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_seq, T = (8, 1) if workload == "c3a" else (1, 4096)
+    w = C3
+    hbm, _, peak_kind = peaks()
+    step_bytes, in_bytes, y_bytes = gdn_bytes(n_seq, T)
+    n_sets = 1 if step_bytes > 2 * L2_BYTES else math.ceil(2 * L2_BYTES / step_bytes) + 1
+    sets = [gdn_inputs(torch, dev, n_seq, T, 100 + i) for i in range(n_sets)]
+    n_dst = w["S"] * w["H"] * T * n_seq + w["slots"] * w["S"] ** 2 * w["H"] * n_seq
+    dsts = [torch.empty(n_dst, dtype=torch.float32, device=dev) for _ in range(n_sets)]
+
+    def step(i):
+        x = sets[i % n_sets]
+        xq.gated_delta_net(*x, slots=w["slots"], out=dsts[i % n_sets])
+
+    clk = ClockSampler(dev.index)
+    clk.start()
+    ms = graph_timed(torch, step, args.steps, args.warmup) / args.steps
+    clocks = clk.stop()
+    # end to end: this step's q, k, v, g, beta from pinned host memory, y back;
+    # the recurrent state stays resident on the device
+    hosts = [t.cpu().pin_memory() for t in sets[0][:5]]
+    y_host = torch.empty(n_seq * T * w["H"] * w["S"], dtype=torch.float32, pin_memory=True)
+
+    def e2e_step(i):
+        for h, d in zip(hosts, sets[0][:5]):
+            d.copy_(h, non_blocking=True)
+        xq.gated_delta_net(*sets[0], slots=w["slots"], out=dsts[0])
+        y_host.copy_(dsts[0][:y_host.numel()], non_blocking=True)
+    e2e_ms = graph_timed(torch, e2e_step, args.steps, args.warmup) / args.steps
+    value = step_bytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": "gated-delta-net GB/s", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; q, k L2-normalised N(0,1), v N(0,1), g = -softplus, "
+                "beta = sigmoid, state 0.1 N(0,1))",
+        "config": {"workload": ("BASELINE config 3 decode (GDN, 8 seqs x 1 token)"
+                                if workload == "c3a" else
+                                "BASELINE config 3 prefill (GDN, 1 seq x 4096 tokens)"),
+                   "n_seq": n_seq, "tokens": T, "v_heads": w["H"], "k_heads": w["H_k"],
+                   "head_dim": w["S"], "slots": w["slots"],
+                   "l2": ("rotating %d input sets (%.0f MB > 2x L2)" % (n_sets,
+                          n_sets * step_bytes / 1e6)) if n_sets > 1 else
+                         "inputs %.0f MB > L2" % (step_bytes / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": hbm, "unit": "GB/s",
+                     "frac": round(value / hbm, 4), "peak_kind": peak_kind,
+                     "kernel": "gdn_kernel", "traffic": profile_traffic("gdn_" + workload)},
+        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": in_bytes,
+                "d2h_bytes_per_step": y_bytes},
+        "gpu_launches": args.steps,
+        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
+        "clocks": clocks,
+    }
+
+
+def prefill_flops(n_q, H, D):
+    return 4.0 * D * H * n_q * (n_q + 1) / 2
+
+
+def run_prefill(args, torch):
+    import xq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = C4
+    H, Hkv, D, N = w["n_head"], w["n_hkv"], w["D"], w["n_q"]
+    _, tflops, peak_kind = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q = torch.randn((1, H, N, D), generator=g, device=dev)
+    k = xq.quantize_rows(xq.F16, torch.randn((1, N, Hkv, D), generator=g, device=dev))
+    v = xq.quantize_rows(xq.F16, torch.randn((1, N, Hkv, D), generator=g, device=dev))
+    mask = torch.full((1, 1, N, N), float("-inf"), dtype=torch.float16, device=dev).triu_(1)
+    out = torch.empty((1, N, H, D), dtype=torch.float32, device=dev)
+    scale = 1.0 / math.sqrt(D)
+
+    def step(i):
+        xq.flash_attn_ext(q, k, v, xq.F16, mask=mask, scale=scale, out=out)
+
+    clk = ClockSampler(dev.index)
+    clk.start()
+    ms = graph_timed(torch, step, args.steps, args.warmup) / args.steps
+    clocks = clk.stop()
+    q_host = q.cpu().pin_memory()
+    o_host = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
+
+    def e2e_step(i):
+        q.copy_(q_host, non_blocking=True)
+        step(i)
+        o_host.copy_(out, non_blocking=True)
+    e2e_ms = graph_timed(torch, e2e_step, max(3, args.steps // 4), args.warmup) / max(
+        3, args.steps // 4)
+    fl = prefill_flops(N, H, D)
+    value = fl / (ms * 1e-3) / 1e12
+    return {
+        "metric": "causal prefill TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded N(0,1); K/V rounded to F16; explicit causal F16 mask)",
+        "config": {"workload": "BASELINE config 4 (causal prefill, 8192 tokens)",
+                   "n_q": N, "n_kv": N, "n_head": H, "n_head_kv": Hkv, "head_dim": D,
+                   "flops_per_step": fl,
+                   "l2": "inputs %.0f MB > L2" % ((q.numel() * 4 + k.numel() * 2 +
+                                                   mask.numel() * 2) / 1e6)},
+        "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": tflops,
+                     "unit": "TFLOP/s", "frac": round(value / tflops, 4),
+                     "peak_kind": peak_kind + " (bf16 burst)", "kernel": "fa_prefill_kernel",
+                     "traffic": profile_traffic("fa_prefill_c4")},
+        "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": q.numel() * 4,
+                "d2h_bytes_per_step": out.numel() * 4},
+        "gpu_launches": args.steps * 2,
+        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
+        "clocks": clocks,
+    }
+
+
+def cpu_gdn_sample(workload):
+    import oracle
+    n_seq, T = (8, 1) if workload == "c3a" else (1, 256)
+    rng = np.random.default_rng(0)
+    S, H, Hk = C3["S"], C3["H"], C3["H_k"]
+
+    def nrm(x):
+        return (x / np.linalg.norm(x, axis=-1, keepdims=True)).astype(np.float32)
+    q = nrm(rng.normal(0, 1, (n_seq, T, Hk, S)))
+    k = nrm(rng.normal(0, 1, (n_seq, T, Hk, S)))
+    v = rng.normal(0, 1, (n_seq, T, H, S)).astype(np.float32)
+    gg = -np.log1p(np.exp(rng.normal(0, 1, (n_seq, T, H, 1)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.normal(0, 1, (n_seq, T, H, 1))))).astype(np.float32)
+    state = (0.1 * rng.normal(0, 1, (n_seq, H, S, S))).astype(np.float32)
+    cores = os.cpu_count() or 1
+    oracle.gated_delta_net(q, k, v, gg, beta, state, slots=1, n_workers=cores)
+    t = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.gated_delta_net(q, k, v, gg, beta, state, slots=1, n_workers=cores)
+        reps += 1
+        if time.perf_counter() - t > 3.0 or reps >= 10:
+            break
+    dt = (time.perf_counter() - t) / reps
+    b = gdn_bytes(n_seq, T)[0]
+    return b / dt / 1e9, {"cores": cores, "unit": "GB/s",
+                          "sample": f"{n_seq} seqs x {T} tokens, {reps} reps, "
+                                    f"{dt * 1e3:.2f} ms each, {cores} threads"}
+
+
+def cpu_prefill_sample(rows=16):
+    """The last `rows` queries of config 4 (the longest causal rows)."""
+    import oracle
+    H, Hkv, D, N = C4["n_head"], C4["n_hkv"], C4["D"], C4["n_q"]
+    rng = np.random.default_rng(0)
+    q = rng.normal(0, 1, (1, H, rows, D)).astype(np.float32)
+    kf = rng.normal(0, 1, (1, N, Hkv, D)).astype(np.float32)
+    k = oracle.quantize(oracle.F16, kf)
+    v = oracle.quantize(oracle.F16, rng.normal(0, 1, kf.shape).astype(np.float32))
+    pos = np.arange(N - rows, N)
+    mask = np.where(np.arange(N)[None, :] > pos[:, None], -np.inf, 0).astype(np.float16)
+    mask = mask.reshape(1, 1, rows, N)
+    cores = os.cpu_count() or 1
+    t = time.perf_counter()
+    oracle.flash_attn_ext(q, k, v, oracle.F16, oracle.F16, mask=mask, scale=1 / 16,
+                          nth=cores, n_workers=cores)
+    dt = time.perf_counter() - t
+    fl = 4.0 * D * H * float((pos + 1).sum())
+    return fl / dt / 1e12, {"cores": cores, "unit": "TFLOP/s",
+                            "sample": f"last {rows} of {N} causal queries x {H} heads, "
+                                      f"{dt:.2f} s, {cores} threads"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto", choices=["auto", "c2", "c2q4", "c5"])
+    ap.add_argument("--workload", default="auto",
+                    choices=["auto", "c1", "c2", "c2q4", "c3a", "c3b", "c4", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -356,22 +577,43 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     workload = args.workload if args.workload != "auto" else ("c2" if world == 1 else "c5")
 
+    single = workload in ("c3a", "c3b", "c4")
     if args.impl == "reference":
         if rank != 0:
             return 0
-        val, info = cpu_oracle_sample(workload)
-        line = {"metric": "flash-decode KV GB/s", "value": round(val, 3), "unit": "GB/s",
+        metric, unit = "flash-decode KV GB/s", "GB/s"
+        if workload in ("c3a", "c3b"):
+            (val, info), metric = cpu_gdn_sample(workload), "gated-delta-net GB/s"
+        elif workload == "c4":
+            (val, info), metric, unit = cpu_prefill_sample(), "causal prefill TFLOP/s", "TFLOP/s"
+        else:
+            val, info = cpu_oracle_sample(workload)
+        val = float(f"{val:.4g}")
+        line = {"metric": metric, "value": val, "unit": unit,
                 "impl": "reference", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
                 "config": {"workload": workload}, "data": "synthetic",
-                "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": info["cores"],
+                "cpu_baseline": {"value": val, "unit": unit, "cores": info["cores"],
                                  "kind": "port", "sample": info["sample"]},
-                "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
 
     import torch
+    if single:
+        # GDN and prefill rows are measured on one GPU
+        if world > 1:
+            print(json.dumps({"error": f"workload {workload} runs on one GPU"}), flush=True)
+            return 2
+        line = run_gdn(args, torch, workload) if workload != "c4" else run_prefill(args, torch)
+        if not args.no_cpu_baseline:
+            val, info = cpu_gdn_sample(workload) if workload != "c4" else cpu_prefill_sample()
+            line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": info["unit"],
+                                    "cores": info["cores"], "kind": "port",
+                                    "sample": info["sample"]}
+        print(json.dumps(line), flush=True)
+        return 0
     dist = None
     if world > 1:
         import datetime
@@ -384,7 +626,7 @@ def main():
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline:
             val, info = cpu_oracle_sample(workload)
-            line["cpu_baseline"] = {"value": round(val, 3), "unit": "GB/s",
+            line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": "GB/s",
                                     "cores": info["cores"], "kind": "port",
                                     "sample": info["sample"]}
         print(json.dumps(line), flush=True)
