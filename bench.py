@@ -206,9 +206,9 @@ def run_ours(args, rank, world, torch, dist):
     n_rows_out = n_seq * H
 
     if workload == "c5":
+        from xq import shard
         rows_per_split, n_splits = 1024, w["n_kv"] // 1024
-        per = n_splits // world
-        sb, se = rank * per, (rank + 1) * per
+        sb, se = shard.split_block(n_splits, world, rank)
         local_rows = (se - sb) * rows_per_split
         # each GPU holds only its block of KV rows; global row r = sb*1024 + local r
         k = make_kv(torch, xq, w, ty, local_rows, 1000 + rank, dev)
@@ -245,7 +245,7 @@ def run_ours(args, rank, world, torch, dist):
         src = part_local
         if world > 1:
             if "gather" in parts:
-                dist.all_gather_into_tensor(part_all, part_local)
+                shard.gather_partials(part_local, n_splits, out=part_all)
             src = part_all
         if "merge" in parts:
             xq.lse_merge(src, out=out, want_lse=False)
