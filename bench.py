@@ -18,10 +18,11 @@ stated distributions -- no datasets are involved):
   c4   config 4: causal prefill, 8192 tokens, 24 Q / 4 KV heads, D=256, F16
        K/V, explicit causal F16 mask (tensor-core kernel); metric TFLOP/s.
   c5   config 5: 8 sequences x 262144 KV rows, 24 Q / 4 KV heads, D=256, Q8_0;
-       the KV rows are cut into 256 fixed global splits, each GPU holds and
-       reads its contiguous block of splits, the (m, l, O) partials are
-       all-gathered over NCCL and merged in split order (bit-identical for any
-       GPU count).  Default for N > 1 ("strong" scaling: total work fixed).
+       the KV rows are cut into 256 fixed global splits in 8 fixed groups; each
+       GPU holds and reads its contiguous block of groups, merges each group
+       into one (O, lse) record, the group records are all-gathered over NCCL
+       and merged in group order (bit-identical for any GPU count dividing 8).
+       Default for N > 1 ("strong" scaling: total work fixed).
 A step = the attention kernels of one decode step over that workload.
 `value` is KV GB/s (algorithmic bytes: K + V + q + out per step) with inputs
 resident; `e2e` is the same metric through the public call xq.flash_attn_ext
@@ -207,8 +208,10 @@ def run_ours(args, rank, world, torch, dist):
 
     if workload == "c5":
         from xq import shard
-        rows_per_split, n_splits = 1024, w["n_kv"] // 1024
-        sb, se = shard.split_block(n_splits, world, rank)
+        rows_per_split, n_splits, n_groups = 1024, w["n_kv"] // 1024, 8
+        per_group = n_splits // n_groups
+        gb, ge = shard.split_block(n_groups, world, rank)
+        sb, se = gb * per_group, ge * per_group
         local_rows = (se - sb) * rows_per_split
         # each GPU holds only its block of KV rows; global row r = sb*1024 + local r
         k = make_kv(torch, xq, w, ty, local_rows, 1000 + rank, dev)
@@ -233,7 +236,10 @@ def run_ours(args, rank, world, torch, dist):
         n_splits = math.ceil(w["n_kv"] / rows_per_split)
         sb, se = 0, n_splits
     part_local = torch.empty((se - sb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
-    part_all = torch.empty((n_splits, n_rows_out, D + 2), dtype=torch.float32, device=dev)
+    if workload == "c5":
+        # two-level merge: local group records, gathered, merged in group order
+        rec_local = torch.empty((ge - gb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
+        rec_all = torch.empty((n_groups, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     out = torch.empty((n_rows_out, D), dtype=torch.float32, device=dev)
 
     def step(i, parts=("dec", "gather", "merge")):
@@ -243,10 +249,14 @@ def run_ours(args, rank, world, torch, dist):
             xq.fa_partials(q, k, v, ty, rows_per_split, 0 if workload == "c5" else sb,
                            (se - sb) if workload == "c5" else se, scale=scale, out=part_local)
         src = part_local
-        if world > 1:
-            if "gather" in parts:
-                shard.gather_partials(part_local, n_splits, out=part_all)
-            src = part_all
+        if workload == "c5":
+            if "merge" in parts:
+                xq.lse_merge_records(part_local, per_group, out=rec_local)
+            src = rec_local
+            if world > 1:
+                if "gather" in parts:
+                    shard.gather_partials(rec_local, n_groups, out=rec_all)
+                src = rec_all
         if "merge" in parts:
             xq.lse_merge(src, out=out, want_lse=False)
 
@@ -321,7 +331,7 @@ def run_ours(args, rank, world, torch, dist):
                 "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": int(q_host.numel() * 4),
                 "d2h_bytes_per_step": int(o_host.numel() * 4)},
-        "gpu_launches": args.steps * 2,
+        "gpu_launches": args.steps * (3 if workload == "c5" else 2),
         "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps if use_graph
                   else "eager launches, CUDA events",
         "clocks": clocks,

@@ -110,6 +110,16 @@ int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_
 int xq_lse_merge(const float *partials, int64_t n_splits, int64_t n_rows, int64_t D,
                  float *out, float *lse, xq_stream_t stream);
 
+/* First level of a two-level merge (the reduce step of the reference's      */
+/* split-K reduction, rkva_range_reduce_opt.hlsl:26-133, applied per group).  */
+/* partials [n_groups * splits_per_group][n_rows][D+2] -> records            */
+/* [n_groups][n_rows][D+2]: group g merges its splits in order and writes    */
+/* (O, lse, 1), (0, -FLT_MAX, 0) when empty, NaN when poisoned.  The records  */
+/* merge again with xq_lse_merge exactly like splits; with a fixed grouping  */
+/* the result is bit-identical however the groups are spread over GPUs.      */
+int xq_lse_merge_records(const float *partials, int64_t n_groups, int64_t splits_per_group,
+                         int64_t n_rows, int64_t D, float *records, xq_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* RKVA RANGE_ATTN: (O, LSE) over a compact KV range [0, active) whose row r */
 /* holds absolute position origin + r.  k/v: [capacity][n_head_kv][D] in     */

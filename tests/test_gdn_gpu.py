@@ -127,3 +127,16 @@ def test_gdn_key_head_is_h_mod_Hk():
     y = y.cpu().numpy()
     assert np.abs(y - y_mod).max() < 1e-5
     assert np.abs(y - y_div).max() > 1e-3
+
+
+@pytest.mark.parametrize("T,K,pad", [(40, 3, 3), (40, 1, 0)])
+def test_gdn_staged_path_vs_oracle(T, K, pad):
+    """Sequences longer than 8 tokens stage their inputs through shared memory:
+    16-byte copies for aligned rows, 4-byte copies for the padded layout."""
+    got, views = _gpu_selftest(T, K, pad)
+    written = min(T, K)
+    _, yo, so = oracle.gated_delta_net(*views, slots=K, lanes8=True)
+    y = got[:4096 * T].reshape(T, 32, 128)
+    s4 = got[4096 * T:4096 * T + 524288 * written].reshape(written, 32, 128, 128)
+    assert np.abs(y - yo[0]).max() <= 1e-6 * np.abs(yo[0]).max()
+    assert np.abs(s4 - so[:written, 0]).max() <= 1e-6 * np.abs(so[:written, 0]).max()

@@ -131,3 +131,42 @@ def test_f16_codec_bit_exact():
     assert np.array_equal(bits, g["f16_bits"][: bits.size])
     back = xq.dequantize_rows(oracle.F16, torch.from_numpy(raw).cuda(), 32).cpu().numpy()
     assert np.array_equal(back.reshape(-1), bits.view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("rows", [24, 64])  # cluster kernel / warp-per-row kernel
+def test_lse_merge_records_two_level(rows):
+    """Group records (O, lse, 1) of xq_lse_merge_records match the oracle's
+    per-group merge; empty groups give (0, -FLT_MAX, 0), poisoned rows NaN;
+    merging the records equals merging all splits at once."""
+    xq = _xq()
+    rng = np.random.default_rng(11)
+    G, per, D = 4, 5, 256
+    part = np.zeros((G * per, rows, D + 2), np.float32)
+    part[:, :, :D] = rng.normal(0, 1, (G * per, rows, D))
+    part[:, :, D] = rng.normal(0, 2, (G * per, rows))
+    part[:, :, D + 1] = rng.uniform(0.5, 3, (G * per, rows))
+    part[per:2 * per, 3, :D] = 0.0            # group 1, row 3: empty
+    part[per:2 * per, 3, D] = -3.402823466e38
+    part[per:2 * per, 3, D + 1] = 0.0
+    part[2 * per + 1, 5, 7] = np.nan         # group 2, row 5: poisoned
+    rec = xq.lse_merge_records(torch.from_numpy(part).cuda(), per).cpu().numpy()
+    for g in range(G):
+        o, lse = oracle.lse_merge(part[g * per:(g + 1) * per])
+        for r in range(rows):
+            if np.isnan(lse[r]):
+                assert np.isnan(rec[g, r]).all(), (g, r)
+            elif np.isneginf(lse[r]):
+                assert (rec[g, r, :D] == 0).all() and rec[g, r, D + 1] == 0
+                assert rec[g, r, D] == np.float32(-3.402823466e38)
+            else:
+                np.testing.assert_allclose(rec[g, r, :D], o[r], rtol=1e-5, atol=1e-6)
+                np.testing.assert_allclose(rec[g, r, D], lse[r], rtol=1e-6, atol=1e-6)
+                assert rec[g, r, D + 1] == 1.0
+    out2, lse2 = xq.lse_merge(torch.from_numpy(rec).cuda())
+    out1, lse1 = oracle.lse_merge(part)
+    out2, lse2 = out2.cpu().numpy(), lse2.cpu().numpy()
+    assert np.array_equal(np.isnan(out2), np.isnan(out1))
+    fin = ~np.isnan(out1)
+    np.testing.assert_allclose(out2[fin], out1[fin], rtol=1e-4, atol=1e-5)
+    fl = ~np.isnan(lse1)
+    np.testing.assert_allclose(lse2[fl], lse1[fl], rtol=1e-5, atol=1e-5)

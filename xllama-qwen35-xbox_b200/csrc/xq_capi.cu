@@ -330,6 +330,17 @@ int xq_lse_merge(const float *partials, int64_t n_splits, int64_t n_rows, int64_
                        "lse_merge");
 }
 
+int xq_lse_merge_records(const float *partials, int64_t n_groups, int64_t splits_per_group,
+                         int64_t n_rows, int64_t D, float *records, xq_stream_t stream) {
+    if (!partials || !records || n_groups <= 0 || splits_per_group <= 0 || n_rows < 0 ||
+        (D != 64 && D != 128 && D != 256))
+        return fail(XQ_ERR_INVALID, "lse_merge_records: bad arguments (D must be 64/128/256)");
+    return cuda_status(xq::launch_merge(partials, splits_per_group, n_rows, (int)D, records,
+                                        nullptr, nullptr, 1,
+                                        reinterpret_cast<cudaStream_t>(stream), n_groups, true),
+                       "lse_merge_records");
+}
+
 // ---------------------------------------------------------------------------
 // RKVA range attention.
 

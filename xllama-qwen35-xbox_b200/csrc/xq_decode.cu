@@ -386,13 +386,18 @@ __device__ __forceinline__ void st_peer(int *local, uint32_t rank, int v) {
 }
 } // namespace mg
 
+// Rows are (group, row) pairs: group g merges splits [g * n_splits, (g + 1) *
+// n_splits) of the partials.  With `records` set, each merged row is written
+// as a partial record itself -- (O normalised, lse, 1), or (0, -FLT_MAX, 0)
+// when empty, NaN when poisoned -- so merged groups merge again exactly like
+// splits (sinks are applied only by a final, non-record merge).
 template <int D>
 __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restrict__ part,
                                                            int64_t n_splits, int64_t n_rows,
                                                            float *__restrict__ out,
                                                            float *__restrict__ lse,
                                                            const float *__restrict__ sinks,
-                                                           int n_head) {
+                                                           int n_head, int records) {
     using namespace mg;
     constexpr int NC = D / 32; // CTAs per row (the cluster)
     __shared__ float2 wd_s[CACHE]; // (m, l), then (w, l) of each split
@@ -401,9 +406,10 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     __shared__ int flags_s[NC]; // slot r: CTA r's poison flag (written by CTA r)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int chunk = blockIdx.x % NC; // == rank in the cluster
-    const int64_t row = blockIdx.x / NC;
+    const int64_t row = blockIdx.x / NC; // group * n_rows + row in the group
+    const int64_t grp = row / n_rows, grow = row - grp * n_rows;
     const int64_t stride = (int64_t)n_rows * (D + 2);
-    const float *base = part + row * (D + 2);
+    const float *base = part + grp * n_splits * stride + grow * (D + 2);
     const bool cached = n_splits <= CACHE;
     auto md = [&](int64_t s) {
         return make_float2(base[s * stride + D], base[s * stride + D + 1]);
@@ -530,8 +536,143 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
 #pragma unroll
         for (int r = 0; r < NC; ++r)
             poison |= flags_s[r];
-        out[row * D + d] = poison ? NAN : o;
-        if (lse && chunk == 0 && lane == 0)
+        if (records) {
+            float *rec = out + row * (D + 2);
+            rec[d] = poison ? NAN : o;
+            if (chunk == 0 && lane == 0) {
+                rec[D] = poison ? NAN : (L == 0.0f ? -FLT_MAX : l);
+                rec[D + 1] = poison ? NAN : (L == 0.0f ? 0.0f : 1.0f);
+            }
+        } else {
+            out[row * D + d] = poison ? NAN : o;
+            if (lse && chunk == 0 && lane == 0)
+                lse[row] = poison ? NAN : l;
+        }
+    }
+}
+
+
+// Merge for many rows with few splits each (e.g. the per-group merges of a
+// KV-sharded step): one warp per merged row, lane l owning dims l + 32 j, and
+// the splits taken 32 at a time (lane s holds split c + s's max and
+// denominator and broadcasts its weight).  Numerators are added in split order
+// per dim; the row's poison flag stays inside the warp.  Same inputs, outputs
+// and record mode as lse_merge_kernel.
+template <int D>
+__global__ void __launch_bounds__(256) lse_merge_rows_kernel(const float *__restrict__ part,
+                                                             int64_t n_splits, int64_t n_rows,
+                                                             int64_t n_total,
+                                                             float *__restrict__ out,
+                                                             float *__restrict__ lse,
+                                                             const float *__restrict__ sinks,
+                                                             int n_head, int records) {
+    constexpr int J = D / 32, SB = 8;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); // warp-uniform
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    mg::grid_dep_wait();
+    if (row >= n_total)
+        return;
+    const int64_t grp = row / n_rows, grow = row - grp * n_rows;
+    const int64_t stride = (int64_t)n_rows * (D + 2);
+    const float *base = part + grp * n_splits * stride + grow * (D + 2);
+
+    float M = -FLT_MAX;
+    int bad = 0;
+    for (int64_t c = 0; c < n_splits; c += 32) {
+        const int64_t sp = c + lane;
+        if (sp < n_splits) {
+            const float m = base[sp * stride + D], den = base[sp * stride + D + 1];
+            if (den != 0.0f) {
+                if (!isfinite(den) || den < 0.0f || !isfinite(m))
+                    bad = 1;
+                else
+                    M = fmaxf(M, m);
+            }
+        }
+    }
+    M = warp_max(M);
+    float lp = 0.0f;
+    for (int64_t c = 0; c < n_splits; c += 32) {
+        const int64_t sp = c + lane;
+        if (sp < n_splits) {
+            const float m = base[sp * stride + D], den = base[sp * stride + D + 1];
+            if (den != 0.0f)
+                lp += den * expf(m - M);
+        }
+    }
+    float L = warp_sum(lp);
+
+    float acc[J], chk = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+        acc[j] = 0.0f;
+    for (int64_t c = 0; c < n_splits; c += 32) {
+        const int64_t sp = c + lane;
+        float wl = 0.0f, dl = 0.0f;
+        if (sp < n_splits) {
+            dl = base[sp * stride + D + 1];
+            wl = dl != 0.0f ? expf(base[sp * stride + D] - M) : 0.0f;
+        }
+        const int nc = (int)min((int64_t)32, n_splits - c);
+        for (int s0 = 0; s0 < nc; s0 += SB) {
+            float x[SB][J];
+#pragma unroll
+            for (int i = 0; i < SB; ++i)
+#pragma unroll
+                for (int j = 0; j < J; ++j)
+                    x[i][j] = s0 + i < nc ? base[(c + s0 + i) * stride + lane + 32 * j] : 0.0f;
+#pragma unroll
+            for (int i = 0; i < SB; ++i) {
+                const float w = __shfl_sync(0xffffffffu, wl, (s0 + i) & 31);
+                const float dn = __shfl_sync(0xffffffffu, dl, (s0 + i) & 31);
+                if (s0 + i < nc && dn != 0.0f) {
+#pragma unroll
+                    for (int j = 0; j < J; ++j) {
+                        acc[j] = fmaf(x[i][j], w, acc[j]);
+                        chk = fmaf(x[i][j], 0.0f, chk);
+                    }
+                }
+            }
+        }
+    }
+    if (!records && sinks) {
+        const float sk = sinks[grow % n_head];
+        if (L == 0.0f || sk > M) {
+            const float ms = L == 0.0f ? 0.0f : expf(M - sk);
+#pragma unroll
+            for (int j = 0; j < J; ++j)
+                acc[j] *= ms;
+            L = L * ms + 1.0f;
+            M = sk;
+        } else {
+            L += expf(sk - M);
+        }
+    }
+    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+    const float l = L == 0.0f ? -INFINITY : M + logf(L);
+    bool rowbad = bad || !isfinite(chk) || !isfinite(L) || L < 0.0f || !isfinite(inv) ||
+                  (L != 0.0f && !isfinite(l));
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        acc[j] *= inv;
+        rowbad |= !isfinite(acc[j]);
+    }
+    const bool poison = __any_sync(0xffffffffu, rowbad);
+    if (records) {
+        float *rec = out + row * (D + 2);
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            rec[lane + 32 * j] = poison ? NAN : acc[j];
+        if (lane == 0) {
+            rec[D] = poison ? NAN : (L == 0.0f ? -FLT_MAX : l);
+            rec[D + 1] = poison ? NAN : (L == 0.0f ? 0.0f : 1.0f);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            out[row * D + lane + 32 * j] = poison ? NAN : acc[j];
+        if (lse && lane == 0)
             lse[row] = poison ? NAN : l;
     }
 }
@@ -631,12 +772,35 @@ cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &c, dim3 grid,
 
 cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
                          float *out, float *lse, const float *sinks, int n_head,
-                         cudaStream_t st) {
-    if (n_rows <= 0)
+                         cudaStream_t st, int64_t n_groups, bool records) {
+    if (n_rows <= 0 || n_groups <= 0)
         return cudaSuccess;
-    if (n_rows * (D / 32) > 0x7fffffff)
+    if (n_groups * n_rows * (D / 32) > 0x7fffffff)
         return cudaErrorInvalidValue;
-    void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int);
+    const int64_t total = n_groups * n_rows;
+    if (total >= 128) {
+        // enough rows to fill the GPU with one warp each
+        void (*rk)(const float *, int64_t, int64_t, int64_t, float *, float *, const float *,
+                   int, int);
+        switch (D) {
+        case 64: rk = lse_merge_rows_kernel<64>; break;
+        case 128: rk = lse_merge_rows_kernel<128>; break;
+        case 256: rk = lse_merge_rows_kernel<256>; break;
+        default: return cudaErrorInvalidValue;
+        }
+        cudaLaunchConfig_t rc = {};
+        rc.gridDim = dim3((unsigned)((total + 7) / 8), 1, 1);
+        rc.blockDim = dim3(256, 1, 1);
+        rc.stream = st;
+        cudaLaunchAttribute ra[1];
+        ra[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        ra[0].val.programmaticStreamSerializationAllowed = 1;
+        rc.attrs = ra;
+        rc.numAttrs = 1;
+        return cudaLaunchKernelEx(&rc, rk, partials, n_splits, n_rows, total, out, lse, sinks,
+                                  n_head, records ? 1 : 0);
+    }
+    void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int, int);
     switch (D) {
     case 64: kern = lse_merge_kernel<64>; break;
     case 128: kern = lse_merge_kernel<128>; break;
@@ -646,7 +810,7 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     // one cluster of D / 32 CTAs per row; launched as a programmatic dependent
     // of the kernel before it on the stream (the merge waits for it in-kernel)
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(n_rows * (D / 32)), 1, 1);
+    cfg.gridDim = dim3((unsigned)(n_groups * n_rows * (D / 32)), 1, 1);
     cfg.blockDim = dim3(mg::NT, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
@@ -659,7 +823,8 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, partials, n_splits, n_rows, out, lse, sinks, n_head);
+    return cudaLaunchKernelEx(&cfg, kern, partials, n_splits, n_rows, out, lse, sinks, n_head,
+                              records ? 1 : 0);
 }
 
 } // namespace xq

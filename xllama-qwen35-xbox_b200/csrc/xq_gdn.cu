@@ -8,7 +8,9 @@
 //   S[col][:] += k_t * d
 //   y_t[col] = (sum_i S[col][i] q_t[i]) / sqrt(S_k)
 // with key head h % H_k.  Columns are independent, so a CTA owns CB columns
-// of one (sequence, head) and keeps them in registers for all T tokens.  Eight
+// of one (sequence, head) and keeps them in registers for all T tokens; the
+// token inputs are staged through shared memory 16 tokens at a time
+// (double-buffered cp.async), so no token waits for a global load.  Eight
 // lanes share a column; lane l holds elements i = l + 8e, accumulates its
 // partial dot in increasing i and the eight partials meet in the tree
 // (l, l+4), (l, l+2), (l, l+1) -- the order of the reference mirror's
@@ -19,14 +21,24 @@
 
 namespace xq {
 
-template <int S, int CB>
+// STAGED: token inputs through shared memory (long sequences); otherwise each
+// token reads them straight from global memory (a few tokens, e.g. decode).
+template <int S, int CB, int VW, bool STAGED>
 __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) {
     constexpr int TPC = 8;       // lanes per column
     constexpr int EPT = S / TPC; // elements per lane
+    constexpr int NT = CB * TPC;
+    constexpr int TC = 16;       // tokens per staged chunk (double-buffered)
+    constexpr int PR = S * 4 / VW;
+    __shared__ __align__(16) float k_s[2][TC][S];
+    __shared__ __align__(16) float q_s[2][TC][S];
+    __shared__ __align__(16) float v_s[2][TC][CB];
+    __shared__ float g_s[2][TC], b_s[2][TC], d_s[2][TC];
+    const int tid = threadIdx.x;
     const int unit = blockIdx.x;
     const int h = unit % a.H, seq = unit / a.H;
-    const int col = blockIdx.y * CB + threadIdx.x / TPC;
-    const int l = threadIdx.x % TPC;
+    const int col0 = blockIdx.y * CB, cc = tid / TPC, col = col0 + cc;
+    const int l = tid % TPC;
     const int hk = h % a.H_k;
     const int sq = seq / a.rq3, sk = seq / a.rk3;
 
@@ -50,56 +62,124 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
     const float *gb = ptr(a.g, seq * a.g_nb3 + h * a.g_nb1);
     const float *bb = ptr(a.beta, seq * a.b_nb3 + h * a.b_nb1);
 
-    for (int t = 0; t < a.T; ++t) {
-        const float *qt = ptr(qb, t * a.q_nb2);
-        const float *kt = ptr(kb, t * a.k_nb2);
-        float kx[EPT], qx[EPT];
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) {
-            kx[e] = __ldg(kt + l + TPC * e);
-            qx[e] = __ldg(qt + l + TPC * e);
+    // chunk c of TC tokens -> buffer buf (one commit group per call, empty past T)
+    auto stage = [&](int c, int buf) {
+        const int t0 = c * TC, nt = min(TC, a.T - t0);
+        for (int idx = tid; idx < TC * PR; idx += NT) {
+            const int r = idx / PR, pc = idx - r * PR;
+            if (r < nt) {
+                cp_async<VW>(smem_u32(&k_s[buf][r][0]) + pc * VW,
+                             reinterpret_cast<const char *>(ptr(kb, (int64_t)(t0 + r) * a.k_nb2)) +
+                                 pc * VW);
+                cp_async<VW>(smem_u32(&q_s[buf][r][0]) + pc * VW,
+                             reinterpret_cast<const char *>(ptr(qb, (int64_t)(t0 + r) * a.q_nb2)) +
+                                 pc * VW);
+            }
         }
-        const float vv = __ldg(ptr(vb, t * a.v_nb2) + col);
-        const float gg = __ldg(ptr(gb, t * a.g_nb2));
-        const float beta = __ldg(ptr(bb, t * a.b_nb2));
-        const float decay = (float)exp((double)gg);
+        for (int idx = tid; idx < TC * CB; idx += NT) {
+            const int r = idx / CB, c2 = idx - r * CB;
+            if (r < nt)
+                cp_async<4>(smem_u32(&v_s[buf][r][c2]), ptr(vb, (int64_t)(t0 + r) * a.v_nb2) +
+                                                            col0 + c2);
+        }
+        if (tid < nt) {
+            cp_async<4>(smem_u32(&g_s[buf][tid]), ptr(gb, (int64_t)(t0 + tid) * a.g_nb2));
+            cp_async<4>(smem_u32(&b_s[buf][tid]), ptr(bb, (int64_t)(t0 + tid) * a.b_nb2));
+        }
+        cp_async_commit();
+    };
+    const int n_chunks = (a.T + TC - 1) / TC;
+    if constexpr (STAGED) {
+        stage(0, 0);
+        stage(1, 1);
+    }
+    for (int c = 0; c < n_chunks; ++c) {
+        const int buf = c & 1, t0 = c * TC, nt = min(TC, a.T - t0);
+        if constexpr (STAGED) {
+            cp_async_wait<1>(); // chunk c has landed (chunk c + 1 may be in flight)
+            __syncthreads();
+            if (tid < nt)
+                d_s[buf][tid] = (float)exp((double)g_s[buf][tid]);
+            __syncthreads();
+        }
+        for (int r = 0; r < nt; ++r) {
+            const int t = t0 + r;
+            float kx[EPT], qx[EPT], vv, beta, decay;
+            if constexpr (STAGED) {
+#pragma unroll
+                for (int e = 0; e < EPT; ++e) {
+                    kx[e] = k_s[buf][r][l + TPC * e];
+                    qx[e] = q_s[buf][r][l + TPC * e];
+                }
+                vv = v_s[buf][r][cc];
+                beta = b_s[buf][r];
+                decay = d_s[buf][r];
+            } else {
+                const float *qt = ptr(qb, (int64_t)t * a.q_nb2);
+                const float *kt = ptr(kb, (int64_t)t * a.k_nb2);
+#pragma unroll
+                for (int e = 0; e < EPT; ++e) {
+                    kx[e] = __ldg(kt + l + TPC * e);
+                    qx[e] = __ldg(qt + l + TPC * e);
+                }
+                vv = __ldg(ptr(vb, (int64_t)t * a.v_nb2) + col);
+                beta = __ldg(ptr(bb, (int64_t)t * a.b_nb2));
+                decay = (float)exp((double)__ldg(ptr(gb, (int64_t)t * a.g_nb2)));
+            }
 
-        float kv = 0.0f;
+            float kv = 0.0f;
 #pragma unroll
-        for (int e = 0; e < EPT; ++e) {
-            st[e] = __fmul_rn(st[e], decay);
-            kv = __fadd_rn(kv, __fmul_rn(st[e], kx[e]));
-        }
-        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 4));
-        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 2));
-        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 1));
-        const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
-        float at = 0.0f;
+            for (int e = 0; e < EPT; ++e) {
+                st[e] = __fmul_rn(st[e], decay);
+                kv = __fadd_rn(kv, __fmul_rn(st[e], kx[e]));
+            }
+            kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 4));
+            kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 2));
+            kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 1));
+            const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
+            float at = 0.0f;
 #pragma unroll
-        for (int e = 0; e < EPT; ++e) {
-            st[e] = __fadd_rn(st[e], __fmul_rn(kx[e], delta));
-            at = __fadd_rn(at, __fmul_rn(st[e], qx[e]));
-        }
-        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 4));
-        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 2));
-        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 1));
-        if (l == 0)
-            a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = __fmul_rn(at, a.scale);
+            for (int e = 0; e < EPT; ++e) {
+                st[e] = __fadd_rn(st[e], __fmul_rn(kx[e], delta));
+                at = __fadd_rn(at, __fmul_rn(st[e], qx[e]));
+            }
+            at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 4));
+            at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 2));
+            at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 1));
+            if (l == 0)
+                a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = __fmul_rn(at, a.scale);
 
-        const int slot = a.T - 1 - t;
-        if ((a.slots > 1 && slot < a.slots) || (a.slots == 1 && t + 1 == a.T)) {
-            float *o = snap + (size_t)(a.slots == 1 ? 0 : slot) * slot_elems + snap_off;
+            const int slot = a.T - 1 - t;
+            if ((a.slots > 1 && slot < a.slots) || (a.slots == 1 && t + 1 == a.T)) {
+                float *o = snap + (size_t)(a.slots == 1 ? 0 : slot) * slot_elems + snap_off;
 #pragma unroll
-            for (int e = 0; e < EPT; ++e)
-                o[l + TPC * e] = st[e];
+                for (int e = 0; e < EPT; ++e)
+                    o[l + TPC * e] = st[e];
+            }
+        }
+        if constexpr (STAGED) {
+            __syncthreads(); // buffer buf is free again
+            stage(c + 2, buf);
         }
     }
+    if constexpr (STAGED)
+        cp_async_wait<0>();
 }
 
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st) {
     constexpr int S = 128, CB = 16;
     dim3 grid((unsigned)(a.H * a.n_seq), S / CB);
-    gdn_recurrent_kernel<S, CB><<<grid, CB * 8, 0, st>>>(a);
+    // 16-byte staging when every q / k row starts on a 16-byte boundary
+    const bool v16 = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                       (uintptr_t)a.q_nb1 | (uintptr_t)a.q_nb2 | (uintptr_t)a.q_nb3 |
+                       (uintptr_t)a.k_nb1 | (uintptr_t)a.k_nb2 | (uintptr_t)a.k_nb3) &
+                      15) == 0;
+    if (a.T <= 8)
+        gdn_recurrent_kernel<S, CB, 4, false><<<grid, CB * 8, 0, st>>>(a);
+    else if (v16)
+        gdn_recurrent_kernel<S, CB, 16, true><<<grid, CB * 8, 0, st>>>(a);
+    else
+        gdn_recurrent_kernel<S, CB, 4, true><<<grid, CB * 8, 0, st>>>(a);
     return cudaGetLastError();
 }
 

@@ -48,9 +48,11 @@ cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &cfg, dim3 gri
 bool decode_mma_ok(int type, int D, const DecodeArgs &a);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
                               cudaStream_t st);
+// n_groups > 1 merges consecutive blocks of n_splits splits separately; with
+// records, the merged rows are written as partial records (see lse_merge_kernel).
 cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
                          float *out, float *lse, const float *sinks, int n_head,
-                         cudaStream_t st);
+                         cudaStream_t st, int64_t n_groups = 1, bool records = false);
 
 // One tensor-core prefill launch (F16 K/V, F32 q / dst).
 struct PrefillShape {

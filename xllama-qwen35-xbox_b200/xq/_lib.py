@@ -17,6 +17,7 @@ F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
 # Every symbol include/xq_b200.h declares (checked by the CPU test suite).
 EXPORTS = (
     "xq_flash_attn_ext_workspace", "xq_flash_attn_ext", "xq_fa_partials", "xq_lse_merge",
+    "xq_lse_merge_records",
     "xq_attend_range_workspace", "xq_attend_range", "xq_split_k", "xq_gated_delta_net",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
     "xq_flash_attn_ext_noalloc",
@@ -59,6 +60,7 @@ def lib():
         "xq_flash_attn_ext": (C.c_int, [P(FaParams), vp, sz, vp]),
         "xq_fa_partials": (C.c_int, [P(FaParams), i64, i64, i64, vp, vp]),
         "xq_lse_merge": (C.c_int, [vp, i64, i64, i64, vp, vp, vp]),
+        "xq_lse_merge_records": (C.c_int, [vp, i64, i64, i64, i64, vp, vp]),
         "xq_attend_range_workspace": (sz, [i32, u32, u32, u32, u32, u32, u32]),
         "xq_attend_range": (C.c_int, [i32, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp, C.c_float,
                                       u32, vp, vp, vp, sz, vp]),

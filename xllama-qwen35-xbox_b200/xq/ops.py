@@ -145,6 +145,19 @@ def lse_merge(partials: torch.Tensor, out=None, lse=None, want_lse=True, stream=
     return o, lz
 
 
+def lse_merge_records(partials: torch.Tensor, splits_per_group: int, out=None, stream=None):
+    """partials float32 (n_groups * splits_per_group, n_rows, D + 2) -> one
+    record per (group, row): float32 (n_groups, n_rows, D + 2) = (O, lse, 1)."""
+    n_splits, n_rows, d2 = partials.shape
+    assert partials.is_contiguous() and n_splits % splits_per_group == 0
+    n_groups = n_splits // splits_per_group
+    rec = out if out is not None else torch.empty((n_groups, n_rows, d2), dtype=torch.float32,
+                                                  device=partials.device)
+    check(lib().xq_lse_merge_records(partials.data_ptr(), n_groups, splits_per_group, n_rows,
+                                     d2 - 2, rec.data_ptr(), _stream(stream)))
+    return rec
+
+
 def split_k(active: int, mode: int) -> int:
     return int(lib().xq_split_k(active, mode))
 

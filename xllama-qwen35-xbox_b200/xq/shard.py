@@ -1,13 +1,19 @@
 """KV-sharded flash decode over several GPUs (one process per GPU).
 
 The KV rows of every sequence are cut into a fixed global list of splits of
-`rows_per_split` rows.  Rank r holds and reads a contiguous block of those
-splits (`split_block`), writes one partial record (acc[D], max, denom) per
-(split, sequence, head) with `xq.fa_partials`, the blocks are all-gathered in
-global split order (`gather_partials`, NCCL on GPUs), and every rank merges
-them with `xq.lse_merge`.  Because the list of splits and the merge order do
-not depend on the number of ranks, the output is bit-identical for any GPU
-count.  There is no other exchange step.
+`rows_per_split` rows, and the splits into a fixed list of `n_groups` groups
+of consecutive splits.  Rank r holds and reads a contiguous block of groups
+(`split_block` over groups) and:
+  1. writes one partial record (acc[D], max, denom) per (split, sequence,
+     head) with `xq.fa_partials`;
+  2. merges each of its groups in split order into one record (O, lse, 1)
+     with `xq.lse_merge_records`;
+  3. all-gathers the group records in group order (`gather_partials`, NCCL on
+     GPUs: n_groups x n_rows x (D + 2) floats in total);
+  4. merges the group records with `xq.lse_merge`.
+The grouping and both merge orders are fixed by (n_splits, n_groups) alone,
+so the output is bit-identical for any rank count that divides n_groups.
+There is no other exchange step.
 """
 from __future__ import annotations
 
@@ -53,29 +59,32 @@ def gather_partials(part_local, n_splits: int, group=None, out=None):
 
 
 def sharded_flash_decode(q, k_local, v_local, k_type: int, rows_per_split: int, n_splits: int,
-                         scale: float = 1.0, group=None, out=None, partials_fn=None,
-                         merge_fn=None):
+                         scale: float = 1.0, group=None, out=None, n_groups: int = 8,
+                         partials_fn=None, records_fn=None, merge_fn=None):
     """One decode step whose KV rows are spread over the ranks of `group`.
 
-    k_local / v_local hold this rank's rows only: split_block(n_splits, ...)
-    of the global splits, row 0 = first row of its first split.  Returns the
-    merged output (n_seq * n_q * n_head, D) and the lse on every rank.
-    `partials_fn(q, k, v, k_type, rows_per_split, n_local, scale)` and
-    `merge_fn(partials)` default to the B200 kernels (xq.fa_partials,
-    xq.lse_merge)."""
+    k_local / v_local hold this rank's rows only: the splits of groups
+    split_block(n_groups, world, rank), row 0 = first row of its first split.
+    Returns the merged (out (n_seq * n_q * n_head, D), lse) on every rank.
+    `partials_fn(q, k, v, k_type, rows_per_split, n_local_splits, scale)`,
+    `records_fn(partials, splits_per_group)` and `merge_fn(records)` default to
+    the B200 kernels (xq.fa_partials, xq.lse_merge_records, xq.lse_merge)."""
     import torch.distributed as dist
     world, rank = dist.get_world_size(group), dist.get_rank(group)
-    b, e = split_block(n_splits, world, rank)
+    if n_splits % n_groups or n_groups % world:
+        raise ValueError(f"{n_splits} splits / {n_groups} groups / {world} ranks do not divide")
+    per_group = n_splits // n_groups
+    gb, ge = split_block(n_groups, world, rank)
+    from . import ops
     if partials_fn is None:
-        from . import ops
-
         def partials_fn(q, k, v, ty, rows, n_local, sc):
             return ops.fa_partials(q, k, v, ty, rows, 0, n_local, scale=sc)
+    if records_fn is None:
+        records_fn = ops.lse_merge_records
     if merge_fn is None:
-        from . import ops
-
-        def merge_fn(p):
-            return ops.lse_merge(p, out=out)
-    local = partials_fn(q, k_local, v_local, k_type, rows_per_split, e - b, scale)
-    full = gather_partials(local, n_splits, group)
-    return merge_fn(full)
+        def merge_fn(r):
+            return ops.lse_merge(r, out=out)
+    local = partials_fn(q, k_local, v_local, k_type, rows_per_split, (ge - gb) * per_group,
+                        scale)
+    records = records_fn(local, per_group)
+    return merge_fn(gather_partials(records, n_groups, group))
