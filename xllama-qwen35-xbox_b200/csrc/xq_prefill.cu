@@ -401,27 +401,39 @@ __global__ void __launch_bounds__(pf::NT, 1)
                     sv[32 + i] = t[i];
             }
             const int kbase = kt * BN;
-            float mt = -INFINITY;
+            if (kbase + BN > a.n_kv) { // last tile: keys past n_kv are dead
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                float x = sv[i] * a.scale_log2;
-                if (kbase + i >= a.n_kv)
-                    x = -INFINITY;
-                sv[i] = x;
+                for (int i = 0; i < 64; ++i)
+                    if (kbase + i >= a.n_kv)
+                        sv[i] = -INFINITY;
             }
-            if (cls == 2) {
+            // mt: the tile's row max in the log2 domain; p = 2^(sv * c - m_used)
+            float c = 1.0f;
+            const bool raw = cls == 1 && a.scale_log2 > 0.0f;
+            if (!raw) {
                 const __half *mp = reinterpret_cast<const __half *>(mrow) + kbase;
 #pragma unroll
                 for (int i = 0; i < 64; ++i) {
-                    if (kbase + i < a.n_kv) {
+                    float x = sv[i] * a.scale_log2;
+                    if (cls == 2 && kbase + i < a.n_kv) {
                         const float mv = __half2float(mp[i]);
-                        sv[i] = mv == -INFINITY ? -INFINITY : sv[i] + mv * 1.4426950408889634f;
+                        x = mv == -INFINITY ? -INFINITY : x + mv * 1.4426950408889634f;
                     }
+                    sv[i] = sv[i] == -INFINITY ? -INFINITY : x;
                 }
+            } else {
+                c = a.scale_log2; // scale > 0: the max of the raw scores, scaled once
             }
+            float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-                mt = fmaxf(mt, sv[i]);
+            for (int i = 0; i < 64; i += 4) {
+                m4[0] = fmaxf(m4[0], sv[i]);
+                m4[1] = fmaxf(m4[1], sv[i + 1]);
+                m4[2] = fmaxf(m4[2], sv[i + 2]);
+                m4[3] = fmaxf(m4[3], sv[i + 3]);
+            }
+            const float mraw = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+            const float mt = mraw == -INFINITY ? -INFINITY : mraw * c;
             // lazy rescale: move m_used only when the max grew by > 8 (log2); the
             // decision is per row, the TMEM traffic is warp-collective
             const bool grow = mt > m_used + 8.0f || (m_used == -INFINITY && mt != -INFINITY);
@@ -436,28 +448,33 @@ __global__ void __launch_bounds__(pf::NT, 1)
                 }
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < D; c += 32) {
+                for (int cc = 0; cc < D; cc += 32) {
                     float o[32];
-                    tmem_ld32(lane_base + TM_O + c, o);
+                    tmem_ld32(lane_base + TM_O + cc, o);
                     uint32_t w[32];
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
                         w[i] = __float_as_uint(o[i] * f);
-                    tmem_st32(lane_base + TM_O + c, w);
+                    tmem_st32(lane_base + TM_O + cc, w);
                 }
             }
             l *= f;
             m_used = mnew;
+            // p = 2^(sv * c - m_used): -inf scores give 2^-inf = 0 (m_used is
+            // finite whenever a live key exists; a row with none keeps 0)
+            const float mu = m_used == -INFINITY ? 0.0f : m_used;
+            const float2 c2 = make_float2(c, c), nm2 = make_float2(-mu, -mu);
             uint32_t pk[32];
-            float lt = 0.0f;
+            float2 lt2 = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-                const float p0 = sv[2 * i] == -INFINITY ? 0.0f : ex2(sv[2 * i] - m_used);
-                const float p1 = sv[2 * i + 1] == -INFINITY ? 0.0f : ex2(sv[2 * i + 1] - m_used);
-                const __half2 hp = __floats2half2_rn(p0, p1);
-                lt += __low2float(hp) + __high2float(hp);
+                const float2 x = __ffma2_rn(make_float2(sv[2 * i], sv[2 * i + 1]), c2, nm2);
+                const float2 pp = make_float2(ex2(x.x), ex2(x.y));
+                lt2 = __fadd2_rn(lt2, pp);
+                const __half2 hp = __floats2half2_rn(pp.x, pp.y);
                 pk[i] = *reinterpret_cast<const uint32_t *>(&hp);
             }
+            const float lt = lt2.x + lt2.y;
             l += lt;
             tmem_st32(s_tm, pk);
             tmem_wait_st();
