@@ -7,9 +7,11 @@
 //
 // One CTA = 128 query rows of one head (TMEM lane r <-> query row r).
 //   warp 0      TMA producer: K_j, V_j tiles (64 keys x D, SW128) into a
-//               4-slot ring, completion on mbarriers (expect_tx)
+//               6-slot (D=256) / 8-slot ring, completion on mbarriers (expect_tx)
 //   warp 1      TMEM allocator + MMA issuer (one lane):
-//                 S_j = Q K_j^T   (SS, M=128, N=64, K=D; S in TMEM, 2 buffers)
+//                 S_j = Q K_j^T   (TS, M=128, N=64, K=D; A = Q in TMEM, so
+//                                  only K is read from shared memory; S in
+//                                  TMEM, 2 buffers)
 //                 O  += P_j V_j   (TS, A = P_j in TMEM, B = V_j MN-major, N=D)
 //               issue order S_0, S_1, PV_0, S_2, PV_1, ... so the tensor
 //               core computes S_{j+1} while the softmax works on S_j
@@ -18,7 +20,7 @@
 //               A operand of PV_j), row sums; O is rescaled in TMEM only when
 //               the running max grows by more than 2^8 (lazy rescale, exact:
 //               the same m_used scales both O and l); epilogue O / l
-//   all warps   convert the Q tile F32 -> f16 into the SW128 K-major layout
+//   warps 4-7   first store their query rows (F32 -> f16 pairs) into TMEM
 // A 128x64 block classification of the mask (all -inf / all 0 / mixed),
 // computed by a pre-pass over the mask, lets every role skip dead blocks and
 // read mask values only for mixed blocks.
@@ -40,7 +42,8 @@ namespace pf {
 
 constexpr int BM = 128;   // query rows per CTA
 constexpr int BN = 64;    // keys per tile
-constexpr int NSLOT = 4;  // K/V ring slots
+// K/V ring slots (one K or V tile each): the whole shared memory goes to the ring
+__host__ __device__ constexpr int nslot(int D) { return D == 256 ? 6 : 8; }
 constexpr int NT = 256;   // threads
 constexpr uint64_t kWaitLimitNs = 2000000000ull; // 2 s: far beyond any legitimate wait
 
@@ -161,6 +164,13 @@ __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
 }
 
+// True in exactly one lane of the (fully active) warp.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile("{\n.reg .pred P;\nelect.sync _|P, 0xffffffff;\nselp.u32 %0, 1, 0, P;\n}\n"
+                 : "=r"(pred));
+    return pred != 0;
+}
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -188,12 +198,14 @@ __global__ void __launch_bounds__(pf::NT, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
     using namespace pf;
-    constexpr int QBYTES = BM * D * 2;            // Q tile, f16
+    constexpr int NSLOT = nslot(D);
     constexpr int TBYTES = BN * D * 2;            // one K or V tile
     constexpr int NBOX = D / 64;                  // 64-element (128 B) column boxes
     constexpr uint32_t TM_O = 0;                  // O: columns [0, D)
     constexpr uint32_t TM_S = D;                  // S buffers: [D, D + 2*BN)
-    constexpr uint32_t TM_COLS = D + 2 * BN <= 256 ? 256 : 512;
+    constexpr uint32_t TM_Q = D + 2 * BN;         // Q as f16 pairs: [TM_Q, TM_Q + D/2)
+    constexpr uint32_t TM_COLS = 512;
+    static_assert(TM_Q + D / 2 <= TM_COLS, "TMEM columns");
     constexpr uint32_t ID_QK = idesc(BM, BN, 0, 0);
     constexpr uint32_t ID_PV = idesc(BM, D, 0, 1);
     static_assert(D == 128 || D == 256, "head dim");
@@ -201,11 +213,10 @@ __global__ void __launch_bounds__(pf::NT, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *q_s = smem;
-    uint8_t *ring = smem + QBYTES;
+    uint8_t *ring = smem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + NSLOT * TBYTES);
-    // bars: full[NSLOT], empty[NSLOT], s_full[2], p_full[2], o_done, drain
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NSLOT + 6);
+    // bars: full[NSLOT], empty[NSLOT], s_full[2], p_full[2], o_done, drain, q_ready
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * NSLOT + 7);
     volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -220,7 +231,7 @@ __global__ void __launch_bounds__(pf::NT, 1)
 
     auto bar = [&](int i) { return smem_u32(bars + i); };
     const int B_FULL = 0, B_EMPTY = NSLOT, B_S = 2 * NSLOT, B_P = 2 * NSLOT + 2,
-              B_O = 2 * NSLOT + 4, B_DRAIN = 2 * NSLOT + 5;
+              B_O = 2 * NSLOT + 4, B_DRAIN = 2 * NSLOT + 5, B_Q = 2 * NSLOT + 6;
 
     if (tid == 0) {
         for (int i = 0; i < NSLOT; ++i) {
@@ -233,6 +244,7 @@ __global__ void __launch_bounds__(pf::NT, 1)
         mbar_init(bar(B_P + 1), 128);
         mbar_init(bar(B_O), 1);
         mbar_init(bar(B_DRAIN), 1);
+        mbar_init(bar(B_Q), 128);
         *abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -243,26 +255,6 @@ __global__ void __launch_bounds__(pf::NT, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
     }
 
-    // ---- Q tile: F32 global -> f16 SW128 K-major boxes [NBOX][BM rows][128 B] ----
-    for (int idx = tid; idx < BM * (D / 8); idx += NT) {
-        const int r = idx / (D / 8), c8 = idx % (D / 8); // 8-element chunk
-        const int d0 = c8 * 8;
-        uint4 packed = make_uint4(0, 0, 0, 0);
-        if (q0 + r < a.n_q) {
-            const float4 *src = reinterpret_cast<const float4 *>(
-                a.q + (int64_t)(q0 + r) * a.q_nb1 + (int64_t)h * a.q_nb2 + (int64_t)s * a.q_nb3 +
-                4 * d0);
-            const float4 x0 = src[0], x1 = src[1];
-            __half2 h0 = __floats2half2_rn(x0.x, x0.y), h1 = __floats2half2_rn(x0.z, x0.w);
-            __half2 h2 = __floats2half2_rn(x1.x, x1.y), h3 = __floats2half2_rn(x1.z, x1.w);
-            packed = make_uint4(*reinterpret_cast<uint32_t *>(&h0), *reinterpret_cast<uint32_t *>(&h1),
-                                *reinterpret_cast<uint32_t *>(&h2), *reinterpret_cast<uint32_t *>(&h3));
-        }
-        const int box = d0 / 64, chunk = (d0 % 64) / 8;
-        *reinterpret_cast<uint4 *>(q_s + box * (BM * 128) + r * 128 + ((chunk ^ (r & 7)) * 16)) =
-            packed;
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -306,62 +298,79 @@ __global__ void __launch_bounds__(pf::NT, 1)
         }
     } else if (warp == 1) {
         // -------------------------------- MMA ---------------------------------
-        if (lane == 0 && n_live > 0) {
-            const uint32_t q_base = smem_u32(q_s);
+        // The whole warp runs the schedule (its waits, descriptors and TMEM
+        // addresses stay warp-uniform); one elected lane issues each MMA and
+        // commit.  Shared-memory descriptors are precomputed for ring slot 0
+        // and offset by constants (the 14-bit address field cannot carry: shared
+        // memory is below 256 KB).
+        if (n_live > 0) {
+            const uint64_t dk0 = sdesc(smem_u32(ring), 16, 1024);       // K: K-major
+            const uint64_t dv0 = sdesc(smem_u32(ring), BN * 128, 1024); // V: MN-major
+            constexpr uint64_t SLOT_STEP = TBYTES >> 4;
+            const bool leader = elect_one();
+            auto wait_all = [&](int b, uint32_t parity) {
+                return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, abort_s));
+            };
             auto issue_s = [&](int j) -> bool {
                 const int n = 2 * j, slot = n % NSLOT, use = n / NSLOT;
-                if (!mbar_wait(bar(B_FULL + slot), use & 1, abort_s))
+                if (!wait_all(B_FULL + slot, use & 1))
                     return false;
                 // S buffer j%2 is free: PV_{j-2} (which read P_{j-2} there) was
                 // issued before this point and the tensor pipe runs in order.
                 tc_fence_after();
-                const uint32_t k_base = smem_u32(ring + slot * TBYTES);
+                const uint64_t db0 = dk0 + (uint64_t)slot * SLOT_STEP;
                 const uint32_t d_tm = tmem + TM_S + (j & 1) * BN;
+                if (leader) {
+                    // A = Q from TMEM (8 columns = 16 f16 per K step), B = K from
+                    // smem: step kk at byte (kk / 4) * BN * 128 + (kk % 4) * 32
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk & 3) * 32; // 16 f16 = 32 B inside the SW128 row
-                    const uint64_t da = sdesc(q_base + (kk / 4) * (BM * 128) + off, 16, 1024);
-                    const uint64_t db = sdesc(k_base + (kk / 4) * (BN * 128) + off, 16, 1024);
-                    mma_ss(d_tm, da, db, ID_QK, kk > 0);
+                    for (int kk = 0; kk < D / 16; ++kk)
+                        mma_ts(d_tm, tmem + TM_Q + kk * 8,
+                               db0 + (uint64_t)((kk / 4) * (BN * 128 / 16) + (kk & 3) * 2),
+                               ID_QK, kk > 0);
+                    mma_commit(bar(B_S + (j & 1)));
+                    mma_commit(bar(B_EMPTY + slot));
                 }
-                mma_commit(bar(B_S + (j & 1)));
-                mma_commit(bar(B_EMPTY + slot));
+                __syncwarp();
                 return true;
             };
-            bool ok = issue_s(0);
+            // Q rows are in TMEM once all 128 softmax threads arrived
+            bool ok = wait_all(B_Q, 0);
+            tc_fence_after();
+            ok = ok && issue_s(0);
             for (int j = 0; ok && j < n_live; ++j) {
                 if (j + 1 < n_live)
                     ok = issue_s(j + 1);
                 if (!ok)
                     break;
                 // PV_j: wait for P_j from the softmax warps and V_j from TMA
-                if (!mbar_wait(bar(B_P + (j & 1)), (j >> 1) & 1, abort_s)) {
-                    ok = false;
-                    break;
-                }
                 const int n = 2 * j + 1, slot = n % NSLOT, use = n / NSLOT;
-                if (!mbar_wait(bar(B_FULL + slot), use & 1, abort_s)) {
+                if (!wait_all(B_P + (j & 1), (j >> 1) & 1) || !wait_all(B_FULL + slot, use & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t v_base = smem_u32(ring + slot * TBYTES);
+                const uint64_t db0 = dv0 + (uint64_t)slot * SLOT_STEP;
                 const uint32_t p_tm = tmem + TM_S + (j & 1) * BN;
-#pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
+                if (leader) {
                     // B = V rows [16kk, 16kk+16) x all D columns, MN-major SW128:
                     // 64-column boxes BN*128 bytes apart (LBO), 8-row groups
-                    // 1024 bytes apart (SBO)
-                    const uint64_t db = sdesc(v_base + kk * 2048, BN * 128, 1024);
-                    mma_ts(tmem + TM_O, p_tm + kk * 8, db, ID_PV, (j > 0 || kk > 0));
+                    // 1024 bytes apart (SBO); step kk at byte kk * 2048
+#pragma unroll
+                    for (int kk = 0; kk < BN / 16; ++kk)
+                        mma_ts(tmem + TM_O, p_tm + kk * 8, db0 + (uint64_t)(kk * 128), ID_PV,
+                               (j > 0 || kk > 0));
+                    mma_commit(bar(B_O));
+                    mma_commit(bar(B_EMPTY + slot));
                 }
-                mma_commit(bar(B_O));
-                mma_commit(bar(B_EMPTY + slot));
+                __syncwarp();
             }
-            if (!ok)
+            if (!ok && lane == 0)
                 *abort_s = 1;
             // every tcgen05.mma issued above has completed once this commits
-            mma_commit(bar(B_DRAIN));
+            if (leader)
+                mma_commit(bar(B_DRAIN));
+            __syncwarp();
             volatile int none = 0;
             mbar_wait(bar(B_DRAIN), 0, &none, 100000000ull);
         }
@@ -374,6 +383,27 @@ __global__ void __launch_bounds__(pf::NT, 1)
                                            (int64_t)(h % a.m_ne2) * a.m_nb2 +
                                            (int64_t)(s % a.m_ne3) * a.m_nb3
                                      : nullptr;
+        {
+            // this thread's query row -> f16 pairs in TMEM lane r (the A operand of S)
+            const float4 *src = reinterpret_cast<const float4 *>(
+                a.q + (int64_t)min(qrow, a.n_q - 1) * a.q_nb1 + (int64_t)h * a.q_nb2 +
+                (int64_t)s * a.q_nb3);
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 64) {
+                uint32_t w[32];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const float4 x = qrow < a.n_q ? src[c0 / 4 + i] : make_float4(0, 0, 0, 0);
+                    const __half2 h0 = __floats2half2_rn(x.x, x.y), h1 = __floats2half2_rn(x.z, x.w);
+                    w[2 * i] = *reinterpret_cast<const uint32_t *>(&h0);
+                    w[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&h1);
+                }
+                tmem_st32(lane_base + TM_Q + c0 / 2, w);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(B_Q));
+        }
         float m_used = -INFINITY, l = 0.0f;
         int j = 0;
         bool ok = true;
@@ -647,7 +677,7 @@ cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, co
     a.n_qt = n_qt;
     a.n_kt = n_kt;
     a.scale_log2 = ps.scale * 1.4426950408889634f;
-    const size_t smem = 1024 + (size_t)pf::BM * D * 2 + (size_t)pf::NSLOT * pf::BN * D * 2 + 256;
+    const size_t smem = 1024 + (size_t)pf::nslot(D) * pf::BN * D * 2 + 256;
     dim3 grid((unsigned)(n_qt * ps.n_head * ps.n_seq));
     if (D == 256) {
         cudaFuncSetAttribute(fa_prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
