@@ -63,16 +63,17 @@ def test_gdn_reference_selftest_protocol(T, K, pad):
     samp = snaps[:, g["snap_sample_idx"]]
     ref_s = g[key + "_snap_sample"]
     assert np.abs(samp - ref_s).max() / np.abs(ref_s).max() <= 1e-4
-    # same eight-lane order as the reference's mirror: bit-exact while exp(g)
-    # rounds the same as the host libm (short T); within float noise beyond
+    # T <= 8 runs the reference mirror's eight-lane order: bit-exact while
+    # exp(g) rounds the same as the host libm (short T).  Longer sequences run
+    # the packed-FMA stream kernel: float rounding only (2e-5 of the max)
     _, yo, so = oracle.gated_delta_net(*views, slots=K, lanes8=True)
     s4 = snaps.reshape(written, 32, 128, 128)
     if T <= 5:
         assert np.array_equal(y.view(np.uint32), yo[0].view(np.uint32))
         assert np.array_equal(s4.view(np.uint32), so[:written, 0].view(np.uint32))
     else:
-        assert np.abs(y - yo[0]).max() <= 1e-6 * np.abs(yo[0]).max()
-        assert np.abs(s4 - so[:written, 0]).max() <= 1e-6 * np.abs(so[:written, 0]).max()
+        assert np.abs(y - yo[0]).max() <= 2e-5 * np.abs(yo[0]).max()
+        assert np.abs(s4 - so[:written, 0]).max() <= 2e-5 * np.abs(so[:written, 0]).max()
 
 
 def test_gdn_prefix_invariance_across_T_and_K():
@@ -129,14 +130,16 @@ def test_gdn_key_head_is_h_mod_Hk():
     assert np.abs(y - y_div).max() > 1e-3
 
 
-@pytest.mark.parametrize("T,K,pad", [(40, 3, 3), (40, 1, 0)])
-def test_gdn_staged_path_vs_oracle(T, K, pad):
-    """Sequences longer than 8 tokens stage their inputs through shared memory:
-    16-byte copies for aligned rows, 4-byte copies for the padded layout."""
+@pytest.mark.parametrize("T,K,pad", [(40, 3, 3), (40, 1, 0), (9, 5, 0), (33, 17, 0)])
+def test_gdn_stream_path_vs_oracle(T, K, pad):
+    """Sequences longer than 8 tokens run the stream kernel, which stages its
+    inputs through shared memory (16-byte copies for aligned rows, 4-byte
+    copies for the padded layout) and reorders the float arithmetic: within
+    2e-5 of the max of the sequential reference, snapshot slots included."""
     got, views = _gpu_selftest(T, K, pad)
     written = min(T, K)
     _, yo, so = oracle.gated_delta_net(*views, slots=K, lanes8=True)
     y = got[:4096 * T].reshape(T, 32, 128)
     s4 = got[4096 * T:4096 * T + 524288 * written].reshape(written, 32, 128, 128)
-    assert np.abs(y - yo[0]).max() <= 1e-6 * np.abs(yo[0]).max()
-    assert np.abs(s4 - so[:written, 0]).max() <= 1e-6 * np.abs(so[:written, 0]).max()
+    assert np.abs(y - yo[0]).max() <= 2e-5 * np.abs(yo[0]).max()
+    assert np.abs(s4 - so[:written, 0]).max() <= 2e-5 * np.abs(so[:written, 0]).max()

@@ -8,9 +8,9 @@
 //   S[col][:] += k_t * d
 //   y_t[col] = (sum_i S[col][i] q_t[i]) / sqrt(S_k)
 // with key head h % H_k.  Columns are independent, so a CTA owns CB columns
-// of one (sequence, head) and keeps them in registers for all T tokens; the
-// token inputs are staged through shared memory 16 tokens at a time
-// (double-buffered cp.async), so no token waits for a global load.  Eight
+// of one (sequence, head) and keeps them in registers for all T tokens.  This
+// bit-comparable kernel serves short sequences (decode, T <= 8); longer ones
+// go to gdn_stream_kernel below.  Eight
 // lanes share a column; lane l holds elements i = l + 8e, accumulates its
 // partial dot in increasing i and the eight partials meet in the tree
 // (l, l+4), (l, l+2), (l, l+1) -- the order of the reference mirror's
@@ -21,24 +21,14 @@
 
 namespace xq {
 
-// STAGED: token inputs through shared memory (long sequences); otherwise each
-// token reads them straight from global memory (a few tokens, e.g. decode).
-template <int S, int CB, int VW, bool STAGED>
+template <int S, int CB>
 __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) {
     constexpr int TPC = 8;       // lanes per column
     constexpr int EPT = S / TPC; // elements per lane
-    constexpr int NT = CB * TPC;
-    constexpr int TC = 16;       // tokens per staged chunk (double-buffered)
-    constexpr int PR = S * 4 / VW;
-    __shared__ __align__(16) float k_s[2][TC][S];
-    __shared__ __align__(16) float q_s[2][TC][S];
-    __shared__ __align__(16) float v_s[2][TC][CB];
-    __shared__ float g_s[2][TC], b_s[2][TC], d_s[2][TC];
-    const int tid = threadIdx.x;
     const int unit = blockIdx.x;
     const int h = unit % a.H, seq = unit / a.H;
-    const int col0 = blockIdx.y * CB, cc = tid / TPC, col = col0 + cc;
-    const int l = tid % TPC;
+    const int col = blockIdx.y * CB + threadIdx.x / TPC;
+    const int l = threadIdx.x % TPC;
     const int hk = h % a.H_k;
     const int sq = seq / a.rq3, sk = seq / a.rk3;
 
@@ -62,7 +52,103 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
     const float *gb = ptr(a.g, seq * a.g_nb3 + h * a.g_nb1);
     const float *bb = ptr(a.beta, seq * a.b_nb3 + h * a.b_nb1);
 
-    // chunk c of TC tokens -> buffer buf (one commit group per call, empty past T)
+    for (int t = 0; t < a.T; ++t) {
+        const float *qt = ptr(qb, (int64_t)t * a.q_nb2);
+        const float *kt = ptr(kb, (int64_t)t * a.k_nb2);
+        float kx[EPT], qx[EPT];
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            kx[e] = __ldg(kt + l + TPC * e);
+            qx[e] = __ldg(qt + l + TPC * e);
+        }
+        const float vv = __ldg(ptr(vb, (int64_t)t * a.v_nb2) + col);
+        const float beta = __ldg(ptr(bb, (int64_t)t * a.b_nb2));
+        const float decay = (float)exp((double)__ldg(ptr(gb, (int64_t)t * a.g_nb2)));
+
+        float kv = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            st[e] = __fmul_rn(st[e], decay);
+            kv = __fadd_rn(kv, __fmul_rn(st[e], kx[e]));
+        }
+        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 4));
+        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 2));
+        kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 1));
+        const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
+        float at = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            st[e] = __fadd_rn(st[e], __fmul_rn(kx[e], delta));
+            at = __fadd_rn(at, __fmul_rn(st[e], qx[e]));
+        }
+        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 4));
+        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 2));
+        at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 1));
+        if (l == 0)
+            a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = __fmul_rn(at, a.scale);
+
+        const int slot = a.T - 1 - t;
+        if ((a.slots > 1 && slot < a.slots) || (a.slots == 1 && t + 1 == a.T)) {
+            float *o = snap + (size_t)(a.slots == 1 ? 0 : slot) * slot_elems + snap_off;
+#pragma unroll
+            for (int e = 0; e < EPT; ++e)
+                o[l + TPC * e] = st[e];
+        }
+    }
+}
+
+// Long sequences (T > 8): the same recurrence, the token inputs staged through
+// shared memory 16 tokens at a time (double-buffered cp.async), and the
+// arithmetic reorganised for issue rate instead of the reference mirror's
+// lane order: lane l of a column owns key elements 4l + 32j + {0..3}
+// (j = 0..3, so each input vector arrives as four conflict-free 16-byte
+// shared loads), dot products are packed FP32x2 FMAs, and the decay is
+// applied to the reduced dot product (S k after the decay equals
+// decay * (S k)) and fused into the state update S = S * decay + k * delta.
+// Results agree with the sequential reference to float rounding, not bit for
+// bit.
+template <int S, int CB, int VW>
+__global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
+    constexpr int TPC = 8;      // lanes per column
+    constexpr int NT = CB * TPC;
+    constexpr int TC = 16;      // tokens per staged chunk
+    constexpr int PR = S * 4 / VW;
+    static_assert(S == 128, "element ownership assumes 128-long rows");
+    __shared__ __align__(16) float k_s[2][TC][S];
+    __shared__ __align__(16) float q_s[2][TC][S];
+    __shared__ __align__(16) float v_s[2][TC][CB];
+    __shared__ float g_s[2][TC], b_s[2][TC], d_s[2][TC];
+    const int tid = threadIdx.x;
+    const int h = blockIdx.x % a.H, seq = blockIdx.x / a.H;
+    const int col0 = blockIdx.y * CB, cc = tid / TPC, col = col0 + cc;
+    const int l = tid % TPC;
+    const int hk = h % a.H_k;
+    const int sq = seq / a.rq3, sk = seq / a.rk3;
+
+    // state row `col`, elements 4l + 32j + x held as float2 pairs st[2j], st[2j+1]
+    const float *st_row = reinterpret_cast<const float *>(
+        reinterpret_cast<const char *>(a.state) + seq * a.s_nb3 + (int64_t)h * a.s_nb2 +
+        (int64_t)col * a.s_nb1);
+    float2 st[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int e = 4 * l + 32 * j;
+        st[2 * j] = make_float2(st_row[e], st_row[e + 1]);
+        st[2 * j + 1] = make_float2(st_row[e + 2], st_row[e + 3]);
+    }
+    const size_t slot_elems = (size_t)S * S * a.H * a.n_seq;
+    float *snap = a.dst + (size_t)S * a.H * a.T * a.n_seq;
+    const size_t snap_off = ((size_t)(seq * a.H + h) * S + col) * S;
+
+    auto ptr = [](const float *base, int64_t o) {
+        return reinterpret_cast<const float *>(reinterpret_cast<const char *>(base) + o);
+    };
+    const float *qb = ptr(a.q, sq * a.q_nb3 + hk * a.q_nb1);
+    const float *kb = ptr(a.k, sk * a.k_nb3 + hk * a.k_nb1);
+    const float *vb = ptr(a.v, seq * a.v_nb3 + h * a.v_nb1);
+    const float *gb = ptr(a.g, seq * a.g_nb3 + h * a.g_nb1);
+    const float *bb = ptr(a.beta, seq * a.b_nb3 + h * a.b_nb1);
+
     auto stage = [&](int c, int buf) {
         const int t0 = c * TC, nt = min(TC, a.T - t0);
         for (int idx = tid; idx < TC * PR; idx += NT) {
@@ -89,81 +175,70 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
         cp_async_commit();
     };
     const int n_chunks = (a.T + TC - 1) / TC;
-    if constexpr (STAGED) {
-        stage(0, 0);
-        stage(1, 1);
-    }
+    stage(0, 0);
+    stage(1, 1);
     for (int c = 0; c < n_chunks; ++c) {
         const int buf = c & 1, t0 = c * TC, nt = min(TC, a.T - t0);
-        if constexpr (STAGED) {
-            cp_async_wait<1>(); // chunk c has landed (chunk c + 1 may be in flight)
-            __syncthreads();
-            if (tid < nt)
-                d_s[buf][tid] = (float)exp((double)g_s[buf][tid]);
-            __syncthreads();
-        }
+        cp_async_wait<1>(); // chunk c has landed (chunk c + 1 may be in flight)
+        __syncthreads();
+        if (tid < nt)
+            d_s[buf][tid] = (float)exp((double)g_s[buf][tid]);
+        __syncthreads();
         for (int r = 0; r < nt; ++r) {
             const int t = t0 + r;
-            float kx[EPT], qx[EPT], vv, beta, decay;
-            if constexpr (STAGED) {
+            float4 kx[4], qx[4];
 #pragma unroll
-                for (int e = 0; e < EPT; ++e) {
-                    kx[e] = k_s[buf][r][l + TPC * e];
-                    qx[e] = q_s[buf][r][l + TPC * e];
-                }
-                vv = v_s[buf][r][cc];
-                beta = b_s[buf][r];
-                decay = d_s[buf][r];
-            } else {
-                const float *qt = ptr(qb, (int64_t)t * a.q_nb2);
-                const float *kt = ptr(kb, (int64_t)t * a.k_nb2);
-#pragma unroll
-                for (int e = 0; e < EPT; ++e) {
-                    kx[e] = __ldg(kt + l + TPC * e);
-                    qx[e] = __ldg(qt + l + TPC * e);
-                }
-                vv = __ldg(ptr(vb, (int64_t)t * a.v_nb2) + col);
-                beta = __ldg(ptr(bb, (int64_t)t * a.b_nb2));
-                decay = (float)exp((double)__ldg(ptr(gb, (int64_t)t * a.g_nb2)));
+            for (int j = 0; j < 4; ++j) {
+                kx[j] = *reinterpret_cast<const float4 *>(&k_s[buf][r][4 * l + 32 * j]);
+                qx[j] = *reinterpret_cast<const float4 *>(&q_s[buf][r][4 * l + 32 * j]);
             }
-
-            float kv = 0.0f;
+            const float vv = v_s[buf][r][cc], beta = b_s[buf][r], decay = d_s[buf][r];
+            // (S k) before the decay, two independent packed accumulators
+            float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int e = 0; e < EPT; ++e) {
-                st[e] = __fmul_rn(st[e], decay);
-                kv = __fadd_rn(kv, __fmul_rn(st[e], kx[e]));
+            for (int j = 0; j < 4; ++j) {
+                a0 = __ffma2_rn(st[2 * j], make_float2(kx[j].x, kx[j].y), a0);
+                a1 = __ffma2_rn(st[2 * j + 1], make_float2(kx[j].z, kx[j].w), a1);
             }
-            kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 4));
-            kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 2));
-            kv = __fadd_rn(kv, __shfl_xor_sync(0xffffffffu, kv, 1));
-            const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
-            float at = 0.0f;
+            float kv = (a0.x + a0.y) + (a1.x + a1.y);
+            kv += __shfl_xor_sync(0xffffffffu, kv, 4);
+            kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+            kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+            const float delta = (vv - kv * decay) * beta;
+            const float2 d2 = make_float2(decay, decay), dl2 = make_float2(delta, delta);
+            float2 b0 = make_float2(0.0f, 0.0f), b1 = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int e = 0; e < EPT; ++e) {
-                st[e] = __fadd_rn(st[e], __fmul_rn(kx[e], delta));
-                at = __fadd_rn(at, __fmul_rn(st[e], qx[e]));
+            for (int j = 0; j < 4; ++j) {
+                st[2 * j] = __ffma2_rn(make_float2(kx[j].x, kx[j].y), dl2, __fmul2_rn(st[2 * j], d2));
+                st[2 * j + 1] =
+                    __ffma2_rn(make_float2(kx[j].z, kx[j].w), dl2, __fmul2_rn(st[2 * j + 1], d2));
+                b0 = __ffma2_rn(st[2 * j], make_float2(qx[j].x, qx[j].y), b0);
+                b1 = __ffma2_rn(st[2 * j + 1], make_float2(qx[j].z, qx[j].w), b1);
             }
-            at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 4));
-            at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 2));
-            at = __fadd_rn(at, __shfl_xor_sync(0xffffffffu, at, 1));
+            float at = (b0.x + b0.y) + (b1.x + b1.y);
+            at += __shfl_xor_sync(0xffffffffu, at, 4);
+            at += __shfl_xor_sync(0xffffffffu, at, 2);
+            at += __shfl_xor_sync(0xffffffffu, at, 1);
             if (l == 0)
-                a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = __fmul_rn(at, a.scale);
+                a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = at * a.scale;
 
             const int slot = a.T - 1 - t;
             if ((a.slots > 1 && slot < a.slots) || (a.slots == 1 && t + 1 == a.T)) {
                 float *o = snap + (size_t)(a.slots == 1 ? 0 : slot) * slot_elems + snap_off;
 #pragma unroll
-                for (int e = 0; e < EPT; ++e)
-                    o[l + TPC * e] = st[e];
+                for (int j = 0; j < 4; ++j) {
+                    const int e = 4 * l + 32 * j;
+                    o[e] = st[2 * j].x;
+                    o[e + 1] = st[2 * j].y;
+                    o[e + 2] = st[2 * j + 1].x;
+                    o[e + 3] = st[2 * j + 1].y;
+                }
             }
         }
-        if constexpr (STAGED) {
-            __syncthreads(); // buffer buf is free again
-            stage(c + 2, buf);
-        }
+        __syncthreads(); // buffer buf is free again
+        stage(c + 2, buf);
     }
-    if constexpr (STAGED)
-        cp_async_wait<0>();
+    cp_async_wait<0>();
 }
 
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st) {
@@ -174,12 +249,14 @@ cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st) {
                        (uintptr_t)a.q_nb1 | (uintptr_t)a.q_nb2 | (uintptr_t)a.q_nb3 |
                        (uintptr_t)a.k_nb1 | (uintptr_t)a.k_nb2 | (uintptr_t)a.k_nb3) &
                       15) == 0;
+    // a few tokens (decode, speculative verify): the reference mirror's exact
+    // lane order; longer sequences: the staged, packed-FMA stream kernel
     if (a.T <= 8)
-        gdn_recurrent_kernel<S, CB, 4, false><<<grid, CB * 8, 0, st>>>(a);
+        gdn_recurrent_kernel<S, CB><<<grid, CB * 8, 0, st>>>(a);
     else if (v16)
-        gdn_recurrent_kernel<S, CB, 16, true><<<grid, CB * 8, 0, st>>>(a);
+        gdn_stream_kernel<S, CB, 16><<<grid, CB * 8, 0, st>>>(a);
     else
-        gdn_recurrent_kernel<S, CB, 4, true><<<grid, CB * 8, 0, st>>>(a);
+        gdn_stream_kernel<S, CB, 4><<<grid, CB * 8, 0, st>>>(a);
     return cudaGetLastError();
 }
 
