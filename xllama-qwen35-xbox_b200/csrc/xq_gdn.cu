@@ -102,9 +102,10 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
 // arithmetic reorganised for issue rate instead of the reference mirror's
 // lane order: lane l of a column owns key elements 4l + 32j + {0..3}
 // (j = 0..3, so each input vector arrives as four conflict-free 16-byte
-// shared loads), dot products are packed FP32x2 FMAs, and the decay is
-// applied to the reduced dot product (S k after the decay equals
-// decay * (S k)) and fused into the state update S = S * decay + k * delta.
+// shared loads), dot products are packed FP32x2 FMAs, the decay is applied
+// to the reduced dot product (S k after the decay equals decay * (S k)) and
+// fused into the state update S = S * decay + k * delta, and a token's output
+// dot (q_t . S_t) and the next token's (k_{t+1} . S_t) share one shuffle tree.
 // Results agree with the sequential reference to float rounding, not bit for
 // bit.
 template <int S, int CB, int VW>
@@ -184,41 +185,54 @@ __global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
         if (tid < nt)
             d_s[buf][tid] = (float)exp((double)g_s[buf][tid]);
         __syncthreads();
-        for (int r = 0; r < nt; ++r) {
+        // software pipeline over the chunk: the dot products of token r's
+        // updated state with q_r (its output) and with k_{r+1} (the next
+        // token's delta) share one interleaved shuffle tree
+        auto dot = [&](const float4 (&x)[4]) {
+            float2 p0 = make_float2(0.0f, 0.0f), p1 = make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                p0 = __ffma2_rn(st[2 * j], make_float2(x[j].x, x[j].y), p0);
+                p1 = __ffma2_rn(st[2 * j + 1], make_float2(x[j].z, x[j].w), p1);
+            }
+            return (p0.x + p0.y) + (p1.x + p1.y);
+        };
+        auto load = [&](float4 (&x)[4], const float (*rows)[S], int r) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                x[j] = *reinterpret_cast<const float4 *>(&rows[r][4 * l + 32 * j]);
+        };
+        float4 kcur[4];
+        load(kcur, k_s[buf], 0);
+        float kvp = dot(kcur); // S_{t0-1} . k_{t0}, reduced below
+        kvp += __shfl_xor_sync(0xffffffffu, kvp, 4);
+        kvp += __shfl_xor_sync(0xffffffffu, kvp, 2);
+        kvp += __shfl_xor_sync(0xffffffffu, kvp, 1);
+        auto step = [&](int r) {
             const int t = t0 + r;
-            float4 kx[4], qx[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                kx[j] = *reinterpret_cast<const float4 *>(&k_s[buf][r][4 * l + 32 * j]);
-                qx[j] = *reinterpret_cast<const float4 *>(&q_s[buf][r][4 * l + 32 * j]);
-            }
+            float4 qx[4], knext[4];
+            load(qx, q_s[buf], r);
+            load(knext, k_s[buf], r + 1 < nt ? r + 1 : r);
             const float vv = v_s[buf][r][cc], beta = b_s[buf][r], decay = d_s[buf][r];
-            // (S k) before the decay, two independent packed accumulators
-            float2 a0 = make_float2(0.0f, 0.0f), a1 = make_float2(0.0f, 0.0f);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                a0 = __ffma2_rn(st[2 * j], make_float2(kx[j].x, kx[j].y), a0);
-                a1 = __ffma2_rn(st[2 * j + 1], make_float2(kx[j].z, kx[j].w), a1);
-            }
-            float kv = (a0.x + a0.y) + (a1.x + a1.y);
-            kv += __shfl_xor_sync(0xffffffffu, kv, 4);
-            kv += __shfl_xor_sync(0xffffffffu, kv, 2);
-            kv += __shfl_xor_sync(0xffffffffu, kv, 1);
-            const float delta = (vv - kv * decay) * beta;
+            const float delta = (vv - kvp * decay) * beta;
             const float2 d2 = make_float2(decay, decay), dl2 = make_float2(delta, delta);
-            float2 b0 = make_float2(0.0f, 0.0f), b1 = make_float2(0.0f, 0.0f);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                st[2 * j] = __ffma2_rn(make_float2(kx[j].x, kx[j].y), dl2, __fmul2_rn(st[2 * j], d2));
-                st[2 * j + 1] =
-                    __ffma2_rn(make_float2(kx[j].z, kx[j].w), dl2, __fmul2_rn(st[2 * j + 1], d2));
-                b0 = __ffma2_rn(st[2 * j], make_float2(qx[j].x, qx[j].y), b0);
-                b1 = __ffma2_rn(st[2 * j + 1], make_float2(qx[j].z, qx[j].w), b1);
+                st[2 * j] = __ffma2_rn(make_float2(kcur[j].x, kcur[j].y), dl2,
+                                       __fmul2_rn(st[2 * j], d2));
+                st[2 * j + 1] = __ffma2_rn(make_float2(kcur[j].z, kcur[j].w), dl2,
+                                           __fmul2_rn(st[2 * j + 1], d2));
             }
-            float at = (b0.x + b0.y) + (b1.x + b1.y);
-            at += __shfl_xor_sync(0xffffffffu, at, 4);
-            at += __shfl_xor_sync(0xffffffffu, at, 2);
-            at += __shfl_xor_sync(0xffffffffu, at, 1);
+            float at = dot(qx), kn = dot(knext);
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) {
+                at += __shfl_xor_sync(0xffffffffu, at, o);
+                kn += __shfl_xor_sync(0xffffffffu, kn, o);
+            }
+            kvp = kn;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                kcur[j] = knext[j];
             if (l == 0)
                 a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = at * a.scale;
 
@@ -234,6 +248,14 @@ __global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
                     o[e + 3] = st[2 * j + 1].y;
                 }
             }
+        };
+        if (nt == TC) {
+#pragma unroll
+            for (int r = 0; r < TC; ++r)
+                step(r);
+        } else {
+            for (int r = 0; r < nt; ++r)
+                step(r);
         }
         __syncthreads(); // buffer buf is free again
         stage(c + 2, buf);
