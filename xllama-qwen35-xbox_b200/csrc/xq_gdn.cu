@@ -100,18 +100,19 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
 // Long sequences (T > 8): the same recurrence, the token inputs staged through
 // shared memory 16 tokens at a time (double-buffered cp.async), and the
 // arithmetic reorganised for issue rate instead of the reference mirror's
-// lane order: lane l of a column owns key elements 4l + 32j + {0..3}
-// (j = 0..3, so each input vector arrives as four conflict-free 16-byte
-// shared loads), dot products are packed FP32x2 FMAs, the decay is applied
+// lane order: lane l of a column's TPC lanes owns key elements
+// 4l + 4 TPC j + {0..3} (so each input vector arrives as conflict-free
+// 16-byte shared loads), dot products are packed FP32x2 FMAs, the decay is applied
 // to the reduced dot product (S k after the decay equals decay * (S k)) and
 // fused into the state update S = S * decay + k * delta, and a token's output
 // dot (q_t . S_t) and the next token's (k_{t+1} . S_t) share one shuffle tree.
 // Results agree with the sequential reference to float rounding, not bit for
 // bit.
-template <int S, int CB, int VW>
-__global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
-    constexpr int TPC = 8;      // lanes per column
+template <int S, int CB, int VW, int TPC>
+__global__ void __launch_bounds__(CB * TPC) gdn_stream_kernel(const GdnArgs a) {
     constexpr int NT = CB * TPC;
+    constexpr int J = S / (4 * TPC); // float4 groups of key elements per lane
+    static_assert(TPC == 8 || TPC == 16, "lanes per column");
     constexpr int TC = 16;      // tokens per staged chunk
     constexpr int PR = S * 4 / VW;
     static_assert(S == 128, "element ownership assumes 128-long rows");
@@ -126,14 +127,14 @@ __global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
     const int hk = h % a.H_k;
     const int sq = seq / a.rq3, sk = seq / a.rk3;
 
-    // state row `col`, elements 4l + 32j + x held as float2 pairs st[2j], st[2j+1]
+    // state row `col`, elements 4l + 4 TPC j + x held as float2 pairs st[2j], st[2j+1]
     const float *st_row = reinterpret_cast<const float *>(
         reinterpret_cast<const char *>(a.state) + seq * a.s_nb3 + (int64_t)h * a.s_nb2 +
         (int64_t)col * a.s_nb1);
-    float2 st[8];
+    float2 st[2 * J];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int e = 4 * l + 32 * j;
+    for (int j = 0; j < J; ++j) {
+        const int e = 4 * l + 4 * TPC * j;
         st[2 * j] = make_float2(st_row[e], st_row[e + 1]);
         st[2 * j + 1] = make_float2(st_row[e + 2], st_row[e + 3]);
     }
@@ -188,36 +189,36 @@ __global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
         // software pipeline over the chunk: the dot products of token r's
         // updated state with q_r (its output) and with k_{r+1} (the next
         // token's delta) share one interleaved shuffle tree
-        auto dot = [&](const float4 (&x)[4]) {
+        auto dot = [&](const float4 (&x)[J]) {
             float2 p0 = make_float2(0.0f, 0.0f), p1 = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < J; ++j) {
                 p0 = __ffma2_rn(st[2 * j], make_float2(x[j].x, x[j].y), p0);
                 p1 = __ffma2_rn(st[2 * j + 1], make_float2(x[j].z, x[j].w), p1);
             }
             return (p0.x + p0.y) + (p1.x + p1.y);
         };
-        auto load = [&](float4 (&x)[4], const float (*rows)[S], int r) {
+        auto load = [&](float4 (&x)[J], const float (*rows)[S], int r) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                x[j] = *reinterpret_cast<const float4 *>(&rows[r][4 * l + 32 * j]);
+            for (int j = 0; j < J; ++j)
+                x[j] = *reinterpret_cast<const float4 *>(&rows[r][4 * l + 4 * TPC * j]);
         };
-        float4 kcur[4];
+        float4 kcur[J];
         load(kcur, k_s[buf], 0);
         float kvp = dot(kcur); // S_{t0-1} . k_{t0}, reduced below
-        kvp += __shfl_xor_sync(0xffffffffu, kvp, 4);
-        kvp += __shfl_xor_sync(0xffffffffu, kvp, 2);
-        kvp += __shfl_xor_sync(0xffffffffu, kvp, 1);
+#pragma unroll
+        for (int o = TPC / 2; o > 0; o >>= 1)
+            kvp += __shfl_xor_sync(0xffffffffu, kvp, o);
         auto step = [&](int r) {
             const int t = t0 + r;
-            float4 qx[4], knext[4];
+            float4 qx[J], knext[J];
             load(qx, q_s[buf], r);
             load(knext, k_s[buf], r + 1 < nt ? r + 1 : r);
             const float vv = v_s[buf][r][cc], beta = b_s[buf][r], decay = d_s[buf][r];
             const float delta = (vv - kvp * decay) * beta;
             const float2 d2 = make_float2(decay, decay), dl2 = make_float2(delta, delta);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < J; ++j) {
                 st[2 * j] = __ffma2_rn(make_float2(kcur[j].x, kcur[j].y), dl2,
                                        __fmul2_rn(st[2 * j], d2));
                 st[2 * j + 1] = __ffma2_rn(make_float2(kcur[j].z, kcur[j].w), dl2,
@@ -225,13 +226,13 @@ __global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
             }
             float at = dot(qx), kn = dot(knext);
 #pragma unroll
-            for (int o = 4; o > 0; o >>= 1) {
+            for (int o = TPC / 2; o > 0; o >>= 1) {
                 at += __shfl_xor_sync(0xffffffffu, at, o);
                 kn += __shfl_xor_sync(0xffffffffu, kn, o);
             }
             kvp = kn;
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < J; ++j)
                 kcur[j] = knext[j];
             if (l == 0)
                 a.dst[((size_t)(seq * a.T + t) * a.H + h) * S + col] = at * a.scale;
@@ -240,8 +241,8 @@ __global__ void __launch_bounds__(CB * 8) gdn_stream_kernel(const GdnArgs a) {
             if ((a.slots > 1 && slot < a.slots) || (a.slots == 1 && t + 1 == a.T)) {
                 float *o = snap + (size_t)(a.slots == 1 ? 0 : slot) * slot_elems + snap_off;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int e = 4 * l + 32 * j;
+                for (int j = 0; j < J; ++j) {
+                    const int e = 4 * l + 4 * TPC * j;
                     o[e] = st[2 * j].x;
                     o[e + 1] = st[2 * j].y;
                     o[e + 2] = st[2 * j + 1].x;
@@ -275,10 +276,16 @@ cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st) {
     // lane order; longer sequences: the staged, packed-FMA stream kernel
     if (a.T <= 8)
         gdn_recurrent_kernel<S, CB><<<grid, CB * 8, 0, st>>>(a);
-    else if (v16)
-        gdn_stream_kernel<S, CB, 16><<<grid, CB * 8, 0, st>>>(a);
-    else
-        gdn_stream_kernel<S, CB, 4><<<grid, CB * 8, 0, st>>>(a);
+    else {
+        // 8 lanes per value column, 16 columns per CTA (16 lanes per column
+        // measured slower: the extra shuffle level outweighs the extra warps)
+        constexpr int SC = 16, TPC = 8;
+        dim3 sgrid((unsigned)(a.H * a.n_seq), S / SC);
+        if (v16)
+            gdn_stream_kernel<S, SC, 16, TPC><<<sgrid, SC * TPC, 0, st>>>(a);
+        else
+            gdn_stream_kernel<S, SC, 4, TPC><<<sgrid, SC * TPC, 0, st>>>(a);
+    }
     return cudaGetLastError();
 }
 
