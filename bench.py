@@ -26,7 +26,8 @@ stated distributions -- no datasets are involved):
 A step = the attention kernels of one decode step over that workload.
 `value` is KV GB/s (algorithmic bytes: K + V + q + out per step) with inputs
 resident; `e2e` is the same metric through the public call xq.flash_attn_ext
-with q copied host->device (pinned) and the output read back every step.
+with q and the output in pinned host memory (q copied to the GPU by the
+library's staging kernel, the result written back over PCIe) every step.
 --impl reference times the reference's CPU algorithm (the ggml-cpu
 restatement in oracle/, all host threads) on the same workload.
 """
@@ -279,13 +280,13 @@ def run_ours(args, rank, world, torch, dist):
     o_host = torch.empty((n_seq, 1, H, D), dtype=torch.float32, pin_memory=True)
     q_dev = torch.empty_like(qs[0])
     if workload != "c5":
-        o_dev = torch.empty((n_seq, 1, H, D), dtype=torch.float32, device=dev)
 
         def e2e_step(i):
+            # q and the output stay in pinned host memory: the library copies q
+            # to the GPU with its staging kernel and writes the result back over
+            # PCIe every step
             k, v = sets[i % len(sets)]
-            q_dev.copy_(q_host, non_blocking=True)
-            xq.flash_attn_ext(q_dev, k, v, ty, scale=scale, n_splits=n_splits, out=o_dev)
-            o_host.copy_(o_dev, non_blocking=True)
+            xq.flash_attn_ext(q_host, k, v, ty, scale=scale, n_splits=n_splits, out=o_host)
     else:
         def e2e_step(i):
             q_dev.copy_(q_host, non_blocking=True)

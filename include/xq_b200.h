@@ -76,7 +76,9 @@ typedef struct {
 /* DK in {64, 128, 256}.  Decode-shaped calls (n_q * n_head / n_head_kv <=   */
 /* 16) run the split-KV kernel; larger F16 calls run the tensor-core prefill */
 /* kernel.  Workspace: xq_flash_attn_ext_workspace() bytes, any contents;    */
-/* it may be NULL when that size is 0.                                       */
+/* it may be NULL when that size is 0.  q and dst may be pinned host memory:  */
+/* q is then copied to the workspace by a kernel of this library and dst is  */
+/* written in place; pageable host pointers return XQ_ERR_INVALID.           */
 /* ------------------------------------------------------------------------ */
 typedef struct {
     xq_tensor q, k, v, mask;

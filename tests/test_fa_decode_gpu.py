@@ -155,3 +155,26 @@ def test_unsupported_types_fail_loudly():
     k = torch.zeros((1, 64, 4, 192), dtype=torch.uint8, device="cuda")
     with pytest.raises(xq.XqError):
         xq.flash_attn_ext(q, k, k, oracle.F16)
+
+
+@pytest.mark.parametrize("ty,D,H,Hkv,n_kv,n_q", [(oracle.Q8_0, 256, 16, 2, 32768, 1),
+                                                  (oracle.F16, 128, 16, 4, 4096, 1),
+                                                  (oracle.Q4_0, 256, 24, 4, 3000, 3)])
+def test_pinned_host_q_and_out(ty, D, H, Hkv, n_kv, n_q):
+    """q and the output may live in pinned host memory: the library copies q
+    to the GPU with a kernel and writes the result in place; the output is
+    the same as with device buffers."""
+    xq = _xq()
+    rng = np.random.default_rng(77)
+    qn = rng.normal(0, 1, (1, H, n_q, D)).astype(np.float32)
+    k = torch.from_numpy(oracle.quantize(ty, rng.normal(0, 1, (1, n_kv, Hkv, D)).astype(np.float32))).cuda()
+    v = torch.from_numpy(oracle.quantize(ty, rng.normal(0, 1, (1, n_kv, Hkv, D)).astype(np.float32))).cuda()
+    want = xq.flash_attn_ext(torch.from_numpy(qn).cuda(), k, v, ty, scale=D ** -0.5).cpu()
+    q_host = torch.from_numpy(qn).pin_memory()
+    out_host = torch.full((1, n_q, H, D), float("nan"), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        xq.flash_attn_ext(q_host, k, v, ty, scale=D ** -0.5, out=out_host)
+        torch.cuda.synchronize()
+        assert torch.equal(out_host, want)
+    with pytest.raises(Exception):
+        xq.flash_attn_ext(torch.from_numpy(qn), k, v, ty, scale=D ** -0.5)  # pageable q

@@ -219,6 +219,57 @@ void plan_splits(FaPlan *pl, int64_t requested) {
     pl->n_splits = n_kv == 0 ? 1 : (n_kv + rows - 1) / rows;
 }
 
+// Where a caller's pointer lives: 0 device (or managed) memory, 1 pinned host
+// memory (dev = its device-side address), -1 pageable host memory.
+struct HostView {
+    void *dev;
+};
+int host_view(const void *ptr, HostView *v) {
+    v->dev = const_cast<void *>(ptr);
+    if (!ptr)
+        return 0;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+        cudaGetLastError(); // clear: treated as unknown (device) memory
+        return 0;
+    }
+    if (at.type == cudaMemoryTypeHost) {
+        v->dev = at.devicePointer;
+        return v->dev ? 1 : -1;
+    }
+    return at.type == cudaMemoryTypeUnregistered ? -1 : 0;
+}
+
+size_t q_stage_bytes(const xq_tensor &q) {
+    return (size_t)q.ne[0] * q.ne[1] * q.ne[2] * q.ne[3] * sizeof(float);
+}
+
+// Strided F32 [ne0, ne1, ne2, ne3] (ggml view, any byte strides) -> contiguous.
+__global__ void stage_rows_kernel(const uint8_t *__restrict__ src, int64_t nb1, int64_t nb2,
+                                  int64_t nb3, int64_t ne0, int64_t ne1, int64_t ne2,
+                                  int64_t n_rows, float *__restrict__ dst) {
+    const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+    if (row >= n_rows)
+        return;
+    const int64_t i1 = row % ne1, i2 = (row / ne1) % ne2, i3 = row / (ne1 * ne2);
+    const float *s = reinterpret_cast<const float *>(src + i1 * nb1 + i2 * nb2 + i3 * nb3);
+    for (int64_t i = threadIdx.x % 32; i < ne0; i += 32)
+        dst[row * ne0 + i] = s[i];
+}
+
+int stage_q(const xq_tensor &q, const void *src, float *dst, cudaStream_t st) {
+    if (q.type != XQ_TYPE_F32 || q.nb[0] != 4)
+        return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: q must be F32 with contiguous rows");
+    const int64_t n_rows = q.ne[1] * q.ne[2] * q.ne[3];
+    if (n_rows <= 0)
+        return XQ_OK;
+    const unsigned blocks = (unsigned)((n_rows + 7) / 8);
+    stage_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t *>(src), q.nb[1],
+                                              q.nb[2], q.nb[3], q.ne[0], q.ne[1], q.ne[2],
+                                              n_rows, dst);
+    return cuda_status(cudaGetLastError(), "flash_attn_ext: staging q");
+}
+
 } // namespace
 
 extern "C" {
@@ -247,7 +298,8 @@ uint32_t xq_split_k(uint32_t active, uint32_t mode) {
     return k < 1 ? 1 : k;
 }
 
-size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
+// Workspace of the kernels themselves (device-resident q).
+static size_t fa_main_workspace(const xq_fa_params *p) {
     FaPlan pl;
     if (fa_prepare(p, &pl) != XQ_OK)
         return 0;
@@ -260,7 +312,15 @@ size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
     return (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * sizeof(float);
 }
 
-int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t stream) {
+size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
+    const size_t main = fa_main_workspace(p);
+    HostView hq;
+    if (!p || host_view(p->q.data, &hq) != 1)
+        return main;
+    return (main + 255) / 256 * 256 + q_stage_bytes(p->q);
+}
+
+static int fa_run(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t stream) {
     FaPlan pl;
     int rc = fa_prepare(p, &pl);
     if (rc)
@@ -297,6 +357,41 @@ int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_strea
     return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p->dst,
                                         nullptr, p->sinks, pl.a.n_head, st),
                        "flash_attn_ext merge");
+}
+
+int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t stream) {
+    if (!p)
+        return fail(XQ_ERR_INVALID, "flash_attn_ext: null params");
+    HostView hq, hd;
+    const int kq = host_view(p->q.data, &hq), kd = host_view(p->dst, &hd);
+    if (kq < 0 || kd < 0)
+        return fail(XQ_ERR_INVALID,
+                    "flash_attn_ext: q / dst in pageable host memory (pin it or use the device)");
+    if (kq == 0 && kd == 0)
+        return fa_run(p, ws, ws_bytes, stream);
+    // pinned host q: copied into the tail of the workspace by a kernel, then
+    // read from there; pinned host dst: written in place by the kernels
+    xq_fa_params p2 = *p;
+    if (kd == 1)
+        p2.dst = static_cast<float *>(hd.dev);
+    size_t main = fa_main_workspace(&p2);
+    if (kq == 1) {
+        const size_t off = (main + 255) / 256 * 256, need = off + q_stage_bytes(p->q);
+        if (!ws || ws_bytes < need)
+            return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes,
+                        need);
+        float *staged = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + off);
+        const int rc = stage_q(p->q, hq.dev, staged, reinterpret_cast<cudaStream_t>(stream));
+        if (rc)
+            return rc;
+        p2.q.data = staged;
+        p2.q.nb[0] = 4;
+        p2.q.nb[1] = 4 * p->q.ne[0];
+        p2.q.nb[2] = p2.q.nb[1] * p->q.ne[1];
+        p2.q.nb[3] = p2.q.nb[2] * p->q.ne[2];
+        ws_bytes = off;
+    }
+    return fa_run(&p2, ws, ws_bytes, stream);
 }
 
 int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_begin,

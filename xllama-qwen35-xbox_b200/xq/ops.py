@@ -30,7 +30,7 @@ def _stream(stream):
 
 def _dense(t: torch.Tensor) -> Tensor:
     """float32 / float16 torch tensor (<= 4 dims) -> ggml view."""
-    assert t.is_cuda, "device tensor expected"
+    assert t.is_cuda or t.is_pinned(), "device or pinned host tensor expected"
     ty = {torch.float32: F32, torch.float16: F16}[t.dtype]
     shape = [1] * (4 - t.dim()) + list(t.shape)
     strides = [0] * (4 - t.dim()) + list(t.stride())
@@ -64,6 +64,8 @@ def _kv(raw: torch.Tensor, ggml_type: int, D: int) -> Tensor:
 def _workspace(nbytes: int, device) -> torch.Tensor | None:
     if nbytes == 0:
         return None
+    if device.type != "cuda":  # host (pinned) inputs: the workspace is on the GPU
+        device = torch.device("cuda", torch.cuda.current_device())
     key = (device.index if device.index is not None else torch.cuda.current_device())
     buf = _ws_cache.get(key)
     if buf is None or buf.numel() < nbytes:
@@ -95,11 +97,13 @@ def flash_attn_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_type: in
                    stream=None) -> torch.Tensor:
     """GGML_OP_FLASH_ATTN_EXT.  q float32 (n_seq, n_head, n_q, D); k/v raw
     uint8 caches (n_seq_kv, n_kv, n_head_kv, row_bytes); mask float16
-    (m3, m2, >=n_q, n_kv) or None.  Returns float32 (n_seq, n_q, n_head, D)."""
+    (m3, m2, >=n_q, n_kv) or None.  Returns float32 (n_seq, n_q, n_head, D).
+    q and `out` may be pinned host tensors: q is then copied to the GPU by a
+    kernel of the library and the result written straight into `out`."""
     v_type = k_type if v_type is None else v_type
     n_seq, n_head, n_q, D = q.shape
     dst = out if out is not None else torch.empty((n_seq, n_q, n_head, D), dtype=torch.float32,
-                                                  device=q.device)
+                                                  device=q.device, pin_memory=not q.is_cuda)
     p = _fa_params(q, k, v, k_type, v_type, mask, sinks, dst, scale, max_bias, softcap, n_splits)
     L = lib()
     nbytes = L.xq_flash_attn_ext_workspace(C.byref(p))
