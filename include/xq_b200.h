@@ -30,6 +30,11 @@
  *   xq_dequantize_rows    ggml to_float for F16/Q8_0/Q4_0 (ggml-quants.c)
  *   xq_quantize_rows      ggml from_float reference quantizers (the KV-cache
  *                         write path, shaders/rkva/rkva_store_f16.hlsl)
+ *   xq_set_rows           GGML_OP_SET_ROWS, the KV-cache write node
+ *                         (ggml-cpu dispatch: ggml-cpu.c:1957-1959 of the
+ *                         snapshot under bench/results/diag-ubatch-20261007;
+ *                         node `cache_k_l1 (view)` in
+ *                         docs/training-architecture.md:278-282)
  */
 #ifndef XQ_B200_H
 #define XQ_B200_H
@@ -52,7 +57,14 @@ enum xq_status {
 };
 
 /* ggml type ids (ggml.h enum ggml_type values, stable across versions). */
-enum xq_type { XQ_TYPE_F32 = 0, XQ_TYPE_F16 = 1, XQ_TYPE_Q4_0 = 2, XQ_TYPE_Q8_0 = 8 };
+enum xq_type {
+    XQ_TYPE_F32 = 0,
+    XQ_TYPE_F16 = 1,
+    XQ_TYPE_Q4_0 = 2,
+    XQ_TYPE_Q8_0 = 8,
+    XQ_TYPE_I32 = 26, /* row indices (SET_ROWS) */
+    XQ_TYPE_I64 = 27
+};
 
 /* A ggml tensor view: ne = elements per dim, nb = byte strides. */
 typedef struct {
@@ -160,6 +172,19 @@ uint32_t xq_split_k(uint32_t active, uint32_t mode);
 int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
                        const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
                        float *dst, int32_t slots, xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* GGML_OP_SET_ROWS (quantize-on-append into the KV cache).  src F32         */
+/* [ne0, ne1, ne2, ne3] with contiguous rows; idx I32 or I64 [ne1, i1, i2]   */
+/* (ne2 % i1 == 0, ne3 % i2 == 0); dst F32/F16/Q8_0/Q4_0 [ne0, rows, ne2,    */
+/* ne3] (ne0 % 32 == 0 for Q8_0/Q4_0).  Row (r, j, k) of src is written,     */
+/* converted by ggml's reference quantizer (bit-exact with                   */
+/* quantize_row_q8_0_ref / q4_0_ref and fp32->fp16 round-to-nearest-even),   */
+/* to row idx[r, j % i1, k % i2] of dst plane (j, k).  An index outside      */
+/* [0, rows) skips its row (ggml-cpu asserts instead).                        */
+/* ------------------------------------------------------------------------ */
+int xq_set_rows(const xq_tensor *src, const xq_tensor *idx, const xq_tensor *dst,
+                xq_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Block codecs.  n_per_row multiple of 32 for Q8_0/Q4_0.  Rows at byte      */

@@ -258,6 +258,28 @@ def lse_merge(partials: np.ndarray):
     return out, lse
 
 
+def set_rows(cache: np.ndarray, src: np.ndarray, idx: np.ndarray, ty: int) -> np.ndarray:
+    """ggml GGML_OP_SET_ROWS restated (ggml-cpu.c:1957-1959 dispatches it to
+    ggml_compute_forward_set_rows, one task): row t of src plane (s, h) is
+    converted by the destination type's from_float and stored as row
+    idx[s % i2, h % i1, t] of cache plane (s, h).  The converters are this
+    oracle's reference quantizers (gguf-pinned).  cache: (n_seq, n_rows,
+    n_head_kv, row_bytes) uint8, or float32 (.., D) for F32; src float32
+    (n_seq, n_tok, n_head_kv, D); idx (n_tok,) or (i2, i1, n_tok).  Returns
+    the updated copy; rows with an index outside [0, n_rows) are skipped."""
+    out = cache.copy()
+    n_seq, n_tok, n_hkv, _ = src.shape
+    ix = idx.reshape(1, 1, -1) if idx.ndim == 1 else idx
+    rows = src.astype(np.float32) if ty == F32 else quantize(ty, np.ascontiguousarray(src))
+    for s_ in range(n_seq):
+        for h in range(n_hkv):
+            for t in range(n_tok):
+                r = int(ix[s_ % ix.shape[0], h % ix.shape[1], t])
+                if 0 <= r < cache.shape[1]:
+                    out[s_, r, h] = rows[s_, t, h]
+    return out
+
+
 # ----------------------------------------------------------------------------
 # GATED_DELTA_NET
 

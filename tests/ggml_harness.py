@@ -14,8 +14,8 @@ BACKEND_LIB = os.path.join(PKG, "lib", "libxq_ggml_b200.so")
 
 # placeholder op ids of ggml_abi_mirror.h
 OP_NONE, OP_RESHAPE, OP_VIEW, OP_PERMUTE, OP_TRANSPOSE = 0, 36, 37, 38, 39
-OP_FLASH_ATTN_EXT, OP_GATED_DELTA_NET, OP_MUL_MAT = 72, 84, 29
-F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
+OP_FLASH_ATTN_EXT, OP_GATED_DELTA_NET, OP_MUL_MAT, OP_SET_ROWS = 72, 84, 29, 41
+F32, F16, Q4_0, Q8_0, I32, I64 = 0, 1, 2, 8, 26, 27
 FLAG_COMPUTE = 16
 
 
@@ -61,7 +61,7 @@ def libs():
     return _libs
 
 
-BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_0: (32, 18)}
+BLOCK = {F32: (1, 4), F16: (1, 2), Q8_0: (32, 34), Q4_0: (32, 18), I32: (1, 4), I64: (1, 8)}
 
 
 def tensor(ty, ne, nb=None, data=None, op=OP_NONE, srcs=(), op_params=()):
@@ -96,6 +96,14 @@ def fa_node(q, k, v, mask=None, sinks=None, scale=1.0, max_bias=0.0, softcap=0.0
     out = tensor(F32, (D, H, n_q, S), data=dst_data, op=OP_FLASH_ATTN_EXT,
                  srcs=(q, k, v, mask, sinks),
                  op_params=(f32_bits(scale), f32_bits(max_bias), f32_bits(softcap)))
+    out.flags = FLAG_COMPUTE
+    return out
+
+
+def set_rows_node(cache, rows, idx):
+    """ggml_set_rows(cache, rows, idx): a view of `cache` whose op writes rows."""
+    out = tensor(cache.type, tuple(cache.ne), nb=tuple(cache.nb), data=cache.data,
+                 op=OP_SET_ROWS, srcs=(rows, idx))
     out.flags = FLAG_COMPUTE
     return out
 

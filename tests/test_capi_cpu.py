@@ -65,3 +65,18 @@ def test_contract_errors_before_launch():
     assert L.xq_lse_merge(None, 1, 1, 256, None, None, None) == XL.XQ_ERR_INVALID
     t = XL.Tensor()
     assert L.xq_gated_delta_net(*[C.byref(t)] * 6, None, 1, None) == XL.XQ_ERR_INVALID
+    # SET_ROWS: ggml_set_rows' shape rules and types, checked before any launch
+    src, idx, dst = XL.Tensor(), XL.Tensor(), XL.Tensor()
+    src.type, src.nb[0], idx.type, dst.type = XL.F32, 4, XL.I64, XL.Q8_0
+    for t_, ne in ((src, (256, 5, 2, 1)), (idx, (5, 1, 1, 1)), (dst, (256, 64, 2, 1))):
+        t_.data = 0x1000
+        for i in range(4):
+            t_.ne[i] = ne[i]
+    dst.ne[0] = 128  # row lengths differ
+    assert L.xq_set_rows(C.byref(src), C.byref(idx), C.byref(dst), None) == XL.XQ_ERR_INVALID
+    assert b"set_rows" in L.xq_last_error()
+    dst.ne[0] = 256
+    idx.type = XL.F32  # float indices
+    assert L.xq_set_rows(C.byref(src), C.byref(idx), C.byref(dst), None) == XL.XQ_ERR_UNSUPPORTED
+    idx.type, idx.ne[1] = XL.I32, 3  # 2 heads not a multiple of 3
+    assert L.xq_set_rows(C.byref(src), C.byref(idx), C.byref(dst), None) == XL.XQ_ERR_INVALID

@@ -5,7 +5,7 @@ Mirrors how the reference gates its D3D12 GATED_DELTA_NET
 FLASH_ATTN_EXT to what the kernels take; everything else is refused so the
 scheduler leaves it on its current backend."""
 import ggml_harness as gh
-from ggml_harness import F16, F32, Q4_0, Q8_0, tensor
+from ggml_harness import F16, F32, I32, I64, Q4_0, Q8_0, tensor
 
 
 def fa(D=256, H=16, Hkv=2, n_kv=4096, n_q=1, S=1, kt=Q8_0, vt=None, mask=False, mt=F16,
@@ -58,6 +58,24 @@ def test_gdn_claims_and_refusals():
     assert not supported(gdn(g_dim=128))             # per-dim gates
     assert not supported(gdn(slots=0))
     assert not supported(gdn(H=24, Hk=16))           # H % H_k
+
+
+def set_rows(ct=Q8_0, D=256, rows=4096, Hkv=2, n_tok=1, it=I64, i1=1, st=F32):
+    cache = tensor(ct, (D, rows, Hkv, 1))
+    src = tensor(st, (D, n_tok, Hkv, 1))
+    idx = tensor(it, (n_tok, i1, 1, 1))
+    return gh.set_rows_node(cache, src, idx)
+
+
+def test_set_rows_claims_and_refusals():
+    for ct in (F32, F16, Q8_0, Q4_0):
+        assert supported(set_rows(ct=ct))              # KV-cache append
+    assert supported(set_rows(n_tok=512, it=I32, i1=2))  # prefill, per-head indices
+    assert supported(set_rows(D=512, Hkv=1))           # llama.cpp's 2D cache rows
+    assert not supported(set_rows(st=F16))             # rows must be F32
+    assert not supported(set_rows(it=F32))             # indices I32 / I64 only
+    assert not supported(set_rows(i1=3))               # heads % i1
+    assert not supported(set_rows(ct=Q8_0, D=80))      # whole 32-element blocks
 
 
 def test_view_ops_and_others():

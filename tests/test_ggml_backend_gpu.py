@@ -190,3 +190,26 @@ def test_unclaimed_node_fails_without_fallback():
         assert s.be.iface.graph_compute(s.bep, C.byref(gh.Graph(1, arr))) != 0
     finally:
         s.close()
+
+
+def test_set_rows_through_graph_compute():
+    """The KV-cache write node: F32 rows quantized into a Q8_0 cache view at
+    I64 indices, then read back bit-identical to the oracle."""
+    rng = np.random.default_rng(41)
+    s = Session(64 << 20)
+    try:
+        D, rows, Hkv, n_tok = 256, 512, 2, 7
+        ch = oracle.quantize(Q8_0, rng.normal(0, 1, (1, rows, Hkv, D)).astype(np.float32))
+        xh = rng.normal(0, 1, (1, n_tok, Hkv, D)).astype(np.float32)
+        ih = rng.choice(rows, n_tok, replace=False).astype(np.int64)
+        cache = s.place(tensor(Q8_0, (D, rows, Hkv, 1), nb=(34, Hkv * 272, 272, rows * Hkv * 272)),
+                        ch)
+        src = s.place(tensor(F32, (D, n_tok, Hkv, 1), nb=(4, Hkv * D * 4, D * 4, n_tok * Hkv * D * 4)),
+                      xh)
+        idx = s.place(tensor(gh.I64, (n_tok, 1, 1, 1)), ih)
+        node = gh.set_rows_node(cache, src, idx)
+        assert s.compute([node]) == 0
+        got = s.get(cache, ch.shape, np.uint8)
+        assert np.array_equal(got, oracle.set_rows(ch, xh, ih, Q8_0))
+    finally:
+        s.close()

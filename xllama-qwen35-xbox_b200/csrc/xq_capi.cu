@@ -598,6 +598,53 @@ int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *
 // ---------------------------------------------------------------------------
 // Codecs.
 
+int xq_set_rows(const xq_tensor *src, const xq_tensor *idx, const xq_tensor *dst,
+                xq_stream_t stream) {
+    if (!src || !idx || !dst)
+        return fail(XQ_ERR_INVALID, "set_rows: null tensor");
+    if (src->type != XQ_TYPE_F32 || src->nb[0] != 4)
+        return fail(XQ_ERR_UNSUPPORTED, "set_rows: src must be F32 with contiguous rows");
+    if (idx->type != XQ_TYPE_I32 && idx->type != XQ_TYPE_I64)
+        return fail(XQ_ERR_UNSUPPORTED, "set_rows: indices must be I32 or I64");
+    const int t = dst->type;
+    if (t != XQ_TYPE_F32 && t != XQ_TYPE_F16 && t != XQ_TYPE_Q8_0 && t != XQ_TYPE_Q4_0)
+        return fail(XQ_ERR_UNSUPPORTED, "set_rows: dst type %d (F32/F16/Q8_0/Q4_0)", t);
+    const int64_t ne0 = src->ne[0], ne1 = src->ne[1], ne2 = src->ne[2], ne3 = src->ne[3];
+    if (dst->ne[0] != ne0 || dst->ne[2] != ne2 || dst->ne[3] != ne3 || idx->ne[0] != ne1 ||
+        idx->ne[1] <= 0 || idx->ne[2] <= 0 || ne2 % idx->ne[1] || ne3 % idx->ne[2] ||
+        idx->ne[3] != 1 || ne0 <= 0)
+        return fail(XQ_ERR_INVALID, "set_rows: shapes (ggml_set_rows rules)");
+    if ((t == XQ_TYPE_Q8_0 || t == XQ_TYPE_Q4_0) && ne0 % 32)
+        return fail(XQ_ERR_INVALID, "set_rows: row length %lld not a multiple of 32",
+                    (long long)ne0);
+    if (!src->data || !idx->data || !dst->data)
+        return fail(XQ_ERR_INVALID, "set_rows: null data");
+    xq::SetRowsArgs a;
+    a.src = static_cast<const uint8_t *>(src->data);
+    a.s_nb1 = src->nb[1];
+    a.s_nb2 = src->nb[2];
+    a.s_nb3 = src->nb[3];
+    a.idx = static_cast<const uint8_t *>(idx->data);
+    a.i_nb0 = idx->nb[0];
+    a.i_nb1 = idx->nb[1];
+    a.i_nb2 = idx->nb[2];
+    a.i_ne1 = idx->ne[1];
+    a.i_ne2 = idx->ne[2];
+    a.idx_i64 = idx->type == XQ_TYPE_I64;
+    a.dst = static_cast<uint8_t *>(const_cast<void *>(dst->data));
+    a.d_nb1 = dst->nb[1];
+    a.d_nb2 = dst->nb[2];
+    a.d_nb3 = dst->nb[3];
+    a.d_rows = dst->ne[1];
+    a.ne0 = ne0;
+    a.ne1 = ne1;
+    a.ne2 = ne2;
+    a.ne3 = ne3;
+    a.n_units = ne1 * ne2 * ne3 * ((t == XQ_TYPE_F32 || t == XQ_TYPE_F16) ? ne0 : ne0 / 32);
+    return cuda_status(xq::launch_set_rows(t, a, reinterpret_cast<cudaStream_t>(stream)),
+                       "set_rows");
+}
+
 int xq_dequantize_rows(int32_t type, const void *src, uint64_t src_row_stride, float *dst,
                        uint64_t dst_row_stride, int64_t n_rows, int64_t n_per_row,
                        xq_stream_t stream) {

@@ -320,17 +320,15 @@ __global__ void dequant_kernel(const uint8_t *__restrict__ src, uint64_t ss,
     }
 }
 
+// One output unit of the ggml reference quantizers for row x: element b (F32,
+// F16) or 32-element block b (Q8_0: quantize_row_q8_0_ref, Q4_0:
+// quantize_row_q4_0_ref) written to row y.
 template <int T>
-__global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t *__restrict__ dst,
-                             uint64_t ds, int64_t n_rows, int64_t n_per_row) {
-    const int64_t nb = T == kF16 ? n_per_row : n_per_row / 32;
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n_rows * nb)
-        return;
-    const int64_t r = i / nb, b = i - r * nb;
-    const float *x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(src) + r * ss);
-    uint8_t *y = dst + r * ds;
-    if constexpr (T == kF16) {
+__device__ __forceinline__ void quant_block(const float *__restrict__ x, uint8_t *__restrict__ y,
+                                            int64_t b) {
+    if constexpr (T == kF32) {
+        reinterpret_cast<float *>(y)[b] = x[b];
+    } else if constexpr (T == kF16) {
         reinterpret_cast<uint16_t *>(y)[b] = __half_as_ushort(__float2half_rn(x[b]));
     } else if constexpr (T == kQ8) {
         const float *xb = x + 32 * b;
@@ -362,6 +360,54 @@ __global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t
             blk[2 + j] = (uint8_t)(lo | (hi << 4));
         }
     }
+}
+
+template <int T>
+__global__ void quant_kernel(const float *__restrict__ src, uint64_t ss, uint8_t *__restrict__ dst,
+                             uint64_t ds, int64_t n_rows, int64_t n_per_row) {
+    const int64_t nb = T == kF16 ? n_per_row : n_per_row / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows * nb)
+        return;
+    const int64_t r = i / nb, b = i - r * nb;
+    const float *x = reinterpret_cast<const float *>(reinterpret_cast<const char *>(src) + r * ss);
+    quant_block<T>(x, dst + r * ds, b);
+}
+
+// ggml SET_ROWS (the KV-cache write): source row (i1, i2, i3) of F32 `src`
+// goes, converted by the reference quantizer of dst's type, to row
+// idx[i1, i2 % idx_ne1, i3 % idx_ne2] of dst (same i2, i3).  One thread per
+// output unit; rows whose index falls outside [0, dst_rows) are skipped.
+template <int T>
+__global__ void set_rows_kernel(const SetRowsArgs a) {
+    const int64_t nb = (T == kF16 || T == kF32) ? a.ne0 : a.ne0 / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.n_units)
+        return;
+    const int64_t row = i / nb, b = i - row * nb;
+    const int64_t i1 = row % a.ne1, i2 = (row / a.ne1) % a.ne2, i3 = row / (a.ne1 * a.ne2);
+    const uint8_t *ip = a.idx + i1 * a.i_nb0 + (i2 % a.i_ne1) * a.i_nb1 + (i3 % a.i_ne2) * a.i_nb2;
+    const int64_t dr = a.idx_i64 ? *reinterpret_cast<const int64_t *>(ip)
+                                 : (int64_t)*reinterpret_cast<const int32_t *>(ip);
+    if (dr < 0 || dr >= a.d_rows)
+        return;
+    const float *x = reinterpret_cast<const float *>(a.src + i1 * a.s_nb1 + i2 * a.s_nb2 +
+                                                     i3 * a.s_nb3);
+    quant_block<T>(x, a.dst + dr * a.d_nb1 + i2 * a.d_nb2 + i3 * a.d_nb3, b);
+}
+
+cudaError_t launch_set_rows(int type, const SetRowsArgs &a, cudaStream_t st) {
+    if (a.n_units <= 0)
+        return cudaSuccess;
+    const unsigned blocks = (unsigned)((a.n_units + 255) / 256);
+    switch (type) {
+    case kF32: set_rows_kernel<kF32><<<blocks, 256, 0, st>>>(a); break;
+    case kF16: set_rows_kernel<kF16><<<blocks, 256, 0, st>>>(a); break;
+    case kQ8: set_rows_kernel<kQ8><<<blocks, 256, 0, st>>>(a); break;
+    case kQ4: set_rows_kernel<kQ4><<<blocks, 256, 0, st>>>(a); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
 }
 
 cudaError_t launch_dequant(int type, const void *src, uint64_t ss, float *dst, uint64_t ds,

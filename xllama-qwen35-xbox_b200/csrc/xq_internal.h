@@ -72,6 +72,19 @@ size_t prefill_map_bytes(const PrefillShape &ps);
 void *tensor_map_encoder();
 cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, const char **why);
 
+// ggml SET_ROWS: F32 rows -> rows of a F32/F16/Q8_0/Q4_0 tensor at I32/I64 indices.
+struct SetRowsArgs {
+    const uint8_t *src;             // F32 [ne0, ne1, ne2, ne3]
+    int64_t s_nb1, s_nb2, s_nb3;
+    const uint8_t *idx;             // I32/I64 [ne1, i_ne1, i_ne2]
+    int64_t i_nb0, i_nb1, i_nb2, i_ne1, i_ne2;
+    int idx_i64;
+    uint8_t *dst;                   // [ne0, d_rows, ne2, ne3]
+    int64_t d_nb1, d_nb2, d_nb3, d_rows;
+    int64_t ne0, ne1, ne2, ne3, n_units;
+};
+cudaError_t launch_set_rows(int type, const SetRowsArgs &a, cudaStream_t st);
+
 struct GdnArgs {
     const float *q, *k, *v, *g, *beta, *state;
     int64_t q_nb1, q_nb2, q_nb3, k_nb1, k_nb2, k_nb3, v_nb1, v_nb2, v_nb3;

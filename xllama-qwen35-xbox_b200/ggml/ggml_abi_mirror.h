@@ -25,7 +25,14 @@ extern "C" {
 #define GGML_MAX_NAME 64
 #define GGML_BACKEND_API_VERSION 2
 
-enum ggml_type { GGML_TYPE_F32 = 0, GGML_TYPE_F16 = 1, GGML_TYPE_Q4_0 = 2, GGML_TYPE_Q8_0 = 8 };
+enum ggml_type {
+    GGML_TYPE_F32 = 0,
+    GGML_TYPE_F16 = 1,
+    GGML_TYPE_Q4_0 = 2,
+    GGML_TYPE_Q8_0 = 8,
+    GGML_TYPE_I32 = 26,
+    GGML_TYPE_I64 = 27,
+};
 
 enum ggml_op {
     GGML_OP_NONE = 0,
@@ -33,6 +40,7 @@ enum ggml_op {
     GGML_OP_VIEW = 37,
     GGML_OP_PERMUTE = 38,
     GGML_OP_TRANSPOSE = 39,
+    GGML_OP_SET_ROWS = 41,
     GGML_OP_FLASH_ATTN_EXT = 72,
     GGML_OP_GATED_DELTA_NET = 84,
 };

@@ -3,9 +3,9 @@
 //
 // Same plugin surface as the reference's D3D12 backend
 // (src/bridge/ggml_d3d12.cpp): a registry (:2473-2478) with one device per
-// GPU, a device (:2427-2446) whose supports_op claims FLASH_ATTN_EXT and
+// GPU, a device (:2427-2446) whose supports_op claims FLASH_ATTN_EXT, SET_ROWS and
 // GATED_DELTA_NET, a device buffer type (:1516-1527) and buffer (:1371-1383),
-// and a backend (:2268-2285) whose graph_compute runs those two ops.  Unlike
+// and a backend (:2268-2285) whose graph_compute runs those three ops.  Unlike
 // the reference (whose graph_compute is synchronous, synchronize = nullptr)
 // work is queued on one CUDA stream per backend: set/get_tensor_async and
 // synchronize are implemented.  Nothing falls back to the CPU: an op the
@@ -123,6 +123,25 @@ bool gdn_supported(const ggml_tensor *op) {
     return op->type == GGML_TYPE_F32 && op->ne[0] == S * H &&
            op->ne[1] == T * NS + (int64_t)slots * S * NS && op->ne[2] == 1 && op->ne[3] == 1 &&
            op->nb[0] == 4 && op->nb[1] == 4 * (size_t)op->ne[0];
+}
+
+// SET_ROWS (the KV-cache write): node = view of the cache (F32/F16/Q8_0/Q4_0,
+// [ne0, rows, ne2, ne3]); src0 F32 rows [ne0, ne1, ne2, ne3]; src1 I32/I64
+// indices [ne1, i1, i2] with ne2 % i1 == ne3 % i2 == 0 (ggml_set_rows' rules).
+bool set_rows_supported(const ggml_tensor *op) {
+    const ggml_tensor *b = op->src[0], *c = op->src[1];
+    if (!b || !c || b->type != GGML_TYPE_F32 || b->nb[0] != 4)
+        return false;
+    if (c->type != GGML_TYPE_I32 && c->type != GGML_TYPE_I64)
+        return false;
+    const int t = op->type;
+    if (t != GGML_TYPE_F32 && t != GGML_TYPE_F16 && t != GGML_TYPE_Q8_0 && t != GGML_TYPE_Q4_0)
+        return false;
+    if (op->ne[0] != b->ne[0] || op->ne[2] != b->ne[2] || op->ne[3] != b->ne[3] ||
+        c->ne[0] != b->ne[1] || c->ne[1] <= 0 || c->ne[2] <= 0 || b->ne[2] % c->ne[1] ||
+        b->ne[3] % c->ne[2] || c->ne[3] != 1)
+        return false;
+    return (t != GGML_TYPE_Q8_0 && t != GGML_TYPE_Q4_0) || op->ne[0] % 32 == 0;
 }
 
 xq_tensor xt(const ggml_tensor *t) {
@@ -311,6 +330,15 @@ ggml_status run_gdn(BackendCtx *c, ggml_tensor *op) {
     return GGML_STATUS_SUCCESS;
 }
 
+ggml_status run_set_rows(BackendCtx *c, ggml_tensor *op) {
+    const xq_tensor src = xt(op->src[0]), idx = xt(op->src[1]), dst = xt(op);
+    if (xq_set_rows(&src, &idx, &dst, reinterpret_cast<xq_stream_t>(c->stream))) {
+        log_err("SET_ROWS", xq_last_error());
+        return GGML_STATUS_FAILED;
+    }
+    return GGML_STATUS_SUCCESS;
+}
+
 ggml_status be_graph_compute(ggml_backend_t b, ggml_cgraph *g) {
     auto *c = static_cast<BackendCtx *>(b->context);
     if (!ok_cuda(cudaSetDevice(c->device), "graph_compute"))
@@ -325,6 +353,8 @@ ggml_status be_graph_compute(ggml_backend_t b, ggml_cgraph *g) {
             st = run_fa(c, node);
         else if (node->op == GGML_OP_GATED_DELTA_NET && gdn_supported(node))
             st = run_gdn(c, node);
+        else if (node->op == GGML_OP_SET_ROWS && set_rows_supported(node))
+            st = run_set_rows(c, node);
         else {
             log_err("graph_compute", "node outside the supports_op contract");
             st = GGML_STATUS_FAILED;
@@ -471,6 +501,8 @@ bool ggml_xq_b200_supports_op(const ggml_tensor *op) {
         return fa_supported(op);
     if (op->op == GGML_OP_GATED_DELTA_NET)
         return gdn_supported(op);
+    if (op->op == GGML_OP_SET_ROWS)
+        return set_rows_supported(op);
     return false;
 }
 

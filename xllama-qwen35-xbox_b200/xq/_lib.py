@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(PKG_DIR, "lib", "libxq_b200.so")
 
 XQ_OK, XQ_ERR_INVALID, XQ_ERR_UNSUPPORTED, XQ_ERR_CUDA, XQ_ERR_WORKSPACE = range(5)
 F32, F16, Q4_0, Q8_0 = 0, 1, 2, 8
+I32, I64 = 26, 27
 
 # Every symbol include/xq_b200.h declares (checked by the CPU test suite).
 EXPORTS = (
@@ -20,7 +21,7 @@ EXPORTS = (
     "xq_lse_merge_records",
     "xq_attend_range_workspace", "xq_attend_range", "xq_split_k", "xq_gated_delta_net",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
-    "xq_flash_attn_ext_noalloc",
+    "xq_flash_attn_ext_noalloc", "xq_set_rows",
 )
 
 
@@ -69,6 +70,7 @@ def lib():
         "xq_dequantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_quantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_flash_attn_ext_noalloc": (C.c_int, [P(FaParams), vp]),
+        "xq_set_rows": (C.c_int, [P(Tensor), P(Tensor), P(Tensor), vp]),
         "xq_version": (C.c_char_p, []),
         "xq_last_error": (C.c_char_p, []),
     }

@@ -12,7 +12,7 @@ import ctypes as C
 
 import torch
 
-from ._lib import F16, F32, FaParams, Q4_0, Q8_0, Tensor, check, lib
+from ._lib import F16, F32, I32, I64, FaParams, Q4_0, Q8_0, Tensor, check, lib
 
 _BLOCK_BYTES = {F16: 2, Q8_0: 34, Q4_0: 18, F32: 4}
 _BLOCK_ELEMS = {F16: 1, Q8_0: 32, Q4_0: 32, F32: 1}
@@ -160,6 +160,43 @@ def lse_merge_records(partials: torch.Tensor, splits_per_group: int, out=None, s
     check(lib().xq_lse_merge_records(partials.data_ptr(), n_groups, splits_per_group, n_rows,
                                      d2 - 2, rec.data_ptr(), _stream(stream)))
     return rec
+
+
+def _rows_view(t: torch.Tensor, ggml_type: int, elems: int) -> Tensor:
+    """(n_seq, n_rows, n_head_kv, last) tensor -> ggml [elems, n_rows, n_head_kv, n_seq]
+    (the KV-cache view convention of _kv), rows contiguous."""
+    assert t.is_cuda and t.dim() == 4 and t.stride(3) == 1
+    es = t.element_size()
+    x = Tensor()
+    x.type, x.data = ggml_type, t.data_ptr()
+    x.ne[0], x.ne[1], x.ne[2], x.ne[3] = elems, t.shape[1], t.shape[2], t.shape[0]
+    x.nb[0] = _BLOCK_BYTES[ggml_type] if ggml_type in _BLOCK_BYTES else es
+    x.nb[1], x.nb[2], x.nb[3] = t.stride(1) * es, t.stride(2) * es, t.stride(0) * es
+    return x
+
+
+def set_rows(cache: torch.Tensor, src: torch.Tensor, idx: torch.Tensor, ggml_type: int,
+             stream=None) -> torch.Tensor:
+    """GGML_OP_SET_ROWS (the KV-cache write), in place.  cache: uint8 (n_seq,
+    n_rows, n_head_kv, row_bytes) for F16/Q8_0/Q4_0 or float32 (n_seq, n_rows,
+    n_head_kv, D) for F32; src float32 (n_seq, n_tok, n_head_kv, D); idx int32
+    or int64 (n_tok,) or (i2, i1, n_tok) with n_head_kv % i1 == 0 and
+    n_seq % i2 == 0.  Row (s, t, h) of src lands in cache row
+    idx[s % i2, h % i1, t] of (s, h)."""
+    D = src.shape[-1]
+    dst = _rows_view(cache, ggml_type, D)
+    s = _rows_view(src, F32, D)
+    ix = idx.reshape((1, 1) + tuple(idx.shape)) if idx.dim() == 1 else idx
+    assert ix.dim() == 3 and ix.is_cuda and ix.stride(2) == 1
+    it = Tensor()
+    it.type = {torch.int32: I32, torch.int64: I64}[ix.dtype]
+    it.data = ix.data_ptr()
+    es = ix.element_size()
+    it.ne[0], it.ne[1], it.ne[2], it.ne[3] = ix.shape[2], ix.shape[1], ix.shape[0], 1
+    it.nb[0], it.nb[1], it.nb[2] = es, ix.stride(1) * es, ix.stride(0) * es
+    it.nb[3] = it.nb[2] * ix.shape[0]
+    check(lib().xq_set_rows(C.byref(s), C.byref(it), C.byref(dst), _stream(stream)))
+    return cache
 
 
 def split_k(active: int, mode: int) -> int:
