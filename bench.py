@@ -2,7 +2,7 @@
 """Benchmark of the B200 attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c5]
+                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c5|kvw]
 
 Workloads (seeded synthetic tensors, random data of the
 stated distributions -- no datasets are involved):
@@ -17,6 +17,9 @@ stated distributions -- no datasets are involved):
   c3b  config 3 prefill: GATED_DELTA_NET, 1 sequence x 4096 tokens.
   c4   config 4: causal prefill, 8192 tokens, 24 Q / 4 KV heads, D=256, F16
        K/V, explicit causal F16 mask (tensor-core kernel); metric TFLOP/s.
+  kvw  KV-cache write (GGML_OP_SET_ROWS, the row after the hot path): a
+       prefill batch of 8192 tokens x 4 KV heads x D=256, K and V, quantized
+       to Q8_0 into 32768-row caches (4 rotated input sets > 2 x L2).
   c5   config 5: 8 sequences x 262144 KV rows, 24 Q / 4 KV heads, D=256, Q8_0;
        the KV rows are cut into 256 fixed global splits in 8 fixed groups; each
        GPU holds and reads its contiguous block of groups, merges each group
@@ -520,6 +523,112 @@ def run_prefill(args, torch):
     }
 
 
+KVW = dict(n_tok=8192, n_hkv=4, D=256, rows=32768)
+
+
+def kvw_bytes(w=KVW):
+    import xq
+    n = w["n_tok"] * w["n_hkv"]
+    return 2 * (n * w["D"] * 4 + n * xq.row_bytes(xq.Q8_0, w["D"]) + w["n_tok"] * 8)
+
+
+def run_kvw(args, torch):
+    import xq
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = KVW
+    hbm, _, peak_kind = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    n_sets = 4
+    srcs = [(torch.randn((1, w["n_tok"], w["n_hkv"], w["D"]), generator=g, device=dev),
+             torch.randn((1, w["n_tok"], w["n_hkv"], w["D"]), generator=g, device=dev))
+            for _ in range(n_sets)]
+    rb = xq.row_bytes(xq.Q8_0, w["D"])
+    kc = torch.zeros((1, w["rows"], w["n_hkv"], rb), dtype=torch.uint8, device=dev)
+    vc = torch.zeros_like(kc)
+    bases = [i * w["n_tok"] % w["rows"] for i in range(n_sets)]
+    idxs = [torch.arange(b, b + w["n_tok"], dtype=torch.int64, device=dev) for b in bases]
+
+    def step(i):
+        k, v = srcs[i % n_sets]
+        xq.set_rows(kc, k, idxs[i % n_sets], xq.Q8_0)
+        xq.set_rows(vc, v, idxs[i % n_sets], xq.Q8_0)
+
+    clk = ClockSampler(dev.index)
+    clk.start()
+    ms = graph_timed(torch, step, args.steps, args.warmup) / args.steps
+    clocks = clk.stop()
+    one_ms = graph_timed(torch, lambda i: xq.set_rows(kc, srcs[i % n_sets][0], idxs[i % n_sets],
+                                                      xq.Q8_0), args.steps, args.warmup) / args.steps
+    # end to end: the new rows from pinned host memory, the written rows read back
+    kh = srcs[0][0].cpu().pin_memory()
+    vh = srcs[0][1].cpu().pin_memory()
+    kback = torch.empty((1, w["n_tok"], w["n_hkv"], rb), dtype=torch.uint8, pin_memory=True)
+    vback = torch.empty(kback.shape, dtype=torch.uint8, pin_memory=True)
+    b0 = bases[0]
+
+    def e2e_step(i):
+        srcs[0][0].copy_(kh, non_blocking=True)
+        srcs[0][1].copy_(vh, non_blocking=True)
+        step(0)
+        kback.copy_(kc[:, b0:b0 + w["n_tok"]], non_blocking=True)
+        vback.copy_(vc[:, b0:b0 + w["n_tok"]], non_blocking=True)
+    e2e_ms = graph_timed(torch, e2e_step, max(3, args.steps // 4), args.warmup) / max(
+        3, args.steps // 4)
+    step_bytes = kvw_bytes()
+    value = step_bytes / (ms * 1e-3) / 1e9
+    achieved = (step_bytes / 2) / (one_ms * 1e-3) / 1e9
+    return {
+        "metric": "KV-cache write GB/s", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32->q8_0",
+        "data": "synthetic (seeded N(0,1) rows, contiguous append positions)",
+        "config": {"workload": "KV-cache write (SET_ROWS), 8192 tokens x 4 KV heads x D=256, "
+                               "K and V to Q8_0", "cache_rows": w["rows"],
+                   "l2": "rotating %d input sets (%.0f MB > 2x L2)" % (
+                       n_sets, n_sets * 2 * w["n_tok"] * w["n_hkv"] * w["D"] * 4 / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                     "kernel": "set_rows_kernel", "traffic": profile_traffic("set_rows_kvw")},
+        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": int(kh.numel() * 8),
+                "d2h_bytes_per_step": int(kback.numel() * 2)},
+        "gpu_launches": args.steps * 2,
+        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
+        "clocks": clocks,
+    }
+
+
+def cpu_kvw_sample(n_tok=1024):
+    """The oracle's reference quantizer (all rows of n_tok tokens, K and V)
+    plus the scatter, on the host."""
+    import oracle
+    w = KVW
+    rng = np.random.default_rng(0)
+    k = rng.normal(0, 1, (1, n_tok, w["n_hkv"], w["D"])).astype(np.float32)
+    v = rng.normal(0, 1, k.shape).astype(np.float32)
+    rb = oracle.row_size(oracle.Q8_0, w["D"])
+    kc = np.zeros((1, w["rows"], w["n_hkv"], rb), np.uint8)
+    vc = np.zeros_like(kc)
+    pos = np.arange(100, 100 + n_tok)
+    t = time.perf_counter()
+    reps = 0
+    while True:
+        kc[0, pos] = oracle.quantize(oracle.Q8_0, k)[0]
+        vc[0, pos] = oracle.quantize(oracle.Q8_0, v)[0]
+        reps += 1
+        if time.perf_counter() - t > 2.0 or reps >= 20:
+            break
+    dt = (time.perf_counter() - t) / reps
+    b = kvw_bytes() * n_tok / w["n_tok"]
+    return b / dt / 1e9, {"cores": 1, "unit": "GB/s",
+                          "sample": f"{n_tok} tokens x {w['n_hkv']} heads x D={w['D']}, K and V, "
+                                    f"{reps} reps, {dt * 1e3:.2f} ms each, 1 thread"}
+
+
 def cpu_gdn_sample(workload):
     import oracle
     n_seq, T = (8, 1) if workload == "c3a" else (1, 256)
@@ -580,7 +689,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "c1", "c2", "c2q4", "c3a", "c3b", "c4", "c5"])
+                    choices=["auto", "c1", "c2", "c2q4", "c3a", "c3b", "c4", "c5", "kvw"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -588,7 +697,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     workload = args.workload if args.workload != "auto" else ("c2" if world == 1 else "c5")
 
-    single = workload in ("c3a", "c3b", "c4")
+    single = workload in ("c3a", "c3b", "c4", "kvw")
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -597,6 +706,8 @@ def main():
             (val, info), metric = cpu_gdn_sample(workload), "gated-delta-net GB/s"
         elif workload == "c4":
             (val, info), metric, unit = cpu_prefill_sample(), "causal prefill TFLOP/s", "TFLOP/s"
+        elif workload == "kvw":
+            (val, info), metric = cpu_kvw_sample(), "KV-cache write GB/s"
         else:
             val, info = cpu_oracle_sample(workload)
         val = float(f"{val:.4g}")
@@ -613,13 +724,15 @@ def main():
 
     import torch
     if single:
-        # GDN and prefill rows are measured on one GPU
+        # GDN, prefill and KV-write rows are measured on one GPU
         if world > 1:
             print(json.dumps({"error": f"workload {workload} runs on one GPU"}), flush=True)
             return 2
-        line = run_gdn(args, torch, workload) if workload != "c4" else run_prefill(args, torch)
+        runs = {"c4": run_prefill, "kvw": run_kvw}
+        line = runs[workload](args, torch) if workload in runs else run_gdn(args, torch, workload)
         if not args.no_cpu_baseline:
-            val, info = cpu_gdn_sample(workload) if workload != "c4" else cpu_prefill_sample()
+            samples = {"c4": cpu_prefill_sample, "kvw": cpu_kvw_sample}
+            val, info = samples[workload]() if workload in samples else cpu_gdn_sample(workload)
             line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": info["unit"],
                                     "cores": info["cores"], "kind": "port",
                                     "sample": info["sample"]}

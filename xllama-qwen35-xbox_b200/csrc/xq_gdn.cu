@@ -396,9 +396,103 @@ __global__ void set_rows_kernel(const SetRowsArgs a) {
     quant_block<T>(x, a.dst + dr * a.d_nb1 + i2 * a.d_nb2 + i3 * a.d_nb3, b);
 }
 
+// The same for Q8_0 / Q4_0 with 8 lanes per 32-element block: each lane loads
+// one float4 (a warp reads 512 contiguous bytes), amax (and Q4_0's signed max,
+// the first element of largest magnitude as in the reference loop) meet in a
+// 3-level shuffle tree, and the per-element arithmetic is the reference's.
+// Needs 16-byte aligned source rows.
+template <int T>
+__global__ void __launch_bounds__(256) set_rows_coop_kernel(const SetRowsArgs a) {
+    const int64_t nb = a.ne0 / 32;
+    const int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const int sub = threadIdx.x & 7;
+    const bool live = unit < a.n_units; // whole 8-lane groups share `live`
+    const int64_t u = live ? unit : 0;
+    const int64_t row = u / nb, b = u - row * nb;
+    const int64_t i1 = row % a.ne1, i2 = (row / a.ne1) % a.ne2, i3 = row / (a.ne1 * a.ne2);
+    const uint8_t *ip = a.idx + i1 * a.i_nb0 + (i2 % a.i_ne1) * a.i_nb1 + (i3 % a.i_ne2) * a.i_nb2;
+    const int64_t dr = a.idx_i64 ? *reinterpret_cast<const int64_t *>(ip)
+                                 : (int64_t)*reinterpret_cast<const int32_t *>(ip);
+    const bool store = live && dr >= 0 && dr < a.d_rows;
+    const float4 x = *reinterpret_cast<const float4 *>(
+        a.src + i1 * a.s_nb1 + i2 * a.s_nb2 + i3 * a.s_nb3 + 4 * (32 * b + 4 * sub));
+    const float xv[4] = {x.x, x.y, x.z, x.w};
+    uint8_t *blk = a.dst + (store ? dr : 0) * a.d_nb1 + i2 * a.d_nb2 + i3 * a.d_nb3;
+    if constexpr (T == kQ8) {
+        float amax = fmaxf(fmaxf(fabsf(xv[0]), fabsf(xv[1])), fmaxf(fabsf(xv[2]), fabsf(xv[3])));
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1)
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint32_t w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w |= (uint32_t)(uint8_t)(int8_t)roundf(__fmul_rn(xv[j], id)) << (8 * j);
+        if (store) {
+            blk += 34 * b;
+            uint16_t *c = reinterpret_cast<uint16_t *>(blk + 2 + 4 * sub);
+            c[0] = (uint16_t)w;
+            c[1] = (uint16_t)(w >> 16);
+            if (sub == 0)
+                *reinterpret_cast<uint16_t *>(blk) = __half_as_ushort(__float2half_rn(d));
+        }
+    } else {
+        // first element of largest magnitude: (|x|, -index) ordering
+        float am = -1.0f, vm = 0.0f;
+        int im = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (fabsf(xv[j]) > am) {
+                am = fabsf(xv[j]);
+                vm = xv[j];
+                im = 4 * sub + j;
+            }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+            const float a2 = __shfl_xor_sync(0xffffffffu, am, o);
+            const float v2 = __shfl_xor_sync(0xffffffffu, vm, o);
+            const int i2x = __shfl_xor_sync(0xffffffffu, im, o);
+            if (a2 > am || (a2 == am && i2x < im)) {
+                am = a2;
+                vm = v2;
+                im = i2x;
+            }
+        }
+        const float d = (am > 0.0f ? vm : 0.0f) / -8.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint32_t q4 = 0; // four 4-bit codes of this lane's elements
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            q4 |= (uint32_t)min(15, (int)(int8_t)__fadd_rn(__fmul_rn(xv[j], id), 8.5f)) << (8 * j);
+        // byte k of the block holds element k (low nibble) and k + 16 (high):
+        // lanes 0-3 combine their codes with those of lanes 4-7
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, q4, 4);
+        if (store && sub < 4) {
+            blk += 18 * b;
+            const uint32_t w = q4 | (hi << 4);
+            uint16_t *c = reinterpret_cast<uint16_t *>(blk + 2 + 4 * sub);
+            c[0] = (uint16_t)w;
+            c[1] = (uint16_t)(w >> 16);
+            if (sub == 0)
+                *reinterpret_cast<uint16_t *>(blk) = __half_as_ushort(__float2half_rn(d));
+        }
+    }
+}
+
 cudaError_t launch_set_rows(int type, const SetRowsArgs &a, cudaStream_t st) {
     if (a.n_units <= 0)
         return cudaSuccess;
+    const bool src16 = ((reinterpret_cast<uintptr_t>(a.src) | (uintptr_t)a.s_nb1 |
+                         (uintptr_t)a.s_nb2 | (uintptr_t)a.s_nb3) & 15) == 0;
+    if ((type == kQ8 || type == kQ4) && src16) {
+        const unsigned blocks = (unsigned)((a.n_units * 8 + 255) / 256);
+        if (type == kQ8)
+            set_rows_coop_kernel<kQ8><<<blocks, 256, 0, st>>>(a);
+        else
+            set_rows_coop_kernel<kQ4><<<blocks, 256, 0, st>>>(a);
+        return cudaGetLastError();
+    }
     const unsigned blocks = (unsigned)((a.n_units + 255) / 256);
     switch (type) {
     case kF32: set_rows_kernel<kF32><<<blocks, 256, 0, st>>>(a); break;
