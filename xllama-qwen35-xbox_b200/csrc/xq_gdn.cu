@@ -401,15 +401,19 @@ __global__ void set_rows_kernel(const SetRowsArgs a) {
 // the first element of largest magnitude as in the reference loop) meet in a
 // 3-level shuffle tree, and the per-element arithmetic is the reference's.
 // Needs 16-byte aligned source rows.
+// Grid: x over the blocks of one (i2, i3) plane (32-bit: ne1 * ne0 / 32 units),
+// z over the planes, so the only per-lane division is unit -> (row, block).
 template <int T>
 __global__ void __launch_bounds__(256) set_rows_coop_kernel(const SetRowsArgs a) {
-    const int64_t nb = a.ne0 / 32;
-    const int64_t unit = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const uint32_t nb = (uint32_t)(a.ne0 / 32);
+    const uint32_t plane_units = (uint32_t)a.ne1 * nb;
+    const uint32_t unit = (blockIdx.x * blockDim.x + threadIdx.x) >> 3;
     const int sub = threadIdx.x & 7;
-    const bool live = unit < a.n_units; // whole 8-lane groups share `live`
-    const int64_t u = live ? unit : 0;
-    const int64_t row = u / nb, b = u - row * nb;
-    const int64_t i1 = row % a.ne1, i2 = (row / a.ne1) % a.ne2, i3 = row / (a.ne1 * a.ne2);
+    const bool live = unit < plane_units; // whole 8-lane groups share `live`
+    const uint32_t u = live ? unit : 0;
+    const uint32_t i1u = u / nb;
+    const int64_t i1 = i1u, b = u - i1u * nb;
+    const int64_t i2 = blockIdx.z % a.ne2, i3 = blockIdx.z / a.ne2; // uniform
     const uint8_t *ip = a.idx + i1 * a.i_nb0 + (i2 % a.i_ne1) * a.i_nb1 + (i3 % a.i_ne2) * a.i_nb2;
     const int64_t dr = a.idx_i64 ? *reinterpret_cast<const int64_t *>(ip)
                                  : (int64_t)*reinterpret_cast<const int32_t *>(ip);
@@ -485,12 +489,14 @@ cudaError_t launch_set_rows(int type, const SetRowsArgs &a, cudaStream_t st) {
         return cudaSuccess;
     const bool src16 = ((reinterpret_cast<uintptr_t>(a.src) | (uintptr_t)a.s_nb1 |
                          (uintptr_t)a.s_nb2 | (uintptr_t)a.s_nb3) & 15) == 0;
-    if ((type == kQ8 || type == kQ4) && src16) {
-        const unsigned blocks = (unsigned)((a.n_units * 8 + 255) / 256);
+    const int64_t planes = a.ne2 * a.ne3, plane_units = a.ne1 * (a.ne0 / 32);
+    if ((type == kQ8 || type == kQ4) && src16 && planes <= 65535 &&
+        plane_units * 8 <= 0x7fffffffll) {
+        const dim3 grid((unsigned)((plane_units * 8 + 255) / 256), 1, (unsigned)planes);
         if (type == kQ8)
-            set_rows_coop_kernel<kQ8><<<blocks, 256, 0, st>>>(a);
+            set_rows_coop_kernel<kQ8><<<grid, 256, 0, st>>>(a);
         else
-            set_rows_coop_kernel<kQ4><<<blocks, 256, 0, st>>>(a);
+            set_rows_coop_kernel<kQ4><<<grid, 256, 0, st>>>(a);
         return cudaGetLastError();
     }
     const unsigned blocks = (unsigned)((a.n_units + 255) / 256);
