@@ -683,14 +683,10 @@ __global__ void __launch_bounds__(256) lse_merge_rows_kernel(const float *__rest
 template <int T, int D, int NR, int R, int VW>
 static cudaError_t launch_one(const DecodeArgs &a, size_t smem, dim3 grid, cudaStream_t st) {
     auto kern = fa_decode_kernel<T, D, NR, R, VW>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess)
-            return e;
-        attr_set = true;
-    }
+    static std::atomic<unsigned long long> attr_done{0};
+    cudaError_t e = set_smem_limit((const void *)kern, smem, attr_done);
+    if (e != cudaSuccess)
+        return e;
     kern<<<grid, kThreads, smem, st>>>(a);
     return cudaGetLastError();
 }

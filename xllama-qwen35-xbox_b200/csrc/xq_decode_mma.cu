@@ -896,14 +896,10 @@ template <int T, int D, int ST, int VW>
 static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
     constexpr size_t smem = mma_smem<T, D, ST>();
     auto kern = fa_decode_mma_kernel<T, D, ST, VW>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e =
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess)
-            return e;
-        attr_set = true;
-    }
+    static std::atomic<unsigned long long> attr_done{0};
+    cudaError_t e = set_smem_limit((const void *)kern, smem, attr_done);
+    if (e != cudaSuccess)
+        return e;
     CUtensorMap maps[2];
     memset(maps, 0, sizeof(maps));
     if constexpr (dm::tma_mode(T, VW)) {

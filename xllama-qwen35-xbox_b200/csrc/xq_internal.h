@@ -4,7 +4,27 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace xq {
+
+// Raise a kernel's dynamic shared-memory limit on the current device once.
+// The attribute belongs to the kernel on one device, so one process driving
+// several GPUs needs it set on each: `done` holds one bit per device ordinal.
+inline cudaError_t set_smem_limit(const void *kern, size_t smem,
+                                  std::atomic<unsigned long long> &done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return e;
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit))
+        return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && bit)
+        done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 // One split-KV decode launch.  Byte strides follow ggml nb[].
 struct DecodeArgs {

@@ -679,13 +679,16 @@ cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, co
     a.scale_log2 = ps.scale * 1.4426950408889634f;
     const size_t smem = 1024 + (size_t)pf::nslot(D) * pf::BN * D * 2 + 256;
     dim3 grid((unsigned)(n_qt * ps.n_head * ps.n_seq));
+    static std::atomic<unsigned long long> attr_done[2];
     if (D == 256) {
-        cudaFuncSetAttribute(fa_prefill_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
+        e = set_smem_limit((const void *)fa_prefill_kernel<256>, smem, attr_done[1]);
+        if (e != cudaSuccess)
+            return e;
         fa_prefill_kernel<256><<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
     } else {
-        cudaFuncSetAttribute(fa_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
+        e = set_smem_limit((const void *)fa_prefill_kernel<128>, smem, attr_done[0]);
+        if (e != cudaSuccess)
+            return e;
         fa_prefill_kernel<128><<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
     }
     return cudaGetLastError();
