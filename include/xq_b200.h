@@ -19,6 +19,9 @@
  *                         (patches/0006-cpu-flash-attn-consistent-kv-reduction.patch:7-14)
  *   xq_gated_delta_net    GGML_OP_GATED_DELTA_NET (ggml-cpu.c:2148-2150 and the
  *                         D3D12 kernel dispatch src/bridge/ggml_d3d12.cpp:1905-1941)
+ *   xq_gated_delta_net_ws the same op in chunked form for long prefill (the
+ *                         CPU op's per-token loop, ops.cpp of the snapshot,
+ *                         restated as 64-token WY chunks on the tensor cores)
  *   xq_attend_range       RemoteAttnEngine::attend_range
  *                         (uwp/rkva/remote-attn-engine.h:152-154,
  *                          remote-attn-engine.cpp:2774-3251)
@@ -172,6 +175,24 @@ uint32_t xq_split_k(uint32_t active, uint32_t mode);
 int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
                        const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
                        float *dst, int32_t slots, xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* GATED_DELTA_NET for long sequences (prefill), same contract as above, in  */
+/* chunked (WY) form: 64-token chunks, the per-chunk products on the tensor  */
+/* cores with TF32 operands and FP32 accumulation (error vs the sequential   */
+/* FP32 recurrence ~1e-3 of max|y|, inside max-abs 2e-3 / rel 1e-2), the     */
+/* state carried in FP32.  Used when T spans at least two chunks and q/k/v   */
+/* rows are 16-byte aligned; otherwise (and for T <= 64) it runs exactly     */
+/* xq_gated_delta_net.  workspace: device memory, 256-byte aligned, of       */
+/* xq_gated_delta_net_workspace(v, slots) bytes (0: none needed); too small  */
+/* => XQ_ERR_WORKSPACE.  With slots > 1 the last `slots` tokens run the      */
+/* per-token kernel, which writes the snapshots.                             */
+/* ------------------------------------------------------------------------ */
+size_t xq_gated_delta_net_workspace(const xq_tensor *v, int32_t slots);
+int xq_gated_delta_net_ws(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                          const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                          float *dst, int32_t slots, void *workspace, size_t workspace_bytes,
+                          xq_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* GGML_OP_SET_ROWS (quantize-on-append into the KV cache).  src F32         */

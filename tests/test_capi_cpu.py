@@ -65,6 +65,8 @@ def test_contract_errors_before_launch():
     assert L.xq_lse_merge(None, 1, 1, 256, None, None, None) == XL.XQ_ERR_INVALID
     t = XL.Tensor()
     assert L.xq_gated_delta_net(*[C.byref(t)] * 6, None, 1, None) == XL.XQ_ERR_INVALID
+    assert L.xq_gated_delta_net_ws(*[C.byref(t)] * 6, None, 1, None, 0, None) == \
+        XL.XQ_ERR_INVALID
     # SET_ROWS: ggml_set_rows' shape rules and types, checked before any launch
     src, idx, dst = XL.Tensor(), XL.Tensor(), XL.Tensor()
     src.type, src.nb[0], idx.type, dst.type = XL.F32, 4, XL.I64, XL.Q8_0
@@ -80,3 +82,24 @@ def test_contract_errors_before_launch():
     assert L.xq_set_rows(C.byref(src), C.byref(idx), C.byref(dst), None) == XL.XQ_ERR_UNSUPPORTED
     idx.type, idx.ne[1] = XL.I32, 3  # 2 heads not a multiple of 3
     assert L.xq_set_rows(C.byref(src), C.byref(idx), C.byref(dst), None) == XL.XQ_ERR_INVALID
+
+
+def test_gdn_chunked_workspace_sizes():
+    """Workspace of the chunked GATED_DELTA_NET: [T''; M] (32 KiB) and factors
+    (1 KiB) per (chunk, head, sequence), an error word, and the handed-off
+    state when the last tokens run per token; none below two chunks."""
+    import xq._lib as XL
+    L = _lib()
+    v = XL.Tensor()
+    v.type = XL.F32
+
+    def ws(T, H, n_seq, slots):
+        v.ne[0], v.ne[1], v.ne[2], v.ne[3] = 128, H, T, n_seq
+        return L.xq_gated_delta_net_workspace(C.byref(v), slots)
+
+    unit = 32768 + 1024
+    assert ws(4096, 32, 1, 1) == 64 * 32 * unit + 256
+    assert ws(200, 32, 2, 1) == 4 * 32 * 2 * unit + 256          # last chunk padded
+    assert ws(300, 32, 1, 5) == 4 * 32 * unit + 256 + 32 * 65536  # 44 tokens per token
+    assert ws(64, 32, 1, 1) == 0 and ws(100, 32, 1, 64) == 0
+    assert ws(4096, 32, 1, 0) == 0  # slots outside [1, 64]

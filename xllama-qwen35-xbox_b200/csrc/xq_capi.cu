@@ -537,9 +537,10 @@ int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_he
 // ---------------------------------------------------------------------------
 // GATED_DELTA_NET.
 
-int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
-                       const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
-                       float *dst, int32_t slots, xq_stream_t stream) {
+// Validates a GATED_DELTA_NET call and fills the kernel arguments.
+static int gdn_args(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                    const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                    float *dst, int32_t slots, xq::GdnArgs *out) {
     if (!q || !k || !v || !g || !beta || !state || !dst)
         return fail(XQ_ERR_INVALID, "gated_delta_net: null argument");
     const xq_tensor *all[6] = {q, k, v, g, beta, state};
@@ -591,8 +592,47 @@ int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *
     a.rk3 = (int)(n_seq / k->ne[3]);
     a.slots = slots;
     a.scale = 1.0f / sqrtf((float)S);
+    *out = a;
+    return XQ_OK;
+}
+
+int xq_gated_delta_net(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                       const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                       float *dst, int32_t slots, xq_stream_t stream) {
+    xq::GdnArgs a;
+    const int rc = gdn_args(q, k, v, g, beta, state, dst, slots, &a);
+    if (rc != XQ_OK)
+        return rc;
     return cuda_status(xq::launch_gdn(a, reinterpret_cast<cudaStream_t>(stream)),
                        "gated_delta_net");
+}
+
+size_t xq_gated_delta_net_workspace(const xq_tensor *v, int32_t slots) {
+    if (!v || v->ne[0] != 128 || v->ne[1] <= 0 || v->ne[2] <= 0 || v->ne[3] <= 0 ||
+        v->ne[1] > 65535 || v->ne[2] > INT32_MAX || v->ne[3] > 65535 || slots < 1 || slots > 64)
+        return 0;
+    return xq::gdn_chunk_workspace((int)v->ne[2], (int)v->ne[1], (int)v->ne[3], slots);
+}
+
+int xq_gated_delta_net_ws(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                          const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                          float *dst, int32_t slots, void *workspace, size_t workspace_bytes,
+                          xq_stream_t stream) {
+    xq::GdnArgs a;
+    const int rc = gdn_args(q, k, v, g, beta, state, dst, slots, &a);
+    if (rc != XQ_OK)
+        return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (!xq::gdn_chunk_eligible(a))
+        return cuda_status(xq::launch_gdn(a, st), "gated_delta_net");
+    const size_t need = xq::gdn_chunk_workspace(a.T, a.H, a.n_seq, a.slots);
+    if (!workspace || workspace_bytes < need)
+        return fail(XQ_ERR_WORKSPACE, "gated_delta_net: workspace %zu bytes, %zu needed",
+                    workspace_bytes, need);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return fail(XQ_ERR_WORKSPACE, "gated_delta_net: workspace must be 256-byte aligned");
+    return cuda_status(xq::launch_gdn_chunked(a, workspace, workspace_bytes, st),
+                       "gated_delta_net (chunked)");
 }
 
 // ---------------------------------------------------------------------------

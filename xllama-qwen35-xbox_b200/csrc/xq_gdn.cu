@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
     const float *gb = ptr(a.g, seq * a.g_nb3 + h * a.g_nb1);
     const float *bb = ptr(a.beta, seq * a.b_nb3 + h * a.b_nb1);
 
-    for (int t = 0; t < a.T; ++t) {
+    for (int t = a.t_begin; t < a.T; ++t) {
         const float *qt = ptr(qb, (int64_t)t * a.q_nb2);
         const float *kt = ptr(kb, (int64_t)t * a.k_nb2);
         float kx[EPT], qx[EPT];
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(CB * TPC) gdn_stream_kernel(const GdnArgs a) {
     const float *bb = ptr(a.beta, seq * a.b_nb3 + h * a.b_nb1);
 
     auto stage = [&](int c, int buf) {
-        const int t0 = c * TC, nt = min(TC, a.T - t0);
+        const int t0 = a.t_begin + c * TC, nt = min(TC, a.T - t0);
         for (int idx = tid; idx < TC * PR; idx += NT) {
             const int r = idx / PR, pc = idx - r * PR;
             if (r < nt) {
@@ -176,11 +176,11 @@ __global__ void __launch_bounds__(CB * TPC) gdn_stream_kernel(const GdnArgs a) {
         }
         cp_async_commit();
     };
-    const int n_chunks = (a.T + TC - 1) / TC;
+    const int n_chunks = (a.T - a.t_begin + TC - 1) / TC;
     stage(0, 0);
     stage(1, 1);
     for (int c = 0; c < n_chunks; ++c) {
-        const int buf = c & 1, t0 = c * TC, nt = min(TC, a.T - t0);
+        const int buf = c & 1, t0 = a.t_begin + c * TC, nt = min(TC, a.T - t0);
         cp_async_wait<1>(); // chunk c has landed (chunk c + 1 may be in flight)
         __syncthreads();
         if (tid < nt)

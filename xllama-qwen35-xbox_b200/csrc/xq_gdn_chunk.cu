@@ -1,0 +1,824 @@
+// GATED_DELTA_NET over long sequences in chunked (WY) form on the tcgen05
+// tensor cores, TF32 operands with FP32 accumulation.
+//
+// Recurrence (ggml-cpu, one value head; S is S_v x S_k, row j = value column):
+//   S_t = g~_t S_{t-1} + u_t k_t^T,   u_t = beta_t (v_t - g~_t S_{t-1} k_t),
+//   y_t = scale * S_t q_t,            g~_t = exp(g_t)
+// Over a chunk of C = 64 tokens with S_0 the state entering it, G_t the
+// inclusive prefix sum of g inside the chunk, b_t = exp(G_t),
+// e_t = exp(G_C - G_t):
+//   A_ts = beta_t exp(G_t - G_s) k_t.k_s          (s < t, else 0)
+//   T''  = (I + A)^-1 diag(beta)
+//   M_ts = scale exp(G_t - G_s) q_t.k_s           (s <= t, else 0)
+//   X    = K S_0^T,  X' = V - diag(b) X,  U = T'' X'
+//   Y    = scale diag(b) Q S_0^T + M U
+//   S_C^T = b_C S_0^T + K^T diag(e) U
+// (u_t of the recurrence is row t of U; expanding S_{t-1} over the chunk gives
+// (I + A) U = diag(beta) (V - diag(b) K S_0^T).)
+//
+// Two kernels:
+//   gdn_chunk_prep_kernel  one CTA per (chunk, head, sequence), all in
+//     parallel: [K;Q] K^T on the tensor core (M=128, N=64, K=128), the gates,
+//     the unit lower-triangular inverse in FP32 (16x16 diagonal blocks by
+//     forward substitution, then block rows), and writes [T''; M] (128 x 64)
+//     plus b, e, b_C to the workspace.
+//   gdn_chunk_scan_kernel  one CTA per (32 state rows, head, sequence),
+//     sequential over chunks with the state in registers (thread i holds
+//     column i of the 32 rows) and an operand copy in shared memory:
+//       MMA1  [K;Q] S_0^T          SS, M=128 (64 K rows + 64 Q rows), N=32, K=128
+//       MMA2  [T'';M] X'           TS, A in TMEM, B = X' MN-major, K=64
+//       MMA3  [T'';M] U            TS (rows 64..127: M U lands on the lanes
+//                                  holding scale b Q S_0^T)
+//       MMA4  K^T (diag(e) U)      TS, K^T copied into TMEM by the chain
+//                                  threads (M=128 over the key elements)
+//     MN-major TF32 operands (X', U, diag(e) U) use the 128-byte swizzle with
+//     32-byte granules, the only MN-major layout for 32-bit elements; K-major
+//     operands use the plain 128-byte swizzle TMA writes.
+//     A warp-specialised TMA producer double-buffers K/Q/V tiles and streams
+//     [T''; M] through one landing buffer into TMEM.
+// Operands produced here (S, X', U, T'', M) are rounded to TF32 to nearest;
+// K, Q, V tiles enter the tensor core as stored (fp32 read as TF32).  Tokens
+// past T read as zeros with g = beta = 0, so a partial last chunk is exact.
+// Every mbarrier wait is bounded; on timeout the kernel records an error,
+// drains its own copies and MMAs with bounded waits, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "xq_common.cuh"
+#include "xq_internal.h"
+#include "xq_tc.cuh"
+
+namespace xq {
+
+namespace gc {
+constexpr int C = 64;        // tokens per chunk
+constexpr int SK = 128;      // head size (key and value)
+constexpr int R = 32;        // state rows per scan CTA
+constexpr int AST = 68;      // padded row stride (floats) of the solve matrices
+constexpr int ATM_FLOATS = 128 * 64; // [T''; M] per unit
+constexpr int FAC_FLOATS = 256;      // b[64], e[64], b_C, pad
+constexpr int PREP_NT = 128;
+constexpr int SCAN_NT = 160;         // 4 chain warps + 1 producer warp
+constexpr float kLog2e = 1.4426950408889634f;
+
+// prep kernel shared memory
+constexpr int P_KQ = 0;                       // 4 slabs x 16 KB, rows 0-63 K, 64-127 Q
+constexpr int P_AM = 65536;                   // A [64][AST]
+constexpr int P_TT = P_AM + 64 * AST * 4;     // T transposed [col][row]
+constexpr int P_G = P_TT + 64 * AST * 4;      // G[64], beta[64]
+constexpr int P_BAR = P_G + 512;
+constexpr int P_BYTES = P_BAR + 32 + 1024;    // + alignment slack
+
+// scan kernel shared memory
+constexpr int S_KQ = 0;                       // 2 stages x 64 KB
+constexpr int S_V = 131072;                   // 2 stages x 8 KB
+constexpr int S_ATM = 147456;                 // landing buffer, 2 slabs x 16 KB
+constexpr int S_SB = 180224;                  // S operand, 4 slabs x 4 KB (K-major)
+constexpr int S_XB = 196608;                  // X' (MN-major, 64 x 32)
+constexpr int S_UB = 204800;                  // U
+constexpr int S_U2 = 212992;                  // diag(e) U
+constexpr int S_FAC = 221184;                 // 2 stages x 1 KB
+constexpr int S_BAR = 223232;
+constexpr int S_BYTES = S_BAR + 64 + 1024;
+
+// scan kernel TMEM columns
+constexpr uint32_t TM_ATM = 0;  // [T''; M], 2 buffers x 64
+constexpr uint32_t TM_KT = 128; // K^T (lane i, column t): A of the state update
+constexpr uint32_t TM_D1 = 192, TM_D2 = 224, TM_D3 = 256, TM_D4 = 288;
+constexpr uint32_t TM_COLS = 512;
+
+__host__ __device__ constexpr int n_chunks(int T, int slots) {
+    // one snapshot slot: every token, the last chunk padded; K > 1 slots: the
+    // last K tokens go to the per-token kernel, which writes the snapshots
+    return slots == 1 ? (T + C - 1) / C : (T > slots ? (T - slots) / C : 0);
+}
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+    return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+__device__ __forceinline__ const float *at(const float *base, int64_t off) {
+    return reinterpret_cast<const float *>(reinterpret_cast<const char *>(base) + off);
+}
+// AND of `ok` over the 128 chain threads (named barrier 1).
+__device__ __forceinline__ bool chain_and(bool ok) {
+    uint32_t r;
+    asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\n"
+                 "bar.red.and.pred q, 1, 128, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+                 : "=r"(r)
+                 : "r"((uint32_t)ok)
+                 : "memory");
+    return r != 0;
+}
+} // namespace gc
+
+struct GdnChunkArgs {
+    const float *g, *beta, *state;
+    int64_t g_nb1, g_nb2, g_nb3, b_nb1, b_nb2, b_nb3, s_nb1, s_nb2, s_nb3;
+    float *atm;       // [unit][128][64]
+    float *fac;       // [unit][256]
+    float *dst;       // y [n_seq][T][H][128]
+    float *state_out; // [n_seq][H][128][128]
+    int *err;
+    int H, H_k, T, n_seq, rq3, rk3, NC;
+    float scale;
+};
+
+// ---------------------------------------------------------------------------
+// Per-chunk preparation.
+
+// Block row BI of T = (I + A)^-1 for this thread's column cc (BI > cc / 16):
+// E = A[16BI.., :16BI] T[:16BI, cc], then T[16BI + r, cc] = -(D_BI E)_r with
+// D_BI = T[16BI.., 16BI..] (already in Tt).  Tt is column-major: Tt[cc][row].
+template <int BI>
+__device__ __forceinline__ void solve_block_row(const float *Am, float *Tt, int cc) {
+    using namespace gc;
+    float e[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+        e[r] = 0.0f;
+    const float *tcol = Tt + cc * AST;
+#pragma unroll
+    for (int m4 = 0; m4 < 4 * BI; ++m4) {
+        const float4 tv = *reinterpret_cast<const float4 *>(tcol + 4 * m4);
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const float4 av =
+                *reinterpret_cast<const float4 *>(Am + (16 * BI + r) * AST + 4 * m4);
+            e[r] = fmaf(av.x, tv.x, e[r]);
+            e[r] = fmaf(av.y, tv.y, e[r]);
+            e[r] = fmaf(av.z, tv.z, e[r]);
+            e[r] = fmaf(av.w, tv.w, e[r]);
+        }
+    }
+    float o[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+        o[r] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) {
+        const float *dcol = Tt + (16 * BI + m) * AST + 16 * BI; // D[:, m] (zero above)
+#pragma unroll
+        for (int r4 = 0; r4 < 4; ++r4) {
+            const float4 d = *reinterpret_cast<const float4 *>(dcol + 4 * r4);
+            o[4 * r4] = fmaf(d.x, e[m], o[4 * r4]);
+            o[4 * r4 + 1] = fmaf(d.y, e[m], o[4 * r4 + 1]);
+            o[4 * r4 + 2] = fmaf(d.z, e[m], o[4 * r4 + 2]);
+            o[4 * r4 + 3] = fmaf(d.w, e[m], o[4 * r4 + 3]);
+        }
+    }
+#pragma unroll
+    for (int r4 = 0; r4 < 4; ++r4)
+        *reinterpret_cast<float4 *>(Tt + cc * AST + 16 * BI + 4 * r4) =
+            make_float4(-o[4 * r4], -o[4 * r4 + 1], -o[4 * r4 + 2], -o[4 * r4 + 3]);
+}
+
+__global__ void __launch_bounds__(gc::PREP_NT)
+    gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap qmap, const GdnChunkArgs a) {
+    using namespace tc;
+    using namespace gc;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    float *Am = reinterpret_cast<float *>(smem + P_AM);
+    float *Tt = reinterpret_cast<float *>(smem + P_TT);
+    float *Gs = reinterpret_cast<float *>(smem + P_G);
+    float *Bs = Gs + 64;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_BAR);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2);
+    volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
+    const int hk = h % a.H_k, t0 = c * C;
+    const size_t unit = ((size_t)n * a.H + h) * a.NC + c;
+    const uint32_t bar_tma = smem_u32(bars), bar_mma = smem_u32(bars + 1);
+
+    if (tid == 0) {
+        prefetch_map(&kmap);
+        prefetch_map(&qmap);
+        mbar_init(bar_tma, 1);
+        mbar_init(bar_mma, 1);
+        *abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        mbar_expect_tx(bar_tma, 65536);
+#pragma unroll
+        for (int ib = 0; ib < 4; ++ib) {
+            const uint32_t slab = smem_u32(smem + P_KQ + ib * 16384);
+            tma_load_4d(slab, &kmap, 32 * ib, hk, t0, n / a.rk3, bar_tma);
+            tma_load_4d(slab + 8192, &qmap, 32 * ib, hk, t0, n / a.rq3, bar_tma);
+        }
+    }
+    if (warp == 1)
+        tmem_alloc(smem_u32(tmem_slot), 64);
+    if (tid < 64) {
+        // G = inclusive prefix sum of g over the chunk; padding tokens g = beta = 0
+        const int t = t0 + tid;
+        float gv = 0.0f, bv = 0.0f;
+        if (t < a.T) {
+            gv = *at(a.g, n * a.g_nb3 + (int64_t)t * a.g_nb2 + h * a.g_nb1);
+            bv = *at(a.beta, n * a.b_nb3 + (int64_t)t * a.b_nb2 + h * a.b_nb1);
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, gv, o);
+            if (lane >= o)
+                gv += y;
+        }
+        Gs[tid] = gv;
+        Bs[tid] = bv;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid >= 32 && tid < 64)
+        Gs[tid] += Gs[31];
+
+    // S = [K; Q] K^T  (rows 0-63: K K^T, rows 64-127: Q K^T)
+    bool ok = true;
+    if (warp == 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(bar_tma, 0, abort_s));
+        if (ok) {
+            tc_fence_after();
+            if (elect_one()) {
+                constexpr uint32_t ID = idesc_tf32(128, 64, 0, 0);
+                const uint32_t base = smem_u32(smem + P_KQ);
+#pragma unroll
+                for (int kk = 0; kk < 16; ++kk) {
+                    const uint64_t d = sdesc(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+                    mma_ss_tf32(tmem, d, d, ID, kk > 0);
+                }
+                mma_commit(bar_mma);
+            }
+            __syncwarp();
+        } else {
+            *abort_s = 1;
+        }
+    }
+    __syncthreads(); // Gs complete
+    ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, abort_s));
+    tc_fence_after();
+    float sv[64];
+    {
+        float lo[32], hi[32];
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        tmem_ld32(lane_base, lo);
+        tmem_ld32(lane_base + 32, hi);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            sv[i] = lo[i];
+            sv[32 + i] = hi[i];
+        }
+    }
+    float *atm = a.atm + unit * ATM_FLOATS;
+    if (tid < 64) {
+        const int t = tid;
+        const float Gt = Gs[t], bt = Bs[t];
+#pragma unroll
+        for (int s4 = 0; s4 < 16; ++s4) {
+            float w[4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const int s = 4 * s4 + x;
+                w[x] = s < t ? bt * ex2((Gt - Gs[s]) * kLog2e) * sv[s] : 0.0f;
+            }
+            *reinterpret_cast<float4 *>(Am + t * AST + 4 * s4) = make_float4(w[0], w[1], w[2], w[3]);
+        }
+    } else {
+        const int t = tid - 64;
+        const float Gt = Gs[t];
+        float4 *row = reinterpret_cast<float4 *>(atm + (64 + t) * 64);
+#pragma unroll
+        for (int s4 = 0; s4 < 16; ++s4) {
+            uint32_t w[4];
+#pragma unroll
+            for (int x = 0; x < 4; ++x) {
+                const int s = 4 * s4 + x;
+                w[x] = s <= t ? to_tf32(a.scale * ex2((Gt - Gs[s]) * kLog2e) * sv[s]) : 0u;
+            }
+            row[s4] = make_float4(__uint_as_float(w[0]), __uint_as_float(w[1]),
+                                  __uint_as_float(w[2]), __uint_as_float(w[3]));
+        }
+    }
+    __syncthreads(); // A complete
+
+    // T = (I + A)^-1, column cc per thread: diagonal 16x16 blocks first
+    if (tid < 64) {
+        const int cc = tid, bi = cc >> 4, c0 = cc & 15;
+        float *tcol = Tt + cc * AST;
+#pragma unroll
+        for (int r4 = 0; r4 < 16; ++r4)
+            *reinterpret_cast<float4 *>(tcol + 4 * r4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        float x[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+            x[m] = m == c0 ? 1.0f : 0.0f;
+        const float *Ab = Am + (16 * bi) * AST + 16 * bi;
+#pragma unroll
+        for (int r = 1; r < 16; ++r) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int m = 0; m < r; ++m)
+                acc = fmaf(Ab[r * AST + m], x[m], acc);
+            if (r > c0)
+                x[r] = -acc;
+        }
+#pragma unroll
+        for (int r4 = 0; r4 < 4; ++r4)
+            *reinterpret_cast<float4 *>(tcol + 16 * bi + 4 * r4) =
+                make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
+    }
+    __syncthreads(); // every diagonal block is in Tt
+    if (tid < 64) {
+        const int cc = tid, bj = cc >> 4;
+        // block rows below the thread's own diagonal block, in order: row BI
+        // reads only this thread's column (rows < 16 BI) and D_BI
+        if (bj < 1)
+            solve_block_row<1>(Am, Tt, cc);
+        if (bj < 2)
+            solve_block_row<2>(Am, Tt, cc);
+        if (bj < 3)
+            solve_block_row<3>(Am, Tt, cc);
+        // T'' = T diag(beta): column cc scaled by beta_cc, rows 0-63 of [T''; M]
+        const float bc = Bs[cc];
+        const float *tcol = Tt + cc * AST;
+#pragma unroll 8
+        for (int t = 0; t < 64; ++t)
+            atm[t * 64 + cc] = __uint_as_float(to_tf32(tcol[t] * bc));
+        // decay factors
+        float *fac = a.fac + unit * FAC_FLOATS;
+        const float Gt = Gs[cc], GC = Gs[63];
+        fac[cc] = ex2(Gt * kLog2e);
+        fac[64 + cc] = ex2((GC - Gt) * kLog2e);
+        if (cc == 0)
+            fac[128] = ex2(GC * kLog2e);
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+        if (*abort_s) {
+            // the tile copies may still be landing: bounded drain before exit
+            volatile int none = 0;
+            mbar_wait(bar_tma, 0, &none, 100000000ull);
+            atomicExch(a.err, 1);
+        }
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 64);
+    }
+    (void)ok;
+}
+
+// ---------------------------------------------------------------------------
+// Sequential scan over chunks.
+
+__global__ void __launch_bounds__(gc::SCAN_NT, 1)
+    gdn_chunk_scan_kernel(const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap qmap,
+                          const __grid_constant__ CUtensorMap vmap,
+                          const __grid_constant__ CUtensorMap amap, const GdnChunkArgs a) {
+    using namespace tc;
+    using namespace gc;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S_BAR);
+    // bars: full[2], kq_empty[2], atm_full, atm_empty, mma
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
+    volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    auto bar = [&](int i) { return smem_u32(bars + i); };
+    constexpr int B_FULL = 0, B_KQE = 2, B_AF = 4, B_AE = 5, B_MMA = 6;
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int slice = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
+    const int j0 = slice * R, hk = h % a.H_k;
+    const size_t unit0 = ((size_t)n * a.H + h) * a.NC;
+
+    if (tid == 0) {
+        prefetch_map(&kmap);
+        prefetch_map(&qmap);
+        prefetch_map(&vmap);
+        prefetch_map(&amap);
+        for (int i = 0; i < 4; ++i)
+            mbar_init(bar(i), 1);
+        mbar_init(bar(B_AF), 1);
+        mbar_init(bar(B_AE), 128);
+        mbar_init(bar(B_MMA), 1);
+        *abort_s = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0)
+        tmem_alloc(smem_u32(tmem_slot), TM_COLS);
+
+    // state rows j0..j0+31, column i = tid, kept in FP32 registers; the
+    // operand copy (TF32) goes to the K-major S tile: row j, K index i
+    float S[R];
+    if (tid < 128) {
+        const float *sp = at(a.state, n * a.s_nb3 + (int64_t)h * a.s_nb2);
+        const int i = tid;
+#pragma unroll
+        for (int jj = 0; jj < R; ++jj) {
+            S[jj] = *at(sp, (int64_t)(j0 + jj) * a.s_nb1 + 4 * i);
+            *reinterpret_cast<uint32_t *>(smem + S_SB + (i >> 5) * 4096 +
+                                          sw128(jj, (i & 31) >> 2) + (i & 3) * 4) =
+                to_tf32(S[jj]);
+        }
+        fence_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    int mma_pending = 0, mma_phase = 0;
+
+    if (warp == 4) {
+        // ----------------------------- producer -----------------------------
+        if (threadIdx.x % 32 == 0) {
+            int kq_issued = 0, atm_issued = 0;
+            for (int c = 0; c < a.NC; ++c) {
+                const int s = c & 1;
+                if (c >= 2 && !mbar_wait(bar(B_KQE + s), ((c >> 1) - 1) & 1, abort_s)) {
+                    *abort_s = 1;
+                    break;
+                }
+                const uint32_t fb = bar(B_FULL + s);
+                mbar_expect_tx(fb, 65536 + 8192 + 1024);
+                const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
+#pragma unroll
+                for (int ib = 0; ib < 4; ++ib) {
+                    tma_load_4d(kq + ib * 16384, &kmap, 32 * ib, hk, c * C, n / a.rk3, fb);
+                    tma_load_4d(kq + ib * 16384 + 8192, &qmap, 32 * ib, hk, c * C, n / a.rq3,
+                                fb);
+                }
+                tma_load_4d(smem_u32(smem + S_V + s * 8192), &vmap, j0, h, c * C, n, fb);
+                bulk_load(smem_u32(smem + S_FAC + s * 1024), a.fac + (unit0 + c) * FAC_FLOATS,
+                          1024, fb);
+                ++kq_issued;
+                if (c >= 1 && !mbar_wait(bar(B_AE), (c - 1) & 1, abort_s)) {
+                    *abort_s = 1;
+                    break;
+                }
+                mbar_expect_tx(bar(B_AF), 32768);
+                const int row = (int)((unit0 + c) * 128);
+                tma_load_2d(smem_u32(smem + S_ATM), &amap, 0, row, bar(B_AF));
+                tma_load_2d(smem_u32(smem + S_ATM + 16384), &amap, 32, row, bar(B_AF));
+                ++atm_issued;
+            }
+            if (*abort_s) {
+                // copies still in flight land on their barriers: bounded drain
+                volatile int none = 0;
+                for (int m = kq_issued - 2 < 0 ? 0 : kq_issued - 2; m < kq_issued; ++m)
+                    mbar_wait(bar(B_FULL + (m & 1)), (m >> 1) & 1, &none, 100000000ull);
+                if (atm_issued > 0)
+                    mbar_wait(bar(B_AF), (atm_issued - 1) & 1, &none, 100000000ull);
+            }
+        }
+    } else {
+        // ---------------------- chain (TMEM lanes 0-127) ----------------------
+        constexpr uint32_t ID1 = idesc_tf32(128, R, 0, 0);
+        constexpr uint32_t ID2 = idesc_tf32(128, R, 0, 1);
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t sb = smem_u32(smem + S_SB), xb = smem_u32(smem + S_XB),
+                       ub = smem_u32(smem + S_UB), u2 = smem_u32(smem + S_U2);
+        bool ok = true;
+        float yb[R];
+        for (int c = 0; c < a.NC && ok; ++c) {
+            const int s = c & 1;
+            const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
+            const uint32_t atm_t = tmem + TM_ATM + (uint32_t)(c & 1) * 64;
+            const float *fac = reinterpret_cast<const float *>(smem + S_FAC + s * 1024);
+            // 1. chunk inputs, MMA1: D1 = [K; Q] S_0^T
+            ok = chain_and(mbar_wait(bar(B_FULL + s), (c >> 1) & 1, abort_s));
+            if (!ok)
+                break;
+            if (warp == 0) {
+                tc_fence_after();
+                if (elect_one()) {
+#pragma unroll
+                    for (int kk = 0; kk < 16; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        mma_ss_tf32(tmem + TM_D1, sdesc(kq + off, 16, 1024),
+                                    sdesc(sb + (kk >> 2) * 4096 + (kk & 3) * 32, 16, 1024), ID1,
+                                    kk > 0);
+                    }
+                    mma_commit(bar(B_MMA));
+                }
+                __syncwarp();
+            }
+            mma_pending = 1;
+            // 2. [T''; M] landing buffer -> TMEM (this chunk's buffer)
+            ok = chain_and(mbar_wait(bar(B_AF), c & 1, abort_s));
+            if (!ok)
+                break;
+            {
+                const int r = tid;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t w[32];
+                    const uint8_t *slab = smem + S_ATM + half * 16384;
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(slab + sw128(r, q4));
+                        w[4 * q4] = v.x;
+                        w[4 * q4 + 1] = v.y;
+                        w[4 * q4 + 2] = v.z;
+                        w[4 * q4 + 3] = v.w;
+                    }
+                    tmem_st32(((uint32_t)(warp * 32) << 16) + atm_t + half * 32, w);
+                }
+                // K^T: lane i takes column i of the K tile (rows t = 0..63)
+                const uint8_t *kcol = smem + S_KQ + s * 65536 + (r >> 5) * 16384 + (r & 3) * 4;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    uint32_t w[32];
+#pragma unroll
+                    for (int x = 0; x < 32; ++x)
+                        w[x] = *reinterpret_cast<const uint32_t *>(
+                            kcol + sw128(32 * half + x, (r & 31) >> 2));
+                    tmem_st32(((uint32_t)(warp * 32) << 16) + tmem + TM_KT + half * 32, w);
+                }
+                tmem_wait_st();
+                mbar_arrive(bar(B_AE));
+            }
+            // 3. X' = V - b X (rows 0-63); scale b Q S_0^T kept (rows 64-127)
+            ok = chain_and(mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
+            ++mma_phase;
+            mma_pending = 0;
+            if (!ok)
+                break;
+            tc_fence_after();
+            {
+                float d[32];
+                tmem_ld32(lane_base + TM_D1, d);
+                if (tid < 64) {
+                    const int t = tid;
+                    const float bt = fac[t];
+                    const uint8_t *vrow = smem + S_V + s * 8192;
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4) {
+                        const float4 v = *reinterpret_cast<const float4 *>(vrow + sw128(t, q4));
+                        uint4 w;
+                        w.x = to_tf32(fmaf(-bt, d[4 * q4], v.x));
+                        w.y = to_tf32(fmaf(-bt, d[4 * q4 + 1], v.y));
+                        w.z = to_tf32(fmaf(-bt, d[4 * q4 + 2], v.z));
+                        w.w = to_tf32(fmaf(-bt, d[4 * q4 + 3], v.w));
+                        *reinterpret_cast<uint4 *>(smem + S_XB + sw128_32b(t, q4 >> 1) +
+                                                   (q4 & 1) * 16) = w;
+                    }
+                } else {
+                    const float bs = a.scale * fac[tid - 64];
+#pragma unroll
+                    for (int jj = 0; jj < R; ++jj)
+                        yb[jj] = bs * d[jj];
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            chain_and(true);
+            // 4. MMA2: U = T'' X'
+            if (warp == 0) {
+                tc_fence_after();
+                if (elect_one()) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts_tf32(tmem + TM_D2, atm_t + kk * 8,
+                                    sdesc_mn32(xb + kk * 1024, 8192, 512), ID2, kk > 0);
+                    mma_commit(bar(B_MMA));
+                }
+                __syncwarp();
+            }
+            mma_pending = 1;
+            ok = chain_and(mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
+            ++mma_phase;
+            mma_pending = 0;
+            if (!ok)
+                break;
+            tc_fence_after();
+            if (tid < 64) {
+                float u[32];
+                tmem_ld32(lane_base + TM_D2, u);
+                const int t = tid;
+                const float et = fac[64 + t];
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4) {
+                    uint4 w, w2;
+                    w.x = to_tf32(u[4 * q4]);
+                    w.y = to_tf32(u[4 * q4 + 1]);
+                    w.z = to_tf32(u[4 * q4 + 2]);
+                    w.w = to_tf32(u[4 * q4 + 3]);
+                    w2.x = to_tf32(et * u[4 * q4]);
+                    w2.y = to_tf32(et * u[4 * q4 + 1]);
+                    w2.z = to_tf32(et * u[4 * q4 + 2]);
+                    w2.w = to_tf32(et * u[4 * q4 + 3]);
+                    const uint32_t off = sw128_32b(t, q4 >> 1) + (q4 & 1) * 16;
+                    *reinterpret_cast<uint4 *>(smem + S_UB + off) = w;
+                    *reinterpret_cast<uint4 *>(smem + S_U2 + off) = w2;
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            chain_and(true);
+            // 5. MMA3: M U (rows 64-127); MMA4: K^T diag(e) U (the state update)
+            if (warp == 0) {
+                tc_fence_after();
+                if (elect_one()) {
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts_tf32(tmem + TM_D3, atm_t + kk * 8,
+                                    sdesc_mn32(ub + kk * 1024, 8192, 512), ID2, kk > 0);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts_tf32(tmem + TM_D4, tmem + TM_KT + kk * 8,
+                                    sdesc_mn32(u2 + kk * 1024, 8192, 512), ID2, kk > 0);
+                    mma_commit(bar(B_MMA));
+                }
+                __syncwarp();
+            }
+            mma_pending = 1;
+            ok = chain_and(mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
+            ++mma_phase;
+            mma_pending = 0;
+            if (!ok)
+                break;
+            tc_fence_after();
+            // 6. S = b_C S + D4 (FP32 registers); TF32 copy for the next MMA1; y
+            {
+                float d[32];
+                tmem_ld32(lane_base + TM_D4, d);
+                const float bC = fac[128];
+                const int i = tid;
+                uint8_t *srow = smem + S_SB + (i >> 5) * 4096 + (i & 3) * 4;
+#pragma unroll
+                for (int jj = 0; jj < R; ++jj) {
+                    S[jj] = fmaf(bC, S[jj], d[jj]);
+                    *reinterpret_cast<uint32_t *>(srow + sw128(jj, (i & 31) >> 2)) = to_tf32(S[jj]);
+                }
+            }
+            if (tid >= 64) {
+                float d3[32];
+                tmem_ld32(lane_base + TM_D3, d3);
+                const int t = c * C + tid - 64;
+                if (t < a.T) {
+                    float4 *yrow = reinterpret_cast<float4 *>(
+                        a.dst + (((size_t)n * a.T + t) * a.H + h) * SK + j0);
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4)
+                        yrow[q4] = make_float4(yb[4 * q4] + d3[4 * q4], yb[4 * q4 + 1] + d3[4 * q4 + 1],
+                                               yb[4 * q4 + 2] + d3[4 * q4 + 2],
+                                               yb[4 * q4 + 3] + d3[4 * q4 + 3]);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            chain_and(true);
+            if (tid == 0)
+                mbar_arrive(bar(B_KQE + s)); // stage s (K/Q/V/factors) is free
+        }
+        if (!ok) {
+            *abort_s = 1;
+            if (mma_pending) {
+                volatile int none = 0;
+                mbar_wait(bar(B_MMA), mma_phase & 1, &none, 100000000ull);
+            }
+        } else {
+            float *so = a.state_out + (((size_t)n * a.H + h) * SK + j0) * SK + tid;
+#pragma unroll
+            for (int jj = 0; jj < R; ++jj)
+                so[(size_t)jj * SK] = S[jj];
+        }
+    }
+
+    // ---- teardown ----
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && *abort_s)
+        atomicExch(a.err, 1);
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+size_t gdn_chunk_workspace(int T, int H, int n_seq, int slots) {
+    const int nc = gc::n_chunks(T, slots);
+    if (nc < 2) // the per-token kernel runs: no workspace
+        return 0;
+    const size_t units = (size_t)nc * H * n_seq;
+    size_t b = units * (gc::ATM_FLOATS + gc::FAC_FLOATS) * 4; // [T''; M], factors
+    b += 256;                                                  // error flag
+    if (nc * gc::C < T)
+        b += (size_t)H * n_seq * gc::SK * gc::SK * 4; // state handed to the per-token kernel
+    return b;
+}
+
+static bool encode_map(CUtensorMap *m, const void *base, int rank, const cuuint64_t *dims,
+                       const cuuint64_t *strides, const cuuint32_t *box) {
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    if (!enc)
+        return false;
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void *>(base), dims, strides,
+               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+// [S, heads, T, seqs] fp32 rows, boxes of 32 elements x 64 tokens.
+static bool encode_rows(CUtensorMap *m, const float *p, int heads, int T, int seqs, int64_t nb1,
+                        int64_t nb2, int64_t nb3) {
+    const cuuint64_t dims[4] = {(cuuint64_t)gc::SK, (cuuint64_t)heads, (cuuint64_t)T,
+                                (cuuint64_t)seqs};
+    const cuuint64_t strides[3] = {(cuuint64_t)nb1, (cuuint64_t)nb2, (cuuint64_t)nb3};
+    const cuuint32_t box[4] = {32, 1, (cuuint32_t)gc::C, 1};
+    return encode_map(m, p, 4, dims, strides, box);
+}
+
+bool gdn_chunk_eligible(const GdnArgs &a) {
+    const uintptr_t bits =
+        reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+        reinterpret_cast<uintptr_t>(a.v) | (uintptr_t)a.q_nb1 | (uintptr_t)a.q_nb2 |
+        (uintptr_t)a.q_nb3 | (uintptr_t)a.k_nb1 | (uintptr_t)a.k_nb2 | (uintptr_t)a.k_nb3 |
+        (uintptr_t)a.v_nb1 | (uintptr_t)a.v_nb2 | (uintptr_t)a.v_nb3;
+    return (bits & 15) == 0 && gc::n_chunks(a.T, a.slots) >= 2 && a.H <= 65535 &&
+           a.n_seq <= 65535 && tensor_map_encoder() != nullptr;
+}
+
+cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st) {
+    using namespace gc;
+    const int nc = n_chunks(a.T, a.slots);
+    const size_t units = (size_t)nc * a.H * a.n_seq;
+    if (ws_bytes < gdn_chunk_workspace(a.T, a.H, a.n_seq, a.slots) || units * 128 > 0x7fffffffull)
+        return cudaErrorInvalidValue;
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    GdnChunkArgs c;
+    c.g = a.g;
+    c.beta = a.beta;
+    c.state = a.state;
+    c.g_nb1 = a.g_nb1; c.g_nb2 = a.g_nb2; c.g_nb3 = a.g_nb3;
+    c.b_nb1 = a.b_nb1; c.b_nb2 = a.b_nb2; c.b_nb3 = a.b_nb3;
+    c.s_nb1 = a.s_nb1; c.s_nb2 = a.s_nb2; c.s_nb3 = a.s_nb3;
+    c.atm = reinterpret_cast<float *>(w);
+    c.fac = reinterpret_cast<float *>(w + units * ATM_FLOATS * 4);
+    c.err = reinterpret_cast<int *>(w + units * (ATM_FLOATS + FAC_FLOATS) * 4);
+    const bool tail = nc * C < a.T;
+    float *handoff = reinterpret_cast<float *>(w + units * (ATM_FLOATS + FAC_FLOATS) * 4 + 256);
+    c.dst = a.dst;
+    c.state_out = tail ? handoff : a.dst + (size_t)SK * a.H * a.T * a.n_seq; // snapshot slot 0
+    c.H = a.H;
+    c.H_k = a.H_k;
+    c.T = a.T;
+    c.n_seq = a.n_seq;
+    c.rq3 = a.rq3;
+    c.rk3 = a.rk3;
+    c.NC = nc;
+    c.scale = a.scale;
+
+    CUtensorMap kmap, qmap, vmap, amap;
+    const int seq_k = a.n_seq / a.rk3, seq_q = a.n_seq / a.rq3;
+    if (!encode_rows(&kmap, a.k, a.H_k, a.T, seq_k, a.k_nb1, a.k_nb2, a.k_nb3) ||
+        !encode_rows(&qmap, a.q, a.H_k, a.T, seq_q, a.q_nb1, a.q_nb2, a.q_nb3) ||
+        !encode_rows(&vmap, a.v, a.H, a.T, a.n_seq, a.v_nb1, a.v_nb2, a.v_nb3))
+        return cudaErrorNotSupported;
+    {
+        const cuuint64_t dims[2] = {64, (cuuint64_t)units * 128};
+        const cuuint64_t strides[1] = {256};
+        const cuuint32_t box[2] = {32, 128};
+        if (!encode_map(&amap, c.atm, 2, dims, strides, box))
+            return cudaErrorNotSupported;
+    }
+    cudaError_t e = cudaMemsetAsync(c.err, 0, sizeof(int), st);
+    if (e != cudaSuccess)
+        return e;
+    static std::atomic<unsigned long long> prep_attr{0}, scan_attr{0};
+    if ((e = set_smem_limit((const void *)gdn_chunk_prep_kernel, P_BYTES, prep_attr)) !=
+            cudaSuccess ||
+        (e = set_smem_limit((const void *)gdn_chunk_scan_kernel, S_BYTES, scan_attr)) !=
+            cudaSuccess)
+        return e;
+    gdn_chunk_prep_kernel<<<dim3((unsigned)nc, (unsigned)a.H, (unsigned)a.n_seq), PREP_NT,
+                            P_BYTES, st>>>(kmap, qmap, c);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return e;
+    gdn_chunk_scan_kernel<<<dim3(SK / R, (unsigned)a.H, (unsigned)a.n_seq), SCAN_NT, S_BYTES,
+                            st>>>(kmap, qmap, vmap, amap, c);
+    if ((e = cudaGetLastError()) != cudaSuccess)
+        return e;
+    if (tail) {
+        // the last tokens (the snapshot slots) one at a time from the handed-off state
+        GdnArgs r = a;
+        r.t_begin = nc * C;
+        r.state = handoff;
+        r.s_nb1 = SK * 4;
+        r.s_nb2 = (int64_t)SK * SK * 4;
+        r.s_nb3 = (int64_t)a.H * SK * SK * 4;
+        return launch_gdn(r, st);
+    }
+    return cudaSuccess;
+}
+
+} // namespace xq

@@ -112,8 +112,16 @@ struct GdnArgs {
     float *dst;
     int H, H_k, T, n_seq, rq3, rk3, slots;
     float scale;
+    int t_begin = 0; // tokens before this one are already folded into `state`
 };
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st);
+// Chunked (WY) form on the tensor cores for long sequences: workspace bytes
+// (0 when the shape has fewer than one chunk), eligibility (16-byte aligned
+// q/k/v rows, at least two chunks) and the launch (prep, scan, and the
+// per-token kernel for the snapshot tail).
+size_t gdn_chunk_workspace(int T, int H, int n_seq, int slots);
+bool gdn_chunk_eligible(const GdnArgs &a);
+cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st);
 
 cudaError_t launch_dequant(int type, const void *src, uint64_t src_stride, float *dst,
                            uint64_t dst_stride, int64_t n_rows, int64_t n_per_row,

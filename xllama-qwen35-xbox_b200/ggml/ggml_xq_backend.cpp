@@ -321,9 +321,13 @@ ggml_status run_gdn(BackendCtx *c, ggml_tensor *op) {
     xq_tensor t[6];
     for (int i = 0; i < 6; ++i)
         t[i] = xt(op->src[i]);
-    if (xq_gated_delta_net(&t[0], &t[1], &t[2], &t[3], &t[4], &t[5],
-                           static_cast<float *>(op->data), op->op_params[0],
-                           reinterpret_cast<xq_stream_t>(c->stream))) {
+    // long prefill runs the chunked tensor-core form (workspace on the backend)
+    const size_t need = xq_gated_delta_net_workspace(&t[2], op->op_params[0]);
+    if (!ensure_ws(c, need))
+        return GGML_STATUS_ALLOC_FAILED;
+    if (xq_gated_delta_net_ws(&t[0], &t[1], &t[2], &t[3], &t[4], &t[5],
+                              static_cast<float *>(op->data), op->op_params[0], c->ws,
+                              c->ws_bytes, reinterpret_cast<xq_stream_t>(c->stream))) {
         log_err("GATED_DELTA_NET", xq_last_error());
         return GGML_STATUS_FAILED;
     }

@@ -20,6 +20,7 @@ EXPORTS = (
     "xq_flash_attn_ext_workspace", "xq_flash_attn_ext", "xq_fa_partials", "xq_lse_merge",
     "xq_lse_merge_records",
     "xq_attend_range_workspace", "xq_attend_range", "xq_split_k", "xq_gated_delta_net",
+    "xq_gated_delta_net_workspace", "xq_gated_delta_net_ws",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
     "xq_flash_attn_ext_noalloc", "xq_set_rows",
 )
@@ -67,6 +68,8 @@ def lib():
                                       u32, vp, vp, vp, sz, vp]),
         "xq_split_k": (u32, [u32, u32]),
         "xq_gated_delta_net": (C.c_int, [P(Tensor)] * 6 + [vp, i32, vp]),
+        "xq_gated_delta_net_workspace": (sz, [P(Tensor), i32]),
+        "xq_gated_delta_net_ws": (C.c_int, [P(Tensor)] * 6 + [vp, i32, vp, sz, vp]),
         "xq_dequantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_quantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_flash_attn_ext_noalloc": (C.c_int, [P(FaParams), vp]),

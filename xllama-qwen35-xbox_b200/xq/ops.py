@@ -229,18 +229,29 @@ def attend_range(storage: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor
     return out, lse
 
 
-def gated_delta_net(q, k, v, g, beta, state, slots: int = 1, out=None, stream=None):
+def gated_delta_net(q, k, v, g, beta, state, slots: int = 1, out=None, stream=None,
+                    chunked: bool = True):
     """GGML_OP_GATED_DELTA_NET.  q, k (n_seq_qk, T, H_k, S); v (n_seq, T, H, S);
     g, beta (n_seq, T, H, 1); state (n_seq, H, S, S).  Returns
-    (dst_flat, y (n_seq, T, H, S), snapshots (K, n_seq, H, S, S))."""
+    (dst_flat, y (n_seq, T, H, S), snapshots (K, n_seq, H, S, S)).
+    chunked: long sequences take the tensor-core chunked form
+    (xq_gated_delta_net_ws, TF32 products); False keeps the per-token FP32
+    recurrence (xq_gated_delta_net) at every length."""
     n_seq, T, H, S = v.shape
     n_y = S * H * T * n_seq
     n_snap = slots * S * S * H * n_seq
     dst = out if out is not None else torch.empty(n_y + n_snap, dtype=torch.float32,
                                                   device=v.device)
     ts = [_dense(t) for t in (q, k, v, g, beta, state)]
-    check(lib().xq_gated_delta_net(*[C.byref(t) for t in ts], dst.data_ptr(), slots,
-                                   _stream(stream)))
+    refs = [C.byref(t) for t in ts]
+    if chunked:
+        nbytes = lib().xq_gated_delta_net_workspace(refs[2], slots)
+        ws = _workspace(nbytes, v.device)
+        check(lib().xq_gated_delta_net_ws(*refs, dst.data_ptr(), slots,
+                                          ws.data_ptr() if ws is not None else None,
+                                          ws.numel() if ws is not None else 0, _stream(stream)))
+    else:
+        check(lib().xq_gated_delta_net(*refs, dst.data_ptr(), slots, _stream(stream)))
     return dst, dst[:n_y].view(n_seq, T, H, S), dst[n_y:].view(slots, n_seq, H, S, S)
 
 
