@@ -451,11 +451,14 @@ def run_gdn(args, torch, workload):
                          "inputs %.0f MB > L2" % (step_bytes / 1e6)},
         "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": hbm, "unit": "GB/s",
                      "frac": round(value / hbm, 4), "peak_kind": peak_kind,
-                     "kernel": "gdn_kernel", "traffic": profile_traffic("gdn_" + workload)},
+                     "kernel": ("gdn_recurrent_kernel" if workload == "c3a" else
+                                "gdn_chunk_prep_kernel + gdn_chunk_scan_kernel"),
+                     "traffic": profile_traffic("gdn_" + workload)},
         "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": in_bytes,
                 "d2h_bytes_per_step": y_bytes},
-        "gpu_launches": args.steps,
+        # decode: one recurrent kernel; prefill: the chunked prep and scan kernels
+        "gpu_launches": args.steps * (1 if workload == "c3a" else 2),
         "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
         "clocks": clocks,
     }

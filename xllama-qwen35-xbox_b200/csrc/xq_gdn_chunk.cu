@@ -23,19 +23,22 @@
 //     forward substitution, then block rows), and writes [T''; M] (128 x 64)
 //     plus b, e, b_C to the workspace.
 //   gdn_chunk_scan_kernel  one CTA per (32 state rows, head, sequence),
-//     sequential over chunks with the state in registers (thread i holds
-//     column i of the 32 rows) and an operand copy in shared memory:
+//     sequential over chunks with the state in FP32 registers (two threads
+//     per TMEM lane i, 16 of the 32 rows each) and a TF32 copy in shared
+//     memory as the B operand of MMA1:
 //       MMA1  [K;Q] S_0^T          SS, M=128 (64 K rows + 64 Q rows), N=32, K=128
 //       MMA2  [T'';M] X'           TS, A in TMEM, B = X' MN-major, K=64
+//       MMA4  K^T (diag(e) U)      TS (M=128 over the key elements): the
+//                                  state update
 //       MMA3  [T'';M] U            TS (rows 64..127: M U lands on the lanes
-//                                  holding scale b Q S_0^T)
-//       MMA4  K^T (diag(e) U)      TS, K^T copied into TMEM by the chain
-//                                  threads (M=128 over the key elements)
+//                                  holding scale b Q S_0^T), the output
 //     MN-major TF32 operands (X', U, diag(e) U) use the 128-byte swizzle with
 //     32-byte granules, the only MN-major layout for 32-bit elements; K-major
-//     operands use the plain 128-byte swizzle TMA writes.
-//     A warp-specialised TMA producer double-buffers K/Q/V tiles and streams
-//     [T''; M] through one landing buffer into TMEM.
+//     operands use the plain 128-byte swizzle TMA writes.  Warp roles: 8
+//     chain warps, 4 copier warps that move the next chunk's [T''; M] rows and
+//     K^T into double-buffered TMEM, and a producer warp whose three lanes
+//     stream K/Q tiles, V tiles + factors and [T''; M] independently.  Each
+//     chunk's output leaves by TMA store while the next chunk's MMA1 runs.
 // Operands produced here (S, X', U, T'', M) are rounded to TF32 to nearest;
 // K, Q, V tiles enter the tensor core as stored (fp32 read as TF32).  Tokens
 // past T read as zeros with g = beta = 0, so a partial last chunk is exact.
@@ -59,14 +62,15 @@ constexpr int AST = 68;      // padded row stride (floats) of the solve matrices
 constexpr int ATM_FLOATS = 128 * 64; // [T''; M] per unit
 constexpr int FAC_FLOATS = 256;      // b[64], e[64], b_C, pad
 constexpr int PREP_NT = 128;
-constexpr int SCAN_NT = 160;         // 4 chain warps + 1 producer warp
+constexpr int SCAN_NT = 416;         // 8 chain warps, 4 copier warps, 1 producer warp
 constexpr float kLog2e = 1.4426950408889634f;
 
-// prep kernel shared memory
+// prep kernel shared memory (3 CTAs per SM): the solve matrices reuse the
+// K/Q tile once the tensor core has read it
 constexpr int P_KQ = 0;                       // 4 slabs x 16 KB, rows 0-63 K, 64-127 Q
-constexpr int P_AM = 65536;                   // A [64][AST]
-constexpr int P_TT = P_AM + 64 * AST * 4;     // T transposed [col][row]
-constexpr int P_G = P_TT + 64 * AST * 4;      // G[64], beta[64]
+constexpr int P_AM = 0;                       // A [64][AST]            (after the MMA)
+constexpr int P_TT = P_AM + 64 * AST * 4;     // T transposed [col][row] (after the MMA)
+constexpr int P_G = 65536;                    // G[64], beta[64]
 constexpr int P_BAR = P_G + 512;
 constexpr int P_BYTES = P_BAR + 32 + 1024;    // + alignment slack
 
@@ -80,12 +84,12 @@ constexpr int S_UB = 204800;                  // U
 constexpr int S_U2 = 212992;                  // diag(e) U
 constexpr int S_FAC = 221184;                 // 2 stages x 1 KB
 constexpr int S_BAR = 223232;
-constexpr int S_BYTES = S_BAR + 64 + 1024;
+constexpr int S_BYTES = S_BAR + 160 + 1024;
 
-// scan kernel TMEM columns
-constexpr uint32_t TM_ATM = 0;  // [T''; M], 2 buffers x 64
-constexpr uint32_t TM_KT = 128; // K^T (lane i, column t): A of the state update
-constexpr uint32_t TM_D1 = 192, TM_D2 = 224, TM_D3 = 256, TM_D4 = 288;
+// scan kernel TMEM columns (A operands copied in by the copier warps)
+constexpr uint32_t TM_ATM = 0;   // [T''; M], 2 buffers x 64
+constexpr uint32_t TM_KT = 128;  // K^T (lane i, column t), 2 buffers x 64
+constexpr uint32_t TM_D1 = 256, TM_D2 = 288, TM_D3 = 320, TM_D4 = 352;
 constexpr uint32_t TM_COLS = 512;
 
 __host__ __device__ constexpr int n_chunks(int T, int slots) {
@@ -99,16 +103,6 @@ __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
 }
 __device__ __forceinline__ const float *at(const float *base, int64_t off) {
     return reinterpret_cast<const float *>(reinterpret_cast<const char *>(base) + off);
-}
-// AND of `ok` over the 128 chain threads (named barrier 1).
-__device__ __forceinline__ bool chain_and(bool ok) {
-    uint32_t r;
-    asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\n"
-                 "bar.red.and.pred q, 1, 128, p;\nselp.u32 %0, 1, 0, q;\n}\n"
-                 : "=r"(r)
-                 : "r"((uint32_t)ok)
-                 : "memory");
-    return r != 0;
 }
 } // namespace gc
 
@@ -127,50 +121,60 @@ struct GdnChunkArgs {
 // ---------------------------------------------------------------------------
 // Per-chunk preparation.
 
-// Block row BI of T = (I + A)^-1 for this thread's column cc (BI > cc / 16):
-// E = A[16BI.., :16BI] T[:16BI, cc], then T[16BI + r, cc] = -(D_BI E)_r with
-// D_BI = T[16BI.., 16BI..] (already in Tt).  Tt is column-major: Tt[cc][row].
+// Block row BI of T = (I + A)^-1 for column cc, two lanes per column (hh =
+// which 8 of the block's 16 rows): E = A[16BI.., :16BI] T[:16BI, cc], then
+// T[16BI + r, cc] = -(D_BI E)_r with D_BI = T[16BI.., 16BI..] (already in
+// Tt).  Tt is column-major: Tt[col][row].  The partner lane is lane ^ 16.
 template <int BI>
-__device__ __forceinline__ void solve_block_row(const float *Am, float *Tt, int cc) {
+__device__ __forceinline__ void solve_block_row(const float *Am, float *Tt, int cc, int hh) {
     using namespace gc;
-    float e[16];
+    float e[8];
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
+    for (int r = 0; r < 8; ++r)
         e[r] = 0.0f;
     const float *tcol = Tt + cc * AST;
+    const float *arow = Am + (16 * BI + 8 * hh) * AST;
 #pragma unroll
     for (int m4 = 0; m4 < 4 * BI; ++m4) {
         const float4 tv = *reinterpret_cast<const float4 *>(tcol + 4 * m4);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const float4 av =
-                *reinterpret_cast<const float4 *>(Am + (16 * BI + r) * AST + 4 * m4);
+        for (int r = 0; r < 8; ++r) {
+            const float4 av = *reinterpret_cast<const float4 *>(arow + r * AST + 4 * m4);
             e[r] = fmaf(av.x, tv.x, e[r]);
             e[r] = fmaf(av.y, tv.y, e[r]);
             e[r] = fmaf(av.z, tv.z, e[r]);
             e[r] = fmaf(av.w, tv.w, e[r]);
         }
     }
-    float o[16];
+    float E[16];
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
+    for (int r = 0; r < 8; ++r) {
+        const float other = __shfl_xor_sync(0xffffffffu, e[r], 16);
+        E[r] = hh ? other : e[r];
+        E[8 + r] = hh ? e[r] : other;
+    }
+    float o[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
         o[r] = 0.0f;
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
-        const float *dcol = Tt + (16 * BI + m) * AST + 16 * BI; // D[:, m] (zero above)
-#pragma unroll
-        for (int r4 = 0; r4 < 4; ++r4) {
-            const float4 d = *reinterpret_cast<const float4 *>(dcol + 4 * r4);
-            o[4 * r4] = fmaf(d.x, e[m], o[4 * r4]);
-            o[4 * r4 + 1] = fmaf(d.y, e[m], o[4 * r4 + 1]);
-            o[4 * r4 + 2] = fmaf(d.z, e[m], o[4 * r4 + 2]);
-            o[4 * r4 + 3] = fmaf(d.w, e[m], o[4 * r4 + 3]);
-        }
+        // D[8hh + r][m] for r = 0..7 (zero above the diagonal)
+        const float *dcol = Tt + (16 * BI + m) * AST + 16 * BI + 8 * hh;
+        const float4 d0 = *reinterpret_cast<const float4 *>(dcol);
+        const float4 d1 = *reinterpret_cast<const float4 *>(dcol + 4);
+        o[0] = fmaf(d0.x, E[m], o[0]);
+        o[1] = fmaf(d0.y, E[m], o[1]);
+        o[2] = fmaf(d0.z, E[m], o[2]);
+        o[3] = fmaf(d0.w, E[m], o[3]);
+        o[4] = fmaf(d1.x, E[m], o[4]);
+        o[5] = fmaf(d1.y, E[m], o[5]);
+        o[6] = fmaf(d1.z, E[m], o[6]);
+        o[7] = fmaf(d1.w, E[m], o[7]);
     }
-#pragma unroll
-    for (int r4 = 0; r4 < 4; ++r4)
-        *reinterpret_cast<float4 *>(Tt + cc * AST + 16 * BI + 4 * r4) =
-            make_float4(-o[4 * r4], -o[4 * r4 + 1], -o[4 * r4 + 2], -o[4 * r4 + 3]);
+    float *out = Tt + cc * AST + 16 * BI + 8 * hh;
+    *reinterpret_cast<float4 *>(out) = make_float4(-o[0], -o[1], -o[2], -o[3]);
+    *reinterpret_cast<float4 *>(out + 4) = make_float4(-o[4], -o[5], -o[6], -o[7]);
 }
 
 __global__ void __launch_bounds__(gc::PREP_NT)
@@ -330,28 +334,42 @@ __global__ void __launch_bounds__(gc::PREP_NT)
                 make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
     }
     __syncthreads(); // every diagonal block is in Tt
+    if (warp < 3) {
+        // warp j: the block rows below diagonal block j of its 16 columns
+        const int j = warp, hh = lane >> 4, cc = 16 * j + (lane & 15);
+        if (j < 1)
+            solve_block_row<1>(Am, Tt, cc, hh);
+        __syncwarp();
+        if (j < 2)
+            solve_block_row<2>(Am, Tt, cc, hh);
+        __syncwarp();
+        solve_block_row<3>(Am, Tt, cc, hh);
+    }
+    __syncthreads(); // T complete
+    {
+        // T'' = T diag(beta) as rows 0-63 of [T''; M]: thread (column s, half
+        // of the rows) reads its column of Tt 4 rows at a time; every warp
+        // store covers 128 contiguous bytes of one row
+        const int sc = tid & 63, t0r = 32 * (tid >> 6);
+        const float bc = Bs[sc];
+        const float *tcol = Tt + sc * AST + t0r;
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) {
+            const float4 v = *reinterpret_cast<const float4 *>(tcol + 4 * t4);
+            float *o = atm + (t0r + 4 * t4) * 64 + sc;
+            o[0] = __uint_as_float(to_tf32(v.x * bc));
+            o[64] = __uint_as_float(to_tf32(v.y * bc));
+            o[128] = __uint_as_float(to_tf32(v.z * bc));
+            o[192] = __uint_as_float(to_tf32(v.w * bc));
+        }
+    }
     if (tid < 64) {
-        const int cc = tid, bj = cc >> 4;
-        // block rows below the thread's own diagonal block, in order: row BI
-        // reads only this thread's column (rows < 16 BI) and D_BI
-        if (bj < 1)
-            solve_block_row<1>(Am, Tt, cc);
-        if (bj < 2)
-            solve_block_row<2>(Am, Tt, cc);
-        if (bj < 3)
-            solve_block_row<3>(Am, Tt, cc);
-        // T'' = T diag(beta): column cc scaled by beta_cc, rows 0-63 of [T''; M]
-        const float bc = Bs[cc];
-        const float *tcol = Tt + cc * AST;
-#pragma unroll 8
-        for (int t = 0; t < 64; ++t)
-            atm[t * 64 + cc] = __uint_as_float(to_tf32(tcol[t] * bc));
         // decay factors
         float *fac = a.fac + unit * FAC_FLOATS;
-        const float Gt = Gs[cc], GC = Gs[63];
-        fac[cc] = ex2(Gt * kLog2e);
-        fac[64 + cc] = ex2((GC - Gt) * kLog2e);
-        if (cc == 0)
+        const float Gt = Gs[tid], GC = Gs[63];
+        fac[tid] = ex2(Gt * kLog2e);
+        fac[64 + tid] = ex2((GC - Gt) * kLog2e);
+        if (tid == 0)
             fac[128] = ex2(GC * kLog2e);
     }
 
@@ -373,25 +391,34 @@ __global__ void __launch_bounds__(gc::PREP_NT)
 }
 
 // ---------------------------------------------------------------------------
-// Sequential scan over chunks.
-
+// Sequential scan over chunks, warp-specialised:
+//   warps 0-7   chain: TMEM lane quarter (warp & 3), state columns
+//               16 (warp >> 2) .. +15 of the CTA's 32; warp 0 issues the MMAs
+//   warps 8-11  copier: [T''; M] rows and K^T into TMEM (double-buffered) for
+//               the chunk after the one the chain works on
+//   warp 12     producer: lane 0 K/Q tiles, lane 1 V tile + factors, lane 2
+//               the [T''; M] landing buffer
 __global__ void __launch_bounds__(gc::SCAN_NT, 1)
     gdn_chunk_scan_kernel(const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap qmap,
                           const __grid_constant__ CUtensorMap vmap,
-                          const __grid_constant__ CUtensorMap amap, const GdnChunkArgs a) {
+                          const __grid_constant__ CUtensorMap amap,
+                          const __grid_constant__ CUtensorMap ymap, const GdnChunkArgs a) {
     using namespace tc;
     using namespace gc;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = align1024(smem_raw);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S_BAR);
-    // bars: full[2], kq_empty[2], atm_full, atm_empty, mma
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
     volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
     auto bar = [&](int i) { return smem_u32(bars + i); };
-    constexpr int B_FULL = 0, B_KQE = 2, B_AF = 4, B_AE = 5, B_MMA = 6;
+    // kq_full[2], vf_full[2], kq_empty[2] (MMA1 done + K^T copied),
+    // vf_empty[2], atm_full, atm_empty, tmem_ready[2] (copier -> chain),
+    // tmem_free[2] (chain -> copier), mma (MMA1/MMA2/MMA4), mma3
+    constexpr int B_KQF = 0, B_VFF = 2, B_KQE = 4, B_VFE = 6, B_AF = 8, B_AE = 9, B_TR = 10,
+                  B_TF = 12, B_MMA = 14, B_MMA3 = 15;
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slice = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
     const int j0 = slice * R, hk = h % a.H_k;
     const size_t unit0 = ((size_t)n * a.H + h) * a.NC;
@@ -401,29 +428,39 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
         prefetch_map(&qmap);
         prefetch_map(&vmap);
         prefetch_map(&amap);
-        for (int i = 0; i < 4; ++i)
-            mbar_init(bar(i), 1);
+        prefetch_map(&ymap);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar(B_KQF + i), 1);
+            mbar_init(bar(B_VFF + i), 1);
+            mbar_init(bar(B_KQE + i), 1 + 128); // chain (MMA1 done) + copier threads
+            mbar_init(bar(B_VFE + i), 1);
+            mbar_init(bar(B_TR + i), 128);
+            mbar_init(bar(B_TF + i), 1);
+        }
         mbar_init(bar(B_AF), 1);
         mbar_init(bar(B_AE), 128);
         mbar_init(bar(B_MMA), 1);
+        mbar_init(bar(B_MMA3), 1);
         *abort_s = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 0)
         tmem_alloc(smem_u32(tmem_slot), TM_COLS);
 
-    // state rows j0..j0+31, column i = tid, kept in FP32 registers; the
-    // operand copy (TF32) goes to the K-major S tile: row j, K index i
-    float S[R];
-    if (tid < 128) {
+    // chain thread (row r = TMEM lane, column half hc) holds state rows
+    // j0 + 16 hc .. +15 at column i = r in FP32 registers; the TF32 operand
+    // copy goes to the K-major S tile (row j, K index i)
+    const int r = 32 * (warp & 3) + lane, hc = (warp >> 2) & 1;
+    float S[16];
+    if (warp < 8) {
         const float *sp = at(a.state, n * a.s_nb3 + (int64_t)h * a.s_nb2);
-        const int i = tid;
 #pragma unroll
-        for (int jj = 0; jj < R; ++jj) {
-            S[jj] = *at(sp, (int64_t)(j0 + jj) * a.s_nb1 + 4 * i);
-            *reinterpret_cast<uint32_t *>(smem + S_SB + (i >> 5) * 4096 +
-                                          sw128(jj, (i & 31) >> 2) + (i & 3) * 4) =
-                to_tf32(S[jj]);
+        for (int jj = 0; jj < 16; ++jj) {
+            const int j = 16 * hc + jj;
+            S[jj] = *at(sp, (int64_t)(j0 + j) * a.s_nb1 + 4 * r);
+            *reinterpret_cast<uint32_t *>(smem + S_SB + (r >> 5) * 4096 +
+                                          sw128(j, (r & 31) >> 2) + (r & 3) * 4) =
+                to_tf32_fast(S[jj]);
         }
         fence_async_smem();
     }
@@ -431,71 +468,167 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    int mma_pending = 0, mma_phase = 0;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
 
-    if (warp == 4) {
+    if (warp == 12) {
         // ----------------------------- producer -----------------------------
-        if (threadIdx.x % 32 == 0) {
-            int kq_issued = 0, atm_issued = 0;
+        if (lane < 3) {
+            int issued = 0;
             for (int c = 0; c < a.NC; ++c) {
-                const int s = c & 1;
-                if (c >= 2 && !mbar_wait(bar(B_KQE + s), ((c >> 1) - 1) & 1, abort_s)) {
-                    *abort_s = 1;
-                    break;
-                }
-                const uint32_t fb = bar(B_FULL + s);
-                mbar_expect_tx(fb, 65536 + 8192 + 1024);
-                const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
+                const int s = c & 1, use = c >> 1;
+                if (lane == 0) {
+                    if (use >= 1 && !mbar_wait(bar(B_KQE + s), (use - 1) & 1, abort_s))
+                        break;
+                    mbar_expect_tx(bar(B_KQF + s), 65536);
+                    const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
 #pragma unroll
-                for (int ib = 0; ib < 4; ++ib) {
-                    tma_load_4d(kq + ib * 16384, &kmap, 32 * ib, hk, c * C, n / a.rk3, fb);
-                    tma_load_4d(kq + ib * 16384 + 8192, &qmap, 32 * ib, hk, c * C, n / a.rq3,
-                                fb);
+                    for (int ib = 0; ib < 4; ++ib) {
+                        tma_load_4d(kq + ib * 16384, &kmap, 32 * ib, hk, c * C, n / a.rk3,
+                                    bar(B_KQF + s));
+                        tma_load_4d(kq + ib * 16384 + 8192, &qmap, 32 * ib, hk, c * C,
+                                    n / a.rq3, bar(B_KQF + s));
+                    }
+                } else if (lane == 1) {
+                    if (use >= 1 && !mbar_wait(bar(B_VFE + s), (use - 1) & 1, abort_s))
+                        break;
+                    mbar_expect_tx(bar(B_VFF + s), 8192 + 1024);
+                    tma_load_4d(smem_u32(smem + S_V + s * 8192), &vmap, j0, h, c * C, n,
+                                bar(B_VFF + s));
+                    bulk_load(smem_u32(smem + S_FAC + s * 1024),
+                              a.fac + (unit0 + c) * FAC_FLOATS, 1024, bar(B_VFF + s));
+                } else {
+                    if (c >= 1 && !mbar_wait(bar(B_AE), (c - 1) & 1, abort_s))
+                        break;
+                    mbar_expect_tx(bar(B_AF), 32768);
+                    const int row = (int)((unit0 + c) * 128);
+                    tma_load_2d(smem_u32(smem + S_ATM), &amap, 0, row, bar(B_AF));
+                    tma_load_2d(smem_u32(smem + S_ATM + 16384), &amap, 32, row, bar(B_AF));
                 }
-                tma_load_4d(smem_u32(smem + S_V + s * 8192), &vmap, j0, h, c * C, n, fb);
-                bulk_load(smem_u32(smem + S_FAC + s * 1024), a.fac + (unit0 + c) * FAC_FLOATS,
-                          1024, fb);
-                ++kq_issued;
-                if (c >= 1 && !mbar_wait(bar(B_AE), (c - 1) & 1, abort_s)) {
-                    *abort_s = 1;
-                    break;
-                }
-                mbar_expect_tx(bar(B_AF), 32768);
-                const int row = (int)((unit0 + c) * 128);
-                tma_load_2d(smem_u32(smem + S_ATM), &amap, 0, row, bar(B_AF));
-                tma_load_2d(smem_u32(smem + S_ATM + 16384), &amap, 32, row, bar(B_AF));
-                ++atm_issued;
+                issued = c + 1;
             }
-            if (*abort_s) {
-                // copies still in flight land on their barriers: bounded drain
+            if (issued < a.NC) {
+                // a wait failed: stop everyone, then let this lane's copies in
+                // flight complete their barriers (bounded)
+                *abort_s = 1;
                 volatile int none = 0;
-                for (int m = kq_issued - 2 < 0 ? 0 : kq_issued - 2; m < kq_issued; ++m)
-                    mbar_wait(bar(B_FULL + (m & 1)), (m >> 1) & 1, &none, 100000000ull);
-                if (atm_issued > 0)
-                    mbar_wait(bar(B_AF), (atm_issued - 1) & 1, &none, 100000000ull);
+                for (int m = issued - 2 < 0 ? 0 : issued - 2; m < issued; ++m) {
+                    if (lane == 0)
+                        mbar_wait(bar(B_KQF + (m & 1)), (m >> 1) & 1, &none, 100000000ull);
+                    else if (lane == 1)
+                        mbar_wait(bar(B_VFF + (m & 1)), (m >> 1) & 1, &none, 100000000ull);
+                    else if (m == issued - 1)
+                        mbar_wait(bar(B_AF), m & 1, &none, 100000000ull);
+                }
             }
         }
+    } else if (warp >= 8) {
+        // ------------------------------ copier ------------------------------
+        uint32_t w[16];
+        for (int cn = 0; cn < a.NC; ++cn) {
+            const int b = cn & 1;
+            bool ok = mbar_wait(bar(B_KQF + b), (cn >> 1) & 1, abort_s) &&
+                      mbar_wait(bar(B_AF), cn & 1, abort_s) &&
+                      (cn < 2 || mbar_wait(bar(B_TF + b), ((cn >> 1) - 1) & 1, abort_s));
+            if (!ok) {
+                *abort_s = 1;
+                break;
+            }
+            tc_fence_after();
+            // [T''; M] row r -> TMEM buffer b (A of MMA2 / MMA3)
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+                for (int hq = 0; hq < 2; ++hq) {
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(
+                            smem + S_ATM + half * 16384 + sw128(r, 4 * hq + q4));
+                        w[4 * q4] = v.x;
+                        w[4 * q4 + 1] = v.y;
+                        w[4 * q4 + 2] = v.z;
+                        w[4 * q4 + 3] = v.w;
+                    }
+                    tmem_st16(lane_base + TM_ATM + 64 * b + 32 * half + 16 * hq, w);
+                }
+            // K^T: lane r takes column r of the K tile (rows t = 0..63), the A
+            // operand of MMA4
+            const uint8_t *kcol = smem + S_KQ + b * 65536 + (r >> 5) * 16384 + (r & 3) * 4;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                for (int x = 0; x < 16; ++x)
+                    w[x] = *reinterpret_cast<const uint32_t *>(
+                        kcol + sw128(16 * q + x, (r & 31) >> 2));
+                tmem_st16(lane_base + TM_KT + 64 * b + 16 * q, w);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(B_AE));     // the landing buffer is free
+            mbar_arrive(bar(B_KQE + b)); // this thread is done with the K tile
+            mbar_arrive(bar(B_TR + b));  // the chain may use TMEM buffer b
+        }
     } else {
-        // ---------------------- chain (TMEM lanes 0-127) ----------------------
+        // ------------------------------- chain --------------------------------
         constexpr uint32_t ID1 = idesc_tf32(128, R, 0, 0);
         constexpr uint32_t ID2 = idesc_tf32(128, R, 0, 1);
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
         const uint32_t sb = smem_u32(smem + S_SB), xb = smem_u32(smem + S_XB),
                        ub = smem_u32(smem + S_UB), u2 = smem_u32(smem + S_U2);
+        auto chain_and = [](bool v) {
+            uint32_t res;
+            asm volatile("{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\n"
+                         "bar.red.and.pred q, 1, 256, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+                         : "=r"(res)
+                         : "r"((uint32_t)v)
+                         : "memory");
+            return res != 0;
+        };
+        int mma_pending = 0, mma_phase = 0, mma3_phase = 0, y_pending = 0;
+        float yb[16];
+        // y of chunk cy = scale b Q S_0^T (yb, rows 64-127) + M U (MMA3),
+        // 128-byte swizzled into the X' buffer and stored by TMA; MMA3 done
+        // also frees TMEM buffer cy & 1 for the copier
+        auto emit_y = [&](int cy) -> bool {
+            if (!chain_and(mbar_wait(bar(B_MMA3), mma3_phase & 1, abort_s)))
+                return false;
+            ++mma3_phase;
+            tc_fence_after();
+            if (tid == 0)
+                mbar_arrive(bar(B_TF + (cy & 1)));
+            if (r >= 64) {
+                float d3[16];
+                tmem_ld16(lane_base + TM_D3 + 16 * hc, d3);
+                const int t = r - 64;
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4)
+                    *reinterpret_cast<float4 *>(smem + S_XB + sw128(t, 4 * hc + q4)) =
+                        make_float4(yb[4 * q4] + d3[4 * q4], yb[4 * q4 + 1] + d3[4 * q4 + 1],
+                                    yb[4 * q4 + 2] + d3[4 * q4 + 2],
+                                    yb[4 * q4 + 3] + d3[4 * q4 + 3]);
+            }
+            fence_async_smem();
+            chain_and(true);
+            if (tid == 0) {
+                // rows past T fall outside the map and are not written
+                tma_store_4d(&ymap, xb, j0, h, cy * C, n);
+                bulk_commit();
+                y_pending = 1;
+            }
+            return true;
+        };
         bool ok = true;
-        float yb[R];
         for (int c = 0; c < a.NC && ok; ++c) {
             const int s = c & 1;
-            const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
-            const uint32_t atm_t = tmem + TM_ATM + (uint32_t)(c & 1) * 64;
+            const uint32_t atm_t = tmem + TM_ATM + (uint32_t)s * 64;
+            const uint32_t kt_t = tmem + TM_KT + (uint32_t)s * 64;
             const float *fac = reinterpret_cast<const float *>(smem + S_FAC + s * 1024);
-            // 1. chunk inputs, MMA1: D1 = [K; Q] S_0^T
-            ok = chain_and(mbar_wait(bar(B_FULL + s), (c >> 1) & 1, abort_s));
+            // 1. MMA1: D1 = [K; Q] S_0^T (both operands in shared memory)
+            ok = chain_and(mbar_wait(bar(B_KQF + s), (c >> 1) & 1, abort_s));
             if (!ok)
                 break;
             if (warp == 0) {
                 tc_fence_after();
                 if (elect_one()) {
+                    const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
 #pragma unroll
                     for (int kk = 0; kk < 16; ++kk) {
                         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -508,76 +641,58 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                 __syncwarp();
             }
             mma_pending = 1;
-            // 2. [T''; M] landing buffer -> TMEM (this chunk's buffer)
-            ok = chain_and(mbar_wait(bar(B_AF), c & 1, abort_s));
-            if (!ok)
+            // the previous chunk's output while MMA1 runs
+            if (c > 0 && !emit_y(c - 1)) {
+                ok = false;
                 break;
-            {
-                const int r = tid;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t w[32];
-                    const uint8_t *slab = smem + S_ATM + half * 16384;
-#pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
-                        const uint4 v = *reinterpret_cast<const uint4 *>(slab + sw128(r, q4));
-                        w[4 * q4] = v.x;
-                        w[4 * q4 + 1] = v.y;
-                        w[4 * q4 + 2] = v.z;
-                        w[4 * q4 + 3] = v.w;
-                    }
-                    tmem_st32(((uint32_t)(warp * 32) << 16) + atm_t + half * 32, w);
-                }
-                // K^T: lane i takes column i of the K tile (rows t = 0..63)
-                const uint8_t *kcol = smem + S_KQ + s * 65536 + (r >> 5) * 16384 + (r & 3) * 4;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    uint32_t w[32];
-#pragma unroll
-                    for (int x = 0; x < 32; ++x)
-                        w[x] = *reinterpret_cast<const uint32_t *>(
-                            kcol + sw128(32 * half + x, (r & 31) >> 2));
-                    tmem_st32(((uint32_t)(warp * 32) << 16) + tmem + TM_KT + half * 32, w);
-                }
-                tmem_wait_st();
-                mbar_arrive(bar(B_AE));
             }
-            // 3. X' = V - b X (rows 0-63); scale b Q S_0^T kept (rows 64-127)
-            ok = chain_and(mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
+            if (tid == 0 && y_pending) {
+                bulk_wait_read(); // the y tile has left the X' buffer
+                y_pending = 0;
+            }
+            ok = chain_and(mbar_wait(bar(B_VFF + s), (c >> 1) & 1, abort_s) &&
+                           mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
             ++mma_phase;
             mma_pending = 0;
             if (!ok)
                 break;
             tc_fence_after();
+            if (tid == 0)
+                mbar_arrive(bar(B_KQE + s)); // MMA1 has read the K/Q tiles
+            // 2. X' = V - b X (rows 0-63); scale b Q S_0^T kept (rows 64-127)
             {
-                float d[32];
-                tmem_ld32(lane_base + TM_D1, d);
-                if (tid < 64) {
-                    const int t = tid;
+                float d[16];
+                tmem_ld16(lane_base + TM_D1 + 16 * hc, d);
+                if (r < 64) {
+                    const int t = r;
                     const float bt = fac[t];
                     const uint8_t *vrow = smem + S_V + s * 8192;
 #pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) {
-                        const float4 v = *reinterpret_cast<const float4 *>(vrow + sw128(t, q4));
-                        uint4 w;
-                        w.x = to_tf32(fmaf(-bt, d[4 * q4], v.x));
-                        w.y = to_tf32(fmaf(-bt, d[4 * q4 + 1], v.y));
-                        w.z = to_tf32(fmaf(-bt, d[4 * q4 + 2], v.z));
-                        w.w = to_tf32(fmaf(-bt, d[4 * q4 + 3], v.w));
-                        *reinterpret_cast<uint4 *>(smem + S_XB + sw128_32b(t, q4 >> 1) +
-                                                   (q4 & 1) * 16) = w;
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 v =
+                            *reinterpret_cast<const float4 *>(vrow + sw128(t, 4 * hc + q4));
+                        uint4 x;
+                        x.x = to_tf32_fast(fmaf(-bt, d[4 * q4], v.x));
+                        x.y = to_tf32_fast(fmaf(-bt, d[4 * q4 + 1], v.y));
+                        x.z = to_tf32_fast(fmaf(-bt, d[4 * q4 + 2], v.z));
+                        x.w = to_tf32_fast(fmaf(-bt, d[4 * q4 + 3], v.w));
+                        const int q8 = 4 * hc + q4; // 16-byte unit of the 128-byte row
+                        *reinterpret_cast<uint4 *>(smem + S_XB + sw128_32b(t, q8 >> 1) +
+                                                   (q8 & 1) * 16) = x;
                     }
                 } else {
-                    const float bs = a.scale * fac[tid - 64];
+                    const float bs = a.scale * fac[r - 64];
 #pragma unroll
-                    for (int jj = 0; jj < R; ++jj)
+                    for (int jj = 0; jj < 16; ++jj)
                         yb[jj] = bs * d[jj];
                 }
             }
             fence_async_smem();
             tc_fence_before();
-            chain_and(true);
-            // 4. MMA2: U = T'' X'
+            // 3. MMA2: U = T'' X' once the copier has this chunk's [T''; M]
+            ok = chain_and(mbar_wait(bar(B_TR + s), (c >> 1) & 1, abort_s));
+            if (!ok)
+                break;
             if (warp == 0) {
                 tc_fence_after();
                 if (elect_one()) {
@@ -596,96 +711,90 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
             if (!ok)
                 break;
             tc_fence_after();
-            if (tid < 64) {
-                float u[32];
-                tmem_ld32(lane_base + TM_D2, u);
-                const int t = tid;
+            // 4. U and diag(e) U as MN-major operands (rows 0-63)
+            if (r < 64) {
+                float u[16];
+                tmem_ld16(lane_base + TM_D2 + 16 * hc, u);
+                const int t = r;
                 const float et = fac[64 + t];
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {
-                    uint4 w, w2;
-                    w.x = to_tf32(u[4 * q4]);
-                    w.y = to_tf32(u[4 * q4 + 1]);
-                    w.z = to_tf32(u[4 * q4 + 2]);
-                    w.w = to_tf32(u[4 * q4 + 3]);
-                    w2.x = to_tf32(et * u[4 * q4]);
-                    w2.y = to_tf32(et * u[4 * q4 + 1]);
-                    w2.z = to_tf32(et * u[4 * q4 + 2]);
-                    w2.w = to_tf32(et * u[4 * q4 + 3]);
-                    const uint32_t off = sw128_32b(t, q4 >> 1) + (q4 & 1) * 16;
-                    *reinterpret_cast<uint4 *>(smem + S_UB + off) = w;
-                    *reinterpret_cast<uint4 *>(smem + S_U2 + off) = w2;
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    uint4 x, x2;
+                    x.x = to_tf32_fast(u[4 * q4]);
+                    x.y = to_tf32_fast(u[4 * q4 + 1]);
+                    x.z = to_tf32_fast(u[4 * q4 + 2]);
+                    x.w = to_tf32_fast(u[4 * q4 + 3]);
+                    x2.x = to_tf32_fast(et * u[4 * q4]);
+                    x2.y = to_tf32_fast(et * u[4 * q4 + 1]);
+                    x2.z = to_tf32_fast(et * u[4 * q4 + 2]);
+                    x2.w = to_tf32_fast(et * u[4 * q4 + 3]);
+                    const int q8 = 4 * hc + q4;
+                    const uint32_t off = sw128_32b(t, q8 >> 1) + (q8 & 1) * 16;
+                    *reinterpret_cast<uint4 *>(smem + S_UB + off) = x;
+                    *reinterpret_cast<uint4 *>(smem + S_U2 + off) = x2;
                 }
             }
             fence_async_smem();
             tc_fence_before();
             chain_and(true);
-            // 5. MMA3: M U (rows 64-127); MMA4: K^T diag(e) U (the state update)
+            // 5. MMA4: K^T diag(e) U (the state update), then MMA3: M U (rows
+            // 64-127, the output), committed separately
             if (warp == 0) {
                 tc_fence_after();
                 if (elect_one()) {
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
-                        mma_ts_tf32(tmem + TM_D3, atm_t + kk * 8,
-                                    sdesc_mn32(ub + kk * 1024, 8192, 512), ID2, kk > 0);
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ts_tf32(tmem + TM_D4, tmem + TM_KT + kk * 8,
+                        mma_ts_tf32(tmem + TM_D4, kt_t + kk * 8,
                                     sdesc_mn32(u2 + kk * 1024, 8192, 512), ID2, kk > 0);
                     mma_commit(bar(B_MMA));
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_ts_tf32(tmem + TM_D3, atm_t + kk * 8,
+                                    sdesc_mn32(ub + kk * 1024, 8192, 512), ID2, kk > 0);
+                    mma_commit(bar(B_MMA3));
                 }
                 __syncwarp();
             }
             mma_pending = 1;
             ok = chain_and(mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
             ++mma_phase;
-            mma_pending = 0;
             if (!ok)
                 break;
             tc_fence_after();
-            // 6. S = b_C S + D4 (FP32 registers); TF32 copy for the next MMA1; y
+            // 6. S = b_C S + D4 (FP32 registers); TF32 copy for the next MMA1
             {
-                float d[32];
-                tmem_ld32(lane_base + TM_D4, d);
+                float d[16];
+                tmem_ld16(lane_base + TM_D4 + 16 * hc, d);
                 const float bC = fac[128];
-                const int i = tid;
-                uint8_t *srow = smem + S_SB + (i >> 5) * 4096 + (i & 3) * 4;
+                uint8_t *srow = smem + S_SB + (r >> 5) * 4096 + (r & 3) * 4;
 #pragma unroll
-                for (int jj = 0; jj < R; ++jj) {
+                for (int jj = 0; jj < 16; ++jj) {
                     S[jj] = fmaf(bC, S[jj], d[jj]);
-                    *reinterpret_cast<uint32_t *>(srow + sw128(jj, (i & 31) >> 2)) = to_tf32(S[jj]);
-                }
-            }
-            if (tid >= 64) {
-                float d3[32];
-                tmem_ld32(lane_base + TM_D3, d3);
-                const int t = c * C + tid - 64;
-                if (t < a.T) {
-                    float4 *yrow = reinterpret_cast<float4 *>(
-                        a.dst + (((size_t)n * a.T + t) * a.H + h) * SK + j0);
-#pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4)
-                        yrow[q4] = make_float4(yb[4 * q4] + d3[4 * q4], yb[4 * q4 + 1] + d3[4 * q4 + 1],
-                                               yb[4 * q4 + 2] + d3[4 * q4 + 2],
-                                               yb[4 * q4 + 3] + d3[4 * q4 + 3]);
+                    *reinterpret_cast<uint32_t *>(srow + sw128(16 * hc + jj, (r & 31) >> 2)) =
+                        to_tf32_fast(S[jj]);
                 }
             }
             fence_async_smem();
             tc_fence_before();
             chain_and(true);
             if (tid == 0)
-                mbar_arrive(bar(B_KQE + s)); // stage s (K/Q/V/factors) is free
+                mbar_arrive(bar(B_VFE + s)); // V / factors of chunk c are no longer read
         }
+        if (ok && a.NC > 0)
+            ok = emit_y(a.NC - 1);
+        if (tid == 0 && y_pending)
+            bulk_wait_all();
         if (!ok) {
             *abort_s = 1;
             if (mma_pending) {
                 volatile int none = 0;
                 mbar_wait(bar(B_MMA), mma_phase & 1, &none, 100000000ull);
+                mbar_wait(bar(B_MMA3), mma3_phase & 1, &none, 100000000ull);
             }
         } else {
-            float *so = a.state_out + (((size_t)n * a.H + h) * SK + j0) * SK + tid;
+            float *so = a.state_out + (((size_t)n * a.H + h) * SK + j0 + 16 * hc) * SK + r;
 #pragma unroll
-            for (int jj = 0; jj < R; ++jj)
+            for (int jj = 0; jj < 16; ++jj)
                 so[(size_t)jj * SK] = S[jj];
         }
     }
@@ -741,7 +850,8 @@ static bool encode_rows(CUtensorMap *m, const float *p, int heads, int T, int se
 bool gdn_chunk_eligible(const GdnArgs &a) {
     const uintptr_t bits =
         reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
-        reinterpret_cast<uintptr_t>(a.v) | (uintptr_t)a.q_nb1 | (uintptr_t)a.q_nb2 |
+        reinterpret_cast<uintptr_t>(a.v) | reinterpret_cast<uintptr_t>(a.dst) |
+        (uintptr_t)a.q_nb1 | (uintptr_t)a.q_nb2 |
         (uintptr_t)a.q_nb3 | (uintptr_t)a.k_nb1 | (uintptr_t)a.k_nb2 | (uintptr_t)a.k_nb3 |
         (uintptr_t)a.v_nb1 | (uintptr_t)a.v_nb2 | (uintptr_t)a.v_nb3;
     return (bits & 15) == 0 && gc::n_chunks(a.T, a.slots) >= 2 && a.H <= 65535 &&
@@ -778,11 +888,13 @@ cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cuda
     c.NC = nc;
     c.scale = a.scale;
 
-    CUtensorMap kmap, qmap, vmap, amap;
+    CUtensorMap kmap, qmap, vmap, amap, ymap;
     const int seq_k = a.n_seq / a.rk3, seq_q = a.n_seq / a.rq3;
     if (!encode_rows(&kmap, a.k, a.H_k, a.T, seq_k, a.k_nb1, a.k_nb2, a.k_nb3) ||
         !encode_rows(&qmap, a.q, a.H_k, a.T, seq_q, a.q_nb1, a.q_nb2, a.q_nb3) ||
-        !encode_rows(&vmap, a.v, a.H, a.T, a.n_seq, a.v_nb1, a.v_nb2, a.v_nb3))
+        !encode_rows(&vmap, a.v, a.H, a.T, a.n_seq, a.v_nb1, a.v_nb2, a.v_nb3) ||
+        !encode_rows(&ymap, a.dst, a.H, a.T, a.n_seq, (int64_t)SK * 4, (int64_t)a.H * SK * 4,
+                     (int64_t)a.T * a.H * SK * 4))
         return cudaErrorNotSupported;
     {
         const cuuint64_t dims[2] = {64, (cuuint64_t)units * 128};
@@ -805,7 +917,7 @@ cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cuda
     if ((e = cudaGetLastError()) != cudaSuccess)
         return e;
     gdn_chunk_scan_kernel<<<dim3(SK / R, (unsigned)a.H, (unsigned)a.n_seq), SCAN_NT, S_BYTES,
-                            st>>>(kmap, qmap, vmap, amap, c);
+                            st>>>(kmap, qmap, vmap, amap, ymap, c);
     if ((e = cudaGetLastError()) != cudaSuccess)
         return e;
     if (tail) {
