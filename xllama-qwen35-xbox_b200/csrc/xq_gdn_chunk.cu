@@ -26,19 +26,20 @@
 //     sequential over chunks with the state in FP32 registers (two threads
 //     per TMEM lane i, 16 of the 32 rows each) and a TF32 copy in shared
 //     memory as the B operand of MMA1:
-//       MMA1  [K;Q] S_0^T          SS, M=128 (64 K rows + 64 Q rows), N=32, K=128
+//       MMA1  [K;Q'] S_0^T         TS, M=128 (64 K rows + 64 rows of
+//                                  Q' = diag(scale b) Q), N=32, K=128
 //       MMA2  [T'';M] X'           TS, A in TMEM, B = X' MN-major, K=64
 //       MMA4  K^T (diag(e) U)      TS (M=128 over the key elements): the
 //                                  state update
-//       MMA3  [T'';M] U            TS (rows 64..127: M U lands on the lanes
-//                                  holding scale b Q S_0^T), the output
+//       MMA3  [T'';M] U            TS, accumulated onto MMA1's result: rows
+//                                  64..127 become y = scale b Q S_0^T + M U
 //     MN-major TF32 operands (X', U, diag(e) U) use the 128-byte swizzle with
 //     32-byte granules, the only MN-major layout for 32-bit elements; K-major
 //     operands use the plain 128-byte swizzle TMA writes.  Warp roles: 8
-//     chain warps, 4 copier warps that move the next chunk's [T''; M] rows and
-//     K^T into double-buffered TMEM, and a producer warp whose three lanes
-//     stream K/Q tiles, V tiles + factors and [T''; M] independently.  Each
-//     chunk's output leaves by TMA store while the next chunk's MMA1 runs.
+//     chain warps, 4 copier warps that move the next chunk's A operands into
+//     TMEM and the finished output rows to a TMA store, and a producer warp
+//     whose three lanes stream K/Q tiles, V tiles + factors and [T''; M]
+//     independently.
 // Operands produced here (S, X', U, T'', M) are rounded to TF32 to nearest;
 // K, Q, V tiles enter the tensor core as stored (fp32 read as TF32).  Tokens
 // past T read as zeros with g = beta = 0, so a partial last chunk is exact.
@@ -60,7 +61,8 @@ constexpr int SK = 128;      // head size (key and value)
 constexpr int R = 32;        // state rows per scan CTA
 constexpr int AST = 68;      // padded row stride (floats) of the solve matrices
 constexpr int ATM_FLOATS = 128 * 64; // [T''; M] per unit
-constexpr int FAC_FLOATS = 256;      // b[64], e[64], b_C, pad
+constexpr int FAC_FLOATS = 256;      // b[64], e[64], b_C, pad (workspace stride)
+constexpr int FAC_BYTES = 528;       // the part the scan loads: b, e, b_C (+3 pad)
 constexpr int PREP_NT = 128;
 constexpr int SCAN_NT = 416;         // 8 chain warps, 4 copier warps, 1 producer warp
 constexpr float kLog2e = 1.4426950408889634f;
@@ -78,18 +80,21 @@ constexpr int P_BYTES = P_BAR + 32 + 1024;    // + alignment slack
 constexpr int S_KQ = 0;                       // 2 stages x 64 KB
 constexpr int S_V = 131072;                   // 2 stages x 8 KB
 constexpr int S_ATM = 147456;                 // landing buffer, 2 slabs x 16 KB
-constexpr int S_SB = 180224;                  // S operand, 4 slabs x 4 KB (K-major)
+constexpr int S_SB = 180224;                  // S operand, MN-major: row i (128), 32 columns
 constexpr int S_XB = 196608;                  // X' (MN-major, 64 x 32)
 constexpr int S_UB = 204800;                  // U
 constexpr int S_U2 = 212992;                  // diag(e) U
-constexpr int S_FAC = 221184;                 // 2 stages x 1 KB
-constexpr int S_BAR = 223232;
-constexpr int S_BYTES = S_BAR + 160 + 1024;
+constexpr int S_Y = 221184;                   // output tile (64 x 32, 128-byte swizzled)
+constexpr int S_FAC = 229376;                 // 2 stages x FAC_BYTES
+constexpr int S_BAR = S_FAC + 2 * FAC_BYTES;
+constexpr int S_BYTES = S_BAR + 192 + 1024;
 
 // scan kernel TMEM columns (A operands copied in by the copier warps)
 constexpr uint32_t TM_ATM = 0;   // [T''; M], 2 buffers x 64
 constexpr uint32_t TM_KT = 128;  // K^T (lane i, column t), 2 buffers x 64
-constexpr uint32_t TM_D1 = 256, TM_D2 = 288, TM_D3 = 320, TM_D4 = 352;
+constexpr uint32_t TM_KQ = 256;  // [K; diag(scale b) Q] rows, 128 columns
+constexpr uint32_t TM_D1 = 384;  // MMA1 (+ MMA3 on rows 64-127), 2 buffers x 32
+constexpr uint32_t TM_D2 = 448, TM_D4 = 480;
 constexpr uint32_t TM_COLS = 512;
 
 __host__ __device__ constexpr int n_chunks(int T, int slots) {
@@ -393,11 +398,16 @@ __global__ void __launch_bounds__(gc::PREP_NT)
 // ---------------------------------------------------------------------------
 // Sequential scan over chunks, warp-specialised:
 //   warps 0-7   chain: TMEM lane quarter (warp & 3), state columns
-//               16 (warp >> 2) .. +15 of the CTA's 32; warp 0 issues the MMAs
-//   warps 8-11  copier: [T''; M] rows and K^T into TMEM (double-buffered) for
-//               the chunk after the one the chain works on
+//               16 (warp >> 2) .. +15 of the CTA's 32; warp 0 issues MMA1,
+//               MMA2, MMA4 and warp 4 issues MMA3
+//   warps 8-11  copier: the next chunk's A operands into TMEM ([T''; M] rows
+//               and K^T double-buffered, [K; diag(scale b) Q] rows single-
+//               buffered once the chain's MMA1 is done), then the finished
+//               chunk's output rows from TMEM to a TMA store
 //   warp 12     producer: lane 0 K/Q tiles, lane 1 V tile + factors, lane 2
 //               the [T''; M] landing buffer
+// With Q pre-scaled by scale b_t, MMA1's rows 64-127 are the first term of
+// y; MMA3 accumulates M U onto them, so the output never enters the chain.
 __global__ void __launch_bounds__(gc::SCAN_NT, 1)
     gdn_chunk_scan_kernel(const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap qmap,
@@ -409,14 +419,16 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = align1024(smem_raw);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S_BAR);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 20);
     volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
     auto bar = [&](int i) { return smem_u32(bars + i); };
-    // kq_full[2], vf_full[2], kq_empty[2] (MMA1 done + K^T copied),
-    // vf_empty[2], atm_full, atm_empty, tmem_ready[2] (copier -> chain),
-    // tmem_free[2] (chain -> copier), mma (MMA1/MMA2/MMA4), mma3
+    // kq_full[2], vf_full[2], kq_empty[2] (copier done with the K/Q tiles),
+    // vf_empty[2], atm_full, atm_empty, tmem_ready[2] (copier -> chain: A
+    // operands of chunk c in TMEM), kq_free (chain -> copier: MMA1 done, the
+    // [K; Q] columns may be overwritten), d1_free[2] (copier -> chain: output
+    // rows read), mma (MMA1/MMA2/MMA4), mma3
     constexpr int B_KQF = 0, B_VFF = 2, B_KQE = 4, B_VFE = 6, B_AF = 8, B_AE = 9, B_TR = 10,
-                  B_TF = 12, B_MMA = 14, B_MMA3 = 15;
+                  B_KQFREE = 12, B_D1F = 13, B_MMA = 15, B_MMA3 = 16;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slice = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
@@ -432,13 +444,14 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar(B_KQF + i), 1);
             mbar_init(bar(B_VFF + i), 1);
-            mbar_init(bar(B_KQE + i), 1 + 128); // chain (MMA1 done) + copier threads
+            mbar_init(bar(B_KQE + i), 128);
             mbar_init(bar(B_VFE + i), 1);
             mbar_init(bar(B_TR + i), 128);
-            mbar_init(bar(B_TF + i), 1);
+            mbar_init(bar(B_D1F + i), 1);
         }
         mbar_init(bar(B_AF), 1);
         mbar_init(bar(B_AE), 128);
+        mbar_init(bar(B_KQFREE), 1);
         mbar_init(bar(B_MMA), 1);
         mbar_init(bar(B_MMA3), 1);
         *abort_s = 0;
@@ -447,21 +460,30 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
     if (warp == 0)
         tmem_alloc(smem_u32(tmem_slot), TM_COLS);
 
-    // chain thread (row r = TMEM lane, column half hc) holds state rows
-    // j0 + 16 hc .. +15 at column i = r in FP32 registers; the TF32 operand
-    // copy goes to the K-major S tile (row j, K index i)
+    // chain thread (row r = TMEM lane = key element i, column half hc) holds
+    // state rows j0 + 16 hc .. +15 at column i in FP32 registers; the TF32
+    // operand copy is the MN-major S tile (row i, 32 value columns)
     const int r = 32 * (warp & 3) + lane, hc = (warp >> 2) & 1;
     float S[16];
+    auto store_s = [&]() {
+        uint32_t v[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+            v[jj] = to_tf32_fast(S[jj]);
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+            uint8_t *p = smem + S_SB + sw128_32b(r, 2 * hc + g);
+            *reinterpret_cast<uint4 *>(p) = make_uint4(v[8 * g], v[8 * g + 1], v[8 * g + 2], v[8 * g + 3]);
+            *reinterpret_cast<uint4 *>(p + 16) =
+                make_uint4(v[8 * g + 4], v[8 * g + 5], v[8 * g + 6], v[8 * g + 7]);
+        }
+    };
     if (warp < 8) {
         const float *sp = at(a.state, n * a.s_nb3 + (int64_t)h * a.s_nb2);
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-            const int j = 16 * hc + jj;
-            S[jj] = *at(sp, (int64_t)(j0 + j) * a.s_nb1 + 4 * r);
-            *reinterpret_cast<uint32_t *>(smem + S_SB + (r >> 5) * 4096 +
-                                          sw128(j, (r & 31) >> 2) + (r & 3) * 4) =
-                to_tf32_fast(S[jj]);
-        }
+        for (int jj = 0; jj < 16; ++jj)
+            S[jj] = *at(sp, (int64_t)(j0 + 16 * hc + jj) * a.s_nb1 + 4 * r);
+        store_s();
         fence_async_smem();
     }
     tc_fence_before();
@@ -491,11 +513,11 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                 } else if (lane == 1) {
                     if (use >= 1 && !mbar_wait(bar(B_VFE + s), (use - 1) & 1, abort_s))
                         break;
-                    mbar_expect_tx(bar(B_VFF + s), 8192 + 1024);
+                    mbar_expect_tx(bar(B_VFF + s), 8192 + FAC_BYTES);
                     tma_load_4d(smem_u32(smem + S_V + s * 8192), &vmap, j0, h, c * C, n,
                                 bar(B_VFF + s));
-                    bulk_load(smem_u32(smem + S_FAC + s * 1024),
-                              a.fac + (unit0 + c) * FAC_FLOATS, 1024, bar(B_VFF + s));
+                    bulk_load(smem_u32(smem + S_FAC + s * FAC_BYTES),
+                              a.fac + (unit0 + c) * FAC_FLOATS, FAC_BYTES, bar(B_VFF + s));
                 } else {
                     if (c >= 1 && !mbar_wait(bar(B_AE), (c - 1) & 1, abort_s))
                         break;
@@ -523,16 +545,53 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
         }
     } else if (warp >= 8) {
         // ------------------------------ copier ------------------------------
+        auto copier_sync = []() { asm volatile("bar.sync 2, 128;" ::: "memory"); };
         uint32_t w[16];
-        for (int cn = 0; cn < a.NC; ++cn) {
-            const int b = cn & 1;
-            bool ok = mbar_wait(bar(B_KQF + b), (cn >> 1) & 1, abort_s) &&
-                      mbar_wait(bar(B_AF), cn & 1, abort_s) &&
-                      (cn < 2 || mbar_wait(bar(B_TF + b), ((cn >> 1) - 1) & 1, abort_s));
-            if (!ok) {
-                *abort_s = 1;
-                break;
+        int y_pending = 0;
+        // output rows of chunk cy: D1 rows 64-127 once MMA3 has accumulated
+        // M U onto them; 128-byte swizzled tile, one TMA store
+        auto emit_y = [&](int cy) -> bool {
+            if (!mbar_wait(bar(B_MMA3), cy & 1, abort_s))
+                return false;
+            tc_fence_after();
+            if (tid == 256 && y_pending) {
+                bulk_wait_read(); // the previous tile has left the buffer
+                y_pending = 0;
             }
+            copier_sync();
+            if (r >= 64) {
+                float y[32];
+                tmem_ld32(lane_base + TM_D1 + 32 * (cy & 1), y);
+                const int t = r - 64;
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                    *reinterpret_cast<float4 *>(smem + S_Y + sw128(t, q4)) =
+                        make_float4(y[4 * q4], y[4 * q4 + 1], y[4 * q4 + 2], y[4 * q4 + 3]);
+            }
+            fence_async_smem();
+            tc_fence_before();
+            copier_sync();
+            if (tid == 256) {
+                mbar_arrive(bar(B_D1F + (cy & 1))); // MMA1 may overwrite these columns
+                // rows past T fall outside the map and are not written
+                tma_store_4d(&ymap, smem_u32(smem + S_Y), j0, h, cy * C, n);
+                bulk_commit();
+                y_pending = 1;
+            }
+            return true;
+        };
+        bool ok = true;
+        for (int cn = 0; cn < a.NC && ok; ++cn) {
+            const int b = cn & 1;
+            ok = mbar_wait(bar(B_KQF + b), (cn >> 1) & 1, abort_s) &&
+                 mbar_wait(bar(B_AF), cn & 1, abort_s) &&
+                 mbar_wait(bar(B_VFF + b), (cn >> 1) & 1, abort_s);
+            // the previous chunk's MMA1 done: every MMA of chunk cn-2 (the last
+            // reader of TMEM buffer b) and of the [K; Q] columns has completed
+            if (ok && cn >= 1)
+                ok = mbar_wait(bar(B_KQFREE), (cn - 1) & 1, abort_s);
+            if (!ok)
+                break;
             tc_fence_after();
             // [T''; M] row r -> TMEM buffer b (A of MMA2 / MMA3)
 #pragma unroll
@@ -552,7 +611,8 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                 }
             // K^T: lane r takes column r of the K tile (rows t = 0..63), the A
             // operand of MMA4
-            const uint8_t *kcol = smem + S_KQ + b * 65536 + (r >> 5) * 16384 + (r & 3) * 4;
+            const uint8_t *kq = smem + S_KQ + b * 65536;
+            const uint8_t *kcol = kq + (r >> 5) * 16384 + (r & 3) * 4;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
 #pragma unroll
@@ -561,15 +621,49 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                         kcol + sw128(16 * q + x, (r & 31) >> 2));
                 tmem_st16(lane_base + TM_KT + 64 * b + 16 * q, w);
             }
+            mbar_arrive(bar(B_AE)); // the landing buffer is free
+            // [K; diag(scale b) Q] rows -> TMEM (A of MMA1)
+            const float qs = r >= 64 ? a.scale * reinterpret_cast<const float *>(
+                                                     smem + S_FAC + b * FAC_BYTES)[r - 64]
+                                     : 0.0f;
+#pragma unroll
+            for (int ib = 0; ib < 4; ++ib)
+#pragma unroll
+                for (int hq = 0; hq < 2; ++hq) {
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(
+                            kq + ib * 16384 + sw128(r, 4 * hq + q4));
+                        if (r >= 64) {
+                            w[4 * q4] = to_tf32_fast(qs * __uint_as_float(v.x));
+                            w[4 * q4 + 1] = to_tf32_fast(qs * __uint_as_float(v.y));
+                            w[4 * q4 + 2] = to_tf32_fast(qs * __uint_as_float(v.z));
+                            w[4 * q4 + 3] = to_tf32_fast(qs * __uint_as_float(v.w));
+                        } else {
+                            w[4 * q4] = v.x;
+                            w[4 * q4 + 1] = v.y;
+                            w[4 * q4 + 2] = v.z;
+                            w[4 * q4 + 3] = v.w;
+                        }
+                    }
+                    tmem_st16(lane_base + TM_KQ + 32 * ib + 16 * hq, w);
+                }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(bar(B_AE));     // the landing buffer is free
-            mbar_arrive(bar(B_KQE + b)); // this thread is done with the K tile
-            mbar_arrive(bar(B_TR + b));  // the chain may use TMEM buffer b
+            mbar_arrive(bar(B_KQE + b)); // this thread is done with the K/Q tiles
+            mbar_arrive(bar(B_TR + b));  // chunk cn's A operands are in TMEM
+            if (cn >= 1)
+                ok = emit_y(cn - 1);
         }
+        if (ok && a.NC > 0)
+            ok = emit_y(a.NC - 1);
+        if (tid == 256 && y_pending)
+            bulk_wait_all();
+        if (!ok)
+            *abort_s = 1;
     } else {
         // ------------------------------- chain --------------------------------
-        constexpr uint32_t ID1 = idesc_tf32(128, R, 0, 0);
+        constexpr uint32_t ID1 = idesc_tf32(128, R, 0, 1);
         constexpr uint32_t ID2 = idesc_tf32(128, R, 0, 1);
         const uint32_t sb = smem_u32(smem + S_SB), xb = smem_u32(smem + S_XB),
                        ub = smem_u32(smem + S_UB), u2 = smem_u32(smem + S_U2);
@@ -582,74 +676,32 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                          : "memory");
             return res != 0;
         };
-        int mma_pending = 0, mma_phase = 0, mma3_phase = 0, y_pending = 0;
-        float yb[16];
-        // y of chunk cy = scale b Q S_0^T (yb, rows 64-127) + M U (MMA3),
-        // 128-byte swizzled into the X' buffer and stored by TMA; MMA3 done
-        // also frees TMEM buffer cy & 1 for the copier
-        auto emit_y = [&](int cy) -> bool {
-            if (!chain_and(mbar_wait(bar(B_MMA3), mma3_phase & 1, abort_s)))
-                return false;
-            ++mma3_phase;
-            tc_fence_after();
-            if (tid == 0)
-                mbar_arrive(bar(B_TF + (cy & 1)));
-            if (r >= 64) {
-                float d3[16];
-                tmem_ld16(lane_base + TM_D3 + 16 * hc, d3);
-                const int t = r - 64;
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4)
-                    *reinterpret_cast<float4 *>(smem + S_XB + sw128(t, 4 * hc + q4)) =
-                        make_float4(yb[4 * q4] + d3[4 * q4], yb[4 * q4 + 1] + d3[4 * q4 + 1],
-                                    yb[4 * q4 + 2] + d3[4 * q4 + 2],
-                                    yb[4 * q4 + 3] + d3[4 * q4 + 3]);
-            }
-            fence_async_smem();
-            chain_and(true);
-            if (tid == 0) {
-                // rows past T fall outside the map and are not written
-                tma_store_4d(&ymap, xb, j0, h, cy * C, n);
-                bulk_commit();
-                y_pending = 1;
-            }
-            return true;
-        };
+        int mma_pending = 0, mma3_issued = 0, mma_phase = 0;
         bool ok = true;
         for (int c = 0; c < a.NC && ok; ++c) {
             const int s = c & 1;
-            const uint32_t atm_t = tmem + TM_ATM + (uint32_t)s * 64;
-            const uint32_t kt_t = tmem + TM_KT + (uint32_t)s * 64;
-            const float *fac = reinterpret_cast<const float *>(smem + S_FAC + s * 1024);
-            // 1. MMA1: D1 = [K; Q] S_0^T (both operands in shared memory)
-            ok = chain_and(mbar_wait(bar(B_KQF + s), (c >> 1) & 1, abort_s));
+            const uint32_t d1 = tmem + TM_D1 + 32 * (uint32_t)s;
+            const uint32_t atm_t = tmem + TM_ATM + 64 * (uint32_t)s;
+            const uint32_t kt_t = tmem + TM_KT + 64 * (uint32_t)s;
+            const float *fac = reinterpret_cast<const float *>(smem + S_FAC + s * FAC_BYTES);
+            // 1. MMA1: D1 = [K; diag(scale b) Q] S_0^T once the copier has
+            // chunk c's operands and the output rows of chunk c-2 are out
+            ok = chain_and(mbar_wait(bar(B_TR + s), (c >> 1) & 1, abort_s) &&
+                           (c < 2 || mbar_wait(bar(B_D1F + s), ((c >> 1) - 1) & 1, abort_s)));
             if (!ok)
                 break;
             if (warp == 0) {
                 tc_fence_after();
                 if (elect_one()) {
-                    const uint32_t kq = smem_u32(smem + S_KQ + s * 65536);
 #pragma unroll
-                    for (int kk = 0; kk < 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        mma_ss_tf32(tmem + TM_D1, sdesc(kq + off, 16, 1024),
-                                    sdesc(sb + (kk >> 2) * 4096 + (kk & 3) * 32, 16, 1024), ID1,
-                                    kk > 0);
-                    }
+                    for (int kk = 0; kk < 16; ++kk)
+                        mma_ts_tf32(d1, tmem + TM_KQ + kk * 8,
+                                    sdesc_mn32(sb + kk * 1024, 8192, 512), ID1, kk > 0);
                     mma_commit(bar(B_MMA));
                 }
                 __syncwarp();
             }
             mma_pending = 1;
-            // the previous chunk's output while MMA1 runs
-            if (c > 0 && !emit_y(c - 1)) {
-                ok = false;
-                break;
-            }
-            if (tid == 0 && y_pending) {
-                bulk_wait_read(); // the y tile has left the X' buffer
-                y_pending = 0;
-            }
             ok = chain_and(mbar_wait(bar(B_VFF + s), (c >> 1) & 1, abort_s) &&
                            mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
             ++mma_phase;
@@ -658,41 +710,31 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                 break;
             tc_fence_after();
             if (tid == 0)
-                mbar_arrive(bar(B_KQE + s)); // MMA1 has read the K/Q tiles
-            // 2. X' = V - b X (rows 0-63); scale b Q S_0^T kept (rows 64-127)
-            {
+                mbar_arrive(bar(B_KQFREE)); // MMA1 has read the [K; Q] columns
+            // 2. X' = V - b X (rows 0-63)
+            if (r < 64) {
                 float d[16];
-                tmem_ld16(lane_base + TM_D1 + 16 * hc, d);
-                if (r < 64) {
-                    const int t = r;
-                    const float bt = fac[t];
-                    const uint8_t *vrow = smem + S_V + s * 8192;
+                tmem_ld16(lane_base + TM_D1 + 32 * s + 16 * hc, d);
+                const int t = r;
+                const float bt = fac[t];
+                const uint8_t *vrow = smem + S_V + s * 8192;
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; ++q4) {
-                        const float4 v =
-                            *reinterpret_cast<const float4 *>(vrow + sw128(t, 4 * hc + q4));
-                        uint4 x;
-                        x.x = to_tf32_fast(fmaf(-bt, d[4 * q4], v.x));
-                        x.y = to_tf32_fast(fmaf(-bt, d[4 * q4 + 1], v.y));
-                        x.z = to_tf32_fast(fmaf(-bt, d[4 * q4 + 2], v.z));
-                        x.w = to_tf32_fast(fmaf(-bt, d[4 * q4 + 3], v.w));
-                        const int q8 = 4 * hc + q4; // 16-byte unit of the 128-byte row
-                        *reinterpret_cast<uint4 *>(smem + S_XB + sw128_32b(t, q8 >> 1) +
-                                                   (q8 & 1) * 16) = x;
-                    }
-                } else {
-                    const float bs = a.scale * fac[r - 64];
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj)
-                        yb[jj] = bs * d[jj];
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    const float4 v = *reinterpret_cast<const float4 *>(vrow + sw128(t, 4 * hc + q4));
+                    uint4 x;
+                    x.x = to_tf32_fast(fmaf(-bt, d[4 * q4], v.x));
+                    x.y = to_tf32_fast(fmaf(-bt, d[4 * q4 + 1], v.y));
+                    x.z = to_tf32_fast(fmaf(-bt, d[4 * q4 + 2], v.z));
+                    x.w = to_tf32_fast(fmaf(-bt, d[4 * q4 + 3], v.w));
+                    const int q8 = 4 * hc + q4; // 16-byte unit of the 128-byte row
+                    *reinterpret_cast<uint4 *>(smem + S_XB + sw128_32b(t, q8 >> 1) +
+                                               (q8 & 1) * 16) = x;
                 }
             }
             fence_async_smem();
             tc_fence_before();
-            // 3. MMA2: U = T'' X' once the copier has this chunk's [T''; M]
-            ok = chain_and(mbar_wait(bar(B_TR + s), (c >> 1) & 1, abort_s));
-            if (!ok)
-                break;
+            chain_and(true);
+            // 3. MMA2: U = T'' X'
             if (warp == 0) {
                 tc_fence_after();
                 if (elect_one()) {
@@ -737,27 +779,33 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
             fence_async_smem();
             tc_fence_before();
             chain_and(true);
-            // 5. MMA4: K^T diag(e) U (the state update), then MMA3: M U (rows
-            // 64-127, the output), committed separately
-            if (warp == 0) {
+            // 5. MMA4 (warp 0): K^T diag(e) U, the state update; MMA3 (warp 4):
+            // M U accumulated onto D1 rows 64-127, the output (rows 0-63 of D1,
+            // X, are no longer needed)
+            if (warp == 0 || warp == 4) {
                 tc_fence_after();
                 if (elect_one()) {
+                    if (warp == 0) {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ts_tf32(tmem + TM_D4, kt_t + kk * 8,
-                                    sdesc_mn32(u2 + kk * 1024, 8192, 512), ID2, kk > 0);
-                    mma_commit(bar(B_MMA));
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_ts_tf32(tmem + TM_D4, kt_t + kk * 8,
+                                        sdesc_mn32(u2 + kk * 1024, 8192, 512), ID2, kk > 0);
+                        mma_commit(bar(B_MMA));
+                    } else {
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_ts_tf32(tmem + TM_D3, atm_t + kk * 8,
-                                    sdesc_mn32(ub + kk * 1024, 8192, 512), ID2, kk > 0);
-                    mma_commit(bar(B_MMA3));
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_ts_tf32(d1, atm_t + kk * 8, sdesc_mn32(ub + kk * 1024, 8192, 512),
+                                        ID2, 1);
+                        mma_commit(bar(B_MMA3));
+                    }
                 }
                 __syncwarp();
             }
             mma_pending = 1;
+            ++mma3_issued;
             ok = chain_and(mbar_wait(bar(B_MMA), mma_phase & 1, abort_s));
             ++mma_phase;
+            mma_pending = 0;
             if (!ok)
                 break;
             tc_fence_after();
@@ -766,13 +814,10 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
                 float d[16];
                 tmem_ld16(lane_base + TM_D4 + 16 * hc, d);
                 const float bC = fac[128];
-                uint8_t *srow = smem + S_SB + (r >> 5) * 4096 + (r & 3) * 4;
 #pragma unroll
-                for (int jj = 0; jj < 16; ++jj) {
+                for (int jj = 0; jj < 16; ++jj)
                     S[jj] = fmaf(bC, S[jj], d[jj]);
-                    *reinterpret_cast<uint32_t *>(srow + sw128(16 * hc + jj, (r & 31) >> 2)) =
-                        to_tf32_fast(S[jj]);
-                }
+                store_s();
             }
             fence_async_smem();
             tc_fence_before();
@@ -780,17 +825,13 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
             if (tid == 0)
                 mbar_arrive(bar(B_VFE + s)); // V / factors of chunk c are no longer read
         }
-        if (ok && a.NC > 0)
-            ok = emit_y(a.NC - 1);
-        if (tid == 0 && y_pending)
-            bulk_wait_all();
         if (!ok) {
             *abort_s = 1;
-            if (mma_pending) {
-                volatile int none = 0;
+            volatile int none = 0;
+            if (mma_pending)
                 mbar_wait(bar(B_MMA), mma_phase & 1, &none, 100000000ull);
-                mbar_wait(bar(B_MMA3), mma3_phase & 1, &none, 100000000ull);
-            }
+            if (mma3_issued > 0) // the last MMA3 (the copier may not have waited it)
+                mbar_wait(bar(B_MMA3), (mma3_issued - 1) & 1, &none, 100000000ull);
         } else {
             float *so = a.state_out + (((size_t)n * a.H + h) * SK + j0 + 16 * hc) * SK + r;
 #pragma unroll
