@@ -18,10 +18,11 @@
 //
 // Two kernels:
 //   gdn_chunk_prep_kernel  one CTA per (chunk, head, sequence), all in
-//     parallel: [K;Q] K^T on the tensor core (M=128, N=64, K=128), the gates,
-//     the unit lower-triangular inverse in FP32 (16x16 diagonal blocks by
-//     forward substitution, then block rows), and writes [T''; M] (128 x 64)
-//     plus b, e, b_C to the workspace.
+//     parallel, 3 CTAs per SM: [K;Q] K^T on the tensor core (M=128, N=64,
+//     K=128), the gates, the unit lower-triangular inverse in FP32 (16x16
+//     diagonal blocks by forward substitution, then block rows; four lanes
+//     per column), and writes [T''; M] (128 x 64) plus b, e, b_C to the
+//     workspace.
 //   gdn_chunk_scan_kernel  one CTA per (32 state rows, head, sequence),
 //     sequential over chunks with the state in FP32 registers (two threads
 //     per TMEM lane i, 16 of the 32 rows each) and a TF32 copy in shared
@@ -63,7 +64,7 @@ constexpr int AST = 68;      // padded row stride (floats) of the solve matrices
 constexpr int ATM_FLOATS = 128 * 64; // [T''; M] per unit
 constexpr int FAC_FLOATS = 256;      // b[64], e[64], b_C, pad (workspace stride)
 constexpr int FAC_BYTES = 528;       // the part the scan loads: b, e, b_C (+3 pad)
-constexpr int PREP_NT = 128;
+constexpr int PREP_NT = 256;
 constexpr int SCAN_NT = 416;         // 8 chain warps, 4 copier warps, 1 producer warp
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -124,65 +125,59 @@ struct GdnChunkArgs {
 };
 
 // ---------------------------------------------------------------------------
-// Per-chunk preparation.
+// Per-chunk preparation (256 threads; four lanes per column of T in the
+// solve, adjacent lanes of one warp).
 
-// Block row BI of T = (I + A)^-1 for column cc, two lanes per column (hh =
-// which 8 of the block's 16 rows): E = A[16BI.., :16BI] T[:16BI, cc], then
-// T[16BI + r, cc] = -(D_BI E)_r with D_BI = T[16BI.., 16BI..] (already in
-// Tt).  Tt is column-major: Tt[col][row].  The partner lane is lane ^ 16.
+// Block row BI of T = (I + A)^-1 for column cc (BI > cc / 16), lane p of the
+// column's four computing rows 4p..4p+3 of the block row:
+// E = A[16BI.., 16j:16BI] T[16j:16BI, cc] (T is zero above the column's own
+// diagonal block j), then T[16BI + r, cc] = -(D_BI E)_r with
+// D_BI = T[16BI.., 16BI..] (already in Tt).  Tt is column-major: Tt[col][row].
 template <int BI>
-__device__ __forceinline__ void solve_block_row(const float *Am, float *Tt, int cc, int hh) {
+__device__ __forceinline__ void solve_block_row(const float *Am, float *Tt, int cc, int p,
+                                                int lane) {
     using namespace gc;
-    float e[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-        e[r] = 0.0f;
+    const int j = cc >> 4;
+    float e[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const float *tcol = Tt + cc * AST;
-    const float *arow = Am + (16 * BI + 8 * hh) * AST;
+    const float *arow = Am + (16 * BI + 4 * p) * AST;
 #pragma unroll
     for (int m4 = 0; m4 < 4 * BI; ++m4) {
+        if (m4 < 4 * j)
+            continue;
         const float4 tv = *reinterpret_cast<const float4 *>(tcol + 4 * m4);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const float4 av = *reinterpret_cast<const float4 *>(arow + r * AST + 4 * m4);
-            e[r] = fmaf(av.x, tv.x, e[r]);
-            e[r] = fmaf(av.y, tv.y, e[r]);
-            e[r] = fmaf(av.z, tv.z, e[r]);
-            e[r] = fmaf(av.w, tv.w, e[r]);
+        for (int x = 0; x < 4; ++x) {
+            const float4 av = *reinterpret_cast<const float4 *>(arow + x * AST + 4 * m4);
+            e[x] = fmaf(av.x, tv.x, e[x]);
+            e[x] = fmaf(av.y, tv.y, e[x]);
+            e[x] = fmaf(av.z, tv.z, e[x]);
+            e[x] = fmaf(av.w, tv.w, e[x]);
         }
     }
+    // the column's 16 E values from its four lanes
     float E[16];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-        const float other = __shfl_xor_sync(0xffffffffu, e[r], 16);
-        E[r] = hh ? other : e[r];
-        E[8 + r] = hh ? e[r] : other;
-    }
-    float o[8];
+    for (int q = 0; q < 4; ++q)
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
-        o[r] = 0.0f;
+        for (int x = 0; x < 4; ++x)
+            E[4 * q + x] = __shfl_sync(0xffffffffu, e[x], (lane & ~3) | q);
+    float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
-        // D[8hh + r][m] for r = 0..7 (zero above the diagonal)
-        const float *dcol = Tt + (16 * BI + m) * AST + 16 * BI + 8 * hh;
-        const float4 d0 = *reinterpret_cast<const float4 *>(dcol);
-        const float4 d1 = *reinterpret_cast<const float4 *>(dcol + 4);
-        o[0] = fmaf(d0.x, E[m], o[0]);
-        o[1] = fmaf(d0.y, E[m], o[1]);
-        o[2] = fmaf(d0.z, E[m], o[2]);
-        o[3] = fmaf(d0.w, E[m], o[3]);
-        o[4] = fmaf(d1.x, E[m], o[4]);
-        o[5] = fmaf(d1.y, E[m], o[5]);
-        o[6] = fmaf(d1.z, E[m], o[6]);
-        o[7] = fmaf(d1.w, E[m], o[7]);
+        // D[4p + x][m] for x = 0..3 (zero above the diagonal)
+        const float4 d =
+            *reinterpret_cast<const float4 *>(Tt + (16 * BI + m) * AST + 16 * BI + 4 * p);
+        o[0] = fmaf(d.x, E[m], o[0]);
+        o[1] = fmaf(d.y, E[m], o[1]);
+        o[2] = fmaf(d.z, E[m], o[2]);
+        o[3] = fmaf(d.w, E[m], o[3]);
     }
-    float *out = Tt + cc * AST + 16 * BI + 8 * hh;
-    *reinterpret_cast<float4 *>(out) = make_float4(-o[0], -o[1], -o[2], -o[3]);
-    *reinterpret_cast<float4 *>(out + 4) = make_float4(-o[4], -o[5], -o[6], -o[7]);
+    *reinterpret_cast<float4 *>(Tt + cc * AST + 16 * BI + 4 * p) =
+        make_float4(-o[0], -o[1], -o[2], -o[3]);
 }
 
-__global__ void __launch_bounds__(gc::PREP_NT)
+__global__ void __launch_bounds__(gc::PREP_NT, 3)
     gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap kmap,
                           const __grid_constant__ CUtensorMap qmap, const GdnChunkArgs a) {
     using namespace tc;
@@ -245,9 +240,8 @@ __global__ void __launch_bounds__(gc::PREP_NT)
         Gs[tid] += Gs[31];
 
     // S = [K; Q] K^T  (rows 0-63: K K^T, rows 64-127: Q K^T)
-    bool ok = true;
     if (warp == 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(bar_tma, 0, abort_s));
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(bar_tma, 0, abort_s));
         if (ok) {
             tc_fence_after();
             if (elect_one()) {
@@ -266,45 +260,40 @@ __global__ void __launch_bounds__(gc::PREP_NT)
         }
     }
     __syncthreads(); // Gs complete
-    ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, abort_s));
+    __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, abort_s));
     tc_fence_after();
-    float sv[64];
-    {
-        float lo[32], hi[32];
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        tmem_ld32(lane_base, lo);
-        tmem_ld32(lane_base + 32, hi);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            sv[i] = lo[i];
-            sv[32 + i] = hi[i];
-        }
-    }
+    // thread (row r = TMEM lane, column half hh): columns 32 hh .. +31 of S;
+    // the K/Q tile is dead now and its space holds A and T
+    const int r = 32 * (warp & 3) + lane, hh = warp >> 2;
+    float sv[32];
+    tmem_ld32(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 32 * hh, sv);
     float *atm = a.atm + unit * ATM_FLOATS;
-    if (tid < 64) {
-        const int t = tid;
+    if (r < 64) {
+        const int t = r;
         const float Gt = Gs[t], bt = Bs[t];
 #pragma unroll
-        for (int s4 = 0; s4 < 16; ++s4) {
+        for (int s4 = 0; s4 < 8; ++s4) {
             float w[4];
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
-                const int s = 4 * s4 + x;
-                w[x] = s < t ? bt * ex2((Gt - Gs[s]) * kLog2e) * sv[s] : 0.0f;
+                const int s = 32 * hh + 4 * s4 + x;
+                w[x] = s < t ? bt * ex2((Gt - Gs[s]) * kLog2e) * sv[4 * s4 + x] : 0.0f;
             }
-            *reinterpret_cast<float4 *>(Am + t * AST + 4 * s4) = make_float4(w[0], w[1], w[2], w[3]);
+            *reinterpret_cast<float4 *>(Am + t * AST + 32 * hh + 4 * s4) =
+                make_float4(w[0], w[1], w[2], w[3]);
         }
     } else {
-        const int t = tid - 64;
+        const int t = r - 64;
         const float Gt = Gs[t];
-        float4 *row = reinterpret_cast<float4 *>(atm + (64 + t) * 64);
+        float4 *row = reinterpret_cast<float4 *>(atm + (64 + t) * 64 + 32 * hh);
 #pragma unroll
-        for (int s4 = 0; s4 < 16; ++s4) {
+        for (int s4 = 0; s4 < 8; ++s4) {
             uint32_t w[4];
 #pragma unroll
             for (int x = 0; x < 4; ++x) {
-                const int s = 4 * s4 + x;
-                w[x] = s <= t ? to_tf32(a.scale * ex2((Gt - Gs[s]) * kLog2e) * sv[s]) : 0u;
+                const int s = 32 * hh + 4 * s4 + x;
+                w[x] = s <= t ? to_tf32(a.scale * ex2((Gt - Gs[s]) * kLog2e) * sv[4 * s4 + x])
+                              : 0u;
             }
             row[s4] = make_float4(__uint_as_float(w[0]), __uint_as_float(w[1]),
                                   __uint_as_float(w[2]), __uint_as_float(w[3]));
@@ -312,54 +301,62 @@ __global__ void __launch_bounds__(gc::PREP_NT)
     }
     __syncthreads(); // A complete
 
-    // T = (I + A)^-1, column cc per thread: diagonal 16x16 blocks first
-    if (tid < 64) {
-        const int cc = tid, bi = cc >> 4, c0 = cc & 15;
+    // T = (I + A)^-1.  Diagonal 16x16 blocks by forward substitution: column
+    // cc = tid / 4, lane p = tid % 4 holds x[4k + p]; row r's dot product is
+    // split over the four lanes (A is zero on and above the diagonal, and the
+    // x entries not yet computed are zero, so every row sums all 16 terms)
+    const int cc = tid >> 2, p = tid & 3;
+    {
+        const int bi = cc >> 4, c0 = cc & 15;
         float *tcol = Tt + cc * AST;
+        *reinterpret_cast<float4 *>(tcol + 16 * p) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(tcol + 16 * p + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(tcol + 16 * p + 8) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(tcol + 16 * p + 12) = make_float4(0.f, 0.f, 0.f, 0.f);
+        float xs[4];
 #pragma unroll
-        for (int r4 = 0; r4 < 16; ++r4)
-            *reinterpret_cast<float4 *>(tcol + 4 * r4) = make_float4(0.f, 0.f, 0.f, 0.f);
-        float x[16];
+        for (int k = 0; k < 4; ++k)
+            xs[k] = 4 * k + p == c0 ? 1.0f : 0.0f;
+        const float *Ab = Am + (16 * bi) * AST + 16 * bi + p;
 #pragma unroll
-        for (int m = 0; m < 16; ++m)
-            x[m] = m == c0 ? 1.0f : 0.0f;
-        const float *Ab = Am + (16 * bi) * AST + 16 * bi;
+        for (int rr = 1; rr < 16; ++rr) {
+            float part = 0.0f;
 #pragma unroll
-        for (int r = 1; r < 16; ++r) {
-            float acc = 0.0f;
-#pragma unroll
-            for (int m = 0; m < r; ++m)
-                acc = fmaf(Ab[r * AST + m], x[m], acc);
-            if (r > c0)
-                x[r] = -acc;
+            for (int k = 0; k < 4; ++k)
+                part = fmaf(Ab[rr * AST + 4 * k], xs[k], part);
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            if (rr > c0 && (rr & 3) == p)
+                xs[rr >> 2] = -part;
         }
+        __syncwarp();
 #pragma unroll
-        for (int r4 = 0; r4 < 4; ++r4)
-            *reinterpret_cast<float4 *>(tcol + 16 * bi + 4 * r4) =
-                make_float4(x[4 * r4], x[4 * r4 + 1], x[4 * r4 + 2], x[4 * r4 + 3]);
+        for (int k = 0; k < 4; ++k)
+            tcol[16 * bi + 4 * k + p] = xs[k];
     }
     __syncthreads(); // every diagonal block is in Tt
-    if (warp < 3) {
-        // warp j: the block rows below diagonal block j of its 16 columns
-        const int j = warp, hh = lane >> 4, cc = 16 * j + (lane & 15);
+    {
+        // the block rows below the column's own diagonal block, in order
+        const int j = cc >> 4; // warp-uniform: a warp holds 8 columns of one block
         if (j < 1)
-            solve_block_row<1>(Am, Tt, cc, hh);
+            solve_block_row<1>(Am, Tt, cc, p, lane);
         __syncwarp();
         if (j < 2)
-            solve_block_row<2>(Am, Tt, cc, hh);
+            solve_block_row<2>(Am, Tt, cc, p, lane);
         __syncwarp();
-        solve_block_row<3>(Am, Tt, cc, hh);
+        if (j < 3)
+            solve_block_row<3>(Am, Tt, cc, p, lane);
     }
     __syncthreads(); // T complete
     {
-        // T'' = T diag(beta) as rows 0-63 of [T''; M]: thread (column s, half
-        // of the rows) reads its column of Tt 4 rows at a time; every warp
-        // store covers 128 contiguous bytes of one row
-        const int sc = tid & 63, t0r = 32 * (tid >> 6);
+        // T'' = T diag(beta) as rows 0-63 of [T''; M]: thread (column s, row
+        // quarter q) reads its column of Tt 4 rows at a time; every warp store
+        // covers 128 contiguous bytes of one row
+        const int sc = tid & 63, t0r = 16 * (tid >> 6);
         const float bc = Bs[sc];
         const float *tcol = Tt + sc * AST + t0r;
 #pragma unroll
-        for (int t4 = 0; t4 < 8; ++t4) {
+        for (int t4 = 0; t4 < 4; ++t4) {
             const float4 v = *reinterpret_cast<const float4 *>(tcol + 4 * t4);
             float *o = atm + (t0r + 4 * t4) * 64 + sc;
             o[0] = __uint_as_float(to_tf32(v.x * bc));
@@ -392,7 +389,6 @@ __global__ void __launch_bounds__(gc::PREP_NT)
         tc_fence_after();
         tmem_dealloc(tmem, 64);
     }
-    (void)ok;
 }
 
 // ---------------------------------------------------------------------------
