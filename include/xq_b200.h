@@ -28,6 +28,8 @@
  *   xq_fa_partials +      split partials + LSE reduction
  *   xq_lse_merge          (shaders/rkva/rkva_range_attn.hlsl:59-106,
  *                          rkva_range_reduce_opt.hlsl:26-133)
+ *   xq_attend_range_kvarn4  RemoteAttnEngine::attend_range over native KVarN4
+ *                         records (shaders/rkva/rkva_range_attn_kvarn4.hlsl)
  *   xq_split_k            rkva_rprof::reference_split_k / optimized_split_k
  *                         (uwp/rkva/rkva-range-profile.h:98-111)
  *   xq_dequantize_rows    ggml to_float for F16/Q8_0/Q4_0 (ggml-quants.c)
@@ -159,6 +161,41 @@ int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_he
 
 /* Split count of the reference policies (host function, no GPU). */
 uint32_t xq_split_k(uint32_t active, uint32_t mode);
+
+/* ------------------------------------------------------------------------ */
+/* RKVA native KVarN4 range attention (descriptor v1 resident image; the    */
+/* reference's RemoteAttnEngine::attend_range over storage KVarN4,          */
+/* docs/rkva-kvarn-range.md "Descriptor and records",                        */
+/* shaders/rkva/rkva_range_attn_kvarn4.hlsl:64-150).  head_dim 256 = two     */
+/* 128-dim physical slices per KV head.  Each plane (K, V), 16-byte aligned: */
+/*   records [ceil(capacity/128)][2 n_head_kv][8960 B]: 4-bit values low     */
+/*           nibble first as a 128 x 128 matrix (K [dim][token], V [token]  */
+/*           [dim]), 128 F16 scales, 128 F16 zeros (per row), 128 F16        */
+/*           factors (per column); value = (q * scale + zero) * factor       */
+/*   stage   [384][n_head_kv][256] F16 rotated rows (slot 0 global group 0,  */
+/*           1 + (g - 1) % 2 otherwise)                                     */
+/*   tail    [128][n_head_kv][256] F16 original-domain rows (row % 128),     */
+/*           present when precision_tail == 128                             */
+/* Rows >= active - precision_tail come from the tail; global group 0 and  */
+/* the incomplete live group from the stage; the rest from the records.    */
+/* Rotated rows (WHT256 = Sylvester H256 / 16) meet WHT(q) and their value  */
+/* numerator is rotated back.  Query t sees rows [0, min(active,           */
+/* positions[t] - origin + 1)).  q F32 [n_tokens][n_head][256] original     */
+/* domain; out F32 [n_tokens][n_head][256]; lse F32 [n_tokens][n_head]     */
+/* (natural log; empty => O = 0, LSE = -inf).  positions: device memory.   */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    int32_t origin;         /* global position of compact row 0, % 128 == 0 */
+    int32_t capacity;       /* rows the planes hold */
+    int32_t precision_tail; /* 0 or 128 */
+    int32_t n_head_kv;
+} xq_kvarn4_desc;
+size_t xq_attend_range_kvarn4_workspace(const xq_kvarn4_desc *d, uint32_t n_head,
+                                        uint32_t active, uint32_t n_tokens);
+int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const void *v_plane,
+                           uint32_t n_head, uint32_t active, uint32_t n_tokens,
+                           const int32_t *positions, const float *q, float kq_scale, float *out,
+                           float *lse, void *ws, size_t ws_bytes, xq_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* GGML_OP_GATED_DELTA_NET                                                   */

@@ -18,6 +18,10 @@ Sources of truth (none of them this repository's own code):
   reduce.npz      tests/rkva_range_kvarn4_opt_model.py reduce_partials() on
                   the empty / poisoned / overflow states of
                   tests/rkva_range_reduce_finite_model.py.
+  kvarn4.npz      tests/rkva_range_kvarn4_opt_model.py oracle_sources() +
+                  oracle_attention() (float64, explicit Sylvester H256/16) on
+                  planes built by oracle/kvarn4.make_plane from the stored
+                  seeds (with each plane's SHA-256 to catch drift).
   gdn_selftest.npz  src/bridge/ggml_d3d12.cpp:113-158 d3d12_gdn_emulate
                   (compiled by oracle/build_ref.sh) on the selftest protocol
                   of ggml_d3d12.cpp:174-369, plus the first draws of
@@ -179,15 +183,62 @@ def make_gdn(out):
     np.savez_compressed(os.path.join(out, "gdn_selftest.npz"), **arrays)
 
 
+# (origin, capacity, precision tail, active, positions relative to origin, seed)
+KVARN4_CASES = [
+    (0, 640, 0, 520, [519], 11),
+    (0, 640, 128, 520, [300], 12),
+    (102400, 4224, 128, 4133, [4132, 4000], 13),
+    (128, 512, 128, 512, [511, -5, 200], 14),
+    (256, 1024, 0, 1000, [999], 15),
+]
+
+
+def make_kvarn4(out, ref_tests):
+    import hashlib
+    sys.path.insert(0, ref_tests)
+    import rkva_range_kvarn4_opt_model as km
+    from oracle import kvarn4 as ok
+    arrays = {}
+    for i, (origin, cap, tail, active, rel, seed) in enumerate(KVARN4_CASES):
+        desc = ok.Desc(origin, cap, tail, km.N_HEAD_KV)
+        lay = km.Layout(origin, cap, tail)
+        assert lay.half == desc.plane_bytes
+        kp = ok.make_plane(desc, active, seed)
+        vp = ok.make_plane(desc, active, seed + 1000)
+        rng = np.random.default_rng(seed + 2000)
+        q = rng.normal(0, 1, (len(rel), km.N_HEAD, km.D)).astype(np.float32)
+        pos = np.array([origin + r for r in rel], np.int32)
+        ks, exact = km.oracle_sources(lay, kp.tobytes(), active, False)
+        vs, _ = km.oracle_sources(lay, vp.tobytes(), active, True)
+        outs, lses = [], []
+        for t, p in enumerate(pos):
+            limit = km.causal_limit(lay, active, int(p))
+            o, l = km.oracle_attention(q[t], ks, vs, exact, limit, 1 / 16.0)
+            outs.append(o)
+            lses.append(l)
+        key = "c%d" % i
+        arrays[key + "_cfg"] = np.array([origin, cap, tail, active, seed], np.int64)
+        arrays[key + "_pos"] = pos
+        arrays[key + "_q"] = q
+        arrays[key + "_out"] = np.array(outs)
+        arrays[key + "_lse"] = np.array(lses)
+        arrays[key + "_sha"] = np.frombuffer(
+            hashlib.sha256(kp.tobytes() + vp.tobytes()).digest(), np.uint8)
+    np.savez_compressed(os.path.join(out, "kvarn4.npz"), **arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("XQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default=None, help="codecs|range|reduce|kvarn4|gdn")
     args = ap.parse_args()
     ref_tests = os.path.join(args.reference, "tests")
-    make_codecs(HERE)
-    make_range(HERE, ref_tests)
-    make_reduce(HERE, ref_tests)
-    make_gdn(HERE)
+    steps = {"codecs": lambda: make_codecs(HERE), "range": lambda: make_range(HERE, ref_tests),
+             "reduce": lambda: make_reduce(HERE, ref_tests),
+             "kvarn4": lambda: make_kvarn4(HERE, ref_tests), "gdn": lambda: make_gdn(HERE)}
+    for name, fn in steps.items():
+        if args.only in (None, name):
+            fn()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

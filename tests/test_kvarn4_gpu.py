@@ -1,0 +1,75 @@
+"""B200 parity: native KVarN4 range attention through the C ABI.
+
+Against the reference's own float64 model (tests/golden/kvarn4.npz, see
+test_kvarn4_cpu.py) and against the oracle restatement (oracle/kvarn4.py) on
+the edge cases: every row from the tail, records only, stage only, masked and
+partial queries, other GQA widths, many splits, an empty range.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import kvarn4 as ok
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(desc, kp, vp, active, q, pos, scale=1 / 16.0):
+    import xq
+    dev = torch.device("cuda", 0)
+    out, lse = xq.attend_range_kvarn4(
+        torch.from_numpy(kp).to(dev), torch.from_numpy(vp).to(dev),
+        torch.from_numpy(np.ascontiguousarray(q)).to(dev),
+        torch.from_numpy(np.asarray(pos, np.int32)).to(dev), desc.n_head_kv, desc.origin,
+        desc.capacity, desc.tail, active, scale)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), lse.cpu().numpy()
+
+
+def _check(out, lse, ref_out, ref_lse):
+    assert np.array_equal(np.isneginf(lse), np.isneginf(ref_lse))
+    fin = np.isfinite(ref_lse)
+    np.testing.assert_allclose(out, ref_out, rtol=1e-2, atol=2e-3)
+    np.testing.assert_allclose(lse[fin], ref_lse[fin], rtol=1e-2, atol=2e-3)
+    assert np.abs(out - ref_out).max() <= 1e-4 * max(np.abs(ref_out).max(), 1e-30)
+    if fin.any():
+        assert np.abs(lse[fin] - ref_lse[fin]).max() <= 1e-4 * np.abs(ref_lse[fin]).max()
+    assert np.all(out[~fin] == 0.0)
+
+
+@pytest.mark.parametrize("i", range(5))
+def test_kvarn4_vs_reference_model(i):
+    g = golden("kvarn4.npz")
+    origin, cap, tail, active, seed = (int(x) for x in g["c%d_cfg" % i])
+    desc = ok.Desc(origin, cap, tail, 4)
+    kp = ok.make_plane(desc, active, seed)
+    vp = ok.make_plane(desc, active, seed + 1000)
+    out, lse = _run(desc, kp, vp, active, g["c%d_q" % i], g["c%d_pos" % i])
+    _check(out, lse, g["c%d_out" % i], g["c%d_lse" % i])
+
+
+# (origin, capacity, tail, active, n_head, n_head_kv, positions relative to origin)
+CASES = [
+    (0, 256, 128, 100, 24, 4, [99, 40]),          # every row from the tail
+    (1280, 1024, 0, 1024, 24, 4, [1023]),         # records only
+    (0, 256, 0, 127, 24, 4, [126]),               # stage only (sink group, live group)
+    (384, 640, 128, 600, 16, 4, [599, -1, 250]),  # G = 4, masked and partial queries
+    (0, 1024, 128, 777, 16, 2, [776, 700]),       # G = 8
+    (128, 8192, 128, 8100, 24, 4, [8099]),        # many splits
+    (0, 512, 128, 0, 24, 4, [5]),                 # empty range
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_kvarn4_vs_oracle(case):
+    origin, cap, tail, active, n_head, n_kv, rel = case
+    desc = ok.Desc(origin, cap, tail, n_kv)
+    seed = 500 + cap + active
+    kp = ok.make_plane(desc, active, seed)
+    vp = ok.make_plane(desc, active, seed + 1)
+    q = np.random.default_rng(seed + 2).normal(0, 1, (len(rel), n_head, 256)).astype(np.float32)
+    pos = [origin + r for r in rel]
+    out, lse = _run(desc, kp, vp, active, q, pos)
+    ref_out, ref_lse = ok.attend(desc, kp, vp, active, q, pos, 1 / 16.0, n_head)
+    _check(out, lse, ref_out, ref_lse)

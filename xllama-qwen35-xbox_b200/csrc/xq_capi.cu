@@ -535,6 +535,76 @@ int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_he
 }
 
 // ---------------------------------------------------------------------------
+// Native KVarN4 range attention.
+
+// Splits of whole 128-row record groups: about two CTAs per SM, at most one
+// split per group.
+static int64_t kvarn4_rows_per_split(uint32_t active, uint32_t n_head_kv, uint32_t n_tokens) {
+    const int64_t groups = active ? (active + 127) / 128 : 1;
+    int64_t s = (2 * (int64_t)sm_count() + (int64_t)n_head_kv * n_tokens - 1) /
+                ((int64_t)n_head_kv * n_tokens);
+    s = s < 1 ? 1 : s > groups ? groups : s;
+    return 128 * ((groups + s - 1) / s);
+}
+
+size_t xq_attend_range_kvarn4_workspace(const xq_kvarn4_desc *d, uint32_t n_head,
+                                        uint32_t active, uint32_t n_tokens) {
+    if (!d || d->n_head_kv <= 0 || !n_tokens)
+        return 0;
+    const int64_t rows = kvarn4_rows_per_split(active, (uint32_t)d->n_head_kv, n_tokens);
+    const int64_t s = active ? (active + rows - 1) / rows : 1;
+    return (size_t)s * n_tokens * n_head * 258 * sizeof(float);
+}
+
+int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const void *v_plane,
+                           uint32_t n_head, uint32_t active, uint32_t n_tokens,
+                           const int32_t *positions, const float *q, float kq_scale, float *out,
+                           float *lse, void *ws, size_t ws_bytes, xq_stream_t stream) {
+    if (!d || !k_plane || !v_plane || !positions || !q || !out)
+        return fail(XQ_ERR_INVALID, "attend_range_kvarn4: null argument");
+    if (d->origin < 0 || d->origin % 128 || d->capacity <= 0 ||
+        (d->precision_tail != 0 && d->precision_tail != 128) || d->n_head_kv <= 0)
+        return fail(XQ_ERR_INVALID,
+                    "attend_range_kvarn4: descriptor (origin %% 128, capacity > 0, tail 0/128)");
+    if (active > (uint32_t)d->capacity || n_head == 0 || n_head % d->n_head_kv ||
+        n_head / d->n_head_kv > 8 || n_tokens == 0 || n_tokens > 65535 ||
+        (uint32_t)d->n_head_kv > 65535)
+        return fail(XQ_ERR_INVALID,
+                    "attend_range_kvarn4: shape (active <= capacity, 1..8 q heads per kv head)");
+    if (((reinterpret_cast<uintptr_t>(k_plane) | reinterpret_cast<uintptr_t>(v_plane)) & 15) != 0)
+        return fail(XQ_ERR_INVALID, "attend_range_kvarn4: planes must be 16-byte aligned");
+    const int64_t rows = kvarn4_rows_per_split(active, (uint32_t)d->n_head_kv, n_tokens);
+    const int64_t s = active ? (active + rows - 1) / rows : 1;
+    const size_t need = (size_t)s * n_tokens * n_head * 258 * sizeof(float);
+    if (!ws || ws_bytes < need)
+        return fail(XQ_ERR_WORKSPACE, "attend_range_kvarn4: workspace %zu < %zu bytes", ws_bytes,
+                    need);
+    xq::Kvarn4Launch l;
+    l.k = static_cast<const uint8_t *>(k_plane);
+    l.v = static_cast<const uint8_t *>(v_plane);
+    l.q = q;
+    l.positions = positions;
+    l.partials = static_cast<float *>(ws);
+    l.records_bytes = (int64_t)((d->capacity + 127) / 128) * 2 * d->n_head_kv * 8960;
+    l.origin = d->origin;
+    l.active = (int)active;
+    l.tail = d->precision_tail;
+    l.n_head = (int)n_head;
+    l.n_head_kv = d->n_head_kv;
+    l.n_tokens = (int)n_tokens;
+    l.rows_per_split = (int)rows;
+    l.n_splits = (int)s;
+    l.scale = kq_scale;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int rc = cuda_status(xq::launch_kvarn4(l, st), "attend_range_kvarn4 partials");
+    if (rc)
+        return rc;
+    return cuda_status(xq::launch_merge(l.partials, s, (int64_t)n_tokens * n_head, 256, out, lse,
+                                        nullptr, 1, st),
+                       "attend_range_kvarn4 merge");
+}
+
+// ---------------------------------------------------------------------------
 // GATED_DELTA_NET.
 
 // Validates a GATED_DELTA_NET call and fills the kernel arguments.

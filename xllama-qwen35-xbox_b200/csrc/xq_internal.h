@@ -123,6 +123,20 @@ size_t gdn_chunk_workspace(int T, int H, int n_seq, int slots);
 bool gdn_chunk_eligible(const GdnArgs &a);
 cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st);
 
+// Native KVarN4 range-attention partials (xq_kvarn4.cu): one (acc[256], max,
+// denom) record per (split, token, query head); splits cover rows_per_split
+// rows, a multiple of 128.
+struct Kvarn4Launch {
+    const uint8_t *k, *v;
+    const float *q;
+    const int32_t *positions;
+    float *partials;
+    int64_t records_bytes;
+    int origin, active, tail, n_head, n_head_kv, n_tokens, rows_per_split, n_splits;
+    float scale;
+};
+cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st);
+
 cudaError_t launch_dequant(int type, const void *src, uint64_t src_stride, float *dst,
                            uint64_t dst_stride, int64_t n_rows, int64_t n_per_row,
                            cudaStream_t st);

@@ -21,6 +21,7 @@ EXPORTS = (
     "xq_lse_merge_records",
     "xq_attend_range_workspace", "xq_attend_range", "xq_split_k", "xq_gated_delta_net",
     "xq_gated_delta_net_workspace", "xq_gated_delta_net_ws",
+    "xq_attend_range_kvarn4_workspace", "xq_attend_range_kvarn4",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
     "xq_flash_attn_ext_noalloc", "xq_set_rows",
 )
@@ -35,6 +36,11 @@ class XqError(RuntimeError):
 class Tensor(C.Structure):
     _fields_ = [("type", C.c_int32), ("reserved", C.c_int32), ("data", C.c_void_p),
                 ("ne", C.c_int64 * 4), ("nb", C.c_uint64 * 4)]
+
+
+class Kvarn4Desc(C.Structure):
+    _fields_ = [("origin", C.c_int32), ("capacity", C.c_int32), ("precision_tail", C.c_int32),
+                ("n_head_kv", C.c_int32)]
 
 
 class FaParams(C.Structure):
@@ -69,6 +75,9 @@ def lib():
         "xq_split_k": (u32, [u32, u32]),
         "xq_gated_delta_net": (C.c_int, [P(Tensor)] * 6 + [vp, i32, vp]),
         "xq_gated_delta_net_workspace": (sz, [P(Tensor), i32]),
+        "xq_attend_range_kvarn4_workspace": (sz, [P(Kvarn4Desc), u32, u32, u32]),
+        "xq_attend_range_kvarn4": (C.c_int, [P(Kvarn4Desc), vp, vp, u32, u32, u32, vp, vp,
+                                             C.c_float, vp, vp, vp, sz, vp]),
         "xq_gated_delta_net_ws": (C.c_int, [P(Tensor)] * 6 + [vp, i32, vp, sz, vp]),
         "xq_dequantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_quantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),

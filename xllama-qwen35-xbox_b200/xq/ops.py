@@ -229,6 +229,28 @@ def attend_range(storage: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor
     return out, lse
 
 
+def attend_range_kvarn4(k_plane: torch.Tensor, v_plane: torch.Tensor, q: torch.Tensor,
+                        positions: torch.Tensor, n_head_kv: int, origin: int, capacity: int,
+                        precision_tail: int, active: int, kq_scale: float, stream=None):
+    """RKVA range attention over native KVarN4 planes (uint8, 16-byte aligned,
+    layout in include/xq_b200.h); q float32 (n_tokens, n_head, 256),
+    positions int32 (n_tokens,) on the device.  Returns (out, lse)."""
+    from ._lib import Kvarn4Desc
+    n_tokens, n_head, D = q.shape
+    assert D == 256 and q.is_contiguous() and positions.dtype == torch.int32
+    desc = Kvarn4Desc(origin, capacity, precision_tail, n_head_kv)
+    out = torch.empty((n_tokens, n_head, D), dtype=torch.float32, device=q.device)
+    lse = torch.empty((n_tokens, n_head), dtype=torch.float32, device=q.device)
+    nbytes = lib().xq_attend_range_kvarn4_workspace(C.byref(desc), n_head, active, n_tokens)
+    ws = _workspace(nbytes, q.device)
+    check(lib().xq_attend_range_kvarn4(C.byref(desc), k_plane.data_ptr(), v_plane.data_ptr(),
+                                       n_head, active, n_tokens, positions.data_ptr(),
+                                       q.data_ptr(), kq_scale, out.data_ptr(), lse.data_ptr(),
+                                       ws.data_ptr() if ws is not None else None,
+                                       ws.numel() if ws is not None else 0, _stream(stream)))
+    return out, lse
+
+
 def gated_delta_net(q, k, v, g, beta, state, slots: int = 1, out=None, stream=None,
                     chunked: bool = True):
     """GGML_OP_GATED_DELTA_NET.  q, k (n_seq_qk, T, H_k, S); v (n_seq, T, H, S);
