@@ -605,6 +605,122 @@ def run_kvw(args, torch):
     }
 
 
+# native KVarN4 range attention: the reference's overflow layout (records past
+# origin 102400, precision tail 128), 24 Q / 4 KV heads, D=256, one query
+KV4 = dict(n_head=24, n_hkv=4, origin=102400, active=32768, tail=128)
+
+
+def kvarn4_bytes(w=KV4, active=None):
+    """Bytes the call must read and write: the records of every group that has
+    rows below the tail (each KV head's two slices, K and V), the stage and
+    tail rows used, q, out and lse."""
+    from oracle import kvarn4 as ok
+    active = w["active"] if active is None else active
+    desc = ok.Desc(w["origin"], active, w["tail"], w["n_hkv"])
+    tail_begin = active - min(active, w["tail"])
+    rec_groups = stage_rows = 0
+    for g in range((active + 127) // 128):
+        lo, hi = 128 * g, min(128 * (g + 1), tail_begin)
+        if lo >= hi:
+            continue
+        if ok.staged(desc, g, active):
+            stage_rows += hi - lo
+        else:
+            rec_groups += 1
+    n = (rec_groups * desc.phys * ok.RECORD + (stage_rows + active - tail_begin) * desc.row_bytes)
+    return 2 * n + w["n_head"] * 256 * 4 * 2 + w["n_head"] * 4
+
+
+def run_kvarn4(args, torch):
+    import xq
+    from oracle import kvarn4 as ok
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    w = KV4
+    hbm, _, peak_kind = peaks()
+    desc = ok.Desc(w["origin"], w["active"], w["tail"], w["n_hkv"])
+    kp = torch.from_numpy(ok.make_plane(desc, w["active"], 1)).to(dev)
+    vp = torch.from_numpy(ok.make_plane(desc, w["active"], 2)).to(dev)
+    step_bytes = kvarn4_bytes()
+    n_sets = max(4, math.ceil(2 * L2_BYTES / step_bytes) + 1)
+    planes = [(kp.clone(), vp.clone()) for _ in range(n_sets)]
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    q = torch.randn((1, w["n_head"], 256), generator=g, device=dev)
+    pos = torch.tensor([w["origin"] + w["active"] - 1], dtype=torch.int32, device=dev)
+
+    def step(i):
+        k, v = planes[i % n_sets]
+        xq.attend_range_kvarn4(k, v, q, pos, w["n_hkv"], w["origin"], w["active"], w["tail"],
+                               w["active"], 1 / 16.0)
+
+    clk = ClockSampler(dev.index)
+    clk.start()
+    ms = graph_timed(torch, step, args.steps, args.warmup) / args.steps
+    clocks = clk.stop()
+    # end to end: q from pinned host memory, out + lse read back; the planes
+    # stay resident (the server's KV image)
+    q_host = q.cpu().pin_memory()
+    o_host = torch.empty((1, w["n_head"], 256), dtype=torch.float32, pin_memory=True)
+    outs = {}
+
+    def e2e_step(i):
+        q.copy_(q_host, non_blocking=True)
+        k, v = planes[0]
+        o, _ = xq.attend_range_kvarn4(k, v, q, pos, w["n_hkv"], w["origin"], w["active"],
+                                      w["tail"], w["active"], 1 / 16.0)
+        outs[0] = o
+        o_host.copy_(o, non_blocking=True)
+    e2e_ms = graph_timed(torch, e2e_step, max(3, args.steps // 4), args.warmup) / max(
+        3, args.steps // 4)
+    value = step_bytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": "KVarN4 range attention GB/s", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u4 records / f16 rows -> f32",
+        "data": "synthetic (seeded native records, stage and tail rows; q N(0,1))",
+        "config": {"workload": "native KVarN4 range attention, 24 Q / 4 KV heads, D=256, "
+                               "32768 rows past origin 102400, precision tail 128, 1 query",
+                   "bytes_per_step": step_bytes,
+                   "l2": "rotating %d plane sets (%.0f MB > 2x L2)" % (n_sets,
+                                                                      n_sets * step_bytes / 1e6)},
+        "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": hbm, "unit": "GB/s",
+                     "frac": round(value / hbm, 4), "peak_kind": peak_kind,
+                     "kernel": "kvarn4_partials_kernel + lse_merge",
+                     "traffic": profile_traffic("kvarn4_kv4")},
+        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": int(q.numel() * 4),
+                "d2h_bytes_per_step": int(o_host.numel() * 4)},
+        "gpu_launches": args.steps * 2,
+        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
+        "clocks": clocks,
+    }
+
+
+def cpu_kvarn4_sample(active=4096):
+    """The oracle restatement (float64 numpy, record decode per group) on the
+    first `active` rows of the same layout."""
+    from oracle import kvarn4 as ok
+    w = KV4
+    desc = ok.Desc(w["origin"], active, w["tail"], w["n_hkv"])
+    kp = ok.make_plane(desc, active, 1)
+    vp = ok.make_plane(desc, active, 2)
+    q = np.random.default_rng(0).normal(0, 1, (1, w["n_head"], 256)).astype(np.float32)
+    t = time.perf_counter()
+    reps = 0
+    while True:
+        ok.attend(desc, kp, vp, active, q, [w["origin"] + active - 1], 1 / 16.0, w["n_head"])
+        reps += 1
+        if time.perf_counter() - t > 3.0 or reps >= 10:
+            break
+    dt = (time.perf_counter() - t) / reps
+    return kvarn4_bytes(active=active) / dt / 1e9, {
+        "cores": 1, "unit": "GB/s",
+        "sample": f"{active} rows (of {w['active']}), {reps} reps, {dt * 1e3:.0f} ms each, "
+                  f"numpy float64, 1 thread"}
+
+
 def cpu_kvw_sample(n_tok=1024):
     """The oracle's reference quantizer (all rows of n_tok tokens, K and V)
     plus the scatter, on the host."""
@@ -692,7 +808,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="auto",
-                    choices=["auto", "c1", "c2", "c2q4", "c3a", "c3b", "c4", "c5", "kvw"])
+                    choices=["auto", "c1", "c2", "c2q4", "c3a", "c3b", "c4", "c5", "kvw", "kv4"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -700,7 +816,7 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     workload = args.workload if args.workload != "auto" else ("c2" if world == 1 else "c5")
 
-    single = workload in ("c3a", "c3b", "c4", "kvw")
+    single = workload in ("c3a", "c3b", "c4", "kvw", "kv4")
     if args.impl == "reference":
         if rank != 0:
             return 0
@@ -711,6 +827,8 @@ def main():
             (val, info), metric, unit = cpu_prefill_sample(), "causal prefill TFLOP/s", "TFLOP/s"
         elif workload == "kvw":
             (val, info), metric = cpu_kvw_sample(), "KV-cache write GB/s"
+        elif workload == "kv4":
+            (val, info), metric = cpu_kvarn4_sample(), "KVarN4 range attention GB/s"
         else:
             val, info = cpu_oracle_sample(workload)
         val = float(f"{val:.4g}")
@@ -731,10 +849,10 @@ def main():
         if world > 1:
             print(json.dumps({"error": f"workload {workload} runs on one GPU"}), flush=True)
             return 2
-        runs = {"c4": run_prefill, "kvw": run_kvw}
+        runs = {"c4": run_prefill, "kvw": run_kvw, "kv4": run_kvarn4}
         line = runs[workload](args, torch) if workload in runs else run_gdn(args, torch, workload)
         if not args.no_cpu_baseline:
-            samples = {"c4": cpu_prefill_sample, "kvw": cpu_kvw_sample}
+            samples = {"c4": cpu_prefill_sample, "kvw": cpu_kvw_sample, "kv4": cpu_kvarn4_sample}
             val, info = samples[workload]() if workload in samples else cpu_gdn_sample(workload)
             line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": info["unit"],
                                     "cores": info["cores"], "kind": "port",
