@@ -13,10 +13,12 @@
 // groups.  A record group's four records (K and V, two 128-dim slices each)
 // are double-buffered into shared memory with cp.async.  Scores use the
 // factorised decode other_t * (sum_d (q_d scale_d) nib_dt + sum_d q_d zero_d)
-// (thread = token x slice); the value numerator is accumulated per dimension
-// in registers, other_d * (sum_t (w_t scale_t) nib_td + sum_t w_t zero_t)
-// (thread = dimension).  Stage and tail rows are read straight from global
-// memory with the same thread mapping.
+// and the value numerator other_d * (sum_t (w_t scale_t) nib_td + sum_t w_t
+// zero_t) are tensor-core products (mma.sync m16n8k16): the 4-bit values
+// expand exactly to f16 in registers, the f32 query / weight operand is split
+// into an f16 high part and remainder (two products, ~2^-22 relative), the
+// accumulators stay in the mma fragment layout.  Stage and tail rows are read
+// straight from global memory into the same products.
 #include <cuda_fp16.h>
 #include <float.h>
 #include <math.h>
@@ -101,8 +103,38 @@ namespace k4 {
 struct Cta {
     float *q, *qr, *qs, *p, *s, *ws, *red; // red: [0,16) qz, [16,24) m, [24,32) den,
                                            // [32,40) alpha, [40,56) wz
-    int tid, warp, lane, G;
+    int tid, warp, lane, g, c, G;          // g = lane / 4, c = lane % 4 (mma fragments)
 };
+
+// D += A B, m16n8k16, f16 inputs, f32 accumulate.  Rows 8..15 of A are zero
+// here (at most 8 query heads per KV head), so their registers are 0.
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+// f32 pair -> f16x2 high part and f16x2 remainder: x = hi + lo to about 2^-22
+// relative, so two f16 products carry an fp32 operand
+__device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+// two 4-bit values -> f16x2 exactly: 0x6400 | n is the f16 1024 + n
+__device__ __forceinline__ uint32_t nib2(uint32_t n0, uint32_t n1) {
+    const uint32_t v = n0 | (n1 << 16) | 0x64006400u;
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&v), __floats2half2_rn(1024.f, 1024.f));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t h2pair(const uint8_t *p0, const uint8_t *p1) {
+    return (uint32_t) * reinterpret_cast<const uint16_t *>(p0) |
+           ((uint32_t) * reinterpret_cast<const uint16_t *>(p1) << 16);
+}
 
 // Online softmax over the scores in s[g][0..n): running max / denominator
 // update, weights back into s, per-query rescale factor in red[32 + g].
@@ -136,90 +168,93 @@ __device__ __forceinline__ void softmax_tile(const Cta c, int n) {
     __syncthreads();
 }
 
+// A fragment (rows g < G, columns k0 + 2c, +1, +8, +9) of a [8][ld] float
+// matrix with row stride ld (or of a [k][8] matrix when transposed), as hi/lo
+__device__ __forceinline__ void afrag(const Cta c, const float *m, int k0, int rs, int ks,
+                                      uint32_t &a0h, uint32_t &a0l, uint32_t &a2h, uint32_t &a2l) {
+    const int k = k0 + 2 * c.c;
+    const bool on = c.g < c.G;
+    const float *r = m + c.g * rs;
+    split2(on ? r[k * ks] : 0.f, on ? r[(k + 1) * ks] : 0.f, a0h, a0l);
+    split2(on ? r[(k + 8) * ks] : 0.f, on ? r[(k + 9) * ks] : 0.f, a2h, a2l);
+}
+
 // n <= 128 consecutive F16 rows (row stride row_bytes; this KV head's 256
-// values at +kv*512): stage rows (rotated, meet WHT(q), accumulate into
-// acc_r) or tail rows (original, meet q, accumulate into acc_t).
+// values): stage rows (rotated, meet WHT(q), accumulate into acc_r) or tail
+// rows (original, meet q, accumulate into acc_t).  Accumulators are in the
+// mma C layout: query head g, dims 32 warp + 8 i + 2 c + {0, 1}.
 template <bool ORIGINAL>
 __device__ __forceinline__ void f16_tile(const Cta c, const uint8_t *krows, const uint8_t *vrows,
                                          int64_t row_bytes, int n, float scale,
-                                         float (&acc_r)[GMAX], float (&acc_t)[GMAX]) {
+                                         float (&acc_r)[4][2], float (&acc_t)[4][2]) {
     {
-        // scores: thread = (row, slice); the slice's 8 + 8 loads in flight
-        const int t = c.tid & 127, sl = c.tid >> 7;
-        float acc[GMAX];
+        // scores: warp w takes rows 16 w .. 16 w + 15 (two 8-row n-tiles)
+        float dk[2][4] = {};
+        const float *qv = ORIGINAL ? c.q : c.qr;
+        for (int kk = 0; kk < 16; ++kk) {
+            uint32_t a0h, a0l, a2h, a2l;
+            afrag(c, qv, 16 * kk, 256, 1, a0h, a0l, a2h, a2l);
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            acc[g] = 0.0f;
-        if (t < n) {
-            const uint4 *krow = reinterpret_cast<const uint4 *>(krows + t * row_bytes + sl * 256);
-            const float *qv = (ORIGINAL ? c.q : c.qr) + sl * 128;
-#pragma unroll
-            for (int hlf = 0; hlf < 2; ++hlf) {
-                uint4 raw[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    raw[i] = __ldg(krow + 8 * hlf + i);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const __half2 *hp = reinterpret_cast<const __half2 *>(&raw[i]);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float2 kf = __half22float2(hp[j]);
-                        const int d = 8 * (8 * hlf + i) + 2 * j;
-#pragma unroll
-                        for (int g = 0; g < GMAX; ++g)
-                            if (g < c.G)
-                                acc[g] = fmaf(qv[g * 256 + d], kf.x,
-                                              fmaf(qv[g * 256 + d + 1], kf.y, acc[g]));
-                    }
+            for (int ti = 0; ti < 2; ++ti) {
+                const int row = 16 * c.warp + 8 * ti + c.g;
+                uint32_t b0 = 0, b1 = 0;
+                if (row < n) {
+                    const uint8_t *kr = krows + row * row_bytes + 2 * (16 * kk + 2 * c.c);
+                    b0 = __ldg(reinterpret_cast<const uint32_t *>(kr));
+                    b1 = __ldg(reinterpret_cast<const uint32_t *>(kr + 16));
                 }
+                mma16816(dk[ti], a0h, a2h, b0, b1);
+                mma16816(dk[ti], a0l, a2l, b0, b1);
             }
         }
+        if (c.g < c.G)
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            if (g < c.G)
-                c.p[(sl * 8 + g) * 128 + t] = acc[g];
-    }
-    __syncthreads();
-    for (int i = c.tid; i < c.G * 128; i += NT) {
-        const int g = i >> 7, t = i & 127;
-        c.s[g * 128 + t] = t < n ? (c.p[g * 128 + t] + c.p[(8 + g) * 128 + t]) * scale : -FLT_MAX;
+            for (int ti = 0; ti < 2; ++ti)
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    const int t = 16 * c.warp + 8 * ti + 2 * c.c + x;
+                    c.s[c.g * 128 + t] = t < n ? dk[ti][x] * scale : -FLT_MAX;
+                }
     }
     __syncthreads();
     softmax_tile(c, n);
     {
-        // value numerator: thread = dimension, 16 rows' loads in flight
-        const int d = c.tid;
-        float add[GMAX];
+        // value numerator: warp w takes dims 32 w .. 32 w + 31 (four n-tiles)
+        float dv[4][4] = {};
+        for (int kk = 0; kk < (n + 15) / 16; ++kk) {
+            uint32_t a0h, a0l, a2h, a2l;
+            const int k = 16 * kk + 2 * c.c;
+            const bool on = c.g < c.G;
+            const float *wr = c.s + c.g * 128;
+            split2(on && k < n ? wr[k] : 0.f, on && k + 1 < n ? wr[k + 1] : 0.f, a0h, a0l);
+            split2(on && k + 8 < n ? wr[k + 8] : 0.f, on && k + 9 < n ? wr[k + 9] : 0.f, a2h, a2l);
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            add[g] = 0.0f;
-        for (int t0 = 0; t0 < n; t0 += 16) {
-            float vf[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                vf[j] = t0 + j < n ? __half2float(__ldg(reinterpret_cast<const __half *>(
-                                         vrows + (t0 + j) * row_bytes + 2 * d)))
-                                   : 0.0f;
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-#pragma unroll
-                for (int g = 0; g < GMAX; ++g)
-                    if (g < c.G)
-                        add[g] = fmaf(t0 + j < n ? c.s[g * 128 + t0 + j] : 0.0f, vf[j], add[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            if (g < c.G) {
-                const float al = c.red[32 + g];
-                if (ORIGINAL) {
-                    acc_t[g] = acc_t[g] * al + add[g];
-                    acc_r[g] *= al;
-                } else {
-                    acc_r[g] = acc_r[g] * al + add[g];
-                    acc_t[g] *= al;
-                }
+            for (int i = 0; i < 4; ++i) {
+                const int d = 32 * c.warp + 8 * i + c.g;
+                const uint8_t *vr = vrows + 2 * d;
+                const uint32_t b0 = h2pair(k < n ? vr + k * row_bytes : vr,
+                                           k + 1 < n ? vr + (k + 1) * row_bytes : vr);
+                const uint32_t b1 = h2pair(k + 8 < n ? vr + (k + 8) * row_bytes : vr,
+                                           k + 9 < n ? vr + (k + 9) * row_bytes : vr);
+                mma16816(dv[i], a0h, a2h, b0, b1);
+                mma16816(dv[i], a0l, a2l, b0, b1);
             }
+        }
+        if (c.g < c.G) {
+            const float al = c.red[32 + c.g];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    if (ORIGINAL) {
+                        acc_t[i][x] = acc_t[i][x] * al + dv[i][x];
+                        acc_r[i][x] *= al;
+                    } else {
+                        acc_r[i][x] = acc_r[i][x] * al + dv[i][x];
+                        acc_t[i][x] *= al;
+                    }
+                }
+        }
     }
     __syncthreads();
 }
@@ -227,8 +262,8 @@ __device__ __forceinline__ void f16_tile(const Cta c, const uint8_t *krows, cons
 // Rows [t0, t0 + n) of one complete record group whose four records (K slice
 // 0/1, V slice 0/1) are in shared memory at rk.
 __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int t0, int n,
-                                            float scale, float (&acc_r)[GMAX],
-                                            float (&acc_t)[GMAX]) {
+                                            float scale, float (&acc_r)[4][2],
+                                            float (&acc_t)[4][2]) {
     // per-group query factors: qs[s][d][g] = WHT(q)_g[s*128 + d] * scale_k_s[d],
     // qz[s][g] = sum_d WHT(q)_g[s*128 + d] * zero_k_s[d]
     {
@@ -259,51 +294,58 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
     }
     __syncthreads();
     {
-        // scores: thread = (token, slice)
-        const int t = c.tid & 127, sl = c.tid >> 7;
-        const uint8_t *nib = rk + sl * REC; // [d][token] nibbles
-        const float4 *qs4 = reinterpret_cast<const float4 *>(c.qs + sl * 128 * 8);
-        float acc[GMAX];
+        // scores: warp w takes tokens 16 w .. 16 w + 15 (two 8-token n-tiles);
+        // K nibbles are [dim][token]: the word (d, tn) holds tokens 8 tn .. +7
+        float dk[2][2][4] = {};
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            acc[g] = 0.0f;
-        for (int d = 0; d < 128; ++d) {
-            const uint32_t b = nib[d * 64 + (t >> 1)];
-            const float nv = (float)((b >> ((t & 1) * 4)) & 15u);
-            const float4 qa = qs4[d * 2], qb = qs4[d * 2 + 1];
-            acc[0] = fmaf(qa.x, nv, acc[0]);
-            acc[1] = fmaf(qa.y, nv, acc[1]);
-            acc[2] = fmaf(qa.z, nv, acc[2]);
-            acc[3] = fmaf(qa.w, nv, acc[3]);
-            acc[4] = fmaf(qb.x, nv, acc[4]);
-            acc[5] = fmaf(qb.y, nv, acc[5]);
-            acc[6] = fmaf(qb.z, nv, acc[6]);
-            acc[7] = fmaf(qb.w, nv, acc[7]);
+        for (int sl = 0; sl < 2; ++sl) {
+            const uint32_t *nw = reinterpret_cast<const uint32_t *>(rk + sl * REC);
+            for (int kk = 0; kk < 8; ++kk) {
+                uint32_t a0h, a0l, a2h, a2l;
+                afrag(c, c.qs + sl * 128 * 8, 16 * kk, 1, 8, a0h, a0l, a2h, a2l);
+                const int d = 16 * kk + 2 * c.c, sh = 4 * c.g;
+#pragma unroll
+                for (int ti = 0; ti < 2; ++ti) {
+                    const int tn = 2 * c.warp + ti;
+                    const uint32_t b0 = nib2((nw[d * 16 + tn] >> sh) & 15u,
+                                             (nw[(d + 1) * 16 + tn] >> sh) & 15u);
+                    const uint32_t b1 = nib2((nw[(d + 8) * 16 + tn] >> sh) & 15u,
+                                             (nw[(d + 9) * 16 + tn] >> sh) & 15u);
+                    mma16816(dk[sl][ti], a0h, a2h, b0, b1);
+                    mma16816(dk[sl][ti], a0l, a2l, b0, b1);
+                }
+            }
         }
-        const float other = h2f(nib + 8704 + 2 * t);
+        if (c.g < c.G) {
+            const float z0 = c.red[c.g], z1 = c.red[8 + c.g];
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            c.p[(sl * 8 + g) * 128 + t] = (acc[g] + c.red[sl * 8 + g]) * other;
-    }
-    __syncthreads();
-    for (int i = c.tid; i < c.G * 128; i += NT) {
-        const int g = i >> 7, j = i & 127, t = t0 + j;
-        c.s[g * 128 + j] =
-            j < n ? (c.p[g * 128 + t] + c.p[(8 + g) * 128 + t]) * scale : -FLT_MAX;
+            for (int ti = 0; ti < 2; ++ti)
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    const int t = 16 * c.warp + 8 * ti + 2 * c.c + x;
+                    const float o0 = h2f(rk + 8704 + 2 * t), o1 = h2f(rk + REC + 8704 + 2 * t);
+                    const float sc = ((dk[0][ti][x] + z0) * o0 + (dk[1][ti][x] + z1) * o1) * scale;
+                    if (t >= t0 && t < t0 + n)
+                        c.s[c.g * 128 + (t - t0)] = sc;
+                }
+        }
     }
     __syncthreads();
     softmax_tile(c, n);
     {
-        // weights * scale_v and sum_t weights * zero_v, per slice
-        const int j = c.tid & 127, sl = c.tid >> 7;
+        // weights * scale_v (indexed by token, zero outside the range) and
+        // sum_t weights * zero_v, per slice
+        const int t = c.tid & 127, sl = c.tid >> 7;
+        const int j = t - t0;
+        const bool in = j >= 0 && j < n;
         const uint8_t *vrec = rk + (2 + sl) * REC;
-        const float sc = j < n ? h2f(vrec + 8192 + 2 * (t0 + j)) : 0.0f;
-        const float zr = j < n ? h2f(vrec + 8448 + 2 * (t0 + j)) : 0.0f;
+        const float sc = in ? h2f(vrec + 8192 + 2 * t) : 0.0f;
+        const float zr = in ? h2f(vrec + 8448 + 2 * t) : 0.0f;
         float w[GMAX];
 #pragma unroll
         for (int g = 0; g < GMAX; ++g)
-            w[g] = (g < c.G && j < n) ? c.s[g * 128 + j] : 0.0f;
-        float4 *ws4 = reinterpret_cast<float4 *>(c.ws + (sl * 128 + j) * 8);
+            w[g] = (g < c.G && in) ? c.s[g * 128 + j] : 0.0f;
+        float4 *ws4 = reinterpret_cast<float4 *>(c.ws + (sl * 128 + t) * 8);
         ws4[0] = make_float4(w[0] * sc, w[1] * sc, w[2] * sc, w[3] * sc);
         ws4[1] = make_float4(w[4] * sc, w[5] * sc, w[6] * sc, w[7] * sc);
 #pragma unroll
@@ -313,7 +355,7 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
             for (int o = 16; o; o >>= 1)
                 z += __shfl_xor_sync(0xffffffffu, z, o);
             if (c.lane == 0)
-                c.p[(sl * 8 + g) * 128 + (j >> 5)] = z;
+                c.p[(sl * 8 + g) * 128 + (t >> 5)] = z;
         }
     }
     __syncthreads();
@@ -323,35 +365,39 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
     }
     __syncthreads();
     {
-        // value numerator: thread = dimension (slice sl, dim cc)
-        const int d = c.tid, sl = d >> 7, cc = d & 127;
-        const uint8_t *vrec = rk + (2 + sl) * REC; // [token][dim] nibbles
-        const float4 *ws4 = reinterpret_cast<const float4 *>(c.ws + sl * 128 * 8);
-        float add[GMAX];
+        // value numerator: warp w takes dims 32 w .. +31 of slice w / 4;
+        // V nibbles are [token][dim]: the word (t, dn) holds dims 8 dn .. +7
+        const int sl = c.warp >> 2, dl = 32 * (c.warp & 3);
+        const uint32_t *vw = reinterpret_cast<const uint32_t *>(rk + (2 + sl) * REC);
+        float dv[4][4] = {};
+        const int k_lo = t0 >> 4, k_hi = (t0 + n + 15) >> 4;
+        for (int kk = k_lo; kk < k_hi; ++kk) {
+            uint32_t a0h, a0l, a2h, a2l;
+            afrag(c, c.ws + sl * 128 * 8, 16 * kk, 1, 8, a0h, a0l, a2h, a2l);
+            const int t = 16 * kk + 2 * c.c, sh = 4 * c.g;
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            add[g] = 0.0f;
-        for (int j = 0; j < n; ++j) {
-            const uint32_t b = vrec[(t0 + j) * 64 + (cc >> 1)];
-            const float nv = (float)((b >> ((cc & 1) * 4)) & 15u);
-            const float4 wa = ws4[j * 2], wb = ws4[j * 2 + 1];
-            add[0] = fmaf(wa.x, nv, add[0]);
-            add[1] = fmaf(wa.y, nv, add[1]);
-            add[2] = fmaf(wa.z, nv, add[2]);
-            add[3] = fmaf(wa.w, nv, add[3]);
-            add[4] = fmaf(wb.x, nv, add[4]);
-            add[5] = fmaf(wb.y, nv, add[5]);
-            add[6] = fmaf(wb.z, nv, add[6]);
-            add[7] = fmaf(wb.w, nv, add[7]);
-        }
-        const float other = h2f(vrec + 8704 + 2 * cc);
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            if (g < c.G) {
-                const float al = c.red[32 + g];
-                acc_r[g] = acc_r[g] * al + (add[g] + c.red[40 + sl * 8 + g]) * other;
-                acc_t[g] *= al;
+            for (int i = 0; i < 4; ++i) {
+                const int dn = (dl >> 3) + i;
+                const uint32_t b0 = nib2((vw[t * 16 + dn] >> sh) & 15u,
+                                         (vw[(t + 1) * 16 + dn] >> sh) & 15u);
+                const uint32_t b1 = nib2((vw[(t + 8) * 16 + dn] >> sh) & 15u,
+                                         (vw[(t + 9) * 16 + dn] >> sh) & 15u);
+                mma16816(dv[i], a0h, a2h, b0, b1);
+                mma16816(dv[i], a0l, a2l, b0, b1);
             }
+        }
+        if (c.g < c.G) {
+            const float al = c.red[32 + c.g], wz = c.red[40 + sl * 8 + c.g];
+            const uint8_t *vrec = rk + (2 + sl) * REC;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {
+                    const float other = h2f(vrec + 8704 + 2 * (dl + 8 * i + 2 * c.c + x));
+                    acc_r[i][x] = acc_r[i][x] * al + (dv[i][x] + wz) * other;
+                    acc_t[i][x] *= al;
+                }
+        }
     }
     __syncthreads();
 }
@@ -383,6 +429,8 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     c.tid = threadIdx.x;
     c.warp = c.tid >> 5;
     c.lane = c.tid & 31;
+    c.g = c.lane >> 2;
+    c.c = c.lane & 3;
     c.G = a.n_head / a.n_head_kv;
     const int split = blockIdx.x, kv = blockIdx.y, tok = blockIdx.z;
     const int64_t row_bytes = (int64_t)a.n_head_kv * 512;
@@ -409,10 +457,7 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     const int live = a.active ? (a.active - 1) / GROUP : 0;
     const bool live_partial = (a.active % GROUP) != 0;
     const int og = a.origin / GROUP;
-    float acc_r[GMAX], acc_t[GMAX];
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g)
-        acc_r[g] = acc_t[g] = 0.0f;
+    float acc_r[4][2] = {}, acc_t[4][2] = {};
 
     // a group is read from its records when it has rows in [r0, r1) below the
     // tail and is neither the global sink group nor the incomplete live group
@@ -463,22 +508,25 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     cp_async_wait<0>();
 
     // ---- numerator = WHT(rotated part) + tail part; partial record
-    float *x = c.qr; // the rotated query is no longer needed
+    float *x = c.qr;  // the rotated query is no longer needed
+    float *xt = c.qs; // tail part (the group factors are no longer needed)
     __syncthreads();
+    if (c.g < c.G)
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g)
-        if (g < c.G)
-            x[g * 256 + c.tid] = acc_r[g];
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int d = 32 * c.warp + 8 * i + 2 * c.c + e;
+                x[c.g * 256 + d] = acc_r[i][e];
+                xt[c.g * 256 + d] = acc_t[i][e];
+            }
     __syncthreads();
     wht256_smem(x, c.G, c.tid);
     const int64_t n_rows = (int64_t)a.n_tokens * a.n_head;
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-        if (g >= c.G)
-            break;
+    for (int g = 0; g < c.G; ++g) {
         const int64_t row = (int64_t)tok * a.n_head + kv * c.G + g;
         float *rec = a.partials + ((int64_t)split * n_rows + row) * 258;
-        rec[c.tid] = x[g * 256 + c.tid] + acc_t[g];
+        rec[c.tid] = x[g * 256 + c.tid] + xt[g * 256 + c.tid];
         if (c.tid == 0) {
             rec[256] = c.red[16 + g];
             rec[257] = c.red[24 + g];
