@@ -8,17 +8,26 @@
 // is rotated back with WHT at the end of the split and added to the tail's,
 // with one shared running max and denominator.
 //
-// One CTA = (split, KV head, query token), the G = n_head / n_head_kv query
-// heads of that KV head, 256 threads.  Splits cover whole 128-row record
-// groups.  A record group's four records (K and V, two 128-dim slices each)
-// are double-buffered into shared memory with cp.async.  Scores use the
-// factorised decode other_t * (sum_d (q_d scale_d) nib_dt + sum_d q_d zero_d)
-// and the value numerator other_d * (sum_t (w_t scale_t) nib_td + sum_t w_t
-// zero_t) are tensor-core products (mma.sync m16n8k16): the 4-bit values
-// expand exactly to f16 in registers, the f32 query / weight operand is split
-// into an f16 high part and remainder (two products, ~2^-22 relative), the
-// accumulators stay in the mma fragment layout.  Stage and tail rows are read
-// straight from global memory into the same products.
+// One CTA = (split, KV head, query token), the G = n_head / n_head_kv <= 8
+// query heads of that KV head, 256 threads, two CTAs per SM.  Splits cover
+// whole 128-row record groups.  A record group's four records (K and V, two
+// 128-dim slices each) are double-buffered into shared memory with cp.async,
+// the 64-byte nibble rows with their four 16-byte chunks XOR-swizzled by
+// (row / 2) % 4 so that the fragment loads below are free of bank conflicts.
+//
+// Every product is a tensor-core mma.sync m16n8k16 whose A operand is the KV
+// side (16 tokens for scores, 16 dims for the value numerator) and whose B
+// operand is the G query heads (n = 8):
+//   scores  s_t = other_t * (sum_d (q_d scale_d) nib_dt + sum_d q_d zero_d)
+//   values  n_d = other_d * (sum_t (w_t scale_t) nib_td + sum_t w_t zero_t)
+// A lane's A fragment is one byte of two words: its low nibbles are rows g and
+// its high nibbles rows g + 8 (the m axis is permuted so row g is token / dim
+// 2g and row g + 8 is 2g + 1 of the 16), expanded exactly to f16 with one
+// byte permute, one mask and one f16 multiply-add.  The fp32 query / weight
+// side is split into an f16 high part and remainder (two products, ~2^-22
+// relative).  Stage and tail rows are read straight from global memory into
+// the same products: F16 K rows are already A fragments; F16 V pairs are
+// byte-permuted into them.
 #include <cuda_fp16.h>
 #include <float.h>
 #include <math.h>
@@ -30,21 +39,24 @@ namespace xq {
 
 namespace k4 {
 constexpr int NT = 256;
-constexpr int GMAX = 8;         // query heads per KV head
-constexpr int REC = 8960;       // bytes per record
-constexpr int GROUP = 128;      // rows per record group
-constexpr int SET = 4 * REC;    // K slice 0, K slice 1, V slice 0, V slice 1
+constexpr int GMAX = 8;      // query heads per KV head
+constexpr int REC = 8960;    // bytes per record
+constexpr int GROUP = 128;   // rows per record group
+constexpr int SET = 4 * REC; // K slice 0, K slice 1, V slice 0, V slice 1
+constexpr int QLD = 264;     // padded row stride (floats) of [8][256] query / numerator rows
+constexpr int SLD = 136;     // padded row stride of the [8][128] scores
 // shared memory
-constexpr int SM_REC = 0;                        // 2 x SET
-constexpr int SM_Q = SM_REC + 2 * SET;           // q [G][256] original
-constexpr int SM_QR = SM_Q + GMAX * 256 * 4;     // WHT(q) [G][256]
-constexpr int SM_QS = SM_QR + GMAX * 256 * 4;    // per group: q_r * scale_k, [2][128][8]
-constexpr int SM_P = SM_QS + 2 * 128 * 8 * 4;    // slice partial scores [2][8][128]
-constexpr int SM_S = SM_P + 2 * 8 * 128 * 4;     // scores -> weights [8][128]
-constexpr int SM_WS = SM_QS;                     // weights * scale_v, [2][128][8] (the
-                                                 // value pass, after the scores)
-constexpr int SM_RED = SM_S + 8 * 128 * 4;       // small vectors
-constexpr int SM_BYTES = SM_RED + 4 * 64 * 4;
+constexpr int SM_REC = 0;                      // 2 x SET; x / xt numerators after the loop
+constexpr int SM_QR = SM_REC + 2 * SET;        // WHT(q) [8][QLD]
+constexpr int SM_BF = SM_QR + GMAX * QLD * 4;  // B fragments of a tile [2][8][32] uint4
+constexpr int SM_FQ = SM_BF + 2 * 8 * 32 * 16; // F16-tile B fragments of q [16][32] uint4
+constexpr int SM_FQR = SM_FQ + 16 * 32 * 16;   // ... of WHT(q)
+constexpr int SM_S = SM_FQR + 16 * 32 * 16;    // scores -> weights [8][SLD]
+constexpr int SM_MX = SM_S + GMAX * SLD * 4;   // per-warp tile max [8 warps][8]
+constexpr int SM_ZP = SM_MX + 8 * 8 * 4;       // zero-point partials [2 slices][8][4]
+constexpr int SM_DP = SM_ZP + 2 * 8 * 4 * 4;   // denominator partials [8][8]
+constexpr int SM_ST = SM_DP + 8 * 8 * 4;       // m, den, alpha, m_new [4][8]
+constexpr int SM_BYTES = SM_ST + 4 * 8 * 4;
 } // namespace k4
 
 struct Kvarn4Args {
@@ -57,64 +69,25 @@ struct Kvarn4Args {
     float scale;
 };
 
-__device__ __forceinline__ float h2f(const uint8_t *p) {
-    return __half2float(*reinterpret_cast<const __half *>(p));
-}
-
-// In-place WHT256 of x[G][256] in shared memory (thread = dimension): the
-// reference's order, seven butterfly strides inside each 128-slice, 1/sqrt(128)
-// per slice, then the (a + b, a - b) / sqrt(2) slice mix.
-__device__ void wht256_smem(float *x, int G, int d) {
-    for (int stride = 1; stride < 128; stride <<= 1) {
-        float nv[k4::GMAX];
-#pragma unroll
-        for (int g = 0; g < k4::GMAX; ++g)
-            if (g < G) {
-                const float own = x[g * 256 + d], oth = x[g * 256 + (d ^ stride)];
-                nv[g] = (d & stride) ? oth - own : own + oth;
-            }
-        __syncthreads();
-#pragma unroll
-        for (int g = 0; g < k4::GMAX; ++g)
-            if (g < G)
-                x[g * 256 + d] = nv[g];
-        __syncthreads();
-    }
-    float nv[k4::GMAX];
-    const int lo = d & 127;
-#pragma unroll
-    for (int g = 0; g < k4::GMAX; ++g)
-        if (g < G) {
-            const float a = x[g * 256 + lo] * 0.08838834764831845f;
-            const float b = x[g * 256 + lo + 128] * 0.08838834764831845f;
-            nv[g] = (d < 128 ? a + b : a - b) * 0.7071067811865475f;
-        }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < k4::GMAX; ++g)
-        if (g < G)
-            x[g * 256 + d] = nv[g];
-    __syncthreads();
-}
-
 namespace k4 {
-// Per-CTA shared-memory views and indices, passed by value to the inlined
-// phases (nothing of the kernel's state has its address taken).
+// Per-CTA shared-memory views and lane indices, passed by value to the
+// inlined phases (nothing of the kernel's state has its address taken).
 struct Cta {
-    float *q, *qr, *qs, *p, *s, *ws, *red; // red: [0,16) qz, [16,24) m, [24,32) den,
-                                           // [32,40) alpha, [40,56) wz
-    int tid, warp, lane, g, c, G;          // g = lane / 4, c = lane % 4 (mma fragments)
+    uint8_t *sm;
+    float *qr, *s, *mx, *zp, *dp, *st; // st: [0,8) m, [8,16) den, [16,24) alpha, [24,32) m_new
+    uint4 *bf, *fq, *fqr;
+    int tid, warp, lane, g, c, G;      // g = lane / 4, c = lane % 4 (mma fragments)
+    uint32_t sel;                      // byte permute: byte g % 4 of two words -> bytes 0, 2
 };
 
-// D += A B, m16n8k16, f16 inputs, f32 accumulate.  Rows 8..15 of A are zero
-// here (at most 8 query heads per KV head), so their registers are 0.
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0,
-                                         uint32_t b1) {
+// D += A B, m16n8k16, f16 inputs, f32 accumulate
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
         "{%8, %9}, {%0, %1, %2, %3};\n"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 // f32 pair -> f16x2 high part and f16x2 remainder: x = hi + lo to about 2^-22
 // relative, so two f16 products carry an fp32 operand
@@ -125,292 +98,373 @@ __device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t 
     hi = *reinterpret_cast<const uint32_t *>(&h);
     lo = *reinterpret_cast<const uint32_t *>(&l);
 }
-// two 4-bit values -> f16x2 exactly: 0x6400 | n is the f16 1024 + n
-__device__ __forceinline__ uint32_t nib2(uint32_t n0, uint32_t n1) {
-    const uint32_t v = n0 | (n1 << 16) | 0x64006400u;
-    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&v), __floats2half2_rn(1024.f, 1024.f));
-    return *reinterpret_cast<const uint32_t *>(&r);
+__device__ __forceinline__ uint4 split4(float x0, float x1, float x8, float x9) {
+    uint4 f;
+    split2(x0, x1, f.x, f.z);
+    split2(x8, x9, f.y, f.w);
+    return f;
 }
-__device__ __forceinline__ uint32_t h2pair(const uint8_t *p0, const uint8_t *p1) {
-    return (uint32_t) * reinterpret_cast<const uint16_t *>(p0) |
-           ((uint32_t) * reinterpret_cast<const uint16_t *>(p1) << 16);
+// Byte g % 4 of words x (-> row g, k pair low half) and y (high half): low
+// nibbles -> f16x2 of row g, high nibbles -> row g + 8.  0x6400 | n is the f16
+// 1024 + n and 0x6400 | 16 n is 1024 + 16 n; both map back to n exactly.
+__device__ __forceinline__ void nib_frag(uint32_t x, uint32_t y, uint32_t sel, uint32_t &lo,
+                                         uint32_t &hi) {
+    const uint32_t t = __byte_perm(x, y, sel);
+    const uint32_t a = (t & 0x000f000fu) | 0x64006400u, b = (t & 0x00f000f0u) | 0x64006400u;
+    const __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a), __float2half2_rn(1024.f));
+    const __half2 hb = __hfma2(*reinterpret_cast<const __half2 *>(&b), __float2half2_rn(0.0625f),
+                               __float2half2_rn(-64.f));
+    lo = *reinterpret_cast<const uint32_t *>(&ha);
+    hi = *reinterpret_cast<const uint32_t *>(&hb);
+}
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) {
+    return *reinterpret_cast<const uint32_t *>(p);
+}
+// two F16 values at p (4-byte aligned) as floats
+__device__ __forceinline__ float2 h2x2(const uint8_t *p) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(p));
+}
+__device__ __forceinline__ float sum4(const float *p) {
+    const float4 v = *reinterpret_cast<const float4 *>(p);
+    return (v.x + v.y) + (v.z + v.w);
 }
 
-// Online softmax over the scores in s[g][0..n): running max / denominator
-// update, weights back into s, per-query rescale factor in red[32 + g].
-__device__ __forceinline__ void softmax_tile(const Cta c, int n) {
-    if (c.warp < c.G) {
-        const int g = c.warp;
-        float mx = -FLT_MAX;
-        for (int t = c.lane; t < n; t += 32)
-            mx = fmaxf(mx, c.s[g * 128 + t]);
+// In-register WHT256 of the 256-vector held as v[i] = x[8 lane + i] by one
+// warp: Sylvester butterflies (a + b, a - b) over the index bits, three inside
+// the lane and five across lanes, then / 16.
+__device__ __forceinline__ void wht_regs(float (&v)[8], int lane) {
 #pragma unroll
-        for (int o = 16; o; o >>= 1)
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        const float m_old = c.red[16 + g], den_old = c.red[24 + g];
-        const float m_new = fmaxf(m_old, mx);
-        const float alpha = den_old == 0.0f ? 0.0f : __expf(m_old - m_new);
-        float sum = 0.0f;
-        for (int t = c.lane; t < n; t += 32) {
-            const float w = __expf(c.s[g * 128 + t] - m_new);
-            c.s[g * 128 + t] = w;
-            sum += w;
+    for (int s = 1; s < 8; s <<= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (!(i & s)) {
+                const float a = v[i], b = v[i + s];
+                v[i] = a + b;
+                v[i + s] = a - b;
+            }
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+            v[i] = (lane & m) ? o - v[i] : v[i] + o;
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1)
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (c.lane == 0) {
-            c.red[16 + g] = m_new;
-            c.red[24 + g] = den_old * alpha + sum;
-            c.red[32 + g] = alpha;
+    for (int i = 0; i < 8; ++i)
+        v[i] *= 0.0625f;
+}
+// F16-tile B fragments of query head g from v[i] = x[8 lane + i]: MMA step
+// 2j + h covers dims 32 j + 8 c + 4 h + {0, 1} (b0) and {2, 3} (b1), matching
+// a 16-byte K row load per lane.
+__device__ __forceinline__ void q_frags(const float (&v)[8], uint4 *f, int g, int lane) {
+    const int j = lane >> 2, cc = lane & 3;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        f[(2 * j + h) * 32 + 4 * g + cc] = split4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+}
+
+// Scores of tokens (row, row + 1) x queries (2c, 2c + 1) into s, and the warp's
+// per-query max into mx.  sv = {(row, q0), (row, q1), (row + 1, q0), (row + 1, q1)}.
+__device__ __forceinline__ void put_scores(const Cta c, int row, const float (&sv)[4]) {
+    const int q0 = 2 * c.c;
+    *reinterpret_cast<float2 *>(c.s + q0 * SLD + row) = make_float2(sv[0], sv[2]);
+    *reinterpret_cast<float2 *>(c.s + (q0 + 1) * SLD + row) = make_float2(sv[1], sv[3]);
+    float m0 = fmaxf(sv[0], sv[2]), m1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+        m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+    }
+    if (c.g == 0) {
+        c.mx[c.warp * 8 + q0] = m0;
+        c.mx[c.warp * 8 + q0 + 1] = m1;
+    }
+}
+// Running max after this tile for query q (< G); thread tid < 8 also publishes
+// alpha = exp(m_old - m_new) and m_new of query tid.
+__device__ __forceinline__ float tile_max(const Cta c, int q) {
+    float m = c.st[q];
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+        m = fmaxf(m, c.mx[w * 8 + q]);
+    return m;
+}
+__device__ __forceinline__ void publish_alpha(const Cta c) {
+    if (c.tid < GMAX) {
+        const int q = c.tid;
+        if (q < c.G) {
+            const float m_new = tile_max(c, q);
+            c.st[16 + q] = c.st[8 + q] == 0.0f ? 0.0f : __expf(c.st[q] - m_new);
+            c.st[24 + q] = m_new;
+        } else {
+            c.st[16 + q] = 0.0f;
         }
     }
-    __syncthreads();
 }
-
-// A fragment (rows g < G, columns k0 + 2c, +1, +8, +9) of a [8][ld] float
-// matrix with row stride ld (or of a [k][8] matrix when transposed), as hi/lo
-__device__ __forceinline__ void afrag(const Cta c, const float *m, int k0, int rs, int ks,
-                                      uint32_t &a0h, uint32_t &a0l, uint32_t &a2h, uint32_t &a2l) {
-    const int k = k0 + 2 * c.c;
-    const bool on = c.g < c.G;
-    const float *r = m + c.g * rs;
-    split2(on ? r[k * ks] : 0.f, on ? r[(k + 1) * ks] : 0.f, a0h, a0l);
-    split2(on ? r[(k + 8) * ks] : 0.f, on ? r[(k + 9) * ks] : 0.f, a2h, a2l);
+// After the value pass: den = den * alpha + tile sum, m = m_new
+__device__ __forceinline__ void update_state(const Cta c) {
+    if (c.tid < c.G) {
+        const int q = c.tid;
+        c.st[8 + q] = c.st[8 + q] * c.st[16 + q] + (sum4(c.dp + q * 8) + sum4(c.dp + q * 8 + 4));
+        c.st[q] = c.st[24 + q];
+    }
 }
 
 // n <= 128 consecutive F16 rows (row stride row_bytes; this KV head's 256
 // values): stage rows (rotated, meet WHT(q), accumulate into acc_r) or tail
-// rows (original, meet q, accumulate into acc_t).  Accumulators are in the
-// mma C layout: query head g, dims 32 warp + 8 i + 2 c + {0, 1}.
+// rows (original, meet q, accumulate into acc_t).  acc[mt][.] is the mma D
+// layout of the value numerator: rows = dims 32 warp + 16 mt + 2 g + {0, 1},
+// columns = queries 2c, 2c + 1.
 template <bool ORIGINAL>
 __device__ __forceinline__ void f16_tile(const Cta c, const uint8_t *krows, const uint8_t *vrows,
                                          int64_t row_bytes, int n, float scale,
-                                         float (&acc_r)[4][2], float (&acc_t)[4][2]) {
+                                         float (&acc_r)[2][4], float (&acc_t)[2][4]) {
     {
-        // scores: warp w takes rows 16 w .. 16 w + 15 (two 8-row n-tiles)
-        float dk[2][4] = {};
-        const float *qv = ORIGINAL ? c.q : c.qr;
-        for (int kk = 0; kk < 16; ++kk) {
-            uint32_t a0h, a0l, a2h, a2l;
-            afrag(c, qv, 16 * kk, 256, 1, a0h, a0l, a2h, a2l);
+        // scores: warp w takes rows 16 w + 2 g (A row g) and + 1 (A row g + 8)
+        const int row = 16 * c.warp + 2 * c.g;
+        const bool va = row < n, vb = row + 1 < n;
+        const uint8_t *pa = krows + (int64_t)row * row_bytes + 16 * c.c;
+        const uint8_t *pb = pa + row_bytes;
+        const uint4 *fb = ORIGINAL ? c.fq : c.fqr;
+        const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+        uint4 ka[8], kb[8];
 #pragma unroll
-            for (int ti = 0; ti < 2; ++ti) {
-                const int row = 16 * c.warp + 8 * ti + c.g;
-                uint32_t b0 = 0, b1 = 0;
-                if (row < n) {
-                    const uint8_t *kr = krows + row * row_bytes + 2 * (16 * kk + 2 * c.c);
-                    b0 = __ldg(reinterpret_cast<const uint32_t *>(kr));
-                    b1 = __ldg(reinterpret_cast<const uint32_t *>(kr + 16));
-                }
-                mma16816(dk[ti], a0h, a2h, b0, b1);
-                mma16816(dk[ti], a0l, a2l, b0, b1);
-            }
+        for (int j = 0; j < 8; ++j) {
+            ka[j] = va ? __ldg(reinterpret_cast<const uint4 *>(pa + 64 * j)) : z4;
+            kb[j] = vb ? __ldg(reinterpret_cast<const uint4 *>(pb + 64 * j)) : z4;
         }
-        if (c.g < c.G)
+        float d[4] = {};
 #pragma unroll
-            for (int ti = 0; ti < 2; ++ti)
-#pragma unroll
-                for (int x = 0; x < 2; ++x) {
-                    const int t = 16 * c.warp + 8 * ti + 2 * c.c + x;
-                    c.s[c.g * 128 + t] = t < n ? dk[ti][x] * scale : -FLT_MAX;
-                }
+        for (int j = 0; j < 8; ++j) {
+            const uint4 f0 = fb[(2 * j) * 32 + c.lane], f1 = fb[(2 * j + 1) * 32 + c.lane];
+            mma16816(d, ka[j].x, kb[j].x, ka[j].y, kb[j].y, f0.x, f0.y);
+            mma16816(d, ka[j].x, kb[j].x, ka[j].y, kb[j].y, f0.z, f0.w);
+            mma16816(d, ka[j].z, kb[j].z, ka[j].w, kb[j].w, f1.x, f1.y);
+            mma16816(d, ka[j].z, kb[j].z, ka[j].w, kb[j].w, f1.z, f1.w);
+        }
+        const float sv[4] = {va ? d[0] * scale : -INFINITY, va ? d[1] * scale : -INFINITY,
+                             vb ? d[2] * scale : -INFINITY, vb ? d[3] * scale : -INFINITY};
+        put_scores(c, row, sv);
     }
     __syncthreads();
-    softmax_tile(c, n);
     {
-        // value numerator: warp w takes dims 32 w .. 32 w + 31 (four n-tiles)
-        float dv[4][4] = {};
-        for (int kk = 0; kk < (n + 15) / 16; ++kk) {
-            uint32_t a0h, a0l, a2h, a2l;
-            const int k = 16 * kk + 2 * c.c;
-            const bool on = c.g < c.G;
-            const float *wr = c.s + c.g * 128;
-            split2(on && k < n ? wr[k] : 0.f, on && k + 1 < n ? wr[k + 1] : 0.f, a0h, a0l);
-            split2(on && k + 8 < n ? wr[k + 8] : 0.f, on && k + 9 < n ? wr[k + 9] : 0.f, a2h, a2l);
+        // weights: warp w takes tokens 16 w .. 16 w + 15 (B fragments of MMA step w)
+        publish_alpha(c);
+        float dsum = 0.0f;
+        uint4 f = make_uint4(0u, 0u, 0u, 0u);
+        if (c.g < c.G) {
+            const float m = tile_max(c, c.g);
+            const float *sr = c.s + c.g * SLD + 16 * c.warp + 2 * c.c;
+            const float2 s01 = *reinterpret_cast<const float2 *>(sr);
+            const float2 s89 = *reinterpret_cast<const float2 *>(sr + 8);
+            const float w0 = __expf(s01.x - m), w1 = __expf(s01.y - m);
+            const float w8 = __expf(s89.x - m), w9 = __expf(s89.y - m);
+            f = split4(w0, w1, w8, w9);
+            dsum = (w0 + w1) + (w8 + w9);
+        }
+        c.bf[c.warp * 32 + c.lane] = f;
+        dsum += __shfl_xor_sync(0xffffffffu, dsum, 1);
+        dsum += __shfl_xor_sync(0xffffffffu, dsum, 2);
+        if (c.c == 0)
+            c.dp[c.g * 8 + c.warp] = dsum;
+    }
+    __syncthreads();
+    {
+        // value numerator: warp w takes dims 32 w + 16 mt + 2 g (+ 1); lane
+        // loads the dim pair of tokens 16 kk + 2c + {0, 1, 8, 9}
+        const uint8_t *vp = vrows + 2 * (32 * c.warp + 2 * c.g);
+        float dv[2][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const int t = 16 * kk + 2 * c.c;
+            uint32_t x[2][4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int te = t + (e & 1) + 8 * (e >> 1);
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt)
+                    x[mt][e] = te < n ? __ldg(reinterpret_cast<const uint32_t *>(
+                                            vp + (int64_t)te * row_bytes + 32 * mt))
+                                      : 0u;
+            }
+            const uint4 b = c.bf[kk * 32 + c.lane];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const uint32_t a0 = __byte_perm(x[mt][0], x[mt][1], 0x5410);
+                const uint32_t a1 = __byte_perm(x[mt][0], x[mt][1], 0x7632);
+                const uint32_t a2 = __byte_perm(x[mt][2], x[mt][3], 0x5410);
+                const uint32_t a3 = __byte_perm(x[mt][2], x[mt][3], 0x7632);
+                mma16816(dv[mt], a0, a1, a2, a3, b.x, b.y);
+                mma16816(dv[mt], a0, a1, a2, a3, b.z, b.w);
+            }
+        }
+        const float al0 = c.st[16 + 2 * c.c], al1 = c.st[17 + 2 * c.c];
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const int d = 32 * c.warp + 8 * i + c.g;
-                const uint8_t *vr = vrows + 2 * d;
-                const uint32_t b0 = h2pair(k < n ? vr + k * row_bytes : vr,
-                                           k + 1 < n ? vr + (k + 1) * row_bytes : vr);
-                const uint32_t b1 = h2pair(k + 8 < n ? vr + (k + 8) * row_bytes : vr,
-                                           k + 9 < n ? vr + (k + 9) * row_bytes : vr);
-                mma16816(dv[i], a0h, a2h, b0, b1);
-                mma16816(dv[i], a0l, a2l, b0, b1);
-            }
-        }
-        if (c.g < c.G) {
-            const float al = c.red[32 + c.g];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int x = 0; x < 2; ++x) {
-                    if (ORIGINAL) {
-                        acc_t[i][x] = acc_t[i][x] * al + dv[i][x];
-                        acc_r[i][x] *= al;
-                    } else {
-                        acc_r[i][x] = acc_r[i][x] * al + dv[i][x];
-                        acc_t[i][x] *= al;
-                    }
+                const float al = (i & 1) ? al1 : al0;
+                if (ORIGINAL) {
+                    acc_t[mt][i] = acc_t[mt][i] * al + dv[mt][i];
+                    acc_r[mt][i] *= al;
+                } else {
+                    acc_r[mt][i] = acc_r[mt][i] * al + dv[mt][i];
+                    acc_t[mt][i] *= al;
                 }
-        }
+            }
+        update_state(c);
     }
-    __syncthreads();
 }
 
 // Rows [t0, t0 + n) of one complete record group whose four records (K slice
-// 0/1, V slice 0/1) are in shared memory at rk.
+// 0/1, V slice 0/1; nibble rows swizzled) are in shared memory at rk.
 __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int t0, int n,
-                                            float scale, float (&acc_r)[4][2],
-                                            float (&acc_t)[4][2]) {
-    // per-group query factors: qs[s][d][g] = WHT(q)_g[s*128 + d] * scale_k_s[d],
-    // qz[s][g] = sum_d WHT(q)_g[s*128 + d] * zero_k_s[d]
+                                            float scale, float (&acc_r)[2][4],
+                                            float (&acc_t)[2][4]) {
+    const int fsl = c.tid >> 7, qt = (c.tid >> 5) & 3; // fragment passes: slice, quarter
     {
-        const int d = c.tid & 127, sl = c.tid >> 7;
-        const uint8_t *rec = rk + sl * REC;
-        const float sc = h2f(rec + 8192 + 2 * d), zr = h2f(rec + 8448 + 2 * d);
-        float qv[GMAX];
+        // B fragments qs[d][g] = WHT(q)_g[d] * scale_k[d] of MMA steps qt, qt + 4
+        // of slice fsl, and the partial sums of WHT(q) . zero_k
+        const uint8_t *kr = rk + fsl * REC;
+        float z = 0.0f;
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            qv[g] = g < c.G ? c.qr[g * 256 + sl * 128 + d] : 0.0f;
-        float4 *qs4 = reinterpret_cast<float4 *>(c.qs + (sl * 128 + d) * 8);
-        qs4[0] = make_float4(qv[0] * sc, qv[1] * sc, qv[2] * sc, qv[3] * sc);
-        qs4[1] = make_float4(qv[4] * sc, qv[5] * sc, qv[6] * sc, qv[7] * sc);
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-            float z = qv[g] * zr;
-#pragma unroll
-            for (int o = 16; o; o >>= 1)
-                z += __shfl_xor_sync(0xffffffffu, z, o);
-            if (c.lane == 0)
-                c.p[(sl * 8 + g) * 128 + (d >> 5)] = z; // four warp sums per (s, g)
+        for (int h = 0; h < 2; ++h) {
+            const int kk = qt + 4 * h, dl = 16 * kk + 2 * c.c;
+            const float *qrow = c.qr + c.g * QLD + fsl * 128 + dl;
+            const float2 q01 = *reinterpret_cast<const float2 *>(qrow);
+            const float2 q89 = *reinterpret_cast<const float2 *>(qrow + 8);
+            const float2 s01 = h2x2(kr + 8192 + 2 * dl), s89 = h2x2(kr + 8192 + 2 * dl + 16);
+            const float2 z01 = h2x2(kr + 8448 + 2 * dl), z89 = h2x2(kr + 8448 + 2 * dl + 16);
+            c.bf[(fsl * 8 + kk) * 32 + c.lane] =
+                split4(q01.x * s01.x, q01.y * s01.y, q89.x * s89.x, q89.y * s89.y);
+            z += (q01.x * z01.x + q01.y * z01.y) + (q89.x * z89.x + q89.y * z89.y);
         }
-    }
-    __syncthreads();
-    if (c.tid < 16) {
-        const float *z = c.p + c.tid * 128;
-        c.red[c.tid] = (z[0] + z[1]) + (z[2] + z[3]);
+        z += __shfl_xor_sync(0xffffffffu, z, 1);
+        z += __shfl_xor_sync(0xffffffffu, z, 2);
+        if (c.c == 0)
+            c.zp[(fsl * 8 + c.g) * 4 + qt] = z;
     }
     __syncthreads();
     {
-        // scores: warp w takes tokens 16 w .. 16 w + 15 (two 8-token n-tiles);
-        // K nibbles are [dim][token]: the word (d, tn) holds tokens 8 tn .. +7
-        float dk[2][2][4] = {};
+        // scores: warp w takes tokens 16 w + 2 g (+ 1), all 256 dims; the K
+        // nibble rows are dims, the lane's word holds tokens 16 w + 8 (g / 4) ..
+        const int w = c.warp;
+        const int lane_off = 128 * c.c + 16 * ((w >> 1) ^ c.c) + 4 * (2 * (w & 1) + (c.g >> 2));
+        float d[2][4] = {};
 #pragma unroll
         for (int sl = 0; sl < 2; ++sl) {
-            const uint32_t *nw = reinterpret_cast<const uint32_t *>(rk + sl * REC);
+            const uint8_t *base = rk + sl * REC + lane_off;
+#pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
-                uint32_t a0h, a0l, a2h, a2l;
-                afrag(c, c.qs + sl * 128 * 8, 16 * kk, 1, 8, a0h, a0l, a2h, a2l);
-                const int d = 16 * kk + 2 * c.c, sh = 4 * c.g;
-#pragma unroll
-                for (int ti = 0; ti < 2; ++ti) {
-                    const int tn = 2 * c.warp + ti;
-                    const uint32_t b0 = nib2((nw[d * 16 + tn] >> sh) & 15u,
-                                             (nw[(d + 1) * 16 + tn] >> sh) & 15u);
-                    const uint32_t b1 = nib2((nw[(d + 8) * 16 + tn] >> sh) & 15u,
-                                             (nw[(d + 9) * 16 + tn] >> sh) & 15u);
-                    mma16816(dk[sl][ti], a0h, a2h, b0, b1);
-                    mma16816(dk[sl][ti], a0l, a2l, b0, b1);
-                }
+                const uint8_t *p = base + kk * 1024;
+                uint32_t a0, a1, a2, a3;
+                nib_frag(lds32(p), lds32(p + 64), c.sel, a0, a1);
+                nib_frag(lds32(p + 512), lds32(p + 576), c.sel, a2, a3);
+                const uint4 b = c.bf[(sl * 8 + kk) * 32 + c.lane];
+                mma16816(d[sl], a0, a1, a2, a3, b.x, b.y);
+                mma16816(d[sl], a0, a1, a2, a3, b.z, b.w);
             }
         }
-        if (c.g < c.G) {
-            const float z0 = c.red[c.g], z1 = c.red[8 + c.g];
-#pragma unroll
-            for (int ti = 0; ti < 2; ++ti)
-#pragma unroll
-                for (int x = 0; x < 2; ++x) {
-                    const int t = 16 * c.warp + 8 * ti + 2 * c.c + x;
-                    const float o0 = h2f(rk + 8704 + 2 * t), o1 = h2f(rk + REC + 8704 + 2 * t);
-                    const float sc = ((dk[0][ti][x] + z0) * o0 + (dk[1][ti][x] + z1) * o1) * scale;
-                    if (t >= t0 && t < t0 + n)
-                        c.s[c.g * 128 + (t - t0)] = sc;
-                }
-        }
-    }
-    __syncthreads();
-    softmax_tile(c, n);
-    {
-        // weights * scale_v (indexed by token, zero outside the range) and
-        // sum_t weights * zero_v, per slice
-        const int t = c.tid & 127, sl = c.tid >> 7;
-        const int j = t - t0;
-        const bool in = j >= 0 && j < n;
-        const uint8_t *vrec = rk + (2 + sl) * REC;
-        const float sc = in ? h2f(vrec + 8192 + 2 * t) : 0.0f;
-        const float zr = in ? h2f(vrec + 8448 + 2 * t) : 0.0f;
-        float w[GMAX];
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g)
-            w[g] = (g < c.G && in) ? c.s[g * 128 + j] : 0.0f;
-        float4 *ws4 = reinterpret_cast<float4 *>(c.ws + (sl * 128 + t) * 8);
-        ws4[0] = make_float4(w[0] * sc, w[1] * sc, w[2] * sc, w[3] * sc);
-        ws4[1] = make_float4(w[4] * sc, w[5] * sc, w[6] * sc, w[7] * sc);
-#pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-            float z = w[g] * zr;
-#pragma unroll
-            for (int o = 16; o; o >>= 1)
-                z += __shfl_xor_sync(0xffffffffu, z, o);
-            if (c.lane == 0)
-                c.p[(sl * 8 + g) * 128 + (t >> 5)] = z;
-        }
-    }
-    __syncthreads();
-    if (c.tid < 16) {
-        const float *z = c.p + c.tid * 128;
-        c.red[40 + c.tid] = (z[0] + z[1]) + (z[2] + z[3]);
+        const int row = 16 * w + 2 * c.g, q0 = 2 * c.c;
+        const float2 o0 = h2x2(rk + 8704 + 2 * row), o1 = h2x2(rk + REC + 8704 + 2 * row);
+        const float z00 = sum4(c.zp + q0 * 4), z01 = sum4(c.zp + q0 * 4 + 4);
+        const float z10 = sum4(c.zp + 32 + q0 * 4), z11 = sum4(c.zp + 32 + q0 * 4 + 4);
+        const bool va = row >= t0 && row < t0 + n, vb = row + 1 >= t0 && row + 1 < t0 + n;
+        const float sv[4] = {
+            va ? (o0.x * (d[0][0] + z00) + o1.x * (d[1][0] + z10)) * scale : -INFINITY,
+            va ? (o0.x * (d[0][1] + z01) + o1.x * (d[1][1] + z11)) * scale : -INFINITY,
+            vb ? (o0.y * (d[0][2] + z00) + o1.y * (d[1][2] + z10)) * scale : -INFINITY,
+            vb ? (o0.y * (d[0][3] + z01) + o1.y * (d[1][3] + z11)) * scale : -INFINITY};
+        put_scores(c, row, sv);
     }
     __syncthreads();
     {
-        // value numerator: warp w takes dims 32 w .. +31 of slice w / 4;
-        // V nibbles are [token][dim]: the word (t, dn) holds dims 8 dn .. +7
-        const int sl = c.warp >> 2, dl = 32 * (c.warp & 3);
-        const uint32_t *vw = reinterpret_cast<const uint32_t *>(rk + (2 + sl) * REC);
-        float dv[4][4] = {};
-        const int k_lo = t0 >> 4, k_hi = (t0 + n + 15) >> 4;
-        for (int kk = k_lo; kk < k_hi; ++kk) {
-            uint32_t a0h, a0l, a2h, a2l;
-            afrag(c, c.ws + sl * 128 * 8, 16 * kk, 1, 8, a0h, a0l, a2h, a2l);
-            const int t = 16 * kk + 2 * c.c, sh = 4 * c.g;
+        // B fragments ws[t][g] = w_g[t] * scale_v[t] of MMA steps qt, qt + 4 of
+        // slice fsl, and the partial sums of w . zero_v and of w
+        publish_alpha(c);
+        const uint8_t *vr = rk + (2 + fsl) * REC;
+        float z = 0.0f, dsum = 0.0f;
+        const bool on = c.g < c.G;
+        const float m = on ? tile_max(c, c.g) : 0.0f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int dn = (dl >> 3) + i;
-                const uint32_t b0 = nib2((vw[t * 16 + dn] >> sh) & 15u,
-                                         (vw[(t + 1) * 16 + dn] >> sh) & 15u);
-                const uint32_t b1 = nib2((vw[(t + 8) * 16 + dn] >> sh) & 15u,
-                                         (vw[(t + 9) * 16 + dn] >> sh) & 15u);
-                mma16816(dv[i], a0h, a2h, b0, b1);
-                mma16816(dv[i], a0l, a2l, b0, b1);
+        for (int h = 0; h < 2; ++h) {
+            const int kk = qt + 4 * h, t = 16 * kk + 2 * c.c;
+            uint4 f = make_uint4(0u, 0u, 0u, 0u);
+            if (on) {
+                const float *sr = c.s + c.g * SLD + t;
+                const float2 s01 = *reinterpret_cast<const float2 *>(sr);
+                const float2 s89 = *reinterpret_cast<const float2 *>(sr + 8);
+                const float w0 = __expf(s01.x - m), w1 = __expf(s01.y - m);
+                const float w8 = __expf(s89.x - m), w9 = __expf(s89.y - m);
+                const float2 c01 = h2x2(vr + 8192 + 2 * t), c89 = h2x2(vr + 8192 + 2 * t + 16);
+                const float2 z01 = h2x2(vr + 8448 + 2 * t), z89 = h2x2(vr + 8448 + 2 * t + 16);
+                f = split4(w0 * c01.x, w1 * c01.y, w8 * c89.x, w9 * c89.y);
+                z += (w0 * z01.x + w1 * z01.y) + (w8 * z89.x + w9 * z89.y);
+                dsum += (w0 + w1) + (w8 + w9);
             }
+            c.bf[(fsl * 8 + kk) * 32 + c.lane] = f;
         }
-        if (c.g < c.G) {
-            const float al = c.red[32 + c.g], wz = c.red[40 + sl * 8 + c.g];
-            const uint8_t *vrec = rk + (2 + sl) * REC;
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int x = 0; x < 2; ++x) {
-                    const float other = h2f(vrec + 8704 + 2 * (dl + 8 * i + 2 * c.c + x));
-                    acc_r[i][x] = acc_r[i][x] * al + (dv[i][x] + wz) * other;
-                    acc_t[i][x] *= al;
-                }
+        z += __shfl_xor_sync(0xffffffffu, z, 1);
+        z += __shfl_xor_sync(0xffffffffu, z, 2);
+        dsum += __shfl_xor_sync(0xffffffffu, dsum, 1);
+        dsum += __shfl_xor_sync(0xffffffffu, dsum, 2);
+        if (c.c == 0) {
+            c.zp[(fsl * 8 + c.g) * 4 + qt] = z;
+            c.dp[c.g * 8 + fsl * 4 + qt] = fsl == 0 ? dsum : 0.0f;
         }
     }
     __syncthreads();
+    {
+        // value numerator: warp w takes dims 16 mt + 2 g (+ 1) of unit
+        // 2 (w % 4) + mt of slice w / 4, all 128 tokens; the V nibble rows are
+        // tokens, the lane's word holds dims 16 unit + 8 (g / 4) ..
+        const int w = c.warp, sl = w >> 2;
+        const uint8_t *vbase =
+            rk + (2 + sl) * REC + 128 * c.c + 16 * ((w & 3) ^ c.c) + 4 * (c.g >> 2);
+        float dv[2][4] = {};
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+            const uint4 b = c.bf[(sl * 8 + kk) * 32 + c.lane];
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+                const uint8_t *p = vbase + kk * 1024 + 8 * mt;
+                uint32_t a0, a1, a2, a3;
+                nib_frag(lds32(p), lds32(p + 64), c.sel, a0, a1);
+                nib_frag(lds32(p + 512), lds32(p + 576), c.sel, a2, a3);
+                mma16816(dv[mt], a0, a1, a2, a3, b.x, b.y);
+                mma16816(dv[mt], a0, a1, a2, a3, b.z, b.w);
+            }
+        }
+        const int q0 = 2 * c.c;
+        const float al0 = c.st[16 + q0], al1 = c.st[17 + q0];
+        const float wz0 = sum4(c.zp + (sl * 8 + q0) * 4), wz1 = sum4(c.zp + (sl * 8 + q0) * 4 + 4);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+            const float2 o = h2x2(rk + (2 + sl) * REC + 8704 + 2 * (32 * (w & 3) + 16 * mt + 2 * c.g));
+            acc_r[mt][0] = acc_r[mt][0] * al0 + o.x * (dv[mt][0] + wz0);
+            acc_r[mt][1] = acc_r[mt][1] * al1 + o.x * (dv[mt][1] + wz1);
+            acc_r[mt][2] = acc_r[mt][2] * al0 + o.y * (dv[mt][2] + wz0);
+            acc_r[mt][3] = acc_r[mt][3] * al1 + o.y * (dv[mt][3] + wz1);
+            acc_t[mt][0] *= al0;
+            acc_t[mt][1] *= al1;
+            acc_t[mt][2] *= al0;
+            acc_t[mt][3] *= al1;
+        }
+        update_state(c);
+    }
 }
 
-// cp.async of group grp's four records of KV head kv into dst
+// cp.async of group grp's four records of KV head kv into dst, nibble rows
+// swizzled: 16-byte chunk ch of row r lands at chunk ch ^ ((r >> 1) & 3)
 __device__ __forceinline__ void prefetch_group(const Kvarn4Args &a, uint8_t *dst, int grp,
                                                int kv, int tid) {
     const int phys = 2 * a.n_head_kv;
     for (int i = tid; i < SET / 16; i += NT) {
-        const int which = i / (REC / 16), off = (i % (REC / 16)) * 16;
+        const int which = i / (REC / 16), u = i % (REC / 16);
         const uint8_t *plane = which < 2 ? a.k : a.v;
-        cp_async<16>(smem_u32(dst + which * REC + off),
-                     plane + ((int64_t)grp * phys + 2 * kv + (which & 1)) * REC + off);
+        const int du = u < 512 ? (u & ~3) | ((u ^ (u >> 3)) & 3) : u;
+        cp_async<16>(smem_u32(dst + which * REC + du * 16),
+                     plane + ((int64_t)grp * phys + 2 * kv + (which & 1)) * REC + u * 16);
     }
 }
 } // namespace k4
@@ -419,35 +473,28 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     using namespace k4;
     extern __shared__ __align__(16) uint8_t sm[];
     Cta c;
-    c.q = reinterpret_cast<float *>(sm + SM_Q);
+    c.sm = sm;
     c.qr = reinterpret_cast<float *>(sm + SM_QR);
-    c.qs = reinterpret_cast<float *>(sm + SM_QS);
-    c.p = reinterpret_cast<float *>(sm + SM_P);
     c.s = reinterpret_cast<float *>(sm + SM_S);
-    c.ws = reinterpret_cast<float *>(sm + SM_WS);
-    c.red = reinterpret_cast<float *>(sm + SM_RED);
+    c.mx = reinterpret_cast<float *>(sm + SM_MX);
+    c.zp = reinterpret_cast<float *>(sm + SM_ZP);
+    c.dp = reinterpret_cast<float *>(sm + SM_DP);
+    c.st = reinterpret_cast<float *>(sm + SM_ST);
+    c.bf = reinterpret_cast<uint4 *>(sm + SM_BF);
+    c.fq = reinterpret_cast<uint4 *>(sm + SM_FQ);
+    c.fqr = reinterpret_cast<uint4 *>(sm + SM_FQR);
     c.tid = threadIdx.x;
     c.warp = c.tid >> 5;
     c.lane = c.tid & 31;
     c.g = c.lane >> 2;
     c.c = c.lane & 3;
     c.G = a.n_head / a.n_head_kv;
+    {
+        const uint32_t b = c.g & 3;
+        c.sel = b | (b << 4) | ((b + 4) << 8) | ((b + 4) << 12);
+    }
     const int split = blockIdx.x, kv = blockIdx.y, tok = blockIdx.z;
     const int64_t row_bytes = (int64_t)a.n_head_kv * 512;
-
-    // ---- the query rows of this KV head, original and rotated
-    for (int i = c.tid; i < c.G * 256; i += NT) {
-        const int g = i >> 8, d = i & 255;
-        const float x = a.q[((int64_t)tok * a.n_head + kv * c.G + g) * 256 + d];
-        c.q[i] = x;
-        c.qr[i] = x;
-    }
-    if (c.tid < GMAX) {
-        c.red[16 + c.tid] = -FLT_MAX;
-        c.red[24 + c.tid] = 0.0f;
-    }
-    __syncthreads();
-    wht256_smem(c.qr, c.G, c.tid);
 
     const int pos = a.positions[tok];
     const int limit = pos < a.origin ? 0 : min(a.active, pos - a.origin + 1);
@@ -457,7 +504,6 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     const int live = a.active ? (a.active - 1) / GROUP : 0;
     const bool live_partial = (a.active % GROUP) != 0;
     const int og = a.origin / GROUP;
-    float acc_r[4][2] = {}, acc_t[4][2] = {};
 
     // a group is read from its records when it has rows in [r0, r1) below the
     // tail and is neither the global sink group nor the incomplete live group
@@ -469,10 +515,39 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     int next = g0;
     while (next < g1 && !record_group(next))
         ++next;
-    int buf = 0;
     if (next < g1)
         prefetch_group(a, sm + SM_REC, next, kv, c.tid);
     cp_async_commit();
+
+    // ---- query head g = warp: q and WHT(q) as F16-tile fragments, WHT(q) rows
+    {
+        const int g = c.warp;
+        float v[8];
+        if (g < c.G) {
+            const float *src = a.q + ((int64_t)tok * a.n_head + kv * c.G + g) * 256 + 8 * c.lane;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                v[i] = src[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                v[i] = 0.0f;
+        }
+        q_frags(v, c.fq, g, c.lane);
+        wht_regs(v, c.lane);
+        float4 *qd = reinterpret_cast<float4 *>(c.qr + g * QLD + 8 * c.lane);
+        qd[0] = make_float4(v[0], v[1], v[2], v[3]);
+        qd[1] = make_float4(v[4], v[5], v[6], v[7]);
+        q_frags(v, c.fqr, g, c.lane);
+        if (c.tid < GMAX) {
+            c.st[c.tid] = -FLT_MAX;
+            c.st[8 + c.tid] = 0.0f;
+        }
+    }
+    __syncthreads();
+
+    float acc_r[2][4] = {}, acc_t[2][4] = {};
+    int buf = 0;
     for (int grp = g0; grp < g1; ++grp) {
         const int lo = max(r0, grp * GROUP), hi = min(r1, (grp + 1) * GROUP);
         const int body_hi = min(hi, tail_begin);
@@ -485,14 +560,14 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
                 f16_tile<false>(c, a.k + a.stage_off + first, a.v + a.stage_off + first,
                                 row_bytes, body_hi - lo, a.scale, acc_r, acc_t);
             } else {
+                cp_async_wait<0>();
+                __syncthreads(); // records landed; every thread is past the previous tile
                 int nxt = grp + 1;
                 while (nxt < g1 && !record_group(nxt))
                     ++nxt;
                 if (nxt < g1)
                     prefetch_group(a, sm + SM_REC + (buf ^ 1) * SET, nxt, kv, c.tid);
                 cp_async_commit();
-                cp_async_wait<1>();
-                __syncthreads();
                 record_tile(c, sm + SM_REC + buf * SET, lo - grp * GROUP, body_hi - lo, a.scale,
                             acc_r, acc_t);
                 buf ^= 1;
@@ -506,30 +581,45 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
         }
     }
     cp_async_wait<0>();
+    __syncthreads();
 
     // ---- numerator = WHT(rotated part) + tail part; partial record
-    float *x = c.qr;  // the rotated query is no longer needed
-    float *xt = c.qs; // tail part (the group factors are no longer needed)
-    __syncthreads();
-    if (c.g < c.G)
+    float *x = reinterpret_cast<float *>(sm + SM_REC), *xt = x + GMAX * QLD;
+    {
+        const int q0 = 2 * c.c;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int d = 32 * c.warp + 8 * i + 2 * c.c + e;
-                x[c.g * 256 + d] = acc_r[i][e];
-                xt[c.g * 256 + d] = acc_t[i][e];
-            }
+        for (int mt = 0; mt < 2; ++mt) {
+            const int d = 32 * c.warp + 16 * mt + 2 * c.g;
+            *reinterpret_cast<float2 *>(x + q0 * QLD + d) = make_float2(acc_r[mt][0], acc_r[mt][2]);
+            *reinterpret_cast<float2 *>(x + (q0 + 1) * QLD + d) =
+                make_float2(acc_r[mt][1], acc_r[mt][3]);
+            *reinterpret_cast<float2 *>(xt + q0 * QLD + d) = make_float2(acc_t[mt][0], acc_t[mt][2]);
+            *reinterpret_cast<float2 *>(xt + (q0 + 1) * QLD + d) =
+                make_float2(acc_t[mt][1], acc_t[mt][3]);
+        }
+    }
     __syncthreads();
-    wht256_smem(x, c.G, c.tid);
-    const int64_t n_rows = (int64_t)a.n_tokens * a.n_head;
-    for (int g = 0; g < c.G; ++g) {
+    if (c.warp < c.G) {
+        const int g = c.warp;
+        float v[8], t[8];
+        const float4 *xs = reinterpret_cast<const float4 *>(x + g * QLD + 8 * c.lane);
+        const float4 *ts = reinterpret_cast<const float4 *>(xt + g * QLD + 8 * c.lane);
+        const float4 v0 = xs[0], v1 = xs[1], t0 = ts[0], t1 = ts[1];
+        v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w;
+        v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
+        t[0] = t0.x, t[1] = t0.y, t[2] = t0.z, t[3] = t0.w;
+        t[4] = t1.x, t[5] = t1.y, t[6] = t1.z, t[7] = t1.w;
+        wht_regs(v, c.lane);
+        const int64_t n_rows = (int64_t)a.n_tokens * a.n_head;
         const int64_t row = (int64_t)tok * a.n_head + kv * c.G + g;
         float *rec = a.partials + ((int64_t)split * n_rows + row) * 258;
-        rec[c.tid] = x[g * 256 + c.tid] + xt[g * 256 + c.tid];
-        if (c.tid == 0) {
-            rec[256] = c.red[16 + g];
-            rec[257] = c.red[24 + g];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<float2 *>(rec + 8 * c.lane + 2 * i) =
+                make_float2(v[2 * i] + t[2 * i], v[2 * i + 1] + t[2 * i + 1]);
+        if (c.lane == 0) {
+            rec[256] = c.st[g];
+            rec[257] = c.st[8 + g];
         }
     }
 }
