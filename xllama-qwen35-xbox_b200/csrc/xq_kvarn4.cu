@@ -11,9 +11,11 @@
 // One CTA = (split, KV head, query token), the G = n_head / n_head_kv <= 8
 // query heads of that KV head, 256 threads, two CTAs per SM.  Splits cover
 // whole 128-row record groups.  A record group's four records (K and V, two
-// 128-dim slices each) are double-buffered into shared memory with cp.async,
-// the 64-byte nibble rows with their four 16-byte chunks XOR-swizzled by
-// (row / 2) % 4 so that the fragment loads below are free of bank conflicts.
+// 128-dim slices each) are double-buffered into shared memory by one thread:
+// each record's 128 nibble rows of 64 bytes as one TMA box with the 64-byte
+// swizzle (16-byte chunk c of row r lands at chunk c ^ ((r / 2) % 4), which
+// makes the fragment loads below free of bank conflicts) and its 768 bytes of
+// F16 axes as one bulk copy, all completing on the buffer's mbarrier.
 //
 // Every product is a tensor-core mma.sync m16n8k16 whose A operand is the KV
 // side (16 tokens for scores, 16 dims for the value numerator) and whose B
@@ -28,12 +30,15 @@
 // relative).  Stage and tail rows are read straight from global memory into
 // the same products: F16 K rows are already A fragments; F16 V pairs are
 // byte-permuted into them.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <float.h>
 #include <math.h>
 
 #include "xq_common.cuh"
 #include "xq_internal.h"
+#include "xq_tc.cuh"
 
 namespace xq {
 
@@ -41,8 +46,14 @@ namespace k4 {
 constexpr int NT = 256;
 constexpr int GMAX = 8;      // query heads per KV head
 constexpr int REC = 8960;    // bytes per record
+constexpr int NIB = 8192;    // its 128 x 128 nibbles (128 rows of 64 bytes)
+constexpr int AXB = 768;     // then 128 F16 scales, zeros, factors
 constexpr int GROUP = 128;   // rows per record group
-constexpr int SET = 4 * REC; // K slice 0, K slice 1, V slice 0, V slice 1
+// a record group in shared memory: the nibbles of K slice 0, K slice 1, V
+// slice 0, V slice 1 (512-byte aligned: the swizzle's period), then their axes
+constexpr int SET = 4 * REC;
+__host__ __device__ constexpr int nib_off(int which) { return which * NIB; }
+__host__ __device__ constexpr int ax_off(int which) { return 4 * NIB + which * AXB; }
 constexpr int QLD = 264;     // padded row stride (floats) of [8][256] query / numerator rows
 constexpr int SLD = 136;     // padded row stride of the [8][128] scores
 // shared memory
@@ -56,7 +67,8 @@ constexpr int SM_MX = SM_S + GMAX * SLD * 4;   // per-warp tile max [8 warps][8]
 constexpr int SM_ZP = SM_MX + 8 * 8 * 4;       // zero-point partials [2 slices][8][4]
 constexpr int SM_DP = SM_ZP + 2 * 8 * 4 * 4;   // denominator partials [8][8]
 constexpr int SM_ST = SM_DP + 8 * 8 * 4;       // m, den, alpha, m_new [4][8]
-constexpr int SM_BYTES = SM_ST + 4 * 8 * 4;
+constexpr int SM_BAR = SM_ST + 4 * 8 * 4;      // two mbarriers (one per record buffer), a zero word
+constexpr int SM_BYTES = SM_BAR + 32 + 512;    // + alignment slack
 } // namespace k4
 
 struct Kvarn4Args {
@@ -325,7 +337,7 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
     {
         // B fragments qs[d][g] = WHT(q)_g[d] * scale_k[d] of MMA steps qt, qt + 4
         // of slice fsl, and the partial sums of WHT(q) . zero_k
-        const uint8_t *kr = rk + fsl * REC;
+        const uint8_t *kax = rk + ax_off(fsl);
         float z = 0.0f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -333,8 +345,8 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
             const float *qrow = c.qr + c.g * QLD + fsl * 128 + dl;
             const float2 q01 = *reinterpret_cast<const float2 *>(qrow);
             const float2 q89 = *reinterpret_cast<const float2 *>(qrow + 8);
-            const float2 s01 = h2x2(kr + 8192 + 2 * dl), s89 = h2x2(kr + 8192 + 2 * dl + 16);
-            const float2 z01 = h2x2(kr + 8448 + 2 * dl), z89 = h2x2(kr + 8448 + 2 * dl + 16);
+            const float2 s01 = h2x2(kax + 2 * dl), s89 = h2x2(kax + 2 * dl + 16);
+            const float2 z01 = h2x2(kax + 256 + 2 * dl), z89 = h2x2(kax + 256 + 2 * dl + 16);
             c.bf[(fsl * 8 + kk) * 32 + c.lane] =
                 split4(q01.x * s01.x, q01.y * s01.y, q89.x * s89.x, q89.y * s89.y);
             z += (q01.x * z01.x + q01.y * z01.y) + (q89.x * z89.x + q89.y * z89.y);
@@ -353,7 +365,7 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
         float d[2][4] = {};
 #pragma unroll
         for (int sl = 0; sl < 2; ++sl) {
-            const uint8_t *base = rk + sl * REC + lane_off;
+            const uint8_t *base = rk + nib_off(sl) + lane_off;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 const uint8_t *p = base + kk * 1024;
@@ -366,7 +378,8 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
             }
         }
         const int row = 16 * w + 2 * c.g, q0 = 2 * c.c;
-        const float2 o0 = h2x2(rk + 8704 + 2 * row), o1 = h2x2(rk + REC + 8704 + 2 * row);
+        const float2 o0 = h2x2(rk + ax_off(0) + 512 + 2 * row);
+        const float2 o1 = h2x2(rk + ax_off(1) + 512 + 2 * row);
         const float z00 = sum4(c.zp + q0 * 4), z01 = sum4(c.zp + q0 * 4 + 4);
         const float z10 = sum4(c.zp + 32 + q0 * 4), z11 = sum4(c.zp + 32 + q0 * 4 + 4);
         const bool va = row >= t0 && row < t0 + n, vb = row + 1 >= t0 && row + 1 < t0 + n;
@@ -382,7 +395,7 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
         // B fragments ws[t][g] = w_g[t] * scale_v[t] of MMA steps qt, qt + 4 of
         // slice fsl, and the partial sums of w . zero_v and of w
         publish_alpha(c);
-        const uint8_t *vr = rk + (2 + fsl) * REC;
+        const uint8_t *vax = rk + ax_off(2 + fsl);
         float z = 0.0f, dsum = 0.0f;
         const bool on = c.g < c.G;
         const float m = on ? tile_max(c, c.g) : 0.0f;
@@ -396,8 +409,8 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
                 const float2 s89 = *reinterpret_cast<const float2 *>(sr + 8);
                 const float w0 = __expf(s01.x - m), w1 = __expf(s01.y - m);
                 const float w8 = __expf(s89.x - m), w9 = __expf(s89.y - m);
-                const float2 c01 = h2x2(vr + 8192 + 2 * t), c89 = h2x2(vr + 8192 + 2 * t + 16);
-                const float2 z01 = h2x2(vr + 8448 + 2 * t), z89 = h2x2(vr + 8448 + 2 * t + 16);
+                const float2 c01 = h2x2(vax + 2 * t), c89 = h2x2(vax + 2 * t + 16);
+                const float2 z01 = h2x2(vax + 256 + 2 * t), z89 = h2x2(vax + 256 + 2 * t + 16);
                 f = split4(w0 * c01.x, w1 * c01.y, w8 * c89.x, w9 * c89.y);
                 z += (w0 * z01.x + w1 * z01.y) + (w8 * z89.x + w9 * z89.y);
                 dsum += (w0 + w1) + (w8 + w9);
@@ -419,8 +432,7 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
         // 2 (w % 4) + mt of slice w / 4, all 128 tokens; the V nibble rows are
         // tokens, the lane's word holds dims 16 unit + 8 (g / 4) ..
         const int w = c.warp, sl = w >> 2;
-        const uint8_t *vbase =
-            rk + (2 + sl) * REC + 128 * c.c + 16 * ((w & 3) ^ c.c) + 4 * (c.g >> 2);
+        const uint8_t *vbase = rk + nib_off(2 + sl) + 128 * c.c + 16 * ((w & 3) ^ c.c) + 4 * (c.g >> 2);
         float dv[2][4] = {};
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -440,7 +452,7 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
         const float wz0 = sum4(c.zp + (sl * 8 + q0) * 4), wz1 = sum4(c.zp + (sl * 8 + q0) * 4 + 4);
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt) {
-            const float2 o = h2x2(rk + (2 + sl) * REC + 8704 + 2 * (32 * (w & 3) + 16 * mt + 2 * c.g));
+            const float2 o = h2x2(rk + ax_off(2 + sl) + 512 + 2 * (32 * (w & 3) + 16 * mt + 2 * c.g));
             acc_r[mt][0] = acc_r[mt][0] * al0 + o.x * (dv[mt][0] + wz0);
             acc_r[mt][1] = acc_r[mt][1] * al1 + o.x * (dv[mt][1] + wz1);
             acc_r[mt][2] = acc_r[mt][2] * al0 + o.y * (dv[mt][2] + wz0);
@@ -454,24 +466,32 @@ __device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int 
     }
 }
 
-// cp.async of group grp's four records of KV head kv into dst, nibble rows
-// swizzled: 16-byte chunk ch of row r lands at chunk ch ^ ((r >> 1) & 3)
-__device__ __forceinline__ void prefetch_group(const Kvarn4Args &a, uint8_t *dst, int grp,
-                                               int kv, int tid) {
-    const int phys = 2 * a.n_head_kv;
-    for (int i = tid; i < SET / 16; i += NT) {
-        const int which = i / (REC / 16), u = i % (REC / 16);
-        const uint8_t *plane = which < 2 ? a.k : a.v;
-        const int du = u < 512 ? (u & ~3) | ((u ^ (u >> 3)) & 3) : u;
-        cp_async<16>(smem_u32(dst + which * REC + du * 16),
-                     plane + ((int64_t)grp * phys + 2 * kv + (which & 1)) * REC + u * 16);
+// One thread: group grp's four records of KV head kv into the buffer at dst,
+// completing on bar.  The tensor maps view each plane's records as rows of 64
+// bytes (a record = 140 rows, its nibbles the first 128).
+__device__ __forceinline__ void issue_group(const CUtensorMap *kmap, const CUtensorMap *vmap,
+                                            const Kvarn4Args &a, uint8_t *dst, uint32_t bar,
+                                            int grp, int kv) {
+    tc::mbar_expect_tx(bar, SET);
+    const int64_t r0 = (int64_t)grp * 2 * a.n_head_kv + 2 * kv;
+#pragma unroll
+    for (int which = 0; which < 4; ++which) {
+        const int64_t r = r0 + (which & 1);
+        tc::tma_load_2d(smem_u32(dst + nib_off(which)), which < 2 ? kmap : vmap, 0,
+                        (int)(r * (REC / 64)), bar);
+        tc::bulk_load(smem_u32(dst + ax_off(which)), (which < 2 ? a.k : a.v) + r * REC + NIB, AXB,
+                      bar);
     }
 }
 } // namespace k4
 
-__global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4Args a) {
+__global__ void __launch_bounds__(k4::NT, 2)
+    kvarn4_partials_kernel(const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap, const Kvarn4Args a) {
     using namespace k4;
-    extern __shared__ __align__(16) uint8_t sm[];
+    extern __shared__ __align__(1024) uint8_t sm_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 511) &
+                                              ~uintptr_t(511));
     Cta c;
     c.sm = sm;
     c.qr = reinterpret_cast<float *>(sm + SM_QR);
@@ -512,12 +532,21 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
         const int lo = max(r0, grp * GROUP), hi = min(min(r1, (grp + 1) * GROUP), tail_begin);
         return lo < hi && og + grp != 0 && !(grp == live && live_partial);
     };
-    int next = g0;
-    while (next < g1 && !record_group(next))
-        ++next;
-    if (next < g1)
-        prefetch_group(a, sm + SM_REC, next, kv, c.tid);
-    cp_async_commit();
+    const uint32_t bar0 = smem_u32(sm + SM_BAR);
+    volatile int *zero = reinterpret_cast<volatile int *>(sm + SM_BAR + 16);
+    if (c.tid == 0) {
+        tc::mbar_init(bar0, 1);
+        tc::mbar_init(bar0 + 8, 1);
+        *zero = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        tc::prefetch_map(&kmap);
+        tc::prefetch_map(&vmap);
+        int next = g0;
+        while (next < g1 && !record_group(next))
+            ++next;
+        if (next < g1)
+            issue_group(&kmap, &vmap, a, sm + SM_REC, bar0, next, kv);
+    }
 
     // ---- query head g = warp: q and WHT(q) as F16-tile fragments, WHT(q) rows
     {
@@ -548,6 +577,8 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
 
     float acc_r[2][4] = {}, acc_t[2][4] = {};
     int buf = 0;
+    uint32_t phase = 0;   // bit b: parity of buffer b's next completion
+    bool failed = false;  // a record wait ran out (CTA-uniform)
     for (int grp = g0; grp < g1; ++grp) {
         const int lo = max(r0, grp * GROUP), hi = min(r1, (grp + 1) * GROUP);
         const int body_hi = min(hi, tail_begin);
@@ -560,14 +591,21 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
                 f16_tile<false>(c, a.k + a.stage_off + first, a.v + a.stage_off + first,
                                 row_bytes, body_hi - lo, a.scale, acc_r, acc_t);
             } else {
-                cp_async_wait<0>();
-                __syncthreads(); // records landed; every thread is past the previous tile
-                int nxt = grp + 1;
-                while (nxt < g1 && !record_group(nxt))
-                    ++nxt;
-                if (nxt < g1)
-                    prefetch_group(a, sm + SM_REC + (buf ^ 1) * SET, nxt, kv, c.tid);
-                cp_async_commit();
+                const bool ok = tc::mbar_wait(bar0 + 8 * buf, (phase >> buf) & 1, zero);
+                // records landed; every thread is past the previous tile
+                if (__syncthreads_or(!ok)) {
+                    failed = true;
+                    break;
+                }
+                phase ^= 1u << buf;
+                if (c.tid == 0) {
+                    int nxt = grp + 1;
+                    while (nxt < g1 && !record_group(nxt))
+                        ++nxt;
+                    if (nxt < g1)
+                        issue_group(&kmap, &vmap, a, sm + SM_REC + (buf ^ 1) * SET,
+                                    bar0 + 8 * (buf ^ 1), nxt, kv);
+                }
                 record_tile(c, sm + SM_REC + buf * SET, lo - grp * GROUP, body_hi - lo, a.scale,
                             acc_r, acc_t);
                 buf ^= 1;
@@ -580,7 +618,8 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
                            hi - tail_lo, a.scale, acc_r, acc_t);
         }
     }
-    cp_async_wait<0>();
+    if (failed && c.tid == 0) // give the copies still in flight a bounded time to land
+        tc::mbar_wait(bar0 + 8 * buf, (phase >> buf) & 1, zero, 100000000ull);
     __syncthreads();
 
     // ---- numerator = WHT(rotated part) + tail part; partial record
@@ -619,7 +658,7 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
                 make_float2(v[2 * i] + t[2 * i], v[2 * i + 1] + t[2 * i + 1]);
         if (c.lane == 0) {
             rec[256] = c.st[g];
-            rec[257] = c.st[8 + g];
+            rec[257] = failed ? __int_as_float(0x7fc00000) : c.st[8 + g]; // NaN poisons the row
         }
     }
 }
@@ -642,12 +681,29 @@ cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st) {
     a.n_tokens = l.n_tokens;
     a.rows_per_split = l.rows_per_split;
     a.scale = l.scale;
+    // each plane's records as a 2D byte tensor of 64-byte rows; box = one
+    // record's 128 nibble rows, 64-byte swizzle
+    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
+    if (!enc)
+        return cudaErrorNotSupported;
+    CUtensorMap maps[2];
+    for (int i = 0; i < 2; ++i) {
+        cuuint64_t dims[2] = {64, (cuuint64_t)(l.records_bytes / 64)};
+        cuuint64_t strides[1] = {64};
+        cuuint32_t box[2] = {64, 128};
+        cuuint32_t es[2] = {1, 1};
+        if (enc(&maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(i ? l.v : l.k),
+                dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
     static std::atomic<unsigned long long> attr{0};
     cudaError_t e = set_smem_limit((const void *)kvarn4_partials_kernel, k4::SM_BYTES, attr);
     if (e != cudaSuccess)
         return e;
     dim3 grid((unsigned)l.n_splits, (unsigned)l.n_head_kv, (unsigned)l.n_tokens);
-    kvarn4_partials_kernel<<<grid, k4::NT, k4::SM_BYTES, st>>>(a);
+    kvarn4_partials_kernel<<<grid, k4::NT, k4::SM_BYTES, st>>>(maps[0], maps[1], a);
     return cudaGetLastError();
 }
 
