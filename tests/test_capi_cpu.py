@@ -103,3 +103,39 @@ def test_gdn_chunked_workspace_sizes():
     assert ws(300, 32, 1, 5) == 4 * 32 * unit + 256 + 32 * 65536  # 44 tokens per token
     assert ws(64, 32, 1, 1) == 0 and ws(100, 32, 1, 64) == 0
     assert ws(4096, 32, 1, 0) == 0  # slots outside [1, 64]
+
+
+def test_kvarn4_workspace_and_contract():
+    """KVarN4 split plan (no GPU: 148 SMs assumed): body splits of whole
+    128-row groups over rows [0, active - tail), about two CTAs per SM counting
+    one tail split; argument contracts fail before any launch."""
+    import xq._lib as XL
+    L = _lib()
+
+    def ws(origin, cap, tail, n_kv, n_head, active, n_tok=1):
+        d = XL.Kvarn4Desc(origin, cap, tail, n_kv)
+        return L.xq_attend_range_kvarn4_workspace(C.byref(d), n_head, active, n_tok)
+
+    rec = 24 * 258 * 4
+    # 255 body groups: 73 splits wanted -> 4 groups each -> 64 body splits + tail
+    assert ws(102400, 32768, 128, 4, 24, 32768) == 65 * rec
+    assert ws(102400, 32768, 0, 4, 24, 32768) == 64 * rec      # no tail split
+    assert ws(0, 640, 128, 4, 24, 100) == 1 * rec              # everything in the tail
+    assert ws(0, 640, 128, 4, 24, 0) == 1 * rec                # empty: one split
+    assert ws(0, 640, 0, 4, 24, 520, n_tok=3) == 5 * 3 * rec   # one group per split
+    assert ws(0, 640, -1, 4, 24, 520) == 0
+
+    d = XL.Kvarn4Desc(0, 1024, 128, 4)
+    fake = C.c_void_p(4096)
+
+    def call(desc, n_head=24, active=1000, kp=fake, ws_bytes=1 << 30):
+        return L.xq_attend_range_kvarn4(C.byref(desc), kp, fake, n_head, active, 1, fake, fake,
+                                        0.0625, fake, fake, fake, ws_bytes, None)
+
+    assert call(XL.Kvarn4Desc(64, 1024, 128, 4)) == XL.XQ_ERR_INVALID   # origin % 128
+    assert call(XL.Kvarn4Desc(0, 1024, 64, 4)) == XL.XQ_ERR_INVALID     # tail not 0 / 128
+    assert call(d, n_head=40) == XL.XQ_ERR_INVALID                      # 10 q heads per kv head
+    assert call(d, active=2000) == XL.XQ_ERR_INVALID                    # active > capacity
+    assert call(d, kp=C.c_void_p(4100)) == XL.XQ_ERR_INVALID            # plane not 16-byte aligned
+    assert call(d, ws_bytes=100) == XL.XQ_ERR_WORKSPACE
+    assert b"workspace" in L.xq_last_error()

@@ -537,23 +537,37 @@ int xq_attend_range(int32_t storage, const void *k, const void *v, uint32_t n_he
 // ---------------------------------------------------------------------------
 // Native KVarN4 range attention.
 
-// Splits of whole 128-row record groups: about two CTAs per SM, at most one
-// split per group.
-static int64_t kvarn4_rows_per_split(uint32_t active, uint32_t n_head_kv, uint32_t n_tokens) {
-    const int64_t groups = active ? (active + 127) / 128 : 1;
-    int64_t s = (2 * (int64_t)sm_count() + (int64_t)n_head_kv * n_tokens - 1) /
-                ((int64_t)n_head_kv * n_tokens);
+// Split plan: body splits of whole 128-row groups over rows [0, active - tail)
+// (about two CTAs per SM in all, at most one split per group) and one split
+// for the precision tail rows.
+struct Kvarn4Plan {
+    int64_t rows; // rows per body split
+    int n_body, n_splits;
+};
+static Kvarn4Plan kvarn4_plan(uint32_t active, uint32_t tail, uint32_t n_head_kv,
+                              uint32_t n_tokens) {
+    const int64_t tail_rows = active < tail ? active : tail;
+    const int64_t body = (int64_t)active - tail_rows;
+    const int64_t groups = (body + 127) / 128;
+    const int64_t per = (int64_t)n_head_kv * n_tokens;
+    int64_t s = (2 * (int64_t)sm_count() + per - 1) / per - (tail_rows ? 1 : 0);
     s = s < 1 ? 1 : s > groups ? groups : s;
-    return 128 * ((groups + s - 1) / s);
+    Kvarn4Plan pl;
+    pl.rows = groups ? 128 * ((groups + s - 1) / s) : 128;
+    pl.n_body = groups ? (int)((body + pl.rows - 1) / pl.rows) : 0;
+    pl.n_splits = pl.n_body + (tail_rows ? 1 : 0);
+    if (pl.n_splits == 0)
+        pl.n_splits = 1; // nothing active: one empty split (O = 0, LSE = -inf)
+    return pl;
 }
 
 size_t xq_attend_range_kvarn4_workspace(const xq_kvarn4_desc *d, uint32_t n_head,
                                         uint32_t active, uint32_t n_tokens) {
-    if (!d || d->n_head_kv <= 0 || !n_tokens)
+    if (!d || d->n_head_kv <= 0 || !n_tokens || d->precision_tail < 0)
         return 0;
-    const int64_t rows = kvarn4_rows_per_split(active, (uint32_t)d->n_head_kv, n_tokens);
-    const int64_t s = active ? (active + rows - 1) / rows : 1;
-    return (size_t)s * n_tokens * n_head * 258 * sizeof(float);
+    const Kvarn4Plan pl =
+        kvarn4_plan(active, (uint32_t)d->precision_tail, (uint32_t)d->n_head_kv, n_tokens);
+    return (size_t)pl.n_splits * n_tokens * n_head * 258 * sizeof(float);
 }
 
 int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const void *v_plane,
@@ -573,8 +587,9 @@ int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const v
                     "attend_range_kvarn4: shape (active <= capacity, 1..8 q heads per kv head)");
     if (((reinterpret_cast<uintptr_t>(k_plane) | reinterpret_cast<uintptr_t>(v_plane)) & 15) != 0)
         return fail(XQ_ERR_INVALID, "attend_range_kvarn4: planes must be 16-byte aligned");
-    const int64_t rows = kvarn4_rows_per_split(active, (uint32_t)d->n_head_kv, n_tokens);
-    const int64_t s = active ? (active + rows - 1) / rows : 1;
+    const Kvarn4Plan pl =
+        kvarn4_plan(active, (uint32_t)d->precision_tail, (uint32_t)d->n_head_kv, n_tokens);
+    const int64_t s = pl.n_splits;
     const size_t need = (size_t)s * n_tokens * n_head * 258 * sizeof(float);
     if (!ws || ws_bytes < need)
         return fail(XQ_ERR_WORKSPACE, "attend_range_kvarn4: workspace %zu < %zu bytes", ws_bytes,
@@ -592,8 +607,9 @@ int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const v
     l.n_head = (int)n_head;
     l.n_head_kv = d->n_head_kv;
     l.n_tokens = (int)n_tokens;
-    l.rows_per_split = (int)rows;
-    l.n_splits = (int)s;
+    l.rows_per_split = (int)pl.rows;
+    l.n_body = pl.n_body;
+    l.n_splits = pl.n_splits;
     l.scale = kq_scale;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     int rc = cuda_status(xq::launch_kvarn4(l, st), "attend_range_kvarn4 partials");

@@ -132,7 +132,10 @@ struct Kvarn4Launch {
     const int32_t *positions;
     float *partials;
     int64_t records_bytes;
-    int origin, active, tail, n_head, n_head_kv, n_tokens, rows_per_split, n_splits;
+    // splits [0, n_body) cover rows [0, active - tail) in rows_per_split
+    // chunks (rotated domain); split n_body, when n_splits > n_body, covers the
+    // precision tail (original domain)
+    int origin, active, tail, n_head, n_head_kv, n_tokens, rows_per_split, n_body, n_splits;
     float scale;
 };
 cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st);
