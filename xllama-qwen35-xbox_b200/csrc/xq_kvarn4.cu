@@ -1,46 +1,50 @@
 // Native KVarN4 range attention (RKVA descriptor v1 resident image, head_dim
-// 256): split partials over 4-bit Bee records, rotated F16 stage rows and the
-// original-domain F16 precision tail, in the (acc[256], max, denom) partial
-// layout the LSE merge reduces (xq_decode.cu).  Semantics as the reference's
-// shaders/rkva/rkva_range_attn_kvarn4.hlsl:64-150: rows >= active - tail come
-// from the tail and meet the original q; the other rows are in the rotated
-// domain (WHT256 = Sylvester H256 / 16) and meet WHT(q); their value numerator
-// is rotated back with WHT and added to the tail's.  Here the tail rows form a
-// split of their own (original domain, no rotation) and every body split
-// rotates its numerator back before it writes its partial, so the merge adds
-// original-domain partials only.
+// 256) on the tcgen05 tensor cores: split partials over 4-bit Bee records,
+// rotated F16 stage rows and the original-domain F16 precision tail, in the
+// (acc[256], max, denom) partial layout the LSE merge reduces (xq_decode.cu).
+// Semantics as the reference's shaders/rkva/rkva_range_attn_kvarn4.hlsl:64-150:
+// rows >= active - tail come from the tail and meet the original q; the other
+// rows are in the rotated domain (WHT256 = Sylvester H256 / 16) and meet
+// WHT(q); their value numerator is rotated back with WHT and added to the
+// tail's.  Here the tail rows form a split of their own (original domain) and
+// every body split rotates its numerator back before it writes its partial,
+// so the merge adds original-domain partials only.
 //
 // One CTA = (split, KV head, query token), the G = n_head / n_head_kv <= 8
-// query heads of that KV head, 256 threads, two CTAs per SM.  Body splits
-// cover whole 128-row groups.  A record group's four records (K and V, two
-// 128-dim slices each) are double-buffered into shared memory by one thread:
-// each record's 128 nibble rows of 64 bytes as one TMA box with the 64-byte
-// swizzle (16-byte chunk c of row r lands at chunk c ^ ((r / 2) % 4), which
-// makes the fragment loads below free of bank conflicts) and its 768 bytes of
-// F16 axes as one bulk copy, all completing on the buffer's mbarrier.
+// query heads of that KV head, 256 threads, two CTAs per SM, 64 TMEM columns.
+// Per 128-row record group (four records: K and V, two 128-dim slices each):
 //
-// Warps w and w + 4 form pair p = w % 4 and own tokens 32p .. 32p + 31 of
-// every 128-row tile; warp w covers dims slice w / 4 (128 dims).  Each warp
-// computes its slice's partial scores of the pair's tokens, the pair adds them
-// through shared memory (a 64-thread barrier), and each warp then runs its own
-// online softmax over the pair's tokens and accumulates the value numerator of
-// its slice; pairs are combined at the end of the split.  Per record group the
-// CTA meets one CTA-wide barrier (records landed), one 128-thread barrier per
-// slice (query-side fragments) and one pair barrier.
+//   1. the K records' 4-bit values are widened to bytes in shared memory as
+//      the MN-major UMMA A operand (one 128-byte row per dim: the low nibbles
+//      of the row's 64 bytes, then the high nibbles, i.e. tokens 0, 2, .., 126,
+//      1, 3, .., 127; 128-byte swizzle); the query side q_d scale_d of each
+//      slice is written as the K-major B operand in three balanced int8 limbs
+//      (x = 2^-E (l0 + 2^8 l1 + 2^16 l2), one power-of-two exponent per query
+//      head and slice, |x 2^E| < 2^22);
+//   2. scores: eight tcgen05.mma kind::i8 (M = 128 tokens, N = 32 = 8 heads x 3
+//      limbs + 8 unused, K = 32) accumulate exact int32 sums in TMEM;
+//      s_t = scale * sum_slices other_t (2^-E (D0 + 2^8 D1 + 2^16 D2) +
+//      sum_d q_d zero_d);
+//   3. the V records are widened the same way (rows = tokens, bytes = dims);
+//   4. one warp per query head runs the online-softmax step over the 128
+//      tokens and writes w_t scale_v[t] as three int8 limbs (the V B operand),
+//      with sum_t w_t zero_v[t];
+//   5. values: eight more kind::i8 MMAs (M = 128 dims, N = 32, K = 32); each
+//      thread owns one dim of one slice for all eight heads:
+//      acc = acc * alpha + other_d (2^-E (D0 + 2^8 D1 + 2^16 D2) +
+//      sum_t w_t zero_v[t]).
 //
-// Every product is a tensor-core mma.sync m16n8k16: A = the G query heads'
-// fp32 operand split into an f16 high part (rows g) and remainder (rows g + 8),
-// B = the KV side expanded exactly to f16 in registers (4-bit values: one byte
-// permute, one mask and one f16 multiply-add give two n-tiles, the byte's low
-// and high nibble):
-//   scores  s_t = other_t * (sum_d (q_d scale_d) nib_dt + sum_d q_d zero_d)
-//   values  n_d = other_d * (sum_t (w_t scale_t) nib_td + sum_t w_t zero_t)
-// The n axis is permuted so that a lane's score columns are exactly the token
-// k-slots of its value-product A fragment (tokens 2c, 2c + 1, 2c + 8, 2c + 9 of
-// each 16), so the softmax weights never leave the lane.  Stage and tail rows
-// (F16) are read straight from global memory into the same products.
+// The int8 products are exact; the only rounding on the tensor-core side is
+// the 22-bit limb quantisation of the fp32 query / weight operands (relative
+// 2^-22 of each head's largest value) and fp32 when the limbs are combined.
+// F16 stage / tail rows run the same five steps with kind::f16 MMAs: F16 K rows
+// (K-major) and V rows (MN-major, even dims then odd dims so that a thread
+// owns the same dim in both kinds of tile) staged into shared memory, and the
+// query / weights as an f16 high part plus remainder (N = 16 = 8 heads x 2).
+// TMEM: scores of slice s at column 32 s, values at 64 + 32 s.
+// Every mbarrier wait is bounded; on timeout the CTA poisons its partial (NaN
+// denominator), waits a bounded time for its MMAs, frees TMEM and returns.
 #include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <float.h>
 #include <math.h>
@@ -53,27 +57,32 @@ namespace xq {
 
 namespace k4 {
 constexpr int NT = 256;
-constexpr int GMAX = 8;      // query heads per KV head
-constexpr int REC = 8960;    // bytes per record
-constexpr int NIB = 8192;    // its 128 x 128 nibbles (128 rows of 64 bytes)
-constexpr int AXB = 768;     // then 128 F16 scales, zeros, factors
-constexpr int GROUP = 128;   // rows per record group
-// a record group in shared memory: the nibbles of K slice 0, K slice 1, V
-// slice 0, V slice 1 (512-byte aligned: the swizzle's period), then their axes
-constexpr int SET = 4 * REC;
-__host__ __device__ constexpr int nib_off(int which) { return which * NIB; }
-__host__ __device__ constexpr int ax_off(int which) { return 4 * NIB + which * AXB; }
-constexpr int QLD = 264;     // padded row stride (floats) of [8][256] rows
-// shared memory
-constexpr int SM_REC = 0;                      // 2 x SET; x [4 pairs][8][QLD] after the loop
-constexpr int SM_QR = SM_REC + 2 * SET;        // WHT(q) [8][QLD] (body splits)
-constexpr int SM_KF = SM_QR + GMAX * QLD * 4;  // record-tile A fragments [2 slices][8][32] uint4
-constexpr int SM_FQ = SM_KF + 2 * 8 * 32 * 16; // F16-tile A fragments [2][8][32] uint4
-constexpr int SM_XS = SM_FQ + 2 * 8 * 32 * 16; // partial scores [2 parities][2][4 pairs][32][8]
-constexpr int SM_ZP = SM_XS + 2 * 2 * 4 * 32 * 8 * 4; // q . zero_k partials [2][8][4]
-constexpr int SM_MP = SM_ZP + 2 * 8 * 4 * 4;   // per-pair max and denominator [2][4][8]
-constexpr int SM_BAR = SM_MP + 2 * 4 * 8 * 4;  // two mbarriers (one per record buffer), a zero word
-constexpr int SM_BYTES = SM_BAR + 32 + 512;    // + alignment slack
+constexpr int GMAX = 8;    // query heads per KV head
+constexpr int REC = 8960;  // bytes per record: 8192 of nibbles (128 rows x 64 B), then
+constexpr int NIB = 8192;  // 128 F16 scales, 128 zeros (per row), 128 factors (per column)
+constexpr int GROUP = 128; // rows per record group
+constexpr int QLD = 264;   // padded fp32 row stride of [8][256] rows
+constexpr int PLD = 132;   // padded row stride of the partial scores [2][8][128]
+// shared memory (1024-byte aligned base; every operand tile 1024-aligned)
+constexpr int SM_A0 = 0;     // 32 KB: K operand (records: slice s at 16 KB s; F16: K or V slice 0)
+constexpr int SM_A1 = 32768; // 32 KB: V operand (records: slice s at 16 KB s; F16: K or V slice 1)
+constexpr int SM_BQ = 65536; // 8 KB: query operand (slice s at 4 KB s: int8 32 rows, f16 16 x 2)
+constexpr int SM_BW = 73728; // 8 KB: weight operand (same)
+constexpr int SM_QV = 81920; // q (tail split) or WHT(q) (body splits) [8][QLD] fp32
+constexpr int SM_PS = SM_QV + GMAX * QLD * 4;   // partial scores [2 slices][8][PLD]
+constexpr int SM_VEC = SM_PS + 2 * 8 * PLD * 4; // per-head vectors [16][8]
+constexpr int SM_BAR = SM_VEC + 16 * 8 * 4;     // bar_S, bar_V, TMEM slot, zero word
+constexpr int SM_BYTES = SM_BAR + 64 + 1024;    // + alignment slack
+// rows of the per-head vectors
+constexpr int V_M = 0, V_DEN = 1, V_ALPHA = 2, V_EQ = 3, V_QZ = 5, V_EW = 7, V_WZ = 9;
+constexpr uint32_t TMEM_COLS = 128; // scores slice 0 / 1 at 0 / 32, values at 64 / 96
+
+// tcgen05.mma kind::i8, A s8 MN-major (the 4-bit values 0..15), B s8 K-major,
+// s32 accumulator
+constexpr uint32_t ID_I8 = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (0u << 16) |
+                           ((32u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t ID_F16_S = tc::idesc(128, 16, 0, 0); // K rows K-major
+constexpr uint32_t ID_F16_V = tc::idesc(128, 16, 1, 0); // V rows MN-major
 } // namespace k4
 
 struct Kvarn4Args {
@@ -81,102 +90,463 @@ struct Kvarn4Args {
     const float *q;       // [n_tokens][n_head][256]
     const int32_t *positions;
     float *partials;      // [n_splits][n_tokens * n_head][258]
-    int64_t records_bytes, stage_off, tail_off;
+    int64_t stage_off, tail_off;
     int origin, active, tail, n_head, n_head_kv, n_tokens, rows_per_split, n_body;
     float scale;
 };
 
 namespace k4 {
-// Per-CTA shared-memory views and lane indices, passed by value to the
-// inlined phases (nothing of the kernel's state has its address taken).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+    asm volatile(
+        "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(ID_I8), "r"(acc));
+}
+__device__ __forceinline__ uint4 ldg128(const uint8_t *p) {
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+__device__ __forceinline__ float h2f(const uint8_t *p) {
+    return __half2float(*reinterpret_cast<const __half *>(p));
+}
+__device__ __forceinline__ void h8(const uint8_t *p, float (&x)[8]) { // 8 F16 at p (16 B)
+    const uint4 u = ldg128(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void h4(const uint8_t *p, float (&x)[4]) { // 4 F16 at p (8 B)
+    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
+}
+// Byte offset of 16-byte chunk c of row r in a tile of 128-byte rows with the
+// 128-byte swizzle
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
+    return r * 128u + ((c ^ (r & 7u)) << 4);
+}
+// Widen one 16-byte chunk (32 nibbles, low nibble first) of row r, chunk c4 of
+// the row's four: low nibbles to chunk c4, high nibbles to chunk 4 + c4.
+__device__ __forceinline__ void widen(uint8_t *tile, int r, int c4, uint4 w) {
+    const uint32_t m = 0x0f0f0f0fu;
+    *reinterpret_cast<uint4 *>(tile + swz(r, c4)) = make_uint4(w.x & m, w.y & m, w.z & m, w.w & m);
+    *reinterpret_cast<uint4 *>(tile + swz(r, 4 + c4)) =
+        make_uint4((w.x >> 4) & m, (w.y >> 4) & m, (w.z >> 4) & m, (w.w >> 4) & m);
+}
+// Position p of a widened row -> token / dim index (low nibbles are the even
+// ones)
+__device__ __forceinline__ int unperm(int p) { return p < 64 ? 2 * p : 2 * (p - 64) + 1; }
+// Three balanced int8 limbs of v = rint(x * 2^E), |v| < 2^22:
+// v = l0 + 2^8 l1 + 2^16 l2 with l0, l1 in [-128, 127], |l2| <= 64
+__device__ __forceinline__ void limbs(float x, float mul, int &l0, int &l1, int &l2) {
+    const int v = __float2int_rn(x * mul);
+    l0 = ((v + 128) & 255) - 128;
+    const int v1 = (v - l0) >> 8;
+    l1 = ((v1 + 128) & 255) - 128;
+    l2 = (v1 - l1) >> 8;
+}
+// 2^E with E = 21 - ilogb(mx): the largest |x| maps below 2^22; 1 when mx = 0
+__device__ __forceinline__ float limb_scale(float mx) {
+    return mx > 0.0f ? ldexpf(1.0f, 21 - ilogbf(mx)) : 1.0f;
+}
+// D0 + 2^8 D1 + 2^16 D2 of the int32 sums held as float bit patterns
+__device__ __forceinline__ float combine(float d0, float d1, float d2) {
+    return fmaf((float)__float_as_int(d2), 65536.0f,
+                fmaf((float)__float_as_int(d1), 256.0f, (float)__float_as_int(d0)));
+}
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) |
+           ((uint32_t)(d & 255) << 24);
+}
+__device__ __forceinline__ uint32_t f16x2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// f32 x -> f16 high part, remainder
+__device__ __forceinline__ void hilo(float x, float &hi, float &lo) {
+    hi = __half2float(__float2half_rn(x));
+    lo = x - hi;
+}
+
 struct Cta {
-    float *qr, *xs, *zp;
-    uint4 *kf, *fq;
-    int tid, warp, lane, g, c, s, p, G; // g = lane / 4, c = lane % 4; s = slice, p = pair
-    uint32_t sel; // byte permute: byte g / 2 of two words -> bytes 0 and 2
-};
-// Online-softmax state of one lane (query head g; replicated over c) and the
-// value numerator of its slice: acc[u][i] = dim 16u + {2c, 2c+1, 2c+8, 2c+9}[i].
-struct Run {
-    float m, den;
-    float acc[8][4];
+    uint8_t *sm;
+    float *qv, *ps, *vec;
+    uint32_t tmem, bar_s, bar_v;
+    volatile int *zero;
+    int tid, warp, lane, G;
 };
 
-// D += A B, m16n8k16, f16 inputs, f32 accumulate
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint4 &a, uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-        "{%8, %9}, {%0, %1, %2, %3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
-}
-// f32 pair -> f16x2 high part and f16x2 remainder: x = hi + lo to about 2^-22
-// relative, so the two A rows g (hi) and g + 8 (lo) carry an fp32 operand
-__device__ __forceinline__ void split2(float x, float y, uint32_t &hi, uint32_t &lo) {
-    const __half2 h = __floats2half2_rn(x, y);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
-    hi = *reinterpret_cast<const uint32_t *>(&h);
-    lo = *reinterpret_cast<const uint32_t *>(&l);
-}
-// A fragment of k-slots (2c, 2c+1) = (x0, x1) and (2c+8, 2c+9) = (x8, x9)
-__device__ __forceinline__ uint4 afrag(float x0, float x1, float x8, float x9) {
-    uint4 f;
-    split2(x0, x1, f.x, f.y);
-    split2(x8, x9, f.z, f.w);
-    return f;
-}
-// Byte g / 2 of words x (k-slot 2c) and y (k-slot 2c + 1): the low nibbles as
-// the B register of n-tile parity 0, the high nibbles of parity 1.  0x6400 | n
-// is the f16 1024 + n and 0x6400 | 16 n is 1024 + 16 n; both map back to n
-// exactly.
-__device__ __forceinline__ void nib_frag(uint32_t x, uint32_t y, uint32_t sel, uint32_t &lo,
-                                         uint32_t &hi) {
-    const uint32_t t = __byte_perm(x, y, sel);
-    const uint32_t a = (t & 0x000f000fu) | 0x64006400u, b = (t & 0x00f000f0u) | 0x64006400u;
-    const uint32_t k1024 = 0x64006400u, k16th = 0x2c002c00u, km64 = 0xd400d400u;
-    const __half2 ha = __hsub2(*reinterpret_cast<const __half2 *>(&a),
-                               *reinterpret_cast<const __half2 *>(&k1024));
-    const __half2 hb = __hfma2(*reinterpret_cast<const __half2 *>(&b),
-                               *reinterpret_cast<const __half2 *>(&k16th),
-                               *reinterpret_cast<const __half2 *>(&km64));
-    lo = *reinterpret_cast<const uint32_t *>(&ha);
-    hi = *reinterpret_cast<const uint32_t *>(&hb);
-}
-__device__ __forceinline__ uint32_t lds32(const uint8_t *p) {
-    return *reinterpret_cast<const uint32_t *>(p);
-}
-__device__ __forceinline__ uint32_t ldg32(const uint8_t *p) {
-    return __ldg(reinterpret_cast<const uint32_t *>(p));
-}
-// two F16 values at p (4-byte aligned) as floats
-__device__ __forceinline__ float2 h2x2(const uint8_t *p) {
-    return __half22float2(*reinterpret_cast<const __half2 *>(p));
-}
-__device__ __forceinline__ float sum4(const float *p) {
-    const float4 v = *reinterpret_cast<const float4 *>(p);
-    return (v.x + v.y) + (v.z + v.w);
-}
-// Named barriers with constant ids: 1 + s for the 128 threads of slice s,
-// 3 + p for the 64 threads of pair p (0 is __syncthreads)
-template <int ID, int COUNT>
-__device__ __forceinline__ void bar_sync_c() {
-    asm volatile("bar.sync %0, %1;\n" ::"n"(ID), "n"(COUNT) : "memory");
-}
-__device__ __forceinline__ void slice_sync(int s) {
-    if (s == 0)
-        bar_sync_c<1, 128>();
-    else
-        bar_sync_c<2, 128>();
-}
-__device__ __forceinline__ void pair_sync(int p) {
-    switch (p) {
-    case 0: bar_sync_c<3, 64>(); break;
-    case 1: bar_sync_c<4, 64>(); break;
-    case 2: bar_sync_c<5, 64>(); break;
-    default: bar_sync_c<6, 64>(); break;
+// ---- step 4: the online-softmax step of the tile (warp q = query head q;
+// lane l holds tokens 4l .. 4l + 3) over scores = scale * (slice 0 + slice 1
+// partials), masked to [t0, t0 + n).  Writes the weight operand: int8 limbs
+// of w * scale_v (records) or f16 high / remainder of w (F16 rows).
+template <bool REC_TILE>
+__device__ __forceinline__ void softmax_step(const Cta c, int t0, int n, float scale,
+                                             const uint8_t *vrec0, const uint8_t *vrec1) {
+    const int q = c.warp, t = 4 * c.lane;
+    float *vec = c.vec;
+    if (q >= c.G) {
+        if (c.lane == 0) {
+            vec[V_ALPHA * 8 + q] = 0.0f;
+            vec[V_EW * 8 + q] = vec[(V_EW + 1) * 8 + q] = 0.0f;
+            vec[V_WZ * 8 + q] = vec[(V_WZ + 1) * 8 + q] = 0.0f;
+        }
+        return;
     }
+    const float4 p0 = *reinterpret_cast<const float4 *>(c.ps + q * PLD + t);
+    const float4 p1 = *reinterpret_cast<const float4 *>(c.ps + (8 + q) * PLD + t);
+    const float sp[4] = {p0.x + p1.x, p0.y + p1.y, p0.z + p1.z, p0.w + p1.w};
+    float sc[4], mt = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        sc[i] = (t + i >= t0 && t + i < t0 + n) ? sp[i] * scale : -INFINITY;
+        mt = fmaxf(mt, sc[i]);
+    }
+    mt = warp_max(mt);
+    const float m_old = vec[V_M * 8 + q], den_old = vec[V_DEN * 8 + q];
+    const float m_new = fmaxf(m_old, mt);
+    const float alpha = den_old == 0.0f ? 0.0f : __expf(m_old - m_new);
+    float w[4], sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        w[i] = __expf(sc[i] - m_new);
+        sum += w[i];
+    }
+    sum = warp_sum(sum);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        uint8_t *bw = c.sm + SM_BW + s * 4096;
+        if (REC_TILE) {
+            const uint8_t *vr = s ? vrec1 : vrec0;
+            float sv[4], zv[4], ws[4], mx = 0.0f, wz = 0.0f;
+            h4(vr + NIB + 2 * t, sv);
+            h4(vr + NIB + 256 + 2 * t, zv);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                ws[i] = w[i] * sv[i];
+                mx = fmaxf(mx, fabsf(ws[i]));
+                wz = fmaf(w[i], zv[i], wz);
+            }
+            mx = warp_max(mx);
+            wz = warp_sum(wz);
+            const float mul = limb_scale(mx);
+            int l[3][4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                limbs(ws[i], mul, l[0][i], l[1][i], l[2][i]);
+            // K-major B: row 8 j + q = limb j; k = token
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+                *reinterpret_cast<uint32_t *>(bw + swz(8 * j + q, t >> 4) + (t & 15)) =
+                    pack4(l[j][0], l[j][1], l[j][2], l[j][3]);
+            if (c.lane == 0) {
+                vec[(V_EW + s) * 8 + q] = 1.0f / mul;
+                vec[(V_WZ + s) * 8 + q] = wz;
+            }
+        } else if (s == 0) {
+            // F16 rows: both slices' products use the same weights; rows q (f16
+            // high part) and 8 + q (remainder), two 64-token atom columns
+            float h[4], l[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                hilo(w[i], h[i], l[i]);
+#pragma unroll
+            for (int ss = 0; ss < 2; ++ss) {
+                uint8_t *b = c.sm + SM_BW + ss * 4096 + (t >> 6) * 2048;
+                const int tc = t & 63;
+                *reinterpret_cast<uint2 *>(b + swz(q, tc >> 3) + 2 * (tc & 7)) =
+                    make_uint2(f16x2(h[0], h[1]), f16x2(h[2], h[3]));
+                *reinterpret_cast<uint2 *>(b + swz(8 + q, tc >> 3) + 2 * (tc & 7)) =
+                    make_uint2(f16x2(l[0], l[1]), f16x2(l[2], l[3]));
+            }
+            if (c.lane == 0) {
+                vec[V_EW * 8 + q] = vec[(V_EW + 1) * 8 + q] = 1.0f;
+                vec[V_WZ * 8 + q] = vec[(V_WZ + 1) * 8 + q] = 0.0f;
+            }
+        }
+    }
+    if (c.lane == 0) {
+        vec[V_M * 8 + q] = m_new;
+        vec[V_DEN * 8 + q] = den_old * alpha + sum;
+        vec[V_ALPHA * 8 + q] = alpha;
+    }
+}
+
+// ---- step 5 epilogue: this thread's value-numerator dim (slice s = warp / 4,
+// TMEM lane L = 32 (warp % 4) + lane, dim position unperm(L)) for all heads
+template <bool REC_TILE>
+__device__ __forceinline__ void value_epilogue(const Cta c, const uint8_t *vrec0,
+                                               const uint8_t *vrec1, float (&acc)[8]) {
+    const int s = c.warp >> 2, L = 32 * (c.warp & 3) + c.lane;
+    const uint32_t ta = c.tmem + ((uint32_t)(32 * (c.warp & 3)) << 16) + 64 + 32 * s;
+    if (REC_TILE) {
+        float d[32];
+        tc::tmem_ld32(ta, d);
+        const float o = h2f((s ? vrec1 : vrec0) + NIB + 512 + 2 * unperm(L));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float val = fmaf(combine(d[q], d[8 + q], d[16 + q]), c.vec[(V_EW + s) * 8 + q],
+                                   c.vec[(V_WZ + s) * 8 + q]);
+            acc[q] = fmaf(o, val, acc[q] * c.vec[V_ALPHA * 8 + q]);
+        }
+    } else {
+        float d[16];
+        tc::tmem_ld16(ta, d);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            acc[q] = fmaf(acc[q], c.vec[V_ALPHA * 8 + q], d[q] + d[8 + q]);
+    }
+}
+
+// ---- step 2 epilogue: this thread's token (slice s, TMEM lane L, token
+// position pos(L)) partial scores for all heads into ps[s][q][token]
+template <bool REC_TILE>
+__device__ __forceinline__ void score_epilogue(const Cta c, const uint8_t *krec0,
+                                               const uint8_t *krec1) {
+    const int s = c.warp >> 2, L = 32 * (c.warp & 3) + c.lane;
+    const uint32_t ta = c.tmem + ((uint32_t)(32 * (c.warp & 3)) << 16) + 32 * s;
+    const int tok = REC_TILE ? unperm(L) : L;
+    float *ps = c.ps + s * 8 * PLD + tok;
+    if (REC_TILE) {
+        float d[32];
+        tc::tmem_ld32(ta, d);
+        const float o = h2f((s ? krec1 : krec0) + NIB + 512 + 2 * tok);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            ps[q * PLD] = o * fmaf(combine(d[q], d[8 + q], d[16 + q]), c.vec[(V_EQ + s) * 8 + q],
+                                   c.vec[(V_QZ + s) * 8 + q]);
+    } else {
+        float d[16];
+        tc::tmem_ld16(ta, d);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            ps[q * PLD] = d[q] + d[8 + q];
+    }
+}
+
+// Bounded wait on an MMA barrier by every thread; false on timeout.
+__device__ __forceinline__ bool wait_mma(const Cta c, uint32_t bar, uint32_t &phase) {
+    const bool ok = tc::mbar_wait(bar, phase, c.zero);
+    phase ^= 1u;
+    tc::tc_fence_after();
+    return ok;
+}
+
+// One record group (records of slice 0 / 1 at krec0 / krec1, vrec0 / vrec1 in
+// global memory), rows [t0, t0 + n) of it.  Returns false if an MMA wait ran
+// out (CTA-uniform).
+__device__ __forceinline__ bool record_tile(const Cta c, const uint8_t *krec0,
+                                            const uint8_t *krec1, const uint8_t *vrec0,
+                                            const uint8_t *vrec1, int t0, int n, float scale,
+                                            uint32_t &ph_s, uint32_t &ph_v, float (&acc)[8]) {
+    // the V records' 4-bit values, in flight while the scores run
+    uint4 vw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = c.tid + NT * j, s = i >> 9, r = (i >> 2) & 127, c4 = i & 3;
+        vw[j] = ldg128((s ? vrec1 : vrec0) + r * 64 + c4 * 16);
+    }
+    // 1. K widened into A0 (slice s at 16 KB s); the query operand
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = c.tid + NT * j, s = i >> 9, r = (i >> 2) & 127, c4 = i & 3;
+        widen(c.sm + SM_A0 + s * 16384, r, c4, ldg128((s ? krec1 : krec0) + r * 64 + c4 * 16));
+    }
+    {
+        // thread (slice s, head q, dims 8 ch .. 8 ch + 7); the 16 threads of a
+        // (s, q) are one half-warp
+        const int s = c.tid >> 7, q = (c.tid >> 4) & 7, ch = c.tid & 15;
+        const uint8_t *kr = s ? krec1 : krec0;
+        float sk[8], zk[8];
+        h8(kr + NIB + 16 * ch, sk);
+        h8(kr + NIB + 256 + 16 * ch, zk);
+        const float *qr = c.qv + q * QLD + 128 * s + 8 * ch;
+        const float4 qa = *reinterpret_cast<const float4 *>(qr);
+        const float4 qb = *reinterpret_cast<const float4 *>(qr + 4);
+        const float qx[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        float qs[8], mx = 0.0f, z = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            qs[i] = qx[i] * sk[i];
+            mx = fmaxf(mx, fabsf(qs[i]));
+            z = fmaf(qx[i], zk[i], z);
+        }
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            z += __shfl_xor_sync(0xffffffffu, z, o);
+        }
+        const float mul = limb_scale(mx);
+        int l[3][8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            limbs(qs[i], mul, l[0][i], l[1][i], l[2][i]);
+        uint8_t *bq = c.sm + SM_BQ + s * 4096;
+        const uint32_t off = 8 * (ch & 1);
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+            *reinterpret_cast<uint2 *>(bq + swz(8 * j + q, ch >> 1) + off) =
+                make_uint2(pack4(l[j][0], l[j][1], l[j][2], l[j][3]),
+                           pack4(l[j][4], l[j][5], l[j][6], l[j][7]));
+        if (ch == 0) {
+            c.vec[(V_EQ + s) * 8 + q] = 1.0f / mul;
+            c.vec[(V_QZ + s) * 8 + q] = z;
+        }
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    // 2. scores: D[token][limb x head] per slice, K = 128 dims in 4 steps
+    if (c.tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = tc::sdesc(smem_u32(c.sm + SM_A0 + s * 16384 + kk * 4096),
+                                              16384, 1024);
+                const uint64_t bd =
+                    tc::sdesc(smem_u32(c.sm + SM_BQ + s * 4096) + kk * 32, 16, 1024);
+                mma_i8(c.tmem + 32 * s, ad, bd, kk > 0);
+            }
+        tc::mma_commit(c.bar_s);
+    }
+    // 3. V widened into A1 (free: the previous tile's value MMAs are done)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int i = c.tid + NT * j, s = i >> 9, r = (i >> 2) & 127, c4 = i & 3;
+        widen(c.sm + SM_A1 + s * 16384, r, c4, vw[j]);
+    }
+    bool ok = wait_mma(c, c.bar_s, ph_s);
+    score_epilogue<true>(c, krec0, krec1);
+    tc::tc_fence_before();
+    if (__syncthreads_or(!ok))
+        return false;
+    // 4. softmax step, weight operand
+    softmax_step<true>(c, t0, n, scale, vrec0, vrec1);
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    // 5. values: D[dim][limb x head] per slice, K = 128 tokens in 4 steps
+    if (c.tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = tc::sdesc(smem_u32(c.sm + SM_A1 + s * 16384 + kk * 4096),
+                                              16384, 1024);
+                const uint64_t bd =
+                    tc::sdesc(smem_u32(c.sm + SM_BW + s * 4096) + kk * 32, 16, 1024);
+                mma_i8(c.tmem + 64 + 32 * s, ad, bd, kk > 0);
+            }
+        tc::mma_commit(c.bar_v);
+    }
+    ok = wait_mma(c, c.bar_v, ph_v);
+    value_epilogue<true>(c, vrec0, vrec1, acc);
+    tc::tc_fence_before();
+    return __syncthreads_or(!ok) == 0;
+}
+
+// Stage n <= 128 F16 rows (row stride row_bytes, this head's 256 values at
+// rows) into A0 (slice 0) and A1 (slice 1): K rows as K-major tiles (two
+// 64-dim atom columns of 128 rows), V rows MN-major with the even dims of each
+// 8 in the first 64-dim block and the odd dims in the second (the order of the
+// widened records).  Rows >= n are zero.
+template <bool VALUE>
+__device__ __forceinline__ void stage_f16(const Cta c, const uint8_t *rows, int64_t row_bytes,
+                                          int n) {
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+        const int i = c.tid + NT * j, s = i >> 11, r = (i >> 4) & 127, ch = i & 15;
+        const uint4 w = r < n ? ldg128(rows + r * row_bytes + 256 * s + 16 * ch)
+                              : make_uint4(0u, 0u, 0u, 0u);
+        uint8_t *tile = c.sm + (s ? SM_A1 : SM_A0);
+        if (!VALUE) {
+            *reinterpret_cast<uint4 *>(tile + (ch >> 3) * 16384 + swz(r, ch & 7)) = w;
+        } else {
+            // dims 8 ch .. 8 ch + 7: even ones -> positions 4 ch .. (block 0),
+            // odd ones -> 64 + 4 ch .. (block 1)
+            const uint2 ev = make_uint2(__byte_perm(w.x, w.y, 0x5410), __byte_perm(w.z, w.w, 0x5410));
+            const uint2 od = make_uint2(__byte_perm(w.x, w.y, 0x7632), __byte_perm(w.z, w.w, 0x7632));
+            const uint32_t off = swz(r, ch >> 1) + 8 * (ch & 1);
+            *reinterpret_cast<uint2 *>(tile + off) = ev;
+            *reinterpret_cast<uint2 *>(tile + 16384 + off) = od;
+        }
+    }
+}
+
+// n <= 128 F16 rows: stage rows of a body split (rotated, meet WHT(q)) or
+// tail rows of the tail split (original, meet q); qv holds the right one.
+__device__ __forceinline__ bool f16_tile(const Cta c, const uint8_t *krows, const uint8_t *vrows,
+                                         int64_t row_bytes, int n, float scale, uint32_t &ph_s,
+                                         uint32_t &ph_v, float (&acc)[8]) {
+    stage_f16<false>(c, krows, row_bytes, n);
+    {
+        // query operand: rows q (f16 of qv) and 8 + q (remainder); thread
+        // (slice s, head q, dims 8 ch .. 8 ch + 7)
+        const int s = c.tid >> 7, q = (c.tid >> 4) & 7, ch = c.tid & 15;
+        const float *qr = c.qv + q * QLD + 128 * s + 8 * ch;
+        float h[8], l[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            hilo(qr[i], h[i], l[i]);
+        uint8_t *b = c.sm + SM_BQ + s * 4096 + (ch >> 3) * 2048;
+        *reinterpret_cast<uint4 *>(b + swz(q, ch & 7)) =
+            make_uint4(f16x2(h[0], h[1]), f16x2(h[2], h[3]), f16x2(h[4], h[5]), f16x2(h[6], h[7]));
+        *reinterpret_cast<uint4 *>(b + swz(8 + q, ch & 7)) =
+            make_uint4(f16x2(l[0], l[1]), f16x2(l[2], l[3]), f16x2(l[4], l[5]), f16x2(l[6], l[7]));
+    }
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (c.tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t a = smem_u32(c.sm + (s ? SM_A1 : SM_A0)) + (kk >> 2) * 16384 +
+                                   (kk & 3) * 32;
+                const uint32_t b =
+                    smem_u32(c.sm + SM_BQ + s * 4096) + (kk >> 2) * 2048 + (kk & 3) * 32;
+                tc::mma_ss(c.tmem + 32 * s, tc::sdesc(a, 16, 1024), tc::sdesc(b, 16, 1024),
+                           ID_F16_S, kk > 0);
+            }
+        tc::mma_commit(c.bar_s);
+    }
+    bool ok = wait_mma(c, c.bar_s, ph_s);
+    score_epilogue<false>(c, nullptr, nullptr);
+    tc::tc_fence_before();
+    if (__syncthreads_or(!ok))
+        return false;
+    stage_f16<true>(c, vrows, row_bytes, n); // A0 / A1 free: the score MMAs are done
+    softmax_step<false>(c, 0, n, scale, nullptr, nullptr);
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (c.tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t a = smem_u32(c.sm + (s ? SM_A1 : SM_A0)) + kk * 2048;
+                const uint32_t b =
+                    smem_u32(c.sm + SM_BW + s * 4096) + (kk >> 2) * 2048 + (kk & 3) * 32;
+                tc::mma_ss(c.tmem + 64 + 32 * s, tc::sdesc(a, 16384, 1024),
+                           tc::sdesc(b, 16, 1024), ID_F16_V, kk > 0);
+            }
+        tc::mma_commit(c.bar_v);
+    }
+    ok = wait_mma(c, c.bar_v, ph_v);
+    value_epilogue<false>(c, nullptr, nullptr, acc);
+    tc::tc_fence_before();
+    return __syncthreads_or(!ok) == 0;
 }
 
 // In-register WHT256 of the 256-vector held as v[i] = x[8 lane + i] by one
@@ -204,279 +574,35 @@ __device__ __forceinline__ void wht_regs(float (&v)[8], int lane) {
         v[i] *= 0.0625f;
 }
 
-// Sum the pair's partial scores (part: this warp's slice, part[u'][e] for
-// tokens 32p + 16u' + {2c, 2c+1, 2c+8, 2c+9}[e] of the tile), scale, mask
-// tokens outside [t0, t0 + n) and query heads >= G, and run the lane's
-// online-softmax step.  Returns the weights in w and the accumulators'
-// rescale factor.  The exchange buffer alternates with the tile parity, so a
-// partner still reading the previous tile's scores is never overwritten.
-__device__ __forceinline__ float pair_softmax(const Cta c, const float (&part)[2][4], int t0,
-                                              int n, float scale, int parity, Run &r,
-                                              float (&w)[2][4]) {
-    float *own = c.xs + (((parity * 2 + c.s) * 4 + c.p) * 32 + c.lane) * 8;
-    const float *oth = c.xs + (((parity * 2 + (c.s ^ 1)) * 4 + c.p) * 32 + c.lane) * 8;
-    reinterpret_cast<float4 *>(own)[0] = make_float4(part[0][0], part[0][1], part[0][2], part[0][3]);
-    reinterpret_cast<float4 *>(own)[1] = make_float4(part[1][0], part[1][1], part[1][2], part[1][3]);
-    pair_sync(c.p);
-    const float4 o0 = reinterpret_cast<const float4 *>(oth)[0];
-    const float4 o1 = reinterpret_cast<const float4 *>(oth)[1];
-    const float other[2][4] = {{o0.x, o0.y, o0.z, o0.w}, {o1.x, o1.y, o1.z, o1.w}};
-    const bool on = c.g < c.G;
-    float sc[2][4], mt = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int t = 32 * c.p + 16 * u + 2 * c.c + (e & 1) + 8 * (e >> 1);
-            // slice 0 + slice 1 in the same order in both warps of the pair
-            const float v = (c.s == 0 ? part[u][e] + other[u][e] : other[u][e] + part[u][e]) * scale;
-            sc[u][e] = (on && t >= t0 && t < t0 + n) ? v : -INFINITY;
-            mt = fmaxf(mt, sc[u][e]);
-        }
-    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
-    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-    const float m_new = fmaxf(r.m, mt);
-    const float alpha = r.den == 0.0f ? 0.0f : __expf(r.m - m_new);
-    float sum = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 2; ++u)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            w[u][e] = __expf(sc[u][e] - m_new); // masked: exp(-inf) = 0
-            sum += w[u][e];
-        }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (on) {
-        r.den = r.den * alpha + sum;
-        r.m = m_new;
-    }
-    return alpha;
-}
-
-// Scores D of n-tiles (u', parity) -> part[u'][e] in token order {2c, 2c+1,
-// 2c+8, 2c+9}: column 2c is token 2c + parity, column 2c + 1 is 2c + 8 + parity;
-// rows g (hi) and g + 8 (lo) add up.
-__device__ __forceinline__ void gather_scores(const float (&d)[2][2][4], float (&part)[2][4]) {
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        part[u][0] = d[u][0][0] + d[u][0][2];
-        part[u][1] = d[u][1][0] + d[u][1][2];
-        part[u][2] = d[u][0][1] + d[u][0][3];
-        part[u][3] = d[u][1][1] + d[u][1][3];
-    }
-}
-
-// n <= 128 consecutive F16 rows (row stride row_bytes; this KV head's 256
-// values at krows / vrows): stage rows of a body split (rotated; A = WHT(q)
-// fragments) or tail rows of the tail split (original; A = q fragments).
-__device__ __forceinline__ void f16_tile(const Cta c, const uint8_t *krows, const uint8_t *vrows,
-                                         int64_t row_bytes, int n, float scale, int parity, Run &r) {
-    float part[2][4];
-    {
-        // B: lane g' = g takes token 2 (g / 2) + 8 (g % 2) + parity of unit
-        // 2p + u', dims 16 kk + 2c (+ 8) of slice s
-        float d[2][2][4] = {};
-        const uint8_t *kb = krows + 2 * (128 * c.s + 2 * c.c);
-        const int jb = 32 * c.p + 2 * (c.g >> 1) + 8 * (c.g & 1);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint4 a = c.fq[(c.s * 8 + kk) * 32 + c.lane];
-#pragma unroll
-            for (int u = 0; u < 2; ++u)
-#pragma unroll
-                for (int par = 0; par < 2; ++par) {
-                    const int j = jb + 16 * u + par;
-                    const uint8_t *kr = kb + (int64_t)j * row_bytes + 32 * kk;
-                    const uint32_t b0 = j < n ? ldg32(kr) : 0u, b1 = j < n ? ldg32(kr + 16) : 0u;
-                    mma16816(d[u][par], a, b0, b1);
-                }
-        }
-        gather_scores(d, part);
-    }
-    float w[2][4];
-    const float alpha = pair_softmax(c, part, 0, n, scale, parity, r, w);
-    {
-        uint4 av[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u)
-            av[u] = afrag(w[u][0], w[u][1], w[u][2], w[u][3]);
-        // B: lane g takes dims 16 u + 8 (g % 2) + 2 (g / 2) + {0, 1} (the two
-        // parities) of tokens 32p + 16u' + 2c + {0, 1, 8, 9}
-        const uint8_t *vb = vrows + 2 * (128 * c.s + 8 * (c.g & 1) + 2 * (c.g >> 1));
-        const int tb = 32 * c.p + 2 * c.c;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            float dv[2][4] = {};
-#pragma unroll
-            for (int uu = 0; uu < 2; ++uu) {
-                uint32_t x[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int t = tb + 16 * uu + (e & 1) + 8 * (e >> 1);
-                    x[e] = t < n ? ldg32(vb + (int64_t)t * row_bytes + 32 * u) : 0u;
-                }
-                mma16816(dv[0], av[uu], __byte_perm(x[0], x[1], 0x5410),
-                         __byte_perm(x[2], x[3], 0x5410));
-                mma16816(dv[1], av[uu], __byte_perm(x[0], x[1], 0x7632),
-                         __byte_perm(x[2], x[3], 0x7632));
-            }
-            r.acc[u][0] = r.acc[u][0] * alpha + (dv[0][0] + dv[0][2]);
-            r.acc[u][1] = r.acc[u][1] * alpha + (dv[1][0] + dv[1][2]);
-            r.acc[u][2] = r.acc[u][2] * alpha + (dv[0][1] + dv[0][3]);
-            r.acc[u][3] = r.acc[u][3] * alpha + (dv[1][1] + dv[1][3]);
-        }
-    }
-}
-
-// Rows [t0, t0 + n) of one complete record group whose four records are in
-// shared memory at rk (nibble rows swizzled).
-__device__ __forceinline__ void record_tile(const Cta c, const uint8_t *rk, int t0, int n,
-                                            float scale, int parity, Run &r) {
-    {
-        // A fragments of slice s: qs[d] = WHT(q)_g[128 s + d] * scale_k[d] for
-        // MMA steps p and p + 4, and this thread's part of WHT(q) . zero_k
-        const uint8_t *kax = rk + ax_off(c.s);
-        float z = 0.0f;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int kk = c.p + 4 * h, dl = 16 * kk + 2 * c.c;
-            const float *qrow = c.qr + c.g * QLD + 128 * c.s + dl;
-            const float2 q01 = *reinterpret_cast<const float2 *>(qrow);
-            const float2 q89 = *reinterpret_cast<const float2 *>(qrow + 8);
-            const float2 s01 = h2x2(kax + 2 * dl), s89 = h2x2(kax + 2 * dl + 16);
-            const float2 z01 = h2x2(kax + 256 + 2 * dl), z89 = h2x2(kax + 256 + 2 * dl + 16);
-            c.kf[(c.s * 8 + kk) * 32 + c.lane] =
-                afrag(q01.x * s01.x, q01.y * s01.y, q89.x * s89.x, q89.y * s89.y);
-            z += (q01.x * z01.x + q01.y * z01.y) + (q89.x * z89.x + q89.y * z89.y);
-        }
-        z += __shfl_xor_sync(0xffffffffu, z, 1);
-        z += __shfl_xor_sync(0xffffffffu, z, 2);
-        if (c.c == 0)
-            c.zp[(c.s * 8 + c.g) * 4 + c.p] = z;
-        slice_sync(c.s);
-    }
-    float part[2][4];
-    {
-        // scores of tokens 32p + 16u' + ..., all 128 dims of slice s; the K
-        // nibble rows are dims, lane g' reads byte g' / 2 of word 2 (2p + u') +
-        // g' % 2 (tokens 2 (g' / 2) + 8 (g' % 2) + {0, 1} of the unit)
-        float d[2][2][4] = {};
-        const uint8_t *kb = rk + nib_off(c.s) + 128 * c.c + 16 * (c.p ^ c.c) + 4 * (c.g & 1);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-            const uint4 a = c.kf[(c.s * 8 + kk) * 32 + c.lane];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const uint8_t *pp = kb + kk * 1024 + 8 * u;
-                uint32_t b0p0, b0p1, b1p0, b1p1;
-                nib_frag(lds32(pp), lds32(pp + 64), c.sel, b0p0, b0p1);
-                nib_frag(lds32(pp + 512), lds32(pp + 576), c.sel, b1p0, b1p1);
-                mma16816(d[u][0], a, b0p0, b1p0);
-                mma16816(d[u][1], a, b0p1, b1p1);
-            }
-        }
-        gather_scores(d, part);
-        const float qz = sum4(c.zp + (c.s * 8 + c.g) * 4);
-        const uint8_t *oax = rk + ax_off(c.s) + 512;
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int t = 32 * c.p + 16 * u + 2 * c.c;
-            const float2 o01 = h2x2(oax + 2 * t), o89 = h2x2(oax + 2 * t + 16);
-            part[u][0] = o01.x * (part[u][0] + qz);
-            part[u][1] = o01.y * (part[u][1] + qz);
-            part[u][2] = o89.x * (part[u][2] + qz);
-            part[u][3] = o89.y * (part[u][3] + qz);
-        }
-    }
-    float w[2][4];
-    const float alpha = pair_softmax(c, part, t0, n, scale, parity, r, w);
-    {
-        // A = w * scale_v of slice s's V record, and sum_t w_t zero_v[t]
-        const uint8_t *vax = rk + ax_off(2 + c.s);
-        uint4 av[2];
-        float wz = 0.0f;
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int t = 32 * c.p + 16 * u + 2 * c.c;
-            const float2 c01 = h2x2(vax + 2 * t), c89 = h2x2(vax + 2 * t + 16);
-            const float2 z01 = h2x2(vax + 256 + 2 * t), z89 = h2x2(vax + 256 + 2 * t + 16);
-            av[u] = afrag(w[u][0] * c01.x, w[u][1] * c01.y, w[u][2] * c89.x, w[u][3] * c89.y);
-            wz += (w[u][0] * z01.x + w[u][1] * z01.y) + (w[u][2] * z89.x + w[u][3] * z89.y);
-        }
-        wz += __shfl_xor_sync(0xffffffffu, wz, 1);
-        wz += __shfl_xor_sync(0xffffffffu, wz, 2);
-        // value numerator: the V nibble rows are tokens 32p + 16u' + 2c + {0,
-        // 1, 8, 9}; lane g reads byte g / 2 of word 2u + g % 2 (dims 16u + 8 (g
-        // % 2) + 2 (g / 2) + {0, 1})
-        const uint8_t *vb = rk + nib_off(2 + c.s) + 2048 * c.p + 128 * c.c + 4 * (c.g & 1);
-        const uint8_t *oax = vax + 512 + 4 * c.c;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            float dv[2][4] = {};
-            const int off = 16 * ((u >> 1) ^ c.c) + 8 * (u & 1);
-#pragma unroll
-            for (int uu = 0; uu < 2; ++uu) {
-                const uint8_t *pp = vb + 1024 * uu + off;
-                uint32_t b0p0, b0p1, b1p0, b1p1;
-                nib_frag(lds32(pp), lds32(pp + 64), c.sel, b0p0, b0p1);
-                nib_frag(lds32(pp + 512), lds32(pp + 576), c.sel, b1p0, b1p1);
-                mma16816(dv[0], av[uu], b0p0, b1p0);
-                mma16816(dv[1], av[uu], b0p1, b1p1);
-            }
-            const float2 o01 = h2x2(oax + 32 * u), o89 = h2x2(oax + 32 * u + 16);
-            r.acc[u][0] = r.acc[u][0] * alpha + o01.x * ((dv[0][0] + dv[0][2]) + wz);
-            r.acc[u][1] = r.acc[u][1] * alpha + o01.y * ((dv[1][0] + dv[1][2]) + wz);
-            r.acc[u][2] = r.acc[u][2] * alpha + o89.x * ((dv[0][1] + dv[0][3]) + wz);
-            r.acc[u][3] = r.acc[u][3] * alpha + o89.y * ((dv[1][1] + dv[1][3]) + wz);
-        }
-    }
-}
-
-// One thread: group grp's four records of KV head kv into the buffer at dst,
-// completing on bar.  The tensor maps view each plane's records as rows of 64
-// bytes (a record = 140 rows, its nibbles the first 128).
-__device__ __forceinline__ void issue_group(const CUtensorMap *kmap, const CUtensorMap *vmap,
-                                            const Kvarn4Args &a, uint8_t *dst, uint32_t bar,
-                                            int grp, int kv) {
-    tc::mbar_expect_tx(bar, SET);
-    const int64_t r0 = (int64_t)grp * 2 * a.n_head_kv + 2 * kv;
-#pragma unroll
-    for (int which = 0; which < 4; ++which) {
-        const int64_t r = r0 + (which & 1);
-        tc::tma_load_2d(smem_u32(dst + nib_off(which)), which < 2 ? kmap : vmap, 0,
-                        (int)(r * (REC / 64)), bar);
-        tc::bulk_load(smem_u32(dst + ax_off(which)), (which < 2 ? a.k : a.v) + r * REC + NIB, AXB,
-                      bar);
-    }
+// L2 prefetch of a record group's four records (K and V, both slices: two
+// contiguous 17,920-byte runs)
+__device__ __forceinline__ void prefetch_group(const Kvarn4Args &a, int grp, int kv) {
+    const int64_t r = ((int64_t)grp * a.n_head_kv + kv) * 2 * REC;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.k + r), "r"(2 * REC)
+                 : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.v + r), "r"(2 * REC)
+                 : "memory");
 }
 } // namespace k4
 
-__global__ void __launch_bounds__(k4::NT, 2)
-    kvarn4_partials_kernel(const __grid_constant__ CUtensorMap kmap,
-                           const __grid_constant__ CUtensorMap vmap, const Kvarn4Args a) {
+__global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4Args a) {
     using namespace k4;
     extern __shared__ __align__(1024) uint8_t sm_raw[];
-    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 511) &
-                                              ~uintptr_t(511));
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) &
+                                              ~uintptr_t(1023));
     Cta c;
-    c.qr = reinterpret_cast<float *>(sm + SM_QR);
-    c.xs = reinterpret_cast<float *>(sm + SM_XS);
-    c.zp = reinterpret_cast<float *>(sm + SM_ZP);
-    c.kf = reinterpret_cast<uint4 *>(sm + SM_KF);
-    c.fq = reinterpret_cast<uint4 *>(sm + SM_FQ);
+    c.sm = sm;
+    c.qv = reinterpret_cast<float *>(sm + SM_QV);
+    c.ps = reinterpret_cast<float *>(sm + SM_PS);
+    c.vec = reinterpret_cast<float *>(sm + SM_VEC);
+    c.bar_s = smem_u32(sm + SM_BAR);
+    c.bar_v = c.bar_s + 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + SM_BAR + 16);
+    c.zero = reinterpret_cast<volatile int *>(sm + SM_BAR + 20);
     c.tid = threadIdx.x;
     c.warp = c.tid >> 5;
     c.lane = c.tid & 31;
-    c.g = c.lane >> 2;
-    c.c = c.lane & 3;
-    c.s = c.warp >> 2;
-    c.p = c.warp & 3;
     c.G = a.n_head / a.n_head_kv;
-    {
-        const uint32_t b = c.g >> 1;
-        c.sel = b | (b << 4) | ((b + 4) << 8) | ((b + 4) << 12);
-    }
     const int split = blockIdx.x, kv = blockIdx.y, tok = blockIdx.z;
     const int64_t row_bytes = (int64_t)a.n_head_kv * 512;
 
@@ -489,31 +615,23 @@ __global__ void __launch_bounds__(k4::NT, 2)
     const int live = a.active ? (a.active - 1) / GROUP : 0;
     const bool live_partial = (a.active % GROUP) != 0;
     const int og = a.origin / GROUP;
-
     // a body group is read from its records unless it is the global sink group
     // or the incomplete live group (stage rows)
     const int g0 = r0 / GROUP, g1 = (!tail_split && r1 > r0) ? (r1 + GROUP - 1) / GROUP : g0;
     auto record_group = [=](int grp) { return og + grp != 0 && !(grp == live && live_partial); };
-    const uint32_t bar0 = smem_u32(sm + SM_BAR);
-    volatile int *zero = reinterpret_cast<volatile int *>(sm + SM_BAR + 16);
-    if (c.tid == 0) {
-        tc::mbar_init(bar0, 1);
-        tc::mbar_init(bar0 + 8, 1);
-        *zero = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        tc::prefetch_map(&kmap);
-        tc::prefetch_map(&vmap);
-        int next = g0;
-        while (next < g1 && !record_group(next))
-            ++next;
-        if (next < g1)
-            issue_group(&kmap, &vmap, a, sm + SM_REC, bar0, next, kv);
-    }
 
-    // ---- query head g = warp: WHT(q) rows (body splits) and the F16-tile A
-    // fragments of the split's domain; lane l holds dims 8l .. 8l + 7 = half
-    // l % 2 of MMA step l / 2
+    if (c.tid == 0) {
+        tc::mbar_init(c.bar_s, 1);
+        tc::mbar_init(c.bar_v, 1);
+        *c.zero = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        if (g0 < g1 && record_group(g0))
+            prefetch_group(a, g0, kv);
+    }
+    if (c.warp == 0)
+        tc::tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
     {
+        // query head g = warp: q or WHT(q) rows; running max / denominator
         const int g = c.warp;
         float v[8];
         if (g < c.G) {
@@ -526,117 +644,87 @@ __global__ void __launch_bounds__(k4::NT, 2)
             for (int i = 0; i < 8; ++i)
                 v[i] = 0.0f;
         }
-        if (!tail_split) {
+        if (!tail_split)
             wht_regs(v, c.lane);
-            float4 *qd = reinterpret_cast<float4 *>(c.qr + g * QLD + 8 * c.lane);
-            qd[0] = make_float4(v[0], v[1], v[2], v[3]);
-            qd[1] = make_float4(v[4], v[5], v[6], v[7]);
-        }
-        uint2 *fq2 = reinterpret_cast<uint2 *>(c.fq);
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-            uint2 hl;
-            split2(v[2 * cc], v[2 * cc + 1], hl.x, hl.y);
-            fq2[((c.lane >> 1) * 32 + 4 * g + cc) * 2 + (c.lane & 1)] = hl;
+        float4 *qd = reinterpret_cast<float4 *>(c.qv + g * QLD + 8 * c.lane);
+        qd[0] = make_float4(v[0], v[1], v[2], v[3]);
+        qd[1] = make_float4(v[4], v[5], v[6], v[7]);
+        if (c.tid < GMAX) {
+            c.vec[V_M * 8 + c.tid] = -FLT_MAX;
+            c.vec[V_DEN * 8 + c.tid] = 0.0f;
         }
     }
+    tc::tc_fence_before();
     __syncthreads();
+    tc::tc_fence_after();
+    c.tmem = *tmem_slot;
 
-    Run run;
-    run.m = -FLT_MAX;
-    run.den = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            run.acc[u][i] = 0.0f;
-    int parity = 0;       // score-exchange buffer of the next tile
-    bool failed = false;  // a record wait ran out (CTA-uniform)
-    int buf = 0;
-    uint32_t phase = 0;   // bit b: parity of buffer b's next completion
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    uint32_t ph_s = 0, ph_v = 0;
+    bool ok = true;
     if (tail_split) {
         // the tail buffer is a ring of 128 rows: row r at r % 128
-        for (int rr = r0; rr < r1;) {
+        for (int rr = r0; rr < r1 && ok;) {
             const int n = min(r1 - rr, GROUP - rr % GROUP);
             const int64_t first = (int64_t)(rr % GROUP) * row_bytes + kv * 512;
-            f16_tile(c, a.k + a.tail_off + first, a.v + a.tail_off + first, row_bytes, n, a.scale,
-                     parity, run);
-            parity ^= 1;
+            ok = f16_tile(c, a.k + a.tail_off + first, a.v + a.tail_off + first, row_bytes, n,
+                          a.scale, ph_s, ph_v, acc);
             rr += n;
         }
     } else {
-        for (int grp = g0; grp < g1; ++grp) {
+        for (int grp = g0; grp < g1 && ok; ++grp) {
             const int lo = max(r0, grp * GROUP), hi = min(r1, (grp + 1) * GROUP);
+            if (c.tid == 0) {
+                int nxt = grp + 1;
+                while (nxt < g1 && !record_group(nxt))
+                    ++nxt;
+                if (nxt < g1)
+                    prefetch_group(a, nxt, kv);
+            }
             if (!record_group(grp)) {
                 // staged group: rotated F16 rows in its stage slot
                 const int slot = og + grp == 0 ? 0 : 1 + ((og + grp - 1) & 1);
                 const int64_t first =
                     ((int64_t)slot * GROUP + (lo - grp * GROUP)) * row_bytes + kv * 512;
-                f16_tile(c, a.k + a.stage_off + first, a.v + a.stage_off + first, row_bytes,
-                         hi - lo, a.scale, parity, run);
+                ok = f16_tile(c, a.k + a.stage_off + first, a.v + a.stage_off + first,
+                              row_bytes, hi - lo, a.scale, ph_s, ph_v, acc);
             } else {
-                const bool ok = tc::mbar_wait(bar0 + 8 * buf, (phase >> buf) & 1, zero);
-                // records landed; every thread is past the previous tile
-                if (__syncthreads_or(!ok)) {
-                    failed = true;
-                    break;
-                }
-                phase ^= 1u << buf;
-                if (c.tid == 0) {
-                    int nxt = grp + 1;
-                    while (nxt < g1 && !record_group(nxt))
-                        ++nxt;
-                    if (nxt < g1)
-                        issue_group(&kmap, &vmap, a, sm + SM_REC + (buf ^ 1) * SET,
-                                    bar0 + 8 * (buf ^ 1), nxt, kv);
-                }
-                record_tile(c, sm + SM_REC + buf * SET, lo - grp * GROUP, hi - lo, a.scale,
-                            parity, run);
-                buf ^= 1;
+                const int64_t rk = ((int64_t)grp * a.n_head_kv + kv) * 2 * REC;
+                ok = record_tile(c, a.k + rk, a.k + rk + REC, a.v + rk, a.v + rk + REC,
+                                 lo - grp * GROUP, hi - lo, a.scale, ph_s, ph_v, acc);
             }
-            parity ^= 1;
         }
     }
-    if (failed && c.tid == 0) // give the copies still in flight a bounded time to land
-        tc::mbar_wait(bar0 + 8 * buf, (phase >> buf) & 1, zero, 100000000ull);
-
-    // ---- combine the four pairs: per query head the max over pairs, each
-    // pair's numerator and denominator rescaled to it
-    float *mp = reinterpret_cast<float *>(sm + SM_MP); // [0, 32) max, [32, 64) den per (p, q)
-    if (c.s == 0 && c.c == 0)
-        mp[c.p * 8 + c.g] = run.m;
+    if (!ok && c.tid == 0) {
+        // give the MMAs still in flight a bounded time to finish before TMEM goes
+        // (parity of each barrier's last expected phase: immediate if it completed)
+        tc::mbar_wait(c.bar_s, ph_s ^ 1u, c.zero, 100000000ull);
+        tc::mbar_wait(c.bar_v, ph_v ^ 1u, c.zero, 100000000ull);
+    }
+    tc::tc_fence_before();
     __syncthreads();
-    float *x = reinterpret_cast<float *>(sm + SM_REC); // [4 pairs][8][QLD]
+    if (c.warp == 0)
+        tc::tmem_dealloc(c.tmem, TMEM_COLS);
+
+    // ---- numerator rows x[q][dim] (A0 is free now), rotated back in body splits
+    float *x = reinterpret_cast<float *>(sm + SM_A0);
     {
-        float mx = mp[c.g];
+        const int s = c.warp >> 2, L = 32 * (c.warp & 3) + c.lane;
+        const int d = 128 * s + unperm(L);
 #pragma unroll
-        for (int pp = 1; pp < 4; ++pp)
-            mx = fmaxf(mx, mp[pp * 8 + c.g]);
-        const float f = run.den == 0.0f ? 0.0f : __expf(run.m - mx);
-        float *xr = x + (c.p * 8 + c.g) * QLD + 128 * c.s + 2 * c.c;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            *reinterpret_cast<float2 *>(xr + 16 * u) =
-                make_float2(run.acc[u][0] * f, run.acc[u][1] * f);
-            *reinterpret_cast<float2 *>(xr + 16 * u + 8) =
-                make_float2(run.acc[u][2] * f, run.acc[u][3] * f);
-        }
-        if (c.s == 0 && c.c == 0)
-            mp[32 + c.p * 8 + c.g] = run.den * f;
+        for (int q = 0; q < 8; ++q)
+            x[q * QLD + d] = acc[q];
     }
     __syncthreads();
     if (c.warp < c.G) {
         const int g = c.warp;
-        float v[8] = {};
-#pragma unroll
-        for (int pp = 0; pp < 4; ++pp) {
-            const float4 *xs = reinterpret_cast<const float4 *>(x + (pp * 8 + g) * QLD + 8 * c.lane);
-            const float4 v0 = xs[0], v1 = xs[1];
-            v[0] += v0.x, v[1] += v0.y, v[2] += v0.z, v[3] += v0.w;
-            v[4] += v1.x, v[5] += v1.y, v[6] += v1.z, v[7] += v1.w;
-        }
+        float v[8];
+        const float4 *xs = reinterpret_cast<const float4 *>(x + g * QLD + 8 * c.lane);
+        const float4 v0 = xs[0], v1 = xs[1];
+        v[0] = v0.x, v[1] = v0.y, v[2] = v0.z, v[3] = v0.w;
+        v[4] = v1.x, v[5] = v1.y, v[6] = v1.z, v[7] = v1.w;
         if (!tail_split)
-            wht_regs(v, c.lane); // back to the original domain
+            wht_regs(v, c.lane);
         const int64_t n_rows = (int64_t)a.n_tokens * a.n_head;
         const int64_t row = (int64_t)tok * a.n_head + kv * c.G + g;
         float *rec = a.partials + ((int64_t)split * n_rows + row) * 258;
@@ -645,14 +733,8 @@ __global__ void __launch_bounds__(k4::NT, 2)
             *reinterpret_cast<float2 *>(rec + 8 * c.lane + 2 * i) =
                 make_float2(v[2 * i], v[2 * i + 1]);
         if (c.lane == 0) {
-            float mx = mp[g], den = 0.0f;
-#pragma unroll
-            for (int pp = 0; pp < 4; ++pp) {
-                mx = fmaxf(mx, mp[pp * 8 + g]);
-                den += mp[32 + pp * 8 + g];
-            }
-            rec[256] = mx;
-            rec[257] = failed ? __int_as_float(0x7fc00000) : den; // NaN poisons the row
+            rec[256] = c.vec[V_M * 8 + g];
+            rec[257] = ok ? c.vec[V_DEN * 8 + g] : __int_as_float(0x7fc00000); // NaN poisons
         }
     }
 }
@@ -664,7 +746,6 @@ cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st) {
     a.q = l.q;
     a.positions = l.positions;
     a.partials = l.partials;
-    a.records_bytes = l.records_bytes;
     a.stage_off = l.records_bytes;
     a.tail_off = l.records_bytes + (int64_t)384 * l.n_head_kv * 512;
     a.origin = l.origin;
@@ -676,29 +757,12 @@ cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st) {
     a.rows_per_split = l.rows_per_split;
     a.n_body = l.n_body;
     a.scale = l.scale;
-    // each plane's records as a 2D byte tensor of 64-byte rows; box = one
-    // record's 128 nibble rows, 64-byte swizzle
-    auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
-    if (!enc)
-        return cudaErrorNotSupported;
-    CUtensorMap maps[2];
-    for (int i = 0; i < 2; ++i) {
-        cuuint64_t dims[2] = {64, (cuuint64_t)(l.records_bytes / 64)};
-        cuuint64_t strides[1] = {64};
-        cuuint32_t box[2] = {64, 128};
-        cuuint32_t es[2] = {1, 1};
-        if (enc(&maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(i ? l.v : l.k),
-                dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
-    }
     static std::atomic<unsigned long long> attr{0};
     cudaError_t e = set_smem_limit((const void *)kvarn4_partials_kernel, k4::SM_BYTES, attr);
     if (e != cudaSuccess)
         return e;
     dim3 grid((unsigned)l.n_splits, (unsigned)l.n_head_kv, (unsigned)l.n_tokens);
-    kvarn4_partials_kernel<<<grid, k4::NT, k4::SM_BYTES, st>>>(maps[0], maps[1], a);
+    kvarn4_partials_kernel<<<grid, k4::NT, k4::SM_BYTES, st>>>(a);
     return cudaGetLastError();
 }
 
