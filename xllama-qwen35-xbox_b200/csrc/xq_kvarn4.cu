@@ -42,8 +42,14 @@
 // owns the same dim in both kinds of tile) staged into shared memory, and the
 // query / weights as an f16 high part plus remainder (N = 16 = 8 heads x 2).
 // TMEM: scores of slice s at column 32 s, values at 64 + 32 s.
+// A record group's raw bytes arrive one group ahead by bulk copies: the 4-bit
+// rows into the upper halves of the operand slots they are widened into (read
+// into registers before a barrier, so the widening can overwrite them), the
+// F16 scales / zeros / factors into a 3 KB area; K is requested once the
+// previous group's score MMAs are done, V once its value MMAs are done.
 // Every mbarrier wait is bounded; on timeout the CTA poisons its partial (NaN
-// denominator), waits a bounded time for its MMAs, frees TMEM and returns.
+// denominator), waits a bounded time for its MMAs and copies, frees TMEM and
+// returns.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <float.h>
@@ -71,7 +77,8 @@ constexpr int SM_BW = 73728; // 8 KB: weight operand (same)
 constexpr int SM_QV = 81920; // q (tail split) or WHT(q) (body splits) [8][QLD] fp32
 constexpr int SM_PS = SM_QV + GMAX * QLD * 4;   // partial scores [2 slices][8][PLD]
 constexpr int SM_VEC = SM_PS + 2 * 8 * PLD * 4; // per-head vectors [16][8]
-constexpr int SM_BAR = SM_VEC + 16 * 8 * 4;     // bar_S, bar_V, TMEM slot, zero word
+constexpr int SM_AX = SM_VEC + 16 * 8 * 4;      // F16 axes: K slice 0, 1, V slice 0, 1 (768 B each)
+constexpr int SM_BAR = SM_AX + 4 * 768;         // bar_S, bar_V, bar_RK, bar_RV, TMEM slot, zero word
 constexpr int SM_BYTES = SM_BAR + 64 + 1024;    // + alignment slack
 // rows of the per-head vectors
 constexpr int V_M = 0, V_DEN = 1, V_ALPHA = 2, V_EQ = 3, V_QZ = 5, V_EW = 7, V_WZ = 9;
@@ -109,7 +116,7 @@ __device__ __forceinline__ float h2f(const uint8_t *p) {
     return __half2float(*reinterpret_cast<const __half *>(p));
 }
 __device__ __forceinline__ void h8(const uint8_t *p, float (&x)[8]) { // 8 F16 at p (16 B)
-    const uint4 u = ldg128(p);
+    const uint4 u = *reinterpret_cast<const uint4 *>(p);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -119,7 +126,7 @@ __device__ __forceinline__ void h8(const uint8_t *p, float (&x)[8]) { // 8 F16 a
     }
 }
 __device__ __forceinline__ void h4(const uint8_t *p, float (&x)[4]) { // 4 F16 at p (8 B)
-    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(p));
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
     const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
     x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
@@ -175,7 +182,7 @@ __device__ __forceinline__ void hilo(float x, float &hi, float &lo) {
 struct Cta {
     uint8_t *sm;
     float *qv, *ps, *vec;
-    uint32_t tmem, bar_s, bar_v;
+    uint32_t tmem, bar_s, bar_v, bar_rk, bar_rv;
     volatile int *zero;
     int tid, warp, lane, G;
 };
@@ -185,8 +192,7 @@ struct Cta {
 // partials), masked to [t0, t0 + n).  Writes the weight operand: int8 limbs
 // of w * scale_v (records) or f16 high / remainder of w (F16 rows).
 template <bool REC_TILE>
-__device__ __forceinline__ void softmax_step(const Cta c, int t0, int n, float scale,
-                                             const uint8_t *vrec0, const uint8_t *vrec1) {
+__device__ __forceinline__ void softmax_step(const Cta c, int t0, int n, float scale) {
     const int q = c.warp, t = 4 * c.lane;
     float *vec = c.vec;
     if (q >= c.G) {
@@ -221,10 +227,10 @@ __device__ __forceinline__ void softmax_step(const Cta c, int t0, int n, float s
     for (int s = 0; s < 2; ++s) {
         uint8_t *bw = c.sm + SM_BW + s * 4096;
         if (REC_TILE) {
-            const uint8_t *vr = s ? vrec1 : vrec0;
+            const uint8_t *vax = c.sm + SM_AX + (2 + s) * 768;
             float sv[4], zv[4], ws[4], mx = 0.0f, wz = 0.0f;
-            h4(vr + NIB + 2 * t, sv);
-            h4(vr + NIB + 256 + 2 * t, zv);
+            h4(vax + 2 * t, sv);
+            h4(vax + 256 + 2 * t, zv);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 ws[i] = w[i] * sv[i];
@@ -279,14 +285,13 @@ __device__ __forceinline__ void softmax_step(const Cta c, int t0, int n, float s
 // ---- step 5 epilogue: this thread's value-numerator dim (slice s = warp / 4,
 // TMEM lane L = 32 (warp % 4) + lane, dim position unperm(L)) for all heads
 template <bool REC_TILE>
-__device__ __forceinline__ void value_epilogue(const Cta c, const uint8_t *vrec0,
-                                               const uint8_t *vrec1, float (&acc)[8]) {
+__device__ __forceinline__ void value_epilogue(const Cta c, float (&acc)[8]) {
     const int s = c.warp >> 2, L = 32 * (c.warp & 3) + c.lane;
     const uint32_t ta = c.tmem + ((uint32_t)(32 * (c.warp & 3)) << 16) + 64 + 32 * s;
     if (REC_TILE) {
         float d[32];
         tc::tmem_ld32(ta, d);
-        const float o = h2f((s ? vrec1 : vrec0) + NIB + 512 + 2 * unperm(L));
+        const float o = h2f(c.sm + SM_AX + (2 + s) * 768 + 512 + 2 * unperm(L));
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             const float val = fmaf(combine(d[q], d[8 + q], d[16 + q]), c.vec[(V_EW + s) * 8 + q],
@@ -305,8 +310,7 @@ __device__ __forceinline__ void value_epilogue(const Cta c, const uint8_t *vrec0
 // ---- step 2 epilogue: this thread's token (slice s, TMEM lane L, token
 // position pos(L)) partial scores for all heads into ps[s][q][token]
 template <bool REC_TILE>
-__device__ __forceinline__ void score_epilogue(const Cta c, const uint8_t *krec0,
-                                               const uint8_t *krec1) {
+__device__ __forceinline__ void score_epilogue(const Cta c) {
     const int s = c.warp >> 2, L = 32 * (c.warp & 3) + c.lane;
     const uint32_t ta = c.tmem + ((uint32_t)(32 * (c.warp & 3)) << 16) + 32 * s;
     const int tok = REC_TILE ? unperm(L) : L;
@@ -314,7 +318,7 @@ __device__ __forceinline__ void score_epilogue(const Cta c, const uint8_t *krec0
     if (REC_TILE) {
         float d[32];
         tc::tmem_ld32(ta, d);
-        const float o = h2f((s ? krec1 : krec0) + NIB + 512 + 2 * tok);
+        const float o = h2f(c.sm + SM_AX + s * 768 + 512 + 2 * tok);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
             ps[q * PLD] = o * fmaf(combine(d[q], d[8 + q], d[16 + q]), c.vec[(V_EQ + s) * 8 + q],
@@ -336,34 +340,66 @@ __device__ __forceinline__ bool wait_mma(const Cta c, uint32_t bar, uint32_t &ph
     return ok;
 }
 
-// One record group (records of slice 0 / 1 at krec0 / krec1, vrec0 / vrec1 in
-// global memory), rows [t0, t0 + n) of it.  Returns false if an MMA wait ran
-// out (CTA-uniform).
-__device__ __forceinline__ bool record_tile(const Cta c, const uint8_t *krec0,
-                                            const uint8_t *krec1, const uint8_t *vrec0,
-                                            const uint8_t *vrec1, int t0, int n, float scale,
-                                            uint32_t &ph_s, uint32_t &ph_v, float (&acc)[8]) {
-    // the V records' 4-bit values, in flight while the scores run
-    uint4 vw[4];
+// Raw 4-bit rows of the K (A0) or V (A1) records of a group, waited for and
+// read into registers: thread chunks i = tid + 256 j -> slice i / 512, row
+// (i / 4) % 128, 16-byte chunk i % 4, at the upper half of the slice's slot.
+__device__ __forceinline__ bool fetch_raw(const Cta c, int region, uint32_t bar, uint32_t &phase,
+                                          uint4 (&w)[4]) {
+    const bool ok = tc::mbar_wait(bar, phase, c.zero);
+    phase ^= 1u;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int i = c.tid + NT * j, s = i >> 9, r = (i >> 2) & 127, c4 = i & 3;
-        vw[j] = ldg128((s ? vrec1 : vrec0) + r * 64 + c4 * 16);
+        w[j] = *reinterpret_cast<const uint4 *>(c.sm + region + s * 16384 + 8192 + r * 64 + c4 * 16);
     }
+    return ok;
+}
+// One thread: bulk copies of group grp's K (or V) records of KV head kv: the
+// 4-bit rows to the upper halves of the slots, the axes to the axes area.
+__device__ __forceinline__ void issue_raw(const Cta c, const Kvarn4Args &a, bool value, int grp,
+                                          int kv) {
+    const uint8_t *plane = value ? a.v : a.k;
+    const uint32_t bar = value ? c.bar_rv : c.bar_rk;
+    const int64_t r = ((int64_t)grp * a.n_head_kv + kv) * 2 * REC;
+    tc::fence_async_smem(); // earlier generic reads of these bytes come first
+    tc::mbar_expect_tx(bar, 2 * REC);
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        tc::bulk_load(smem_u32(c.sm + (value ? SM_A1 : SM_A0) + s * 16384 + 8192),
+                      plane + r + s * REC, NIB, bar);
+        tc::bulk_load(smem_u32(c.sm + SM_AX + ((value ? 2 : 0) + s) * 768), plane + r + s * REC + NIB,
+                      768, bar);
+    }
+}
+
+// Per-CTA pipeline state: MMA and copy barrier phases, copies in flight
+struct Pipe {
+    uint32_t ph_s, ph_v, ph_rk, ph_rv;
+    bool rk_pend, rv_pend;
+};
+
+// One record group, rows [t0, t0 + n) of it; its raw K rows are in kw, its V
+// rows and all axes landed (or land) in shared memory.  When next >= 0 the
+// next record group's K is requested once the score MMAs are done and read
+// into kw at the end, and its V requested after the final barrier.  Returns
+// false if a wait ran out (CTA-uniform).
+__device__ __forceinline__ bool record_tile(const Cta c, const Kvarn4Args &a, uint4 (&kw)[4],
+                                            int t0, int n, int next, int kv, Pipe &pp,
+                                            float (&acc)[8]) {
     // 1. K widened into A0 (slice s at 16 KB s); the query operand
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int i = c.tid + NT * j, s = i >> 9, r = (i >> 2) & 127, c4 = i & 3;
-        widen(c.sm + SM_A0 + s * 16384, r, c4, ldg128((s ? krec1 : krec0) + r * 64 + c4 * 16));
+        widen(c.sm + SM_A0 + s * 16384, r, c4, kw[j]);
     }
     {
         // thread (slice s, head q, dims 8 ch .. 8 ch + 7); the 16 threads of a
         // (s, q) are one half-warp
         const int s = c.tid >> 7, q = (c.tid >> 4) & 7, ch = c.tid & 15;
-        const uint8_t *kr = s ? krec1 : krec0;
+        const uint8_t *kax = c.sm + SM_AX + s * 768;
         float sk[8], zk[8];
-        h8(kr + NIB + 16 * ch, sk);
-        h8(kr + NIB + 256 + 16 * ch, zk);
+        h8(kax + 16 * ch, sk);
+        h8(kax + 256 + 16 * ch, zk);
         const float *qr = c.qv + q * QLD + 128 * s + 8 * ch;
         const float4 qa = *reinterpret_cast<const float4 *>(qr);
         const float4 qb = *reinterpret_cast<const float4 *>(qr + 4);
@@ -415,19 +451,28 @@ __device__ __forceinline__ bool record_tile(const Cta c, const uint8_t *krec0,
             }
         tc::mma_commit(c.bar_s);
     }
-    // 3. V widened into A1 (free: the previous tile's value MMAs are done)
+    // 3. the V rows into registers (widened after the next barrier)
+    uint4 vw[4];
+    bool ok = fetch_raw(c, SM_A1, c.bar_rv, pp.ph_rv, vw);
+    pp.rv_pend = false;
+    ok &= wait_mma(c, c.bar_s, pp.ph_s);
+    score_epilogue<true>(c);
+    tc::tc_fence_before();
+    if (__syncthreads_or(!ok))
+        return false;
+    if (next >= 0) {
+        // A0 and the K axes are free: the score MMAs are done, the epilogue read
+        if (c.tid == 0)
+            issue_raw(c, a, false, next, kv);
+        pp.rk_pend = true;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const int i = c.tid + NT * j, s = i >> 9, r = (i >> 2) & 127, c4 = i & 3;
         widen(c.sm + SM_A1 + s * 16384, r, c4, vw[j]);
     }
-    bool ok = wait_mma(c, c.bar_s, ph_s);
-    score_epilogue<true>(c, krec0, krec1);
-    tc::tc_fence_before();
-    if (__syncthreads_or(!ok))
-        return false;
     // 4. softmax step, weight operand
-    softmax_step<true>(c, t0, n, scale, vrec0, vrec1);
+    softmax_step<true>(c, t0, n, a.scale);
     tc::fence_async_smem();
     tc::tc_fence_before();
     __syncthreads();
@@ -446,10 +491,22 @@ __device__ __forceinline__ bool record_tile(const Cta c, const uint8_t *krec0,
             }
         tc::mma_commit(c.bar_v);
     }
-    ok = wait_mma(c, c.bar_v, ph_v);
-    value_epilogue<true>(c, vrec0, vrec1, acc);
+    ok = wait_mma(c, c.bar_v, pp.ph_v);
+    value_epilogue<true>(c, acc);
+    if (next >= 0) {
+        ok &= fetch_raw(c, SM_A0, c.bar_rk, pp.ph_rk, kw);
+        pp.rk_pend = false;
+    }
     tc::tc_fence_before();
-    return __syncthreads_or(!ok) == 0;
+    if (__syncthreads_or(!ok))
+        return false;
+    if (next >= 0) {
+        // A1 and the V axes are free: the value MMAs are done, the epilogue read
+        if (c.tid == 0)
+            issue_raw(c, a, true, next, kv);
+        pp.rv_pend = true;
+    }
+    return true;
 }
 
 // Stage n <= 128 F16 rows (row stride row_bytes, this head's 256 values at
@@ -483,8 +540,8 @@ __device__ __forceinline__ void stage_f16(const Cta c, const uint8_t *rows, int6
 // n <= 128 F16 rows: stage rows of a body split (rotated, meet WHT(q)) or
 // tail rows of the tail split (original, meet q); qv holds the right one.
 __device__ __forceinline__ bool f16_tile(const Cta c, const uint8_t *krows, const uint8_t *vrows,
-                                         int64_t row_bytes, int n, float scale, uint32_t &ph_s,
-                                         uint32_t &ph_v, float (&acc)[8]) {
+                                         int64_t row_bytes, int n, float scale, Pipe &pp,
+                                         float (&acc)[8]) {
     stage_f16<false>(c, krows, row_bytes, n);
     {
         // query operand: rows q (f16 of qv) and 8 + q (remainder); thread
@@ -519,13 +576,13 @@ __device__ __forceinline__ bool f16_tile(const Cta c, const uint8_t *krows, cons
             }
         tc::mma_commit(c.bar_s);
     }
-    bool ok = wait_mma(c, c.bar_s, ph_s);
-    score_epilogue<false>(c, nullptr, nullptr);
+    bool ok = wait_mma(c, c.bar_s, pp.ph_s);
+    score_epilogue<false>(c);
     tc::tc_fence_before();
     if (__syncthreads_or(!ok))
         return false;
     stage_f16<true>(c, vrows, row_bytes, n); // A0 / A1 free: the score MMAs are done
-    softmax_step<false>(c, 0, n, scale, nullptr, nullptr);
+    softmax_step<false>(c, 0, n, scale);
     tc::fence_async_smem();
     tc::tc_fence_before();
     __syncthreads();
@@ -543,8 +600,8 @@ __device__ __forceinline__ bool f16_tile(const Cta c, const uint8_t *krows, cons
             }
         tc::mma_commit(c.bar_v);
     }
-    ok = wait_mma(c, c.bar_v, ph_v);
-    value_epilogue<false>(c, nullptr, nullptr, acc);
+    ok = wait_mma(c, c.bar_v, pp.ph_v);
+    value_epilogue<false>(c, acc);
     tc::tc_fence_before();
     return __syncthreads_or(!ok) == 0;
 }
@@ -574,15 +631,6 @@ __device__ __forceinline__ void wht_regs(float (&v)[8], int lane) {
         v[i] *= 0.0625f;
 }
 
-// L2 prefetch of a record group's four records (K and V, both slices: two
-// contiguous 17,920-byte runs)
-__device__ __forceinline__ void prefetch_group(const Kvarn4Args &a, int grp, int kv) {
-    const int64_t r = ((int64_t)grp * a.n_head_kv + kv) * 2 * REC;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.k + r), "r"(2 * REC)
-                 : "memory");
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.v + r), "r"(2 * REC)
-                 : "memory");
-}
 } // namespace k4
 
 __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4Args a) {
@@ -597,8 +645,10 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     c.vec = reinterpret_cast<float *>(sm + SM_VEC);
     c.bar_s = smem_u32(sm + SM_BAR);
     c.bar_v = c.bar_s + 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + SM_BAR + 16);
-    c.zero = reinterpret_cast<volatile int *>(sm + SM_BAR + 20);
+    c.bar_rk = c.bar_s + 16;
+    c.bar_rv = c.bar_s + 24;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + SM_BAR + 32);
+    c.zero = reinterpret_cast<volatile int *>(sm + SM_BAR + 36);
     c.tid = threadIdx.x;
     c.warp = c.tid >> 5;
     c.lane = c.tid & 31;
@@ -620,14 +670,23 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     const int g0 = r0 / GROUP, g1 = (!tail_split && r1 > r0) ? (r1 + GROUP - 1) / GROUP : g0;
     auto record_group = [=](int grp) { return og + grp != 0 && !(grp == live && live_partial); };
 
+    // the next record group after grp, if the tile after grp is one (else -1)
+    auto next_record = [=](int grp) { return grp + 1 < g1 && record_group(grp + 1) ? grp + 1 : -1; };
+    Pipe pp = {0u, 0u, 0u, 0u, false, false};
+    const bool first_rec = g0 < g1 && record_group(g0);
     if (c.tid == 0) {
         tc::mbar_init(c.bar_s, 1);
         tc::mbar_init(c.bar_v, 1);
+        tc::mbar_init(c.bar_rk, 1);
+        tc::mbar_init(c.bar_rv, 1);
         *c.zero = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        if (g0 < g1 && record_group(g0))
-            prefetch_group(a, g0, kv);
+        if (first_rec) {
+            issue_raw(c, a, false, g0, kv);
+            issue_raw(c, a, true, g0, kv);
+        }
     }
+    pp.rk_pend = pp.rv_pend = first_rec;
     if (c.warp == 0)
         tc::tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
     {
@@ -660,7 +719,8 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     c.tmem = *tmem_slot;
 
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    uint32_t ph_s = 0, ph_v = 0;
+    uint4 kw[4];          // raw K rows of the coming record group
+    bool have_kw = false; // kw holds them (read at the end of the previous record tile)
     bool ok = true;
     if (tail_split) {
         // the tail buffer is a ring of 128 rows: row r at r % 128
@@ -668,38 +728,51 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
             const int n = min(r1 - rr, GROUP - rr % GROUP);
             const int64_t first = (int64_t)(rr % GROUP) * row_bytes + kv * 512;
             ok = f16_tile(c, a.k + a.tail_off + first, a.v + a.tail_off + first, row_bytes, n,
-                          a.scale, ph_s, ph_v, acc);
+                          a.scale, pp, acc);
             rr += n;
         }
     } else {
         for (int grp = g0; grp < g1 && ok; ++grp) {
             const int lo = max(r0, grp * GROUP), hi = min(r1, (grp + 1) * GROUP);
-            if (c.tid == 0) {
-                int nxt = grp + 1;
-                while (nxt < g1 && !record_group(nxt))
-                    ++nxt;
-                if (nxt < g1)
-                    prefetch_group(a, nxt, kv);
-            }
+            const int next = next_record(grp);
             if (!record_group(grp)) {
                 // staged group: rotated F16 rows in its stage slot
                 const int slot = og + grp == 0 ? 0 : 1 + ((og + grp - 1) & 1);
                 const int64_t first =
                     ((int64_t)slot * GROUP + (lo - grp * GROUP)) * row_bytes + kv * 512;
                 ok = f16_tile(c, a.k + a.stage_off + first, a.v + a.stage_off + first,
-                              row_bytes, hi - lo, a.scale, ph_s, ph_v, acc);
+                              row_bytes, hi - lo, a.scale, pp, acc);
+                if (ok && next >= 0) {
+                    // A0, A1 and the axes are free again after the tile's last barrier
+                    if (c.tid == 0) {
+                        issue_raw(c, a, false, next, kv);
+                        issue_raw(c, a, true, next, kv);
+                    }
+                    pp.rk_pend = pp.rv_pend = true;
+                }
+                have_kw = false;
             } else {
-                const int64_t rk = ((int64_t)grp * a.n_head_kv + kv) * 2 * REC;
-                ok = record_tile(c, a.k + rk, a.k + rk + REC, a.v + rk, a.v + rk + REC,
-                                 lo - grp * GROUP, hi - lo, a.scale, ph_s, ph_v, acc);
+                if (!have_kw) {
+                    ok = fetch_raw(c, SM_A0, c.bar_rk, pp.ph_rk, kw);
+                    pp.rk_pend = false;
+                    if (__syncthreads_or(!ok)) // every raw read is done before the widening
+                        break;
+                }
+                ok = record_tile(c, a, kw, lo - grp * GROUP, hi - lo, next, kv, pp, acc);
+                have_kw = next >= 0;
             }
         }
     }
     if (!ok && c.tid == 0) {
-        // give the MMAs still in flight a bounded time to finish before TMEM goes
-        // (parity of each barrier's last expected phase: immediate if it completed)
-        tc::mbar_wait(c.bar_s, ph_s ^ 1u, c.zero, 100000000ull);
-        tc::mbar_wait(c.bar_v, ph_v ^ 1u, c.zero, 100000000ull);
+        // give the MMAs and copies still in flight a bounded time to finish
+        // before TMEM and shared memory go (MMA barriers: parity of the last
+        // expected phase, immediate if it completed)
+        tc::mbar_wait(c.bar_s, pp.ph_s ^ 1u, c.zero, 100000000ull);
+        tc::mbar_wait(c.bar_v, pp.ph_v ^ 1u, c.zero, 100000000ull);
+        if (pp.rk_pend)
+            tc::mbar_wait(c.bar_rk, pp.ph_rk, c.zero, 100000000ull);
+        if (pp.rv_pend)
+            tc::mbar_wait(c.bar_rv, pp.ph_rv, c.zero, 100000000ull);
     }
     tc::tc_fence_before();
     __syncthreads();
