@@ -636,8 +636,10 @@ __device__ __forceinline__ void wht_regs(float (&v)[8], int lane) {
 __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4Args a) {
     using namespace k4;
     extern __shared__ __align__(1024) uint8_t sm_raw[];
-    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) &
-                                              ~uintptr_t(1023));
+    // aligned by an offset on the shared array itself, so that every access
+    // through sm stays a shared-memory access (a round trip through an integer
+    // would leave the compiler only generic addresses)
+    uint8_t *sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
     Cta c;
     c.sm = sm;
     c.qv = reinterpret_cast<float *>(sm + SM_QV);
