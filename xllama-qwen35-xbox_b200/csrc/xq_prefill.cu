@@ -82,8 +82,11 @@ __global__ void __launch_bounds__(pf::NT, 1)
     static_assert(D == 128 || D == 256, "head dim");
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned by an offset on the shared array (accesses stay
+    // shared-memory accesses; an integer round trip leaves generic addresses)
+    uint8_t *smem =
+        smem_raw + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) &
+                    1023u);
     uint8_t *ring = smem;
     uint64_t *bars = reinterpret_cast<uint64_t *>(ring + NSLOT * TBYTES);
     // bars: full[NSLOT], empty[NSLOT], s_full[2], p_full[2], o_done, drain, q_ready
