@@ -657,25 +657,19 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
     c.G = a.n_head / a.n_head_kv;
     const int split = blockIdx.x, kv = blockIdx.y, tok = blockIdx.z;
     const int64_t row_bytes = (int64_t)a.n_head_kv * 512;
-
-    const int pos = a.positions[tok];
-    const int limit = pos < a.origin ? 0 : min(a.active, pos - a.origin + 1);
-    const int tail_begin = a.active - min(a.active, a.tail);
-    const bool tail_split = split >= a.n_body; // rows [tail_begin, active), original domain
-    const int r0 = tail_split ? tail_begin : split * a.rows_per_split;
-    const int r1 = tail_split ? limit : min(min(r0 + a.rows_per_split, tail_begin), limit);
     const int live = a.active ? (a.active - 1) / GROUP : 0;
     const bool live_partial = (a.active % GROUP) != 0;
     const int og = a.origin / GROUP;
     // a body group is read from its records unless it is the global sink group
     // or the incomplete live group (stage rows)
-    const int g0 = r0 / GROUP, g1 = (!tail_split && r1 > r0) ? (r1 + GROUP - 1) / GROUP : g0;
     auto record_group = [=](int grp) { return og + grp != 0 && !(grp == live && live_partial); };
 
-    // the next record group after grp, if the tile after grp is one (else -1)
-    auto next_record = [=](int grp) { return grp + 1 < g1 && record_group(grp + 1) ? grp + 1 : -1; };
-    Pipe pp = {0u, 0u, 0u, 0u, false, false};
-    const bool first_rec = g0 < g1 && record_group(g0);
+    // Launched as a programmatic dependent: until griddepcontrol.wait the
+    // kernel before this one may still be writing q, the positions or the
+    // planes, and reading the partials this kernel writes, so only set-up and
+    // an L2 prefetch of the split's first group (no data consumed) come first.
+    // The merge after this kernel may launch at once; it waits for this grid.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     if (c.tid == 0) {
         tc::mbar_init(c.bar_s, 1);
         tc::mbar_init(c.bar_v, 1);
@@ -683,14 +677,36 @@ __global__ void __launch_bounds__(k4::NT, 2) kvarn4_partials_kernel(const Kvarn4
         tc::mbar_init(c.bar_rv, 1);
         *c.zero = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        if (first_rec) {
-            issue_raw(c, a, false, g0, kv);
-            issue_raw(c, a, true, g0, kv);
+        const int gp = split * a.rows_per_split / GROUP;
+        if (split < a.n_body && record_group(gp)) {
+            const int64_t r = ((int64_t)gp * a.n_head_kv + kv) * 2 * REC;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.k + r), "r"(2 * REC)
+                         : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a.v + r), "r"(2 * REC)
+                         : "memory");
         }
     }
-    pp.rk_pend = pp.rv_pend = first_rec;
     if (c.warp == 0)
         tc::tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+
+    const int pos = a.positions[tok];
+    const int limit = pos < a.origin ? 0 : min(a.active, pos - a.origin + 1);
+    const int tail_begin = a.active - min(a.active, a.tail);
+    const bool tail_split = split >= a.n_body; // rows [tail_begin, active), original domain
+    const int r0 = tail_split ? tail_begin : split * a.rows_per_split;
+    const int r1 = tail_split ? limit : min(min(r0 + a.rows_per_split, tail_begin), limit);
+    const int g0 = r0 / GROUP, g1 = (!tail_split && r1 > r0) ? (r1 + GROUP - 1) / GROUP : g0;
+
+    // the next record group after grp, if the tile after grp is one (else -1)
+    auto next_record = [=](int grp) { return grp + 1 < g1 && record_group(grp + 1) ? grp + 1 : -1; };
+    Pipe pp = {0u, 0u, 0u, 0u, false, false};
+    const bool first_rec = g0 < g1 && record_group(g0);
+    if (c.tid == 0 && first_rec) {
+        issue_raw(c, a, false, g0, kv);
+        issue_raw(c, a, true, g0, kv);
+    }
+    pp.rk_pend = pp.rv_pend = first_rec;
     {
         // query head g = warp: q or WHT(q) rows; running max / denominator
         const int g = c.warp;
@@ -836,9 +852,19 @@ cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st) {
     cudaError_t e = set_smem_limit((const void *)kvarn4_partials_kernel, k4::SM_BYTES, attr);
     if (e != cudaSuccess)
         return e;
-    dim3 grid((unsigned)l.n_splits, (unsigned)l.n_head_kv, (unsigned)l.n_tokens);
-    kvarn4_partials_kernel<<<grid, k4::NT, k4::SM_BYTES, st>>>(a);
-    return cudaGetLastError();
+    // programmatic dependent of the previous kernel on the stream (see the
+    // kernel's griddepcontrol.wait)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)l.n_splits, (unsigned)l.n_head_kv, (unsigned)l.n_tokens);
+    cfg.blockDim = dim3(k4::NT, 1, 1);
+    cfg.dynamicSmemBytes = k4::SM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kvarn4_partials_kernel, a);
 }
 
 } // namespace xq
