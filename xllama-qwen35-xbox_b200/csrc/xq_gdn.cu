@@ -34,6 +34,20 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
 
     const char *st_row = reinterpret_cast<const char *>(a.state) + seq * a.s_nb3 +
                          (int64_t)h * a.s_nb2 + (int64_t)col * a.s_nb1;
+    // Launched as a programmatic dependent: the next kernel may launch now (it
+    // waits for this grid before it reads what this one writes); until
+    // griddepcontrol.wait the kernel before this one may still be writing the
+    // state and the token inputs, so only an L2 prefetch of this CTA's state
+    // rows (contiguous, no data consumed) comes first.
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    if (threadIdx.x == 0) {
+        const char *rows = st_row - (int64_t)(threadIdx.x / TPC) * a.s_nb1;
+        if (a.s_nb1 == 4 * S && ((reinterpret_cast<uintptr_t>(rows)) & 15) == 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(rows),
+                         "r"((uint32_t)(CB * 4 * S))
+                         : "memory");
+    }
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
     float st[EPT];
 #pragma unroll
     for (int e = 0; e < EPT; ++e)
@@ -274,9 +288,20 @@ cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st) {
                       15) == 0;
     // a few tokens (decode, speculative verify): the reference mirror's exact
     // lane order; longer sequences: the staged, packed-FMA stream kernel
-    if (a.T <= 8)
-        gdn_recurrent_kernel<S, CB><<<grid, CB * 8, 0, st>>>(a);
-    else {
+    if (a.T <= 8) {
+        // programmatic dependent of the previous kernel on the stream (see the
+        // kernel's griddepcontrol.wait)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(CB * 8, 1, 1);
+        cfg.stream = st;
+        cudaLaunchAttribute pdl[1];
+        pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pdl[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = pdl;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, gdn_recurrent_kernel<S, CB>, a);
+    } else {
         // 8 lanes per value column, 16 columns per CTA (16 lanes per column
         // measured slower: the extra shuffle level outweighs the extra warps)
         constexpr int SC = 16, TPC = 8;
