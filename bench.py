@@ -298,6 +298,14 @@ def run_ours(args, rank, world, torch, dist):
             o_host.view(-1).copy_(out.view(-1), non_blocking=True)
     e2e_ms = timed(e2e_step, args.steps) / args.steps
 
+    # the N = 1 point of the config-5 series, measured in the same run: the
+    # default N = 1 line is config 2, so a scaling series read across the
+    # default lines would mix workloads
+    ref1 = None
+    if workload == "c5" and world > 1:
+        if rank == 0:
+            ref1 = c5_single_gpu(torch, xq, dev, ty, args.steps, args.warmup, step_bytes)
+        dist.barrier()
     if rank != 0:
         return None
     value = step_bytes / (ms * 1e-3) / 1e9
@@ -336,11 +344,42 @@ def run_ours(args, rank, world, torch, dist):
                 "h2d_bytes_per_step": int(q_host.numel() * 4),
                 "d2h_bytes_per_step": int(o_host.numel() * 4)},
         "gpu_launches": args.steps * (3 if workload == "c5" else 2),
+        **({"scaling_reference": ref1} if ref1 else {}),
         "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps if use_graph
                   else "eager launches, CUDA events",
         "clocks": clocks,
     }
     return line
+
+
+def c5_single_gpu(torch, xq, dev, ty, steps, warmup, step_bytes):
+    """Config 5 on one GPU (all 256 splits, the 8 group merges, the final
+    merge; no collective): the N = 1 point of the KV-sharded series."""
+    w = C5
+    n_splits, rows_per_split, per_group = w["n_kv"] // 1024, 1024, 32
+    k = make_kv(torch, xq, w, ty, w["n_kv"], 1000, dev)
+    v = make_kv(torch, xq, w, ty, w["n_kv"], 2000, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    q = torch.randn((w["n_seq"], w["n_head"], 1, w["D"]), generator=g, device=dev)
+    rows = w["n_seq"] * w["n_head"]
+    part = torch.empty((n_splits, rows, w["D"] + 2), dtype=torch.float32, device=dev)
+    rec = torch.empty((n_splits // per_group, rows, w["D"] + 2), dtype=torch.float32, device=dev)
+    out = torch.empty((rows, w["D"]), dtype=torch.float32, device=dev)
+    scale = 1.0 / math.sqrt(w["D"])
+
+    def step(i):
+        xq.fa_partials(q, k, v, ty, rows_per_split, 0, n_splits, scale=scale, out=part)
+        xq.lse_merge_records(part, per_group, out=rec)
+        xq.lse_merge(rec, out=out, want_lse=False)
+
+    ms = graph_timed(torch, step, steps, warmup) / steps
+    del k, v
+    return {"n_gpus": 1, "workload": "BASELINE config 5 on one GPU (no collective)",
+            "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 5),
+            "note": "the N = 1 point of this strong-scaling series (the default N = 1 line "
+                    "is BASELINE config 2)"}
 
 
 def cpu_oracle_sample(workload, seconds_cap=20.0, sample_kv=None):
