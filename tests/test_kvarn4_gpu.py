@@ -58,6 +58,9 @@ CASES = [
     (0, 1024, 128, 777, 16, 2, [776, 700]),       # G = 8
     (128, 8192, 128, 8100, 24, 4, [8099]),        # many splits
     (0, 512, 128, 0, 24, 4, [5]),                 # empty range
+    (0, 1024, 0, 700, 24, 4, [699, 300]),         # sink stage, records, live stage group
+    (256, 768, 128, 700, 4, 4, [699, 500]),       # G = 1
+    (0, 640, 128, 450, 12, 4, [449, 130]),        # G = 3, tail across the ring's end
 ]
 
 
