@@ -182,7 +182,11 @@ uint32_t xq_split_k(uint32_t active, uint32_t mode);
 /* numerator is rotated back.  Query t sees rows [0, min(active,           */
 /* positions[t] - origin + 1)).  q F32 [n_tokens][n_head][256] original     */
 /* domain; out F32 [n_tokens][n_head][256]; lse F32 [n_tokens][n_head]     */
-/* (natural log; empty => O = 0, LSE = -inf).  positions: device memory.   */
+/* (natural log; empty => O = 0, LSE = -inf; lse may be NULL).  q, out and */
+/* lse may be in device or pinned host memory (q is then staged into the   */
+/* workspace by a kernel, out / lse written over PCIe by the merge);       */
+/* pageable host memory => XQ_ERR_INVALID.  positions: device memory.      */
+/* The workspace holds the split partials and room to stage q.             */
 /* ------------------------------------------------------------------------ */
 typedef struct {
     int32_t origin;         /* global position of compact row 0, % 128 == 0 */

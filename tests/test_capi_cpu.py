@@ -116,13 +116,16 @@ def test_kvarn4_workspace_and_contract():
         d = XL.Kvarn4Desc(origin, cap, tail, n_kv)
         return L.xq_attend_range_kvarn4_workspace(C.byref(d), n_head, active, n_tok)
 
-    rec = 24 * 258 * 4
+    def size(splits, n_tok=1):
+        # split partials, then (256-byte aligned) room to stage a host q
+        return (splits * n_tok * 24 * 258 * 4 + 255) // 256 * 256 + n_tok * 24 * 256 * 4
+
     # 255 body groups: 73 splits wanted -> 4 groups each -> 64 body splits + tail
-    assert ws(102400, 32768, 128, 4, 24, 32768) == 65 * rec
-    assert ws(102400, 32768, 0, 4, 24, 32768) == 64 * rec      # no tail split
-    assert ws(0, 640, 128, 4, 24, 100) == 1 * rec              # everything in the tail
-    assert ws(0, 640, 128, 4, 24, 0) == 1 * rec                # empty: one split
-    assert ws(0, 640, 0, 4, 24, 520, n_tok=3) == 5 * 3 * rec   # one group per split
+    assert ws(102400, 32768, 128, 4, 24, 32768) == size(65)
+    assert ws(102400, 32768, 0, 4, 24, 32768) == size(64)      # no tail split
+    assert ws(0, 640, 128, 4, 24, 100) == size(1)              # everything in the tail
+    assert ws(0, 640, 128, 4, 24, 0) == size(1)                # empty: one split
+    assert ws(0, 640, 0, 4, 24, 520, n_tok=3) == size(5, 3)    # one group per split
     assert ws(0, 640, -1, 4, 24, 520) == 0
 
     d = XL.Kvarn4Desc(0, 1024, 128, 4)

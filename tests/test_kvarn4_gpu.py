@@ -76,3 +76,35 @@ def test_kvarn4_vs_oracle(case):
     out, lse = _run(desc, kp, vp, active, q, pos)
     ref_out, ref_lse = ok.attend(desc, kp, vp, active, q, pos, 1 / 16.0, n_head)
     _check(out, lse, ref_out, ref_lse)
+
+
+def test_kvarn4_pinned_host_buffers():
+    """q, out and lse in pinned host memory (q staged by the library, out / lse
+    written over PCIe by the merge) give the device-memory result bit for bit;
+    pageable host memory is refused."""
+    import ctypes as C
+    import xq
+    import xq._lib as XL
+    dev = torch.device("cuda", 0)
+    desc = ok.Desc(384, 640, 128, 4)
+    kp = torch.from_numpy(ok.make_plane(desc, 600, 31)).to(dev)
+    vp = torch.from_numpy(ok.make_plane(desc, 600, 32)).to(dev)
+    q = torch.from_numpy(np.random.default_rng(33).normal(0, 1, (2, 24, 256)).astype(np.float32))
+    pos = torch.tensor([384 + 599, 384 + 250], dtype=torch.int32, device=dev)
+    out_d, lse_d = xq.attend_range_kvarn4(kp, vp, q.to(dev), pos, 4, 384, 640, 128, 600, 0.0625)
+    q_h = q.pin_memory()
+    out_h = torch.empty((2, 24, 256), dtype=torch.float32).pin_memory()
+    lse_h = torch.empty((2, 24), dtype=torch.float32).pin_memory()
+    xq.attend_range_kvarn4(kp, vp, q_h, pos, 4, 384, 640, 128, 600, 0.0625, out=out_h, lse=lse_h)
+    torch.cuda.synchronize()
+    assert torch.equal(out_h, out_d.cpu()) and torch.equal(lse_h, lse_d.cpu())
+    # pageable q: refused before any launch
+    L = XL.lib()
+    d = XL.Kvarn4Desc(384, 640, 128, 4)
+    nbytes = L.xq_attend_range_kvarn4_workspace(C.byref(d), 24, 600, 2)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    q_pageable = q.clone()
+    rc = L.xq_attend_range_kvarn4(C.byref(d), kp.data_ptr(), vp.data_ptr(), 24, 600, 2,
+                                  pos.data_ptr(), q_pageable.data_ptr(), 0.0625,
+                                  out_d.data_ptr(), lse_d.data_ptr(), ws.data_ptr(), nbytes, None)
+    assert rc == XL.XQ_ERR_INVALID and b"pageable" in L.xq_last_error()

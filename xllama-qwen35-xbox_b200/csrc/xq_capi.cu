@@ -561,13 +561,19 @@ static Kvarn4Plan kvarn4_plan(uint32_t active, uint32_t tail, uint32_t n_head_kv
     return pl;
 }
 
+// Workspace: the split partials, then (256-byte aligned) room for q when the
+// caller's q is in pinned host memory and is staged to the device first.
+static size_t kvarn4_q_offset(const Kvarn4Plan &pl, uint32_t n_head, uint32_t n_tokens) {
+    return ((size_t)pl.n_splits * n_tokens * n_head * 258 * sizeof(float) + 255) / 256 * 256;
+}
+
 size_t xq_attend_range_kvarn4_workspace(const xq_kvarn4_desc *d, uint32_t n_head,
                                         uint32_t active, uint32_t n_tokens) {
     if (!d || d->n_head_kv <= 0 || !n_tokens || d->precision_tail < 0)
         return 0;
     const Kvarn4Plan pl =
         kvarn4_plan(active, (uint32_t)d->precision_tail, (uint32_t)d->n_head_kv, n_tokens);
-    return (size_t)pl.n_splits * n_tokens * n_head * 258 * sizeof(float);
+    return kvarn4_q_offset(pl, n_head, n_tokens) + (size_t)n_tokens * n_head * 256 * sizeof(float);
 }
 
 int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const void *v_plane,
@@ -590,10 +596,36 @@ int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const v
     const Kvarn4Plan pl =
         kvarn4_plan(active, (uint32_t)d->precision_tail, (uint32_t)d->n_head_kv, n_tokens);
     const int64_t s = pl.n_splits;
-    const size_t need = (size_t)s * n_tokens * n_head * 258 * sizeof(float);
+    const size_t q_off = kvarn4_q_offset(pl, n_head, n_tokens);
+    const size_t need = q_off + (size_t)n_tokens * n_head * 256 * sizeof(float);
     if (!ws || ws_bytes < need)
         return fail(XQ_ERR_WORKSPACE, "attend_range_kvarn4: workspace %zu < %zu bytes", ws_bytes,
                     need);
+    // q, out and lse may be in pinned host memory: q is staged into the
+    // workspace by a kernel, out / lse are written through their device view
+    HostView hq, ho, hl;
+    const int kq = host_view(q, &hq), ko = host_view(out, &ho), kl = host_view(lse, &hl);
+    if (kq < 0 || ko < 0 || kl < 0)
+        return fail(XQ_ERR_INVALID,
+                    "attend_range_kvarn4: q / out / lse in pageable host memory (pin them or use "
+                    "the device)");
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (kq == 1) {
+        float *staged = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + q_off);
+        xq_tensor qt = {};
+        qt.type = XQ_TYPE_F32;
+        qt.ne[0] = 256, qt.ne[1] = n_head, qt.ne[2] = n_tokens, qt.ne[3] = 1;
+        qt.nb[0] = 4, qt.nb[1] = 1024, qt.nb[2] = 1024 * (int64_t)n_head;
+        qt.nb[3] = qt.nb[2] * n_tokens;
+        const int rc = stage_q(qt, hq.dev, staged, st);
+        if (rc)
+            return rc;
+        q = staged;
+    }
+    if (ko == 1)
+        out = static_cast<float *>(ho.dev);
+    if (kl == 1)
+        lse = static_cast<float *>(hl.dev);
     xq::Kvarn4Launch l;
     l.k = static_cast<const uint8_t *>(k_plane);
     l.v = static_cast<const uint8_t *>(v_plane);
@@ -611,7 +643,6 @@ int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const v
     l.n_body = pl.n_body;
     l.n_splits = pl.n_splits;
     l.scale = kq_scale;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     int rc = cuda_status(xq::launch_kvarn4(l, st), "attend_range_kvarn4 partials");
     if (rc)
         return rc;

@@ -231,18 +231,24 @@ def attend_range(storage: int, k: torch.Tensor, v: torch.Tensor, q: torch.Tensor
 
 def attend_range_kvarn4(k_plane: torch.Tensor, v_plane: torch.Tensor, q: torch.Tensor,
                         positions: torch.Tensor, n_head_kv: int, origin: int, capacity: int,
-                        precision_tail: int, active: int, kq_scale: float, stream=None):
+                        precision_tail: int, active: int, kq_scale: float, stream=None,
+                        out=None, lse=None):
     """RKVA range attention over native KVarN4 planes (uint8, 16-byte aligned,
-    layout in include/xq_b200.h); q float32 (n_tokens, n_head, 256),
-    positions int32 (n_tokens,) on the device.  Returns (out, lse)."""
+    layout in include/xq_b200.h); q float32 (n_tokens, n_head, 256) on the
+    device or in pinned host memory, positions int32 (n_tokens,) on the
+    device; out / lse, when given, may be pinned host tensors too.  Returns
+    (out, lse)."""
     from ._lib import Kvarn4Desc
     n_tokens, n_head, D = q.shape
     assert D == 256 and q.is_contiguous() and positions.dtype == torch.int32
+    dev = k_plane.device
     desc = Kvarn4Desc(origin, capacity, precision_tail, n_head_kv)
-    out = torch.empty((n_tokens, n_head, D), dtype=torch.float32, device=q.device)
-    lse = torch.empty((n_tokens, n_head), dtype=torch.float32, device=q.device)
+    if out is None:
+        out = torch.empty((n_tokens, n_head, D), dtype=torch.float32, device=dev)
+    if lse is None:
+        lse = torch.empty((n_tokens, n_head), dtype=torch.float32, device=dev)
     nbytes = lib().xq_attend_range_kvarn4_workspace(C.byref(desc), n_head, active, n_tokens)
-    ws = _workspace(nbytes, q.device)
+    ws = _workspace(nbytes, dev)
     check(lib().xq_attend_range_kvarn4(C.byref(desc), k_plane.data_ptr(), v_plane.data_ptr(),
                                        n_head, active, n_tokens, positions.data_ptr(),
                                        q.data_ptr(), kq_scale, out.data_ptr(), lse.data_ptr(),
