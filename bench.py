@@ -2,7 +2,7 @@
 """Benchmark of the B200 attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c5|kvw]
+                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c5|kvw|kv4]
 
 Workloads (seeded synthetic tensors, random data of the
 stated distributions -- no datasets are involved):
@@ -20,12 +20,18 @@ stated distributions -- no datasets are involved):
   kvw  KV-cache write (GGML_OP_SET_ROWS, the row after the hot path): a
        prefill batch of 8192 tokens x 4 KV heads x D=256, K and V, quantized
        to Q8_0 into 32768-row caches (4 rotated input sets > 2 x L2).
+  kv4  native KVarN4 range attention (the RKVA server's resident image):
+       24 Q / 4 KV heads, D=256, 32768 rows past origin 102400 in 4-bit
+       records plus the 128-row F16 precision tail, one query (9 rotated
+       plane sets > 2 x L2).
   c5   config 5: 8 sequences x 262144 KV rows, 24 Q / 4 KV heads, D=256, Q8_0;
        the KV rows are cut into 256 fixed global splits in 8 fixed groups; each
        GPU holds and reads its contiguous block of groups, merges each group
        into one (O, lse) record, the group records are all-gathered over NCCL
        and merged in group order (bit-identical for any GPU count dividing 8).
-       Default for N > 1 ("strong" scaling: total work fixed).
+       Default for N > 1 ("strong" scaling: total work fixed); those lines
+       also carry `scaling_reference`, config 5 timed on one GPU in the same
+       run (the N = 1 point of the series).
 A step = the attention kernels of one decode step over that workload.
 `value` is KV GB/s (algorithmic bytes: K + V + q + out per step) with inputs
 resident; `e2e` is the same metric through the public call xq.flash_attn_ext
