@@ -18,7 +18,7 @@
 //
 // Two kernels:
 //   gdn_chunk_prep_kernel  one CTA per (chunk, head, sequence), all in
-//     parallel, 3 CTAs per SM: [K;Q] K^T on the tensor core (M=128, N=64,
+//     parallel (chunk-major order), 3 CTAs per SM: [K;Q] K^T on the tensor core (M=128, N=64,
 //     K=128), the gates, the unit lower-triangular inverse in FP32 (16x16
 //     diagonal blocks by forward substitution, then block rows; four lanes
 //     per column), and writes [T''; M] (128 x 64) plus b, e, b_C to the
@@ -193,7 +193,12 @@ __global__ void __launch_bounds__(gc::PREP_NT, 3)
     volatile int *abort_s = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int c = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
+    // blocks run chunk by chunk; inside a chunk the value heads that share a
+    // key head (h = hk + j H_k) are adjacent, so the second CTA's K/Q tiles
+    // come from L2
+    const int c = (int)(blockIdx.x / (unsigned)a.H), x = (int)(blockIdx.x % (unsigned)a.H);
+    const int J = a.H % a.H_k == 0 ? a.H / a.H_k : 1;
+    const int h = J > 1 ? (x % J) * a.H_k + x / J : x, n = blockIdx.z;
     const int hk = h % a.H_k, t0 = c * C;
     const size_t unit = ((size_t)n * a.H + h) * a.NC + c;
     const uint32_t bar_tma = smem_u32(bars), bar_mma = smem_u32(bars + 1);
@@ -949,7 +954,7 @@ cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cuda
         (e = set_smem_limit((const void *)gdn_chunk_scan_kernel, S_BYTES, scan_attr)) !=
             cudaSuccess)
         return e;
-    gdn_chunk_prep_kernel<<<dim3((unsigned)nc, (unsigned)a.H, (unsigned)a.n_seq), PREP_NT,
+    gdn_chunk_prep_kernel<<<dim3((unsigned)(nc * a.H), 1, (unsigned)a.n_seq), PREP_NT,
                             P_BYTES, st>>>(kmap, qmap, c);
     if ((e = cudaGetLastError()) != cudaSuccess)
         return e;
