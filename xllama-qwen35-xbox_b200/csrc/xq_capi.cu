@@ -244,17 +244,39 @@ size_t q_stage_bytes(const xq_tensor &q) {
     return (size_t)q.ne[0] * q.ne[1] * q.ne[2] * q.ne[3] * sizeof(float);
 }
 
-// Strided F32 [ne0, ne1, ne2, ne3] (ggml view, any byte strides) -> contiguous.
+// Strided F32 [ne0, ne1, ne2, ne3] (ggml view, any byte strides) -> contiguous,
+// one warp per row, every element of a lane's row loaded before any store (one
+// PCIe round trip for host memory).  Launched as a programmatic dependent that
+// releases its own dependent at once, so the attention kernel after it sets up
+// and prefetches K/V into L2 while the rows cross PCIe; both the source (which
+// the kernel before this one may have written) and the destination (which it
+// may still be reading) are touched only after griddepcontrol.wait.
 __global__ void stage_rows_kernel(const uint8_t *__restrict__ src, int64_t nb1, int64_t nb2,
                                   int64_t nb3, int64_t ne0, int64_t ne1, int64_t ne2,
                                   int64_t n_rows, float *__restrict__ dst) {
+    constexpr int VR = 8; // elements per lane loaded at once (ne0 <= 256)
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int64_t row = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
     if (row >= n_rows)
         return;
     const int64_t i1 = row % ne1, i2 = (row / ne1) % ne2, i3 = row / (ne1 * ne2);
     const float *s = reinterpret_cast<const float *>(src + i1 * nb1 + i2 * nb2 + i3 * nb3);
-    for (int64_t i = threadIdx.x % 32; i < ne0; i += 32)
-        dst[row * ne0 + i] = s[i];
+    float *d = dst + row * ne0;
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    if (ne0 <= 32 * VR) {
+        float v[VR];
+#pragma unroll
+        for (int k = 0; k < VR; ++k)
+            v[k] = lane + 32 * k < ne0 ? s[lane + 32 * k] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < VR; ++k)
+            if (lane + 32 * k < ne0)
+                d[lane + 32 * k] = v[k];
+    } else {
+        for (int64_t i = lane; i < ne0; i += 32)
+            d[i] = s[i];
+    }
 }
 
 int stage_q(const xq_tensor &q, const void *src, float *dst, cudaStream_t st) {
@@ -263,11 +285,19 @@ int stage_q(const xq_tensor &q, const void *src, float *dst, cudaStream_t st) {
     const int64_t n_rows = q.ne[1] * q.ne[2] * q.ne[3];
     if (n_rows <= 0)
         return XQ_OK;
-    const unsigned blocks = (unsigned)((n_rows + 7) / 8);
-    stage_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint8_t *>(src), q.nb[1],
-                                              q.nb[2], q.nb[3], q.ne[0], q.ne[1], q.ne[2],
-                                              n_rows, dst);
-    return cuda_status(cudaGetLastError(), "flash_attn_ext: staging q");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n_rows + 7) / 8), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, stage_rows_kernel,
+                                          static_cast<const uint8_t *>(src), q.nb[1], q.nb[2],
+                                          q.nb[3], q.ne[0], q.ne[1], q.ne[2], n_rows, dst),
+                       "flash_attn_ext: staging q");
 }
 
 } // namespace
