@@ -930,9 +930,12 @@ static cudaError_t mma_vw(const DecodeArgs &a, int vw, dim3 grid, cudaStream_t s
     constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
     if constexpr (rec_bytes(T, D) % 16 == 0)
         if (vw == 16) {
-            // TMA boxes: two stages (one group in flight behind the one in use)
-            // measured faster than three, as the first wave of requests is smaller
-            constexpr int STV = dm::tma_mode(T, 16) ? 2 : ST;
+            // TMA boxes.  Q8_0: two stages (one group in flight behind the one
+            // in use) measured faster than three, as the first wave of requests
+            // is smaller.  Q4_0 boxes are half as large and two stages leave the
+            // stream short of requests: four (three groups in flight per warp,
+            // still two CTAs per SM) measured 15.2 against 17.9 us on config 2.
+            constexpr int STV = dm::tma_mode(T, 16) ? (T == kQ4 ? 4 : 2) : ST;
             const cudaError_t e = launch_mma<T, D, STV, 16>(a, grid, st);
             if (e != cudaErrorNotSupported)
                 return e;
