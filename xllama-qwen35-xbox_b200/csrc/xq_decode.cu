@@ -390,8 +390,10 @@ __device__ __forceinline__ void st_peer(int *local, uint32_t rank, int v) {
 // n_splits) of the partials.  With `records` set, each merged row is written
 // as a partial record itself -- (O normalised, lse, 1), or (0, -FLT_MAX, 0)
 // when empty, NaN when poisoned -- so merged groups merge again exactly like
-// splits (sinks are applied only by a final, non-record merge).
-template <int D>
+// splits (sinks are applied only by a final, non-record merge).  A lane owns
+// DL adjacent dims (DL = 2: 8-byte loads, half the CTAs per row); every dim is
+// summed over the same split ranges in the same order either way.
+template <int D, int DL>
 __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restrict__ part,
                                                            int64_t n_splits, int64_t n_rows,
                                                            float *__restrict__ out,
@@ -399,10 +401,11 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
                                                            const float *__restrict__ sinks,
                                                            int n_head, int records) {
     using namespace mg;
-    constexpr int NC = D / 32; // CTAs per row (the cluster)
+    constexpr int NC = D / (32 * DL); // CTAs per row (the cluster)
+    constexpr int CD = 32 * DL;       // dims per CTA
     __shared__ float2 wd_s[CACHE]; // (m, l), then (w, l) of each split
     __shared__ float red[NW];
-    __shared__ float accw[NW][32];
+    __shared__ float accw[NW][CD];
     __shared__ int flags_s[NC]; // slot r: CTA r's poison flag (written by CTA r)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int chunk = blockIdx.x % NC; // == rank in the cluster
@@ -414,20 +417,37 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     auto md = [&](int64_t s) {
         return make_float2(base[s * stride + D], base[s * stride + D + 1]);
     };
+    auto ld = [&](const float *p, float (&v)[DL]) {
+        if constexpr (DL == 2) {
+            const float2 t = *reinterpret_cast<const float2 *>(p);
+            v[0] = t.x;
+            v[1] = t.y;
+        } else {
+            v[0] = *p;
+        }
+    };
     cluster_arrive_relaxed(); // every peer has started before any DSMEM store below
     // the next decode may launch now; it waits for this grid before it writes
     // the partials read here
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
     grid_dep_wait(); // partials come from the preceding kernel
-    // this warp's splits [s0, s1), lane = dim; first XR numerators in flight now
-    const int d = chunk * 32 + lane;
+    // this warp's splits [s0, s1), lane = dims d .. d + DL - 1; first XR
+    // numerators in flight now
+    const int d = chunk * CD + DL * lane;
     const int64_t s0 = n_splits * warp / NW, s1 = n_splits * (warp + 1) / NW;
     const float *xb = base + d;
-    float x[XR];
+    float x[XR][DL];
 #pragma unroll
-    for (int i = 0; i < XR; ++i)
-        x[i] = s0 + i < s1 ? xb[(s0 + i) * stride] : 0.0f;
+    for (int i = 0; i < XR; ++i) {
+        if (s0 + i < s1) {
+            ld(xb + (s0 + i) * stride, x[i]);
+        } else {
+#pragma unroll
+            for (int c = 0; c < DL; ++c)
+                x[i][c] = 0.0f;
+        }
+    }
 
     float mx = -FLT_MAX;
     int bad = 0;
@@ -470,49 +490,81 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     for (int w = 1; w < NW; ++w)
         L += red[w];
 
-    float acc = 0.0f, chk = 0.0f; // chk: NaN iff some live numerator is not finite
-    if (cached) {
-        for (int64_t c = s0; c < s1; c += XR) {
-            if (c != s0) {
+    // chk: NaN iff some live numerator is not finite
+    float acc[DL], chk[DL];
 #pragma unroll
-                for (int i = 0; i < XR; ++i)
-                    x[i] = c + i < s1 ? xb[(c + i) * stride] : 0.0f;
+    for (int c = 0; c < DL; ++c)
+        acc[c] = chk[c] = 0.0f;
+    if (cached) {
+        for (int64_t cs = s0; cs < s1; cs += XR) {
+            if (cs != s0) {
+#pragma unroll
+                for (int i = 0; i < XR; ++i) {
+                    if (cs + i < s1) {
+                        ld(xb + (cs + i) * stride, x[i]);
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < DL; ++c)
+                            x[i][c] = 0.0f;
+                    }
+                }
             }
 #pragma unroll
             for (int i = 0; i < XR; ++i) {
-                if (c + i < s1) {
-                    const float2 v = wd_s[c + i];
-                    const float y = v.y != 0.0f ? x[i] : 0.0f;
-                    acc = fmaf(y, v.x, acc);
-                    chk = fmaf(y, 0.0f, chk);
+                if (cs + i < s1) {
+                    const float2 v = wd_s[cs + i];
+#pragma unroll
+                    for (int c = 0; c < DL; ++c) {
+                        const float y = v.y != 0.0f ? x[i][c] : 0.0f;
+                        acc[c] = fmaf(y, v.x, acc[c]);
+                        chk[c] = fmaf(y, 0.0f, chk[c]);
+                    }
                 }
             }
         }
     } else {
         // more splits than the shared-memory cache: weights recomputed per split
-        for (int64_t c = s0; c < s1; ++c) {
-            const float2 v = md(c);
+        for (int64_t cs = s0; cs < s1; ++cs) {
+            const float2 v = md(cs);
             const float w = v.y != 0.0f ? expf(v.x - M) : 0.0f;
-            const float y = v.y != 0.0f ? xb[c * stride] : 0.0f;
-            acc = fmaf(y, w, acc);
-            chk = fmaf(y, 0.0f, chk);
+            float xv[DL];
+            ld(xb + cs * stride, xv);
+#pragma unroll
+            for (int c = 0; c < DL; ++c) {
+                const float y = v.y != 0.0f ? xv[c] : 0.0f;
+                acc[c] = fmaf(y, w, acc[c]);
+                chk[c] = fmaf(y, 0.0f, chk[c]);
+            }
         }
     }
-    accw[warp][lane] = acc;
-    bad |= __syncthreads_or(!isfinite(chk));
-
-    float o = 0.0f, l = 0.0f;
-    if (warp == 0) {
-        o = accw[0][lane];
+    bool nonfinite = false;
 #pragma unroll
-        for (int w = 1; w < NW; ++w)
-            o += accw[w][lane];
+    for (int c = 0; c < DL; ++c) {
+        accw[warp][DL * lane + c] = acc[c];
+        nonfinite = nonfinite || !isfinite(chk[c]);
+    }
+    bad |= __syncthreads_or(nonfinite);
+
+    float o[DL], l = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DL; ++c)
+        o[c] = 0.0f;
+    if (warp == 0) {
+#pragma unroll
+        for (int c = 0; c < DL; ++c) {
+            o[c] = accw[0][DL * lane + c];
+#pragma unroll
+            for (int w = 1; w < NW; ++w)
+                o[c] += accw[w][DL * lane + c];
+        }
         // the sink joins as one more split of weight exp(sink - M)
         if (sinks) {
             const float sk = sinks[row % n_head];
             if (L == 0.0f || sk > M) {
                 const float ms = L == 0.0f ? 0.0f : expf(M - sk);
-                o *= ms;
+#pragma unroll
+                for (int c = 0; c < DL; ++c)
+                    o[c] *= ms;
                 L = L * ms + 1.0f;
                 M = sk;
             } else {
@@ -521,10 +573,13 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
         }
         const float inv = L == 0.0f ? 0.0f : 1.0f / L;
         l = L == 0.0f ? -INFINITY : M + logf(L);
-        const bool rowbad =
-            !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
-        o *= inv;
-        bad |= __any_sync(0xffffffffu, rowbad || !isfinite(o));
+        bool rowbad = !isfinite(L) || L < 0.0f || !isfinite(inv) || (L != 0.0f && !isfinite(l));
+#pragma unroll
+        for (int c = 0; c < DL; ++c) {
+            o[c] *= inv;
+            rowbad = rowbad || !isfinite(o[c]);
+        }
+        bad |= __any_sync(0xffffffffu, rowbad);
     }
     // push this CTA's flag into slot `chunk` of every CTA of the row
     cluster_wait();
@@ -536,17 +591,17 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
 #pragma unroll
         for (int r = 0; r < NC; ++r)
             poison |= flags_s[r];
-        if (records) {
-            float *rec = out + row * (D + 2);
-            rec[d] = poison ? NAN : o;
-            if (chunk == 0 && lane == 0) {
-                rec[D] = poison ? NAN : (L == 0.0f ? -FLT_MAX : l);
-                rec[D + 1] = poison ? NAN : (L == 0.0f ? 0.0f : 1.0f);
-            }
-        } else {
-            out[row * D + d] = poison ? NAN : o;
-            if (lse && chunk == 0 && lane == 0)
+        float *dst = records ? out + row * (D + 2) : out + row * D;
+#pragma unroll
+        for (int c = 0; c < DL; ++c)
+            dst[d + c] = poison ? NAN : o[c];
+        if (chunk == 0 && lane == 0) {
+            if (records) {
+                dst[D] = poison ? NAN : (L == 0.0f ? -FLT_MAX : l);
+                dst[D + 1] = poison ? NAN : (L == 0.0f ? 0.0f : 1.0f);
+            } else if (lse) {
                 lse[row] = poison ? NAN : l;
+            }
         }
     }
 }
@@ -797,22 +852,29 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
                                   n_head, records ? 1 : 0);
     }
     void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int, int);
-    switch (D) {
-    case 64: kern = lse_merge_kernel<64>; break;
-    case 128: kern = lse_merge_kernel<128>; break;
-    case 256: kern = lse_merge_kernel<256>; break;
+    // two dims per lane (8-byte loads) where the records allow it: half the
+    // CTAs per row, the same sums; the smaller grid leaves SMs free for the
+    // next decode to start under the merge (config 2: 15.8 -> 14.9 us a step)
+    const int dl = D >= 128 && ((uintptr_t)partials & 7) == 0 ? 2 : 1;
+    switch (D * 4 + dl) {
+    case 64 * 4 + 1: kern = lse_merge_kernel<64, 1>; break;
+    case 128 * 4 + 1: kern = lse_merge_kernel<128, 1>; break;
+    case 256 * 4 + 1: kern = lse_merge_kernel<256, 1>; break;
+    case 128 * 4 + 2: kern = lse_merge_kernel<128, 2>; break;
+    case 256 * 4 + 2: kern = lse_merge_kernel<256, 2>; break;
     default: return cudaErrorInvalidValue;
     }
-    // one cluster of D / 32 CTAs per row; launched as a programmatic dependent
-    // of the kernel before it on the stream (the merge waits for it in-kernel)
+    const int nc = D / (32 * dl);
+    // one cluster of nc CTAs per row; launched as a programmatic dependent of
+    // the kernel before it on the stream (the merge waits for it in-kernel)
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(n_groups * n_rows * (D / 32)), 1, 1);
+    cfg.gridDim = dim3((unsigned)(n_groups * n_rows * nc), 1, 1);
     cfg.blockDim = dim3(mg::NT, 1, 1);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)(D / 32);
+    attr[0].val.clusterDim.x = (unsigned)nc;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
