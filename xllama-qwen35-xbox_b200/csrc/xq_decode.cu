@@ -18,6 +18,7 @@
 // stream into shared memory through a 2-stage cp.async pipeline; scores use
 // LPR lanes per row (dims interleaved in 4-dim chunks) and warp shuffles; the
 // PV product gives each thread 4 dims x NR q-rows over a group of rows.
+#include <atomic>
 #include <float.h>
 #include <math.h>
 
@@ -365,6 +366,7 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 // number of splits, never on which GPU or launch produced each split.
 namespace mg {
 constexpr int NT = 256, NW = NT / 32, CACHE = 2048, XR = 24;
+constexpr size_t STG_CAP = 64 * 1024; // staged numerators per CTA at most
 
 __device__ __forceinline__ void grid_dep_wait() {
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
@@ -391,9 +393,12 @@ __device__ __forceinline__ void st_peer(int *local, uint32_t rank, int v) {
 // as a partial record itself -- (O normalised, lse, 1), or (0, -FLT_MAX, 0)
 // when empty, NaN when poisoned -- so merged groups merge again exactly like
 // splits (sinks are applied only by a final, non-record merge).  A lane owns
-// DL adjacent dims (DL = 2: 8-byte loads, half the CTAs per row); every dim is
-// summed over the same split ranges in the same order either way.
-template <int D, int DL>
+// DL adjacent dims (DL = 2: 8-byte loads, half the CTAs per row).  With STG
+// the CTA's numerators are first copied into shared memory (8-byte cp.async,
+// dynamic shared memory of n_splits x 32 DL floats) instead of being held in
+// registers.  Every dim is summed over the same split ranges in the same
+// order in all variants.
+template <int D, int DL, bool STG>
 __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restrict__ part,
                                                            int64_t n_splits, int64_t n_rows,
                                                            float *__restrict__ out,
@@ -437,15 +442,28 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     const int d = chunk * CD + DL * lane;
     const int64_t s0 = n_splits * warp / NW, s1 = n_splits * (warp + 1) / NW;
     const float *xb = base + d;
-    float x[XR][DL];
+    constexpr int XRR = STG ? 1 : XR;
+    float x[XRR][DL];
+    extern __shared__ __align__(16) float xs_s[]; // STG: [n_splits][CD] numerators
+    if constexpr (STG) {
+        // every numerator of this CTA's dims copied to shared memory (8-byte
+        // copies, no registers held); read back in the same order below
+        const float *cb = base + chunk * CD;
+        for (int64_t k = tid; k < n_splits * (CD / 2); k += NT) {
+            const int64_t sp = k / (CD / 2), j = k - sp * (CD / 2);
+            cp_async<8>(smem_u32(xs_s + sp * CD + 2 * j), cb + sp * stride + 2 * j);
+        }
+        cp_async_commit();
+    } else {
 #pragma unroll
-    for (int i = 0; i < XR; ++i) {
-        if (s0 + i < s1) {
-            ld(xb + (s0 + i) * stride, x[i]);
-        } else {
+        for (int i = 0; i < XR; ++i) {
+            if (s0 + i < s1) {
+                ld(xb + (s0 + i) * stride, x[i]);
+            } else {
 #pragma unroll
-            for (int c = 0; c < DL; ++c)
-                x[i][c] = 0.0f;
+                for (int c = 0; c < DL; ++c)
+                    x[i][c] = 0.0f;
+            }
         }
     }
 
@@ -484,6 +502,8 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
     lsum = warp_sum(lsum);
     if (lane == 0)
         red[warp] = lsum;
+    if constexpr (STG)
+        cp_async_wait<0>();
     __syncthreads();
     float L = red[0];
 #pragma unroll
@@ -495,7 +515,17 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
 #pragma unroll
     for (int c = 0; c < DL; ++c)
         acc[c] = chk[c] = 0.0f;
-    if (cached) {
+    if constexpr (STG) {
+        for (int64_t cs = s0; cs < s1; ++cs) {
+            const float2 v = wd_s[cs];
+#pragma unroll
+            for (int c = 0; c < DL; ++c) {
+                const float y = v.y != 0.0f ? xs_s[cs * CD + DL * lane + c] : 0.0f;
+                acc[c] = fmaf(y, v.x, acc[c]);
+                chk[c] = fmaf(y, 0.0f, chk[c]);
+            }
+        }
+    } else if (cached) {
         for (int64_t cs = s0; cs < s1; cs += XR) {
             if (cs != s0) {
 #pragma unroll
@@ -856,13 +886,27 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     // CTAs per row, the same sums; the smaller grid leaves SMs free for the
     // next decode to start under the merge (config 2: 15.8 -> 14.9 us a step)
     const int dl = D >= 128 && ((uintptr_t)partials & 7) == 0 ? 2 : 1;
+    // numerators staged in shared memory (32 registers, no array in flight)
+    // for D = 128: config 1 11.3 -> 10.1 us a step; at D = 256 the same
+    // change made config 2 slower (14.9 -> 16.4 us) although the merge alone
+    // got faster, so it stays on the register path there.  Same sums either way.
+    const size_t stg_bytes = (size_t)n_splits * 64 * sizeof(float);
+    const bool stg = dl == 2 && D == 128 && stg_bytes <= mg::STG_CAP;
     switch (D * 4 + dl) {
-    case 64 * 4 + 1: kern = lse_merge_kernel<64, 1>; break;
-    case 128 * 4 + 1: kern = lse_merge_kernel<128, 1>; break;
-    case 256 * 4 + 1: kern = lse_merge_kernel<256, 1>; break;
-    case 128 * 4 + 2: kern = lse_merge_kernel<128, 2>; break;
-    case 256 * 4 + 2: kern = lse_merge_kernel<256, 2>; break;
+    case 64 * 4 + 1: kern = lse_merge_kernel<64, 1, false>; break;
+    case 128 * 4 + 1: kern = lse_merge_kernel<128, 1, false>; break;
+    case 256 * 4 + 1: kern = lse_merge_kernel<256, 1, false>; break;
+    case 128 * 4 + 2:
+        kern = stg ? lse_merge_kernel<128, 2, true> : lse_merge_kernel<128, 2, false>;
+        break;
+    case 256 * 4 + 2: kern = lse_merge_kernel<256, 2, false>; break;
     default: return cudaErrorInvalidValue;
+    }
+    if (stg) {
+        static std::atomic<unsigned long long> stg_attr{0};
+        const cudaError_t e = set_smem_limit((const void *)kern, mg::STG_CAP, stg_attr);
+        if (e != cudaSuccess)
+            return e;
     }
     const int nc = D / (32 * dl);
     // one cluster of nc CTAs per row; launched as a programmatic dependent of
@@ -870,7 +914,7 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(n_groups * n_rows * nc), 1, 1);
     cfg.blockDim = dim3(mg::NT, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = stg ? stg_bytes : 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
