@@ -883,8 +883,8 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     }
     void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int, int);
     // two dims per lane (8-byte loads) where the records allow it: half the
-    // CTAs per row, the same sums; the smaller grid leaves SMs free for the
-    // next decode to start under the merge (config 2: 15.8 -> 14.9 us a step)
+    // CTAs per row, the same sums (config 2: 15.8 -> 14.9 us a step, while
+    // the merge timed on its own did not change)
     const int dl = D >= 128 && ((uintptr_t)partials & 7) == 0 ? 2 : 1;
     // numerators staged in shared memory (32 registers, no array in flight)
     // for D = 128: config 1 11.3 -> 10.1 us a step; at D = 256 the same
