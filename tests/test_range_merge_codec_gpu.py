@@ -170,3 +170,56 @@ def test_lse_merge_records_two_level(rows):
     np.testing.assert_allclose(out2[fin], out1[fin], rtol=1e-4, atol=1e-5)
     fl = ~np.isnan(lse1)
     np.testing.assert_allclose(lse2[fl], lse1[fl], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("n_splits", [1, 37, 148, 2500])
+def test_lse_merge_variants_bit_identical(D, n_splits):
+    """The cluster merge picks its lane width (and, at D = 128, numerators
+    staged in shared memory) from the partials' alignment; every variant sums
+    each dim over the same splits in the same order, so partials at an 8-byte
+    aligned address and the same records 4 bytes off give the same bits --
+    plain, empty, poisoned and record-mode rows alike -- and agree with the
+    oracle."""
+    xq = _xq()
+    rng = np.random.default_rng(D * 7919 + n_splits)
+    rows = 12
+    part = np.zeros((n_splits, rows, D + 2), np.float32)
+    part[:, :, :D] = rng.normal(0, 1, (n_splits, rows, D))
+    part[:, :, D] = rng.normal(0, 3, (n_splits, rows))
+    part[:, :, D + 1] = rng.uniform(0.5, 2.0, (n_splits, rows))
+    empty = rng.random((n_splits, rows)) < 0.2
+    part[:, :, D + 1][empty] = 0.0
+    part[:, :, D][empty] = -3.402823466e38
+    part[:, 2, D + 1] = 0.0                         # row 2: every split empty
+    part[:, 2, D] = -3.402823466e38
+    live = np.nonzero(part[:, 4, D + 1] != 0.0)[0]
+    if live.size:
+        part[live[-1], 4, 5] = np.inf               # row 4: poisoned
+    n = part.size
+    buf = torch.zeros(n + 2, dtype=torch.float32, device="cuda")
+    aligned = buf[:n].view(part.shape)               # 8-byte aligned (allocator: 256)
+    shifted = buf[1:n + 1]                           # 4 bytes off
+    assert aligned.data_ptr() % 8 == 0 and shifted.data_ptr() % 8 == 4
+    results = []
+    for view in (aligned, shifted):
+        view.copy_(torch.from_numpy(part).reshape(view.shape).cuda())
+        o, lse = xq.lse_merge(view.view(part.shape))
+        torch.cuda.synchronize()
+        results.append((o.cpu().numpy().view(np.int32), lse.cpu().numpy().view(np.int32)))
+    assert np.array_equal(results[0][0], results[1][0])
+    assert np.array_equal(results[0][1], results[1][1])
+    o_ref, lse_ref = oracle.lse_merge(part)
+    o = results[0][0].view(np.float32)
+    assert np.array_equal(np.isnan(o), np.isnan(o_ref))
+    fin = ~np.isnan(o_ref)
+    np.testing.assert_allclose(o[fin], o_ref[fin], rtol=1e-4, atol=1e-5)
+    if n_splits % 2 == 0 and n_splits > 1:
+        # record mode (two groups), both alignments
+        recs = []
+        for view in (aligned, shifted):
+            view.copy_(torch.from_numpy(part).reshape(view.shape).cuda())
+            r = xq.lse_merge_records(view.view(part.shape), n_splits // 2)
+            torch.cuda.synchronize()
+            recs.append(r.cpu().numpy().view(np.int32))
+        assert np.array_equal(recs[0], recs[1])
