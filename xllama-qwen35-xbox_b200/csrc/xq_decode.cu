@@ -367,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 2) fa_decode_kernel(const DecodeArgs
 namespace mg {
 constexpr int NT = 256, NW = NT / 32, CACHE = 2048, XR = 24;
 constexpr size_t STG_CAP = 64 * 1024; // staged numerators per CTA at most
+constexpr size_t STG_PAD = 96 * 1024; // dynamic shared memory of a D = 256 staged CTA
 
 __device__ __forceinline__ void grid_dep_wait() {
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
@@ -886,12 +887,15 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     // CTAs per row, the same sums (config 2: 15.8 -> 14.9 us a step, while
     // the merge timed on its own did not change)
     const int dl = D >= 128 && ((uintptr_t)partials & 7) == 0 ? 2 : 1;
-    // numerators staged in shared memory (32 registers, no array in flight)
-    // for D = 128: config 1 11.3 -> 10.1 us a step; at D = 256 the same
-    // change made config 2 slower (14.9 -> 16.4 us) although the merge alone
-    // got faster, so it stays on the register path there.  Same sums either way.
+    // numerators staged in shared memory (32 registers, no array in flight):
+    // config 1 11.3 -> 10.1 us a step, kv4 28.6 -> 26.9 us.  At D = 256 the
+    // CTA reserves mg::STG_PAD bytes so that it never shares an SM with two
+    // Q8_0 / Q4_0 decode CTAs (77-81 KB each): sharing made config 2's step
+    // slower (14.9 -> 16.4 us) although the merge alone was faster.  Same sums
+    // in every variant.
     const size_t stg_bytes = (size_t)n_splits * 64 * sizeof(float);
-    const bool stg = dl == 2 && D == 128 && stg_bytes <= mg::STG_CAP;
+    const bool stg = dl == 2 && stg_bytes <= mg::STG_CAP;
+    const size_t stg_dyn = D == 256 ? mg::STG_PAD : stg_bytes;
     switch (D * 4 + dl) {
     case 64 * 4 + 1: kern = lse_merge_kernel<64, 1, false>; break;
     case 128 * 4 + 1: kern = lse_merge_kernel<128, 1, false>; break;
@@ -899,12 +903,14 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     case 128 * 4 + 2:
         kern = stg ? lse_merge_kernel<128, 2, true> : lse_merge_kernel<128, 2, false>;
         break;
-    case 256 * 4 + 2: kern = lse_merge_kernel<256, 2, false>; break;
+    case 256 * 4 + 2:
+        kern = stg ? lse_merge_kernel<256, 2, true> : lse_merge_kernel<256, 2, false>;
+        break;
     default: return cudaErrorInvalidValue;
     }
     if (stg) {
-        static std::atomic<unsigned long long> stg_attr{0};
-        const cudaError_t e = set_smem_limit((const void *)kern, mg::STG_CAP, stg_attr);
+        static std::atomic<unsigned long long> stg_attr[2];
+        const cudaError_t e = set_smem_limit((const void *)kern, mg::STG_PAD, stg_attr[D == 256]);
         if (e != cudaSuccess)
             return e;
     }
@@ -914,7 +920,7 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(n_groups * n_rows * nc), 1, 1);
     cfg.blockDim = dim3(mg::NT, 1, 1);
-    cfg.dynamicSmemBytes = stg ? stg_bytes : 0;
+    cfg.dynamicSmemBytes = stg ? stg_dyn : 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
