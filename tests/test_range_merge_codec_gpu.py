@@ -172,9 +172,10 @@ def test_lse_merge_records_two_level(rows):
     np.testing.assert_allclose(lse2[fl], lse1[fl], rtol=1e-5, atol=1e-5)
 
 
+@pytest.mark.parametrize("rows", [12, 48])  # D = 256: one-wave (staged) / larger grid
 @pytest.mark.parametrize("D", [64, 128, 256])
 @pytest.mark.parametrize("n_splits", [1, 37, 148, 2500])
-def test_lse_merge_variants_bit_identical(D, n_splits):
+def test_lse_merge_variants_bit_identical(D, n_splits, rows):
     """The cluster merge picks its lane width (and, at D = 128, numerators
     staged in shared memory) from the partials' alignment; every variant sums
     each dim over the same splits in the same order, so partials at an 8-byte
@@ -182,8 +183,7 @@ def test_lse_merge_variants_bit_identical(D, n_splits):
     plain, empty, poisoned and record-mode rows alike -- and agree with the
     oracle."""
     xq = _xq()
-    rng = np.random.default_rng(D * 7919 + n_splits)
-    rows = 12
+    rng = np.random.default_rng(D * 7919 + n_splits + rows)
     part = np.zeros((n_splits, rows, D + 2), np.float32)
     part[:, :, :D] = rng.normal(0, 1, (n_splits, rows, D))
     part[:, :, D] = rng.normal(0, 3, (n_splits, rows))

@@ -894,7 +894,16 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     // slower (14.9 -> 16.4 us) although the merge alone was faster.  Same sums
     // in every variant.
     const size_t stg_bytes = (size_t)n_splits * 64 * sizeof(float);
-    const bool stg = dl == 2 && stg_bytes <= mg::STG_CAP;
+    bool stg = dl == 2 && stg_bytes <= mg::STG_CAP;
+    if (stg && D == 256) {
+        // the reservation leaves one merge CTA per SM: staged only where the
+        // whole grid fits in one wave (the register path holds two per SM)
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            sms = 0;
+        stg = n_groups * n_rows * (D / 64) <= sms;
+    }
     const size_t stg_dyn = D == 256 ? mg::STG_PAD : stg_bytes;
     switch (D * 4 + dl) {
     case 64 * 4 + 1: kern = lse_merge_kernel<64, 1, false>; break;
