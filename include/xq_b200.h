@@ -126,6 +126,8 @@ int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_
 /* not NULL, lse [n_rows] (natural log).  Fixed split order; empty splits    */
 /* (denom == 0) are skipped; all empty => O = 0, LSE = -inf; a participating */
 /* non-finite state poisons the row with NaN (rkva_range_reduce_opt.hlsl).   */
+/* partials must be 4-byte aligned; 8-byte aligned partials (any cudaMalloc  */
+/* pointer) take the faster wide-load kernels, with bit-identical results.   */
 int xq_lse_merge(const float *partials, int64_t n_splits, int64_t n_rows, int64_t D,
                  float *out, float *lse, xq_stream_t stream);
 
