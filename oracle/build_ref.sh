@@ -1,8 +1,9 @@
 #!/bin/sh
 # Compiles pieces of the reference that build standalone into oracle/_ref/
 # (git-ignored).  Test infrastructure: used only to pin the oracle and to make
-# the golden fixtures under tests/golden/.  Needs the reference checkout; the
-# GPU box never runs this (it has no reference checkout).
+# the golden fixtures under tests/golden/.  Needs the reference checkout, named
+# by XQ_REFERENCE (default: a `reference` directory beside this repository);
+# the GPU box never runs this (it has no reference checkout).
 #
 #   src/bridge/ggml_d3d12.cpp:77-158  d3d12_gdn_supported + d3d12_gdn_emulate
 #     (the reference's host mirror of its GATED_DELTA_NET shader).  The rest of
@@ -11,7 +12,7 @@
 #     generating the selftest inputs (ggml_d3d12.cpp:174-369 protocol).
 set -eu
 HERE=$(cd "$(dirname "$0")" && pwd)
-REF=${XQ_REFERENCE:-/root/reference}
+REF=${XQ_REFERENCE:-$(cd "$HERE/../.." && pwd)/reference}
 SRC="$REF/src/bridge/ggml_d3d12.cpp"
 OUT="$HERE/_ref"
 if [ ! -f "$SRC" ]; then

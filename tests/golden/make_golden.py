@@ -4,7 +4,7 @@
 Run here, where the reference checkout exists (it does not on the GPU box):
 
     make -C oracle ref            # compiles oracle/_ref/libxq_gdn_ref.so
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py [--reference DIR]   # default: $XQ_REFERENCE
 
 Sources of truth (none of them this repository's own code):
   codecs.npz      gguf 0.19.0 gguf/quants.py Q8_0 / Q4_0 quantize + dequantize
@@ -229,7 +229,8 @@ def make_kvarn4(out, ref_tests):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("XQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get(
+        "XQ_REFERENCE", os.path.join(os.path.dirname(REPO), "reference")))
     ap.add_argument("--only", default=None, help="codecs|range|reduce|kvarn4|gdn")
     args = ap.parse_args()
     ref_tests = os.path.join(args.reference, "tests")
