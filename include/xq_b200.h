@@ -276,13 +276,22 @@ int xq_quantize_rows(int32_t type, const float *src, uint64_t src_row_stride, vo
 /* that every GPU which loads the library holds until the process exits.    */
 /*                                                                           */
 /*  - It runs the split-KV decode kernels (never the tensor-core prefill     */
-/*    kernel) and computes the same results as xq_flash_attn_ext.            */
+/*    kernel).  For every shape that xq_flash_attn_ext also sends to those  */
+/*    kernels (decode and short multi-query calls) the results are bit for  */
+/*    bit the same; F16 calls with 64 or more queries, which               */
+/*    xq_flash_attn_ext sends to the prefill kernel, agree within the       */
+/*    attention tolerance instead.                                          */
+/*  - q and dst may be device memory or pinned host memory, as for          */
+/*    xq_flash_attn_ext: a pinned q is copied into the scratch by a kernel  */
+/*    and a pinned dst is written in place; pageable host memory returns    */
+/*    XQ_ERR_INVALID before anything is launched.                           */
 /*  - The first call on a device looks up the scratch address for that     */
 /*    device (cudaGetSymbolAddress); make that first call before any stream */
-/*    capture.                                                               */
-/*  - A call whose split plan needs more scratch than the maximum returns   */
-/*    XQ_ERR_WORKSPACE with the sizes in xq_last_error(); pass a smaller    */
-/*    n_splits.                                                              */
+/*    capture.  The address is kept for the life of the process: do not     */
+/*    call this entry point again after cudaDeviceReset on that device.     */
+/*  - A call whose split plan (plus the staged q) needs more scratch than   */
+/*    the maximum returns XQ_ERR_WORKSPACE with the sizes in               */
+/*    xq_last_error(); pass a smaller n_splits.                             */
 /*  - All calls share the one array and it keeps the last call's contents;  */
 /*    nothing in it has to start at zero (every partial record is written   */
 /*    before it is read).  Calls that overlap on the GPU (other streams,    */

@@ -874,6 +874,8 @@ void *g_noalloc_ptr[kNoallocMaxDevices];
 } // namespace
 
 extern "C" int xq_flash_attn_ext_noalloc(const xq_fa_params *p, xq_stream_t stream) {
+    if (!p)
+        return fail(XQ_ERR_INVALID, "flash_attn_ext_noalloc: null params");
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess)
@@ -893,31 +895,63 @@ extern "C" int xq_flash_attn_ext_noalloc(const xq_fa_params *p, xq_stream_t stre
         }
         scratch = g_noalloc_ptr[dev];
     }
+    // q and dst: device memory, or pinned host memory (q staged into the
+    // scratch by a kernel, dst written through its device view); pageable
+    // host memory is rejected before anything is launched
+    HostView hq, hd;
+    const int kq = host_view(p->q.data, &hq), kd = host_view(p->dst, &hd);
+    if (kq < 0 || kd < 0)
+        return fail(XQ_ERR_INVALID,
+                    "flash_attn_ext_noalloc: q / dst in pageable host memory (pin it or use the "
+                    "device)");
+    xq_fa_params p2 = *p;
+    if (kd == 1)
+        p2.dst = static_cast<float *>(hd.dev);
     FaPlan pl;
-    int rc = fa_prepare(p, &pl);
+    int rc = fa_prepare(&p2, &pl);
     if (rc)
         return rc;
     plan_splits(&pl, p->n_splits);
+    const size_t part = pl.n_splits > 1
+                            ? (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * 4
+                            : 0;
+    const size_t q_off = (part + 255) / 256 * 256;
+    const size_t need = kq == 1 ? q_off + q_stage_bytes(p->q) : part;
+    if (need > (size_t)XQ_NOALLOC_SCRATCH_BYTES)
+        return fail(XQ_ERR_WORKSPACE,
+                    "flash_attn_ext_noalloc: %lld splits x %lld rows%s need %zu bytes of scratch, "
+                    "the static scratch holds %u; pass a smaller n_splits",
+                    (long long)pl.n_splits, (long long)pl.n_rows,
+                    kq == 1 ? " and the staged q" : "", need, (unsigned)XQ_NOALLOC_SCRATCH_BYTES);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (kq == 1) {
+        float *staged = reinterpret_cast<float *>(static_cast<uint8_t *>(scratch) + q_off);
+        rc = stage_q(p->q, hq.dev, staged, st);
+        if (rc)
+            return rc;
+        p2.q.data = staged;
+        p2.q.nb[0] = 4;
+        p2.q.nb[1] = 4 * p->q.ne[0];
+        p2.q.nb[2] = p2.q.nb[1] * p->q.ne[1];
+        p2.q.nb[3] = p2.q.nb[2] * p->q.ne[2];
+        // same shapes, so the same split plan, now reading the staged q
+        rc = fa_prepare(&p2, &pl);
+        if (rc)
+            return rc;
+        plan_splits(&pl, p->n_splits);
+    }
     dim3 grid((unsigned)pl.n_splits, (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
               (unsigned)pl.a.n_seq);
     if (pl.n_splits == 1) {
         pl.a.direct = 1;
         return cuda_status(run_decode(pl, grid, st), "flash_attn_ext_noalloc decode");
     }
-    const size_t need = (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * 4;
-    if (need > (size_t)XQ_NOALLOC_SCRATCH_BYTES)
-        return fail(XQ_ERR_WORKSPACE,
-                    "flash_attn_ext_noalloc: %lld splits x %lld rows need %zu bytes of scratch, "
-                    "the static scratch holds %u; pass a smaller n_splits",
-                    (long long)pl.n_splits, (long long)pl.n_rows, need,
-                    (unsigned)XQ_NOALLOC_SCRATCH_BYTES);
     pl.a.direct = 0;
     pl.a.partials = static_cast<float *>(scratch);
     rc = cuda_status(run_decode(pl, grid, st), "flash_attn_ext_noalloc decode");
     if (rc)
         return rc;
-    return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p->dst,
+    return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p2.dst,
                                         nullptr, p->sinks, pl.a.n_head, st),
                        "flash_attn_ext_noalloc merge");
 }
