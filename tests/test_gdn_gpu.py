@@ -180,6 +180,15 @@ def test_gdn_chunked_broadcast_qk_and_slow_decay():
     _chunked_vs_oracle((q, k, v, g, beta, st), 1)
 
 
+@pytest.mark.parametrize("K", [1, 3])
+def test_gdn_chunked_vs_ggml_oracle_at_config3(K):
+    """BASELINE config 3 prefill at its full size (1 x 4096 tokens: 64 chunks
+    whose state errors could compound) against the ggml-cpu restatement:
+    elementwise max-abs 2e-3 / rel 1e-2 on y and on every snapshot slot, and
+    the whole-tensor bound of 5e-3 of max|.|."""
+    _chunked_vs_oracle(c3_inputs(4096, 1, 4096), K)
+
+
 def test_gdn_chunked_matches_per_token_path_at_config3():
     """BASELINE config 3 prefill (1 x 4096 tokens): the chunked result against
     the per-token FP32 kernel on the device (no CPU reference at this size)."""
