@@ -103,3 +103,47 @@ def test_c4_config_sampled_rows():
                                  policy=oracle.FA_SCALAR)
     got = out[:, rows].cpu().numpy()
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+def _quant_prefill_case(seed, ty, H, Hkv, D, n_q, n_kv, n_seq=1):
+    rng = np.random.default_rng(seed)
+    q = rng.normal(0, 1, (n_seq, H, n_q, D)).astype(np.float32)
+    k = oracle.quantize(ty, rng.normal(0, 1, (n_seq, n_kv, Hkv, D)).astype(np.float32))
+    v = oracle.quantize(ty, rng.normal(0, 1, (n_seq, n_kv, Hkv, D)).astype(np.float32))
+    return q, k, v, causal_mask(n_q, n_kv)
+
+
+@pytest.mark.parametrize("ty", [oracle.Q8_0, oracle.Q4_0])
+@pytest.mark.parametrize("n_q,n_kv", [(64, 2048), (512, 1024), (200, 700)])
+def test_quantized_kv_prefill_parity(ty, n_q, n_kv):
+    """A prompt chunk over a Q8_0 / Q4_0 cache -- the reference's product
+    configuration (a quantized KV cache forces flash attention on; prompts go
+    in as n_batch-token chunks) -- with the BASELINE config-4 head shape (24 Q
+    / 4 KV heads, D=256), causal over the tail of the cache.  ggml-cpu takes
+    these through one_chunk whatever the query count (its tiled path needs
+    F16/F32 K/V): q quantized to Q8_0, integer block dots, V dequantized to
+    f32.  Ragged last query and key tiles in the (200, 700) case."""
+    import xq
+    q, k, v, m = _quant_prefill_case(1000 + n_q + ty, ty, 24, 4, 256, n_q, n_kv)
+    dev = torch.device("cuda")
+    got = xq.flash_attn_ext(torch.from_numpy(q).to(dev), torch.from_numpy(k).to(dev),
+                            torch.from_numpy(v).to(dev), ty, mask=torch.from_numpy(m).to(dev),
+                            scale=1 / 16)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(q, k, v, ty, ty, mask=m, scale=1 / 16)
+    got = got.cpu().numpy()
+    assert np.all(np.isfinite(got))
+    np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.parametrize("ty", [oracle.Q8_0, oracle.Q4_0])
+def test_quantized_kv_prefill_two_sequences_no_mask(ty):
+    """Two sequences with their own caches, no mask, D=128, GQA 4."""
+    import xq
+    q, k, v, _ = _quant_prefill_case(77 + ty, ty, 8, 2, 128, 130, 300, n_seq=2)
+    dev = torch.device("cuda")
+    got = xq.flash_attn_ext(torch.from_numpy(q).to(dev), torch.from_numpy(k).to(dev),
+                            torch.from_numpy(v).to(dev), ty, scale=128 ** -0.5)
+    torch.cuda.synchronize()
+    want = oracle.flash_attn_ext(q, k, v, ty, ty, scale=128 ** -0.5)
+    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=RTOL, atol=ATOL)

@@ -155,20 +155,26 @@ bool prefill_disabled() {
     return off != 0;
 }
 
-// The tensor-core prefill kernel takes F16 K/V, D 128/256, many queries and
-// no softcap / ALiBi / sinks, with TMA-compatible (16-byte) strides.
+// The tensor-core prefill kernel takes F16 K/V -- or Q8_0 / Q4_0 K/V, which a
+// pre-pass widens to f16 in the workspace -- D 128/256, many queries and no
+// softcap / ALiBi / sinks, with TMA-compatible (16-byte) strides for what it
+// reads through tensor maps (q always, K/V when F16).
 bool prefill_shape(const xq_fa_params *p, const FaPlan &pl, xq::PrefillShape *ps) {
     const xq_tensor &q = p->q, &k = p->k, &v = p->v, &m = p->mask;
-    if (prefill_disabled() || k.type != XQ_TYPE_F16 || v.type != XQ_TYPE_F16 ||
+    const bool quant = k.type == XQ_TYPE_Q8_0 || k.type == XQ_TYPE_Q4_0;
+    if (prefill_disabled() || !(k.type == XQ_TYPE_F16 || quant) || v.type != k.type ||
         (pl.D != 128 && pl.D != 256) || q.ne[1] < 64 || p->softcap != 0.0f ||
         p->max_bias > 0.0f || p->sinks)
         return false;
     auto a16 = [](uint64_t x) { return x % 16 == 0; };
-    if (!a16((uint64_t)(uintptr_t)k.data) || !a16((uint64_t)(uintptr_t)v.data) ||
-        !a16((uint64_t)(uintptr_t)q.data) || !a16(k.nb[1]) || !a16(k.nb[2]) || !a16(k.nb[3]) ||
-        !a16(v.nb[1]) || !a16(v.nb[2]) || !a16(v.nb[3]) || !a16(q.nb[1]) || !a16(q.nb[2]) ||
-        !a16(q.nb[3]) || k.ne[3] != v.ne[3])
+    auto a2 = [](uint64_t x) { return x % 2 == 0; };
+    const auto kv_ok = quant ? +a2 : +a16; // quantized rows are read by the pre-pass
+    if (!kv_ok((uint64_t)(uintptr_t)k.data) || !kv_ok((uint64_t)(uintptr_t)v.data) ||
+        !a16((uint64_t)(uintptr_t)q.data) || !kv_ok(k.nb[1]) || !kv_ok(k.nb[2]) ||
+        !kv_ok(k.nb[3]) || !kv_ok(v.nb[1]) || !kv_ok(v.nb[2]) || !kv_ok(v.nb[3]) ||
+        !a16(q.nb[1]) || !a16(q.nb[2]) || !a16(q.nb[3]) || k.ne[3] != v.ne[3])
         return false;
+    ps->kv_type = k.type;
     ps->q = static_cast<const uint8_t *>(q.data);
     for (int i = 0; i < 4; ++i) {
         ps->q_nb[i] = (int64_t)q.nb[i];
@@ -335,7 +341,7 @@ static size_t fa_main_workspace(const xq_fa_params *p) {
         return 0;
     xq::PrefillShape ps;
     if (prefill_shape(p, pl, &ps))
-        return xq::prefill_map_bytes(ps);
+        return xq::prefill_ws_bytes(ps);
     plan_splits(&pl, p->n_splits);
     if (pl.n_splits <= 1)
         return 0;
@@ -357,10 +363,12 @@ static int fa_run(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t 
         return rc;
     xq::PrefillShape ps;
     if (prefill_shape(p, pl, &ps)) {
-        const size_t need = xq::prefill_map_bytes(ps);
+        const size_t need = xq::prefill_ws_bytes(ps);
         if (!ws || ws_bytes < need)
             return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes,
                         need);
+        if (reinterpret_cast<uintptr_t>(ws) % 16)
+            return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace must be 16-byte aligned");
         const char *why = "";
         cudaError_t e = xq::launch_prefill(ps, ws, reinterpret_cast<cudaStream_t>(stream), &why);
         if (e != cudaSuccess)
@@ -685,9 +693,13 @@ int xq_attend_range_kvarn4(const xq_kvarn4_desc *d, const void *k_plane, const v
 // GATED_DELTA_NET.
 
 // Validates a GATED_DELTA_NET call and fills the kernel arguments.
+// head_begin / n_head_total: the call covers value heads [head_begin,
+// head_begin + v->ne[1]) of an op with n_head_total value heads (< 0: the
+// whole op, head_begin 0).
 static int gdn_args(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
                     const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
-                    float *dst, int32_t slots, xq::GdnArgs *out) {
+                    float *dst, int32_t slots, xq::GdnArgs *out, int64_t head_begin = 0,
+                    int64_t n_head_total = -1) {
     if (!q || !k || !v || !g || !beta || !state || !dst)
         return fail(XQ_ERR_INVALID, "gated_delta_net: null argument");
     const xq_tensor *all[6] = {q, k, v, g, beta, state};
@@ -702,7 +714,12 @@ static int gdn_args(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
     if (S != 128)
         return fail(XQ_ERR_UNSUPPORTED, "gated_delta_net: head size %lld (supported: 128)",
                     (long long)S);
-    if (q->ne[0] != S || k->ne[0] != S || k->ne[1] != H_k || H_k <= 0 || H % H_k ||
+    if (n_head_total < 0)
+        n_head_total = H;
+    if (head_begin < 0 || head_begin + H > n_head_total || H <= 0)
+        return fail(XQ_ERR_INVALID, "gated_delta_net: value heads [%lld, %lld) outside [0, %lld)",
+                    (long long)head_begin, (long long)(head_begin + H), (long long)n_head_total);
+    if (q->ne[0] != S || k->ne[0] != S || k->ne[1] != H_k || H_k <= 0 || n_head_total % H_k ||
         q->ne[2] != T || k->ne[2] != T || q->ne[3] <= 0 || k->ne[3] <= 0 || n_seq % q->ne[3] ||
         n_seq % k->ne[3] || T <= 0)
         return fail(XQ_ERR_INVALID, "gated_delta_net: inconsistent q/k/v shapes");
@@ -739,6 +756,7 @@ static int gdn_args(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
     a.rk3 = (int)(n_seq / k->ne[3]);
     a.slots = slots;
     a.scale = 1.0f / sqrtf((float)S);
+    a.h_off = (int)(head_begin % H_k);
     *out = a;
     return XQ_OK;
 }
@@ -780,6 +798,29 @@ int xq_gated_delta_net_ws(const xq_tensor *q, const xq_tensor *k, const xq_tenso
         return fail(XQ_ERR_WORKSPACE, "gated_delta_net: workspace must be 256-byte aligned");
     return cuda_status(xq::launch_gdn_chunked(a, workspace, workspace_bytes, st),
                        "gated_delta_net (chunked)");
+}
+
+int xq_gated_delta_net_heads(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                             const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                             float *dst, int32_t slots, int64_t head_begin, int64_t n_head_total,
+                             void *workspace, size_t workspace_bytes, xq_stream_t stream) {
+    if (n_head_total <= 0)
+        return fail(XQ_ERR_INVALID, "gated_delta_net_heads: n_head_total must be positive");
+    xq::GdnArgs a;
+    const int rc = gdn_args(q, k, v, g, beta, state, dst, slots, &a, head_begin, n_head_total);
+    if (rc != XQ_OK)
+        return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (!xq::gdn_chunk_eligible(a))
+        return cuda_status(xq::launch_gdn(a, st), "gated_delta_net_heads");
+    const size_t need = xq::gdn_chunk_workspace(a.T, a.H, a.n_seq, a.slots);
+    if (!workspace || workspace_bytes < need)
+        return fail(XQ_ERR_WORKSPACE, "gated_delta_net_heads: workspace %zu bytes, %zu needed",
+                    workspace_bytes, need);
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+        return fail(XQ_ERR_WORKSPACE, "gated_delta_net_heads: workspace must be 256-byte aligned");
+    return cuda_status(xq::launch_gdn_chunked(a, workspace, workspace_bytes, st),
+                       "gated_delta_net_heads (chunked)");
 }
 
 // ---------------------------------------------------------------------------

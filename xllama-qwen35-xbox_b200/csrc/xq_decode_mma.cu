@@ -353,6 +353,8 @@ __global__ void __launch_bounds__(dm::NT, 1)
         // Launched as a programmatic dependent: until griddepcontrol.wait the
         // kernel before this one may still be writing q or the KV cache, so
         // only L2 prefetches (coherent, no data consumed) are issued here.
+        // (Prefetching every group of the split instead -- 160 KB per CTA --
+        // measured slower on config 2: 16.1 against 14.9 us per step.)
         if (lane == 0)
             for (int st = 0; st < STAGES - 1 && st < my_n; ++st) {
                 const int row = (int)(r0 + (warp + NWARP * st) * KG);

@@ -74,12 +74,14 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
                          float *out, float *lse, const float *sinks, int n_head,
                          cudaStream_t st, int64_t n_groups = 1, bool records = false);
 
-// One tensor-core prefill launch (F16 K/V, F32 q / dst).
+// One tensor-core prefill launch (F32 q / dst; F16 K/V, or Q8_0 / Q4_0 K/V
+// widened to f16 in the workspace first).
 struct PrefillShape {
     const uint8_t *q;
     int64_t q_nb[4];
     const void *k, *v;
     int64_t k_nb[4], v_nb[4];
+    int kv_type; // XQ_TYPE_F16 / Q8_0 / Q4_0
     const uint8_t *mask; // F16 or null
     int64_t m_nb1, m_nb2, m_nb3;
     int m_ne2, m_ne3, m_planes;
@@ -87,7 +89,9 @@ struct PrefillShape {
     int D, n_q, n_head, n_head_kv, n_seq, n_seq_kv, n_kv;
     float scale;
 };
-size_t prefill_map_bytes(const PrefillShape &ps);
+// Workspace of one launch: the mask block map and an error word, then (Q8_0 /
+// Q4_0) the f16 copies of K and V.
+size_t prefill_ws_bytes(const PrefillShape &ps);
 // The driver's cuTensorMapEncodeTiled (PFN_cuTensorMapEncodeTiled_v12000), or null.
 void *tensor_map_encoder();
 cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, const char **why);
@@ -113,6 +117,7 @@ struct GdnArgs {
     int H, H_k, T, n_seq, rq3, rk3, slots;
     float scale;
     int t_begin = 0; // tokens before this one are already folded into `state`
+    int h_off = 0;   // global index of value head 0: value head h reads key head (h + h_off) % H_k
 };
 cudaError_t launch_gdn(const GdnArgs &a, cudaStream_t st);
 // Chunked (WY) form on the tensor cores for long sequences: workspace bytes

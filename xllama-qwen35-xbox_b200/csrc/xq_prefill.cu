@@ -5,6 +5,23 @@
 // give 0; the reference's bring-up kernel shaders/rkva/rkva_flash_attn.hlsl:61-125
 // states the same online-softmax contract).
 //
+// Q8_0 / Q4_0 caches (the reference's product configuration: a quantized KV
+// cache forces flash attention on, src/bridge/session.cpp:600-607, and every
+// prompt chunk reaches this op).  ggml-cpu takes them through one_chunk at any
+// query count (patches/0008-flash-attn-query-consistency.patch:18-35): q is
+// quantized to Q8_0 (the K vec_dot type), K.q is the integer block dot times
+// both block scales, V is dequantized to f32.  Here a pre-pass
+// (kv_to_f16_kernel) widens every K and V row once into the workspace -- the
+// exact dequantized value code * f32(d), rounded once to f16 -- and the
+// kernel below (QQ = true) quantizes each q row to Q8_0 exactly as ggml does
+// (d = amax / 127 rounded to f16, codes roundf(x / d)) before rounding the
+// exact q code * d to f16 for the tensor core.  Every operand is therefore
+// ggml's value to within one f16 rounding (2^-11 relative), the same
+// precision as the f16 probabilities P; the products and sums run in fp32 in
+// TMEM.  (Exact int8 block sums would need one int32 TMEM accumulator per
+// 32-dim block per key tile -- 8 x 64 columns at D = 256 -- beside the 256
+// columns of O: more than the 512 columns an SM has.)
+//
 // One CTA = 128 query rows of one head (TMEM lane r <-> query row r).
 //   warp 0      TMA producer: K_j, V_j tiles (64 keys x D, SW128) into a
 //               6-slot (D=256) / 8-slot ring, completion on mbarriers (expect_tx)
@@ -64,7 +81,7 @@ struct PrefillArgs {
     float scale_log2; // scale * log2(e)
 };
 
-template <int D>
+template <int D, bool QQ>
 __global__ void __launch_bounds__(pf::NT, 1)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
@@ -258,19 +275,42 @@ __global__ void __launch_bounds__(pf::NT, 1)
                                            (int64_t)(s % a.m_ne3) * a.m_nb3
                                      : nullptr;
         {
-            // this thread's query row -> f16 pairs in TMEM lane r (the A operand of S)
+            // this thread's query row -> f16 pairs in TMEM lane r (the A operand of S);
+            // with QQ first through ggml's Q8_0 quantizer (quantize_row_q8_0_ref)
             const float4 *src = reinterpret_cast<const float4 *>(
                 a.q + (int64_t)min(qrow, a.n_q - 1) * a.q_nb1 + (int64_t)h * a.q_nb2 +
                 (int64_t)s * a.q_nb3);
 #pragma unroll 1
             for (int c0 = 0; c0 < D; c0 += 64) {
-                uint32_t w[32];
+                float x[64];
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const float4 x = qrow < a.n_q ? src[c0 / 4 + i] : make_float4(0, 0, 0, 0);
-                    const __half2 h0 = __floats2half2_rn(x.x, x.y), h1 = __floats2half2_rn(x.z, x.w);
-                    w[2 * i] = *reinterpret_cast<const uint32_t *>(&h0);
-                    w[2 * i + 1] = *reinterpret_cast<const uint32_t *>(&h1);
+                    const float4 v = qrow < a.n_q ? src[c0 / 4 + i] : make_float4(0, 0, 0, 0);
+                    x[4 * i] = v.x;
+                    x[4 * i + 1] = v.y;
+                    x[4 * i + 2] = v.z;
+                    x[4 * i + 3] = v.w;
+                }
+                if constexpr (QQ) {
+#pragma unroll
+                    for (int hb = 0; hb < 2; ++hb) { // two 32-element Q8_0 blocks
+                        float amax = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            amax = fmaxf(amax, fabsf(x[32 * hb + i]));
+                        const float d = amax / 127.0f;
+                        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+                        const float dh = __half2float(__float2half_rn(d)); // the stored scale
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) // code * scale: exact in fp32
+                            x[32 * hb + i] = roundf(x[32 * hb + i] * id) * dh;
+                    }
+                }
+                uint32_t w[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const __half2 hh = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+                    w[i] = *reinterpret_cast<const uint32_t *>(&hh);
                 }
                 tmem_st32(lane_base + TM_Q + c0 / 2, w);
             }
@@ -460,6 +500,57 @@ __global__ void fill_map_kernel(uint8_t *map, size_t n, int n_kt, int n_kv) {
         map[i] = ((int)(i % n_kt) * pf::BN < n_kv) ? 1 : 0;
 }
 
+// Q8_0 / Q4_0 K or V rows (a ggml view: any byte strides, 2-byte aligned) ->
+// contiguous f16 rows [seq][kv head][row][D].  One thread per 8 elements
+// (a quarter of a 32-element block): value = code * f32(d) as ggml's to_float
+// computes it (exact in fp32: <= 8-bit code times an 11-bit scale), then one
+// round-to-nearest to f16; 16-byte stores.
+template <int T>
+__global__ void kv_to_f16_kernel(const uint8_t *__restrict__ src, int64_t nb1, int64_t nb2,
+                                 int64_t nb3, int D, int n_kv, int n_hkv, int64_t n_units,
+                                 __half *__restrict__ dst) {
+    const int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= n_units)
+        return;
+    const int per_row = D / 8;
+    const int64_t row = u / per_row; // [seq][kv head][row] order
+    const int c = (int)(u - row * per_row);
+    const int64_t r = row % n_kv, hh = (row / n_kv) % n_hkv, sq = row / ((int64_t)n_kv * n_hkv);
+    const uint8_t *rp = src + r * nb1 + hh * nb2 + sq * nb3;
+    const int b = c >> 2, part = c & 3;
+    constexpr int BB = T == kQ8 ? 34 : 18;
+    const uint8_t *blk = rp + BB * b;
+    const float d = h2f_bits(*reinterpret_cast<const uint16_t *>(blk));
+    float x[8];
+    if constexpr (T == kQ8) {
+        const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2 + 8 * part);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = p[i];
+            x[2 * i] = (float)(int)(int8_t)(w & 0xffu) * d;
+            x[2 * i + 1] = (float)(int)(int8_t)(w >> 8) * d;
+        }
+    } else {
+        // elements 0..15 are the low nibbles of bytes 0..15, 16..31 the high ones
+        const uint16_t *p = reinterpret_cast<const uint16_t *>(blk + 2 + 8 * (part & 1));
+        const int sh = 4 * (part >> 1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t w = p[i];
+            x[2 * i] = (float)((int)(((w & 0xffu) >> sh) & 15u) - 8) * d;
+            x[2 * i + 1] = (float)((int)(((w >> 8) >> sh) & 15u) - 8) * d;
+        }
+    }
+    uint4 o;
+    uint32_t *ow = reinterpret_cast<uint32_t *>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 hv = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        ow[i] = *reinterpret_cast<const uint32_t *>(&hv);
+    }
+    *reinterpret_cast<uint4 *>(dst + row * D + 8 * c) = o;
+}
+
 // ---------------------------------------------------------------------------
 // host side
 
@@ -478,24 +569,64 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 
 void *tensor_map_encoder() { return reinterpret_cast<void *>(get_encode()); }
 
-size_t prefill_map_bytes(const PrefillShape &ps) {
+static size_t map_bytes(const PrefillShape &ps) {
     const size_t n_qt = (ps.n_q + pf::BM - 1) / pf::BM, n_kt = (ps.n_kv + pf::BN - 1) / pf::BN;
     return ((size_t)ps.m_planes * n_qt * n_kt + 255) / 256 * 256 + 256;
 }
 
-cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, const char **why) {
+// f16 copy of one of K / V: [n_seq_kv][n_head_kv][n_kv][D], 256-byte multiple
+static size_t f16_copy_bytes(const PrefillShape &ps) {
+    return ((size_t)ps.n_seq_kv * ps.n_head_kv * ps.n_kv * ps.D * 2 + 255) / 256 * 256;
+}
+
+size_t prefill_ws_bytes(const PrefillShape &ps) {
+    return map_bytes(ps) + (ps.kv_type == kF16 ? 0 : 2 * f16_copy_bytes(ps));
+}
+
+static cudaError_t launch_kv_to_f16(int type, const void *src, const int64_t *nb,
+                                    const PrefillShape &ps, __half *dst, cudaStream_t st) {
+    const int64_t n_units = (int64_t)ps.n_seq_kv * ps.n_head_kv * ps.n_kv * (ps.D / 8);
+    const unsigned blocks = (unsigned)((n_units + 255) / 256);
+    const uint8_t *s8 = static_cast<const uint8_t *>(src);
+    if (type == kQ8)
+        kv_to_f16_kernel<kQ8><<<blocks, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.D, ps.n_kv,
+                                                       ps.n_head_kv, n_units, dst);
+    else
+        kv_to_f16_kernel<kQ4><<<blocks, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.D, ps.n_kv,
+                                                       ps.n_head_kv, n_units, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill(const PrefillShape &ps_in, void *ws, cudaStream_t st, const char **why) {
     auto encode = get_encode();
     if (!encode) {
         *why = "cuTensorMapEncodeTiled unavailable";
         return cudaErrorNotSupported;
     }
+    PrefillShape ps = ps_in;
     const int D = ps.D;
     const int n_qt = (ps.n_q + pf::BM - 1) / pf::BM, n_kt = (ps.n_kv + pf::BN - 1) / pf::BN;
     uint8_t *map = static_cast<uint8_t *>(ws);
-    int *err = reinterpret_cast<int *>(map + prefill_map_bytes(ps) - 256);
+    int *err = reinterpret_cast<int *>(map + map_bytes(ps) - 256);
     cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), st);
     if (e != cudaSuccess)
         return e;
+    const bool quant = ps.kv_type != kF16;
+    if (quant) {
+        // K and V widened once into the workspace; the kernel then reads them
+        // through the same tensor maps as an F16 cache
+        __half *k16 = reinterpret_cast<__half *>(map + map_bytes(ps));
+        __half *v16 = reinterpret_cast<__half *>(map + map_bytes(ps) + f16_copy_bytes(ps));
+        if ((e = launch_kv_to_f16(ps.kv_type, ps.k, ps.k_nb, ps, k16, st)) != cudaSuccess ||
+            (e = launch_kv_to_f16(ps.kv_type, ps.v, ps.v_nb, ps, v16, st)) != cudaSuccess)
+            return e;
+        const int64_t nb[4] = {2, 2 * (int64_t)D, 2 * (int64_t)D * ps.n_kv,
+                               2 * (int64_t)D * ps.n_kv * ps.n_head_kv};
+        ps.k = k16;
+        ps.v = v16;
+        for (int i = 0; i < 4; ++i)
+            ps.k_nb[i] = ps.v_nb[i] = nb[i];
+    }
     const int planes = ps.m_planes;
     if (ps.mask) {
         dim3 g(n_kt, n_qt, planes);
@@ -553,18 +684,20 @@ cudaError_t launch_prefill(const PrefillShape &ps, void *ws, cudaStream_t st, co
     a.scale_log2 = ps.scale * 1.4426950408889634f;
     const size_t smem = 1024 + (size_t)pf::nslot(D) * pf::BN * D * 2 + 256;
     dim3 grid((unsigned)(n_qt * ps.n_head * ps.n_seq));
-    static std::atomic<unsigned long long> attr_done[2];
-    if (D == 256) {
-        e = set_smem_limit((const void *)fa_prefill_kernel<256>, smem, attr_done[1]);
-        if (e != cudaSuccess)
-            return e;
-        fa_prefill_kernel<256><<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
-    } else {
-        e = set_smem_limit((const void *)fa_prefill_kernel<128>, smem, attr_done[0]);
-        if (e != cudaSuccess)
-            return e;
-        fa_prefill_kernel<128><<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
-    }
+    static std::atomic<unsigned long long> attr_done[4];
+    auto go = [&](auto kern, int slot) {
+        cudaError_t r = set_smem_limit((const void *)kern, smem, attr_done[slot]);
+        if (r != cudaSuccess)
+            return r;
+        kern<<<grid, pf::NT, smem, st>>>(maps[0], maps[1], a);
+        return cudaSuccess;
+    };
+    if (D == 256)
+        e = quant ? go(fa_prefill_kernel<256, true>, 3) : go(fa_prefill_kernel<256, false>, 1);
+    else
+        e = quant ? go(fa_prefill_kernel<128, true>, 2) : go(fa_prefill_kernel<128, false>, 0);
+    if (e != cudaSuccess)
+        return e;
     return cudaGetLastError();
 }
 
