@@ -22,6 +22,9 @@
  *   xq_gated_delta_net_ws the same op in chunked form for long prefill (the
  *                         CPU op's per-token loop, ops.cpp of the snapshot,
  *                         restated as 64-token WY chunks on the tensor cores)
+ *   xq_gated_delta_net_heads  the same op over a block of value heads (the
+ *                         D3D12 dispatch over value heads,
+ *                         src/bridge/ggml_d3d12.cpp:1937, cut by head)
  *   xq_attend_range       RemoteAttnEngine::attend_range
  *                         (uwp/rkva/remote-attn-engine.h:152-154,
  *                          remote-attn-engine.cpp:2774-3251)
@@ -236,6 +239,27 @@ int xq_gated_delta_net_ws(const xq_tensor *q, const xq_tensor *k, const xq_tenso
                           const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
                           float *dst, int32_t slots, void *workspace, size_t workspace_bytes,
                           xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* GATED_DELTA_NET over a block of value heads: the op sharded by value    */
+/* head across GPUs (one process per GPU, no exchange step).  The block is */
+/* value heads [head_begin, head_begin + v->ne[1]) of an op with            */
+/* n_head_total value heads (n_head_total % H_k == 0): v, g, beta, state    */
+/* and dst cover the block only (their head dims hold v->ne[1] heads; dst   */
+/* is the block's y [n_seq][T][block][S] then its snapshot slots            */
+/* [n_seq][block][S][S]); q and k are the op's full key-head tensors, and   */
+/* block head j reads key head (head_begin + j) % H_k -- the mapping of the */
+/* whole op (the reference's h mod H_k, src/bridge/ggml_d3d12.cpp:143), so  */
+/* every block's outputs equal the whole op's outputs for its heads bit for */
+/* bit.  Workspace and kernel choice as xq_gated_delta_net_ws, sized by    */
+/* xq_gated_delta_net_workspace(v, slots) of the block's v.  The reference  */
+/* runs the op on one device (Dispatch(32, 1, 16) over the value heads,     */
+/* src/bridge/ggml_d3d12.cpp:1937); this is that dispatch cut by head.      */
+/* ------------------------------------------------------------------------ */
+int xq_gated_delta_net_heads(const xq_tensor *q, const xq_tensor *k, const xq_tensor *v,
+                             const xq_tensor *g, const xq_tensor *beta, const xq_tensor *state,
+                             float *dst, int32_t slots, int64_t head_begin, int64_t n_head_total,
+                             void *workspace, size_t workspace_bytes, xq_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* GGML_OP_SET_ROWS (quantize-on-append into the KV cache).  src F32         */

@@ -52,7 +52,8 @@ class RangeArgs(C.Structure):
 class GdnArgs(C.Structure):
     _fields_ = [("q", Tensor), ("k", Tensor), ("v", Tensor), ("g", Tensor), ("beta", Tensor),
                 ("state", Tensor), ("dst", C.c_void_p), ("slots", C.c_int),
-                ("n_workers", C.c_int), ("lanes8", C.c_int)]
+                ("n_workers", C.c_int), ("lanes8", C.c_int), ("head_begin", C.c_int64),
+                ("n_head_total", C.c_int64)]
 
 
 _lib = None
@@ -283,10 +284,13 @@ def set_rows(cache: np.ndarray, src: np.ndarray, idx: np.ndarray, ty: int) -> np
 # ----------------------------------------------------------------------------
 # GATED_DELTA_NET
 
-def gated_delta_net(q, k, v, g, beta, state, slots=1, lanes8=False, n_workers=None):
+def gated_delta_net(q, k, v, g, beta, state, slots=1, lanes8=False, n_workers=None,
+                    head_begin=0, n_head_total=0):
     """q, k: (n_seq_qk, T, H_k, S) ; v: (n_seq, T, H, S) ; g, beta: (n_seq, T, H, 1);
     state: (n_seq, H, S, S) [col][i].  Returns (dst_flat, y, snapshots) with
-    y (n_seq, T, H, S) and snapshots (K, n_seq, H, S, S)."""
+    y (n_seq, T, H, S) and snapshots (K, n_seq, H, S, S).  head_begin /
+    n_head_total: v, g, beta, state hold value heads [head_begin, head_begin +
+    H) of an op with n_head_total heads (0: the whole op)."""
     n_seq, T, H, S = v.shape
     a = GdnArgs()
     a.q, a.k, a.v = dense_tensor(q), dense_tensor(k), dense_tensor(v)
@@ -298,6 +302,7 @@ def gated_delta_net(q, k, v, g, beta, state, slots=1, lanes8=False, n_workers=No
     a.slots = slots
     a.n_workers = n_workers or os.cpu_count() or 1
     a.lanes8 = int(lanes8)
+    a.head_begin, a.n_head_total = head_begin, n_head_total
     rc = lib().xqr_gated_delta_net(C.byref(a))
     if rc:
         raise ValueError(f"xqr_gated_delta_net rejected the shapes ({rc})")

@@ -847,7 +847,7 @@ int xqr_range_attn(const xqr_range_args *a) {
 
 typedef struct {
     const xqr_gdn_args *a;
-    int64_t S_k, H_k, S_v, H, T, n_seq, rq3, rk3;
+    int64_t S_k, H_k, S_v, H, T, n_seq, rq3, rk3, h_off;
     float scale;
     size_t slot_floats;
 } gdn_ctx;
@@ -868,7 +868,7 @@ static void gdn_job(void *p, int64_t unit, int w) {
     const xqr_gdn_args *a = c->a;
     const int64_t h = unit % c->H, s = unit / c->H;
     const int64_t S_v = c->S_v, S_k = c->S_k;
-    const int64_t hk = h % c->H_k;
+    const int64_t hk = (h + c->h_off) % c->H_k;
     const int64_t sq = s / c->rq3, sk = s / c->rk3;
     float *st = (float *)malloc((size_t)S_v * S_k * 4);
     const float *init = (const float *)((const uint8_t *)a->state.data + s * a->state.nb[3] +
@@ -929,9 +929,12 @@ int xqr_gated_delta_net(const xqr_gdn_args *a) {
     c.H = a->v.ne[1];
     c.T = a->v.ne[2];
     c.n_seq = a->v.ne[3];
-    if (c.S_k != c.S_v || a->k.ne[0] != c.S_k || a->k.ne[1] != c.H_k || c.H % c.H_k ||
-        a->slots < 1 || a->q.ne[2] != c.T || c.n_seq % a->q.ne[3] || c.n_seq % a->k.ne[3])
+    const int64_t total = a->n_head_total > 0 ? a->n_head_total : c.H;
+    if (c.S_k != c.S_v || a->k.ne[0] != c.S_k || a->k.ne[1] != c.H_k || total % c.H_k ||
+        a->head_begin < 0 || a->head_begin + c.H > total || a->slots < 1 ||
+        a->q.ne[2] != c.T || c.n_seq % a->q.ne[3] || c.n_seq % a->k.ne[3])
         return -1;
+    c.h_off = a->head_begin % c.H_k;
     c.rq3 = c.n_seq / a->q.ne[3];
     c.rk3 = c.n_seq / a->k.ne[3];
     c.scale = 1.0f / sqrtf((float)c.S_v);

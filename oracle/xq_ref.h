@@ -113,6 +113,10 @@ typedef struct {
     int slots;      /* op_params[0]: K >= 1 */
     int n_workers;
     int lanes8;     /* 1: eight-lane tree reductions of the D3D12 host mirror */
+    /* v, g, beta, state, dst hold value heads [head_begin, head_begin + H) of
+     * an op with n_head_total value heads (0: the whole op); head j of the
+     * block reads key head (head_begin + j) % H_k, the fork's h mod H_k. */
+    int64_t head_begin, n_head_total;
 } xqr_gdn_args;
 
 int xqr_gated_delta_net(const xqr_gdn_args *a);

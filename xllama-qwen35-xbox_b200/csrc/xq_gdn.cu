@@ -29,7 +29,7 @@ __global__ void __launch_bounds__(CB * 8) gdn_recurrent_kernel(const GdnArgs a) 
     const int h = unit % a.H, seq = unit / a.H;
     const int col = blockIdx.y * CB + threadIdx.x / TPC;
     const int l = threadIdx.x % TPC;
-    const int hk = h % a.H_k;
+    const int hk = (h + a.h_off) % a.H_k;
     const int sq = seq / a.rq3, sk = seq / a.rk3;
 
     const char *st_row = reinterpret_cast<const char *>(a.state) + seq * a.s_nb3 +
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(CB * TPC) gdn_stream_kernel(const GdnArgs a) {
     const int h = blockIdx.x % a.H, seq = blockIdx.x / a.H;
     const int col0 = blockIdx.y * CB, cc = tid / TPC, col = col0 + cc;
     const int l = tid % TPC;
-    const int hk = h % a.H_k;
+    const int hk = (h + a.h_off) % a.H_k;
     const int sq = seq / a.rq3, sk = seq / a.rk3;
 
     // state row `col`, elements 4l + 4 TPC j + x held as float2 pairs st[2j], st[2j+1]

@@ -121,6 +121,7 @@ struct GdnChunkArgs {
     float *state_out; // [n_seq][H][128][128]
     int *err;
     int H, H_k, T, n_seq, rq3, rk3, NC;
+    int h_off; // global index of value head 0 (key head of h: (h + h_off) % H_k)
     float scale;
 };
 
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(gc::PREP_NT, 3)
     const int c = (int)(blockIdx.x / (unsigned)a.H), x = (int)(blockIdx.x % (unsigned)a.H);
     const int J = a.H % a.H_k == 0 ? a.H / a.H_k : 1;
     const int h = J > 1 ? (x % J) * a.H_k + x / J : x, n = blockIdx.z;
-    const int hk = h % a.H_k, t0 = c * C;
+    const int hk = (h + a.h_off) % a.H_k, t0 = c * C;
     const size_t unit = ((size_t)n * a.H + h) * a.NC + c;
     const uint32_t bar_tma = smem_u32(bars), bar_mma = smem_u32(bars + 1);
 
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(gc::SCAN_NT, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int slice = blockIdx.x, h = blockIdx.y, n = blockIdx.z;
-    const int j0 = slice * R, hk = h % a.H_k;
+    const int j0 = slice * R, hk = (h + a.h_off) % a.H_k;
     const size_t unit0 = ((size_t)n * a.H + h) * a.NC;
 
     if (tid == 0) {
@@ -923,6 +924,7 @@ cudaError_t launch_gdn_chunked(const GdnArgs &a, void *ws, size_t ws_bytes, cuda
     c.state_out = tail ? handoff : a.dst + (size_t)SK * a.H * a.T * a.n_seq; // snapshot slot 0
     c.H = a.H;
     c.H_k = a.H_k;
+    c.h_off = a.h_off;
     c.T = a.T;
     c.n_seq = a.n_seq;
     c.rq3 = a.rq3;

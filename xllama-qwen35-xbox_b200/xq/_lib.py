@@ -23,7 +23,7 @@ EXPORTS = (
     "xq_gated_delta_net_workspace", "xq_gated_delta_net_ws",
     "xq_attend_range_kvarn4_workspace", "xq_attend_range_kvarn4",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
-    "xq_flash_attn_ext_noalloc", "xq_set_rows",
+    "xq_flash_attn_ext_noalloc", "xq_set_rows", "xq_gated_delta_net_heads",
 )
 
 
@@ -79,6 +79,7 @@ def lib():
         "xq_attend_range_kvarn4": (C.c_int, [P(Kvarn4Desc), vp, vp, u32, u32, u32, vp, vp,
                                              C.c_float, vp, vp, vp, sz, vp]),
         "xq_gated_delta_net_ws": (C.c_int, [P(Tensor)] * 6 + [vp, i32, vp, sz, vp]),
+        "xq_gated_delta_net_heads": (C.c_int, [P(Tensor)] * 6 + [vp, i32, i64, i64, vp, sz, vp]),
         "xq_dequantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_quantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_flash_attn_ext_noalloc": (C.c_int, [P(FaParams), vp]),

@@ -258,13 +258,17 @@ def attend_range_kvarn4(k_plane: torch.Tensor, v_plane: torch.Tensor, q: torch.T
 
 
 def gated_delta_net(q, k, v, g, beta, state, slots: int = 1, out=None, stream=None,
-                    chunked: bool = True):
+                    chunked: bool = True, head_begin: int | None = None,
+                    n_head_total: int | None = None):
     """GGML_OP_GATED_DELTA_NET.  q, k (n_seq_qk, T, H_k, S); v (n_seq, T, H, S);
     g, beta (n_seq, T, H, 1); state (n_seq, H, S, S).  Returns
     (dst_flat, y (n_seq, T, H, S), snapshots (K, n_seq, H, S, S)).
     chunked: long sequences take the tensor-core chunked form
     (xq_gated_delta_net_ws, TF32 products); False keeps the per-token FP32
-    recurrence (xq_gated_delta_net) at every length."""
+    recurrence (xq_gated_delta_net) at every length.
+    head_begin / n_head_total: v, g, beta, state hold value heads
+    [head_begin, head_begin + H) of an op with n_head_total value heads (the
+    op sharded by value head, xq_gated_delta_net_heads); q, k stay whole."""
     n_seq, T, H, S = v.shape
     n_y = S * H * T * n_seq
     n_snap = slots * S * S * H * n_seq
@@ -272,7 +276,15 @@ def gated_delta_net(q, k, v, g, beta, state, slots: int = 1, out=None, stream=No
                                                   device=v.device)
     ts = [_dense(t) for t in (q, k, v, g, beta, state)]
     refs = [C.byref(t) for t in ts]
-    if chunked:
+    if head_begin is not None:
+        nbytes = lib().xq_gated_delta_net_workspace(refs[2], slots)
+        ws = _workspace(nbytes, v.device)
+        check(lib().xq_gated_delta_net_heads(*refs, dst.data_ptr(), slots, head_begin,
+                                             n_head_total if n_head_total is not None else H,
+                                             ws.data_ptr() if ws is not None else None,
+                                             ws.numel() if ws is not None else 0,
+                                             _stream(stream)))
+    elif chunked:
         nbytes = lib().xq_gated_delta_net_workspace(refs[2], slots)
         ws = _workspace(nbytes, v.device)
         check(lib().xq_gated_delta_net_ws(*refs, dst.data_ptr(), slots,

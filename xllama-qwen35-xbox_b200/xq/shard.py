@@ -1,4 +1,18 @@
-"""KV-sharded flash decode over several GPUs (one process per GPU).
+"""The hot path spread over several GPUs (one process per GPU).
+
+Three partitions, one per op shape:
+  * decode (FLASH_ATTN_EXT, one query): KV rows sharded (below);
+  * GATED_DELTA_NET: value heads sharded (`head_block`, `gdn_heads`): rank r
+    runs value heads head_block(H, world, r) through xq_gated_delta_net_heads
+    with the whole q/k (each value head h reads key head h % H_k); outputs and
+    state stay sharded -- there is no exchange step (`gather_heads` is the
+    optional all-gather of y when a caller wants it whole);
+  * prefill (FLASH_ATTN_EXT, many queries): KV-head groups (`prefill_block`):
+    up to n_head_kv ranks take blocks of KV heads with their query heads;
+    beyond that each KV head's query rows are cut into blocks of equal causal
+    work (whole 128-row tiles); outputs are disjoint, no exchange step.
+
+KV-sharded flash decode:
 
 The KV rows of every sequence are cut into a fixed global list of splits of
 `rows_per_split` rows, and the splits into a fixed list of `n_groups` groups
@@ -88,3 +102,117 @@ def sharded_flash_decode(q, k_local, v_local, k_type: int, rows_per_split: int, 
                         scale)
     records = records_fn(local, per_group)
     return merge_fn(gather_partials(records, n_groups, group))
+
+
+# ---------------------------------------------------------------------------
+# GATED_DELTA_NET sharded by value head
+
+def head_block(n_head: int, world: int, rank: int) -> tuple[int, int]:
+    """[begin, end) of the value heads `rank` owns: contiguous blocks."""
+    return split_block(n_head, world, rank)
+
+
+def key_heads(h0: int, h1: int, n_head_kv: int) -> list[int]:
+    """The key heads value heads [h0, h1) read (h % n_head_kv)."""
+    return sorted({h % n_head_kv for h in range(h0, h1)})
+
+
+def gdn_heads(q, k, v, g, beta, state, slots: int = 1, world: int = 1, rank: int = 0,
+              out=None, stream=None):
+    """This rank's share of one GATED_DELTA_NET op sharded by value head.
+    q, k: the whole (n_seq, T, H_k, S) key tensors; v, g, beta, state: the
+    whole op's tensors (this rank's head block is viewed out of them, no
+    copy).  Returns (dst, y (n_seq, T, h1 - h0, S), snapshots) of heads
+    [h0, h1) = head_block(H, world, rank), bit-identical to the same heads of
+    the unsharded op."""
+    from . import ops
+    H = v.shape[2]
+    h0, h1 = head_block(H, world, rank)
+    return ops.gated_delta_net(q, k, v[:, :, h0:h1], g[:, :, h0:h1], beta[:, :, h0:h1],
+                               state[:, h0:h1], slots=slots, out=out, stream=stream,
+                               head_begin=h0, n_head_total=H)
+
+
+def gather_heads(y_local, n_head: int, group=None):
+    """All-gather every rank's y block (n_seq, T, h1 - h0, S) into the whole
+    (n_seq, T, n_head, S) on every rank (the optional exchange after a
+    head-sharded GATED_DELTA_NET)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    blocks = [head_block(n_head, world, r) for r in range(world)]
+    longest = max(e - b for b, e in blocks)
+    n_seq, T, _, S = y_local.shape
+    pad = torch.zeros((n_seq, T, longest, S), dtype=y_local.dtype, device=y_local.device)
+    pad[:, :, : y_local.shape[2]] = y_local
+    bufs = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(bufs, pad.contiguous(), group=group)
+    return torch.cat([bufs[r][:, :, : e - b] for r, (b, e) in enumerate(blocks)], dim=2)
+
+
+# ---------------------------------------------------------------------------
+# FLASH_ATTN_EXT prefill sharded by KV-head group
+
+def prefill_block(n_head: int, n_head_kv: int, n_q: int, n_kv: int, world: int, rank: int,
+                  causal: bool = True, tile: int = 128):
+    """(head range, kv-head range, query-row range) of `rank` for one
+    prefill FLASH_ATTN_EXT sharded by KV-head group.
+
+    world <= n_head_kv: contiguous blocks of KV heads (n_head_kv % world ==
+    0), each with its G = n_head / n_head_kv query heads and every query row.
+    world > n_head_kv (world % n_head_kv == 0): rank r serves KV head
+    r // parts (parts = world / n_head_kv) and its query heads, over one of
+    `parts` blocks of query rows with equal attention work -- under a causal
+    mask over the tail of the cache, row i sees n_kv - n_q + i + 1 keys --
+    cut at whole `tile`-row query tiles, so each block computes exactly the
+    tiles the unsharded kernel computes for those rows (bit-identical)."""
+    G = n_head // n_head_kv
+    if world <= n_head_kv:
+        if n_head_kv % world:
+            raise ValueError(f"{n_head_kv} KV heads do not split over {world} ranks")
+        b, e = split_block(n_head_kv, world, rank)
+        return (b * G, e * G), (b, e), (0, n_q)
+    if world % n_head_kv:
+        raise ValueError(f"{world} ranks are not a multiple of {n_head_kv} KV heads")
+    parts = world // n_head_kv
+    kvh, part = divmod(rank, parts)
+    n_tiles = (n_q + tile - 1) // tile
+
+    def cost(t):  # attention work of query tile t (keys seen, summed over its rows)
+        r0, r1 = t * tile, min(n_q, (t + 1) * tile)
+        if not causal:
+            return (r1 - r0) * n_kv
+        off = n_kv - n_q
+        return sum(min(n_kv, off + i + 1) for i in range(r0, r1))
+    costs = [cost(t) for t in range(n_tiles)]
+    total = float(sum(costs))
+    cuts, acc, t = [0], 0.0, 0
+    for p in range(1, parts):
+        while t < n_tiles and acc + costs[t] / 2 < total * p / parts:
+            acc += costs[t]
+            t += 1
+        cuts.append(t)
+    cuts.append(n_tiles)
+    r0, r1 = cuts[part] * tile, min(n_q, cuts[part + 1] * tile)
+    return (kvh * G, (kvh + 1) * G), (kvh, kvh + 1), (r0, r1)
+
+
+def prefill_part(q, k, v, k_type: int, mask=None, world: int = 1, rank: int = 0,
+                 scale: float = 1.0, out=None, stream=None):
+    """This rank's share of one prefill FLASH_ATTN_EXT sharded by KV-head
+    group: views of the whole q (n_seq, n_head, n_q, D), caches (n_seq_kv,
+    n_kv, n_head_kv, row_bytes) and mask (m3, 1, >= n_q, n_kv) -- the mask
+    must broadcast over heads, as llama.cpp's KQ mask does -- through one
+    xq_flash_attn_ext call.  Returns (out (n_seq, r1 - r0, h1 - h0, D),
+    ((h0, h1), (c0, c1), (r0, r1)))."""
+    from . import ops
+    n_seq, n_head, n_q, D = q.shape
+    n_kv, n_hkv = k.shape[1], k.shape[2]
+    if mask is not None and mask.shape[1] != 1:
+        raise ValueError("a head-sharded prefill needs a mask that broadcasts over heads")
+    plan = prefill_block(n_head, n_hkv, n_q, n_kv, world, rank, causal=mask is not None)
+    (h0, h1), (c0, c1), (r0, r1) = plan
+    m = mask[:, :, r0:r1] if mask is not None else None
+    o = ops.flash_attn_ext(q[:, h0:h1, r0:r1], k[:, :, c0:c1], v[:, :, c0:c1], k_type,
+                           mask=m, scale=scale, out=out, stream=stream)
+    return o, plan
