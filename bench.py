@@ -2,7 +2,7 @@
 """Benchmark of the B200 attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c5|kvw|kv4]
+                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c4q8|c4q4|c5|kvw|kv4]
 
 Workloads (seeded synthetic tensors, random data of the
 stated distributions -- no datasets are involved):
@@ -15,8 +15,17 @@ stated distributions -- no datasets are involved):
   c3a  config 3 decode: GATED_DELTA_NET, 8 sequences x 1 token, 32 v-heads /
        16 k-heads, d 128 (fp32 state read + written; 9 rotated sets).
   c3b  config 3 prefill: GATED_DELTA_NET, 1 sequence x 4096 tokens.
+       With N > 1 both shard the op by value head (each GPU its block of the
+       32 heads, whole q/k, no exchange step; strong scaling) and the line
+       carries `scaling_reference`, the unsharded op on rank 0's GPU.
   c4   config 4: causal prefill, 8192 tokens, 24 Q / 4 KV heads, D=256, F16
        K/V, explicit causal F16 mask (tensor-core kernel); metric TFLOP/s.
+  c4q8 / c4q4  the config-4 shape over a Q8_0 / Q4_0 cache (the reference's
+       product configuration): K/V widened to f16 by the library's pre-pass
+       inside every step, q quantized to Q8_0 as ggml-cpu does.
+       With N > 1 the prefill rows shard by KV-head group (up to 4 GPUs take
+       one KV head group each; at 8, each KV head's query rows are cut in two
+       blocks of equal causal work), strong scaling, with `scaling_reference`.
   kvw  KV-cache write (GGML_OP_SET_ROWS, the row after the hot path): a
        prefill batch of 8192 tokens x 4 KV heads x D=256, K and V, quantized
        to Q8_0 into 32768-row caches (4 rotated input sets > 2 x L2).
@@ -31,12 +40,17 @@ stated distributions -- no datasets are involved):
        and merged in group order (bit-identical for any GPU count dividing 8).
        Default for N > 1 ("strong" scaling: total work fixed); those lines
        also carry `scaling_reference`, config 5 timed on one GPU in the same
-       run (the N = 1 point of the series).
+       run (the N = 1 point of the series), with `bit_identical_to_n_gpus`:
+       the KV rows are generated per global group, so the one-GPU output and
+       the N-GPU output are compared bit for bit.
 A step = the attention kernels of one decode step over that workload.
 `value` is KV GB/s (algorithmic bytes: K + V + q + out per step) with inputs
 resident; `e2e` is the same metric through the public call xq.flash_attn_ext
 with q and the output in pinned host memory (q copied to the GPU by the
-library's staging kernel, the result written back over PCIe) every step.
+library's staging kernel, the result written back over PCIe) every step,
+replayed from a CUDA graph; `e2e_eager` makes the same calls eagerly, one
+prebuilt C-ABI call per step, so the library's per-call host work (as the
+ggml backend's graph_compute pays it) is inside the timed region.
 --impl reference times the reference's CPU algorithm (the ggml-cpu
 restatement in oracle/, all host threads) on the same workload.
 """
@@ -137,6 +151,20 @@ C3 = dict(S=128, H=32, H_k=16, slots=1)
 C4 = dict(n_head=24, n_hkv=4, D=256, n_q=8192)
 TYPE_NAMES = {0: "f32", 1: "f16", 2: "q4_0", 8: "q8_0"}
 C5 = dict(n_head=24, n_hkv=4, D=256, n_kv=262144, n_seq=8)
+WORKLOAD_NAMES = {
+    "c1": "BASELINE config 1 (F16 decode, kv 4096)",
+    "c2": "BASELINE config 2 (Q8_0 decode, kv 32768)",
+    "c2q4": "BASELINE config 2, Q4_0 variant",
+    "c5": "BASELINE config 5 (8 x 262144 Q8_0, KV-sharded)",
+    "c3a": "BASELINE config 3 decode (GDN, 8 seqs x 1 token)",
+    "c3b": "BASELINE config 3 prefill (GDN, 1 seq x 4096 tokens)",
+    "c4": "BASELINE config 4 (causal prefill, 8192 tokens, F16 KV)",
+    "c4q8": "BASELINE config 4 shape over a Q8_0 KV cache (causal prefill, 8192 tokens)",
+    "c4q4": "BASELINE config 4 shape over a Q4_0 KV cache (causal prefill, 8192 tokens)",
+    "kvw": "KV-cache write (SET_ROWS), 8192 tokens x 4 KV heads x D=256, K and V to Q8_0",
+    "kv4": "native KVarN4 range attention, 24 Q / 4 KV heads, D=256, 32768 rows past origin "
+           "102400, precision tail 128, 1 query",
+}
 
 
 def algo_bytes(w, ty):
@@ -201,17 +229,119 @@ def graph_timed(torch, fn, n, warmup, world=1, dist=None, dev=None, use_graph=Tr
     return t
 
 
-def run_ours(args, rank, world, torch, dist):
+def workload_config(workload, world=1):
+    """The `config` object of a JSON line: static facts of the workload (no
+    device query), the same in the repo arm and the reference arm."""
+    def l2_sets(step_bytes):
+        return max(4, math.ceil(2 * L2_BYTES / step_bytes) + 1)
+    if workload in ("c1", "c2", "c2q4", "c5"):
+        w = {"c5": C5, "c1": C1}.get(workload, C2)
+        ty = {"c2q4": 2, "c1": 1}.get(workload, 8)
+        kv, _ = algo_bytes(w, ty)
+        cfg = {"workload": WORKLOAD_NAMES[workload], "kv_type": TYPE_NAMES[ty],
+               "n_seq": w["n_seq"], "n_head": w["n_head"], "n_head_kv": w["n_hkv"],
+               "head_dim": w["D"], "kv_len": w["n_kv"],
+               "parallelism": f"kv-shard{world}" if world > 1 else "single"}
+        if workload == "c5":
+            cfg["l2"] = "inputs %.0f MB per GPU > L2" % (kv / world / 1e6)
+        else:
+            n = l2_sets(kv)
+            cfg["l2"] = "rotating %d input sets (%.0f MB > 2x L2)" % (n, n * kv / 1e6)
+        return cfg
+    if workload in ("c3a", "c3b"):
+        n_seq, T = (8, 1) if workload == "c3a" else (1, 4096)
+        b = gdn_bytes(n_seq, T)[0]
+        n = 1 if b > 2 * L2_BYTES else math.ceil(2 * L2_BYTES / b) + 1
+        return {"workload": WORKLOAD_NAMES[workload], "n_seq": n_seq, "tokens": T,
+                "v_heads": C3["H"], "k_heads": C3["H_k"], "head_dim": C3["S"],
+                "slots": C3["slots"],
+                "parallelism": f"value-head-shard{world}" if world > 1 else "single",
+                "l2": ("rotating %d input sets (%.0f MB > 2x L2)" % (n, n * b / 1e6)) if n > 1
+                      else "inputs %.0f MB > L2" % (b / 1e6)}
+    if workload in ("c4", "c4q8", "c4q4"):
+        w = C4
+        ty = {"c4q8": 8, "c4q4": 2}.get(workload, 1)
+        N, H, Hkv, D = w["n_q"], w["n_head"], w["n_hkv"], w["D"]
+        kv = 2 * N * Hkv * {1: 2 * D, 8: D // 32 * 34, 2: D // 32 * 18}[ty]
+        return {"workload": WORKLOAD_NAMES[workload], "kv_type": TYPE_NAMES[ty], "n_q": N,
+                "n_kv": N, "n_head": H, "n_head_kv": Hkv, "head_dim": D, "mask": "causal F16",
+                "flops_per_step": prefill_flops(N, H, D),
+                "parallelism": f"kv-head-group-shard{world}" if world > 1 else "single",
+                "l2": "inputs %.0f MB > L2" % ((N * H * D * 4 + kv + N * N * 2) / 1e6)}
+    if workload == "kvw":
+        n = 4
+        return {"workload": WORKLOAD_NAMES[workload], "cache_rows": KVW["rows"],
+                "l2": "rotating %d input sets (%.0f MB > 2x L2)" % (
+                    n, n * 2 * KVW["n_tok"] * KVW["n_hkv"] * KVW["D"] * 4 / 1e6)}
+    b = kvarn4_bytes()
+    n = max(4, math.ceil(2 * L2_BYTES / b) + 1)
+    return {"workload": WORKLOAD_NAMES[workload], "bytes_per_step": b,
+            "l2": "rotating %d plane sets (%.0f MB > 2x L2)" % (n, n * b / 1e6)}
+
+
+def eager_timed(torch, fn, n, warmup):
+    """Device time (ms) of n eager calls of fn (no graph: every call's host
+    work -- argument checks, planning, tensor-map encoding, launches -- sits
+    between the kernels, as it does for the ggml backend's graph_compute)."""
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(n):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def fa_eager_call(torch, q, k, v, ty, scale, n_splits, out):
+    """One prebuilt C-ABI call of xq_flash_attn_ext (the argument struct and
+    the workspace are built once, as a C caller keeps them), returned as a
+    zero-argument function: the eager e2e then times the library's own host
+    work plus one ctypes transition per step."""
+    import ctypes as C
+
+    import xq
+    from xq import _lib
+    from xq.ops import _fa_params, _stream, _workspace
+    p = _fa_params(q, k, v, ty, ty, None, None, out, scale, 0.0, 0.0, n_splits)
+    L = _lib.lib()
+    nbytes = L.xq_flash_attn_ext_workspace(C.byref(p))
+    ws = _workspace(nbytes, torch.device("cuda", torch.cuda.current_device()))
+    wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
+    fn, ref, st = L.xq_flash_attn_ext, C.byref(p), _stream(None)
+    keep = (p, ws, q, out)
+
+    def call():
+        rc = fn(ref, wsp, wsn, st)
+        if rc:
+            xq._lib.check(rc)
+        return keep
+    return call
+
+
+def make_kv_groups(torch, xq, w, ty, g0, g1, rows_per_group, seed_base, dev):
+    """KV rows of global groups [g0, g1), each group generated from its own
+    seed (seed_base + g): the same rows whichever GPU holds them."""
+    rb = xq.row_bytes(ty, w["D"])
+    out = torch.empty((w["n_seq"], (g1 - g0) * rows_per_group, w["n_hkv"], rb),
+                      dtype=torch.uint8, device=dev)
+    for g in range(g0, g1):
+        lo = (g - g0) * rows_per_group
+        out[:, lo:lo + rows_per_group] = make_kv(torch, xq, w, ty, rows_per_group,
+                                                 seed_base + g, dev)
+    return out
+
+
+def run_decode(args, rank, world, torch, dist, workload):
     import xq
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
-    workload = args.workload
-    if workload == "auto":
-        workload = "c2" if world == 1 else "c5"
     ty = {"c2q4": xq.Q4_0, "c1": xq.F16}.get(workload, xq.Q8_0)
     w = {"c5": C5, "c1": C1}.get(workload, C2)
     hbm, _, peak_kind = peaks()
-    st = torch.cuda.current_stream()
     D, H, Hkv, n_seq = w["D"], w["n_head"], w["n_hkv"], w["n_seq"]
     kv_bytes, step_bytes = algo_bytes(w, ty)
     n_rows_out = n_seq * H
@@ -222,24 +352,23 @@ def run_ours(args, rank, world, torch, dist):
         per_group = n_splits // n_groups
         gb, ge = shard.split_block(n_groups, world, rank)
         sb, se = gb * per_group, ge * per_group
-        local_rows = (se - sb) * rows_per_split
-        # each GPU holds only its block of KV rows; global row r = sb*1024 + local r
-        k = make_kv(torch, xq, w, ty, local_rows, 1000 + rank, dev)
-        v = make_kv(torch, xq, w, ty, local_rows, 2000 + rank, dev)
+        # each GPU holds only its groups' rows, generated per group (seeded by
+        # global group), so any GPU count sees the same KV cache
+        rpg = per_group * rows_per_split
+        k = make_kv_groups(torch, xq, w, ty, gb, ge, rpg, 1000, dev)
+        v = make_kv_groups(torch, xq, w, ty, gb, ge, rpg, 2000, dev)
         sets = [(k, v)]
-        local_split_rows = rows_per_split
     else:
         n_sets = max(4, math.ceil(2 * L2_BYTES / kv_bytes) + 1)
         sets = [(make_kv(torch, xq, w, ty, w["n_kv"], 10 + 2 * i, dev),
                  make_kv(torch, xq, w, ty, w["n_kv"], 11 + 2 * i, dev)) for i in range(n_sets)]
-        rows_per_split = None
     gq = torch.Generator(device=dev)
     gq.manual_seed(7)
     qs = [torch.randn((n_seq, H, 1, D), generator=gq, device=dev) for _ in sets]
     scale = 1.0 / math.sqrt(D)
 
-    # plan: automatic split count for the single-GPU decode
     if workload != "c5":
+        # the library's automatic plan (about two CTAs per SM in one wave)
         sm = torch.cuda.get_device_properties(dev).multi_processor_count
         n_splits = max(1, min(math.ceil(2 * sm / (Hkv * n_seq)), math.ceil(w["n_kv"] / 64)))
         rows_per_split = math.ceil(w["n_kv"] / n_splits)
@@ -247,7 +376,6 @@ def run_ours(args, rank, world, torch, dist):
         sb, se = 0, n_splits
     part_local = torch.empty((se - sb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     if workload == "c5":
-        # two-level merge: local group records, gathered, merged in group order
         rec_local = torch.empty((ge - gb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
         rec_all = torch.empty((n_groups, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     out = torch.empty((n_rows_out, D), dtype=torch.float32, device=dev)
@@ -270,10 +398,8 @@ def run_ours(args, rank, world, torch, dist):
         if "merge" in parts:
             xq.lse_merge(src, out=out, want_lse=False)
 
-    use_graph = os.environ.get("XQ_BENCH_NO_GRAPH", "0") != "1"
-
     def timed(fn, n):
-        return graph_timed(torch, fn, n, args.warmup, world, dist, dev, use_graph)
+        return graph_timed(torch, fn, n, args.warmup, world, dist, dev)
 
     clk = ClockSampler(dev.index)
     clk.start()
@@ -288,6 +414,7 @@ def run_ours(args, rank, world, torch, dist):
     q_host.copy_(qs[0].cpu())
     o_host = torch.empty((n_seq, 1, H, D), dtype=torch.float32, pin_memory=True)
     q_dev = torch.empty_like(qs[0])
+    eager_ms = None
     if workload != "c5":
 
         def e2e_step(i):
@@ -296,6 +423,10 @@ def run_ours(args, rank, world, torch, dist):
             # PCIe every step
             k, v = sets[i % len(sets)]
             xq.flash_attn_ext(q_host, k, v, ty, scale=scale, n_splits=n_splits, out=o_host)
+        calls = [fa_eager_call(torch, q_host, k_, v_, ty, scale, n_splits, o_host)
+                 for k_, v_ in sets]
+        eager_ms = eager_timed(torch, lambda i: calls[i % len(calls)](), args.steps,
+                               args.warmup) / args.steps
     else:
         def e2e_step(i):
             q_dev.copy_(q_host, non_blocking=True)
@@ -304,21 +435,23 @@ def run_ours(args, rank, world, torch, dist):
             o_host.view(-1).copy_(out.view(-1), non_blocking=True)
     e2e_ms = timed(e2e_step, args.steps) / args.steps
 
-    # the N = 1 point of the config-5 series, measured in the same run: the
-    # default N = 1 line is config 2, so a scaling series read across the
-    # default lines would mix workloads
+    # the N = 1 point of the config-5 series, measured in the same run (the
+    # default N = 1 line is config 2), and the bit-identity of the N-GPU output
     ref1 = None
     if workload == "c5" and world > 1:
+        step(0)
+        torch.cuda.synchronize()
         if rank == 0:
-            ref1 = c5_single_gpu(torch, xq, dev, ty, args.steps, args.warmup, step_bytes)
+            ref1, out1 = c5_single_gpu(torch, xq, dev, ty, args.steps, args.warmup, step_bytes)
+            ref1["bit_identical_to_n_gpus"] = bool(torch.equal(out1, out))
+            del out1
         dist.barrier()
     if rank != 0:
         return None
     value = step_bytes / (ms * 1e-3) / 1e9
     local_kv = kv_bytes / world
     achieved = (local_kv + (step_bytes - kv_bytes) / 2) / (dec_ms * 1e-3) / 1e9
-    kname = f"fa_decode_{workload}"
-    traffic = profile_traffic(kname)
+    traffic = profile_traffic(f"fa_decode_{workload}")
     line = {
         "metric": "flash-decode KV GB/s", "value": round(value, 2), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -326,17 +459,10 @@ def run_ours(args, rank, world, torch, dist):
         "scaling": "strong" if workload == "c5" else "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1), ggml reference quantizer)",
-        "config": {"workload": {"c1": "BASELINE config 1 (F16 decode, kv 4096)",
-                                "c2": "BASELINE config 2 (Q8_0 decode, kv 32768)",
-                                "c2q4": "BASELINE config 2, Q4_0 variant",
-                                "c5": "BASELINE config 5 (8 x 262144 Q8_0, KV-sharded)"}[workload],
-                   "kv_type": TYPE_NAMES[ty],
-                   "n_seq": n_seq, "n_head": H, "n_head_kv": Hkv, "head_dim": D,
-                   "kv_len": w["n_kv"], "kv_splits": n_splits, "rows_per_split": rows_per_split,
-                   "parallelism": f"kv-shard{world}" if world > 1 else "single",
-                   "l2": ("rotating %d input sets (%.0f MB > 2x L2)" % (len(sets),
-                          len(sets) * kv_bytes / 1e6)) if workload != "c5" else
-                         "inputs %.0f MB per GPU > L2" % (local_kv / 1e6)},
+        "config": workload_config(workload, world),
+        "plan": {"kv_splits": n_splits, "rows_per_split": rows_per_split,
+                 **({"split_groups": n_groups, "groups_per_gpu": ge - gb}
+                    if workload == "c5" else {})},
         "breakdown_ms": {"decode_kernel": round(dec_ms, 5), "nccl_gather": round(col_ms, 5),
                          "merge_kernel": round(mrg_ms, 5)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm,
@@ -348,11 +474,18 @@ def run_ours(args, rank, world, torch, dist):
         "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": int(q_host.numel() * 4),
-                "d2h_bytes_per_step": int(o_host.numel() * 4)},
+                "d2h_bytes_per_step": int(o_host.numel() * 4),
+                "timing": "CUDA-graph replay (host launch work outside the timed region)"},
+        **({"e2e_eager": {"value": round(step_bytes / (eager_ms * 1e-3) / 1e9, 2),
+                          "unit": "GB/s", "ms_per_step": round(eager_ms, 5),
+                          "timing": "eager: one prebuilt xq_flash_attn_ext call per step "
+                                    "from a Python loop (the library's host work and one "
+                                    "ctypes transition per step inside the timed region)"}}
+           if eager_ms is not None else {}),
+        # decode + merge per step; e2e adds the q staging kernel
         "gpu_launches": args.steps * (3 if workload == "c5" else 2),
         **({"scaling_reference": ref1} if ref1 else {}),
-        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps if use_graph
-                  else "eager launches, CUDA events",
+        "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
         "clocks": clocks,
     }
     return line
@@ -360,17 +493,19 @@ def run_ours(args, rank, world, torch, dist):
 
 def c5_single_gpu(torch, xq, dev, ty, steps, warmup, step_bytes):
     """Config 5 on one GPU (all 256 splits, the 8 group merges, the final
-    merge; no collective): the N = 1 point of the KV-sharded series."""
+    merge; no collective): the N = 1 point of the KV-sharded series.  Returns
+    (line fragment, merged output of the last step)."""
     w = C5
     n_splits, rows_per_split, per_group = w["n_kv"] // 1024, 1024, 32
-    k = make_kv(torch, xq, w, ty, w["n_kv"], 1000, dev)
-    v = make_kv(torch, xq, w, ty, w["n_kv"], 2000, dev)
+    n_groups = n_splits // per_group
+    k = make_kv_groups(torch, xq, w, ty, 0, n_groups, per_group * rows_per_split, 1000, dev)
+    v = make_kv_groups(torch, xq, w, ty, 0, n_groups, per_group * rows_per_split, 2000, dev)
     g = torch.Generator(device=dev)
     g.manual_seed(7)
     q = torch.randn((w["n_seq"], w["n_head"], 1, w["D"]), generator=g, device=dev)
     rows = w["n_seq"] * w["n_head"]
     part = torch.empty((n_splits, rows, w["D"] + 2), dtype=torch.float32, device=dev)
-    rec = torch.empty((n_splits // per_group, rows, w["D"] + 2), dtype=torch.float32, device=dev)
+    rec = torch.empty((n_groups, rows, w["D"] + 2), dtype=torch.float32, device=dev)
     out = torch.empty((rows, w["D"]), dtype=torch.float32, device=dev)
     scale = 1.0 / math.sqrt(w["D"])
 
@@ -380,12 +515,14 @@ def c5_single_gpu(torch, xq, dev, ty, steps, warmup, step_bytes):
         xq.lse_merge(rec, out=out, want_lse=False)
 
     ms = graph_timed(torch, step, steps, warmup) / steps
+    step(0)
+    torch.cuda.synchronize()
     del k, v
     return {"n_gpus": 1, "workload": "BASELINE config 5 on one GPU (no collective)",
             "value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "ms_per_step": round(ms, 5),
             "note": "the N = 1 point of this strong-scaling series (the default N = 1 line "
-                    "is BASELINE config 2)"}
+                    "is BASELINE config 2)"}, out
 
 
 def cpu_oracle_sample(workload, seconds_cap=20.0, sample_kv=None):
@@ -446,9 +583,12 @@ def gdn_inputs(torch, dev, n_seq, T, seed, w=C3):
     return [q, k, v, gate, beta, state]
 
 
-def run_gdn(args, torch, workload):
+def run_gdn(args, rank, world, torch, dist, workload):
+    """GATED_DELTA_NET, config 3.  N > 1: sharded by value head, rank r runs
+    heads shard.head_block(32, N, r) (strong scaling: the op is fixed)."""
     import xq
-    dev = torch.device("cuda", 0)
+    from xq import shard
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     n_seq, T = (8, 1) if workload == "c3a" else (1, 4096)
     w = C3
@@ -456,54 +596,74 @@ def run_gdn(args, torch, workload):
     step_bytes, in_bytes, y_bytes = gdn_bytes(n_seq, T)
     n_sets = 1 if step_bytes > 2 * L2_BYTES else math.ceil(2 * L2_BYTES / step_bytes) + 1
     sets = [gdn_inputs(torch, dev, n_seq, T, 100 + i) for i in range(n_sets)]
-    n_dst = w["S"] * w["H"] * T * n_seq + w["slots"] * w["S"] ** 2 * w["H"] * n_seq
+    h0, h1 = shard.head_block(w["H"], world, rank)
+    Hl = h1 - h0
+    n_dst = w["S"] * Hl * T * n_seq + w["slots"] * w["S"] ** 2 * Hl * n_seq
     dsts = [torch.empty(n_dst, dtype=torch.float32, device=dev) for _ in range(n_sets)]
 
+    def run(x, dst):
+        if world == 1:
+            xq.gated_delta_net(*x, slots=w["slots"], out=dst)
+        else:
+            shard.gdn_heads(*x, slots=w["slots"], world=world, rank=rank, out=dst)
+
     def step(i):
-        x = sets[i % n_sets]
-        xq.gated_delta_net(*x, slots=w["slots"], out=dsts[i % n_sets])
+        run(sets[i % n_sets], dsts[i % n_sets])
 
     clk = ClockSampler(dev.index)
     clk.start()
-    ms = graph_timed(torch, step, args.steps, args.warmup) / args.steps
+    ms = graph_timed(torch, step, args.steps, args.warmup, world, dist, dev) / args.steps
     clocks = clk.stop()
-    # end to end: this step's q, k, v, g, beta from pinned host memory, y back;
-    # the recurrent state stays resident on the device
-    hosts = [t.cpu().pin_memory() for t in sets[0][:5]]
-    y_host = torch.empty(n_seq * T * w["H"] * w["S"], dtype=torch.float32, pin_memory=True)
+    # end to end: this rank's q, k (whole) and v, g, beta (its heads) from
+    # pinned host memory, its y block back; the recurrent state stays resident
+    x0 = sets[0]
+    blocks = [x0[0], x0[1]] + [t[:, :, h0:h1] for t in x0[2:5]]
+    hosts = [t.cpu().pin_memory() for t in blocks]
+    n_y = n_seq * T * Hl * w["S"]
+    y_host = torch.empty(n_y, dtype=torch.float32, pin_memory=True)
 
     def e2e_step(i):
-        for h, d in zip(hosts, sets[0][:5]):
+        for h, d in zip(hosts, blocks):
             d.copy_(h, non_blocking=True)
-        xq.gated_delta_net(*sets[0], slots=w["slots"], out=dsts[0])
-        y_host.copy_(dsts[0][:y_host.numel()], non_blocking=True)
-    e2e_ms = graph_timed(torch, e2e_step, args.steps, args.warmup) / args.steps
+        run(x0, dsts[0])
+        y_host.copy_(dsts[0][:n_y], non_blocking=True)
+    e2e_ms = graph_timed(torch, e2e_step, args.steps, args.warmup, world, dist, dev) / args.steps
+    h2d = sum(t.numel() for t in hosts) * 4 * world
+    ref1 = None
+    if world > 1:
+        if rank == 0:
+            d1 = torch.empty(w["S"] * w["H"] * T * n_seq + w["slots"] * w["S"] ** 2 * w["H"] *
+                             n_seq, dtype=torch.float32, device=dev)
+            ms1 = graph_timed(torch, lambda i: xq.gated_delta_net(
+                *sets[i % n_sets], slots=w["slots"], out=d1), args.steps, args.warmup) / args.steps
+            ref1 = {"n_gpus": 1, "workload": "the same op unsharded on one GPU",
+                    "value": round(step_bytes / (ms1 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(ms1, 5)}
+        dist.barrier()
+    if rank != 0:
+        return None
     value = step_bytes / (ms * 1e-3) / 1e9
     return {
         "metric": "gated-delta-net GB/s", "value": round(value, 2), "unit": "GB/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded; q, k L2-normalised N(0,1), v N(0,1), g = -softplus, "
                 "beta = sigmoid, state 0.1 N(0,1))",
-        "config": {"workload": ("BASELINE config 3 decode (GDN, 8 seqs x 1 token)"
-                                if workload == "c3a" else
-                                "BASELINE config 3 prefill (GDN, 1 seq x 4096 tokens)"),
-                   "n_seq": n_seq, "tokens": T, "v_heads": w["H"], "k_heads": w["H_k"],
-                   "head_dim": w["S"], "slots": w["slots"],
-                   "l2": ("rotating %d input sets (%.0f MB > 2x L2)" % (n_sets,
-                          n_sets * step_bytes / 1e6)) if n_sets > 1 else
-                         "inputs %.0f MB > L2" % (step_bytes / 1e6)},
+        "config": workload_config(workload, world),
+        "plan": {"value_heads_per_gpu": Hl},
         "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": hbm, "unit": "GB/s",
                      "frac": round(value / hbm, 4), "peak_kind": peak_kind,
                      "kernel": ("gdn_recurrent_kernel" if workload == "c3a" else
                                 "gdn_chunk_prep_kernel + gdn_chunk_scan_kernel"),
                      "traffic": profile_traffic("gdn_" + workload)},
         "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": in_bytes,
+                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": y_bytes},
         # decode: one recurrent kernel; prefill: the chunked prep and scan kernels
         "gpu_launches": args.steps * (1 if workload == "c3a" else 2),
+        **({"scaling_reference": ref1} if ref1 else {}),
         "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
         "clocks": clocks,
     }
@@ -513,59 +673,85 @@ def prefill_flops(n_q, H, D):
     return 4.0 * D * H * n_q * (n_q + 1) / 2
 
 
-def run_prefill(args, torch):
+def run_prefill(args, rank, world, torch, dist, workload):
+    """Causal prefill, config 4 (F16 cache) or its shape over a Q8_0 / Q4_0
+    cache.  N > 1: sharded by KV-head group (shard.prefill_part; strong
+    scaling: the op is fixed)."""
     import xq
-    dev = torch.device("cuda", 0)
+    from xq import shard
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
+    ty = {"c4q8": xq.Q8_0, "c4q4": xq.Q4_0}.get(workload, xq.F16)
     w = C4
     H, Hkv, D, N = w["n_head"], w["n_hkv"], w["D"], w["n_q"]
     _, tflops, peak_kind = peaks()
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     q = torch.randn((1, H, N, D), generator=g, device=dev)
-    k = xq.quantize_rows(xq.F16, torch.randn((1, N, Hkv, D), generator=g, device=dev))
-    v = xq.quantize_rows(xq.F16, torch.randn((1, N, Hkv, D), generator=g, device=dev))
+    k = xq.quantize_rows(ty, torch.randn((1, N, Hkv, D), generator=g, device=dev))
+    v = xq.quantize_rows(ty, torch.randn((1, N, Hkv, D), generator=g, device=dev))
     mask = torch.full((1, 1, N, N), float("-inf"), dtype=torch.float16, device=dev).triu_(1)
-    out = torch.empty((1, N, H, D), dtype=torch.float32, device=dev)
     scale = 1.0 / math.sqrt(D)
+    (h0, h1), (c0, c1), (r0, r1) = shard.prefill_block(H, Hkv, N, N, world, rank)
+    out = torch.empty((1, r1 - r0, h1 - h0, D), dtype=torch.float32, device=dev)
 
     def step(i):
-        xq.flash_attn_ext(q, k, v, xq.F16, mask=mask, scale=scale, out=out)
+        shard.prefill_part(q, k, v, ty, mask, world, rank, scale=scale, out=out)
 
     clk = ClockSampler(dev.index)
     clk.start()
-    ms = graph_timed(torch, step, args.steps, args.warmup) / args.steps
+    ms = graph_timed(torch, step, args.steps, args.warmup, world, dist, dev) / args.steps
     clocks = clk.stop()
-    q_host = q.cpu().pin_memory()
+    q_blk = q[:, h0:h1, r0:r1]
+    q_host = q_blk.cpu().pin_memory()
     o_host = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
 
     def e2e_step(i):
-        q.copy_(q_host, non_blocking=True)
+        q_blk.copy_(q_host, non_blocking=True)
         step(i)
         o_host.copy_(out, non_blocking=True)
-    e2e_ms = graph_timed(torch, e2e_step, max(3, args.steps // 4), args.warmup) / max(
-        3, args.steps // 4)
+    n_e2e = max(3, args.steps // 4)
+    e2e_ms = graph_timed(torch, e2e_step, n_e2e, args.warmup, world, dist, dev) / n_e2e
     fl = prefill_flops(N, H, D)
+    ref1 = None
+    if world > 1:
+        if rank == 0:
+            o1 = torch.empty((1, N, H, D), dtype=torch.float32, device=dev)
+            ms1 = graph_timed(torch, lambda i: xq.flash_attn_ext(q, k, v, ty, mask=mask,
+                                                                 scale=scale, out=o1),
+                              args.steps, args.warmup) / args.steps
+            ref1 = {"n_gpus": 1, "workload": "the same op unsharded on one GPU",
+                    "value": round(fl / (ms1 * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(ms1, 5),
+                    "rank0_block_bit_identical": bool(torch.equal(o1[:, r0:r1, h0:h1], out))}
+        dist.barrier()
+    if rank != 0:
+        return None
     value = fl / (ms * 1e-3) / 1e12
+    quant = ty != xq.F16
     return {
         "metric": "causal prefill TFLOP/s", "value": round(value, 2), "unit": "TFLOP/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic (seeded N(0,1); K/V rounded to F16; explicit causal F16 mask)",
-        "config": {"workload": "BASELINE config 4 (causal prefill, 8192 tokens)",
-                   "n_q": N, "n_kv": N, "n_head": H, "n_head_kv": Hkv, "head_dim": D,
-                   "flops_per_step": fl,
-                   "l2": "inputs %.0f MB > L2" % ((q.numel() * 4 + k.numel() * 2 +
-                                                   mask.numel() * 2) / 1e6)},
+        "data": ("synthetic (seeded N(0,1); K/V " + ("rounded to F16" if not quant else
+                 "quantized by the ggml reference quantizer, widened to f16 by the library's "
+                 "pre-pass inside every step") + "; explicit causal F16 mask)"),
+        "config": workload_config(workload, world),
+        "plan": {"q_heads": [h0, h1], "kv_heads": [c0, c1], "q_rows": [r0, r1]},
         "roofline": {"bound": "tensor", "achieved": round(value, 2), "peak": tflops,
                      "unit": "TFLOP/s", "frac": round(value / tflops, 4),
-                     "peak_kind": peak_kind + " (bf16 burst)", "kernel": "fa_prefill_kernel",
-                     "traffic": profile_traffic("fa_prefill_c4")},
+                     "peak_kind": peak_kind + " (bf16 burst)",
+                     "kernel": "fa_prefill_kernel" + ("<QQ>" if quant else ""),
+                     "traffic": profile_traffic("fa_prefill_" + workload)},
         "e2e": {"value": round(fl / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": q.numel() * 4,
-                "d2h_bytes_per_step": out.numel() * 4},
-        "gpu_launches": args.steps * 2,
+                "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": q_host.numel() * 4 * world,
+                "d2h_bytes_per_step": o_host.numel() * 4 * world},
+        # mask block map + prefill (+ the two K/V widening kernels)
+        "gpu_launches": args.steps * (4 if quant else 2),
+        **({"scaling_reference": ref1} if ref1 else {}),
         "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
         "clocks": clocks,
     }
@@ -633,10 +819,7 @@ def run_kvw(args, torch):
         "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32->q8_0",
         "data": "synthetic (seeded N(0,1) rows, contiguous append positions)",
-        "config": {"workload": "KV-cache write (SET_ROWS), 8192 tokens x 4 KV heads x D=256, "
-                               "K and V to Q8_0", "cache_rows": w["rows"],
-                   "l2": "rotating %d input sets (%.0f MB > 2x L2)" % (
-                       n_sets, n_sets * 2 * w["n_tok"] * w["n_hkv"] * w["D"] * 4 / 1e6)},
+        "config": workload_config("kvw"),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                      "kernel": "set_rows_kernel", "traffic": profile_traffic("set_rows_kvw")},
@@ -723,11 +906,7 @@ def run_kvarn4(args, torch):
         "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "u4 records / f16 rows -> f32",
         "data": "synthetic (seeded native records, stage and tail rows; q N(0,1))",
-        "config": {"workload": "native KVarN4 range attention, 24 Q / 4 KV heads, D=256, "
-                               "32768 rows past origin 102400, precision tail 128, 1 query",
-                   "bytes_per_step": step_bytes,
-                   "l2": "rotating %d plane sets (%.0f MB > 2x L2)" % (n_sets,
-                                                                      n_sets * step_bytes / 1e6)},
+        "config": workload_config("kv4"),
         "roofline": {"bound": "hbm", "achieved": round(value, 2), "peak": hbm, "unit": "GB/s",
                      "frac": round(value / hbm, 4), "peak_kind": peak_kind,
                      "kernel": "kvarn4_partials_kernel + lse_merge",
@@ -821,22 +1000,23 @@ def cpu_gdn_sample(workload):
                                     f"{dt * 1e3:.2f} ms each, {cores} threads"}
 
 
-def cpu_prefill_sample(rows=16):
-    """The last `rows` queries of config 4 (the longest causal rows)."""
+def cpu_prefill_sample(workload="c4", rows=64):
+    """The last `rows` queries of config 4 (the longest causal rows), over the
+    workload's cache type."""
     import oracle
     H, Hkv, D, N = C4["n_head"], C4["n_hkv"], C4["D"], C4["n_q"]
+    ty = {"c4q8": oracle.Q8_0, "c4q4": oracle.Q4_0}.get(workload, oracle.F16)
     rng = np.random.default_rng(0)
     q = rng.normal(0, 1, (1, H, rows, D)).astype(np.float32)
     kf = rng.normal(0, 1, (1, N, Hkv, D)).astype(np.float32)
-    k = oracle.quantize(oracle.F16, kf)
-    v = oracle.quantize(oracle.F16, rng.normal(0, 1, kf.shape).astype(np.float32))
+    k = oracle.quantize(ty, kf)
+    v = oracle.quantize(ty, rng.normal(0, 1, kf.shape).astype(np.float32))
     pos = np.arange(N - rows, N)
     mask = np.where(np.arange(N)[None, :] > pos[:, None], -np.inf, 0).astype(np.float16)
     mask = mask.reshape(1, 1, rows, N)
     cores = os.cpu_count() or 1
     t = time.perf_counter()
-    oracle.flash_attn_ext(q, k, v, oracle.F16, oracle.F16, mask=mask, scale=1 / 16,
-                          nth=cores, n_workers=cores)
+    oracle.flash_attn_ext(q, k, v, ty, ty, mask=mask, scale=1 / 16, nth=cores, n_workers=cores)
     dt = time.perf_counter() - t
     fl = 4.0 * D * H * float((pos + 1).sum())
     return fl / dt / 1e12, {"cores": cores, "unit": "TFLOP/s",
@@ -850,8 +1030,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="auto",
-                    choices=["auto", "c1", "c2", "c2q4", "c3a", "c3b", "c4", "c5", "kvw", "kv4"])
+    ap.add_argument("--workload", default="auto", choices=["auto"] + list(WORKLOAD_NAMES))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -859,15 +1038,15 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     workload = args.workload if args.workload != "auto" else ("c2" if world == 1 else "c5")
 
-    single = workload in ("c3a", "c3b", "c4", "kvw", "kv4")
     if args.impl == "reference":
         if rank != 0:
             return 0
         metric, unit = "flash-decode KV GB/s", "GB/s"
         if workload in ("c3a", "c3b"):
             (val, info), metric = cpu_gdn_sample(workload), "gated-delta-net GB/s"
-        elif workload == "c4":
-            (val, info), metric, unit = cpu_prefill_sample(), "causal prefill TFLOP/s", "TFLOP/s"
+        elif workload in ("c4", "c4q8", "c4q4"):
+            (val, info), metric, unit = (cpu_prefill_sample(workload), "causal prefill TFLOP/s",
+                                         "TFLOP/s")
         elif workload == "kvw":
             (val, info), metric = cpu_kvw_sample(), "KV-cache write GB/s"
         elif workload == "kv4":
@@ -878,7 +1057,7 @@ def main():
         line = {"metric": metric, "value": val, "unit": unit,
                 "impl": "reference", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
-                "config": {"workload": workload}, "data": "synthetic",
+                "config": workload_config(workload, world), "data": "synthetic",
                 "cpu_baseline": {"value": val, "unit": unit, "cores": info["cores"],
                                  "kind": "port", "sample": info["sample"]},
                 "e2e": {"value": val, "unit": unit, "h2d_bytes_per_step": 0,
@@ -887,21 +1066,10 @@ def main():
         return 0
 
     import torch
-    if single:
-        # GDN, prefill and KV-write rows are measured on one GPU
-        if world > 1:
-            print(json.dumps({"error": f"workload {workload} runs on one GPU"}), flush=True)
-            return 2
-        runs = {"c4": run_prefill, "kvw": run_kvw, "kv4": run_kvarn4}
-        line = runs[workload](args, torch) if workload in runs else run_gdn(args, torch, workload)
-        if not args.no_cpu_baseline:
-            samples = {"c4": cpu_prefill_sample, "kvw": cpu_kvw_sample, "kv4": cpu_kvarn4_sample}
-            val, info = samples[workload]() if workload in samples else cpu_gdn_sample(workload)
-            line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": info["unit"],
-                                    "cores": info["cores"], "kind": "port",
-                                    "sample": info["sample"]}
-        print(json.dumps(line), flush=True)
-        return 0
+    if workload in ("kvw", "kv4") and world > 1:
+        # the KV-cache write and the KVarN4 range call are measured on one GPU
+        print(json.dumps({"error": f"workload {workload} runs on one GPU"}), flush=True)
+        return 2
     dist = None
     if world > 1:
         import datetime
@@ -910,11 +1078,30 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    line = run_ours(args, rank, world, torch, dist)
+    if workload in ("c3a", "c3b"):
+        line = run_gdn(args, rank, world, torch, dist, workload)
+    elif workload in ("c4", "c4q8", "c4q4"):
+        line = run_prefill(args, rank, world, torch, dist, workload)
+    elif workload == "kvw":
+        line = run_kvw(args, torch)
+    elif workload == "kv4":
+        line = run_kvarn4(args, torch)
+    else:
+        line = run_decode(args, rank, world, torch, dist, workload)
     if rank == 0 and line is not None:
         if world == 1 and not args.no_cpu_baseline:
-            val, info = cpu_oracle_sample(workload)
-            line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": "GB/s",
+            if workload in ("c3a", "c3b"):
+                val, info = cpu_gdn_sample(workload)
+            elif workload in ("c4", "c4q8", "c4q4"):
+                val, info = cpu_prefill_sample(workload)
+            elif workload == "kvw":
+                val, info = cpu_kvw_sample()
+            elif workload == "kv4":
+                val, info = cpu_kvarn4_sample()
+            else:
+                val, info = cpu_oracle_sample(workload)
+                info["unit"] = "GB/s"
+            line["cpu_baseline"] = {"value": float(f"{val:.4g}"), "unit": info["unit"],
                                     "cores": info["cores"], "kind": "port",
                                     "sample": info["sample"]}
         print(json.dumps(line), flush=True)
