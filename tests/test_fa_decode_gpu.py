@@ -178,3 +178,82 @@ def test_pinned_host_q_and_out(ty, D, H, Hkv, n_kv, n_q):
         assert torch.equal(out_host, want)
     with pytest.raises(Exception):
         xq.flash_attn_ext(torch.from_numpy(qn), k, v, ty, scale=D ** -0.5)  # pageable q
+
+
+def _ws_call(q, k, v, ty, scale, out, ws, n_splits=0, sinks=None):
+    import ctypes as C
+
+    from xq import _lib
+    from xq.ops import _fa_params, _stream
+    p = _fa_params(q, k, v, ty, ty, None, sinks, out, scale, 0.0, 0.0, n_splits)
+    rc = _lib.lib().xq_flash_attn_ext(C.byref(p), ws.data_ptr(), ws.numel(), _stream(None))
+    assert rc == 0, _lib.lib().xq_last_error()
+
+
+@pytest.mark.parametrize("ty,D,H,Hkv,n_kv,n_splits", [
+    (oracle.Q8_0, 256, 16, 2, 32768, 0), (oracle.F16, 128, 16, 4, 4096, 0),
+    (oracle.Q4_0, 256, 16, 2, 9000, 37), (oracle.Q8_0, 128, 8, 1, 5000, 3)])
+def test_any_workspace_contents_graph_replays_and_the_split_records(ty, D, H, Hkv, n_kv,
+                                                                     n_splits):
+    """xq_flash_attn_ext with a caller workspace of any contents (random
+    bytes, then the previous call's leftovers) and under CUDA-graph replays
+    gives the same bits every time; the result equals the split records
+    (xq_fa_partials) merged by xq_lse_merge within fp32 rounding, and the
+    oracle within the north-star tolerance."""
+    xq = _xq()
+    q, k, v, _ = make_case(31 + n_kv, ty, D, H, Hkv, n_kv)
+    dev = torch.device("cuda")
+    tq, tk, tv = (torch.from_numpy(x).to(dev) for x in (q, k, v))
+    scale = D ** -0.5
+    nbytes = xq.flash_attn_ext_workspace(tq, tk, tv, ty, n_splits=n_splits)
+    ws = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=dev)
+    outs = []
+    for _ in range(3):
+        o = torch.full((1, 1, H, D), float("nan"), device=dev)
+        _ws_call(tq, tk, tv, ty, scale, o, ws, n_splits)
+        outs.append(o)
+    ws.random_(0, 256)
+    o = torch.empty((1, 1, H, D), device=dev)
+    _ws_call(tq, tk, tv, ty, scale, o, ws, n_splits)
+    outs.append(o)
+    og = torch.empty((1, 1, H, D), device=dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        _ws_call(tq, tk, tv, ty, scale, og, ws, n_splits)
+    for _ in range(3):
+        og.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        outs.append(og.clone())
+    del g
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    # the same split records through the separate merge kernel
+    nsp = n_splits or None
+    if nsp is None:
+        sm = torch.cuda.get_device_properties(dev).multi_processor_count
+        nsp = max(1, min(-(-2 * sm // Hkv), -(-n_kv // 64)))
+    rows = -(-n_kv // nsp)
+    nsp = -(-n_kv // rows)
+    part = xq.fa_partials(tq, tk, tv, ty, rows, 0, nsp, scale=scale)
+    two, _ = xq.lse_merge(part, want_lse=False)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(outs[0].view(H, D).cpu().numpy(), two.cpu().numpy(), rtol=2e-5,
+                               atol=1e-6)
+    want = oracle.flash_attn_ext(q, k, v, ty, ty, scale=scale, nth=8)
+    np.testing.assert_allclose(outs[0].cpu().numpy(), want, rtol=RTOL, atol=ATOL)
+
+
+def test_a_non_finite_value_poisons_its_rows_through_the_merge():
+    """A NaN block scale in one V row of KV head 0 (config 2, 148 splits): the
+    merge poisons every q head of that KV head (ggml-cpu's result is NaN there
+    too) and leaves KV head 1's heads finite."""
+    xq = _xq()
+    ty, D, H, Hkv, n_kv = oracle.Q8_0, 256, 16, 2, 32768
+    q, k, v, _ = make_case(5, ty, D, H, Hkv, n_kv)
+    v = v.copy()
+    v[0, 20000, 0, 0:2] = np.frombuffer(np.float16(np.nan).tobytes(), np.uint8)
+    dev = torch.device("cuda")
+    got = xq.flash_attn_ext(*(torch.from_numpy(x).to(dev) for x in (q, k, v)), ty, scale=1 / 16)
+    got = got.cpu().numpy()
+    assert np.all(np.isnan(got[0, 0, :8])) and np.all(np.isfinite(got[0, 0, 8:]))
