@@ -7,6 +7,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -33,11 +34,19 @@ int cuda_status(cudaError_t e, const char *what) {
     return fail(XQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+// SM count of the current device, queried once per device.
 int sm_count() {
-    int dev = 0, n = 148;
-    if (cudaGetDevice(&dev) == cudaSuccess)
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 148;
+    static std::atomic<int> cache[64];
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        return 148;
+    if (dev >= 0 && dev < 64 && (n = cache[dev].load(std::memory_order_relaxed)) > 0)
+        return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return 148;
+    if (dev >= 0 && dev < 64)
+        cache[dev].store(n, std::memory_order_relaxed);
+    return n;
 }
 
 bool kv_type_ok(int t) { return t == XQ_TYPE_F16 || t == XQ_TYPE_Q8_0 || t == XQ_TYPE_Q4_0; }
@@ -334,35 +343,11 @@ uint32_t xq_split_k(uint32_t active, uint32_t mode) {
     return k < 1 ? 1 : k;
 }
 
-// Workspace of the kernels themselves (device-resident q).
-static size_t fa_main_workspace(const xq_fa_params *p) {
-    FaPlan pl;
-    if (fa_prepare(p, &pl) != XQ_OK)
-        return 0;
-    xq::PrefillShape ps;
-    if (prefill_shape(p, pl, &ps))
-        return xq::prefill_ws_bytes(ps);
-    plan_splits(&pl, p->n_splits);
-    if (pl.n_splits <= 1)
-        return 0;
-    return (size_t)pl.n_splits * (size_t)pl.n_rows * (size_t)(pl.D + 2) * sizeof(float);
-}
 
-size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
-    const size_t main = fa_main_workspace(p);
-    HostView hq;
-    if (!p || host_view(p->q.data, &hq) != 1)
-        return main;
-    return (main + 255) / 256 * 256 + q_stage_bytes(p->q);
-}
-
-static int fa_run(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t stream) {
-    FaPlan pl;
-    int rc = fa_prepare(p, &pl);
-    if (rc)
-        return rc;
-    xq::PrefillShape ps;
-    if (prefill_shape(p, pl, &ps)) {
+// One planned call: the prefill kernel (pre) or the split-KV decode (+ merge).
+static int fa_execute(const xq_fa_params *p, FaPlan &pl, bool pre, const xq::PrefillShape &ps,
+                      void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (pre) {
         const size_t need = xq::prefill_ws_bytes(ps);
         if (!ws || ws_bytes < need)
             return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes,
@@ -370,14 +355,12 @@ static int fa_run(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t 
         if (reinterpret_cast<uintptr_t>(ws) % 16)
             return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace must be 16-byte aligned");
         const char *why = "";
-        cudaError_t e = xq::launch_prefill(ps, ws, reinterpret_cast<cudaStream_t>(stream), &why);
+        cudaError_t e = xq::launch_prefill(ps, ws, st, &why);
         if (e != cudaSuccess)
             return fail(XQ_ERR_CUDA, "flash_attn_ext prefill: %s (%s)", cudaGetErrorString(e),
                         why);
         return XQ_OK;
     }
-    plan_splits(&pl, p->n_splits);
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     dim3 grid((unsigned)pl.n_splits, (unsigned)(pl.a.n_head_kv * pl.n_qblocks),
               (unsigned)pl.a.n_seq);
     if (pl.n_splits == 1) {
@@ -389,12 +372,30 @@ static int fa_run(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t 
         return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes, need);
     pl.a.direct = 0;
     pl.a.partials = static_cast<float *>(ws);
-    rc = cuda_status(run_decode(pl, grid, st), "flash_attn_ext decode");
+    int rc = cuda_status(run_decode(pl, grid, st), "flash_attn_ext decode");
     if (rc)
         return rc;
     return cuda_status(xq::launch_merge(pl.a.partials, pl.n_splits, pl.n_rows, pl.D, p->dst,
                                         nullptr, p->sinks, pl.a.n_head, st),
                        "flash_attn_ext merge");
+}
+
+// Validate and plan once: the kernels' own workspace bytes in *main.
+static int fa_plan(const xq_fa_params *p, FaPlan *pl, bool *pre, xq::PrefillShape *ps,
+                   size_t *main) {
+    int rc = fa_prepare(p, pl);
+    if (rc)
+        return rc;
+    *pre = prefill_shape(p, *pl, ps);
+    if (*pre) {
+        *main = xq::prefill_ws_bytes(*ps);
+        return XQ_OK;
+    }
+    plan_splits(pl, p->n_splits);
+    *main = pl->n_splits <= 1
+                ? 0
+                : (size_t)pl->n_splits * (size_t)pl->n_rows * (size_t)(pl->D + 2) * sizeof(float);
+    return XQ_OK;
 }
 
 int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_stream_t stream) {
@@ -405,31 +406,55 @@ int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_strea
     if (kq < 0 || kd < 0)
         return fail(XQ_ERR_INVALID,
                     "flash_attn_ext: q / dst in pageable host memory (pin it or use the device)");
-    if (kq == 0 && kd == 0)
-        return fa_run(p, ws, ws_bytes, stream);
-    // pinned host q: copied into the tail of the workspace by a kernel, then
-    // read from there; pinned host dst: written in place by the kernels
+    // pinned host dst: written in place by the kernels through its device view
     xq_fa_params p2 = *p;
     if (kd == 1)
         p2.dst = static_cast<float *>(hd.dev);
-    size_t main = fa_main_workspace(&p2);
+    FaPlan pl;
+    bool pre = false;
+    xq::PrefillShape ps;
+    size_t main = 0;
+    int rc = fa_plan(&p2, &pl, &pre, &ps, &main);
+    if (rc)
+        return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (kq == 1) {
+        // pinned host q: copied into the tail of the workspace by a kernel,
+        // then read from there (contiguous rows)
         const size_t off = (main + 255) / 256 * 256, need = off + q_stage_bytes(p->q);
         if (!ws || ws_bytes < need)
             return fail(XQ_ERR_WORKSPACE, "flash_attn_ext: workspace %zu < %zu bytes", ws_bytes,
                         need);
         float *staged = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + off);
-        const int rc = stage_q(p->q, hq.dev, staged, reinterpret_cast<cudaStream_t>(stream));
+        rc = stage_q(p->q, hq.dev, staged, st);
         if (rc)
             return rc;
-        p2.q.data = staged;
-        p2.q.nb[0] = 4;
-        p2.q.nb[1] = 4 * p->q.ne[0];
-        p2.q.nb[2] = p2.q.nb[1] * p->q.ne[1];
-        p2.q.nb[3] = p2.q.nb[2] * p->q.ne[2];
+        const int64_t nb1 = 4 * p->q.ne[0], nb2 = nb1 * p->q.ne[1], nb3 = nb2 * p->q.ne[2];
+        pl.a.q = reinterpret_cast<const uint8_t *>(staged);
+        pl.a.q_nb1 = nb1;
+        pl.a.q_nb2 = nb2;
+        pl.a.q_nb3 = nb3;
+        ps.q = pl.a.q;
+        ps.q_nb[0] = 4;
+        ps.q_nb[1] = nb1;
+        ps.q_nb[2] = nb2;
+        ps.q_nb[3] = nb3;
         ws_bytes = off;
     }
-    return fa_run(&p2, ws, ws_bytes, stream);
+    return fa_execute(&p2, pl, pre, ps, ws, ws_bytes, st);
+}
+
+size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {
+    FaPlan pl;
+    bool pre = false;
+    xq::PrefillShape ps;
+    size_t main = 0;
+    if (!p || fa_plan(p, &pl, &pre, &ps, &main) != XQ_OK)
+        return 0;
+    HostView hq;
+    if (host_view(p->q.data, &hq) != 1)
+        return main;
+    return (main + 255) / 256 * 256 + q_stage_bytes(p->q);
 }
 
 int xq_fa_partials(const xq_fa_params *p, int64_t rows_per_split, int64_t split_begin,

@@ -877,9 +877,25 @@ bool decode_mma_ok(int type, int D, const DecodeArgs &a) {
 }
 
 // 4D map over one K or V tensor: {row bytes / 2 (u16), n_kv, n_head_kv, n_seq},
-// box = one 16-row group of one head.
+// box = one 16-row group of one head.  The last few encodings of each host
+// thread are kept: a decode loop calls with the same cache views step after
+// step, and encoding is host work on every eager call.
 static bool encode_rows_map(CUtensorMap *m, const uint8_t *base, int rec, int n_kv, int n_hkv,
                             int n_seq, int64_t nb1, int64_t nb2, int64_t nb3) {
+    struct Entry {
+        const uint8_t *base;
+        int64_t key[7];
+        CUtensorMap map;
+    };
+    constexpr int kEntries = 8;
+    thread_local Entry cache[kEntries];
+    thread_local int next = 0;
+    const int64_t key[7] = {rec, n_kv, n_hkv, n_seq, nb1, nb2, nb3};
+    for (int i = 0; i < kEntries; ++i)
+        if (cache[i].base == base && memcmp(cache[i].key, key, sizeof(key)) == 0) {
+            *m = cache[i].map;
+            return true;
+        }
     auto enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(tensor_map_encoder());
     if (!enc || rec % 16 || rec / 2 > 256 || n_kv <= 0)
         return false;
@@ -888,10 +904,16 @@ static bool encode_rows_map(CUtensorMap *m, const uint8_t *base, int rec, int n_
     cuuint64_t strides[3] = {(cuuint64_t)nb1, (cuuint64_t)nb2, (cuuint64_t)nb3};
     cuuint32_t box[4] = {(cuuint32_t)(rec / 2), (cuuint32_t)dm::KG, 1, 1};
     cuuint32_t es[4] = {1, 1, 1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<uint8_t *>(base), dims, strides,
-               box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<uint8_t *>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    Entry &e = cache[next];
+    next = (next + 1) % kEntries;
+    e.base = base;
+    memcpy(e.key, key, sizeof(key));
+    e.map = *m;
+    return true;
 }
 
 template <int T, int D, int ST, int VW>

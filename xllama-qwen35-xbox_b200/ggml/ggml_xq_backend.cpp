@@ -307,10 +307,17 @@ ggml_status run_fa(BackendCtx *c, ggml_tensor *op) {
     std::memcpy(&p.scale, &op->op_params[0], 4);
     std::memcpy(&p.max_bias, &op->op_params[1], 4);
     std::memcpy(&p.softcap, &op->op_params[2], 4);
-    const size_t need = xq_flash_attn_ext_workspace(&p);
-    if (!ensure_ws(c, need))
-        return GGML_STATUS_ALLOC_FAILED;
-    if (xq_flash_attn_ext(&p, c->ws, c->ws_bytes, reinterpret_cast<xq_stream_t>(c->stream))) {
+    // one planned call with the backend's workspace as it is; a call that
+    // needs more returns XQ_ERR_WORKSPACE before launching anything, and only
+    // then is the size asked for and the workspace grown
+    xq_stream_t st = reinterpret_cast<xq_stream_t>(c->stream);
+    int rc = xq_flash_attn_ext(&p, c->ws, c->ws_bytes, st);
+    if (rc == XQ_ERR_WORKSPACE) {
+        if (!ensure_ws(c, xq_flash_attn_ext_workspace(&p)))
+            return GGML_STATUS_ALLOC_FAILED;
+        rc = xq_flash_attn_ext(&p, c->ws, c->ws_bytes, st);
+    }
+    if (rc) {
         log_err("FLASH_ATTN_EXT", xq_last_error());
         return GGML_STATUS_FAILED;
     }
