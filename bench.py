@@ -408,14 +408,38 @@ def run_decode(args, rank, world, torch, dist, workload):
     def timed(fn, n):
         return graph_timed(torch, fn, n, args.warmup, world, dist, dev)
 
+    ex, nccl_ms = None, None
+    if workload == "c5" and world > 1:
+        # the sharded step through the C ABI: group records stored into every
+        # rank's exchange buffer over NVLink (xq_fa_shard_push / _finish);
+        # step numbers rise by one per call on every rank, and the captured
+        # sequences hold an even number of steps (the exchange halves alternate)
+        ex = shard.ShardExchange(n_groups, n_rows_out, D)
+        p2p_ws = torch.empty(max(1 << 20, 2 * part_local.numel() * 4), dtype=torch.uint8,
+                             device=dev)
+        step_no = [0]
+        dist.barrier()
+        torch.cuda.synchronize()
+        nccl_step = step
+
+        def step(i, parts=None):
+            k, v = sets[0]
+            shard.shard_decode_step(qs[0], k, v, ty, ex, rank, world, rows_per_split, per_group,
+                                    step_no[0], scale=scale, out=out, ws=p2p_ws)
+            step_no[0] += 1
+        args.steps += args.steps % 2
+        nccl_ms = timed(nccl_step, args.steps) / args.steps
+
     clk = ClockSampler(dev.index)
     clk.start()
     ms = timed(step, args.steps) / args.steps
     clocks = clk.stop()
     # breakdown: each kernel of the step graph-timed alone
-    dec_ms = timed(lambda i: step(i, ("dec",)), args.steps) / args.steps
-    mrg_ms = timed(lambda i: step(i, ("merge",)), args.steps) / args.steps
-    col_ms = (timed(lambda i: step(i, ("gather",)), args.steps) / args.steps) if world > 1 else 0.0
+    parts_step = nccl_step if ex is not None else step
+    dec_ms = timed(lambda i: parts_step(i, ("dec",)), args.steps) / args.steps
+    mrg_ms = timed(lambda i: parts_step(i, ("merge",)), args.steps) / args.steps
+    col_ms = (timed(lambda i: parts_step(i, ("gather",)), args.steps) / args.steps
+              if world > 1 else 0.0)
 
     # end to end through the public call with host buffers (pinned)
     q_host = torch.empty((n_seq, H, 1, D), dtype=torch.float32, pin_memory=True)
@@ -448,7 +472,10 @@ def run_decode(args, rank, world, torch, dist, workload):
     ref1 = None
     if workload == "c5" and world > 1:
         step(0)
+        step(0)
         torch.cuda.synchronize()
+        dist.barrier()
+        ex.close()
         if rank == 0:
             ref1, out1 = c5_single_gpu(torch, xq, dev, ty, args.steps, args.warmup, step_bytes)
             ref1["bit_identical_to_n_gpus"] = bool(torch.equal(out1, out))
@@ -474,6 +501,9 @@ def run_decode(args, rank, world, torch, dist, workload):
                     if workload == "c5" else {})},
         "breakdown_ms": {"decode_kernel": round(dec_ms, 5), "nccl_gather": round(col_ms, 5),
                          "merge_kernel" + ("s" if workload == "c5" else ""): round(mrg_ms, 5)},
+        **({"exchange": "group records stored into every rank's exchange buffer with NVLink "
+                        "peer stores (xq_fa_shard_push / xq_fa_shard_finish)",
+            "nccl_exchange_step_ms": round(nccl_ms, 5)} if ex is not None else {}),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm,
                      "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "peak_kind": peak_kind,
@@ -491,9 +521,9 @@ def run_decode(args, rank, world, torch, dist, workload):
                                     "from a Python loop (the library's host work and one "
                                     "ctypes transition per step inside the timed region)"}}
            if eager_ms is not None else {}),
-        # decode + merge per step (c5: decode, group merge, final merge); e2e
-        # adds the q staging kernel
-        "gpu_launches": args.steps * (3 if workload == "c5" else 2),
+        # decode + merge per step; c5 over N GPUs: decode, group records, push,
+        # wait, final merge; e2e adds the q staging kernel
+        "gpu_launches": args.steps * ((5 if world > 1 else 3) if workload == "c5" else 2),
         **({"scaling_reference": ref1} if ref1 else {}),
         "timing": "CUDA-graph replay of %d steps, CUDA events" % args.steps,
         "clocks": clocks,

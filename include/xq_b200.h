@@ -28,6 +28,9 @@
  *   xq_attend_range       RemoteAttnEngine::attend_range
  *                         (uwp/rkva/remote-attn-engine.h:152-154,
  *                          remote-attn-engine.cpp:2774-3251)
+ *   xq_fa_shard_push /    the KV position split across devices with an
+ *   xq_fa_shard_finish    (O, LSE) merge (uwp/rkva/remote-attn-engine.cpp:
+ *                         2928-2978), across the GPUs of one box
  *   xq_fa_partials +      split partials + LSE reduction
  *   xq_lse_merge          (shaders/rkva/rkva_range_attn.hlsl:59-106,
  *                          rkva_range_reduce_opt.hlsl:26-133)
@@ -143,6 +146,63 @@ int xq_lse_merge(const float *partials, int64_t n_splits, int64_t n_rows, int64_
 /* the result is bit-identical however the groups are spread over GPUs.      */
 int xq_lse_merge_records(const float *partials, int64_t n_groups, int64_t splits_per_group,
                          int64_t n_rows, int64_t D, float *records, xq_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* KV-sharded decode across the GPUs of one box (one process per GPU).      */
+/* The reference splits a sequence's KV cache by position between devices  */
+/* and merges their (O, LSE) partials (uwp/rkva/remote-attn-engine.cpp:     */
+/* 2928-2978; the RANGE_ATTN reply, uwp/rkva/remote-attn-protocol.h:205-    */
+/* 236).  Here the KV rows of every sequence are cut into fixed global     */
+/* splits of rows_per_split rows and the splits into n_groups groups of    */
+/* splits_per_group; rank r holds the groups [b, e) of a contiguous block   */
+/* split (n_groups / world each, the first n_groups % world ranks one more) */
+/* -- its k / v views start at row 0 of its first split -- and each step:   */
+/*   xq_fa_shard_push    its splits' partial records, one (O, lse, 1)       */
+/*                       record per group (in split order), stored with    */
+/*                       NVLink peer stores into every rank's exchange      */
+/*                       buffer;                                            */
+/*   xq_fa_shard_finish  waits (bounded, 2 s) until every rank's records of */
+/*                       this step arrived, merges all n_groups records in */
+/*                       group order into out / lse (+ sinks).              */
+/* The grouping and both merge orders depend only on the plan's global     */
+/* numbers, so out is bit-identical for every world size.  Exchange       */
+/* buffer: xq_shard_exchange_bytes(n_groups, n_rows, D) bytes from         */
+/* xq_shard_exchange_alloc on each rank's GPU (zeroed); share it with      */
+/* xq_ipc_export / xq_ipc_open (CUDA IPC; the caller moves the 64-byte      */
+/* handles between processes) and list every rank's buffer as this rank    */
+/* maps it in plan.exchange (its own at [rank]).  step: +1 per step on     */
+/* every rank (its parity picks the buffer half; replays of a captured     */
+/* sequence need an even number of steps).  After a timeout (NaN output)   */
+/* re-create the exchange buffers on every rank.                           */
+/* n_rows = n_seq * n_q * n_head.  No TMA and no multicast touch peer      */
+/* memory: plain stores and one system-scope atomic per 16 KB chunk.       */
+/* ------------------------------------------------------------------------ */
+#define XQ_SHARD_MAX_RANKS 16
+typedef struct {
+    unsigned char bytes[64]; /* == cudaIpcMemHandle_t */
+} xq_ipc_handle;
+typedef struct {
+    int64_t rows_per_split, splits_per_group, n_groups;
+    int32_t rank, world;
+    uint32_t step;
+    int32_t reserved;
+    void *exchange[XQ_SHARD_MAX_RANKS];
+} xq_shard_plan;
+size_t xq_shard_exchange_bytes(int64_t n_groups, int64_t n_rows, int64_t D);
+int xq_shard_exchange_alloc(size_t bytes, void **exchange); /* setup: cudaMalloc + zero */
+int xq_shard_exchange_free(void *exchange);
+/* Host read of the exchange buffer's error word (synchronizes the stream):  */
+/* 1 once a finish call's wait ran out (its output is NaN), else 0.          */
+int xq_shard_exchange_error(const void *exchange, int64_t n_groups, int64_t n_rows, int64_t D,
+                            xq_stream_t stream, int32_t *error);
+int xq_ipc_export(const void *dev_ptr, xq_ipc_handle *handle);
+int xq_ipc_open(const xq_ipc_handle *handle, void **dev_ptr);
+int xq_ipc_close(void *dev_ptr);
+size_t xq_fa_shard_workspace(const xq_fa_params *p, const xq_shard_plan *s);
+int xq_fa_shard_push(const xq_fa_params *p, const xq_shard_plan *s, void *workspace,
+                     size_t workspace_bytes, xq_stream_t stream);
+int xq_fa_shard_finish(const xq_shard_plan *s, int64_t n_rows, int64_t D, const float *sinks,
+                       int32_t n_head, float *out, float *lse, xq_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* RKVA RANGE_ATTN: (O, LSE) over a compact KV range [0, active) whose row r */

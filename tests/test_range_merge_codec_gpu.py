@@ -223,3 +223,24 @@ def test_lse_merge_variants_bit_identical(D, n_splits, rows):
             torch.cuda.synchronize()
             recs.append(r.cpu().numpy().view(np.int32))
         assert np.array_equal(recs[0], recs[1])
+
+
+@pytest.mark.parametrize("rows", [6, 48, 200])
+def test_lse_merge_records_of_a_group_block_equal_the_whole(rows):
+    """The records of any block of groups equal the same groups' records of
+    the whole merge, bit for bit, at few rows as at many: a record comes out of
+    one kernel however the groups are spread over GPUs."""
+    import xq
+    rng = np.random.default_rng(rows)
+    n_groups, per, D = 8, 4, 256
+    part = rng.normal(0, 1, (n_groups * per, rows, D + 2)).astype(np.float32)
+    part[:, :, D] = rng.normal(0, 2, (n_groups * per, rows))
+    part[:, :, D + 1] = rng.uniform(0.5, 4, (n_groups * per, rows))
+    tp = torch.from_numpy(part).cuda()
+    whole = xq.lse_merge_records(tp, per)
+    for blocks in (1, 2, 4, 8):
+        size = n_groups // blocks
+        for b in range(blocks):
+            sub = xq.lse_merge_records(tp[b * size * per:(b + 1) * size * per].contiguous(), per)
+            torch.cuda.synchronize()
+            assert torch.equal(sub, whole[b * size:(b + 1) * size]), (rows, blocks, b)

@@ -500,6 +500,197 @@ int xq_lse_merge_records(const float *partials, int64_t n_groups, int64_t splits
 }
 
 // ---------------------------------------------------------------------------
+// KV-sharded decode across GPUs (one process per GPU).
+
+size_t xq_shard_exchange_bytes(int64_t n_groups, int64_t n_rows, int64_t D) {
+    if (n_groups <= 0 || n_rows <= 0 || (D != 64 && D != 128 && D != 256))
+        return 0;
+    return xq::shard_exchange_bytes(n_groups, n_rows, (int)D);
+}
+
+int xq_shard_exchange_alloc(size_t bytes, void **exchange) {
+    if (!exchange || bytes == 0)
+        return fail(XQ_ERR_INVALID, "shard_exchange_alloc: bad arguments");
+    *exchange = nullptr;
+    void *p = nullptr;
+    int rc = cuda_status(cudaMalloc(&p, bytes), "shard_exchange_alloc: cudaMalloc");
+    if (rc)
+        return rc;
+    rc = cuda_status(cudaMemset(p, 0, bytes), "shard_exchange_alloc: cudaMemset");
+    if (rc) {
+        cudaFree(p);
+        return rc;
+    }
+    *exchange = p;
+    return XQ_OK;
+}
+
+int xq_shard_exchange_error(const void *exchange, int64_t n_groups, int64_t n_rows, int64_t D,
+                            xq_stream_t stream, int32_t *error) {
+    if (!exchange || !error || xq_shard_exchange_bytes(n_groups, n_rows, D) == 0)
+        return fail(XQ_ERR_INVALID, "shard_exchange_error: bad arguments");
+    const uint8_t *w = static_cast<const uint8_t *>(exchange) +
+                       xq::shard_ctl_off(n_groups, n_rows, (int)D) + 2 * sizeof(unsigned);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    unsigned v = 0;
+    int rc = cuda_status(cudaMemcpyAsync(&v, w, sizeof(v), cudaMemcpyDeviceToHost, st),
+                         "shard_exchange_error: copy");
+    if (!rc)
+        rc = cuda_status(cudaStreamSynchronize(st), "shard_exchange_error: synchronize");
+    *error = (int32_t)v;
+    return rc;
+}
+
+int xq_shard_exchange_free(void *exchange) {
+    return cuda_status(cudaFree(exchange), "shard_exchange_free");
+}
+
+int xq_ipc_export(const void *dev_ptr, xq_ipc_handle *handle) {
+    static_assert(sizeof(cudaIpcMemHandle_t) == sizeof(handle->bytes), "IPC handle size");
+    if (!dev_ptr || !handle)
+        return fail(XQ_ERR_INVALID, "ipc_export: null argument");
+    cudaIpcMemHandle_t h;
+    const int rc = cuda_status(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)),
+                               "ipc_export: cudaIpcGetMemHandle");
+    if (!rc)
+        memcpy(handle->bytes, &h, sizeof(h));
+    return rc;
+}
+
+int xq_ipc_open(const xq_ipc_handle *handle, void **dev_ptr) {
+    if (!handle || !dev_ptr)
+        return fail(XQ_ERR_INVALID, "ipc_open: null argument");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle->bytes, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                       "ipc_open: cudaIpcOpenMemHandle");
+}
+
+int xq_ipc_close(void *dev_ptr) {
+    return cuda_status(cudaIpcCloseMemHandle(dev_ptr), "ipc_close: cudaIpcCloseMemHandle");
+}
+
+namespace {
+
+// [begin, end) of the groups rank r holds: contiguous blocks, the first
+// n % world ranks one group longer.
+void group_block(int64_t n, int world, int r, int64_t *b, int64_t *e) {
+    const int64_t base = n / world, extra = n % world;
+    *b = r * base + (r < extra ? r : extra);
+    *e = *b + base + (r < extra ? 1 : 0);
+}
+
+int shard_check(const xq_shard_plan *s, const char *who) {
+    if (!s || s->world < 1 || s->world > XQ_SHARD_MAX_RANKS || s->rank < 0 ||
+        s->rank >= s->world || s->rows_per_split <= 0 || s->splits_per_group <= 0 ||
+        s->n_groups < s->world)
+        return fail(XQ_ERR_INVALID, "%s: bad shard plan (1 <= world <= %d, n_groups >= world)",
+                    who, XQ_SHARD_MAX_RANKS);
+    for (int r = 0; r < s->world; ++r)
+        if (!s->exchange[r] || reinterpret_cast<uintptr_t>(s->exchange[r]) % 256)
+            return fail(XQ_ERR_INVALID, "%s: exchange buffer of rank %d missing or unaligned", who,
+                        r);
+    return XQ_OK;
+}
+
+// Local split partials, then local group records (256-byte aligned after them).
+size_t shard_ws_layout(const FaPlan &pl, const xq_shard_plan *s, size_t *rec_off) {
+    int64_t g0, g1;
+    group_block(s->n_groups, s->world, s->rank, &g0, &g1);
+    const size_t rec = (size_t)pl.n_rows * (size_t)(pl.D + 2) * sizeof(float);
+    *rec_off = ((size_t)(g1 - g0) * s->splits_per_group * rec + 255) / 256 * 256;
+    return *rec_off + (size_t)(g1 - g0) * rec;
+}
+
+} // namespace
+
+size_t xq_fa_shard_workspace(const xq_fa_params *p, const xq_shard_plan *s) {
+    FaPlan pl;
+    if (!p || shard_check(s, "fa_shard_workspace") || fa_prepare(p, &pl))
+        return 0;
+    size_t rec_off;
+    return shard_ws_layout(pl, s, &rec_off);
+}
+
+int xq_fa_shard_push(const xq_fa_params *p, const xq_shard_plan *s, void *ws, size_t ws_bytes,
+                     xq_stream_t stream) {
+    int rc = shard_check(s, "fa_shard_push");
+    if (rc)
+        return rc;
+    FaPlan pl;
+    if ((rc = fa_prepare(p, &pl)))
+        return rc;
+    if (p->sinks)
+        return fail(XQ_ERR_UNSUPPORTED, "fa_shard_push: sinks belong to xq_fa_shard_finish");
+    size_t rec_off;
+    const size_t need = shard_ws_layout(pl, s, &rec_off);
+    if (!ws || ws_bytes < need || reinterpret_cast<uintptr_t>(ws) % 256)
+        return fail(XQ_ERR_WORKSPACE, "fa_shard_push: workspace %zu < %zu bytes (256-aligned)",
+                    ws_bytes, need);
+    int64_t g0, g1;
+    group_block(s->n_groups, s->world, s->rank, &g0, &g1);
+    const int64_t n_local = (g1 - g0) * s->splits_per_group;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    // 1. this rank's splits (its k / v views start at its first split's row 0)
+    pl.a.rows_per_split = s->rows_per_split;
+    pl.a.split_begin = 0;
+    pl.a.direct = 0;
+    pl.a.partials = static_cast<float *>(ws);
+    dim3 grid((unsigned)n_local, (unsigned)(pl.a.n_head_kv * pl.n_qblocks), (unsigned)pl.a.n_seq);
+    if ((rc = cuda_status(run_decode(pl, grid, st), "fa_shard_push decode")))
+        return rc;
+    // 2. one (O, lse, 1) record per local group, in split order
+    float *recs = reinterpret_cast<float *>(static_cast<uint8_t *>(ws) + rec_off);
+    if ((rc = cuda_status(xq::launch_merge(pl.a.partials, s->splits_per_group, pl.n_rows, pl.D,
+                                           recs, nullptr, nullptr, 1, st, g1 - g0, true),
+                          "fa_shard_push group records")))
+        return rc;
+    // 3. the records into every rank's exchange half of this step
+    xq::ShardPushArgs a;
+    memset(&a, 0, sizeof(a));
+    const size_t rec_bytes = (size_t)pl.n_rows * (size_t)(pl.D + 2) * sizeof(float);
+    a.src = reinterpret_cast<const float2 *>(recs);
+    a.n8 = (int64_t)((g1 - g0) * rec_bytes / 8);
+    a.dst_off8 = (int64_t)(g0 * rec_bytes / 8);
+    a.parity = (int)(s->step & 1u);
+    a.half_off = (size_t)a.parity * xq::shard_records_bytes(s->n_groups, pl.n_rows, pl.D);
+    a.ctl_off = xq::shard_ctl_off(s->n_groups, pl.n_rows, pl.D);
+    for (int r = 0; r < s->world; ++r)
+        a.peers[r] = static_cast<uint8_t *>(s->exchange[r]);
+    return cuda_status(xq::launch_shard_push(a, s->world, st), "fa_shard_push exchange");
+}
+
+int xq_fa_shard_finish(const xq_shard_plan *s, int64_t n_rows, int64_t D, const float *sinks,
+                       int32_t n_head, float *out, float *lse, xq_stream_t stream) {
+    int rc = shard_check(s, "fa_shard_finish");
+    if (rc)
+        return rc;
+    if (!out || n_rows <= 0 || (D != 64 && D != 128 && D != 256) || (sinks && n_head <= 0))
+        return fail(XQ_ERR_INVALID, "fa_shard_finish: bad arguments");
+    // every rank's chunks, as each pushes its block of groups
+    const size_t rec_bytes = (size_t)n_rows * (size_t)(D + 2) * sizeof(float);
+    int64_t expected = 0;
+    for (int r = 0; r < s->world; ++r) {
+        int64_t b, e;
+        group_block(s->n_groups, s->world, r, &b, &e);
+        expected += xq::shard_chunks((size_t)(e - b) * rec_bytes);
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int parity = (int)(s->step & 1u);
+    void *own = s->exchange[s->rank];
+    if ((rc = cuda_status(xq::launch_shard_wait(own, s->n_groups, n_rows, (int)D, parity,
+                                                (unsigned)expected, st),
+                          "fa_shard_finish wait")))
+        return rc;
+    const float *half = reinterpret_cast<const float *>(
+        static_cast<const uint8_t *>(own) +
+        (size_t)parity * xq::shard_records_bytes(s->n_groups, n_rows, (int)D));
+    return cuda_status(xq::launch_merge(half, s->n_groups, n_rows, (int)D, out, lse, sinks,
+                                        sinks ? n_head : 1, st),
+                       "fa_shard_finish merge");
+}
+
+// ---------------------------------------------------------------------------
 // RKVA range attention.
 
 static int range_prepare(int32_t storage, const void *k, const void *v, uint32_t n_head,

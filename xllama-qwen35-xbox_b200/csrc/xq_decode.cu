@@ -860,8 +860,11 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
     if (n_groups * n_rows * (D / 32) > 0x7fffffff)
         return cudaErrorInvalidValue;
     const int64_t total = n_groups * n_rows;
-    if (total >= 128) {
-        // enough rows to fill the GPU with one warp each
+    if (total >= 128 || records) {
+        // enough rows to fill the GPU with one warp each -- and every record
+        // merge, whatever its row count: a record must come out of the same
+        // kernel (the same summation order) however the groups are spread
+        // over GPUs, or the merged result would depend on the GPU count
         void (*rk)(const float *, int64_t, int64_t, int64_t, float *, float *, const float *,
                    int, int);
         switch (D) {

@@ -145,6 +145,25 @@ struct Kvarn4Launch {
 };
 cudaError_t launch_kvarn4(const Kvarn4Launch &l, cudaStream_t st);
 
+// KV-sharded decode exchange (xq_shard.cu).
+constexpr int kShardMaxRanks = 16;
+struct ShardPushArgs {
+    const float2 *src;  // this rank's group records, contiguous
+    int64_t n8;         // their size in 8-byte units
+    int64_t dst_off8;   // where they start in a half (8-byte units)
+    size_t half_off;    // byte offset of the step's half in an exchange buffer
+    size_t ctl_off;     // byte offset of the counters
+    int parity;
+    uint8_t *peers[kShardMaxRanks];
+};
+size_t shard_records_bytes(int64_t n_groups, int64_t n_rows, int D);
+size_t shard_exchange_bytes(int64_t n_groups, int64_t n_rows, int D);
+size_t shard_ctl_off(int64_t n_groups, int64_t n_rows, int D);
+int64_t shard_chunks(size_t bytes);
+cudaError_t launch_shard_push(const ShardPushArgs &a, int world, cudaStream_t st);
+cudaError_t launch_shard_wait(void *exchange, int64_t n_groups, int64_t n_rows, int D,
+                              int parity, unsigned expected, cudaStream_t st);
+
 cudaError_t launch_dequant(int type, const void *src, uint64_t src_stride, float *dst,
                            uint64_t dst_stride, int64_t n_rows, int64_t n_per_row,
                            cudaStream_t st);

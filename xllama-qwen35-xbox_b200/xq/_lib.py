@@ -24,7 +24,12 @@ EXPORTS = (
     "xq_attend_range_kvarn4_workspace", "xq_attend_range_kvarn4",
     "xq_dequantize_rows", "xq_quantize_rows", "xq_version", "xq_last_error",
     "xq_flash_attn_ext_noalloc", "xq_set_rows", "xq_gated_delta_net_heads",
+    "xq_shard_exchange_bytes", "xq_shard_exchange_alloc", "xq_shard_exchange_free",
+    "xq_shard_exchange_error",
+    "xq_ipc_export", "xq_ipc_open", "xq_ipc_close", "xq_fa_shard_workspace", "xq_fa_shard_push",
+    "xq_fa_shard_finish",
 )
+SHARD_MAX_RANKS = 16
 
 
 class XqError(RuntimeError):
@@ -41,6 +46,17 @@ class Tensor(C.Structure):
 class Kvarn4Desc(C.Structure):
     _fields_ = [("origin", C.c_int32), ("capacity", C.c_int32), ("precision_tail", C.c_int32),
                 ("n_head_kv", C.c_int32)]
+
+
+class IpcHandle(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
+class ShardPlan(C.Structure):
+    _fields_ = [("rows_per_split", C.c_int64), ("splits_per_group", C.c_int64),
+                ("n_groups", C.c_int64), ("rank", C.c_int32), ("world", C.c_int32),
+                ("step", C.c_uint32), ("reserved", C.c_int32),
+                ("exchange", C.c_void_p * 16)]
 
 
 class FaParams(C.Structure):
@@ -84,6 +100,16 @@ def lib():
         "xq_quantize_rows": (C.c_int, [i32, vp, u64, vp, u64, i64, i64, vp]),
         "xq_flash_attn_ext_noalloc": (C.c_int, [P(FaParams), vp]),
         "xq_set_rows": (C.c_int, [P(Tensor), P(Tensor), P(Tensor), vp]),
+        "xq_shard_exchange_bytes": (sz, [i64, i64, i64]),
+        "xq_shard_exchange_alloc": (C.c_int, [sz, P(vp)]),
+        "xq_shard_exchange_free": (C.c_int, [vp]),
+        "xq_shard_exchange_error": (C.c_int, [vp, i64, i64, i64, vp, P(i32)]),
+        "xq_ipc_export": (C.c_int, [vp, P(IpcHandle)]),
+        "xq_ipc_open": (C.c_int, [P(IpcHandle), P(vp)]),
+        "xq_ipc_close": (C.c_int, [vp]),
+        "xq_fa_shard_workspace": (sz, [P(FaParams), P(ShardPlan)]),
+        "xq_fa_shard_push": (C.c_int, [P(FaParams), P(ShardPlan), vp, sz, vp]),
+        "xq_fa_shard_finish": (C.c_int, [P(ShardPlan), i64, i64, vp, i32, vp, vp, vp]),
         "xq_version": (C.c_char_p, []),
         "xq_last_error": (C.c_char_p, []),
     }

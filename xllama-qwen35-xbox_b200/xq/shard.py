@@ -216,3 +216,112 @@ def prefill_part(q, k, v, k_type: int, mask=None, world: int = 1, rank: int = 0,
     o = ops.flash_attn_ext(q[:, h0:h1, r0:r1], k[:, :, c0:c1], v[:, :, c0:c1], k_type,
                            mask=m, scale=scale, out=out, stream=stream)
     return o, plan
+
+
+# ---------------------------------------------------------------------------
+# KV-sharded decode through the C ABI: group records exchanged with NVLink
+# peer stores (xq_fa_shard_push / xq_fa_shard_finish) instead of NCCL.
+
+class ShardExchange:
+    """This rank's exchange buffer (library-allocated, zeroed) and every
+    rank's buffer as this process maps it (CUDA IPC handles moved with an
+    all-gather of the process group).  `buffers` may instead be given: a list
+    of buffers all mapped in this process (one GPU emulating several ranks,
+    for tests)."""
+
+    def __init__(self, n_groups: int, n_rows: int, D: int, group=None, buffers=None):
+        import ctypes as C
+
+        from ._lib import IpcHandle, check, lib
+        self.n_groups, self.n_rows, self.D = n_groups, n_rows, D
+        self._L = lib()
+        self.bytes = self._L.xq_shard_exchange_bytes(n_groups, n_rows, D)
+        self._opened, self._owned = [], []
+        if buffers is not None:
+            self.ptrs = list(buffers)
+            return
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        own = C.c_void_p()
+        check(self._L.xq_shard_exchange_alloc(self.bytes, C.byref(own)))
+        self._owned.append(own.value)
+        h = IpcHandle()
+        check(self._L.xq_ipc_export(own, C.byref(h)))
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(h.bytes), group=group)
+        self.ptrs = []
+        for r in range(world):
+            if r == rank:
+                self.ptrs.append(own.value)
+                continue
+            hr = IpcHandle()
+            C.memmove(hr.bytes, handles[r], 64)
+            p = C.c_void_p()
+            check(self._L.xq_ipc_open(C.byref(hr), C.byref(p)))
+            self._opened.append(p.value)
+            self.ptrs.append(p.value)
+
+    @staticmethod
+    def alloc_local(n_groups: int, n_rows: int, D: int, count: int):
+        """`count` zeroed exchange buffers on the current GPU (emulation)."""
+        import ctypes as C
+
+        from ._lib import check, lib
+        L = lib()
+        nb = L.xq_shard_exchange_bytes(n_groups, n_rows, D)
+        out = []
+        for _ in range(count):
+            p = C.c_void_p()
+            check(L.xq_shard_exchange_alloc(nb, C.byref(p)))
+            out.append(p.value)
+        return out
+
+    def plan(self, rank: int, world: int, rows_per_split: int, splits_per_group: int,
+             step: int):
+        from ._lib import ShardPlan
+        s = ShardPlan()
+        s.rows_per_split, s.splits_per_group, s.n_groups = rows_per_split, splits_per_group, \
+            self.n_groups
+        s.rank, s.world, s.step = rank, world, step & 0xffffffff
+        for r, p in enumerate(self.ptrs[:world]):
+            s.exchange[r] = p
+        return s
+
+    def close(self):
+        for p in self._opened:
+            self._L.xq_ipc_close(p)
+        for p in self._owned:
+            self._L.xq_shard_exchange_free(p)
+        self._opened, self._owned = [], []
+
+
+def shard_decode_step(q, k_local, v_local, k_type: int, exchange: ShardExchange, rank: int,
+                      world: int, rows_per_split: int, splits_per_group: int, step: int,
+                      scale: float = 1.0, out=None, lse=None, ws=None, push=True, finish=True,
+                      stream=None):
+    """One KV-sharded decode step of this rank through the C ABI (push, then
+    finish).  k_local / v_local: this rank's rows (groups head_block-style
+    split_block(n_groups, world, rank)).  Returns out (n_rows, D)."""
+    import ctypes as C
+
+    import torch
+
+    from ._lib import check, lib
+    from .ops import _fa_params, _stream, _workspace
+    n_seq, n_head, n_q, D = q.shape
+    n_rows = n_seq * n_q * n_head
+    o = out if out is not None else torch.empty((n_rows, D), dtype=torch.float32,
+                                                device=q.device)
+    L = lib()
+    s = exchange.plan(rank, world, rows_per_split, splits_per_group, step)
+    st = _stream(stream)
+    if push:
+        dummy = o
+        p = _fa_params(q, k_local, v_local, k_type, k_type, None, None, dummy, scale, 0.0, 0.0, 0)
+        nbytes = L.xq_fa_shard_workspace(C.byref(p), C.byref(s))
+        w = ws if ws is not None else _workspace(nbytes, q.device)
+        check(L.xq_fa_shard_push(C.byref(p), C.byref(s), w.data_ptr(), w.numel(), st))
+    if finish:
+        check(L.xq_fa_shard_finish(C.byref(s), n_rows, D, None, n_head, o.data_ptr(),
+                                   lse.data_ptr() if lse is not None else None, st))
+    return o
