@@ -469,26 +469,52 @@ __global__ void __launch_bounds__(pf::NT, 1)
 }
 
 // Mask block classes for BM x BN blocks: 0 all -inf, 1 all 0, 2 otherwise.
-__global__ void mask_block_map_kernel(const uint8_t *mask, int64_t nb1, int64_t nb2, int64_t nb3,
-                                      int m2, int n_q, int n_kv, int n_qt, int n_kt,
-                                      uint8_t *map) {
+// One CTA per block.  Where the block's rows are whole 16-byte runs (a full
+// block of columns, 16-byte aligned rows) each thread reads half a row with
+// four 16-byte loads and classifies the f16 bit patterns (-inf = 0xFC00,
+// zero = +0 or -0); elsewhere element by element.  The mask is read once, at
+// the HBM rate.
+__global__ void __launch_bounds__(256) mask_block_map_kernel(
+    const uint8_t *mask, int64_t nb1, int64_t nb2, int64_t nb3, int m2, int n_q, int n_kv,
+    int n_qt, int n_kt, int vec, uint8_t *map) {
     const int kt = blockIdx.x, qt = blockIdx.y, plane = blockIdx.z;
     const int i2 = plane % m2, i3 = plane / m2;
+    const uint8_t *base = mask + (int64_t)i2 * nb2 + (int64_t)i3 * nb3;
+    const int r0 = qt * pf::BM, c0 = kt * pf::BN;
+    const int rows = min(pf::BM, n_q - r0);
     int all_inf = 1, all_zero = 1;
-    for (int e = threadIdx.x; e < pf::BM * pf::BN; e += blockDim.x) {
-        const int r = qt * pf::BM + e / pf::BN, c = kt * pf::BN + e % pf::BN;
-        if (r >= n_q || c >= n_kv)
-            continue;
-        const float v = __half2float(*reinterpret_cast<const __half *>(
-            mask + (int64_t)r * nb1 + (int64_t)i2 * nb2 + (int64_t)i3 * nb3 + 2 * (int64_t)c));
-        all_inf &= (v == -INFINITY);
-        all_zero &= (v == 0.0f);
+    if (vec && c0 + pf::BN <= n_kv) {
+        const int r = threadIdx.x >> 1;
+        if (r < rows) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(base + (int64_t)(r0 + r) * nb1 +
+                                                             2 * c0 + 64 * (threadIdx.x & 1));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 w = __ldcs(p + i);
+                const uint32_t x[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    all_inf &= x[j] == 0xFC00FC00u;
+                    all_zero &= (x[j] & 0x7FFF7FFFu) == 0u;
+                }
+            }
+        }
+    } else {
+        for (int e = threadIdx.x; e < pf::BM * pf::BN; e += blockDim.x) {
+            const int r = r0 + e / pf::BN, c = c0 + e % pf::BN;
+            if (r >= n_q || c >= n_kv)
+                continue;
+            const uint16_t h =
+                *reinterpret_cast<const uint16_t *>(base + (int64_t)r * nb1 + 2 * (int64_t)c);
+            all_inf &= h == 0xFC00u;
+            all_zero &= (h & 0x7FFFu) == 0u;
+        }
     }
     all_inf = __syncthreads_and(all_inf);
     all_zero = __syncthreads_and(all_zero);
     if (threadIdx.x == 0) {
         // a block entirely beyond n_kv is dead as well
-        const bool beyond = kt * pf::BN >= n_kv;
+        const bool beyond = c0 >= n_kv;
         map[((size_t)plane * n_qt + qt) * n_kt + kt] =
             (beyond || all_inf) ? 0 : (all_zero ? 1 : 2);
     }
@@ -500,15 +526,66 @@ __global__ void fill_map_kernel(uint8_t *map, size_t n, int n_kt, int n_kv) {
         map[i] = ((int)(i % n_kt) * pf::BN < n_kv) ? 1 : 0;
 }
 
-// Q8_0 / Q4_0 K or V rows (a ggml view: any byte strides, 2-byte aligned) ->
-// contiguous f16 rows [seq][kv head][row][D].  One thread per 8 elements
-// (a quarter of a 32-element block): value = code * f32(d) as ggml's to_float
-// computes it (exact in fp32: <= 8-bit code times an 11-bit scale), then one
-// round-to-nearest to f16; 16-byte stores.
+// Q8_0 / Q4_0 K or V rows (a ggml view) -> contiguous f16 rows [seq][kv head]
+// [row][D]: value = code * f32(d) as ggml's to_float computes it (exact in
+// fp32: <= 8-bit code times an 11-bit scale), then one round-to-nearest to
+// f16.  One warp per row: the row's 4-byte words are read coalesced into
+// shared memory, then each lane widens D / 32 consecutive elements and
+// stores them with one 16- (D = 256) or 8-byte (D = 128) store.  Rows must
+// be 4-byte aligned (every Q8_0 / Q4_0 row of a multiple of 32 elements is a
+// multiple of 4 bytes); kv_to_f16_u16_kernel below takes 2-byte aligned views.
+template <int T, int D>
+__global__ void __launch_bounds__(256) kv_to_f16_kernel(const uint8_t *__restrict__ src,
+                                                        int64_t nb1, int64_t nb2, int64_t nb3,
+                                                        int n_kv, int n_hkv,
+                                                        __half *__restrict__ dst) {
+    constexpr int BB = T == kQ8 ? 34 : 18, REC = D / 32 * BB, WORDS = REC / 4, EPL = D / 32;
+    static_assert(REC % 4 == 0, "rows of whole words");
+    __shared__ uint32_t row_s[8][WORDS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * 8 + warp;  // row in the plane
+    const int plane = blockIdx.y;         // seq * n_hkv + kv head
+    if (r >= n_kv)
+        return;
+    const int hh = plane % n_hkv, sq = plane / n_hkv;
+    const uint32_t *rp = reinterpret_cast<const uint32_t *>(src + (int64_t)r * nb1 +
+                                                            (int64_t)hh * nb2 + (int64_t)sq * nb3);
+    for (int w = lane; w < WORDS; w += 32)
+        row_s[warp][w] = __ldcs(rp + w);
+    __syncwarp();
+    const uint8_t *rb = reinterpret_cast<const uint8_t *>(row_s[warp]);
+    const int j0 = lane * EPL, b = j0 / 32, i0 = j0 % 32; // EPL elements stay in one block
+    const float d = __half2float(*reinterpret_cast<const __half *>(rb + BB * b));
+    uint32_t out[EPL / 2];
+#pragma unroll
+    for (int e = 0; e < EPL; e += 2) {
+        float x[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = i0 + e + k;
+            if constexpr (T == kQ8) {
+                x[k] = (float)(int)(int8_t)rb[BB * b + 2 + i] * d;
+            } else {
+                const uint8_t byte = rb[BB * b + 2 + (i & 15)];
+                x[k] = (float)((int)(i < 16 ? byte & 15u : byte >> 4) - 8) * d;
+            }
+        }
+        const __half2 hv = __floats2half2_rn(x[0], x[1]);
+        out[e / 2] = *reinterpret_cast<const uint32_t *>(&hv);
+    }
+    __half *o = dst + ((int64_t)plane * n_kv + r) * D + j0;
+    if constexpr (EPL == 8)
+        *reinterpret_cast<uint4 *>(o) = make_uint4(out[0], out[1], out[2], out[3]);
+    else
+        *reinterpret_cast<uint2 *>(o) = make_uint2(out[0], out[1]);
+}
+
+// The same widening for views whose rows are only 2-byte aligned: one thread
+// per 8 elements (a quarter of a 32-element block), 2-byte loads.
 template <int T>
-__global__ void kv_to_f16_kernel(const uint8_t *__restrict__ src, int64_t nb1, int64_t nb2,
-                                 int64_t nb3, int D, int n_kv, int n_hkv, int64_t n_units,
-                                 __half *__restrict__ dst) {
+__global__ void kv_to_f16_u16_kernel(const uint8_t *__restrict__ src, int64_t nb1, int64_t nb2,
+                                     int64_t nb3, int D, int n_kv, int n_hkv, int64_t n_units,
+                                     __half *__restrict__ dst) {
     const int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (u >= n_units)
         return;
@@ -585,15 +662,28 @@ size_t prefill_ws_bytes(const PrefillShape &ps) {
 
 static cudaError_t launch_kv_to_f16(int type, const void *src, const int64_t *nb,
                                     const PrefillShape &ps, __half *dst, cudaStream_t st) {
+    const uint8_t *s8 = static_cast<const uint8_t *>(src);
+    const bool words = ((reinterpret_cast<uintptr_t>(src) | (uintptr_t)nb[1] | (uintptr_t)nb[2] |
+                         (uintptr_t)nb[3]) & 3) == 0;
+    if (words) {
+        const dim3 grid((unsigned)((ps.n_kv + 7) / 8), (unsigned)(ps.n_seq_kv * ps.n_head_kv));
+        const int key = (type == kQ8 ? 0 : 2) + (ps.D == 256 ? 1 : 0);
+        switch (key) {
+        case 0: kv_to_f16_kernel<kQ8, 128><<<grid, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.n_kv, ps.n_head_kv, dst); break;
+        case 1: kv_to_f16_kernel<kQ8, 256><<<grid, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.n_kv, ps.n_head_kv, dst); break;
+        case 2: kv_to_f16_kernel<kQ4, 128><<<grid, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.n_kv, ps.n_head_kv, dst); break;
+        default: kv_to_f16_kernel<kQ4, 256><<<grid, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.n_kv, ps.n_head_kv, dst); break;
+        }
+        return cudaGetLastError();
+    }
     const int64_t n_units = (int64_t)ps.n_seq_kv * ps.n_head_kv * ps.n_kv * (ps.D / 8);
     const unsigned blocks = (unsigned)((n_units + 255) / 256);
-    const uint8_t *s8 = static_cast<const uint8_t *>(src);
     if (type == kQ8)
-        kv_to_f16_kernel<kQ8><<<blocks, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.D, ps.n_kv,
-                                                       ps.n_head_kv, n_units, dst);
+        kv_to_f16_u16_kernel<kQ8><<<blocks, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.D, ps.n_kv,
+                                                           ps.n_head_kv, n_units, dst);
     else
-        kv_to_f16_kernel<kQ4><<<blocks, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.D, ps.n_kv,
-                                                       ps.n_head_kv, n_units, dst);
+        kv_to_f16_u16_kernel<kQ4><<<blocks, 256, 0, st>>>(s8, nb[1], nb[2], nb[3], ps.D, ps.n_kv,
+                                                           ps.n_head_kv, n_units, dst);
     return cudaGetLastError();
 }
 
@@ -630,8 +720,10 @@ cudaError_t launch_prefill(const PrefillShape &ps_in, void *ws, cudaStream_t st,
     const int planes = ps.m_planes;
     if (ps.mask) {
         dim3 g(n_kt, n_qt, planes);
+        const int vec = ((reinterpret_cast<uintptr_t>(ps.mask) | (uintptr_t)ps.m_nb1 |
+                          (uintptr_t)ps.m_nb2 | (uintptr_t)ps.m_nb3) & 15) == 0;
         mask_block_map_kernel<<<g, 256, 0, st>>>(ps.mask, ps.m_nb1, ps.m_nb2, ps.m_nb3, ps.m_ne2,
-                                                 ps.n_q, ps.n_kv, n_qt, n_kt, map);
+                                                 ps.n_q, ps.n_kv, n_qt, n_kt, vec, map);
     } else {
         const size_t n = (size_t)planes * n_qt * n_kt;
         fill_map_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(map, n, n_kt, ps.n_kv);
