@@ -22,6 +22,8 @@ CSRC = os.path.join(PKG, "csrc")
 OBJ = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "lib", "libxq_b200.so")
 GGML_LIB = os.path.join(PKG, "lib", "libxq_ggml_b200.so")
+RKVA_SERVER = os.path.join(PKG, "bin", "xq_rkva_server")
+RKVA_SRC = os.path.join(PKG, "rkva", "rkva_server.cpp")
 GGML_SRC = os.path.join(PKG, "ggml", "ggml_xq_backend.cpp")
 INCLUDE = os.path.join(REPO, "include")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -71,6 +73,7 @@ def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = Fa
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
     build_ggml_backend(force)
+    build_rkva_server(force)
     return LIB
 
 
@@ -90,6 +93,23 @@ def build_ggml_backend(force: bool = False) -> str:
     if r.returncode != 0:
         raise RuntimeError(f"ggml backend build failed:\n{r.stderr}")
     return GGML_LIB
+
+
+def build_rkva_server(force: bool = False) -> str:
+    """bin/xq_rkva_server: the RKVA range server over libxq_b200.so."""
+    hdr = os.path.join(PKG, "rkva", "rkva_wire.h")
+    if not force and not _stale(RKVA_SERVER, [RKVA_SRC, hdr, LIB] + _headers()):
+        return RKVA_SERVER
+    os.makedirs(os.path.dirname(RKVA_SERVER), exist_ok=True)
+    cuda = os.path.dirname(os.path.dirname(NVCC))
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-I" + INCLUDE, "-I" + os.path.join(PKG, "rkva"),
+           "-I" + os.path.join(cuda, "include"), RKVA_SRC, "-o", RKVA_SERVER,
+           "-L" + os.path.dirname(LIB), "-lxq_b200", "-L" + os.path.join(cuda, "lib64"),
+           "-lcudart", "-Wl,-rpath,$ORIGIN/../lib"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"RKVA server build failed:\n{r.stderr}")
+    return RKVA_SERVER
 
 
 if __name__ == "__main__":
