@@ -368,11 +368,9 @@ def run_decode(args, rank, world, torch, dist, workload):
     scale = 1.0 / math.sqrt(D)
 
     if workload != "c5":
-        # the library's automatic plan (about two CTAs per SM in one wave)
-        sm = torch.cuda.get_device_properties(dev).multi_processor_count
-        n_splits = max(1, min(math.ceil(2 * sm / (Hkv * n_seq)), math.ceil(w["n_kv"] / 64)))
-        rows_per_split = math.ceil(w["n_kv"] / n_splits)
-        n_splits = math.ceil(w["n_kv"] / rows_per_split)
+        # the library's automatic plan (about two CTAs per SM in one wave,
+        # whole 64-row rounds per split)
+        n_splits, rows_per_split = xq.auto_splits(w["n_kv"], Hkv, 1, H, n_seq)
         sb, se = 0, n_splits
     part_local = torch.empty((se - sb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     if workload == "c5":

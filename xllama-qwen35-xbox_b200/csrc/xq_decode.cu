@@ -405,7 +405,8 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
                                                            float *__restrict__ out,
                                                            float *__restrict__ lse,
                                                            const float *__restrict__ sinks,
-                                                           int n_head, int records) {
+                                                           int n_head, int records,
+                                                           int xchg) {
     using namespace mg;
     constexpr int NC = D / (32 * DL); // CTAs per row (the cluster)
     constexpr int CD = 32 * DL;       // dims per CTA
@@ -432,7 +433,12 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
             v[0] = *p;
         }
     };
-    cluster_arrive_relaxed(); // every peer has started before any DSMEM store below
+    // xchg: a numerator's poison reaches the row's other CTAs through the
+    // cluster; without it (records of the decode kernels, which mark a
+    // non-finite numerator with a NaN denominator) the (m, l) pass below sees
+    // every row's poison in every CTA, and no cluster is launched
+    if (xchg)
+        cluster_arrive_relaxed(); // every peer has started before any DSMEM store below
     // the next decode may launch now; it waits for this grid before it writes
     // the partials read here
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
@@ -613,15 +619,18 @@ __global__ void __launch_bounds__(mg::NT) lse_merge_kernel(const float *__restri
         bad |= __any_sync(0xffffffffu, rowbad);
     }
     // push this CTA's flag into slot `chunk` of every CTA of the row
-    cluster_wait();
-    if (warp == 0 && lane < NC)
-        st_peer(&flags_s[chunk], (uint32_t)lane, bad);
-    cluster_sync();
+    if (xchg) {
+        cluster_wait();
+        if (warp == 0 && lane < NC)
+            st_peer(&flags_s[chunk], (uint32_t)lane, bad);
+        cluster_sync();
+    }
     if (warp == 0) {
-        int poison = 0;
+        int poison = bad;
+        if (xchg)
 #pragma unroll
-        for (int r = 0; r < NC; ++r)
-            poison |= flags_s[r];
+            for (int r = 0; r < NC; ++r)
+                poison |= flags_s[r];
         float *dst = records ? out + row * (D + 2) : out + row * D;
 #pragma unroll
         for (int c = 0; c < DL; ++c)
@@ -854,7 +863,7 @@ cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &c, dim3 grid,
 
 cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
                          float *out, float *lse, const float *sinks, int n_head,
-                         cudaStream_t st, int64_t n_groups, bool records) {
+                         cudaStream_t st, int64_t n_groups, bool records, bool flagged) {
     if (n_rows <= 0 || n_groups <= 0)
         return cudaSuccess;
     if (n_groups * n_rows * (D / 32) > 0x7fffffff)
@@ -885,7 +894,8 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
         return cudaLaunchKernelEx(&rc, rk, partials, n_splits, n_rows, total, out, lse, sinks,
                                   n_head, records ? 1 : 0);
     }
-    void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int, int);
+    void (*kern)(const float *, int64_t, int64_t, float *, float *, const float *, int, int,
+                 int);
     // two dims per lane (8-byte loads) where the records allow it: half the
     // CTAs per row, the same sums (config 2: 15.8 -> 14.9 us a step, while
     // the merge timed on its own did not change)
@@ -927,24 +937,27 @@ cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows
             return e;
     }
     const int nc = D / (32 * dl);
-    // one cluster of nc CTAs per row; launched as a programmatic dependent of
-    // the kernel before it on the stream (the merge waits for it in-kernel)
+    // one cluster of nc CTAs per row (exchanging the row's poison flag), or,
+    // for records whose producer marks poisoned numerators in their
+    // denominators (`flagged`), nc independent CTAs; launched as a
+    // programmatic dependent of the kernel before it on the stream (the merge
+    // waits for it in-kernel)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(n_groups * n_rows * nc), 1, 1);
     cfg.blockDim = dim3(mg::NT, 1, 1);
     cfg.dynamicSmemBytes = stg ? stg_dyn : 0;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)nc;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)nc;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
+    cfg.numAttrs = flagged ? 1 : 2;
     return cudaLaunchKernelEx(&cfg, kern, partials, n_splits, n_rows, out, lse, sinks, n_head,
-                              records ? 1 : 0);
+                              records ? 1 : 0, flagged ? 0 : 1);
 }
 
 } // namespace xq

@@ -786,6 +786,7 @@ __global__ void __launch_bounds__(dm::NT, 1)
     // normalisation folded in, the row's statistics, and its output address
     float4 *wt_s = reinterpret_cast<float4 *>(pt_s); // [8] (pt is free now)
     float **optr_s = reinterpret_cast<float **>(wt_s + 8); // [8]
+    int *nf_s = reinterpret_cast<int *>(optr_s + 8);       // [8] non-finite numerator seen
     if (tid < nj) {
         const int j = tid;
         float M = -INFINITY;
@@ -829,6 +830,7 @@ __global__ void __launch_bounds__(dm::NT, 1)
         static_assert(NWARP == 4, "weights are one float4");
         wt_s[j] = make_float4(f[0] * fin, f[1] * fin, f[2] * fin, f[3] * fin);
         optr_s[j] = optr;
+        nf_s[j] = 0;
     }
     __syncthreads();
 
@@ -853,6 +855,16 @@ __global__ void __launch_bounds__(dm::NT, 1)
             p[0] = o.x;
             p[1] = o.y;
         }
+        if (!a.direct && (!isfinite(o.x) || !isfinite(o.y)))
+            atomicOr(&nf_s[j], 1);
+    }
+    if (!a.direct) {
+        // a live record (denominator != 0; the merge skips empty ones) with a
+        // non-finite numerator carries a NaN denominator, so that every CTA
+        // of the merge sees the row's poison in its (m, l) pass
+        __syncthreads();
+        if (tid < nj && nf_s[tid] && optr_s[tid][D + 1] != 0.0f)
+            optr_s[tid][D + 1] = NAN;
     }
 }
 

@@ -70,9 +70,13 @@ cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3
                               cudaStream_t st);
 // n_groups > 1 merges consecutive blocks of n_splits splits separately; with
 // records, the merged rows are written as partial records (see lse_merge_kernel).
+// flagged: the partials come from fa_decode_mma_kernel, which gives a record
+// whose numerator is not finite a NaN denominator, so the merge needs no
+// cross-CTA exchange of poison flags (same results).
 cudaError_t launch_merge(const float *partials, int64_t n_splits, int64_t n_rows, int D,
                          float *out, float *lse, const float *sinks, int n_head,
-                         cudaStream_t st, int64_t n_groups = 1, bool records = false);
+                         cudaStream_t st, int64_t n_groups = 1, bool records = false,
+                         bool flagged = false);
 
 // One tensor-core prefill launch (F32 q / dst; F16 K/V, or Q8_0 / Q4_0 K/V
 // widened to f16 in the workspace first).
