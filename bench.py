@@ -368,9 +368,9 @@ def run_decode(args, rank, world, torch, dist, workload):
     scale = 1.0 / math.sqrt(D)
 
     if workload != "c5":
-        # the library's automatic plan (about two CTAs per SM in one wave,
-        # whole 64-row rounds per split)
-        n_splits, rows_per_split = xq.auto_splits(w["n_kv"], Hkv, 1, H, n_seq)
+        # the library's automatic plan (every CTA slot of the decode variant
+        # filled in one wave, whole 64-row rounds per split)
+        _, n_splits, rows_per_split = xq.flash_attn_ext_plan(qs[0], sets[0][0], sets[0][1], ty)
         sb, se = 0, n_splits
     part_local = torch.empty((se - sb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     if workload == "c5":

@@ -114,6 +114,15 @@ typedef struct {
 size_t xq_flash_attn_ext_workspace(const xq_fa_params *p);
 int xq_flash_attn_ext(const xq_fa_params *p, void *workspace, size_t workspace_bytes,
                       xq_stream_t stream);
+/* The plan xq_flash_attn_ext makes for these parameters on the current      */
+/* device (host function; no launch): kernel 0 the CUDA-core split-KV       */
+/* decode, 1 the warp-MMA split-KV decode, 2 the tensor-core prefill; for   */
+/* the decodes the KV split count and rows per split (0 for the prefill).   */
+/* A caller reproducing the call's split records with xq_fa_partials       */
+/* passes these.  (ggml-cpu's thread split, ggml-cpu.c:2522 of the snapshot, */
+/* is the reference's counterpart.)                                          */
+int xq_flash_attn_ext_plan(const xq_fa_params *p, int32_t *kernel, int64_t *n_splits,
+                           int64_t *rows_per_split);
 
 /* ------------------------------------------------------------------------ */
 /* Split partials for sharded / remote decode.                               */

@@ -229,11 +229,8 @@ def test_any_workspace_contents_graph_replays_and_the_split_records(ty, D, H, Hk
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
     # the same split records through the separate merge kernel
-    if n_splits:
-        rows = -(-n_kv // n_splits)
-        nsp = -(-n_kv // rows)
-    else:
-        nsp, rows = xq.auto_splits(n_kv, Hkv, 1, H)
+    kern, nsp, rows = xq.flash_attn_ext_plan(tq, tk, tv, ty, n_splits=n_splits)
+    assert kern == 1 and nsp >= 1
     part = xq.fa_partials(tq, tk, tv, ty, rows, 0, nsp, scale=scale)
     two, _ = xq.lse_merge(part, want_lse=False)
     torch.cuda.synchronize()

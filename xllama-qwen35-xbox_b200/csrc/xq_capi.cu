@@ -211,9 +211,9 @@ bool prefill_shape(const xq_fa_params *p, const FaPlan &pl, xq::PrefillShape *ps
     return true;
 }
 
-// Automatic split count: about two CTAs per SM in one wave.
-int64_t auto_splits(int64_t n_kv, int64_t ctas_per_split, int64_t min_rows) {
-    const int64_t target = 2 * (int64_t)sm_count();
+// Automatic split count: about `per_sm` CTAs per SM in one wave.
+int64_t auto_splits(int64_t n_kv, int64_t ctas_per_split, int64_t min_rows, int per_sm = 2) {
+    const int64_t target = per_sm * (int64_t)sm_count();
     int64_t s = (target + ctas_per_split - 1) / ctas_per_split;
     const int64_t cap = (n_kv + min_rows - 1) / min_rows;
     if (s > cap)
@@ -224,7 +224,10 @@ int64_t auto_splits(int64_t n_kv, int64_t ctas_per_split, int64_t min_rows) {
 void plan_splits(FaPlan *pl, int64_t requested) {
     const int64_t n_kv = pl->a.n_kv;
     const int64_t per = (int64_t)pl->a.n_head_kv * pl->n_qblocks * pl->a.n_seq;
-    int64_t s = requested > 0 ? requested : auto_splits(n_kv, per, 64);
+    // the warp-MMA kernel fills every CTA slot its variant has on an SM; the
+    // CUDA-core kernel two
+    const int per_sm = pl->mma ? xq::decode_mma_occupancy(pl->cfg.type, pl->D, pl->cfg.VW) : 2;
+    int64_t s = requested > 0 ? requested : auto_splits(n_kv, per, 64, per_sm);
     if (n_kv == 0)
         s = 1;
     int64_t rows = s > 0 ? (n_kv + s - 1) / s : n_kv;
@@ -232,9 +235,9 @@ void plan_splits(FaPlan *pl, int64_t requested) {
         // automatic plan for the warp-MMA kernel: whole rounds of 64 rows (each
         // of the 4 warps one 16-key group per round, so no warp idles through
         // the last round) and at least 128 rows, which leaves fewer records
-        // to merge on small caches -- config 2: 128 splits of 256 rows, 14.5
-        // against 14.8 us (148 x 222), Q4_0 14.2 against 14.7 us; config 1: 32
-        // splits of 128 rows, 9.95 against 10.7 us (74 x 56)
+        // to merge on small caches -- at two CTAs per SM: config 2 128 splits
+        // of 256 rows, 14.5 against 14.8 us (148 x 222), Q4_0 14.2 against
+        // 14.7 us; config 1: 32 splits of 128 rows, 9.95 against 10.7 us (74 x 56)
         rows = (rows + 63) / 64 * 64;
         if (rows < 128)
             rows = 128;
@@ -453,6 +456,24 @@ int xq_flash_attn_ext(const xq_fa_params *p, void *ws, size_t ws_bytes, xq_strea
         ws_bytes = off;
     }
     return fa_execute(&p2, pl, pre, ps, ws, ws_bytes, st);
+}
+
+int xq_flash_attn_ext_plan(const xq_fa_params *p, int32_t *kernel, int64_t *n_splits,
+                           int64_t *rows_per_split) {
+    FaPlan pl;
+    bool pre = false;
+    xq::PrefillShape ps;
+    size_t main = 0;
+    const int rc = fa_plan(p, &pl, &pre, &ps, &main);
+    if (rc)
+        return rc;
+    if (kernel)
+        *kernel = pre ? 2 : (pl.mma ? 1 : 0);
+    if (n_splits)
+        *n_splits = pre ? 0 : pl.n_splits;
+    if (rows_per_split)
+        *rows_per_split = pre ? 0 : pl.a.rows_per_split;
+    return XQ_OK;
 }
 
 size_t xq_flash_attn_ext_workspace(const xq_fa_params *p) {

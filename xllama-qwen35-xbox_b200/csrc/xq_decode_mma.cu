@@ -272,8 +272,13 @@ __device__ __forceinline__ int out_dim(int m, int row) {
 
 } // namespace dm
 
+// Resident CTAs per SM the kernel is compiled for.  (Three for Q8_0 rows --
+// 162 registers, 73 KB of shared memory, three 16-key rounds per warp on
+// config 2 instead of four -- measured slower: 15.9 against 14.5 us a step.)
+__host__ __device__ constexpr int mma_ctas_per_sm(int) { return 2; }
+
 template <int T, int D, int STAGES, int VW>
-__global__ void __launch_bounds__(dm::NT, 1)
+__global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     fa_decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
     using namespace dm;
@@ -303,7 +308,8 @@ __global__ void __launch_bounds__(dm::NT, 1)
     }
     uint8_t *rings = smem;                                   // [NWARP][STAGES][K|V][GBYTES]
     uint8_t *qsm = rings + BIG;                              // q codes: int8 [8][D] or f16 [8][D]
-    float *dq_s = reinterpret_cast<float *>(qsm + 8 * D * 2); // [NB][8]
+    constexpr int QBYTES = T == kF16 ? 8 * D * 2 : 8 * D;   // f16 or int8 q codes
+    float *dq_s = reinterpret_cast<float *>(qsm + QBYTES); // [NB][8]
     int *qsum_s = reinterpret_cast<int *>(dq_s + NB * 8);    // [NB][8] (8 * sum q)
     float *pt_s = reinterpret_cast<float *>(qsum_s + NB * 8); // [NWARP][16][8]
     float *mw_s = pt_s + NWARP * 16 * 8;                     // [NWARP][8]
@@ -877,7 +883,7 @@ constexpr size_t mma_smem() {
     constexpr size_t ring = (size_t)dm::NWARP * ST * 2 * dm::KG * SS;
     constexpr size_t ow = (size_t)dm::NWARP * 8 * (D + 4) * 4;
     size_t b = ring > ow ? ring : ow;
-    b += (size_t)8 * D * 2 + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
+    b += (size_t)8 * D * (T == kF16 ? 2 : 1) + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
     b += (size_t)dm::NWARP * 128 * 4 + 2 * dm::NWARP * 8 * 4 + 8 * 4 + 8 * 8 + 8 * 4;
     b += (size_t)dm::NWARP * ST * 8; // mbarriers
     return b;
@@ -959,6 +965,52 @@ static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], a);
+}
+
+// CTAs of the variant launch_mma<T, D, ST, VW> that fit on one SM (its
+// shared memory and register bound), asked once per device and variant.
+template <int T, int D, int ST, int VW>
+static int occupancy_of() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return 2;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n > 0)
+        return n;
+    constexpr size_t smem = mma_smem<T, D, ST>();
+    auto kern = fa_decode_mma_kernel<T, D, ST, VW>;
+    static std::atomic<unsigned long long> attr_done{0};
+    if (set_smem_limit((const void *)kern, smem, attr_done) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, dm::NT, smem) != cudaSuccess ||
+        n <= 0) {
+        cudaGetLastError();
+        return 2;
+    }
+    cache[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+template <int T, int D>
+static int mma_occupancy(int vw) {
+    constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
+    if constexpr (rec_bytes(T, D) % 16 == 0)
+        if (vw == 16) {
+            constexpr int STV = dm::tma_mode(T, 16) ? (T == kQ4 ? 4 : 2) : ST;
+            return occupancy_of<T, D, STV, 16>();
+        }
+    if constexpr (rec_bytes(T, D) % 8 == 0)
+        if (vw >= 8)
+            return occupancy_of<T, D, ST, 8>();
+    return occupancy_of<T, D, ST, 4>();
+}
+
+int decode_mma_occupancy(int type, int D, int vw) {
+    switch (type) {
+    case kF16: return D == 128 ? mma_occupancy<kF16, 128>(vw) : mma_occupancy<kF16, 256>(vw);
+    case kQ8: return D == 128 ? mma_occupancy<kQ8, 128>(vw) : mma_occupancy<kQ8, 256>(vw);
+    default: return D == 128 ? mma_occupancy<kQ4, 128>(vw) : mma_occupancy<kQ4, 256>(vw);
+    }
 }
 
 template <int T, int D>

@@ -68,6 +68,8 @@ cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &cfg, dim3 gri
 bool decode_mma_ok(int type, int D, const DecodeArgs &a);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
                               cudaStream_t st);
+// Resident CTAs per SM of the warp-MMA decode variant launch_decode_mma picks.
+int decode_mma_occupancy(int type, int D, int vw);
 // n_groups > 1 merges consecutive blocks of n_splits splits separately; with
 // records, the merged rows are written as partial records (see lse_merge_kernel).
 // flagged: the partials come from fa_decode_mma_kernel, which gives a record

@@ -27,7 +27,7 @@ EXPORTS = (
     "xq_shard_exchange_bytes", "xq_shard_exchange_alloc", "xq_shard_exchange_free",
     "xq_shard_exchange_error",
     "xq_ipc_export", "xq_ipc_open", "xq_ipc_close", "xq_fa_shard_workspace", "xq_fa_shard_push",
-    "xq_fa_shard_finish",
+    "xq_fa_shard_finish", "xq_flash_attn_ext_plan",
 )
 SHARD_MAX_RANKS = 16
 
@@ -81,6 +81,7 @@ def lib():
     P = C.POINTER
     sig = {
         "xq_flash_attn_ext_workspace": (sz, [P(FaParams)]),
+        "xq_flash_attn_ext_plan": (C.c_int, [P(FaParams), P(i32), P(i64), P(i64)]),
         "xq_flash_attn_ext": (C.c_int, [P(FaParams), vp, sz, vp]),
         "xq_fa_partials": (C.c_int, [P(FaParams), i64, i64, i64, vp, vp]),
         "xq_lse_merge": (C.c_int, [vp, i64, i64, i64, vp, vp, vp]),

@@ -113,19 +113,16 @@ def flash_attn_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, k_type: in
     return dst
 
 
-def auto_splits(n_kv: int, n_head_kv: int, n_q: int = 1, n_head: int | None = None,
-                n_seq: int = 1, sm: int | None = None) -> tuple[int, int]:
-    """(n_splits, rows_per_split) of xq_flash_attn_ext's automatic plan for a
-    decode-shaped call on the warp-MMA kernel (D 128 / 256): about two CTAs
-    per SM, rows rounded up to whole 64-row rounds, at least 128."""
-    if sm is None:
-        sm = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
-    G = (n_head // n_head_kv) if n_head else 1
-    per = n_head_kv * -(-(n_q * G) // 8) * n_seq
-    s = max(1, min(-(-2 * sm // per), -(-n_kv // 64)))
-    rows = -(-n_kv // s)
-    rows = max(128, -(-rows // 64) * 64)
-    return -(-n_kv // rows), rows
+def flash_attn_ext_plan(q, k, v, k_type, v_type=None, mask=None, n_splits=0):
+    """(kernel, n_splits, rows_per_split) xq_flash_attn_ext plans for these
+    tensors: kernel 0 CUDA-core decode, 1 warp-MMA decode, 2 tensor-core
+    prefill (n_splits = rows_per_split = 0)."""
+    v_type = k_type if v_type is None else v_type
+    dst = torch.empty(1, device=q.device if q.is_cuda else "cuda")
+    p = _fa_params(q, k, v, k_type, v_type, mask, None, dst, 1.0, 0.0, 0.0, n_splits)
+    kern, ns, rows = C.c_int32(), C.c_int64(), C.c_int64()
+    check(lib().xq_flash_attn_ext_plan(C.byref(p), C.byref(kern), C.byref(ns), C.byref(rows)))
+    return kern.value, ns.value, rows.value
 
 
 def flash_attn_ext_workspace(q, k, v, k_type, v_type=None, mask=None, n_splits=0) -> int:
