@@ -34,6 +34,80 @@ class Graph(C.Structure):
     _fields_ = [("n_nodes", C.c_int), ("nodes", C.POINTER(C.POINTER(Tensor)))]
 
 
+# vtables of ggml_abi_mirror.h (slots the tests call are typed)
+FN = C.CFUNCTYPE
+VP = C.c_void_p
+# (buffer or backend, tensor, data, offset, size): set/get_tensor[_async]
+COPY = FN(None, VP, C.POINTER(Tensor), VP, C.c_size_t, C.c_size_t)
+# (..., offset, size, n_copies, stride_tensor, stride_data): the fork's 2-D slots
+COPY_2D = FN(None, VP, C.POINTER(Tensor), VP, C.c_size_t, C.c_size_t, C.c_size_t, C.c_size_t,
+             C.c_size_t)
+
+
+class RegI(C.Structure):
+    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("get_device_count", FN(C.c_size_t, VP)),
+                ("get_device", FN(VP, VP, C.c_size_t)),
+                ("get_proc_address", FN(VP, VP, C.c_char_p))]
+
+
+class Reg(C.Structure):
+    _fields_ = [("api_version", C.c_int), ("iface", RegI), ("context", VP)]
+
+
+class DevI(C.Structure):
+    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("get_description", FN(C.c_char_p, VP)),
+                ("get_memory", VP), ("get_type", VP), ("get_props", VP),
+                ("init_backend", FN(VP, VP, C.c_char_p)), ("get_buffer_type", FN(VP, VP)),
+                ("get_host_buffer_type", FN(VP, VP)), ("buffer_from_host_ptr", VP),
+                ("supports_op", FN(C.c_bool, VP, C.POINTER(Tensor))),
+                ("supports_buft", FN(C.c_bool, VP, VP)), ("offload_op", VP),
+                ("event_new", FN(VP, VP)), ("event_free", FN(None, VP, VP)),
+                ("event_synchronize", FN(None, VP, VP))]
+
+
+class Dev(C.Structure):
+    _fields_ = [("iface", DevI), ("reg", VP), ("context", VP)]
+
+
+class BuftI(C.Structure):
+    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("alloc_buffer", FN(VP, VP, C.c_size_t)),
+                ("get_alignment", FN(C.c_size_t, VP)), ("get_max_size", VP),
+                ("get_alloc_size", VP), ("is_host", FN(C.c_bool, VP))]
+
+
+class Buft(C.Structure):
+    _fields_ = [("iface", BuftI), ("device", VP), ("context", VP)]
+
+
+class BufI(C.Structure):
+    _fields_ = [("free_buffer", VP), ("get_base", FN(VP, VP)), ("init_tensor", VP),
+                ("memset_tensor", VP),
+                ("set_tensor", COPY), ("get_tensor", COPY), ("set_tensor_2d", COPY_2D), ("get_tensor_2d", COPY_2D),
+                ("cpy_tensor", FN(C.c_bool, VP, C.POINTER(Tensor), C.POINTER(Tensor))),
+                ("clear", FN(None, VP, C.c_uint8)), ("reset", VP)]
+
+
+class Buf(C.Structure):
+    _fields_ = [("iface", BufI), ("buft", VP), ("context", VP), ("size", C.c_size_t),
+                ("usage", C.c_int)]
+
+
+class BackendI(C.Structure):
+    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("free", FN(None, VP)),
+                ("set_tensor_async", COPY), ("get_tensor_async", COPY), ("set_2d_async", COPY_2D),
+                ("get_2d_async", COPY_2D),
+                ("cpy_tensor_async", FN(C.c_bool, VP, VP, C.POINTER(Tensor), C.POINTER(Tensor))),
+                ("synchronize", FN(None, VP)),
+                ("plan_create", VP), ("plan_free", VP), ("plan_update", VP),
+                ("plan_compute", VP), ("graph_compute", FN(C.c_int, VP, C.POINTER(Graph))),
+                ("event_record", FN(None, VP, VP)), ("event_wait", FN(None, VP, VP)),
+                ("graph_optimize", VP)]
+
+
+class Backend(C.Structure):
+    _fields_ = [("guid", VP), ("iface", BackendI), ("device", VP), ("context", VP)]
+
+
 _libs = None
 
 

@@ -93,3 +93,22 @@ def test_registry_without_gpu_registers_nothing():
     if not torch.cuda.is_available():
         assert not be.ggml_xq_b200_register()
         assert mock.xq_mock_registered() == 0
+
+
+def test_proc_address_answers_extra_bufts():
+    """get_proc_address answers "ggml_backend_dev_get_extra_bufts" (as the
+    reference's registry does) with a null-terminated list holding the pinned
+    host buffer type; other names answer null."""
+    import ctypes as C
+    _, be = gh.libs()
+    regp = be.ggml_backend_xq_b200_reg()
+    reg = gh.Reg.from_address(regp)
+    assert reg.iface.get_proc_address(regp, b"ggml_backend_set_n_threads") is None
+    fp = reg.iface.get_proc_address(regp, b"ggml_backend_dev_get_extra_bufts")
+    assert fp
+    lst = C.CFUNCTYPE(C.POINTER(C.c_void_p), C.c_void_p)(fp)(None)
+    assert lst[0] and not lst[1]
+    buft = gh.Buft.from_address(lst[0])
+    assert buft.iface.get_name(lst[0]) == b"XQ_B200_Host"
+    assert buft.iface.is_host(lst[0])
+    assert buft.iface.get_alignment(lst[0]) == 64

@@ -11,73 +11,9 @@ import pytest
 
 import ggml_harness as gh
 import oracle
-from ggml_harness import F32, Q8_0, Tensor, tensor
+from ggml_harness import F32, Q8_0, Backend, Buf, Buft, Dev, Reg, Tensor, tensor
 
 pytestmark = pytest.mark.gpu
-
-FN = C.CFUNCTYPE
-VP = C.c_void_p
-
-
-class RegI(C.Structure):
-    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("get_device_count", FN(C.c_size_t, VP)),
-                ("get_device", FN(VP, VP, C.c_size_t)), ("get_proc_address", VP)]
-
-
-class Reg(C.Structure):
-    _fields_ = [("api_version", C.c_int), ("iface", RegI), ("context", VP)]
-
-
-class DevI(C.Structure):
-    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("get_description", FN(C.c_char_p, VP)),
-                ("get_memory", VP), ("get_type", VP), ("get_props", VP),
-                ("init_backend", FN(VP, VP, C.c_char_p)), ("get_buffer_type", FN(VP, VP)),
-                ("get_host_buffer_type", VP), ("buffer_from_host_ptr", VP),
-                ("supports_op", FN(C.c_bool, VP, C.POINTER(Tensor))),
-                ("supports_buft", FN(C.c_bool, VP, VP)), ("offload_op", VP), ("event_new", VP),
-                ("event_free", VP), ("event_synchronize", VP)]
-
-
-class Dev(C.Structure):
-    _fields_ = [("iface", DevI), ("reg", VP), ("context", VP)]
-
-
-class BuftI(C.Structure):
-    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("alloc_buffer", FN(VP, VP, C.c_size_t)),
-                ("get_alignment", FN(C.c_size_t, VP)), ("get_max_size", VP),
-                ("get_alloc_size", VP), ("is_host", VP)]
-
-
-class Buft(C.Structure):
-    _fields_ = [("iface", BuftI), ("device", VP), ("context", VP)]
-
-
-class BufI(C.Structure):
-    _fields_ = [("free_buffer", VP), ("get_base", FN(VP, VP)), ("init_tensor", VP),
-                ("memset_tensor", VP),
-                ("set_tensor", FN(None, VP, C.POINTER(Tensor), VP, C.c_size_t, C.c_size_t)),
-                ("get_tensor", FN(None, VP, C.POINTER(Tensor), VP, C.c_size_t, C.c_size_t)),
-                ("set_tensor_2d", VP), ("get_tensor_2d", VP), ("cpy_tensor", VP),
-                ("clear", FN(None, VP, C.c_uint8)), ("reset", VP)]
-
-
-class Buf(C.Structure):
-    _fields_ = [("iface", BufI), ("buft", VP), ("context", VP), ("size", C.c_size_t),
-                ("usage", C.c_int)]
-
-
-class BackendI(C.Structure):
-    _fields_ = [("get_name", FN(C.c_char_p, VP)), ("free", FN(None, VP)),
-                ("set_tensor_async", VP), ("get_tensor_async", VP), ("set_2d_async", VP),
-                ("get_2d_async", VP), ("cpy_tensor_async", VP), ("synchronize", FN(None, VP)),
-                ("plan_create", VP), ("plan_free", VP), ("plan_update", VP),
-                ("plan_compute", VP), ("graph_compute", FN(C.c_int, VP, C.POINTER(gh.Graph))),
-                ("event_record", VP), ("event_wait", VP), ("graph_optimize", VP)]
-
-
-class Backend(C.Structure):
-    _fields_ = [("guid", VP), ("iface", BackendI), ("device", VP), ("context", VP)]
-
 
 class Session:
     """Backend + one device buffer carved into tensors."""
@@ -211,5 +147,104 @@ def test_set_rows_through_graph_compute():
         assert s.compute([node]) == 0
         got = s.get(cache, ch.shape, np.uint8)
         assert np.array_equal(got, oracle.set_rows(ch, xh, ih, Q8_0))
+    finally:
+        s.close()
+
+
+def rows_2d(host, off, size, n, stride_tensor, stride_data, dst):
+    """ggml's row-loop definition of set_tensor_2d over a byte image."""
+    for i in range(n):
+        o = off + i * stride_tensor
+        dst[o:o + size] = host[i * stride_data:i * stride_data + size]
+
+
+def test_strided_2d_copies_buffer_and_backend():
+    """The fork's set/get_tensor_2d (buffer) and set/get_tensor_2d_async
+    (backend) slots against ggml's row-by-row definition: pitched strides
+    (one 2-D copy) and overlapping tensor rows (row order decides)."""
+    rng = np.random.default_rng(7)
+    s = Session(1 << 20)
+    try:
+        nbytes = 96 * 1024
+        t = s.alloc(tensor(F32, (nbytes // 4, 1, 1, 1)), nbytes)
+        host_t = rng.integers(0, 256, nbytes, dtype=np.uint8)
+        s.buf.iface.set_tensor(s.bufp, C.byref(t), host_t.ctypes.data, 0, nbytes)
+        cases = [(40, 1000, 64, 1024, 1500),   # pitched on both sides
+                 (8, 700, 50, 512, 700),       # overlapping tensor rows
+                 (0, 256, 33, 2048, 0)]        # one host row broadcast
+        for off, size, n, st, sd in cases:
+            src = rng.integers(0, 256, max(sd * (n - 1) + size, size), dtype=np.uint8)
+            want = host_t.copy()
+            rows_2d(src, off, size, n, st, sd, want)
+            s.buf.iface.set_tensor_2d(s.bufp, C.byref(t), src.ctypes.data, off, size, n, st, sd)
+            assert np.array_equal(s.get(t, (nbytes,), np.uint8), want)
+            hs = max(sd, size)  # host pitch of the read back
+            back = np.zeros(hs * (n - 1) + size + 64, np.uint8)
+            s.buf.iface.get_tensor_2d(s.bufp, C.byref(t), back.ctypes.data, off, size, n, st, hs)
+            for i in range(n):
+                d = i * hs
+                assert np.array_equal(back[d:d + size], want[off + i * st:off + i * st + size])
+            # the backend's async pair on its stream
+            s.buf.iface.set_tensor(s.bufp, C.byref(t), host_t.ctypes.data, 0, nbytes)
+            s.be.iface.set_2d_async(s.bep, C.byref(t), src.ctypes.data, off, size, n, st, sd)
+            back2 = np.zeros_like(back)
+            s.be.iface.get_2d_async(s.bep, C.byref(t), back2.ctypes.data, off, size, n, st, hs)
+            s.be.iface.synchronize(s.bep)
+            assert np.array_equal(back2, back)
+            assert np.array_equal(s.get(t, (nbytes,), np.uint8), want)
+            host_t = want
+    finally:
+        s.close()
+
+
+def test_host_buffer_type_events_and_cross_backend_copy():
+    """Pinned host buffer type (the device's host type and its one extra
+    buffer type), device events recorded and waited on by backends, and
+    cpy_tensor_async between two backends of the device."""
+    rng = np.random.default_rng(9)
+    s = Session(1 << 20)
+    try:
+        hbp = s.dev.iface.get_host_buffer_type(s.devp)
+        hb = Buft.from_address(hbp)
+        assert hb.iface.get_name(hbp) == b"XQ_B200_Host" and hb.iface.is_host(hbp)
+        regp = gh.libs()[1].ggml_backend_xq_b200_reg()
+        fp = Reg.from_address(regp).iface.get_proc_address(regp, b"ggml_backend_dev_get_extra_bufts")
+        extra = C.CFUNCTYPE(C.POINTER(C.c_void_p), C.c_void_p)(fp)(s.devp)
+        assert extra[0] == hbp and not extra[1]
+        assert not s.dev.iface.supports_buft(s.devp, hbp)
+        hbufp = hb.iface.alloc_buffer(hbp, 1 << 16)
+        assert hbufp
+        hbuf = Buf.from_address(hbufp)
+        pinned = tensor(F32, (4096, 1, 1, 1), data=hbuf.iface.get_base(hbufp))
+        pinned.buffer = hbufp
+        x = rng.normal(0, 1, 4096).astype(np.float32)
+        hbuf.iface.set_tensor(hbufp, C.byref(pinned), x.ctypes.data, 0, x.nbytes)
+
+        # pinned -> device on backend 1, event, backend 2 waits then copies on
+        a = s.alloc(tensor(F32, (4096, 1, 1, 1)), x.nbytes)
+        b = s.alloc(tensor(F32, (4096, 1, 1, 1)), x.nbytes)
+        be2p = s.dev.iface.init_backend(s.devp, None)
+        be2 = Backend.from_address(be2p)
+        ev = s.dev.iface.event_new(s.devp)
+        assert ev
+        try:
+            s.be.iface.set_tensor_async(s.bep, C.byref(a), pinned.data, 0, x.nbytes)
+            s.be.iface.event_record(s.bep, ev)
+            be2.iface.event_wait(be2p, ev)
+            assert be2.iface.cpy_tensor_async(s.bep, be2p, C.byref(a), C.byref(b))
+            out = np.zeros(4096, np.float32)
+            be2.iface.get_tensor_async(be2p, C.byref(b), out.ctypes.data, 0, out.nbytes)
+            be2.iface.synchronize(be2p)
+            s.dev.iface.event_synchronize(s.devp, ev)
+            assert np.array_equal(out, x)
+            # a host-buffer source is not this backend's to copy
+            assert not be2.iface.cpy_tensor_async(s.bep, be2p, C.byref(pinned), C.byref(b))
+            back = np.zeros(4096, np.float32)
+            hbuf.iface.get_tensor(hbufp, C.byref(pinned), back.ctypes.data, 0, back.nbytes)
+            assert np.array_equal(back, x)
+        finally:
+            s.dev.iface.event_free(s.devp, ev)
+            be2.iface.free(be2p)
+            s.mock.xq_mock_buffer_free(C.c_void_p(hbufp))
     finally:
         s.close()

@@ -146,8 +146,14 @@ struct ggml_backend_buffer_i {
                        size_t offset, size_t size);
     void (*get_tensor)(ggml_backend_buffer_t buffer, const struct ggml_tensor *tensor, void *data,
                        size_t offset, size_t size);
-    void *set_tensor_2d; // fork slot (2-D strided upload), unused by this backend
-    void *get_tensor_2d; // fork slot (2-D strided download), unused by this backend
+    // fork slots: n_copies rows of `size` bytes, row i at tensor offset
+    // offset + i * stride_tensor and at data + i * stride_data
+    void (*set_tensor_2d)(ggml_backend_buffer_t buffer, struct ggml_tensor *tensor,
+                          const void *data, size_t offset, size_t size, size_t n_copies,
+                          size_t stride_tensor, size_t stride_data);
+    void (*get_tensor_2d)(ggml_backend_buffer_t buffer, const struct ggml_tensor *tensor,
+                          void *data, size_t offset, size_t size, size_t n_copies,
+                          size_t stride_tensor, size_t stride_data);
     bool (*cpy_tensor)(ggml_backend_buffer_t buffer, const struct ggml_tensor *src,
                        struct ggml_tensor *dst);
     void (*clear)(ggml_backend_buffer_t buffer, uint8_t value);
@@ -169,8 +175,12 @@ struct ggml_backend_i {
                              size_t offset, size_t size);
     void (*get_tensor_async)(ggml_backend_t backend, const struct ggml_tensor *tensor, void *data,
                              size_t offset, size_t size);
-    void *set_tensor_2d_async; // fork slot, unused by this backend
-    void *get_tensor_2d_async; // fork slot, unused by this backend
+    void (*set_tensor_2d_async)(ggml_backend_t backend, struct ggml_tensor *tensor,
+                                const void *data, size_t offset, size_t size, size_t n_copies,
+                                size_t stride_tensor, size_t stride_data);
+    void (*get_tensor_2d_async)(ggml_backend_t backend, const struct ggml_tensor *tensor,
+                                void *data, size_t offset, size_t size, size_t n_copies,
+                                size_t stride_tensor, size_t stride_data);
     bool (*cpy_tensor_async)(ggml_backend_t backend_src, ggml_backend_t backend_dst,
                              const struct ggml_tensor *src, struct ggml_tensor *dst);
     void (*synchronize)(ggml_backend_t backend);
@@ -215,6 +225,11 @@ struct ggml_backend_device_i {
 struct ggml_backend_device {
     struct ggml_backend_device_i iface;
     ggml_backend_reg_t reg;
+    void *context;
+};
+
+struct ggml_backend_event {
+    struct ggml_backend_device *device;
     void *context;
 };
 

@@ -7,8 +7,12 @@
 // GATED_DELTA_NET, a device buffer type (:1516-1527) and buffer (:1371-1383),
 // and a backend (:2268-2285) whose graph_compute runs those three ops.  Unlike
 // the reference (whose graph_compute is synchronous, synchronize = nullptr)
-// work is queued on one CUDA stream per backend: set/get_tensor_async and
-// synchronize are implemented.  Nothing falls back to the CPU: an op the
+// work is queued on one CUDA stream per backend: set/get_tensor_async, the
+// fork's 2-D strided copies, cpy_tensor_async between two of these backends,
+// events and synchronize are implemented.  The registry's get_proc_address
+// answers "ggml_backend_dev_get_extra_bufts" as the reference's does (:2462-
+// 2471); the extra buffer type here is pinned host memory, which is also the
+// device's host buffer type.  Nothing falls back to the CPU: an op the
 // kernels cannot take is refused in supports_op, and a failing launch
 // returns GGML_STATUS_FAILED.
 //
@@ -193,6 +197,49 @@ void buf_get(ggml_backend_buffer_t b, const ggml_tensor *t, void *data, size_t o
                        cudaMemcpyDeviceToHost),
             "get_tensor");
 }
+// n_copies rows of `size` bytes between a tensor (row i at byte offset
+// offset + i * stride_tensor) and host memory (row i at data + i *
+// stride_data), the fork's ggml_backend_tensor_{set,get}_2d contract
+// (ggml/src/ggml-backend.cpp:367-409 of the fork).  One strided copy when
+// both strides are pitches cudaMemcpy2D takes, else one copy per row in row
+// order, so that where rows overlap the later one wins as in ggml's loop.
+bool copy_rows(int device, void *dst, size_t dpitch, const void *src, size_t spitch,
+               size_t size, size_t n, cudaMemcpyKind kind, cudaStream_t st, bool async,
+               const char *what) {
+    if (size == 0 || n == 0)
+        return true;
+    int max_pitch = 0;
+    if (cudaDeviceGetAttribute(&max_pitch, cudaDevAttrMaxPitch, device) != cudaSuccess)
+        max_pitch = 0;
+    if (dpitch >= size && spitch >= size && dpitch <= (size_t)max_pitch &&
+        spitch <= (size_t)max_pitch) {
+        return ok_cuda(async ? cudaMemcpy2DAsync(dst, dpitch, src, spitch, size, n, kind, st)
+                             : cudaMemcpy2D(dst, dpitch, src, spitch, size, n, kind),
+                       what);
+    }
+    for (size_t i = 0; i < n; ++i) {
+        char *d = static_cast<char *>(dst) + i * dpitch;
+        const char *s = static_cast<const char *>(src) + i * spitch;
+        if (!ok_cuda(async ? cudaMemcpyAsync(d, s, size, kind, st) : cudaMemcpy(d, s, size, kind),
+                     what))
+            return false;
+    }
+    return true;
+}
+void buf_set_2d(ggml_backend_buffer_t b, ggml_tensor *t, const void *data, size_t off,
+                size_t size, size_t n, size_t stride_tensor, size_t stride_data) {
+    const int dev = static_cast<BufCtx *>(b->context)->device;
+    cudaSetDevice(dev);
+    copy_rows(dev, static_cast<char *>(t->data) + off, stride_tensor, data, stride_data, size, n,
+              cudaMemcpyHostToDevice, nullptr, false, "set_tensor_2d");
+}
+void buf_get_2d(ggml_backend_buffer_t b, const ggml_tensor *t, void *data, size_t off,
+                size_t size, size_t n, size_t stride_tensor, size_t stride_data) {
+    const int dev = static_cast<BufCtx *>(b->context)->device;
+    cudaSetDevice(dev);
+    copy_rows(dev, data, stride_data, static_cast<const char *>(t->data) + off, stride_tensor,
+              size, n, cudaMemcpyDeviceToHost, nullptr, false, "get_tensor_2d");
+}
 bool buf_cpy(ggml_backend_buffer_t b, const ggml_tensor *src, ggml_tensor *dst);
 void buf_clear(ggml_backend_buffer_t b, uint8_t value) {
     cudaSetDevice(static_cast<BufCtx *>(b->context)->device);
@@ -208,6 +255,8 @@ ggml_backend_buffer_i make_buf_iface() {
     i.memset_tensor = buf_memset;
     i.set_tensor = buf_set;
     i.get_tensor = buf_get;
+    i.set_tensor_2d = buf_set_2d;
+    i.get_tensor_2d = buf_get_2d;
     i.cpy_tensor = buf_cpy;
     i.clear = buf_clear;
     return i;
@@ -240,6 +289,68 @@ bool buf_cpy(ggml_backend_buffer_t b, const ggml_tensor *src, ggml_tensor *dst) 
 }
 
 // ---------------------------------------------------------------------------
+// pinned host buffers: the device's host buffer type (staging for the
+// async copies) and its one extra buffer type
+
+struct HostBufCtx {
+    void *base;
+};
+
+bool buft_is_host(ggml_backend_buffer_type_t buft) {
+    return buft && buft->iface.is_host && buft->iface.is_host(buft);
+}
+
+void hbuf_free(ggml_backend_buffer_t b) {
+    auto *c = static_cast<HostBufCtx *>(b->context);
+    cudaFreeHost(c->base);
+    delete c;
+}
+void *hbuf_base(ggml_backend_buffer_t b) { return static_cast<HostBufCtx *>(b->context)->base; }
+void hbuf_memset(ggml_backend_buffer_t, ggml_tensor *t, uint8_t value, size_t off, size_t size) {
+    std::memset(static_cast<char *>(t->data) + off, value, size);
+}
+void hbuf_set(ggml_backend_buffer_t, ggml_tensor *t, const void *data, size_t off, size_t size) {
+    std::memcpy(static_cast<char *>(t->data) + off, data, size);
+}
+void hbuf_get(ggml_backend_buffer_t, const ggml_tensor *t, void *data, size_t off, size_t size) {
+    std::memcpy(data, static_cast<const char *>(t->data) + off, size);
+}
+bool hbuf_cpy(ggml_backend_buffer_t, const ggml_tensor *src, ggml_tensor *dst) {
+    if (!src->buffer || !buft_is_host(src->buffer->buft))
+        return false;
+    std::memcpy(dst->data, src->data, ggml_nbytes(src));
+    return true;
+}
+void hbuf_clear(ggml_backend_buffer_t b, uint8_t value) { std::memset(hbuf_base(b), value, b->size); }
+
+ggml_backend_buffer_i make_host_buf_iface() {
+    ggml_backend_buffer_i i;
+    std::memset(&i, 0, sizeof(i));
+    i.free_buffer = hbuf_free;
+    i.get_base = hbuf_base;
+    i.init_tensor = buf_init_tensor;
+    i.memset_tensor = hbuf_memset;
+    i.set_tensor = hbuf_set;
+    i.get_tensor = hbuf_get;
+    i.cpy_tensor = hbuf_cpy;
+    i.clear = hbuf_clear;
+    return i;
+}
+
+const char *hbuft_name(ggml_backend_buffer_type_t) { return "XQ_B200_Host"; }
+ggml_backend_buffer_t hbuft_alloc(ggml_backend_buffer_type_t buft, size_t size) {
+    if (size == 0)
+        size = 64;
+    void *p = nullptr;
+    // portable: the pages are pinned for every device of the process
+    if (!ok_cuda(cudaHostAlloc(&p, size, cudaHostAllocPortable), "host alloc_buffer"))
+        return nullptr;
+    return ggml_backend_buffer_init(buft, make_host_buf_iface(), new HostBufCtx{p}, size);
+}
+size_t hbuft_align(ggml_backend_buffer_type_t) { return 64; }
+bool hbuft_is_host(ggml_backend_buffer_type_t) { return true; }
+
+// ---------------------------------------------------------------------------
 // backend (one CUDA stream)
 
 struct BackendCtx {
@@ -248,6 +359,7 @@ struct BackendCtx {
     void *ws;
     size_t ws_bytes;
     std::string name;
+    cudaEvent_t order; // orders this stream against another backend's (cpy_tensor_async)
 };
 
 const char *be_name(ggml_backend_t b) { return static_cast<BackendCtx *>(b->context)->name.c_str(); }
@@ -257,6 +369,7 @@ void be_free(ggml_backend_t b) {
     cudaStreamSynchronize(c->stream);
     if (c->ws)
         cudaFree(c->ws);
+    cudaEventDestroy(c->order);
     cudaStreamDestroy(c->stream);
     delete c;
     delete b;
@@ -273,9 +386,74 @@ void be_get_async(ggml_backend_t b, const ggml_tensor *t, void *data, size_t off
                             cudaMemcpyDeviceToHost, c->stream),
             "get_tensor_async");
 }
+void be_set_2d_async(ggml_backend_t b, ggml_tensor *t, const void *data, size_t off,
+                     size_t size, size_t n, size_t stride_tensor, size_t stride_data) {
+    auto *c = static_cast<BackendCtx *>(b->context);
+    copy_rows(c->device, static_cast<char *>(t->data) + off, stride_tensor, data, stride_data,
+              size, n, cudaMemcpyHostToDevice, c->stream, true, "set_tensor_2d_async");
+}
+void be_get_2d_async(ggml_backend_t b, const ggml_tensor *t, void *data, size_t off,
+                     size_t size, size_t n, size_t stride_tensor, size_t stride_data) {
+    auto *c = static_cast<BackendCtx *>(b->context);
+    copy_rows(c->device, data, stride_data, static_cast<const char *>(t->data) + off,
+              stride_tensor, size, n, cudaMemcpyDeviceToHost, c->stream, true,
+              "get_tensor_2d_async");
+}
 void be_sync(ggml_backend_t b) {
     auto *c = static_cast<BackendCtx *>(b->context);
     ok_cuda(cudaStreamSynchronize(c->stream), "synchronize");
+}
+bool is_our_backend(ggml_backend_t b);
+
+// A copy between two tensors in this backend's device buffers, queued on the
+// source backend's stream behind the work both streams already hold; the
+// destination stream then waits for it.  Across GPUs it is a peer copy.
+// Anything else (a host buffer, another backend) answers false and ggml
+// falls back to its synchronous copy.
+bool be_cpy_async(ggml_backend_t bs, ggml_backend_t bd, const ggml_tensor *src,
+                  ggml_tensor *dst) {
+    if (!is_our_backend(bs) || !is_our_backend(bd) || !src->buffer || !dst->buffer ||
+        !is_ours(src->buffer->buft) || !is_ours(dst->buffer->buft))
+        return false;
+    auto *cs = static_cast<BackendCtx *>(bs->context);
+    auto *cd = static_cast<BackendCtx *>(bd->context);
+    const size_t n = ggml_nbytes(src);
+    if (bs != bd) {
+        cudaSetDevice(cd->device);
+        if (!ok_cuda(cudaEventRecord(cd->order, cd->stream), "cpy_tensor_async"))
+            return false;
+        cudaSetDevice(cs->device);
+        if (!ok_cuda(cudaStreamWaitEvent(cs->stream, cd->order, 0), "cpy_tensor_async"))
+            return false;
+    }
+    cudaSetDevice(cs->device);
+    const cudaError_t e =
+        cs->device == cd->device
+            ? cudaMemcpyAsync(dst->data, src->data, n, cudaMemcpyDeviceToDevice, cs->stream)
+            : cudaMemcpyPeerAsync(dst->data, cd->device, src->data, cs->device, n, cs->stream);
+    if (!ok_cuda(e, "cpy_tensor_async"))
+        return false;
+    if (bs != bd) {
+        if (!ok_cuda(cudaEventRecord(cs->order, cs->stream), "cpy_tensor_async"))
+            return false;
+        cudaSetDevice(cd->device);
+        if (!ok_cuda(cudaStreamWaitEvent(cd->stream, cs->order, 0), "cpy_tensor_async"))
+            return false;
+    }
+    return true;
+}
+
+// events: a CUDA event of the device the ggml event was made for
+cudaEvent_t cuda_event(ggml_backend_event_t ev) { return static_cast<cudaEvent_t>(ev->context); }
+void be_event_record(ggml_backend_t b, ggml_backend_event_t ev) {
+    auto *c = static_cast<BackendCtx *>(b->context);
+    cudaSetDevice(c->device);
+    ok_cuda(cudaEventRecord(cuda_event(ev), c->stream), "event_record");
+}
+void be_event_wait(ggml_backend_t b, ggml_backend_event_t ev) {
+    auto *c = static_cast<BackendCtx *>(b->context);
+    cudaSetDevice(c->device);
+    ok_cuda(cudaStreamWaitEvent(c->stream, cuda_event(ev), 0), "event_wait");
 }
 
 bool ensure_ws(BackendCtx *c, size_t need) {
@@ -389,10 +567,17 @@ ggml_backend_i make_backend_iface() {
     i.free = be_free;
     i.set_tensor_async = be_set_async;
     i.get_tensor_async = be_get_async;
+    i.set_tensor_2d_async = be_set_2d_async;
+    i.get_tensor_2d_async = be_get_2d_async;
+    i.cpy_tensor_async = be_cpy_async;
     i.synchronize = be_sync;
     i.graph_compute = be_graph_compute;
+    i.event_record = be_event_record;
+    i.event_wait = be_event_wait;
     return i;
 }
+
+bool is_our_backend(ggml_backend_t b) { return b && b->iface.get_name == be_name; }
 
 // ---------------------------------------------------------------------------
 // device + registry
@@ -416,16 +601,21 @@ void dev_props(ggml_backend_dev_t d, ggml_backend_dev_props *p) {
     p->type = GGML_BACKEND_DEVICE_TYPE_GPU;
     p->device_id = nullptr;
     p->caps.async = true;
-    p->caps.host_buffer = false;
+    p->caps.host_buffer = true;
     p->caps.buffer_from_host_ptr = false;
-    p->caps.events = false;
+    p->caps.events = true;
 }
 ggml_backend_t dev_init(ggml_backend_dev_t d, const char *) {
     auto *dc = static_cast<DevCtx *>(d->context);
     if (!ok_cuda(cudaSetDevice(dc->device), "init_backend"))
         return nullptr;
-    auto *c = new BackendCtx{dc->device, nullptr, nullptr, 0, dc->name};
+    auto *c = new BackendCtx{dc->device, nullptr, nullptr, 0, dc->name, nullptr};
     if (!ok_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "init_backend")) {
+        delete c;
+        return nullptr;
+    }
+    if (!ok_cuda(cudaEventCreateWithFlags(&c->order, cudaEventDisableTiming), "init_backend")) {
+        cudaStreamDestroy(c->stream);
         delete c;
         return nullptr;
     }
@@ -440,11 +630,29 @@ bool dev_supports_op(ggml_backend_dev_t, const ggml_tensor *op) {
 bool dev_supports_buft(ggml_backend_dev_t d, ggml_backend_buffer_type_t buft) {
     return buft == dev_buft(d);
 }
+ggml_backend_event_t dev_event_new(ggml_backend_dev_t d) {
+    cudaEvent_t e = nullptr;
+    if (!ok_cuda(cudaSetDevice(static_cast<DevCtx *>(d->context)->device), "event_new") ||
+        !ok_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event_new"))
+        return nullptr;
+    return new ggml_backend_event{d, e};
+}
+void dev_event_free(ggml_backend_dev_t, ggml_backend_event_t ev) {
+    if (!ev)
+        return;
+    cudaSetDevice(static_cast<DevCtx *>(ev->device->context)->device);
+    cudaEventDestroy(cuda_event(ev));
+    delete ev;
+}
+void dev_event_sync(ggml_backend_dev_t, ggml_backend_event_t ev) {
+    ok_cuda(cudaEventSynchronize(cuda_event(ev)), "event_synchronize");
+}
 
 struct Registry {
     std::vector<DevCtx *> ctx;
     std::vector<ggml_backend_device> devices;
     ggml_backend_reg reg;
+    ggml_backend_buffer_type host_buft; // pinned, shared by every device
 };
 
 const char *reg_name(ggml_backend_reg_t) { return "XQ_B200"; }
@@ -454,7 +662,19 @@ ggml_backend_dev_t reg_device(ggml_backend_reg_t, size_t i) {
     Registry &r = registry();
     return i < r.devices.size() ? &r.devices[i] : nullptr;
 }
-void *reg_proc(ggml_backend_reg_t, const char *) { return nullptr; }
+ggml_backend_buffer_type_t dev_host_buft(ggml_backend_dev_t) { return &registry().host_buft; }
+// ggml_backend_dev_get_extra_bufts_t: a null-terminated list of the buffer
+// types this device offers besides its own (the reference's answer lists its
+// weights buffer type; here it is the pinned host type)
+ggml_backend_buffer_type_t *dev_extra_bufts(ggml_backend_dev_t) {
+    static ggml_backend_buffer_type_t list[2] = {&registry().host_buft, nullptr};
+    return list;
+}
+void *reg_proc(ggml_backend_reg_t, const char *name) {
+    if (name && std::strcmp(name, "ggml_backend_dev_get_extra_bufts") == 0)
+        return reinterpret_cast<void *>(dev_extra_bufts);
+    return nullptr;
+}
 
 Registry &registry() {
     static Registry r;
@@ -468,6 +688,10 @@ Registry &registry() {
             n = 0;
         r.ctx.resize(n);
         r.devices.resize(n);
+        r.host_buft.iface = {hbuft_name, hbuft_alloc, hbuft_align, nullptr, nullptr,
+                             hbuft_is_host};
+        r.host_buft.device = n > 0 ? &r.devices[0] : nullptr;
+        r.host_buft.context = nullptr;
         for (int i = 0; i < n; ++i) {
             cudaDeviceProp prop;
             std::memset(&prop, 0, sizeof(prop));
@@ -489,8 +713,12 @@ Registry &registry() {
             di.get_props = dev_props;
             di.init_backend = dev_init;
             di.get_buffer_type = dev_buft;
+            di.get_host_buffer_type = dev_host_buft;
             di.supports_op = dev_supports_op;
             di.supports_buft = dev_supports_buft;
+            di.event_new = dev_event_new;
+            di.event_free = dev_event_free;
+            di.event_synchronize = dev_event_sync;
             r.devices[i].iface = di;
             r.devices[i].reg = &r.reg;
             r.devices[i].context = dc;
