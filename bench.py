@@ -860,7 +860,7 @@ def run_kvw(args, torch):
         "config": workload_config("kvw"),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
-                     "kernel": "set_rows_kernel", "traffic": profile_traffic("set_rows_kvw")},
+                     "kernel": "set_rows_block_kernel", "traffic": profile_traffic("set_rows_kvw")},
         "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": int(kh.numel() * 8),

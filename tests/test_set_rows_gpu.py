@@ -89,3 +89,51 @@ def test_set_rows_then_decode_reads_the_new_rows():
     v2 = oracle.set_rows(vc, vnew, pos, oracle.Q8_0)
     want = oracle.flash_attn_ext(q, k2, v2, oracle.Q8_0, oracle.Q8_0, scale=1 / 16)
     np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("ty", [oracle.F16, oracle.Q8_0, oracle.Q4_0, oracle.F32])
+@pytest.mark.parametrize("width", [256, 768, 1024, 4096, 4352])
+def test_set_rows_row_widths_and_edge_blocks(ty, width):
+    """Row widths through the warp-per-row kernel (1, 6, 8 and 32 float4
+    units per lane) and past its 4096-element limit (the per-block kernel),
+    with an all-zero block, a block whose largest magnitude appears twice with
+    both signs (Q4_0 keeps the first), tiny and large magnitudes, and a row
+    whose index is negative (left untouched)."""
+    xq = _xq()
+    rng = np.random.default_rng(1000 + width + ty)
+    n_rows, n_tok = 64, 9
+    cache = _cache(rng, ty, 1, n_rows, 1, width)
+    src = rng.normal(0, 1, (1, n_tok, 1, width)).astype(np.float32)
+    src[0, 0, 0, 32:64] = 0.0
+    src[0, 1, 0, 0:32] = rng.normal(0, 1, 32).astype(np.float32)
+    src[0, 1, 0, 5], src[0, 1, 0, 20] = 3.0, -3.0
+    src[0, 2, 0, :32] *= 1e-30
+    src[0, 3, 0, 64:96] *= 1e6
+    idx = rng.choice(n_rows, n_tok, replace=False).astype(np.int64)
+    idx[4] = -1
+    want = oracle.set_rows(cache, src, idx, ty)
+    got = xq.set_rows(torch.from_numpy(cache).cuda(), torch.from_numpy(src).cuda(),
+                      torch.from_numpy(idx).cuda(), ty).cpu().numpy()
+    assert np.array_equal(got.view(np.uint8), want.view(np.uint8))
+
+
+@pytest.mark.parametrize("ty", [oracle.F16, oracle.Q8_0, oracle.Q4_0, oracle.F32])
+@pytest.mark.parametrize("D", [256, 512])
+def test_set_rows_per_head_indices_several_rows_per_warp(ty, D):
+    """Per-head, per-sequence index tensors (i1 = n_head_kv, i2 = n_seq) with
+    rows of 256 and 512 elements, where the row kernel takes four or two rows
+    per warp; row counts that leave the last warp partly empty, and two
+    skipped rows."""
+    xq = _xq()
+    rng = np.random.default_rng(77 + D + ty)
+    n_seq, n_rows, n_hkv, n_tok = 2, 50, 4, 7
+    cache = _cache(rng, ty, n_seq, n_rows, n_hkv, D)
+    src = rng.normal(0, 1, (n_seq, n_tok, n_hkv, D)).astype(np.float32)
+    idx = np.stack([np.stack([rng.choice(n_rows, n_tok, replace=False) for _ in range(n_hkv)])
+                    for _ in range(n_seq)]).astype(np.int32)
+    idx[0, 1, 2] = -3
+    idx[1, 3, 6] = n_rows
+    want = oracle.set_rows(cache, src, idx, ty)
+    got = xq.set_rows(torch.from_numpy(cache).cuda(), torch.from_numpy(src).cuda(),
+                      torch.from_numpy(idx).cuda(), ty).cpu().numpy()
+    assert np.array_equal(got.view(np.uint8), want.view(np.uint8))

@@ -1117,6 +1117,7 @@ int xq_set_rows(const xq_tensor *src, const xq_tensor *idx, const xq_tensor *dst
     a.ne2 = ne2;
     a.ne3 = ne3;
     a.n_units = ne1 * ne2 * ne3 * ((t == XQ_TYPE_F32 || t == XQ_TYPE_F16) ? ne0 : ne0 / 32);
+    a.n_sm = sm_count();
     return cuda_status(xq::launch_set_rows(t, a, reinterpret_cast<cudaStream_t>(stream)),
                        "set_rows");
 }

@@ -509,11 +509,382 @@ __global__ void __launch_bounds__(256) set_rows_coop_kernel(const SetRowsArgs a)
     }
 }
 
+// Float4 unit f = 32 j + lane of a source row (elements 4 f .. 4 f + 3) in
+// dst type T: a 32-element block is the 8 lanes of a quarter warp with
+// set_rows_coop_kernel's arithmetic; Q8_0 / Q4_0 codes and scales go to the
+// staging row `out` (the destination row's bytes), F16 / F32 to `out` itself.
+// Warp-collective for Q8_0 / Q4_0.
+template <int T>
+__device__ __forceinline__ void row_unit(const float4 v, int f, int sub, uint8_t *out) {
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    const int b = f >> 3;
+    if constexpr (T == kF32) {
+        reinterpret_cast<float4 *>(out)[f] = v;
+    } else if constexpr (T == kF16) {
+        const uint32_t lo = (uint32_t)__half_as_ushort(__float2half_rn(e[0])) |
+                            ((uint32_t)__half_as_ushort(__float2half_rn(e[1])) << 16);
+        const uint32_t hi = (uint32_t)__half_as_ushort(__float2half_rn(e[2])) |
+                            ((uint32_t)__half_as_ushort(__float2half_rn(e[3])) << 16);
+        reinterpret_cast<uint2 *>(out)[f] = make_uint2(lo, hi);
+    } else if constexpr (T == kQ8) {
+        float amax = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1)
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = amax / 127.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint32_t w = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            w |= (uint32_t)(uint8_t)(int8_t)roundf(__fmul_rn(e[j], id)) << (8 * j);
+        uint16_t *c = reinterpret_cast<uint16_t *>(out + 34 * b + 2 + 4 * sub);
+        c[0] = (uint16_t)w;
+        c[1] = (uint16_t)(w >> 16);
+        if (sub == 0)
+            *reinterpret_cast<uint16_t *>(out + 34 * b) = __half_as_ushort(__float2half_rn(d));
+    } else {
+        float am = -1.0f, vm = 0.0f;
+        int im = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (fabsf(e[j]) > am) {
+                am = fabsf(e[j]);
+                vm = e[j];
+                im = 4 * sub + j;
+            }
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) {
+            const float a2 = __shfl_xor_sync(0xffffffffu, am, o);
+            const float v2 = __shfl_xor_sync(0xffffffffu, vm, o);
+            const int i2x = __shfl_xor_sync(0xffffffffu, im, o);
+            if (a2 > am || (a2 == am && i2x < im)) {
+                am = a2;
+                vm = v2;
+                im = i2x;
+            }
+        }
+        const float d = (am > 0.0f ? vm : 0.0f) / -8.0f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint32_t q4 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            q4 |= (uint32_t)min(15, (int)(int8_t)__fadd_rn(__fmul_rn(e[j], id), 8.5f)) << (8 * j);
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, q4, 4);
+        if (sub < 4) {
+            const uint32_t w = q4 | (hi << 4);
+            uint16_t *c = reinterpret_cast<uint16_t *>(out + 18 * b + 2 + 4 * sub);
+            c[0] = (uint16_t)w;
+            c[1] = (uint16_t)(w >> 16);
+            if (sub == 0)
+                *reinterpret_cast<uint16_t *>(out + 18 * b) = __half_as_ushort(__float2half_rn(d));
+        }
+    }
+}
+
+// One source row per warp, for destination rows made of whole 16-byte chunks
+// (16-byte aligned; ne0 % 256 == 0 for Q8_0 / Q4_0, % 128 for F16 / F32;
+// ne0 <= 4096).  Each lane loads float4 units 32 j + lane of the row, up to
+// eight in flight before any is used, and converts them with row_unit; Q8_0 /
+// Q4_0 rows are assembled in a per-warp staging row in shared memory and leave
+// in 16-byte stores.  Rows of one sequence (blockIdx.y = i3) go KV head
+// fastest (i2, then i1), so a CTA reads and writes contiguous runs of a
+// token's heads; the row indexing is 32-bit (ne1 * ne2 < 2^31).  (Four rows
+// per warp, more loads in flight at 80 registers, measured slower on 256-wide
+// Q8_0 rows: 32.4 against 29.4 us for a 8192-token K+V write.)
+template <int T>
+__global__ void __launch_bounds__(256) set_rows_row_kernel(const SetRowsArgs a, uint32_t seq_rows,
+                                                           int row_bytes) {
+    constexpr int UJ = 8; // float4 units per lane per load batch
+    extern __shared__ __align__(16) uint8_t stage[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 7;
+    const uint32_t row = blockIdx.x * 8u + (uint32_t)warp;
+    if (row >= seq_rows)
+        return; // warp-uniform, and nothing below synchronises the CTA
+    const uint32_t ne2 = (uint32_t)a.ne2, i3 = blockIdx.y;
+    const uint32_t i1 = row / ne2, i2 = row - i1 * ne2;
+    const uint8_t *ip = a.idx + (uint64_t)i1 * (uint64_t)a.i_nb0 +
+                        (uint64_t)(i2 % (uint32_t)a.i_ne1) * (uint64_t)a.i_nb1 +
+                        (uint64_t)(i3 % (uint32_t)a.i_ne2) * (uint64_t)a.i_nb2;
+    const int64_t dr = a.idx_i64 ? *reinterpret_cast<const int64_t *>(ip)
+                                 : (int64_t)*reinterpret_cast<const int32_t *>(ip);
+    if (dr < 0 || dr >= a.d_rows)
+        return;
+    const float4 *x = reinterpret_cast<const float4 *>(
+        a.src + (uint64_t)i1 * (uint64_t)a.s_nb1 + (uint64_t)i2 * (uint64_t)a.s_nb2 +
+        (uint64_t)i3 * (uint64_t)a.s_nb3);
+    uint8_t *y = a.dst + dr * a.d_nb1 + (uint64_t)i2 * (uint64_t)a.d_nb2 +
+                 (uint64_t)i3 * (uint64_t)a.d_nb3;
+    constexpr bool QUANT = T == kQ8 || T == kQ4;
+    uint8_t *srow = stage + warp * row_bytes;
+    const int nj = (int)(a.ne0 >> 7);
+    for (int j0 = 0; j0 < nj; j0 += UJ) {
+        float4 xv[UJ];
+#pragma unroll
+        for (int u = 0; u < UJ; ++u)
+            if (j0 + u < nj)
+                xv[u] = __ldcs(x + 32 * (j0 + u) + lane); // read once: evict first
+#pragma unroll
+        for (int u = 0; u < UJ; ++u)
+            if (j0 + u < nj) // warp-uniform
+                row_unit<T>(xv[u], 32 * (j0 + u) + lane, sub, QUANT ? srow : y);
+    }
+    if constexpr (QUANT) {
+        __syncwarp();
+        for (int c = lane; c < row_bytes / 16; c += 32)
+            reinterpret_cast<uint4 *>(y)[c] = reinterpret_cast<const uint4 *>(srow)[c];
+    }
+}
+
+template <int T>
+cudaError_t launch_set_rows_rows(const SetRowsArgs &a, uint32_t seq_rows, int rb, cudaStream_t st) {
+    const dim3 grid((seq_rows + 7u) / 8u, (unsigned)a.ne3);
+    const size_t smem = (size_t)8 * rb; // <= 34.8 KB: no opt-in needed
+    set_rows_row_kernel<T><<<grid, 256, smem, st>>>(a, seq_rows, rb);
+    return cudaGetLastError();
+}
+
+// One lane per 32-element block, for Q8_0 / Q4_0 destinations whose rows are
+// 8, 16 or 32 blocks long (ne0 = 256, 512, 1024) and 16-byte aligned.  A tile
+// is 32 consecutive blocks of one sequence (4, 2 or 1 rows, KV head fastest);
+// each warp runs through tiles (persistent grid), its next tile's rows copied
+// into shared memory by 16-byte cp.async (coalesced, two tiles in flight, no
+// spin waits: cp.async.wait_group) while it quantizes the current one.  A lane
+// reads its block's 128 bytes (chunk k of block l at slot k ^ (l & 7): no bank
+// conflicts) and runs the reference quantizer on the block alone
+// (quantize_row_q8_0_ref / quantize_row_q4_0_ref: no shuffles, one division
+// and one reciprocal per block); the 34- or 18-byte blocks are packed into a
+// per-warp staging area in row order and the tile's rows leave in 16-byte
+// stores.  A row whose index is out of range is not written.
+namespace srb {
+constexpr int TILE_IN = 32 * 128;                  // input bytes per tile
+__host__ __device__ constexpr int out_bytes(int T) { return 32 * (T == kQ8 ? 34 : 18); }
+__host__ __device__ constexpr int warp_bytes(int T) { return 2 * TILE_IN + out_bytes(T); }
+} // namespace srb
+
+template <int T, int LNB>
+__global__ void __launch_bounds__(256) set_rows_block_kernel(const SetRowsArgs a,
+                                                             uint32_t seq_rows, uint32_t tiles_seq) {
+    constexpr int NB = 1 << LNB;               // blocks per row
+    constexpr int BB = T == kQ8 ? 34 : 18;     // bytes per block
+    constexpr int RB = NB * BB;                // bytes per row (a multiple of 16)
+    constexpr int RPT = 32 / NB;               // rows per tile
+    constexpr int CPR = RB / 16;               // 16-byte output chunks per row
+    static_assert(RB % 16 == 0, "whole chunks per row");
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t *in = smem + warp * srb::warp_bytes(T); // [2][32 blocks][128 B]
+    uint8_t *out = in + 2 * srb::TILE_IN;           // [32 blocks][BB]
+    const uint32_t ne2 = (uint32_t)a.ne2;
+    const uint32_t n_tiles = tiles_seq * (uint32_t)a.ne3; // < 2^31 (checked by the launcher)
+    const uint32_t stride = gridDim.x * 8u;
+    const uint32_t first = blockIdx.x * 8u + (uint32_t)warp;
+
+    // tile -> buffer: lane copies chunks lane + 32 m (row m >> (LNB - 2) of
+    // the tile for NB >= 4), always one commit group (possibly empty)
+    auto issue = [&](uint32_t tile, int buf) {
+        if (tile < n_tiles) {
+            const uint32_t i3 = tile / tiles_seq;
+            const uint32_t row0 = (tile - i3 * tiles_seq) * RPT;
+            const uint32_t base = smem_u32(in + buf * srb::TILE_IN);
+            uint32_t i1 = row0 / ne2, i2 = row0 - i1 * ne2; // stepped per row below
+#pragma unroll
+            for (int k = 0; k < RPT; ++k) {
+                if (row0 + k >= seq_rows)
+                    break;
+                const uint8_t *src = a.src + (uint64_t)i1 * (uint64_t)a.s_nb1 +
+                                     (uint64_t)i2 * (uint64_t)a.s_nb2 +
+                                     (uint64_t)i3 * (uint64_t)a.s_nb3;
+                if (++i2 == ne2) {
+                    i2 = 0;
+                    ++i1;
+                }
+#pragma unroll
+                for (int m = 0; m < 8 / RPT; ++m) {
+                    const int w = lane + 32 * m;          // 16-byte chunk within the row
+                    const int l = k * NB + (w >> 3), kk = w & 7; // block of the tile, chunk
+                    cp_async<16>(base + 128 * l + 16 * (kk ^ (l & 7)), src + 16 * w);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+
+    // this lane's row of a tile: its index (loaded one tile ahead, so the
+    // load's latency hides behind the current tile) and its address terms
+    struct RowRef {
+        int64_t dr; // destination row, or -1
+        uint32_t i2, i3;
+    };
+    auto row_ref = [&](uint32_t tile) {
+        RowRef r = {-1, 0u, 0u};
+        if (tile >= n_tiles)
+            return r;
+        const uint32_t i3 = tile / tiles_seq;
+        const uint32_t row = (tile - i3 * tiles_seq) * RPT + (uint32_t)(lane >> LNB);
+        if (row >= seq_rows)
+            return r;
+        const uint32_t i1 = row / ne2, i2 = row - i1 * ne2;
+        // ggml broadcasts the index over heads and sequences (i_ne1 | ne2,
+        // i_ne2 | ne3); the usual 1 and full extents need no division
+        const uint32_t in1 = (uint32_t)a.i_ne1, in2 = (uint32_t)a.i_ne2;
+        const uint32_t j2 = in1 == 1u ? 0u : in1 == ne2 ? i2 : i2 % in1;
+        const uint32_t j3 = in2 == 1u ? 0u : in2 == (uint32_t)a.ne3 ? i3 : i3 % in2;
+        const uint8_t *ip = a.idx + (uint64_t)i1 * (uint64_t)a.i_nb0 +
+                            (uint64_t)j2 * (uint64_t)a.i_nb1 + (uint64_t)j3 * (uint64_t)a.i_nb2;
+        r.dr = a.idx_i64 ? *reinterpret_cast<const int64_t *>(ip)
+                         : (int64_t)*reinterpret_cast<const int32_t *>(ip);
+        r.i2 = i2;
+        r.i3 = i3;
+        return r;
+    };
+
+    issue(first, 0);
+    issue(first + stride, 1);
+    RowRef next = row_ref(first);
+    int buf = 0;
+    for (uint32_t tile = first; tile < n_tiles; tile += stride, buf ^= 1) {
+        const RowRef cur = next;
+        next = row_ref(tile + stride);
+        cp_async_wait<1>(); // this tile's copies (the next tile's may be in flight)
+        __syncwarp();       // ... and every other lane's
+        float x[32];
+        {
+            const uint8_t *blkin = in + buf * srb::TILE_IN + 128 * lane;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float4 v = *reinterpret_cast<const float4 *>(blkin + 16 * (k ^ (lane & 7)));
+                x[4 * k] = v.x;
+                x[4 * k + 1] = v.y;
+                x[4 * k + 2] = v.z;
+                x[4 * k + 3] = v.w;
+            }
+        }
+        uint16_t *blk = reinterpret_cast<uint16_t *>(out + BB * lane); // 2-byte aligned
+        if constexpr (T == kQ8) {
+            float m[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                m[j] = fmaxf(fabsf(x[j]), fabsf(x[j + 16]));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int j = 0; j < w; ++j)
+                    m[j] = fmaxf(m[j], m[j + w]);
+            const float d = m[0] / 127.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            blk[0] = __half_as_ushort(__float2half_rn(d));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t c0 = (uint8_t)(int8_t)roundf(__fmul_rn(x[2 * j], id));
+                const uint32_t c1 = (uint8_t)(int8_t)roundf(__fmul_rn(x[2 * j + 1], id));
+                blk[1 + j] = (uint16_t)(c0 | (c1 << 8));
+            }
+        } else {
+            // the first element of largest magnitude, in element order
+            float amax = 0.0f, vmax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (amax < fabsf(x[j])) {
+                    amax = fabsf(x[j]);
+                    vmax = x[j];
+                }
+            const float d = vmax / -8.0f;
+            const float id = d != 0.0f ? 1.0f / d : 0.0f;
+            blk[0] = __half_as_ushort(__float2half_rn(d));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t w = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int e = 2 * j + h;
+                    const uint32_t lo =
+                        (uint32_t)min(15, (int)(int8_t)__fadd_rn(__fmul_rn(x[e], id), 8.5f));
+                    const uint32_t hi =
+                        (uint32_t)min(15, (int)(int8_t)__fadd_rn(__fmul_rn(x[16 + e], id), 8.5f));
+                    w |= (lo | (hi << 4)) << (8 * h);
+                }
+                blk[1 + j] = (uint16_t)w;
+            }
+        }
+        uint8_t *yrow = nullptr; // this lane's destination row (null: not written)
+        if (cur.dr >= 0 && cur.dr < a.d_rows)
+            yrow = a.dst + cur.dr * a.d_nb1 + (uint64_t)cur.i2 * (uint64_t)a.d_nb2 +
+                   (uint64_t)cur.i3 * (uint64_t)a.d_nb3;
+        // destination rows of the tile: row k's pointer from its first block's lane
+        uint8_t *yk[RPT];
+#pragma unroll
+        for (int k = 0; k < RPT; ++k)
+            yk[k] = reinterpret_cast<uint8_t *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(yrow), k * NB));
+        __syncwarp();
+        for (int c = lane; c < RPT * CPR; c += 32) {
+            const int k = c / CPR, off = c - k * CPR;
+            uint8_t *y = yk[0];
+#pragma unroll
+            for (int kk = 1; kk < RPT; ++kk)
+                y = k == kk ? yk[kk] : y;
+            if (y)
+                reinterpret_cast<uint4 *>(y)[off] = reinterpret_cast<const uint4 *>(out)[c];
+        }
+        __syncwarp(); // the input buffer and the staging area are free again
+        issue(tile + 2 * stride, buf); // no wrap: n_tiles + 2 stride < 2^32
+    }
+    cp_async_wait<0>(); // no copy outlives the kernel
+}
+
+template <int T>
+cudaError_t launch_set_rows_blocks(const SetRowsArgs &a, uint32_t seq_rows, cudaStream_t st) {
+    static std::atomic<unsigned long long> attr[3][2];
+    const int nb = (int)(a.ne0 / 32), lnb = nb == 8 ? 3 : nb == 16 ? 4 : 5;
+    const uint32_t rpt = 32u / (uint32_t)nb;
+    const uint32_t tiles_seq = (seq_rows + rpt - 1) / rpt;
+    const uint64_t n_tiles = (uint64_t)tiles_seq * (uint64_t)a.ne3;
+    const size_t smem = (size_t)8 * srb::warp_bytes(T); // 71 or 74 KB: three CTAs per SM
+    const uint64_t want = (n_tiles + 7) / 8, cap = (uint64_t)3 * (a.n_sm > 0 ? a.n_sm : 148);
+    const dim3 grid((unsigned)(want < cap ? want : cap));
+    if (n_tiles > 0x7fffffffull || grid.x > 65535u)
+        return cudaErrorInvalidValue; // the launcher only sends shapes below these bounds
+    const void *kern = lnb == 3   ? (const void *)set_rows_block_kernel<T, 3>
+                       : lnb == 4 ? (const void *)set_rows_block_kernel<T, 4>
+                                  : (const void *)set_rows_block_kernel<T, 5>;
+    cudaError_t e = set_smem_limit(kern, smem, attr[lnb - 3][T == kQ8 ? 0 : 1]);
+    if (e != cudaSuccess)
+        return e;
+    if (lnb == 3)
+        set_rows_block_kernel<T, 3><<<grid, 256, smem, st>>>(a, seq_rows, tiles_seq);
+    else if (lnb == 4)
+        set_rows_block_kernel<T, 4><<<grid, 256, smem, st>>>(a, seq_rows, tiles_seq);
+    else
+        set_rows_block_kernel<T, 5><<<grid, 256, smem, st>>>(a, seq_rows, tiles_seq);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_set_rows(int type, const SetRowsArgs &a, cudaStream_t st) {
     if (a.n_units <= 0)
         return cudaSuccess;
     const bool src16 = ((reinterpret_cast<uintptr_t>(a.src) | (uintptr_t)a.s_nb1 |
                          (uintptr_t)a.s_nb2 | (uintptr_t)a.s_nb3) & 15) == 0;
+    const bool dst16 = ((reinterpret_cast<uintptr_t>(a.dst) | (uintptr_t)a.d_nb1 |
+                         (uintptr_t)a.d_nb2 | (uintptr_t)a.d_nb3) & 15) == 0;
+    const bool quant = type == kQ8 || type == kQ4;
+    const int64_t seq_rows = a.ne1 * a.ne2;
+    if (src16 && dst16 && a.ne0 <= 4096 && a.ne0 % (quant ? 256 : 128) == 0 &&
+        seq_rows <= 0x7fffffffll && a.ne3 <= 65535) {
+        const int rb = type == kQ8 ? 34 * (int)(a.ne0 / 32) : type == kQ4 ? 18 * (int)(a.ne0 / 32) : 0;
+        const uint32_t sr = (uint32_t)seq_rows;
+        if (quant && (a.ne0 == 256 || a.ne0 == 512 || a.ne0 == 1024) &&
+            (uint64_t)((sr + 31u) / 32u * (a.ne0 / 32)) * (uint64_t)a.ne3 <= 0x3fffffffull &&
+            a.n_sm > 0 && a.n_sm <= 8192)
+            return type == kQ8 ? launch_set_rows_blocks<kQ8>(a, sr, st)
+                               : launch_set_rows_blocks<kQ4>(a, sr, st);
+        switch (type) {
+        case kF32: return launch_set_rows_rows<kF32>(a, sr, rb, st);
+        case kF16: return launch_set_rows_rows<kF16>(a, sr, rb, st);
+        case kQ8: return launch_set_rows_rows<kQ8>(a, sr, rb, st);
+        case kQ4: return launch_set_rows_rows<kQ4>(a, sr, rb, st);
+        default: return cudaErrorInvalidValue;
+        }
+    }
     const int64_t planes = a.ne2 * a.ne3, plane_units = a.ne1 * (a.ne0 / 32);
     if ((type == kQ8 || type == kQ4) && src16 && planes <= 65535 &&
         plane_units * 8 <= 0x7fffffffll) {

@@ -112,6 +112,7 @@ struct SetRowsArgs {
     uint8_t *dst;                   // [ne0, d_rows, ne2, ne3]
     int64_t d_nb1, d_nb2, d_nb3, d_rows;
     int64_t ne0, ne1, ne2, ne3, n_units;
+    int n_sm; // SMs of the device (persistent grids)
 };
 cudaError_t launch_set_rows(int type, const SetRowsArgs &a, cudaStream_t st);
 
