@@ -18,11 +18,13 @@
 #define XQ_GGML_BACKEND_H
 
 #include <stdbool.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
 #endif
 
+struct ggml_backend;
 struct ggml_backend_reg;
 struct ggml_tensor;
 
@@ -35,6 +37,18 @@ bool ggml_xq_b200_register(void);
 
 /* The predicate behind the device's supports_op (pure host logic). */
 bool ggml_xq_b200_supports_op(const struct ggml_tensor *op);
+
+/* GPU time per op of one XQ_B200 backend created with XQ_GGML_TIMING=1 in the
+ * environment: CUDA events around every node on the backend's stream, read
+ * back as they complete (all of them at synchronize); op 0 FLASH_ATTN_EXT,
+ * 1 GATED_DELTA_NET, 2 SET_ROWS.  nodes = timed nodes, ms = their summed GPU
+ * time, untimed = nodes whose events failed.  The totals are also printed to
+ * stderr when the backend is freed.  Every node also gets an NVTX range named
+ * after its op.  Replaces the reference backend's GPU timestamp accounting
+ * (src/bridge/ggml_d3d12.cpp:1897-1903, 2148-2151, 2202-2221).  False for
+ * another backend, an op index outside 0..2 or a backend without timing. */
+bool ggml_xq_b200_backend_op_time(struct ggml_backend *backend, int op, uint64_t *nodes,
+                                  double *ms, uint64_t *untimed);
 
 #ifdef __cplusplus
 }

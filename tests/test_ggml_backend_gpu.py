@@ -248,3 +248,50 @@ def test_host_buffer_type_events_and_cross_backend_copy():
             s.mock.xq_mock_buffer_free(C.c_void_p(hbufp))
     finally:
         s.close()
+
+
+def test_per_op_gpu_timing():
+    """A backend created with XQ_GGML_TIMING=1 keeps per-op GPU time (CUDA
+    events around every node, read at synchronize); a backend without it
+    answers false."""
+    import os
+    _, be = gh.libs()
+    be.ggml_xq_b200_backend_op_time.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_uint64),
+                                                C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
+    be.ggml_xq_b200_backend_op_time.restype = C.c_bool
+    rng = np.random.default_rng(3)
+    os.environ["XQ_GGML_TIMING"] = "1"
+    try:
+        s = Session(64 << 20)
+    finally:
+        del os.environ["XQ_GGML_TIMING"]
+    plain = Session(1 << 20)
+    try:
+        D, H, Hkv, n_kv = 128, 8, 2, 2048
+        qh = rng.normal(0, 1, (1, H, 1, D)).astype(np.float32)
+        kh = oracle.quantize(gh.F16, rng.normal(0, 1, (1, n_kv, Hkv, D)).astype(np.float32))
+        vh = oracle.quantize(gh.F16, rng.normal(0, 1, (1, n_kv, Hkv, D)).astype(np.float32))
+        nb = (2, Hkv * 2 * D, 2 * D, n_kv * Hkv * 2 * D)
+        q = s.place(tensor(F32, (D, 1, H, 1)), qh)
+        k = s.place(tensor(gh.F16, (D, n_kv, Hkv, 1), nb=nb), kh)
+        v = s.place(tensor(gh.F16, (D, n_kv, Hkv, 1), nb=nb), vh)
+        out = gh.fa_node(q, k, v, scale=D ** -0.5)
+        s.alloc(out, H * D * 4)
+        for _ in range(3):
+            assert s.compute([out]) == 0
+        nodes, ms, untimed = C.c_uint64(), C.c_double(), C.c_uint64()
+        assert be.ggml_xq_b200_backend_op_time(s.bep, 0, C.byref(nodes), C.byref(ms),
+                                               C.byref(untimed))
+        assert nodes.value == 3 and untimed.value == 0 and 0.0 < ms.value < 1000.0
+        assert be.ggml_xq_b200_backend_op_time(s.bep, 1, C.byref(nodes), C.byref(ms),
+                                               C.byref(untimed))
+        assert nodes.value == 0 and ms.value == 0.0
+        assert not be.ggml_xq_b200_backend_op_time(s.bep, 3, None, None, None)
+        assert not be.ggml_xq_b200_backend_op_time(plain.bep, 0, None, None, None)
+        np.testing.assert_allclose(
+            s.get(out, (1, 1, H, D)),
+            oracle.flash_attn_ext(qh, kh, vh, gh.F16, gh.F16, scale=D ** -0.5),
+            rtol=1e-2, atol=2e-3)
+    finally:
+        plain.close()
+        s.close()

@@ -27,8 +27,10 @@
 #endif
 
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -353,20 +355,85 @@ bool hbuft_is_host(ggml_backend_buffer_type_t) { return true; }
 // ---------------------------------------------------------------------------
 // backend (one CUDA stream)
 
-struct BackendCtx {
-    int device;
-    cudaStream_t stream;
-    void *ws;
-    size_t ws_bytes;
-    std::string name;
-    cudaEvent_t order; // orders this stream against another backend's (cpy_tensor_async)
+// Per-op GPU time of a backend created with XQ_GGML_TIMING=1: CUDA events
+// around every node on the backend's stream, read back at synchronize (the
+// reference backend's timestamp accounting, ggml_d3d12.cpp:1897-1903,
+// 2148-2151, 2202-2221).  Ops: 0 FLASH_ATTN_EXT, 1 GATED_DELTA_NET, 2 SET_ROWS.
+constexpr int kTimedOps = 3;
+const char *const kOpNames[kTimedOps] = {"FLASH_ATTN_EXT", "GATED_DELTA_NET", "SET_ROWS"};
+struct OpTime {
+    uint64_t nodes = 0, untimed = 0;
+    double ms = 0.0;
 };
+struct PendingTime {
+    int op;
+    cudaEvent_t begin, end;
+};
+
+struct BackendCtx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+    std::string name;
+    cudaEvent_t order = nullptr; // orders this stream against another backend's (cpy_tensor_async)
+    bool timing = false;
+    OpTime times[kTimedOps];
+    std::vector<PendingTime> pending; // timed nodes not read back yet
+    std::vector<cudaEvent_t> pool;    // timing events for reuse
+};
+
+cudaEvent_t take_event(BackendCtx *c) {
+    if (!c->pool.empty()) {
+        cudaEvent_t e = c->pool.back();
+        c->pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    return cudaEventCreate(&e) == cudaSuccess ? e : nullptr;
+}
+
+// Read back the timed nodes whose end event has completed, in order (all of
+// them after a stream synchronize).
+void drain_times(BackendCtx *c) {
+    size_t done = 0;
+    for (; done < c->pending.size(); ++done) {
+        PendingTime &p = c->pending[done];
+        const cudaError_t q = cudaEventQuery(p.end);
+        if (q == cudaErrorNotReady)
+            break;
+        float ms = 0.0f;
+        if (q == cudaSuccess && cudaEventElapsedTime(&ms, p.begin, p.end) == cudaSuccess) {
+            c->times[p.op].nodes++;
+            c->times[p.op].ms += ms;
+        } else {
+            cudaGetLastError();
+            c->times[p.op].untimed++;
+        }
+        c->pool.push_back(p.begin);
+        c->pool.push_back(p.end);
+    }
+    c->pending.erase(c->pending.begin(), c->pending.begin() + (std::ptrdiff_t)done);
+}
 
 const char *be_name(ggml_backend_t b) { return static_cast<BackendCtx *>(b->context)->name.c_str(); }
 void be_free(ggml_backend_t b) {
     auto *c = static_cast<BackendCtx *>(b->context);
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
+    drain_times(c);
+    if (c->timing)
+        for (int i = 0; i < kTimedOps; ++i)
+            if (c->times[i].nodes || c->times[i].untimed)
+                std::fprintf(stderr, "[xq_b200] %s %s: %llu nodes, %.3f ms GPU, %llu untimed\n",
+                             c->name.c_str(), kOpNames[i], (unsigned long long)c->times[i].nodes,
+                             c->times[i].ms, (unsigned long long)c->times[i].untimed);
+    for (const PendingTime &p : c->pending) {
+        cudaEventDestroy(p.begin);
+        cudaEventDestroy(p.end);
+    }
+    for (cudaEvent_t e : c->pool)
+        cudaEventDestroy(e);
     if (c->ws)
         cudaFree(c->ws);
     cudaEventDestroy(c->order);
@@ -402,6 +469,7 @@ void be_get_2d_async(ggml_backend_t b, const ggml_tensor *t, void *data, size_t 
 void be_sync(ggml_backend_t b) {
     auto *c = static_cast<BackendCtx *>(b->context);
     ok_cuda(cudaStreamSynchronize(c->stream), "synchronize");
+    drain_times(c);
 }
 bool is_our_backend(ggml_backend_t b);
 
@@ -537,6 +605,24 @@ ggml_status be_graph_compute(ggml_backend_t b, ggml_cgraph *g) {
         ggml_tensor *node = ggml_graph_node(g, i);
         if (is_view_op(node->op) || !(node->flags & GGML_TENSOR_FLAG_COMPUTE))
             continue;
+        const int oi = node->op == GGML_OP_FLASH_ATTN_EXT    ? 0
+                       : node->op == GGML_OP_GATED_DELTA_NET ? 1
+                       : node->op == GGML_OP_SET_ROWS        ? 2
+                                                             : -1;
+        // one NVTX range per node (free unless a profiler is attached)
+        nvtxRangePushA(oi >= 0 ? kOpNames[oi] : "unclaimed");
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        if (c->timing && oi >= 0) {
+            if (c->pending.size() >= 1024)
+                drain_times(c); // completed nodes only: never blocks
+            e0 = take_event(c);
+            e1 = take_event(c);
+            if (e0 && cudaEventRecord(e0, c->stream) != cudaSuccess) {
+                cudaGetLastError();
+                c->pool.push_back(e0);
+                e0 = nullptr;
+            }
+        }
         ggml_status st;
         if (node->op == GGML_OP_FLASH_ATTN_EXT && fa_supported(node))
             st = run_fa(c, node);
@@ -548,6 +634,20 @@ ggml_status be_graph_compute(ggml_backend_t b, ggml_cgraph *g) {
             log_err("graph_compute", "node outside the supports_op contract");
             st = GGML_STATUS_FAILED;
         }
+        if (c->timing && oi >= 0) {
+            if (st == GGML_STATUS_SUCCESS && e0 && e1 &&
+                cudaEventRecord(e1, c->stream) == cudaSuccess) {
+                c->pending.push_back({oi, e0, e1});
+            } else {
+                cudaGetLastError();
+                c->times[oi].untimed++;
+                if (e0)
+                    c->pool.push_back(e0);
+                if (e1)
+                    c->pool.push_back(e1);
+            }
+        }
+        nvtxRangePop();
         if (st != GGML_STATUS_SUCCESS)
             return st;
     }
@@ -609,7 +709,11 @@ ggml_backend_t dev_init(ggml_backend_dev_t d, const char *) {
     auto *dc = static_cast<DevCtx *>(d->context);
     if (!ok_cuda(cudaSetDevice(dc->device), "init_backend"))
         return nullptr;
-    auto *c = new BackendCtx{dc->device, nullptr, nullptr, 0, dc->name, nullptr};
+    auto *c = new BackendCtx;
+    c->device = dc->device;
+    c->name = dc->name;
+    const char *tm = std::getenv("XQ_GGML_TIMING");
+    c->timing = tm && tm[0] && tm[0] != '0';
     if (!ok_cuda(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "init_backend")) {
         delete c;
         return nullptr;
@@ -746,6 +850,23 @@ bool ggml_xq_b200_supports_op(const ggml_tensor *op) {
 }
 
 ggml_backend_reg_t ggml_backend_xq_b200_reg(void) { return &registry().reg; }
+
+bool ggml_xq_b200_backend_op_time(ggml_backend_t backend, int op, uint64_t *nodes, double *ms,
+                                  uint64_t *untimed) {
+    if (!is_our_backend(backend) || op < 0 || op >= kTimedOps)
+        return false;
+    auto *c = static_cast<BackendCtx *>(backend->context);
+    if (!c->timing)
+        return false;
+    drain_times(c);
+    if (nodes)
+        *nodes = c->times[op].nodes;
+    if (ms)
+        *ms = c->times[op].ms;
+    if (untimed)
+        *untimed = c->times[op].untimed;
+    return true;
+}
 
 bool ggml_xq_b200_register(void) {
     static std::once_flag once;
