@@ -2,7 +2,7 @@
 """Benchmark of the B200 attention hot path (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|c1|c2|c2q4|c3a|c3b|c4|c4q8|c4q4|c5|kvw|kv4]
+                    [--workload auto|c1|c2|c2q4|c2mtp|c3a|c3b|c4|c4q8|c4q4|c5|kvw|kv4]
 
 Workloads (seeded synthetic tensors, random data of the
 stated distributions -- no datasets are involved):
@@ -10,6 +10,10 @@ stated distributions -- no datasets are involved):
        (the N=1 headline).  Eight rotated input sets (286 MB > 2 x L2) so every
        step streams its KV from HBM.
   c2q4 the same with Q4_0 KV.
+  c2mtp multi-token-prediction verify over the config-2 cache: 4 query tokens
+       (3 draft tokens + 1) per step, causal among themselves through an F16
+       mask over their last 4 cache rows (the reference's nq 2..9 multi-query
+       tiles), the same rotated input sets.
   c1   config 1: one decode step, F16 KV, 16 Q / 4 KV heads, D=128, kv 4096
        (31 rotated input sets > 2 x L2).
   c3a  config 3 decode: GATED_DELTA_NET, 8 sequences x 1 token, 32 v-heads /
@@ -147,6 +151,7 @@ class ClockSampler:
 
 C1 = dict(n_head=16, n_hkv=4, D=128, n_kv=4096, n_seq=1)
 C2 = dict(n_head=16, n_hkv=2, D=256, n_kv=32768, n_seq=1)
+C2MTP = dict(C2, n_q=4)
 C3 = dict(S=128, H=32, H_k=16, slots=1)
 C4 = dict(n_head=24, n_hkv=4, D=256, n_q=8192)
 TYPE_NAMES = {0: "f32", 1: "f16", 2: "q4_0", 8: "q8_0"}
@@ -155,6 +160,7 @@ WORKLOAD_NAMES = {
     "c1": "BASELINE config 1 (F16 decode, kv 4096)",
     "c2": "BASELINE config 2 (Q8_0 decode, kv 32768)",
     "c2q4": "BASELINE config 2, Q4_0 variant",
+    "c2mtp": "BASELINE config 2 cache, 4-token MTP verify (causal mask over the new rows)",
     "c5": "BASELINE config 5 (8 x 262144 Q8_0, KV-sharded)",
     "c3a": "BASELINE config 3 decode (GDN, 8 seqs x 1 token)",
     "c3b": "BASELINE config 3 prefill (GDN, 1 seq x 4096 tokens)",
@@ -168,10 +174,24 @@ WORKLOAD_NAMES = {
 
 
 def algo_bytes(w, ty):
+    """(K + V bytes, all bytes of a step: K, V, q, out and the F16 mask of a
+    multi-query step)."""
     import xq
+    n_q = w.get("n_q", 1)
     kv = 2 * w["n_seq"] * w["n_kv"] * w["n_hkv"] * xq.row_bytes(ty, w["D"])
-    qo = 2 * w["n_seq"] * w["n_head"] * w["D"] * 4
-    return kv, kv + qo
+    qo = 2 * w["n_seq"] * n_q * w["n_head"] * w["D"] * 4
+    mask = w["n_kv"] * n_q * 2 if n_q > 1 else 0
+    return kv, kv + qo + mask
+
+
+def mtp_mask(torch, w, dev):
+    """F16 mask [1, 1, n_q, n_kv] of an MTP verify step: query i sees the cache
+    and the new rows up to its own (the last n_q rows are the new tokens)."""
+    n_q, n_kv = w["n_q"], w["n_kv"]
+    m = torch.zeros((1, 1, n_q, n_kv), dtype=torch.float16, device=dev)
+    for i in range(n_q):
+        m[0, 0, i, n_kv - n_q + i + 1:] = float("-inf")
+    return m
 
 
 def make_kv(torch, xq, w, ty, n_rows, seed, dev):
@@ -234,13 +254,15 @@ def workload_config(workload, world=1):
     device query), the same in the repo arm and the reference arm."""
     def l2_sets(step_bytes):
         return max(4, math.ceil(2 * L2_BYTES / step_bytes) + 1)
-    if workload in ("c1", "c2", "c2q4", "c5"):
-        w = {"c5": C5, "c1": C1}.get(workload, C2)
+    if workload in ("c1", "c2", "c2q4", "c2mtp", "c5"):
+        w = {"c5": C5, "c1": C1, "c2mtp": C2MTP}.get(workload, C2)
         ty = {"c2q4": 2, "c1": 1}.get(workload, 8)
         kv, _ = algo_bytes(w, ty)
         cfg = {"workload": WORKLOAD_NAMES[workload], "kv_type": TYPE_NAMES[ty],
                "n_seq": w["n_seq"], "n_head": w["n_head"], "n_head_kv": w["n_hkv"],
                "head_dim": w["D"], "kv_len": w["n_kv"],
+               **({"n_q": w["n_q"], "mask": "F16 causal over the new rows"}
+                  if w.get("n_q", 1) > 1 else {}),
                "parallelism": f"kv-shard{world}" if world > 1 else "single"}
         if workload == "c5":
             cfg["l2"] = "inputs %.0f MB per GPU > L2" % (kv / world / 1e6)
@@ -296,7 +318,7 @@ def eager_timed(torch, fn, n, warmup):
     return e0.elapsed_time(e1)
 
 
-def fa_eager_call(torch, q, k, v, ty, scale, n_splits, out):
+def fa_eager_call(torch, q, k, v, ty, scale, n_splits, out, mask=None):
     """One prebuilt C-ABI call of xq_flash_attn_ext (the argument struct and
     the workspace are built once, as a C caller keeps them), returned as a
     zero-argument function: the eager e2e then times the library's own host
@@ -306,13 +328,13 @@ def fa_eager_call(torch, q, k, v, ty, scale, n_splits, out):
     import xq
     from xq import _lib
     from xq.ops import _fa_params, _stream, _workspace
-    p = _fa_params(q, k, v, ty, ty, None, None, out, scale, 0.0, 0.0, n_splits)
+    p = _fa_params(q, k, v, ty, ty, mask, None, out, scale, 0.0, 0.0, n_splits)
     L = _lib.lib()
     nbytes = L.xq_flash_attn_ext_workspace(C.byref(p))
     ws = _workspace(nbytes, torch.device("cuda", torch.cuda.current_device()))
     wsp, wsn = (ws.data_ptr(), ws.numel()) if ws is not None else (None, 0)
     fn, ref, st = L.xq_flash_attn_ext, C.byref(p), _stream(None)
-    keep = (p, ws, q, out)
+    keep = (p, ws, q, out, mask)
 
     def call():
         rc = fn(ref, wsp, wsn, st)
@@ -340,11 +362,13 @@ def run_decode(args, rank, world, torch, dist, workload):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     ty = {"c2q4": xq.Q4_0, "c1": xq.F16}.get(workload, xq.Q8_0)
-    w = {"c5": C5, "c1": C1}.get(workload, C2)
+    w = {"c5": C5, "c1": C1, "c2mtp": C2MTP}.get(workload, C2)
     hbm, _, peak_kind = peaks()
     D, H, Hkv, n_seq = w["D"], w["n_head"], w["n_hkv"], w["n_seq"]
+    n_q = w.get("n_q", 1)
     kv_bytes, step_bytes = algo_bytes(w, ty)
-    n_rows_out = n_seq * H
+    n_rows_out = n_seq * n_q * H
+    mask = mtp_mask(torch, w, dev) if n_q > 1 else None
 
     if workload == "c5":
         from xq import shard
@@ -364,13 +388,14 @@ def run_decode(args, rank, world, torch, dist, workload):
                  make_kv(torch, xq, w, ty, w["n_kv"], 11 + 2 * i, dev)) for i in range(n_sets)]
     gq = torch.Generator(device=dev)
     gq.manual_seed(7)
-    qs = [torch.randn((n_seq, H, 1, D), generator=gq, device=dev) for _ in sets]
+    qs = [torch.randn((n_seq, H, n_q, D), generator=gq, device=dev) for _ in sets]
     scale = 1.0 / math.sqrt(D)
 
     if workload != "c5":
         # the library's automatic plan (every CTA slot of the decode variant
         # filled in one wave, whole 64-row rounds per split)
-        _, n_splits, rows_per_split = xq.flash_attn_ext_plan(qs[0], sets[0][0], sets[0][1], ty)
+        _, n_splits, rows_per_split = xq.flash_attn_ext_plan(qs[0], sets[0][0], sets[0][1], ty,
+                                                             mask=mask)
         sb, se = 0, n_splits
     part_local = torch.empty((se - sb, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     if workload == "c5":
@@ -378,7 +403,7 @@ def run_decode(args, rank, world, torch, dist, workload):
         rec_all = torch.empty((n_groups, n_rows_out, D + 2), dtype=torch.float32, device=dev)
     out = torch.empty((n_rows_out, D), dtype=torch.float32, device=dev)
 
-    out4 = out.view(n_seq, 1, H, D)
+    out4 = out.view(n_seq, n_q, H, D)
 
     def step(i, parts=("dec", "gather", "merge")):
         k, v = sets[i % len(sets)]
@@ -386,11 +411,12 @@ def run_decode(args, rank, world, torch, dist, workload):
         if workload != "c5" and parts == ("dec", "gather", "merge"):
             # the public call (device buffers): the split-KV decode kernel and
             # the merge kernel, as xq_flash_attn_ext launches them
-            xq.flash_attn_ext(q, k, v, ty, scale=scale, n_splits=n_splits, out=out4)
+            xq.flash_attn_ext(q, k, v, ty, mask=mask, scale=scale, n_splits=n_splits, out=out4)
             return
         if "dec" in parts:
             xq.fa_partials(q, k, v, ty, rows_per_split, 0 if workload == "c5" else sb,
-                           (se - sb) if workload == "c5" else se, scale=scale, out=part_local)
+                           (se - sb) if workload == "c5" else se, mask=mask, scale=scale,
+                           out=part_local)
         src = part_local
         if workload == "c5":
             if "merge" in parts:
@@ -440,9 +466,9 @@ def run_decode(args, rank, world, torch, dist, workload):
               if world > 1 else 0.0)
 
     # end to end through the public call with host buffers (pinned)
-    q_host = torch.empty((n_seq, H, 1, D), dtype=torch.float32, pin_memory=True)
+    q_host = torch.empty((n_seq, H, n_q, D), dtype=torch.float32, pin_memory=True)
     q_host.copy_(qs[0].cpu())
-    o_host = torch.empty((n_seq, 1, H, D), dtype=torch.float32, pin_memory=True)
+    o_host = torch.empty((n_seq, n_q, H, D), dtype=torch.float32, pin_memory=True)
     q_dev = torch.empty_like(qs[0])
     eager_ms = None
     if workload != "c5":
@@ -452,8 +478,9 @@ def run_decode(args, rank, world, torch, dist, workload):
             # to the GPU with its staging kernel and writes the result back over
             # PCIe every step
             k, v = sets[i % len(sets)]
-            xq.flash_attn_ext(q_host, k, v, ty, scale=scale, n_splits=n_splits, out=o_host)
-        calls = [fa_eager_call(torch, q_host, k_, v_, ty, scale, n_splits, o_host)
+            xq.flash_attn_ext(q_host, k, v, ty, mask=mask, scale=scale, n_splits=n_splits,
+                              out=o_host)
+        calls = [fa_eager_call(torch, q_host, k_, v_, ty, scale, n_splits, o_host, mask)
                  for k_, v_ in sets]
         eager_ms = eager_timed(torch, lambda i: calls[i % len(calls)](), args.steps,
                                args.warmup) / args.steps
@@ -567,29 +594,35 @@ def cpu_oracle_sample(workload, seconds_cap=20.0, sample_kv=None):
     """Time the CPU restatement of ggml-cpu FLASH_ATTN_EXT on a bounded sample
     of the workload (all host threads); returns (GB/s, info)."""
     import oracle
-    w = {"c5": C5, "c1": C1}.get(workload, C2)
+    w = {"c5": C5, "c1": C1, "c2mtp": C2MTP}.get(workload, C2)
     ty = {"c2q4": oracle.Q4_0, "c1": oracle.F16}.get(workload, oracle.Q8_0)
     n_kv = sample_kv or w["n_kv"]
-    n_seq = 1
+    n_seq, n_q = 1, w.get("n_q", 1)
     rng = np.random.default_rng(0)
-    q = rng.normal(0, 1, (n_seq, w["n_head"], 1, w["D"])).astype(np.float32)
+    q = rng.normal(0, 1, (n_seq, w["n_head"], n_q, w["D"])).astype(np.float32)
     kf = rng.normal(0, 1, (n_seq, n_kv, w["n_hkv"], w["D"])).astype(np.float32)
     k = oracle.quantize(ty, kf)
     v = oracle.quantize(ty, rng.normal(0, 1, kf.shape).astype(np.float32))
     del kf
+    m = None
+    if n_q > 1:
+        m = np.zeros((1, 1, n_q, n_kv), np.float16)
+        for i in range(n_q):
+            m[0, 0, i, n_kv - n_q + i + 1:] = -np.inf
     cores = os.cpu_count() or 1
     sc = 1.0 / math.sqrt(w["D"])
-    oracle.flash_attn_ext(q, k, v, ty, ty, scale=sc, nth=cores, n_workers=cores)  # warm
+    oracle.flash_attn_ext(q, k, v, ty, ty, mask=m, scale=sc, nth=cores, n_workers=cores)  # warm
     t = time.perf_counter()
     reps = 0
     while True:
-        oracle.flash_attn_ext(q, k, v, ty, ty, scale=sc, nth=cores, n_workers=cores)
+        oracle.flash_attn_ext(q, k, v, ty, ty, mask=m, scale=sc, nth=cores, n_workers=cores)
         reps += 1
         if time.perf_counter() - t > min(seconds_cap, 3.0) or reps >= 5:
             break
     dt = (time.perf_counter() - t) / reps
-    b = k.nbytes + v.nbytes + 2 * q.nbytes
-    return b / dt / 1e9, {"cores": cores, "sample": f"1 sequence x {n_kv} rows, {reps} reps, "
+    b = k.nbytes + v.nbytes + 2 * q.nbytes + (m.nbytes if m is not None else 0)
+    return b / dt / 1e9, {"cores": cores, "sample": f"1 sequence x {n_kv} rows x {n_q} "
+                          f"quer{'ies' if n_q > 1 else 'y'}, {reps} reps, "
                           f"{dt * 1e3:.1f} ms each, {cores} threads"}
 
 
