@@ -101,6 +101,32 @@ def test_multi_query_and_sequences(ty, n_q, n_seq):
     np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("ty", [oracle.F16, oracle.Q8_0, oracle.Q4_0])
+@pytest.mark.parametrize("D,n_head,n_hkv,n_q", [(128, 16, 2, 3), (256, 16, 2, 4),
+                                                (128, 12, 2, 5), (256, 32, 4, 7)])
+def test_two_block_ctas(ty, D, n_head, n_hkv, n_q):
+    """More than 16 (query, head) rows per KV head: each CTA serves two 8-row
+    blocks from every K/V group it loads -- full pairs (32 rows), a pair whose
+    second block is empty (24 rows) or partly filled (30 rows: 16 + 14)."""
+    q, k, v, m = make_case(D + 7 * n_q + ty, ty, D, n_head, n_hkv, 1700, n_q=n_q,
+                           mask="causal")
+    for n_splits in (1, 0):
+        got, want = run_both(q, k, v, m, ty, D ** -0.5, n_splits=n_splits)
+        np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL, err_msg=str(n_splits))
+
+
+@pytest.mark.parametrize("ty", [oracle.F16, oracle.Q4_0])
+def test_two_block_ctas_softcap_alibi_sinks(ty):
+    """Per-row ALiBi slopes, sinks and the mask row of each (query, head) row
+    inside a two-block CTA (20 heads over 2 KV heads, 3 queries: 30 rows)."""
+    q, k, v, m = make_case(13, ty, 128, 20, 2, 1200, n_q=3, mask="random")
+    sinks = np.random.default_rng(2).normal(0, 1, 20).astype(np.float32)
+    for kw in ({"softcap": 30.0}, {"max_bias": 8.0}, {"sinks": sinks}):
+        for n_splits in (1, 0):
+            got, want = run_both(q, k, v, m, ty, 0.3, n_splits=n_splits, **kw)
+            np.testing.assert_allclose(got, want, rtol=RTOL, atol=ATOL, err_msg=str(kw))
+
+
 def test_kv_sequence_broadcast():
     q, k, v, m = make_case(5, oracle.Q8_0, 128, 8, 2, 600, n_seq=4, n_seq_kv=2)
     got, want = run_both(q, k, v, m, oracle.Q8_0, 128 ** -0.5)

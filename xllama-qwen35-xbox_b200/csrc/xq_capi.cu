@@ -150,7 +150,7 @@ int fa_prepare(const xq_fa_params *p, FaPlan *pl) {
         return fail(XQ_ERR_UNSUPPORTED, "flash_attn_ext: K/V rows not 4-byte aligned");
     pl->D = (int)D;
     pl->mma = !mma_disabled() && xq::decode_mma_ok(k.type, (int)D, a);
-    const int per_block = pl->mma ? 8 : pl->cfg.NR;
+    const int per_block = pl->mma ? xq::decode_mma_rows_per_cta(a.n_qrows) : pl->cfg.NR;
     pl->n_qblocks = (a.n_qrows + per_block - 1) / per_block;
     pl->n_rows = n_seq * n_q * n_head;
     return XQ_OK;
@@ -226,7 +226,8 @@ void plan_splits(FaPlan *pl, int64_t requested) {
     const int64_t per = (int64_t)pl->a.n_head_kv * pl->n_qblocks * pl->a.n_seq;
     // the warp-MMA kernel fills every CTA slot its variant has on an SM; the
     // CUDA-core kernel two
-    const int per_sm = pl->mma ? xq::decode_mma_occupancy(pl->cfg.type, pl->D, pl->cfg.VW) : 2;
+    const int per_sm =
+        pl->mma ? xq::decode_mma_occupancy(pl->cfg.type, pl->D, pl->cfg.VW, pl->a.n_qrows) : 2;
     int64_t s = requested > 0 ? requested : auto_splits(n_kv, per, 64, per_sm);
     if (n_kv == 0)
         s = 1;

@@ -277,7 +277,7 @@ __device__ __forceinline__ int out_dim(int m, int row) {
 // config 2 instead of four -- measured slower: 15.9 against 14.5 us a step.)
 __host__ __device__ constexpr int mma_ctas_per_sm(int) { return 2; }
 
-template <int T, int D, int STAGES, int VW>
+template <int T, int D, int STAGES, int VW, int QB>
 __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     fa_decode_mma_kernel(const __grid_constant__ CUtensorMap kmap,
                          const __grid_constant__ CUtensorMap vmap, const DecodeArgs a) {
@@ -293,8 +293,12 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     constexpr int VPR = REC / VW;
     constexpr int BB = T == kQ8 ? 34 : 18; // bytes per quant block
     static_assert(REC % VW == 0, "copy width");
-    constexpr int OWS = D + 4;              // merge buffer row stride (bank spread)
-    constexpr int OWB = NWARP * 8 * OWS * 4; // merge buffer, aliases the rings
+    // q-rows of the CTA: QB blocks of 8 (query, head) rows, each the N = 8 side
+    // of the warp MMAs; every K/V group a warp loads serves all of them (the
+    // block dots share the K fragments, the PV products the V conversion)
+    constexpr int RQ = 8 * QB;
+    constexpr int OWS = D + 4;               // merge buffer row stride (bank spread)
+    constexpr int OWB = NWARP * RQ * OWS * 4; // merge buffer, aliases the rings
     constexpr int BIG = NWARP * RING > OWB ? NWARP * RING : OWB;
 
     extern __shared__ __align__(128) uint8_t smem[];
@@ -307,17 +311,17 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
         }
     }
     uint8_t *rings = smem;                                   // [NWARP][STAGES][K|V][GBYTES]
-    uint8_t *qsm = rings + BIG;                              // q codes: int8 [8][D] or f16 [8][D]
-    constexpr int QBYTES = T == kF16 ? 8 * D * 2 : 8 * D;   // f16 or int8 q codes
-    float *dq_s = reinterpret_cast<float *>(qsm + QBYTES); // [NB][8]
-    int *qsum_s = reinterpret_cast<int *>(dq_s + NB * 8);    // [NB][8] (8 * sum q)
-    float *pt_s = reinterpret_cast<float *>(qsum_s + NB * 8); // [NWARP][16][8]
-    float *mw_s = pt_s + NWARP * 16 * 8;                     // [NWARP][8]
-    float *lw_s = mw_s + NWARP * 8;                          // [NWARP][8]
-    float *slope_s = lw_s + NWARP * 8;                       // [8]
-    int64_t *moff_s = reinterpret_cast<int64_t *>(slope_s + 8); // [8]
-    int *lim_s = reinterpret_cast<int *>(moff_s + 8);        // [8]
-    uint64_t *bar_s = reinterpret_cast<uint64_t *>(lim_s + 8); // [NWARP][STAGES]
+    uint8_t *qsm = rings + BIG;                              // q codes: int8 or f16 [RQ][D]
+    constexpr int QBYTES = T == kF16 ? RQ * D * 2 : RQ * D;  // f16 or int8 q codes
+    float *dq_s = reinterpret_cast<float *>(qsm + QBYTES); // [NB][RQ]
+    int *qsum_s = reinterpret_cast<int *>(dq_s + NB * RQ);   // [NB][RQ] (8 * sum q)
+    float *pt_s = reinterpret_cast<float *>(qsum_s + NB * RQ); // [NWARP][QB][16][8]
+    float *mw_s = pt_s + NWARP * QB * 16 * 8;                // [NWARP][RQ]
+    float *lw_s = mw_s + NWARP * RQ;                         // [NWARP][RQ]
+    float *slope_s = lw_s + NWARP * RQ;                      // [RQ]
+    int64_t *moff_s = reinterpret_cast<int64_t *>(slope_s + RQ); // [RQ]
+    int *lim_s = reinterpret_cast<int *>(moff_s + RQ);       // [RQ]
+    uint64_t *bar_s = reinterpret_cast<uint64_t *>(lim_s + RQ); // [NWARP][STAGES]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -326,8 +330,8 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     const int64_t r0 = split * a.rows_per_split;
     const int64_t r1 = min((int64_t)a.n_kv, r0 + a.rows_per_split);
     const int nrows_split = (int)max((int64_t)0, r1 - r0);
-    const int jbase = qb * 8;
-    const int nj = min(8, a.n_qrows - jbase);
+    const int jbase = qb * RQ;
+    const int nj = min(RQ, a.n_qrows - jbase);
     const uint8_t *kbase = a.k + (int64_t)kvh * a.k_nb2 + (int64_t)(s / a.rk3) * a.k_nb3 +
                            r0 * a.k_nb1;
     const uint8_t *vbase = a.v + (int64_t)kvh * a.v_nb2 + (int64_t)(s / a.rv3) * a.v_nb3 +
@@ -370,24 +374,29 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     }
     grid_dep_wait();
     // q loads first: their latency overlaps the K/V copies issued next
-    constexpr int QU = T == kF16 ? 0 : 8 * NB * 2; // quantizer units (two per q block)
-    static_assert(QU <= NT && QU % 32 == 0, "one quantizer unit per thread, whole warps");
-    float xq[16];
+    // quantizer units (two per q block of a q-row): unit tid + NT u, u < QB
+    constexpr int QU = T == kF16 ? 0 : RQ * NB * 2;
+    static_assert(QU <= NT * QB && QU % 32 == 0, "at most QB quantizer units per thread");
+    float xq[QB][16];
     if constexpr (QU > 0) {
-        const int blk = tid >> 1, half = tid & 1;
-        const int j = blk / NB, b = blk - j * NB;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            xq[i] = 0.0f;
-        if (tid < QU && j < nj) {
-            const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
-            const float *src = reinterpret_cast<const float *>(
-                                   a.q + (int64_t)iq1 * a.q_nb1 + (int64_t)h * a.q_nb2 +
-                                   (int64_t)s * a.q_nb3) +
-                               b * 32 + half * 16;
+        for (int u = 0; u < QB; ++u) {
+            const int unit = tid + NT * u;
+            const int blk = unit >> 1, half = unit & 1;
+            const int j = blk / NB, b = blk - j * NB;
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-                xq[i] = src[i];
+                xq[u][i] = 0.0f;
+            if (unit < QU && j < nj) {
+                const int jj = jbase + j, iq1 = jj / a.G, h = kvh * a.G + jj % a.G;
+                const float *src = reinterpret_cast<const float *>(
+                                       a.q + (int64_t)iq1 * a.q_nb1 + (int64_t)h * a.q_nb2 +
+                                       (int64_t)s * a.q_nb3) +
+                                   b * 32 + half * 16;
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    xq[u][i] = src[i];
+            }
         }
     }
     auto issue = [&](int grp, int stage) {
@@ -442,7 +451,7 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     }
 
     // ---- prologue: q in K's dot type, per-q-row constants ----
-    if (tid < 8) {
+    if (tid < RQ) {
         const int j = tid;
         float slope = 1.0f;
         int64_t moff = 0;
@@ -467,7 +476,7 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     }
     if constexpr (T == kF16) {
         __half *q16 = reinterpret_cast<__half *>(qsm);
-        for (int idx = tid; idx < 8 * D; idx += NT) {
+        for (int idx = tid; idx < RQ * D; idx += NT) {
             const int j = idx / D, d = idx - j * D;
             float x = 0.0f;
             if (j < nj) {
@@ -481,10 +490,14 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     } else {
         // ggml quantize_row_q8_0 reference arithmetic; two threads per 32-block
         int8_t *q8 = reinterpret_cast<int8_t *>(qsm);
-        if (tid < QU) {
-            const int blk = tid >> 1, half = tid & 1;
+#pragma unroll
+        for (int u = 0; u < QB; ++u) {
+            const int unit = tid + NT * u;
+            if (unit >= QU) // warp-uniform (QU is a multiple of 32)
+                continue;
+            const int blk = unit >> 1, half = unit & 1;
             const int j = blk / NB, b = blk - j * NB;
-            const float *x = xq; // loaded above (zeros for padding q-rows)
+            const float *x = xq[u]; // loaded above (zeros for padding q-rows)
             float amax = 0.0f;
 #pragma unroll
             for (int i = 0; i < 16; ++i)
@@ -504,47 +517,73 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
             *reinterpret_cast<uint4 *>(q8 + j * D + b * 32 + half * 16) =
                 make_uint4(w[0], w[1], w[2], w[3]);
             if (half == 0) {
-                dq_s[b * 8 + j] = __half2float(__float2half_rn(d));
-                qsum_s[b * 8 + j] = 8 * qs;
+                dq_s[b * RQ + j] = __half2float(__float2half_rn(d));
+                qsum_s[b * RQ + j] = 8 * qs;
             }
         }
     }
     __syncthreads();
 
-    // q as the B operand (8 q-rows = N), kept in registers
+    // q as the B operand (8 q-rows = N per block), kept in registers
     constexpr int QREGS = T == kF16 ? D / 8 : D / 16;
-    uint32_t qf[QREGS];
-    if constexpr (T == kF16) {
-        const __half *q16 = reinterpret_cast<const __half *>(qsm);
+    uint32_t qf[QB][QREGS];
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-            qf[2 * kk] = *reinterpret_cast<const uint32_t *>(q16 + g * D + 16 * kk + 2 * t);
-            qf[2 * kk + 1] = *reinterpret_cast<const uint32_t *>(q16 + g * D + 16 * kk + 8 + 2 * t);
-        }
-    } else {
-        const int8_t *q8 = reinterpret_cast<const int8_t *>(qsm);
+    for (int sb = 0; sb < QB; ++sb) {
+        const int row = 8 * sb + g;
+        if constexpr (T == kF16) {
+            const __half *q16 = reinterpret_cast<const __half *>(qsm);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            qf[2 * b] = *reinterpret_cast<const uint32_t *>(q8 + g * D + 32 * b + 4 * t);
-            qf[2 * b + 1] = *reinterpret_cast<const uint32_t *>(q8 + g * D + 32 * b + 16 + 4 * t);
+            for (int kk = 0; kk < D / 16; ++kk) {
+                qf[sb][2 * kk] =
+                    *reinterpret_cast<const uint32_t *>(q16 + row * D + 16 * kk + 2 * t);
+                qf[sb][2 * kk + 1] =
+                    *reinterpret_cast<const uint32_t *>(q16 + row * D + 16 * kk + 8 + 2 * t);
+            }
+        } else {
+            const int8_t *q8 = reinterpret_cast<const int8_t *>(qsm);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                qf[sb][2 * b] = *reinterpret_cast<const uint32_t *>(q8 + row * D + 32 * b + 4 * t);
+                qf[sb][2 * b + 1] =
+                    *reinterpret_cast<const uint32_t *>(q8 + row * D + 32 * b + 16 + 4 * t);
+            }
         }
     }
-    // this lane's two q-rows (columns 2t, 2t+1)
+    // this lane's two q-rows of each block (columns 2t, 2t+1 of block sb)
     const int c0 = 2 * t, c1 = 2 * t + 1;
     const bool plain = !a.mask && !a.positions && a.softcap == 0.0f; // uniform
-    const bool live0 = c0 < nj, live1 = c1 < nj;
-    const float slope0 = slope_s[c0], slope1 = slope_s[c1];
-    const int lim0 = lim_s[c0], lim1 = lim_s[c1];
-    const int64_t mo0 = moff_s[c0], mo1 = moff_s[c1];
-    const uint32_t dq_base = smem_u32(dq_s + c0);    // + 32 * b
-    const uint32_t qs_base = smem_u32(qsum_s + c0);  // + 32 * b
-
-    float acc[MT][4];
+    bool live0[QB], live1[QB];
+    float slope0[QB], slope1[QB];
+    int lim0[QB], lim1[QB];
+    int64_t mo0[QB], mo1[QB];
+    uint32_t dq_base[QB], qs_base[QB]; // + 4 RQ b bytes for block b of the row
 #pragma unroll
-    for (int m = 0; m < MT; ++m)
-        acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
-    float mu0 = -INFINITY, mu1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-    float *pt = pt_s + warp * 128;
+    for (int sb = 0; sb < QB; ++sb) {
+        const int r0c = 8 * sb + c0, r1c = 8 * sb + c1;
+        live0[sb] = r0c < nj;
+        live1[sb] = r1c < nj;
+        slope0[sb] = slope_s[r0c];
+        slope1[sb] = slope_s[r1c];
+        lim0[sb] = lim_s[r0c];
+        lim1[sb] = lim_s[r1c];
+        mo0[sb] = moff_s[r0c];
+        mo1[sb] = moff_s[r1c];
+        dq_base[sb] = smem_u32(dq_s + r0c);
+        qs_base[sb] = smem_u32(qsum_s + r0c);
+    }
+
+    float acc[QB][MT][4];
+#pragma unroll
+    for (int sb = 0; sb < QB; ++sb)
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+            acc[sb][m][0] = acc[sb][m][1] = acc[sb][m][2] = acc[sb][m][3] = 0.0f;
+    float mu0[QB], mu1[QB], l0[QB], l1[QB];
+#pragma unroll
+    for (int sb = 0; sb < QB; ++sb) {
+        mu0[sb] = mu1[sb] = -INFINITY;
+        l0[sb] = l1[sb] = 0.0f;
+    }
 
     for (int i = 0; i < my_n; ++i) {
         {
@@ -571,20 +610,31 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
         const uint32_t vg_s = kg_s + GBYTES;
         const int k0 = (warp + NWARP * i) * KG; // relative to r0
 
-        // ---------------- scores S^T[key][q-row] ----------------
-        float2 sA = make_float2(0.0f, 0.0f), sB = make_float2(0.0f, 0.0f); // keys g, g+8
+        // ---------------- scores S^T[key][q-row], every q block ----------------
+        float2 sA[QB], sB[QB]; // keys g, g+8 x this lane's two rows of block sb
+#pragma unroll
+        for (int sb = 0; sb < QB; ++sb)
+            sA[sb] = sB[sb] = make_float2(0.0f, 0.0f);
         if constexpr (T == kF16) {
-            float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            float sc[QB][4];
+#pragma unroll
+            for (int sb = 0; sb < QB; ++sb)
+                sc[sb][0] = sc[sb][1] = sc[sb][2] = sc[sb][3] = 0.0f;
             const uint32_t kl = kg_s + ((lane & 7) + ((lane >> 3) & 1) * 8) * SS +
                                 ((lane >> 4) & 1) * 16;
             static_for<D / 16>([&](auto kk_) {
                 constexpr int kk = decltype(kk_)::value;
                 uint32_t a0, a1, a2, a3;
                 ldsm4<32 * kk>(kl, a0, a1, a2, a3);
-                mma_f16(sc, a0, a1, a2, a3, qf[2 * kk], qf[2 * kk + 1]);
+#pragma unroll
+                for (int sb = 0; sb < QB; ++sb)
+                    mma_f16(sc[sb], a0, a1, a2, a3, qf[sb][2 * kk], qf[sb][2 * kk + 1]);
             });
-            sA = make_float2(sc[0], sc[1]);
-            sB = make_float2(sc[2], sc[3]);
+#pragma unroll
+            for (int sb = 0; sb < QB; ++sb) {
+                sA[sb] = make_float2(sc[sb][0], sc[sb][1]);
+                sB[sb] = make_float2(sc[sb][2], sc[sb][3]);
+            }
         } else {
             const uint32_t kA = kg_s + g * SS, kB = kA + 8 * SS;
             const uint32_t kAt = kA + 4 * t, kBt = kB + 4 * t;
@@ -592,105 +642,134 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
                 constexpr int b = decltype(b_)::value;
                 constexpr int QO = BB * b + 2;
                 constexpr bool AL = (QO % 4) == 0;
-                int c[4] = {0, 0, 0, 0};
+                int c[QB][4];
+#pragma unroll
+                for (int sb = 0; sb < QB; ++sb)
+                    c[sb][0] = c[sb][1] = c[sb][2] = c[sb][3] = 0;
                 if constexpr (T == kQ8) {
-                    mma_s8(c, ldsw<QO, AL>(kAt), ldsw<QO, AL>(kBt), ldsw<QO + 16, AL>(kAt),
-                           ldsw<QO + 16, AL>(kBt), qf[2 * b], qf[2 * b + 1]);
+                    const uint32_t ka0 = ldsw<QO, AL>(kAt), kb0 = ldsw<QO, AL>(kBt);
+                    const uint32_t ka1 = ldsw<QO + 16, AL>(kAt), kb1 = ldsw<QO + 16, AL>(kBt);
+#pragma unroll
+                    for (int sb = 0; sb < QB; ++sb)
+                        mma_s8(c[sb], ka0, kb0, ka1, kb1, qf[sb][2 * b], qf[sb][2 * b + 1]);
                 } else {
                     const uint32_t w0 = ldsw<QO, AL>(kAt), w1 = ldsw<QO, AL>(kBt);
-                    mma_u8s8(c, w0 & 0x0F0F0F0Fu, w1 & 0x0F0F0F0Fu, (w0 >> 4) & 0x0F0F0F0Fu,
-                             (w1 >> 4) & 0x0F0F0F0Fu, qf[2 * b], qf[2 * b + 1]);
-                    const int2 q8s = ldsi2<32 * b>(qs_base);
-                    c[0] -= q8s.x;
-                    c[1] -= q8s.y;
-                    c[2] -= q8s.x;
-                    c[3] -= q8s.y;
+                    const uint32_t l0w = w0 & 0x0F0F0F0Fu, l1w = w1 & 0x0F0F0F0Fu;
+                    const uint32_t h0w = (w0 >> 4) & 0x0F0F0F0Fu, h1w = (w1 >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                    for (int sb = 0; sb < QB; ++sb) {
+                        mma_u8s8(c[sb], l0w, l1w, h0w, h1w, qf[sb][2 * b], qf[sb][2 * b + 1]);
+                        const int2 q8s = ldsi2<4 * RQ * b>(qs_base[sb]);
+                        c[sb][0] -= q8s.x;
+                        c[sb][1] -= q8s.y;
+                        c[sb][2] -= q8s.x;
+                        c[sb][3] -= q8s.y;
+                    }
                 }
                 const float dk0 = u16f(lds16<BB * b>(kA)), dk1 = u16f(lds16<BB * b>(kB));
-                const float2 dq = ldsf2<32 * b>(dq_base);
-                sA = __ffma2_rn(make_float2((float)c[0], (float)c[1]),
-                                __fmul2_rn(make_float2(dk0, dk0), dq), sA);
-                sB = __ffma2_rn(make_float2((float)c[2], (float)c[3]),
-                                __fmul2_rn(make_float2(dk1, dk1), dq), sB);
+#pragma unroll
+                for (int sb = 0; sb < QB; ++sb) {
+                    const float2 dq = ldsf2<4 * RQ * b>(dq_base[sb]);
+                    sA[sb] = __ffma2_rn(make_float2((float)c[sb][0], (float)c[sb][1]),
+                                        __fmul2_rn(make_float2(dk0, dk0), dq), sA[sb]);
+                    sB[sb] = __ffma2_rn(make_float2((float)c[sb][2], (float)c[sb][3]),
+                                        __fmul2_rn(make_float2(dk1, dk1), dq), sB[sb]);
+                }
             });
         }
 
-        // ---------------- mask, softmax (log2 domain) ----------------
+        // ---------------- mask, softmax (log2 domain), per q block ----------------
         const int remk = nrows_split - k0; // keys g < remk are inside the split
-        float x[4] = {sA.x, sA.y, sB.x, sB.y}; // (g,c0) (g,c1) (g+8,c0) (g+8,c1)
-        if (plain) {
-            const float sl = a.scale * kLog2e;
-            x[0] = (g < remk && live0) ? x[0] * sl : -INFINITY;
-            x[1] = (g < remk && live1) ? x[1] * sl : -INFINITY;
-            x[2] = (g + 8 < remk && live0) ? x[2] * sl : -INFINITY;
-            x[3] = (g + 8 < remk && live1) ? x[3] * sl : -INFINITY;
-        } else {
+        float2 pab[QB], pcd[QB];           // P^T fragments of each block
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int kr = k0 + g + (e >> 1) * 8; // relative key
-                const int64_t key = r0 + kr;
-                const int col = e & 1;
-                float v = x[e] * a.scale;
-                if (a.softcap != 0.0f)
-                    v = a.softcap * tanhf(v);
-                bool dead = kr >= nrows_split || key >= (col ? lim1 : lim0);
-                if (a.mask && !dead) {
-                    const float mv = (col ? slope1 : slope0) *
-                                     h2f(a.mask + (col ? mo1 : mo0) + 2 * key);
-                    dead = mv == -INFINITY;
-                    v += mv;
+        for (int sb = 0; sb < QB; ++sb) {
+            float x[4] = {sA[sb].x, sA[sb].y, sB[sb].x, sB[sb].y}; // (g,c0) (g,c1) (g+8,c0) (g+8,c1)
+            if (plain) {
+                const float sl = a.scale * kLog2e;
+                x[0] = (g < remk && live0[sb]) ? x[0] * sl : -INFINITY;
+                x[1] = (g < remk && live1[sb]) ? x[1] * sl : -INFINITY;
+                x[2] = (g + 8 < remk && live0[sb]) ? x[2] * sl : -INFINITY;
+                x[3] = (g + 8 < remk && live1[sb]) ? x[3] * sl : -INFINITY;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int kr = k0 + g + (e >> 1) * 8; // relative key
+                    const int64_t key = r0 + kr;
+                    const int col = e & 1;
+                    float v = x[e] * a.scale;
+                    if (a.softcap != 0.0f)
+                        v = a.softcap * tanhf(v);
+                    bool dead = kr >= nrows_split || key >= (col ? lim1[sb] : lim0[sb]);
+                    if (a.mask && !dead) {
+                        const float mv = (col ? slope1[sb] : slope0[sb]) *
+                                         h2f(a.mask + (col ? mo1[sb] : mo0[sb]) + 2 * key);
+                        dead = mv == -INFINITY;
+                        v += mv;
+                    }
+                    x[e] = dead ? -INFINITY : v * kLog2e;
                 }
-                x[e] = dead ? -INFINITY : v * kLog2e;
             }
-        }
-        float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+            float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-        }
-        const bool up0 = mx0 > mu0 + kRescale, up1 = mx1 > mu1 + kRescale;
-        if (__any_sync(0xffffffffu, up0 || up1)) {
-            const float f0 = up0 ? (mu0 == -INFINITY ? 0.0f : ex2(mu0 - mx0)) : 1.0f;
-            const float f1 = up1 ? (mu1 == -INFINITY ? 0.0f : ex2(mu1 - mx1)) : 1.0f;
-            const float2 ff = make_float2(f0, f1);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-                float2 lo = __fmul2_rn(make_float2(acc[m][0], acc[m][1]), ff);
-                float2 hi = __fmul2_rn(make_float2(acc[m][2], acc[m][3]), ff);
-                acc[m][0] = lo.x;
-                acc[m][1] = lo.y;
-                acc[m][2] = hi.x;
-                acc[m][3] = hi.y;
+            for (int o = 4; o < 32; o <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
             }
-            l0 *= f0;
-            l1 *= f1;
-            mu0 = up0 ? mx0 : mu0;
-            mu1 = up1 ? mx1 : mu1;
+            const bool up0 = mx0 > mu0[sb] + kRescale, up1 = mx1 > mu1[sb] + kRescale;
+            if (__any_sync(0xffffffffu, up0 || up1)) {
+                const float f0 = up0 ? (mu0[sb] == -INFINITY ? 0.0f : ex2(mu0[sb] - mx0)) : 1.0f;
+                const float f1 = up1 ? (mu1[sb] == -INFINITY ? 0.0f : ex2(mu1[sb] - mx1)) : 1.0f;
+                const float2 ff = make_float2(f0, f1);
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    float2 lo = __fmul2_rn(make_float2(acc[sb][m][0], acc[sb][m][1]), ff);
+                    float2 hi = __fmul2_rn(make_float2(acc[sb][m][2], acc[sb][m][3]), ff);
+                    acc[sb][m][0] = lo.x;
+                    acc[sb][m][1] = lo.y;
+                    acc[sb][m][2] = hi.x;
+                    acc[sb][m][3] = hi.y;
+                }
+                l0[sb] *= f0;
+                l1[sb] *= f1;
+                mu0[sb] = up0 ? mx0 : mu0[sb];
+                mu1[sb] = up1 ? mx1 : mu1[sb];
+            }
+            const float p0 = x[0] == -INFINITY ? 0.0f : ex2(x[0] - mu0[sb]);
+            const float p1 = x[1] == -INFINITY ? 0.0f : ex2(x[1] - mu1[sb]);
+            const float p2 = x[2] == -INFINITY ? 0.0f : ex2(x[2] - mu0[sb]);
+            const float p3 = x[3] == -INFINITY ? 0.0f : ex2(x[3] - mu1[sb]);
+            l0[sb] += p0 + p2;
+            l1[sb] += p1 + p3;
+            // P^T fragment via a per-warp transpose: pt[key][q-row]
+            float *pt = pt_s + (warp * QB + sb) * 128;
+            *reinterpret_cast<float2 *>(pt + g * 8 + c0) = make_float2(p0, p1);
+            *reinterpret_cast<float2 *>(pt + (g + 8) * 8 + c0) = make_float2(p2, p3);
         }
-        const float p0 = x[0] == -INFINITY ? 0.0f : ex2(x[0] - mu0);
-        const float p1 = x[1] == -INFINITY ? 0.0f : ex2(x[1] - mu1);
-        const float p2 = x[2] == -INFINITY ? 0.0f : ex2(x[2] - mu0);
-        const float p3 = x[3] == -INFINITY ? 0.0f : ex2(x[3] - mu1);
-        l0 += p0 + p2;
-        l1 += p1 + p3;
-        // P^T fragment via a per-warp transpose: pt[key][q-row]
-        *reinterpret_cast<float2 *>(pt + g * 8 + c0) = make_float2(p0, p1);
-        *reinterpret_cast<float2 *>(pt + (g + 8) * 8 + c0) = make_float2(p2, p3);
         __syncwarp();
-        const float2 pab = make_float2(pt[(2 * t) * 8 + g], pt[(2 * t + 1) * 8 + g]);
-        const float2 pcd = make_float2(pt[(2 * t + 8) * 8 + g], pt[(2 * t + 9) * 8 + g]);
+#pragma unroll
+        for (int sb = 0; sb < QB; ++sb) {
+            const float *pt = pt_s + (warp * QB + sb) * 128;
+            pab[sb] = make_float2(pt[(2 * t) * 8 + g], pt[(2 * t + 1) * 8 + g]);
+            pcd[sb] = make_float2(pt[(2 * t + 8) * 8 + g], pt[(2 * t + 9) * 8 + g]);
+        }
 
-        // ---------------- O^T += V^T P^T ----------------
+        // ---------------- O^T += V^T P^T (the V fragments serve every block) ----------------
         if constexpr (T == kF16) {
-            const uint32_t b0 = pack_h2(pab.x, pab.y), b1 = pack_h2(pcd.x, pcd.y);
+            uint32_t b0[QB], b1[QB];
+#pragma unroll
+            for (int sb = 0; sb < QB; ++sb) {
+                b0[sb] = pack_h2(pab[sb].x, pab[sb].y);
+                b1[sb] = pack_h2(pcd[sb].x, pcd[sb].y);
+            }
             const uint32_t vl = vg_s + ((lane & 7) + ((lane >> 4) & 1) * 8) * SS +
                                 ((lane >> 3) & 1) * 16;
             static_for<MT>([&](auto m_) {
                 constexpr int m = decltype(m_)::value;
                 uint32_t a0, a1, a2, a3;
                 ldsm4t<32 * m>(vl, a0, a1, a2, a3);
-                mma_f16(acc[m], a0, a1, a2, a3, b0, b1);
+#pragma unroll
+                for (int sb = 0; sb < QB; ++sb)
+                    mma_f16(acc[sb][m], a0, a1, a2, a3, b0[sb], b1[sb]);
             });
         } else {
             const uint32_t vA = vg_s + (2 * t) * SS, vB = vA + SS, vC = vA + 8 * SS,
@@ -699,11 +778,16 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
             static_for<NB>([&](auto b_) {
                 constexpr int b = decltype(b_)::value;
                 constexpr int SO = BB * b, CO = BB * b + 2;
-                const float2 p01 = __fmul2_rn(
-                    pab, make_float2(u16f(lds16<SO>(vA)), u16f(lds16<SO>(vB))));
-                const float2 p23 = __fmul2_rn(
-                    pcd, make_float2(u16f(lds16<SO>(vC)), u16f(lds16<SO>(vD))));
-                const uint32_t b0 = pack_h2(p01.x, p01.y), b1 = pack_h2(p23.x, p23.y);
+                const float2 sab = make_float2(u16f(lds16<SO>(vA)), u16f(lds16<SO>(vB)));
+                const float2 scd = make_float2(u16f(lds16<SO>(vC)), u16f(lds16<SO>(vD)));
+                uint32_t b0[QB], b1[QB];
+#pragma unroll
+                for (int sb = 0; sb < QB; ++sb) {
+                    const float2 p01 = __fmul2_rn(pab[sb], sab);
+                    const float2 p23 = __fmul2_rn(pcd[sb], scd);
+                    b0[sb] = pack_h2(p01.x, p01.y);
+                    b1[sb] = pack_h2(p23.x, p23.y);
+                }
                 if constexpr (T == kQ8) {
                     constexpr bool AL = (CO % 4) == 0;
                     const uint32_t wa = ldsw<CO, AL>(vA + lo) ^ 0x80808080u;
@@ -711,22 +795,32 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
                     const uint32_t wc = ldsw<CO, AL>(vC + lo) ^ 0x80808080u;
                     const uint32_t wd = ldsw<CO, AL>(vD + lo) ^ 0x80808080u;
                     // tile 2b: bytes 0 (row g) and 1 (row g+8); tile 2b+1: bytes 2, 3
-                    mma_f16(acc[2 * b], s8pair_to_h2(__byte_perm(wa, wb, 0x0400)),
-                            s8pair_to_h2(__byte_perm(wa, wb, 0x0501)),
-                            s8pair_to_h2(__byte_perm(wc, wd, 0x0400)),
-                            s8pair_to_h2(__byte_perm(wc, wd, 0x0501)), b0, b1);
-                    mma_f16(acc[2 * b + 1], s8pair_to_h2(__byte_perm(wa, wb, 0x0602)),
-                            s8pair_to_h2(__byte_perm(wa, wb, 0x0703)),
-                            s8pair_to_h2(__byte_perm(wc, wd, 0x0602)),
-                            s8pair_to_h2(__byte_perm(wc, wd, 0x0703)), b0, b1);
+                    const uint32_t e0 = s8pair_to_h2(__byte_perm(wa, wb, 0x0400));
+                    const uint32_t e1 = s8pair_to_h2(__byte_perm(wa, wb, 0x0501));
+                    const uint32_t e2 = s8pair_to_h2(__byte_perm(wc, wd, 0x0400));
+                    const uint32_t e3 = s8pair_to_h2(__byte_perm(wc, wd, 0x0501));
+                    const uint32_t o0 = s8pair_to_h2(__byte_perm(wa, wb, 0x0602));
+                    const uint32_t o1 = s8pair_to_h2(__byte_perm(wa, wb, 0x0703));
+                    const uint32_t o2 = s8pair_to_h2(__byte_perm(wc, wd, 0x0602));
+                    const uint32_t o3 = s8pair_to_h2(__byte_perm(wc, wd, 0x0703));
+#pragma unroll
+                    for (int sb = 0; sb < QB; ++sb) {
+                        mma_f16(acc[sb][2 * b], e0, e1, e2, e3, b0[sb], b1[sb]);
+                        mma_f16(acc[sb][2 * b + 1], o0, o1, o2, o3, b0[sb], b1[sb]);
+                    }
                 } else {
                     const uint32_t xab = __byte_perm(lds16<CO>(vA + lo), lds16<CO>(vB + lo), 0x5410);
                     const uint32_t xcd = __byte_perm(lds16<CO>(vC + lo), lds16<CO>(vD + lo), 0x5410);
                     // tile 2b: low nibbles (dims 2g, 2g+1); tile 2b+1: high nibbles
-                    mma_f16(acc[2 * b], u4pair_to_h2(xab), u4pair_to_h2(xab >> 8),
-                            u4pair_to_h2(xcd), u4pair_to_h2(xcd >> 8), b0, b1);
-                    mma_f16(acc[2 * b + 1], u4pair_to_h2(xab >> 4), u4pair_to_h2(xab >> 12),
-                            u4pair_to_h2(xcd >> 4), u4pair_to_h2(xcd >> 12), b0, b1);
+                    const uint32_t e0 = u4pair_to_h2(xab), e1 = u4pair_to_h2(xab >> 8);
+                    const uint32_t e2 = u4pair_to_h2(xcd), e3 = u4pair_to_h2(xcd >> 8);
+                    const uint32_t o0 = u4pair_to_h2(xab >> 4), o1 = u4pair_to_h2(xab >> 12);
+                    const uint32_t o2 = u4pair_to_h2(xcd >> 4), o3 = u4pair_to_h2(xcd >> 12);
+#pragma unroll
+                    for (int sb = 0; sb < QB; ++sb) {
+                        mma_f16(acc[sb][2 * b], e0, e1, e2, e3, b0[sb], b1[sb]);
+                        mma_f16(acc[sb][2 * b + 1], o0, o1, o2, o3, b0[sb], b1[sb]);
+                    }
                 }
             });
         }
@@ -741,70 +835,75 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
 
     // ---- per-warp state -> shared memory ----
 #pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-        l0 += __shfl_xor_sync(0xffffffffu, l0, o);
-        l1 += __shfl_xor_sync(0xffffffffu, l1, o);
-    }
+    for (int sb = 0; sb < QB; ++sb)
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            l0[sb] += __shfl_xor_sync(0xffffffffu, l0[sb], o);
+            l1[sb] += __shfl_xor_sync(0xffffffffu, l1[sb], o);
+        }
     __syncthreads(); // every warp is done with its ring: reuse it for O
-    float *ow = reinterpret_cast<float *>(rings); // [NWARP][8][OWS]
-    if (g == 0) {
-        mw_s[warp * 8 + c0] = mu0;
-        mw_s[warp * 8 + c1] = mu1;
-        lw_s[warp * 8 + c0] = l0;
-        lw_s[warp * 8 + c1] = l1;
-    }
-    {
-        float *o0 = ow + (warp * 8 + c0) * OWS, *o1 = ow + (warp * 8 + c1) * OWS;
+    float *ow = reinterpret_cast<float *>(rings); // [NWARP][RQ][OWS]
+#pragma unroll
+    for (int sb = 0; sb < QB; ++sb) {
+        const int r0c = 8 * sb + c0, r1c = 8 * sb + c1;
+        if (g == 0) {
+            mw_s[warp * RQ + r0c] = mu0[sb];
+            mw_s[warp * RQ + r1c] = mu1[sb];
+            lw_s[warp * RQ + r0c] = l0[sb];
+            lw_s[warp * RQ + r1c] = l1[sb];
+        }
+        float *o0 = ow + (warp * RQ + r0c) * OWS, *o1 = ow + (warp * RQ + r1c) * OWS;
+        const float(&ac)[MT][4] = acc[sb];
         if constexpr (T == kQ8) {
             // dims 32b + 4g .. +3 of one q-row are adjacent: one 16-byte store
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 *reinterpret_cast<float4 *>(o0 + 32 * b + 4 * g) =
-                    make_float4(acc[2 * b][0], acc[2 * b][2], acc[2 * b + 1][0], acc[2 * b + 1][2]);
+                    make_float4(ac[2 * b][0], ac[2 * b][2], ac[2 * b + 1][0], ac[2 * b + 1][2]);
                 *reinterpret_cast<float4 *>(o1 + 32 * b + 4 * g) =
-                    make_float4(acc[2 * b][1], acc[2 * b][3], acc[2 * b + 1][1], acc[2 * b + 1][3]);
+                    make_float4(ac[2 * b][1], ac[2 * b][3], ac[2 * b + 1][1], ac[2 * b + 1][3]);
             }
         } else if constexpr (T == kQ4) {
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
                 *reinterpret_cast<float2 *>(o0 + 32 * b + 2 * g) =
-                    make_float2(acc[2 * b][0], acc[2 * b][2]);
+                    make_float2(ac[2 * b][0], ac[2 * b][2]);
                 *reinterpret_cast<float2 *>(o0 + 32 * b + 16 + 2 * g) =
-                    make_float2(acc[2 * b + 1][0], acc[2 * b + 1][2]);
+                    make_float2(ac[2 * b + 1][0], ac[2 * b + 1][2]);
                 *reinterpret_cast<float2 *>(o1 + 32 * b + 2 * g) =
-                    make_float2(acc[2 * b][1], acc[2 * b][3]);
+                    make_float2(ac[2 * b][1], ac[2 * b][3]);
                 *reinterpret_cast<float2 *>(o1 + 32 * b + 16 + 2 * g) =
-                    make_float2(acc[2 * b + 1][1], acc[2 * b + 1][3]);
+                    make_float2(ac[2 * b + 1][1], ac[2 * b + 1][3]);
             }
         } else {
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 const int dA = out_dim<T>(m, g), dB = out_dim<T>(m, g + 8);
-                o0[dA] = acc[m][0];
-                o1[dA] = acc[m][1];
-                o0[dB] = acc[m][2];
-                o1[dB] = acc[m][3];
+                o0[dA] = ac[m][0];
+                o1[dA] = ac[m][1];
+                o0[dB] = ac[m][2];
+                o1[dB] = ac[m][3];
             }
         }
     }
     __syncthreads();
     // per q-row: the warps' merge weights (fixed warp order) with the final
     // normalisation folded in, the row's statistics, and its output address
-    float4 *wt_s = reinterpret_cast<float4 *>(pt_s); // [8] (pt is free now)
-    float **optr_s = reinterpret_cast<float **>(wt_s + 8); // [8]
-    int *nf_s = reinterpret_cast<int *>(optr_s + 8);       // [8] non-finite numerator seen
+    float4 *wt_s = reinterpret_cast<float4 *>(pt_s);       // [RQ] (pt is free now)
+    float **optr_s = reinterpret_cast<float **>(wt_s + RQ); // [RQ]
+    int *nf_s = reinterpret_cast<int *>(optr_s + RQ);       // [RQ] non-finite numerator seen
     if (tid < nj) {
         const int j = tid;
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < NWARP; ++w)
-            if (lw_s[w * 8 + j] != 0.0f)
-                M = fmaxf(M, mw_s[w * 8 + j]);
+            if (lw_s[w * RQ + j] != 0.0f)
+                M = fmaxf(M, mw_s[w * RQ + j]);
         float f[NWARP], L = 0.0f;
 #pragma unroll
         for (int w = 0; w < NWARP; ++w) {
-            const float lw = lw_s[w * 8 + j];
-            f[w] = lw != 0.0f ? ex2(mw_s[w * 8 + j] - M) : 0.0f;
+            const float lw = lw_s[w * RQ + j];
+            f[w] = lw != 0.0f ? ex2(mw_s[w * RQ + j] - M) : 0.0f;
             L += lw * f[w];
         }
         float m_nat = M * kLn2, fin = 1.0f;
@@ -846,10 +945,10 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
     for (int idx = tid; idx < nj * HP; idx += NT) {
         const int j = idx / HP, d = 2 * (idx - j * HP);
         const float4 wt = wt_s[j];
-        const float2 x0 = *reinterpret_cast<const float2 *>(ow + (0 * 8 + j) * OWS + d);
-        const float2 x1 = *reinterpret_cast<const float2 *>(ow + (1 * 8 + j) * OWS + d);
-        const float2 x2 = *reinterpret_cast<const float2 *>(ow + (2 * 8 + j) * OWS + d);
-        const float2 x3 = *reinterpret_cast<const float2 *>(ow + (3 * 8 + j) * OWS + d);
+        const float2 x0 = *reinterpret_cast<const float2 *>(ow + (0 * RQ + j) * OWS + d);
+        const float2 x1 = *reinterpret_cast<const float2 *>(ow + (1 * RQ + j) * OWS + d);
+        const float2 x2 = *reinterpret_cast<const float2 *>(ow + (2 * RQ + j) * OWS + d);
+        const float2 x3 = *reinterpret_cast<const float2 *>(ow + (3 * RQ + j) * OWS + d);
         float2 o = __fmul2_rn(x0, make_float2(wt.x, wt.x));
         o = __ffma2_rn(x1, make_float2(wt.y, wt.y), o);
         o = __ffma2_rn(x2, make_float2(wt.z, wt.z), o);
@@ -877,17 +976,26 @@ __global__ void __launch_bounds__(dm::NT, mma_ctas_per_sm(T))
 // ---------------------------------------------------------------------------
 // host side
 
-template <int T, int D, int ST>
+template <int T, int D, int ST, int QB>
 constexpr size_t mma_smem() {
     constexpr int SS = smem_stride(rec_bytes(T, D));
+    constexpr size_t RQ = 8 * QB;
     constexpr size_t ring = (size_t)dm::NWARP * ST * 2 * dm::KG * SS;
-    constexpr size_t ow = (size_t)dm::NWARP * 8 * (D + 4) * 4;
+    constexpr size_t ow = (size_t)dm::NWARP * RQ * (D + 4) * 4;
     size_t b = ring > ow ? ring : ow;
-    b += (size_t)8 * D * (T == kF16 ? 2 : 1) + (size_t)(D / 32) * 8 * 8; // q codes, dq, qsum
-    b += (size_t)dm::NWARP * 128 * 4 + 2 * dm::NWARP * 8 * 4 + 8 * 4 + 8 * 8 + 8 * 4;
+    b += RQ * D * (T == kF16 ? 2 : 1) + (size_t)(D / 32) * RQ * 8; // q codes, dq, qsum
+    b += (size_t)dm::NWARP * QB * 128 * 4 + 2 * dm::NWARP * RQ * 4 + RQ * 4 + RQ * 8 + RQ * 4;
     b += (size_t)dm::NWARP * ST * 8; // mbarriers
     return b;
 }
+
+// (query, head) rows per CTA of the warp-MMA decode: two q blocks (16 rows)
+// once a KV head has more than 16, so that every K/V group a warp loads feeds
+// both (multi-query steps: MTP verify, short batches); one block otherwise.
+// Config 2's cache, graph-timed step: 4 queries 32.3 against 36.2 us, 9
+// queries 65.9 against 94.3 us; at 2 queries (16 rows) one CTA of 16 rows
+// measured 22.3 against 21.2 us for two CTAs of 8.
+int decode_mma_rows_per_cta(int n_qrows) { return n_qrows > 16 ? 16 : 8; }
 
 bool decode_mma_ok(int type, int D, const DecodeArgs &a) {
     return a.q_convert && (D == 128 || D == 256) &&
@@ -934,10 +1042,10 @@ static bool encode_rows_map(CUtensorMap *m, const uint8_t *base, int rec, int n_
     return true;
 }
 
-template <int T, int D, int ST, int VW>
+template <int T, int D, int ST, int VW, int QB>
 static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
-    constexpr size_t smem = mma_smem<T, D, ST>();
-    auto kern = fa_decode_mma_kernel<T, D, ST, VW>;
+    constexpr size_t smem = mma_smem<T, D, ST, QB>();
+    auto kern = fa_decode_mma_kernel<T, D, ST, VW, QB>;
     static std::atomic<unsigned long long> attr_done{0};
     cudaError_t e = set_smem_limit((const void *)kern, smem, attr_done);
     if (e != cudaSuccess)
@@ -967,9 +1075,9 @@ static cudaError_t launch_mma(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
     return cudaLaunchKernelEx(&cfg, kern, maps[0], maps[1], a);
 }
 
-// CTAs of the variant launch_mma<T, D, ST, VW> that fit on one SM (its
+// CTAs of the variant launch_mma<T, D, ST, VW, QB> that fit on one SM (its
 // shared memory and register bound), asked once per device and variant.
-template <int T, int D, int ST, int VW>
+template <int T, int D, int ST, int VW, int QB>
 static int occupancy_of() {
     static std::atomic<int> cache[64];
     int dev = 0;
@@ -978,8 +1086,8 @@ static int occupancy_of() {
     int n = cache[dev].load(std::memory_order_relaxed);
     if (n > 0)
         return n;
-    constexpr size_t smem = mma_smem<T, D, ST>();
-    auto kern = fa_decode_mma_kernel<T, D, ST, VW>;
+    constexpr size_t smem = mma_smem<T, D, ST, QB>();
+    auto kern = fa_decode_mma_kernel<T, D, ST, VW, QB>;
     static std::atomic<unsigned long long> attr_done{0};
     if (set_smem_limit((const void *)kern, smem, attr_done) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, dm::NT, smem) != cudaSuccess ||
@@ -991,29 +1099,37 @@ static int occupancy_of() {
     return n;
 }
 
-template <int T, int D>
+template <int T, int D, int QB>
 static int mma_occupancy(int vw) {
     constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
     if constexpr (rec_bytes(T, D) % 16 == 0)
         if (vw == 16) {
             constexpr int STV = dm::tma_mode(T, 16) ? (T == kQ4 ? 4 : 2) : ST;
-            return occupancy_of<T, D, STV, 16>();
+            return occupancy_of<T, D, STV, 16, QB>();
         }
     if constexpr (rec_bytes(T, D) % 8 == 0)
         if (vw >= 8)
-            return occupancy_of<T, D, ST, 8>();
-    return occupancy_of<T, D, ST, 4>();
+            return occupancy_of<T, D, ST, 8, QB>();
+    return occupancy_of<T, D, ST, 4, QB>();
 }
 
-int decode_mma_occupancy(int type, int D, int vw) {
+template <int T>
+static int occupancy_td(int D, int vw, int qb) {
+    if (D == 128)
+        return qb == 2 ? mma_occupancy<T, 128, 2>(vw) : mma_occupancy<T, 128, 1>(vw);
+    return qb == 2 ? mma_occupancy<T, 256, 2>(vw) : mma_occupancy<T, 256, 1>(vw);
+}
+
+int decode_mma_occupancy(int type, int D, int vw, int n_qrows) {
+    const int qb = decode_mma_rows_per_cta(n_qrows) / 8;
     switch (type) {
-    case kF16: return D == 128 ? mma_occupancy<kF16, 128>(vw) : mma_occupancy<kF16, 256>(vw);
-    case kQ8: return D == 128 ? mma_occupancy<kQ8, 128>(vw) : mma_occupancy<kQ8, 256>(vw);
-    default: return D == 128 ? mma_occupancy<kQ4, 128>(vw) : mma_occupancy<kQ4, 256>(vw);
+    case kF16: return occupancy_td<kF16>(D, vw, qb);
+    case kQ8: return occupancy_td<kQ8>(D, vw, qb);
+    default: return occupancy_td<kQ4>(D, vw, qb);
     }
 }
 
-template <int T, int D>
+template <int T, int D, int QB>
 static cudaError_t mma_vw(const DecodeArgs &a, int vw, dim3 grid, cudaStream_t st) {
     constexpr int ST = smem_stride(rec_bytes(T, D)) <= 288 ? 3 : 2;
     if constexpr (rec_bytes(T, D) % 16 == 0)
@@ -1024,23 +1140,32 @@ static cudaError_t mma_vw(const DecodeArgs &a, int vw, dim3 grid, cudaStream_t s
             // stream short of requests: four (three groups in flight per warp,
             // still two CTAs per SM) measured 15.2 against 17.9 us on config 2.
             constexpr int STV = dm::tma_mode(T, 16) ? (T == kQ4 ? 4 : 2) : ST;
-            const cudaError_t e = launch_mma<T, D, STV, 16>(a, grid, st);
+            const cudaError_t e = launch_mma<T, D, STV, 16, QB>(a, grid, st);
             if (e != cudaErrorNotSupported)
                 return e;
             vw = 8; // the layout has no tensor map: per-lane copies
         }
     if constexpr (rec_bytes(T, D) % 8 == 0)
         if (vw >= 8)
-            return launch_mma<T, D, ST, 8>(a, grid, st);
-    return launch_mma<T, D, ST, 4>(a, grid, st);
+            return launch_mma<T, D, ST, 8, QB>(a, grid, st);
+    return launch_mma<T, D, ST, 4, QB>(a, grid, st);
+}
+
+template <int T>
+static cudaError_t mma_td(const DecodeArgs &a, int D, int vw, dim3 grid, cudaStream_t st) {
+    // the callers' grid counts CTAs of decode_mma_rows_per_cta(n_qrows) rows
+    const bool two = decode_mma_rows_per_cta(a.n_qrows) == 16;
+    if (D == 128)
+        return two ? mma_vw<T, 128, 2>(a, vw, grid, st) : mma_vw<T, 128, 1>(a, vw, grid, st);
+    return two ? mma_vw<T, 256, 2>(a, vw, grid, st) : mma_vw<T, 256, 1>(a, vw, grid, st);
 }
 
 cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
                               cudaStream_t st) {
     switch (type) {
-    case kF16: return D == 128 ? mma_vw<kF16, 128>(a, vw, grid, st) : mma_vw<kF16, 256>(a, vw, grid, st);
-    case kQ8: return D == 128 ? mma_vw<kQ8, 128>(a, vw, grid, st) : mma_vw<kQ8, 256>(a, vw, grid, st);
-    default: return D == 128 ? mma_vw<kQ4, 128>(a, vw, grid, st) : mma_vw<kQ4, 256>(a, vw, grid, st);
+    case kF16: return mma_td<kF16>(a, D, vw, grid, st);
+    case kQ8: return mma_td<kQ8>(a, D, vw, grid, st);
+    default: return mma_td<kQ4>(a, D, vw, grid, st);
     }
 }
 

@@ -68,8 +68,11 @@ cudaError_t launch_decode(const DecodeArgs &a, const DecodeConfig &cfg, dim3 gri
 bool decode_mma_ok(int type, int D, const DecodeArgs &a);
 cudaError_t launch_decode_mma(const DecodeArgs &a, int type, int D, int vw, dim3 grid,
                               cudaStream_t st);
+// (query, head) rows per CTA of the warp-MMA decode for n_qrows rows per KV
+// head (8, or 16 when the KV head has more than 16: two q blocks per K/V load).
+int decode_mma_rows_per_cta(int n_qrows);
 // Resident CTAs per SM of the warp-MMA decode variant launch_decode_mma picks.
-int decode_mma_occupancy(int type, int D, int vw);
+int decode_mma_occupancy(int type, int D, int vw, int n_qrows);
 // n_groups > 1 merges consecutive blocks of n_splits splits separately; with
 // records, the merged rows are written as partial records (see lse_merge_kernel).
 // flagged: the partials come from fa_decode_mma_kernel, which gives a record
