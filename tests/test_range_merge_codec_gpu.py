@@ -225,6 +225,58 @@ def test_lse_merge_variants_bit_identical(D, n_splits, rows):
         assert np.array_equal(recs[0], recs[1])
 
 
+@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("n_splits", [1, 33, 70])
+def test_lse_merge_many_rows_four_warps_equal_one_warp(D, n_splits):
+    """The warp-per-row merges (many rows, and every record merge) take four
+    warps per row when the rows fit one wave (at most two per SM) and one warp
+    per row beyond; both add every dim over the splits in split order, so the
+    first 160 rows merged alone (four warps) equal the same rows of a 400-row
+    merge (one warp) bit for bit -- outputs, lse and records, with empty,
+    poisoned and partial-chunk rows -- and match the oracle.  At D = 256 the
+    160 rows 4 bytes off (one warp per row: unaligned pairs) agree too."""
+    xq = _xq()
+    rows, sub = 400, 160
+    rng = np.random.default_rng(D + n_splits)
+    part = np.zeros((n_splits, rows, D + 2), np.float32)
+    part[:, :, :D] = rng.normal(0, 1, (n_splits, rows, D))
+    part[:, :, D] = rng.normal(0, 3, (n_splits, rows))
+    part[:, :, D + 1] = rng.uniform(0.5, 2.0, (n_splits, rows))
+    empty = rng.random((n_splits, rows)) < 0.2
+    part[:, :, D + 1][empty] = 0.0
+    part[:, :, D][empty] = -3.402823466e38
+    part[:, 2, D + 1] = 0.0
+    part[:, 2, D] = -3.402823466e38
+    live = np.nonzero(part[:, 4, D + 1] != 0.0)[0]
+    if live.size:
+        part[live[-1], 4, D - 1] = np.nan
+
+    def merged(t):
+        o, lse = xq.lse_merge(t)
+        r = xq.lse_merge_records(t, n_splits)
+        torch.cuda.synchronize()
+        return [x.cpu().numpy() for x in (o, lse, r)]
+
+    whole = merged(torch.from_numpy(part).cuda())
+    head = np.ascontiguousarray(part[:, :sub])
+    alone = merged(torch.from_numpy(head).cuda())
+    for a, w in zip(alone, (whole[0][:sub], whole[1][:sub], whole[2][:, :sub])):
+        assert np.array_equal(a.view(np.int32), np.ascontiguousarray(w).view(np.int32))
+    if D == 256:
+        n = head.size
+        buf = torch.zeros(n + 2, dtype=torch.float32, device="cuda")
+        buf[1:n + 1].copy_(torch.from_numpy(head).reshape(-1).cuda())
+        off = merged(buf[1:n + 1].view(head.shape))
+        for a, b in zip(alone, off):
+            assert np.array_equal(a.view(np.int32), b.view(np.int32))
+    o_ref, lse_ref = oracle.lse_merge(head)
+    assert np.array_equal(np.isnan(alone[0]), np.isnan(o_ref))
+    fin = ~np.isnan(o_ref)
+    np.testing.assert_allclose(alone[0][fin], o_ref[fin], rtol=1e-4, atol=1e-5)
+    fl = ~np.isnan(lse_ref)
+    np.testing.assert_allclose(alone[1][fl], lse_ref[fl], rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("rows", [6, 48, 200])
 def test_lse_merge_records_of_a_group_block_equal_the_whole(rows):
     """The records of any block of groups equal the same groups' records of
